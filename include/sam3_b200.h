@@ -1,0 +1,159 @@
+/*
+ * sam3_b200.h - C ABI of the B200 encoder engine for sam3.cpp.
+ *
+ * The engine replaces the ggml graph builders of the per-frame backbone
+ * forward and of memory attention in sam3.cpp (PABannier/sam3.cpp) with
+ * hand-written sm_100a CUDA kernels. Signatures use plain pointers and sizes
+ * only. Every function returns S3B_OK (0) or a negative S3B_ERR_* code; the
+ * message of the last error is available from s3b_last_error(), and is also
+ * printed to stderr, following the reference's "return false + stderr"
+ * convention (sam3.cpp:1021-1022).
+ *
+ * Layouts follow ggml's memory order: a feature map [C, W, H, B] in ggml
+ * notation is channel-last, row index = (b*H + y)*W + x, C contiguous.
+ */
+#ifndef SAM3_B200_H
+#define SAM3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct s3b_ctx s3b_ctx;
+
+enum {
+    S3B_OK = 0,
+    S3B_ERR_ARG = -1,
+    S3B_ERR_IO = -2,
+    S3B_ERR_FORMAT = -3,
+    S3B_ERR_CUDA = -4,
+    S3B_ERR_STATE = -5,
+    S3B_ERR_UNSUPPORTED = -6,
+    S3B_ERR_DEVICE = -7, /* a kernel's bounded wait expired; see s3b_last_error */
+    S3B_ERR_OOM = -8
+};
+
+/* ggml tensor types used by the .ggml files (sam3.cpp:3242-3251). */
+enum { S3B_F32 = 0, S3B_F16 = 1, S3B_Q4_0 = 2, S3B_Q4_1 = 3, S3B_Q8_0 = 8 };
+
+/* Epilogue activations of s3b_op_gemm. */
+enum { S3B_ACT_NONE = 0, S3B_ACT_GELU_ERF = 1, S3B_ACT_GELU_TANH = 2, S3B_ACT_RELU = 3 };
+
+/* Flags of the encode calls. */
+enum {
+    S3B_ENCODE_NO_NECK = 1, /* backbone only (no FPN / SimpleFPN neck) */
+    S3B_ENCODE_NO_DET = 2   /* SAM 3: skip the detector neck path */
+};
+
+/* ---------------------------------------------------------------- context */
+
+/* Creates a context bound to CUDA device `device` with its own stream.
+ * Replaces the backend set-up of sam3_load_model (sam3.cpp:3275-3288). */
+int s3b_create(int device, s3b_ctx** out);
+void s3b_destroy(s3b_ctx* ctx);
+const char* s3b_last_error(const s3b_ctx* ctx);
+/* Uses `cuda_stream` (a cudaStream_t, or NULL for the context's own) for all work. */
+int s3b_set_stream(s3b_ctx* ctx, void* cuda_stream);
+/* Waits for all work of the context and checks the device error word. */
+int s3b_sync(s3b_ctx* ctx);
+/* Options: "frames_per_pass" (encoder micro-batch, default 8). */
+int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value);
+
+/* ---------------------------------------------------------------- model */
+
+/* Loads the encoder / memory-attention weights of a .ggml file (SAM 3 or
+ * SAM 2.x Hiera; f32, f16, q4_0, q4_1, q8_0 tensors) onto the device.
+ * Replaces sam3_load_model + sam3_load_tensors (sam3.cpp:3091-3344);
+ * tensors outside the engine's scope are skipped. */
+int s3b_load_model(s3b_ctx* ctx, const char* path);
+
+/* info[0] = 1 for SAM 2 (Hiera) else 0, info[1] = img_size, info[2] = number
+ * of backbone blocks, info[3] = backbone embed dim, info[4] = neck dim,
+ * info[5] = memory-attention layers (0 if absent), info[6] = device bytes of
+ * weights (low 31 bits, MiB). */
+int s3b_model_info(s3b_ctx* ctx, int32_t* info, int n);
+
+/* ---------------------------------------------------------------- encoder */
+
+/* Encodes n_frames uint8 HWC frames of img_size^2 (host memory): SAM 3
+ * normalisation (p/255-0.5)/0.5 or SAM 2 ImageNet mean/std
+ * (sam3.cpp:3486-3544), then backbone + neck. Replaces sam3_encode_image
+ * (sam3.cpp:6024-6212, 5857-6018) for frames already at the model size. */
+int s3b_encode_u8(s3b_ctx* ctx, const uint8_t* frames_hwc, int n_frames, int img_size, int flags);
+
+/* Same from preprocessed f32 CHW frames in host memory; replaces
+ * sam3_encode_image_from_preprocessed (sam3.h:426-435, sam3.cpp:6997-7481). */
+int s3b_encode_chw(s3b_ctx* ctx, const float* frames_chw, int n_frames, int img_size, int flags);
+
+/* Same with device pointers (frames already resident in HBM). */
+int s3b_encode_u8_device(s3b_ctx* ctx, const uint8_t* d_frames_hwc, int n_frames, int img_size, int flags);
+int s3b_encode_chw_device(s3b_ctx* ctx, const float* d_frames_chw, int n_frames, int img_size, int flags);
+
+/* Shape (ggml order ne[0..3]) of an output of the last encode call. Names
+ * follow sam3_dump_state_tensor (sam3.cpp:14334-14376): "vit_output",
+ * "neck_trk_0".."neck_trk_3", "neck_det_0".."neck_det_3", "neck_trk_pe_i".
+ * For SAM 2 the FPN levels are "neck_trk_0".."neck_trk_2". */
+int s3b_output_shape(s3b_ctx* ctx, const char* name, int64_t ne[4]);
+/* Copies frame `frame` of an output to host memory (n floats). */
+int s3b_output_copy(s3b_ctx* ctx, const char* name, int frame, float* dst, int64_t n);
+/* Device pointer of frame `frame` of an output (valid until the next encode). */
+int s3b_output_device_ptr(s3b_ctx* ctx, const char* name, int frame, const float** dptr);
+
+/* ---------------------------------------------------------------- memory attention */
+
+/* Memory attention (sam3_build_mem_attn_graph, sam3.cpp:9224-9337) on one
+ * feature map of side `feat` (N = feat^2 tokens, D = 256):
+ *   curr       [N][D]  current-frame features (neck_trk level 2, channel-last)
+ *   src_pos    [N][D]  sinusoidal PE of the current tokens
+ *   prompt     [M][64] memory tokens (spatial slots then object-pointer tokens)
+ *   prompt_pos [M][64]
+ *   n_ptr_tokens: trailing pointer tokens excluded from RoPE
+ *   out        [N][D]
+ * RoPE tables (axial, dim 256, theta 1e4, feat x feat; sam3.cpp:11126-11169)
+ * are computed by the engine. `device_ptrs` = 1 if all pointers are device
+ * pointers, 0 if they are host pointers. */
+int s3b_mem_attn(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const float* prompt,
+                 const float* prompt_pos, int m_total, int n_ptr_tokens, float* out, int device_ptrs);
+
+/* ---------------------------------------------------------------- operators (device pointers) */
+
+/* out[M][N] = act(A[M][K] * B[N][K]^T + bias) (+ resid), A/B f16 row-major
+ * with row strides lda/ldb (multiples of 8 elements); out f16 or f32 with row
+ * stride ldo; resid f32 [M][ldr] or NULL. Replaces ggml_mul_mat + ggml_add
+ * (+ activation) pairs such as sam3.cpp:3738-3739, 3792-3796. */
+int s3b_op_gemm(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
+                const float* bias, int act, void* out, int out_f32, int64_t ldo, const float* resid, int64_t ldr);
+
+/* softmax(q k^T * scale) v for q [B*H][nq][d], k/v [B*H][nk][d] (f16),
+ * out [B][nq][H*d] f16. Replaces ggml_flash_attn_ext (sam3.cpp:3774, 4395,
+ * 9267, 9312) with no mask. d in {64, 80, 96, 128, 256}. */
+int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, void* out, int batch, int heads,
+                     int nq, int nk, int d, float scale);
+
+/* LayerNorm over C of f32 rows: out = (x-mean)/sqrt(var+eps)*g + b, f16 or
+ * f32 out. Replaces ggml_norm + mul + add (sam3.cpp:1036-1060). */
+int s3b_op_layernorm(s3b_ctx* ctx, const float* x, void* out, int out_f32, int64_t rows, int C, const float* g,
+                     const float* b, float eps);
+
+/* Dequantises nrows rows of ne0 values of q4_0 / q4_1 / q8_0 blocks to f32,
+ * bit-exactly as ggml's type-traits to_float (sam3.cpp:1076-1077). */
+int s3b_op_dequantize(s3b_ctx* ctx, const void* src, int type, int64_t ne0, int64_t nrows, float* dst);
+
+/* ---------------------------------------------------------------- host format helpers */
+
+/* Bytes of one row of ne0 values of `type` (ggml_row_size, sam3.cpp:3133-3135). */
+int64_t s3b_row_size(int type, int64_t ne0);
+/* Quantises f32 rows to q4_0 / q4_1 / q8_0 with ggml's reference rounding
+ * (ggml_quantize_chunk as called by examples/quantize.cpp:244-245). */
+int s3b_quantize_rows(int type, const float* src, int64_t ne0, int64_t nrows, void* dst);
+/* Host dequantisation (same values as s3b_op_dequantize). */
+int s3b_dequantize_rows(int type, const void* src, int64_t ne0, int64_t nrows, float* dst);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SAM3_B200_H */

@@ -1,0 +1,160 @@
+"""Shared numpy building blocks of the oracle (test infrastructure only).
+
+Each function restates the ggml op sequence the reference builds; the
+`f16_inputs` switch rounds GEMM operands to f16 the way ggml's CPU mul_mat
+does for f16 weights (sam3.cpp:6635-6636 host reference rounds its input).
+"""
+import numpy as np
+
+
+def f16r(x):
+    return np.asarray(x, np.float32).astype(np.float16).astype(np.float32)
+
+
+def layer_norm(x, w, b, eps):
+    """ggml_norm + mul + add over the last dim (sam3.cpp:1036-1060); f64 statistics."""
+    xd = x.astype(np.float64)
+    mean = xd.mean(axis=-1, keepdims=True)
+    var = ((xd - mean) ** 2).mean(axis=-1, keepdims=True)
+    y = (xd - mean) / np.sqrt(var + eps)
+    y = y * w.astype(np.float64)
+    if b is not None:
+        y = y + b.astype(np.float64)
+    return y.astype(np.float32)
+
+
+def linear(x, w, b=None, f16_inputs=False):
+    """ggml_mul_mat(w, x) + b: x [..., K], w [N, K] -> [..., N] (f32 accumulate)."""
+    if f16_inputs:
+        x, w = f16r(x), f16r(w)
+    y = np.matmul(x.reshape(-1, x.shape[-1]).astype(np.float32), w.astype(np.float32).T)
+    if b is not None:
+        y = y + b.astype(np.float32)
+    return y.reshape(*x.shape[:-1], w.shape[0]).astype(np.float32)
+
+
+def gelu_erf(x):
+    from scipy.special import erf
+    xd = x.astype(np.float64)
+    return (0.5 * xd * (1.0 + erf(xd / np.sqrt(2.0)))).astype(np.float32)
+
+
+def gelu_tanh(x):
+    xd = x.astype(np.float64)
+    return (0.5 * xd * (1.0 + np.tanh(0.7978845608028654 * (xd + 0.044715 * xd ** 3)))).astype(np.float32)
+
+
+def relu(x):
+    return np.maximum(x, 0).astype(np.float32)
+
+
+def rope(x, cis):
+    """sam3_apply_rope (sam3.cpp:3667-3706): x [..., N, D] pairs (2i, 2i+1), cis [N, D/2, 2]."""
+    xr = x[..., 0::2]
+    xi = x[..., 1::2]
+    c = cis[..., 0]
+    s = cis[..., 1]
+    out = np.empty_like(x)
+    out[..., 0::2] = xr * c - xi * s
+    out[..., 1::2] = xr * s + xi * c
+    return out
+
+
+def attention(q, k, v, scale, f16_inputs=False):
+    """softmax(q k^T * scale) v for q [B, Nq, D], k/v [B, Nk, D] (no mask), f32 / f64 softmax."""
+    if f16_inputs:
+        q, k, v = f16r(q), f16r(k), f16r(v)
+    out = np.empty((q.shape[0], q.shape[1], v.shape[2]), np.float32)
+    for b in range(q.shape[0]):
+        # chunk queries to bound memory for the global / memory-attention sizes
+        for s in range(0, q.shape[1], 2048):
+            sc = np.matmul(q[b, s:s + 2048], k[b].T).astype(np.float64) * scale
+            sc -= sc.max(axis=-1, keepdims=True)
+            p = np.exp(sc)
+            p /= p.sum(axis=-1, keepdims=True)
+            out[b, s:s + 2048] = np.matmul(p.astype(np.float32), v[b])
+    return out
+
+
+def window_partition(x, ws):
+    """[B, H, W, C] -> ([B*nw, ws, ws, C], (Hp, Wp)); zero pad after the norm (sam3.cpp:4190-4228)."""
+    B, H, W, C = x.shape
+    ph = (ws - H % ws) % ws
+    pw = (ws - W % ws) % ws
+    if ph or pw:
+        x = np.pad(x, ((0, 0), (0, ph), (0, pw), (0, 0)))
+    Hp, Wp = H + ph, W + pw
+    x = x.reshape(B, Hp // ws, ws, Wp // ws, ws, C).transpose(0, 1, 3, 2, 4, 5).reshape(-1, ws, ws, C)
+    return x, (Hp, Wp)
+
+
+def window_unpartition(w, ws, pad_hw, hw):
+    """Inverse of window_partition (sam3.cpp:4240-4277)."""
+    Hp, Wp = pad_hw
+    H, W = hw
+    B = w.shape[0] // ((Hp // ws) * (Wp // ws))
+    x = w.reshape(B, Hp // ws, Wp // ws, ws, ws, -1).transpose(0, 1, 3, 2, 4, 5).reshape(B, Hp, Wp, -1)
+    return x[:, :H, :W, :]
+
+
+def maxpool2(x):
+    """2x2/s2 max pool on [B, H, W, C] (floor), ggml_pool_2d MAX k=2 s=2 p=0."""
+    B, H, W, C = x.shape
+    H2, W2 = H // 2, W // 2
+    x = x[:, :2 * H2, :2 * W2, :].reshape(B, H2, 2, W2, 2, C)
+    return x.max(axis=(2, 4))
+
+
+def conv2d_cl(x, w, b, stride=1, pad=0, f16_inputs=False):
+    """Conv2d on channel-last x [B, H, W, Cin] with PyTorch weight [Cout, Cin, k, k]."""
+    B, H, W, Cin = x.shape
+    Cout, _, k, _ = w.shape
+    xp = np.pad(x, ((0, 0), (pad, pad), (pad, pad), (0, 0))) if pad else x
+    OH = (H + 2 * pad - k) // stride + 1
+    OW = (W + 2 * pad - k) // stride + 1
+    wf = w.transpose(2, 3, 1, 0).reshape(k * k * Cin, Cout)  # (ky, kx, ci) x co
+    if f16_inputs:
+        xp, wf = f16r(xp), f16r(wf)
+    out = np.zeros((B, OH, OW, Cout), np.float32)
+    for ky in range(k):
+        for kx in range(k):
+            patch = xp[:, ky:ky + stride * OH:stride, kx:kx + stride * OW:stride, :]
+            out += np.matmul(patch.reshape(-1, Cin), wf[(ky * k + kx) * Cin:(ky * k + kx + 1) * Cin]).reshape(
+                B, OH, OW, Cout)
+    if b is not None:
+        out += b.astype(np.float32)
+    return out
+
+
+def deconv2x2_cl(x, w, b, f16_inputs=False):
+    """ConvTranspose2d k=2 s=2 on channel-last x [B, H, W, Cin], weight [Cin, Cout, 2, 2]."""
+    B, H, W, Cin = x.shape
+    Cout = w.shape[1]
+    if f16_inputs:
+        x, w = f16r(x), f16r(w)
+    out = np.zeros((B, 2 * H, 2 * W, Cout), np.float32)
+    xf = x.reshape(-1, Cin)
+    for ky in range(2):
+        for kx in range(2):
+            out[:, ky::2, kx::2, :] = np.matmul(xf, w[:, :, ky, kx]).reshape(B, H, W, Cout)
+    if b is not None:
+        out += b.astype(np.float32)
+    return out
+
+
+def sine_pe_2d(H, W, d_model):
+    """sam3_sinusoidal_pe_2d (sam3.cpp:3597-3633) as channel-last [H, W, d_model]."""
+    half = d_model // 2
+    scale = np.float32(2.0 * np.pi)
+    y = ((np.arange(H, dtype=np.float32) + 1) / np.float32(H)) * scale
+    x = ((np.arange(W, dtype=np.float32) + 1) / np.float32(W)) * scale
+    i = np.arange(half)
+    dim_t = np.power(np.float32(10000.0), (i & ~1).astype(np.float32) / np.float32(half)).astype(np.float32)
+    py = y[:, None] / dim_t[None, :]
+    px = x[:, None] / dim_t[None, :]
+    vy = np.where(i % 2 == 0, np.sin(py), np.cos(py)).astype(np.float32)
+    vx = np.where(i % 2 == 0, np.sin(px), np.cos(px)).astype(np.float32)
+    pe = np.empty((H, W, d_model), np.float32)
+    pe[:, :, :half] = vy[:, None, :]
+    pe[:, :, half:] = vx[None, :, :]
+    return pe

@@ -1,0 +1,279 @@
+"""B200 encoder engine for sam3.cpp — Python host side over the C ABI.
+
+The product is ``libsam3b200.so`` (sm_100a kernels + C++14 host engine) built
+from ``csrc/`` and declared in ``include/sam3_b200.h``. This module binds it
+with ctypes and adds the Python-side plumbing a caller needs: device buffers
+come from PyTorch (``tensor.data_ptr()``), the engine owns its own weights
+and workspace.
+
+The directory is named ``sam3.cpp_b200``; import it through ``load()`` in
+``__graft_entry__.py`` / ``tests/conftest.py`` which registers it as the
+module ``sam3_b200``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "libsam3b200.so")
+CSRC = os.path.join(PKG_DIR, "csrc")
+
+S3B_F32, S3B_F16, S3B_Q4_0, S3B_Q4_1, S3B_Q8_0 = 0, 1, 2, 3, 8
+ACT_NONE, ACT_GELU_ERF, ACT_GELU_TANH, ACT_RELU = 0, 1, 2, 3
+ENCODE_NO_NECK, ENCODE_NO_DET = 1, 2
+
+ERRORS = {
+    0: "S3B_OK", -1: "S3B_ERR_ARG", -2: "S3B_ERR_IO", -3: "S3B_ERR_FORMAT", -4: "S3B_ERR_CUDA",
+    -5: "S3B_ERR_STATE", -6: "S3B_ERR_UNSUPPORTED", -7: "S3B_ERR_DEVICE", -8: "S3B_ERR_OOM",
+}
+
+# Every symbol declared in include/sam3_b200.h: (name, restype, argtypes)
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+_F = ctypes.c_float
+_S = ctypes.c_char_p
+SYMBOLS = [
+    ("s3b_create", _I, [_I, ctypes.POINTER(_P)]),
+    ("s3b_destroy", None, [_P]),
+    ("s3b_last_error", _S, [_P]),
+    ("s3b_set_stream", _I, [_P, _P]),
+    ("s3b_sync", _I, [_P]),
+    ("s3b_set_option", _I, [_P, _S, _I64]),
+    ("s3b_load_model", _I, [_P, _S]),
+    ("s3b_model_info", _I, [_P, ctypes.POINTER(ctypes.c_int32), _I]),
+    ("s3b_encode_u8", _I, [_P, _P, _I, _I, _I]),
+    ("s3b_encode_chw", _I, [_P, _P, _I, _I, _I]),
+    ("s3b_encode_u8_device", _I, [_P, _P, _I, _I, _I]),
+    ("s3b_encode_chw_device", _I, [_P, _P, _I, _I, _I]),
+    ("s3b_output_shape", _I, [_P, _S, ctypes.POINTER(_I64)]),
+    ("s3b_output_copy", _I, [_P, _S, _I, _P, _I64]),
+    ("s3b_output_device_ptr", _I, [_P, _S, _I, ctypes.POINTER(_P)]),
+    ("s3b_mem_attn", _I, [_P, _P, _P, _I, _P, _P, _I, _I, _P, _I]),
+    ("s3b_op_gemm", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _I, _P, _I, _I64, _P, _I64]),
+    ("s3b_op_attention", _I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F]),
+    ("s3b_op_layernorm", _I, [_P, _P, _P, _I, _I64, _I, _P, _P, _F]),
+    ("s3b_op_dequantize", _I, [_P, _P, _I, _I64, _I64, _P]),
+    ("s3b_row_size", _I64, [_I, _I64]),
+    ("s3b_quantize_rows", _I, [_I, _P, _I64, _I64, _P]),
+    ("s3b_dequantize_rows", _I, [_I, _P, _I64, _I64, _P]),
+]
+
+_lib = None
+
+
+def build(verbose: bool = False) -> str:
+    """Compiles libsam3b200.so for sm_100a with the Makefile in csrc/."""
+    cmd = ["make", "-C", CSRC, "-j", str(min(8, os.cpu_count() or 1))]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or r.returncode != 0:
+        print(r.stdout[-4000:], r.stderr[-4000:])
+    if r.returncode != 0:
+        raise RuntimeError("building libsam3b200.so failed")
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """Loads the in-tree shared library (fails loudly when it is missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: run build() (make -C {CSRC}) first")
+    L = ctypes.CDLL(LIB_PATH)
+    for name, res, args in SYMBOLS:
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+class S3BError(RuntimeError):
+    pass
+
+
+def _ptr(x) -> int | None:
+    """Raw address of a torch tensor, numpy array, int, or None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data
+    raise TypeError(type(x))
+
+
+# ---------------------------------------------------------------- host format helpers
+def row_size(qtype: int, ne0: int) -> int:
+    return int(lib().s3b_row_size(qtype, ne0))
+
+
+def quantize_rows(qtype: int, x: np.ndarray) -> np.ndarray:
+    """Quantises f32 rows [nrows, ne0] to raw ggml blocks (uint8 [nrows, row_size])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    ne0 = x.shape[-1]
+    nrows = x.size // ne0
+    out = np.empty((nrows, row_size(qtype, ne0)), dtype=np.uint8)
+    rc = lib().s3b_quantize_rows(qtype, x.ctypes.data, ne0, nrows, out.ctypes.data)
+    if rc != 0:
+        raise S3BError(f"s3b_quantize_rows: {ERRORS.get(rc, rc)}")
+    return out
+
+
+def dequantize_rows(qtype: int, raw: np.ndarray, ne0: int) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    nrows = raw.size // row_size(qtype, ne0)
+    out = np.empty((nrows, ne0), dtype=np.float32)
+    rc = lib().s3b_dequantize_rows(qtype, raw.ctypes.data, ne0, nrows, out.ctypes.data)
+    if rc != 0:
+        raise S3BError(f"s3b_dequantize_rows: {ERRORS.get(rc, rc)}")
+    return out
+
+
+# ---------------------------------------------------------------- engine
+class Engine:
+    """One engine context on one CUDA device (s3b_create / s3b_destroy)."""
+
+    def __init__(self, device: int = 0):
+        self._L = lib()
+        h = ctypes.c_void_p()
+        rc = self._L.s3b_create(device, ctypes.byref(h))
+        if rc != 0:
+            raise S3BError(f"s3b_create({device}) failed: {ERRORS.get(rc, rc)}")
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._L.s3b_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int, what: str):
+        if rc != 0:
+            msg = self._L.s3b_last_error(self.h)
+            raise S3BError(f"{what}: {ERRORS.get(rc, rc)}: {msg.decode() if msg else ''}")
+
+    def last_error(self) -> str:
+        m = self._L.s3b_last_error(self.h)
+        return m.decode() if m else ""
+
+    def set_stream(self, stream_handle: int | None):
+        self._check(self._L.s3b_set_stream(self.h, stream_handle), "s3b_set_stream")
+
+    def sync(self):
+        self._check(self._L.s3b_sync(self.h), "s3b_sync")
+
+    def set_option(self, key: str, value: int):
+        self._check(self._L.s3b_set_option(self.h, key.encode(), value), "s3b_set_option")
+
+    def load_model(self, path: str):
+        self._check(self._L.s3b_load_model(self.h, path.encode()), "s3b_load_model")
+
+    def model_info(self) -> dict:
+        buf = (ctypes.c_int32 * 7)()
+        self._check(self._L.s3b_model_info(self.h, buf, 7), "s3b_model_info")
+        keys = ["is_sam2", "img_size", "n_blocks", "embed_dim", "neck_dim", "mem_attn_layers", "weights_mib"]
+        return dict(zip(keys, list(buf)))
+
+    # -- encoder
+    def encode_u8(self, frames, flags: int = 0):
+        """frames: uint8 [n, S, S, 3] numpy (host) or torch CUDA tensor (device)."""
+        n, S = int(frames.shape[0]), int(frames.shape[1])
+        if hasattr(frames, "is_cuda") and frames.is_cuda:
+            rc = self._L.s3b_encode_u8_device(self.h, frames.data_ptr(), n, S, flags)
+        else:
+            frames = np.ascontiguousarray(frames, dtype=np.uint8)
+            rc = self._L.s3b_encode_u8(self.h, frames.ctypes.data, n, S, flags)
+        self._check(rc, "s3b_encode_u8")
+
+    def encode_chw(self, frames, flags: int = 0):
+        """frames: f32 [n, 3, S, S] numpy (host) or torch CUDA tensor (device)."""
+        n, S = int(frames.shape[0]), int(frames.shape[2])
+        if hasattr(frames, "is_cuda") and frames.is_cuda:
+            rc = self._L.s3b_encode_chw_device(self.h, frames.data_ptr(), n, S, flags)
+        else:
+            frames = np.ascontiguousarray(frames, dtype=np.float32)
+            rc = self._L.s3b_encode_chw(self.h, frames.ctypes.data, n, S, flags)
+        self._check(rc, "s3b_encode_chw")
+
+    def output_shape(self, name: str) -> tuple:
+        ne = (ctypes.c_int64 * 4)()
+        self._check(self._L.s3b_output_shape(self.h, name.encode(), ne), "s3b_output_shape")
+        return tuple(ne)
+
+    def output(self, name: str, frame: int = 0) -> np.ndarray:
+        """Frame `frame` of an output as numpy [H][W][C] (ggml [C, W, H])."""
+        ne = self.output_shape(name)
+        out = np.empty((ne[2], ne[1], ne[0]), dtype=np.float32)
+        self._check(self._L.s3b_output_copy(self.h, name.encode(), frame, out.ctypes.data, out.size),
+                    "s3b_output_copy")
+        return out
+
+    def output_device_ptr(self, name: str, frame: int = 0) -> int:
+        p = ctypes.c_void_p()
+        self._check(self._L.s3b_output_device_ptr(self.h, name.encode(), frame, ctypes.byref(p)),
+                    "s3b_output_device_ptr")
+        return int(p.value)
+
+    # -- memory attention
+    def mem_attn(self, curr, src_pos, feat: int, prompt, prompt_pos, n_ptr_tokens: int, out=None):
+        """All numpy (host) or all torch CUDA tensors (device)."""
+        dev = hasattr(curr, "is_cuda") and curr.is_cuda
+        m_total = int(prompt.shape[0])
+        if out is None:
+            if dev:
+                import torch
+                out = torch.empty_like(curr)
+            else:
+                out = np.empty_like(np.asarray(curr, dtype=np.float32))
+        if not dev:
+            curr = np.ascontiguousarray(curr, dtype=np.float32)
+            src_pos = np.ascontiguousarray(src_pos, dtype=np.float32)
+            prompt = np.ascontiguousarray(prompt, dtype=np.float32)
+            prompt_pos = np.ascontiguousarray(prompt_pos, dtype=np.float32)
+        rc = self._L.s3b_mem_attn(self.h, _ptr(curr), _ptr(src_pos), feat, _ptr(prompt), _ptr(prompt_pos),
+                                  m_total, n_ptr_tokens, _ptr(out), 1 if dev else 0)
+        self._check(rc, "s3b_mem_attn")
+        return out
+
+    # -- operators on device pointers (torch CUDA tensors)
+    def gemm(self, A, B, out, bias=None, act=ACT_NONE, resid=None, K=None):
+        M, lda = A.shape[0], A.stride(0)
+        N, ldb = B.shape[0], B.stride(0)
+        K = K if K is not None else A.shape[1]
+        out_f32 = 1 if out.dtype.itemsize == 4 else 0
+        rc = self._L.s3b_op_gemm(self.h, A.data_ptr(), lda, B.data_ptr(), ldb, M, N, K, _ptr(bias), act,
+                                 out.data_ptr(), out_f32, out.stride(0), _ptr(resid),
+                                 resid.stride(0) if resid is not None else 0)
+        self._check(rc, "s3b_op_gemm")
+
+    def attention(self, q, k, v, out, scale: float):
+        B, H, nq, d = q.shape
+        nk = k.shape[2]
+        rc = self._L.s3b_op_attention(self.h, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, H, nq,
+                                      nk, d, scale)
+        self._check(rc, "s3b_op_attention")
+
+    def layernorm(self, x, out, g, b, eps: float):
+        rows, C = x.shape
+        out_f32 = 1 if out.dtype.itemsize == 4 else 0
+        rc = self._L.s3b_op_layernorm(self.h, x.data_ptr(), out.data_ptr(), out_f32, rows, C, g.data_ptr(),
+                                      _ptr(b), eps)
+        self._check(rc, "s3b_op_layernorm")
+
+    def dequantize(self, raw, qtype: int, ne0: int, nrows: int, out):
+        rc = self._L.s3b_op_dequantize(self.h, raw.data_ptr(), qtype, ne0, nrows, out.data_ptr())
+        self._check(rc, "s3b_op_dequantize")

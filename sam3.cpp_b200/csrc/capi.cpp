@@ -1,0 +1,435 @@
+// extern "C" entry points of the engine (include/sam3_b200.h).
+#include <math.h>
+#include <string.h>
+
+#include <string>
+
+#include "../../include/sam3_b200.h"
+#include "engine.h"
+
+namespace s3b {
+void quantize_row_host(int type, const float* x, int64_t n, uint8_t* dst);
+int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const float* prompt,
+                 const float* prompt_pos, int m_total, int n_ptr, float* out);
+}  // namespace s3b
+
+using namespace s3b;
+
+s3b::DevBuf* s3b_ctx::buf(const std::string& name, size_t bytes, int* rc) {
+  auto& b = ws[name];
+  if (!b) b = std::make_shared<DevBuf>();
+  if (b->reserve(bytes)) {
+    *rc = set_error(this, kErrOOM, "workspace '%s': cudaMalloc(%zu) failed", name.c_str(), bytes);
+    return b.get();
+  }
+  return b.get();
+}
+
+namespace {
+
+int ctx_enter(s3b_ctx* ctx) {
+  if (!ctx) return kErrArg;
+  if (cudaSetDevice(ctx->device) != cudaSuccess) return set_error(ctx, kErrCuda, "cudaSetDevice(%d)", ctx->device);
+  return kOk;
+}
+
+// Reads the device error word; a non-zero value means a bounded wait expired.
+int read_dev_err(s3b_ctx* ctx) {
+  int h = 0;
+  if (cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "reading the device error word: %s", cudaGetErrorString(cudaGetLastError()));
+  if (h != 0) {
+    cudaMemset(ctx->d_err, 0, sizeof(int));
+    return set_error(ctx, kErrDevice, "device-side wait timed out (code %d)", h);
+  }
+  return kOk;
+}
+
+// Sinusoidal 2D PE (sam3_sinusoidal_pe_2d, sam3.cpp:3597-3633), channel-last [H][W][d].
+void sine_pe_2d(int H, int W, int d_model, float* pe) {
+  const int half = d_model / 2;
+  const float scale = 2.0f * (float)M_PI;
+  for (int y = 0; y < H; ++y)
+    for (int x = 0; x < W; ++x) {
+      const float py = ((float)(y + 1) / (float)H) * scale;
+      const float px = ((float)(x + 1) / (float)W) * scale;
+      for (int i = 0; i < half; ++i) {
+        const int paired = i & ~1;
+        const float dim_t = powf(10000.0f, (float)paired / (float)half);
+        float vx, vy;
+        if (i % 2 == 0) {
+          vx = sinf(px / dim_t);
+          vy = sinf(py / dim_t);
+        } else {
+          vx = cosf(px / dim_t);
+          vy = cosf(py / dim_t);
+        }
+        pe[((size_t)y * W + x) * d_model + i] = vy;
+        pe[((size_t)y * W + x) * d_model + i + half] = vx;
+      }
+    }
+}
+
+struct OutRef {
+  const float* dev = nullptr;  // frame 0
+  int64_t ne[4] = {1, 1, 1, 1};
+  int64_t frame_elems = 0;
+  bool is_pe = false;
+  int pe_size = 0;
+};
+
+int resolve_output(s3b_ctx* ctx, const char* name, OutRef& r) {
+  const Outputs& O = ctx->out;
+  const HParams& hp = ctx->model.hp;
+  std::string n(name ? name : "");
+  if (O.n_frames <= 0) return set_error(ctx, kErrState, "no encode has run");
+  if (n == "vit_output" && O.backbone && !hp.is_sam2) {
+    const int G = hp.n_img_embd();
+    r.dev = O.backbone->as<float>();
+    r.ne[0] = hp.vit_embed_dim;
+    r.ne[1] = G;
+    r.ne[2] = G;
+    r.frame_elems = (int64_t)G * G * hp.vit_embed_dim;
+    return kOk;
+  }
+  for (int i = 0; i < 4; ++i) {
+    const std::string si = std::to_string(i);
+    if (n == "neck_trk_" + si && i < O.n_fpn) {
+      r.dev = O.fpn[i]->as<float>();
+      r.ne[0] = hp.neck_dim;
+      r.ne[1] = r.ne[2] = O.fpn_size[i];
+      r.frame_elems = (int64_t)O.fpn_size[i] * O.fpn_size[i] * hp.neck_dim;
+      return kOk;
+    }
+    if (n == "neck_det_" + si && i < O.n_det) {
+      r.dev = O.det[i]->as<float>();
+      r.ne[0] = hp.neck_dim;
+      r.ne[1] = r.ne[2] = O.fpn_size[i];
+      r.frame_elems = (int64_t)O.fpn_size[i] * O.fpn_size[i] * hp.neck_dim;
+      return kOk;
+    }
+    if ((n == "neck_trk_pe_" + si || n == "neck_det_pe_" + si) && i < O.n_fpn) {
+      r.is_pe = true;
+      r.pe_size = O.fpn_size[i];
+      r.ne[0] = hp.neck_dim;
+      r.ne[1] = r.ne[2] = O.fpn_size[i];
+      r.frame_elems = (int64_t)O.fpn_size[i] * O.fpn_size[i] * hp.neck_dim;
+      return kOk;
+    }
+  }
+  return set_error(ctx, kErrArg, "unknown output '%s'", n.c_str());
+}
+
+template <typename T>
+int stage_host(s3b_ctx* ctx, const T* host, size_t n, const char* name, T** dev) {
+  int rc = 0;
+  DevBuf* b = ctx->buf(name, n * sizeof(T), &rc);
+  if (rc) return rc;
+  if (cudaMemcpyAsync(b->p, host, n * sizeof(T), cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "host-to-device copy failed");
+  *dev = b->as<T>();
+  return kOk;
+}
+
+int encode_device_chw(s3b_ctx* ctx, const float* d_chw, int n_frames, int img_size, int flags) {
+  if (!ctx->model.loaded) return set_error(ctx, kErrState, "no model loaded");
+  if (n_frames <= 0) return set_error(ctx, kErrArg, "n_frames must be > 0");
+  if (img_size != ctx->model.hp.img_size)
+    return set_error(ctx, kErrUnsupported, "img_size %d != model img_size %d (resize is done by the caller)", img_size,
+                     ctx->model.hp.img_size);
+  return ctx->model.hp.is_sam2 ? hiera_encode(ctx, d_chw, n_frames, flags) : vit_encode(ctx, d_chw, n_frames, flags);
+}
+
+int encode_device_u8(s3b_ctx* ctx, const uint8_t* d_u8, int n_frames, int img_size, int flags) {
+  if (!ctx->model.loaded) return set_error(ctx, kErrState, "no model loaded");
+  if (n_frames <= 0 || img_size <= 0) return set_error(ctx, kErrArg, "bad frame count / size");
+  int rc = 0;
+  DevBuf* chw = ctx->buf("frames_chw", (size_t)n_frames * 3 * img_size * img_size * 4, &rc);
+  if (rc) return rc;
+  static const float m3[3] = {0.5f, 0.5f, 0.5f}, s3[3] = {0.5f, 0.5f, 0.5f};
+  static const float m2[3] = {0.485f, 0.456f, 0.406f}, s2[3] = {0.229f, 0.224f, 0.225f};
+  const bool sam2 = ctx->model.hp.is_sam2 != 0;
+  rc = preprocess_u8(d_u8, n_frames, img_size, img_size, sam2 ? m2 : m3, sam2 ? s2 : s3, chw->as<float>(),
+                     ctx->stream);
+  if (rc) return set_error(ctx, kErrCuda, "preprocess launch failed");
+  return encode_device_chw(ctx, chw->as<float>(), n_frames, img_size, flags);
+}
+
+}  // namespace
+
+extern "C" {
+
+int s3b_create(int device, s3b_ctx** out) {
+  if (!out) return kErrArg;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    fprintf(stderr, "s3b: no CUDA device %d (count %d)\n", device, n);
+    return kErrCuda;
+  }
+  s3b_ctx* ctx = new s3b_ctx();
+  ctx->device = device;
+  if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess || cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess) {
+    fprintf(stderr, "s3b: context creation failed on device %d\n", device);
+    delete ctx;
+    return kErrCuda;
+  }
+  ctx->own_stream = true;
+  *out = ctx;
+  return kOk;
+}
+
+void s3b_destroy(s3b_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  ctx->ws.clear();
+  ctx->out = Outputs();
+  ctx->model = Model();
+  if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+const char* s3b_last_error(const s3b_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
+
+int s3b_set_stream(s3b_ctx* ctx, void* stream) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  cudaStreamSynchronize(ctx->stream);
+  if (stream) {
+    if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+    ctx->own_stream = false;
+    ctx->stream = reinterpret_cast<cudaStream_t>(stream);
+  } else if (!ctx->own_stream) {
+    cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    ctx->own_stream = true;
+  }
+  return kOk;
+}
+
+int s3b_sync(s3b_ctx* ctx) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return set_error(ctx, kErrCuda, "stream synchronize: %s", cudaGetErrorString(e));
+  return read_dev_err(ctx);
+}
+
+int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
+  if (!ctx || !key) return kErrArg;
+  const std::string k(key);
+  if (k == "frames_per_pass") {
+    if (value < 1 || value > 256) return set_error(ctx, kErrArg, "frames_per_pass out of range");
+    ctx->max_frames_per_pass = (int)value;
+    return kOk;
+  }
+  return set_error(ctx, kErrArg, "unknown option '%s'", key);
+}
+
+int s3b_load_model(s3b_ctx* ctx, const char* path) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!path) return set_error(ctx, kErrArg, "null path");
+  ctx->out = Outputs();
+  return load_model(ctx, path);
+}
+
+int s3b_model_info(s3b_ctx* ctx, int32_t* info, int n) {
+  if (!ctx || !info) return kErrArg;
+  if (!ctx->model.loaded) return set_error(ctx, kErrState, "no model loaded");
+  const HParams& hp = ctx->model.hp;
+  int32_t v[7] = {hp.is_sam2, hp.img_size, hp.is_sam2 ? (int32_t)ctx->model.hiera.size() : hp.vit_depth,
+                  hp.is_sam2 ? hp.hiera_embed_dim : hp.vit_embed_dim, hp.neck_dim,
+                  ctx->model.has_mem_attn ? hp.mem_attn_layers : 0,
+                  (int32_t)((ctx->model.device_bytes >> 20) & 0x7fffffff)};
+  for (int i = 0; i < n && i < 7; ++i) info[i] = v[i];
+  return kOk;
+}
+
+int s3b_encode_u8(s3b_ctx* ctx, const uint8_t* frames, int n_frames, int img_size, int flags) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!frames || n_frames <= 0 || img_size <= 0) return set_error(ctx, kErrArg, "bad arguments");
+  uint8_t* d = nullptr;
+  if ((rc = stage_host(ctx, frames, (size_t)n_frames * img_size * img_size * 3, "frames_u8", &d))) return rc;
+  return encode_device_u8(ctx, d, n_frames, img_size, flags);
+}
+
+int s3b_encode_chw(s3b_ctx* ctx, const float* chw, int n_frames, int img_size, int flags) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!chw || n_frames <= 0 || img_size <= 0) return set_error(ctx, kErrArg, "bad arguments");
+  float* d = nullptr;
+  if ((rc = stage_host(ctx, chw, (size_t)n_frames * 3 * img_size * img_size, "frames_chw_in", &d))) return rc;
+  return encode_device_chw(ctx, d, n_frames, img_size, flags);
+}
+
+int s3b_encode_u8_device(s3b_ctx* ctx, const uint8_t* d_frames, int n_frames, int img_size, int flags) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!d_frames) return set_error(ctx, kErrArg, "null frames");
+  return encode_device_u8(ctx, d_frames, n_frames, img_size, flags);
+}
+
+int s3b_encode_chw_device(s3b_ctx* ctx, const float* d_chw, int n_frames, int img_size, int flags) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!d_chw) return set_error(ctx, kErrArg, "null frames");
+  return encode_device_chw(ctx, d_chw, n_frames, img_size, flags);
+}
+
+int s3b_output_shape(s3b_ctx* ctx, const char* name, int64_t ne[4]) {
+  if (!ctx || !ne) return kErrArg;
+  OutRef r;
+  int rc = resolve_output(ctx, name, r);
+  if (rc) return rc;
+  for (int i = 0; i < 4; ++i) ne[i] = r.ne[i];
+  return kOk;
+}
+
+int s3b_output_copy(s3b_ctx* ctx, const char* name, int frame, float* dst, int64_t n) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  OutRef r;
+  if ((rc = resolve_output(ctx, name, r))) return rc;
+  if (!dst || n != r.frame_elems) return set_error(ctx, kErrArg, "output '%s' has %lld elements per frame", name,
+                                                   (long long)r.frame_elems);
+  if (r.is_pe) {
+    sine_pe_2d(r.pe_size, r.pe_size, (int)r.ne[0], dst);
+    return kOk;
+  }
+  if (frame < 0 || frame >= ctx->out.n_frames) return set_error(ctx, kErrArg, "frame %d out of range", frame);
+  if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return set_error(ctx, kErrCuda, "synchronize failed");
+  if ((rc = read_dev_err(ctx))) return rc;
+  if (cudaMemcpy(dst, r.dev + (size_t)frame * r.frame_elems, n * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "device-to-host copy failed");
+  return kOk;
+}
+
+int s3b_output_device_ptr(s3b_ctx* ctx, const char* name, int frame, const float** dptr) {
+  if (!ctx || !dptr) return kErrArg;
+  OutRef r;
+  int rc = resolve_output(ctx, name, r);
+  if (rc) return rc;
+  if (r.is_pe) return set_error(ctx, kErrArg, "PE outputs are host-computed; use s3b_output_copy");
+  if (frame < 0 || frame >= ctx->out.n_frames) return set_error(ctx, kErrArg, "frame out of range");
+  *dptr = r.dev + (size_t)frame * r.frame_elems;
+  return kOk;
+}
+
+int s3b_mem_attn(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const float* prompt,
+                 const float* prompt_pos, int m_total, int n_ptr_tokens, float* out, int device_ptrs) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!ctx->model.has_mem_attn) return set_error(ctx, kErrState, "model has no memory-attention weights");
+  if (!curr || !src_pos || !prompt || !prompt_pos || !out || feat <= 0 || m_total <= 0 || n_ptr_tokens < 0 ||
+      n_ptr_tokens > m_total)
+    return set_error(ctx, kErrArg, "bad memory-attention arguments");
+  const int D = ctx->model.hp.neck_dim, MD = ctx->model.hp.mem_out_dim;
+  const size_t N = (size_t)feat * feat;
+  if (device_ptrs) return mem_attn_run(ctx, curr, src_pos, feat, prompt, prompt_pos, m_total, n_ptr_tokens, out);
+  float *dc, *dp, *dpr, *dpp;
+  if ((rc = stage_host(ctx, curr, N * D, "ma_h_curr", &dc))) return rc;
+  if ((rc = stage_host(ctx, src_pos, N * D, "ma_h_pos", &dp))) return rc;
+  if ((rc = stage_host(ctx, prompt, (size_t)m_total * MD, "ma_h_prompt", &dpr))) return rc;
+  if ((rc = stage_host(ctx, prompt_pos, (size_t)m_total * MD, "ma_h_ppos", &dpp))) return rc;
+  DevBuf* o = ctx->buf("ma_h_out", N * D * 4, &rc);
+  if (rc) return rc;
+  if ((rc = mem_attn_run(ctx, dc, dp, feat, dpr, dpp, m_total, n_ptr_tokens, o->as<float>()))) return rc;
+  if (cudaMemcpyAsync(out, o->p, N * D * 4, cudaMemcpyDeviceToHost, ctx->stream) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "device-to-host copy failed");
+  return s3b_sync(ctx);
+}
+
+int s3b_op_gemm(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
+                const float* bias, int act, void* out, int out_f32, int64_t ldo, const float* resid, int64_t ldr) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!A || !B || !out || M <= 0 || N <= 0 || K <= 0) return set_error(ctx, kErrArg, "bad gemm arguments");
+  EpiParams ep;
+  ep.mode = EPI_STORE;
+  ep.act = act;
+  ep.bias = bias;
+  ep.out = out;
+  ep.out_f32 = out_f32;
+  ep.ldo = ldo;
+  ep.resid = resid;
+  ep.ldr = ldr;
+  rc = gemm_f16(reinterpret_cast<const __half*>(A), lda, reinterpret_cast<const __half*>(B), ldb, M, N, K, ep,
+                ctx->d_err, ctx->stream);
+  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "gemm launch failed (%d)", rc);
+  return kOk;
+}
+
+int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, void* out, int batch, int heads,
+                     int nq, int nk, int d, float scale) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!q || !k || !v || !out) return set_error(ctx, kErrArg, "null pointer");
+  AttnParams p;
+  p.q = reinterpret_cast<const __half*>(q);
+  p.k = reinterpret_cast<const __half*>(k);
+  p.v = reinterpret_cast<const __half*>(v);
+  p.o = reinterpret_cast<__half*>(out);
+  p.q_bh = (long long)nq * d;
+  p.k_bh = p.v_bh = (long long)nk * d;
+  p.q_n = p.k_n = p.v_n = d;
+  p.heads = heads;
+  p.nq = nq;
+  p.nk = nk;
+  p.o_b = (long long)nq * heads * d;
+  p.o_n = (long long)heads * d;
+  p.scale = scale;
+  rc = attention(p, d, batch * heads, ctx->stream);
+  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "attention launch failed (%d)", rc);
+  return kOk;
+}
+
+int s3b_op_layernorm(s3b_ctx* ctx, const float* x, void* out, int out_f32, int64_t rows, int C, const float* g,
+                     const float* b, float eps) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!x || !out || !g) return set_error(ctx, kErrArg, "null pointer");
+  RowMap id;
+  rc = layernorm(x, C, out, out_f32, C, rows, C, g, b, eps, id, ctx->stream);
+  if (rc) return set_error(ctx, kErrArg, "layernorm launch failed (%d)", rc);
+  return kOk;
+}
+
+int s3b_op_dequantize(s3b_ctx* ctx, const void* src, int type, int64_t ne0, int64_t nrows, float* dst) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  rc = dequant_rows(src, type, ne0, nrows, dst, 1, ne0, ctx->stream);
+  if (rc) return set_error(ctx, kErrArg, "dequantize launch failed (%d)", rc);
+  return kOk;
+}
+
+int64_t s3b_row_size(int type, int64_t ne0) { return qtype_row_bytes(type, ne0); }
+
+int s3b_quantize_rows(int type, const float* src, int64_t ne0, int64_t nrows, void* dst) {
+  if (!src || !dst || ne0 % 32 || nrows < 0) return kErrArg;
+  if (type != QT_Q4_0 && type != QT_Q4_1 && type != QT_Q8_0) return kErrUnsupported;
+  const int64_t rb = qtype_row_bytes(type, ne0);
+  for (int64_t r = 0; r < nrows; ++r)
+    quantize_row_host(type, src + r * ne0, ne0, reinterpret_cast<uint8_t*>(dst) + r * rb);
+  return kOk;
+}
+
+int s3b_dequantize_rows(int type, const void* src, int64_t ne0, int64_t nrows, float* dst) {
+  if (!src || !dst || ne0 % 32 || nrows < 0) return kErrArg;
+  if (type != QT_Q4_0 && type != QT_Q4_1 && type != QT_Q8_0) return kErrUnsupported;
+  FileTensor t;
+  t.dtype = type;
+  t.ne[0] = ne0;
+  t.ne[1] = nrows;
+  const int64_t bytes = qtype_row_bytes(type, ne0) * nrows;
+  t.data.assign(reinterpret_cast<const uint8_t*>(src), reinterpret_cast<const uint8_t*>(src) + bytes);
+  std::vector<float> f;
+  tensor_to_f32(t, f);
+  memcpy(dst, f.data(), f.size() * 4);
+  return kOk;
+}
+
+}  // extern "C"

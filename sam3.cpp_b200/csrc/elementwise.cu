@@ -1,0 +1,333 @@
+// Memory-bound kernels of the encoder hot path: LayerNorm (with the window
+// partition folded into its row gather), im2col for the convolutions that
+// run as tensor-core GEMMs, 2x2 max pools, q-pooling inside windows, image
+// normalisation, casts, and ggml block dequantisation.
+//
+// Reference ops replaced: ggml_norm + mul + add (sam3.cpp:1036-1060, 3825,
+// 4307, 4442), ggml_win_part / sam2_window_partition (3730, 4190-4228),
+// ggml_pool_2d MAX (3914, 4283-4292), sam3_preprocess_image /
+// sam2_preprocess_image normalisation (3486-3544), ggml type traits
+// to_float for Q4_0 / Q4_1 / Q8_0 (1065-1081, 3167-3174).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace s3b {
+namespace {
+
+constexpr int kMaxVec = 16;  // float4 per lane -> C <= 2048
+
+__global__ void layernorm_kernel(const float* __restrict__ x, long long ldx, void* __restrict__ y, int y_f32,
+                                 long long ldy, long long rows, int C, const float* __restrict__ gamma,
+                                 const float* __restrict__ beta, float eps, RowMap map) {
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const long long src = map_row(map, row);
+  if (src < 0) {
+    // padding row of a window partition: zeros (sam3.cpp:4199-4207 pads after the norm)
+    if (y_f32) {
+      float* yo = reinterpret_cast<float*>(y) + row * ldy;
+      for (int c = lane; c < C; c += 32) yo[c] = 0.f;
+    } else {
+      __half* yo = reinterpret_cast<__half*>(y) + row * ldy;
+      for (int c = lane; c < C; c += 32) yo[c] = __float2half_rn(0.f);
+    }
+    return;
+  }
+  const float* xr = x + src * ldx;
+  const int nvec = C >> 2;
+  float4 v[kMaxVec];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nvec) {
+      v[i] = *reinterpret_cast<const float4*>(xr + 4 * vi);
+      sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / (float)C;
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nvec) {
+      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+      var += (a * a + b * b) + (c * c + d * d);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  const float rstd = rsqrtf(var / (float)C + eps);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nvec) {
+      const float4 g = *reinterpret_cast<const float4*>(gamma + 4 * vi);
+      const float4 b = beta ? *reinterpret_cast<const float4*>(beta + 4 * vi) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 o;
+      o.x = (v[i].x - mean) * rstd * g.x + b.x;
+      o.y = (v[i].y - mean) * rstd * g.y + b.y;
+      o.z = (v[i].z - mean) * rstd * g.z + b.z;
+      o.w = (v[i].w - mean) * rstd * g.w + b.w;
+      if (y_f32) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + row * ldy + 4 * vi) = o;
+      } else {
+        __half2 h0 = __floats2half2_rn(o.x, o.y), h1 = __floats2half2_rn(o.z, o.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&h0);
+        u.y = *reinterpret_cast<uint32_t*>(&h1);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(y) + row * ldy + 4 * vi) = u;
+      }
+    }
+  }
+}
+
+__global__ void im2col_image_kernel(const float* __restrict__ img, int B, int Cin, int H, int W, int k, int stride,
+                                    int pad, int OH, int OW, __half* __restrict__ out, int Kpad) {
+  const long long total = (long long)B * OH * OW * Kpad;
+  const int K = Cin * k * k;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / Kpad;
+    const int col = (int)(i - row * Kpad);
+    float val = 0.f;
+    if (col < K) {
+      const int ci = col / (k * k);
+      const int rem = col - ci * k * k;
+      const int ky = rem / k, kx = rem - (rem / k) * k;
+      const long long b = row / ((long long)OH * OW);
+      const int pix = (int)(row - b * OH * OW);
+      const int oy = pix / OW, ox = pix - (pix / OW) * OW;
+      const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+      if (iy >= 0 && iy < H && ix >= 0 && ix < W) val = img[((b * Cin + ci) * H + iy) * (long long)W + ix];
+    }
+    out[i] = __float2half_rn(val);
+  }
+}
+
+__global__ void im2col_3x3_cl_kernel(const __half* __restrict__ x, int B, int H, int W, int C,
+                                     __half* __restrict__ out) {
+  const int c8n = C / 8;
+  const long long total = (long long)B * H * W * 9 * c8n;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int c8 = (int)(i % c8n);
+    const long long t = i / c8n;
+    const int tap = (int)(t % 9);
+    const long long pix = t / 9;
+    const long long b = pix / ((long long)H * W);
+    const int rem = (int)(pix - b * H * W);
+    const int y = rem / W, xx = rem - (rem / W) * W;
+    const int iy = y + tap / 3 - 1, ix = xx + tap % 3 - 1;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+      val = *reinterpret_cast<const uint4*>(x + ((b * H + iy) * W + ix) * C + c8 * 8);
+    *reinterpret_cast<uint4*>(out + pix * 9 * C + (long long)tap * C + c8 * 8) = val;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ T tmax(T a, T b);
+template <>
+__device__ __forceinline__ float tmax<float>(float a, float b) { return fmaxf(a, b); }
+template <>
+__device__ __forceinline__ __half tmax<__half>(__half a, __half b) { return __hmax(a, b); }
+
+template <typename T>
+__global__ void maxpool2_cl_kernel(const T* __restrict__ x, int B, int H, int W, int C, T* __restrict__ y) {
+  const int OH = H / 2, OW = W / 2;
+  const long long total = (long long)B * OH * OW * C;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const long long pix = i / C;
+    const long long b = pix / ((long long)OH * OW);
+    const int rem = (int)(pix - b * OH * OW);
+    const int oy = rem / OW, ox = rem - (rem / OW) * OW;
+    const T* p = x + ((b * H + 2 * oy) * W + 2 * ox) * C + c;
+    y[i] = tmax(tmax(p[0], p[C]), tmax(p[(long long)W * C], p[(long long)W * C + C]));
+  }
+}
+
+__global__ void qpool_kernel(const __half* __restrict__ q, long long nbh, int ws, int D, __half* __restrict__ out) {
+  const int wo = ws / 2;
+  const long long total = nbh * wo * wo * D;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(i % D);
+    const long long t = i / D;
+    const int l = (int)(t % (wo * wo));
+    const long long bh = t / (wo * wo);
+    const int oy = l / wo, ox = l - (l / wo) * wo;
+    const __half* p = q + bh * ws * ws * D;
+    const int i00 = (2 * oy) * ws + 2 * ox;
+    __half m = __hmax(__hmax(p[(long long)i00 * D + d], p[(long long)(i00 + 1) * D + d]),
+                      __hmax(p[(long long)(i00 + ws) * D + d], p[(long long)(i00 + ws + 1) * D + d]));
+    out[i] = m;
+  }
+}
+
+__global__ void preprocess_kernel(const uint8_t* __restrict__ img, int B, int H, int W, float m0, float m1, float m2,
+                                  float s0, float s1, float s2, float* __restrict__ out) {
+  const long long total = (long long)B * H * W;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long b = i / ((long long)H * W);
+    const long long pix = i - b * H * W;
+    const uint8_t* p = img + i * 3;
+    const long long plane = (long long)H * W;
+    out[(b * 3 + 0) * plane + pix] = ((float)p[0] / 255.0f - m0) / s0;
+    out[(b * 3 + 1) * plane + pix] = ((float)p[1] / 255.0f - m1) / s1;
+    out[(b * 3 + 2) * plane + pix] = ((float)p[2] / 255.0f - m2) / s2;
+  }
+}
+
+__global__ void cast_kernel(const float* __restrict__ x, long long n, __half* __restrict__ y) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    y[i] = __float2half_rn(x[i]);
+}
+
+__global__ void add_scaled_kernel(const float* __restrict__ a, const float* __restrict__ b, float s, long long n,
+                                  float* __restrict__ y) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    y[i] = a[i] + s * b[i];
+}
+
+// One thread per 32-value block. Values are produced exactly as ggml's
+// dequantisers define them: q4_0 (q - 8) * d, q4_1 q * d + m (multiply then
+// add, both rounded to f32), q8_0 q * d, with d and m the f16 fields.
+__global__ void dequant_kernel(const uint8_t* __restrict__ src, int qtype, long long ne0, long long nrows,
+                               long long row_bytes, void* __restrict__ dst, int dst_f32, long long ld_dst) {
+  const long long nb = ne0 / 32;
+  const long long total = nb * nrows;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / nb, blk = i - r * nb;
+    float v[32];
+    if (qtype == QT_Q4_0) {
+      const uint8_t* p = src + r * row_bytes + blk * 18;
+      const float d = __half2float(*reinterpret_cast<const __half*>(p));
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint8_t b = p[2 + j];
+        v[j] = (float)((int)(b & 0x0F) - 8) * d;
+        v[j + 16] = (float)((int)(b >> 4) - 8) * d;
+      }
+    } else if (qtype == QT_Q4_1) {
+      const uint8_t* p = src + r * row_bytes + blk * 20;
+      const float d = __half2float(*reinterpret_cast<const __half*>(p));
+      const float m = __half2float(*reinterpret_cast<const __half*>(p + 2));
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint8_t b = p[4 + j];
+        v[j] = __fadd_rn(__fmul_rn((float)(b & 0x0F), d), m);
+        v[j + 16] = __fadd_rn(__fmul_rn((float)(b >> 4), d), m);
+      }
+    } else {  // QT_Q8_0
+      const uint8_t* p = src + r * row_bytes + blk * 34;
+      const float d = __half2float(*reinterpret_cast<const __half*>(p));
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = (float)(reinterpret_cast<const int8_t*>(p + 2)[j]) * d;
+    }
+    if (dst_f32) {
+      float* o = reinterpret_cast<float*>(dst) + r * ld_dst + blk * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) o[j] = v[j];
+    } else {
+      __half* o = reinterpret_cast<__half*>(dst) + r * ld_dst + blk * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) o[j] = __float2half_rn(v[j]);
+    }
+  }
+}
+
+inline int grid_for(long long n, int threads) {
+  long long g = (n + threads - 1) / threads;
+  const long long cap = (long long)num_sms() * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (int)g;
+}
+
+inline int launch_ok() { return cudaGetLastError() == cudaSuccess ? 0 : -14; }
+
+}  // namespace
+
+int layernorm(const float* x, long long ldx, void* y, int y_f32, long long ldy, long long rows, int C,
+              const float* gamma, const float* beta, float eps, const RowMap& map, cudaStream_t st) {
+  if (C % 4 || C > 4 * 32 * kMaxVec || ldx % 4 || ldy % 4 || rows <= 0) return -1;
+  const int warps = 8;
+  const long long blocks = (rows + warps - 1) / warps;
+  layernorm_kernel<<<(unsigned)blocks, warps * 32, 0, st>>>(x, ldx, y, y_f32, ldy, rows, C, gamma, beta, eps, map);
+  return launch_ok();
+}
+
+int im2col_image(const float* img, int B, int Cin, int H, int W, int k, int stride, int pad, int OH, int OW,
+                 __half* out, int Kpad, cudaStream_t st) {
+  if (Kpad < Cin * k * k) return -1;
+  const long long n = (long long)B * OH * OW * Kpad;
+  im2col_image_kernel<<<grid_for(n, 256), 256, 0, st>>>(img, B, Cin, H, W, k, stride, pad, OH, OW, out, Kpad);
+  return launch_ok();
+}
+
+int im2col_3x3_cl(const __half* x, int B, int H, int W, int C, __half* out, cudaStream_t st) {
+  if (C % 8) return -1;
+  const long long n = (long long)B * H * W * 9 * (C / 8);
+  im2col_3x3_cl_kernel<<<grid_for(n, 256), 256, 0, st>>>(x, B, H, W, C, out);
+  return launch_ok();
+}
+
+int maxpool2_cl_f16(const __half* x, int B, int H, int W, int C, __half* y, cudaStream_t st) {
+  const long long n = (long long)B * (H / 2) * (W / 2) * C;
+  maxpool2_cl_kernel<__half><<<grid_for(n, 256), 256, 0, st>>>(x, B, H, W, C, y);
+  return launch_ok();
+}
+int maxpool2_cl_f32(const float* x, int B, int H, int W, int C, float* y, cudaStream_t st) {
+  const long long n = (long long)B * (H / 2) * (W / 2) * C;
+  maxpool2_cl_kernel<float><<<grid_for(n, 256), 256, 0, st>>>(x, B, H, W, C, y);
+  return launch_ok();
+}
+
+int qpool_windows(const __half* q, long long nbh, int ws, int D, __half* out, cudaStream_t st) {
+  const long long n = nbh * (ws / 2) * (ws / 2) * D;
+  qpool_kernel<<<grid_for(n, 256), 256, 0, st>>>(q, nbh, ws, D, out);
+  return launch_ok();
+}
+
+int preprocess_u8(const uint8_t* img, int B, int H, int W, const float mean[3], const float stdv[3], float* out,
+                  cudaStream_t st) {
+  const long long n = (long long)B * H * W;
+  preprocess_kernel<<<grid_for(n, 256), 256, 0, st>>>(img, B, H, W, mean[0], mean[1], mean[2], stdv[0], stdv[1],
+                                                      stdv[2], out);
+  return launch_ok();
+}
+
+int cast_f32_f16(const float* x, long long n, __half* y, cudaStream_t st) {
+  cast_kernel<<<grid_for(n, 256), 256, 0, st>>>(x, n, y);
+  return launch_ok();
+}
+
+int add_scaled_f32(const float* a, const float* b, float s, long long n, float* y, cudaStream_t st) {
+  add_scaled_kernel<<<grid_for(n, 256), 256, 0, st>>>(a, b, s, n, y);
+  return launch_ok();
+}
+
+long long qtype_row_bytes(int qtype, long long ne0) {
+  switch (qtype) {
+    case QT_F32: return ne0 * 4;
+    case QT_F16: return ne0 * 2;
+    case QT_Q4_0: return (ne0 / 32) * 18;
+    case QT_Q4_1: return (ne0 / 32) * 20;
+    case QT_Q8_0: return (ne0 / 32) * 34;
+    default: return -1;
+  }
+}
+
+int dequant_rows(const void* src, int qtype, long long ne0, long long nrows, void* dst, int dst_f32,
+                 long long ld_dst, cudaStream_t st) {
+  if (qtype != QT_Q4_0 && qtype != QT_Q4_1 && qtype != QT_Q8_0) return -1;
+  if (ne0 % 32 || nrows <= 0) return -2;
+  const long long n = (ne0 / 32) * nrows;
+  dequant_kernel<<<grid_for(n, 128), 128, 0, st>>>(reinterpret_cast<const uint8_t*>(src), qtype, ne0, nrows,
+                                                   qtype_row_bytes(qtype, ne0), dst, dst_f32, ld_dst);
+  return launch_ok();
+}
+
+}  // namespace s3b

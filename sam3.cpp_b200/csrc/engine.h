@@ -1,0 +1,229 @@
+// Internal host-side (C++14) structures of the B200 encoder engine.
+//
+// The engine replaces the ggml graph builders of sam3.cpp for the per-frame
+// backbone forward (SAM 3 ViT + SimpleFPN neck, SAM 2 Hiera + FPN neck) and
+// for memory attention, keeping the reference's .ggml files, dtypes and
+// ownership rules: the model owns device weights (sam3.cpp:884-887), the
+// context owns per-frame outputs (sam3.cpp:911-918) and frees them on destroy.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+
+namespace s3b {
+
+// ---------------------------------------------------------------- errors
+enum Status : int {
+  kOk = 0,
+  kErrArg = -1,
+  kErrIO = -2,
+  kErrFormat = -3,
+  kErrCuda = -4,
+  kErrState = -5,
+  kErrUnsupported = -6,
+  kErrDevice = -7,   // a kernel reported a device-side error (bounded wait expired)
+  kErrOOM = -8,
+};
+
+// ---------------------------------------------------------------- .ggml file
+// One tensor record of a .ggml file (sam3.cpp:3093-3143): ne in ggml order
+// (ne[0] contiguous), dtype in {0 F32, 1 F16, 2 Q4_0, 3 Q4_1, 8 Q8_0}.
+struct FileTensor {
+  std::string name;
+  int dtype = 0;
+  int n_dims = 0;
+  int64_t ne[4] = {1, 1, 1, 1};
+  std::vector<uint8_t> data;  // raw bytes as stored
+  int64_t nelements() const { return ne[0] * ne[1] * ne[2] * ne[3]; }
+};
+
+// Hyper-parameters read from the file header (subset of sam3_hparams,
+// sam3.cpp:70-242, needed by the encoder and memory attention).
+struct HParams {
+  int is_sam2 = 0;
+  int ftype = 1;
+  // SAM 3 (sam3.cpp:1477-1520)
+  int img_size = 1008, patch_size = 14, vit_embed_dim = 1024, vit_depth = 32, vit_num_heads = 16;
+  int vit_mlp_dim = 4736, vit_window_size = 24, n_global_attn = 4;
+  int global_attn_idx[4] = {7, 15, 23, 31};
+  int neck_dim = 256, mem_out_dim = 64, mem_attn_layers = 4, num_maskmem = 7, max_obj_ptrs = 16;
+  int visual_only = 0;
+  // SAM 2 (sam3.cpp:1564-1626)
+  int backbone_type = 1;
+  int hiera_embed_dim = 144, hiera_num_heads = 2, hiera_num_stages = 4;
+  int hiera_stages[4] = {2, 6, 36, 4};
+  int hiera_global_n = 3;
+  int hiera_global_idx[8] = {23, 33, 43, 0, 0, 0, 0, 0};
+  int hiera_q_pool = 3;
+  int hiera_window_spec[4] = {8, 4, 16, 8};
+  int bkg_h = 7, bkg_w = 7;
+  int scalp = 1;
+  int fpn_top_down_n = 2;
+  int fpn_top_down_levels[4] = {2, 3, 0, 0};
+
+  bool is_global(int layer) const {
+    for (int i = 0; i < n_global_attn && i < 4; ++i)
+      if (global_attn_idx[i] == layer) return true;
+    return false;
+  }
+  bool is_hiera_global(int b) const {
+    for (int i = 0; i < hiera_global_n && i < 8; ++i)
+      if (hiera_global_idx[i] == b) return true;
+    return false;
+  }
+  int n_img_embd() const { return img_size / patch_size; }
+};
+
+int read_ggml_file(const std::string& path, HParams& hp, std::vector<FileTensor>& tensors, std::string& err);
+
+// f32 values of a file tensor (f32 / f16 / q4_0 / q4_1 / q8_0).
+void tensor_to_f32(const FileTensor& t, std::vector<float>& out);
+
+// ---------------------------------------------------------------- device memory
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  // Grows the buffer to at least n bytes (contents are not preserved).
+  int reserve(size_t n) {
+    if (n <= bytes) return 0;
+    release();
+    if (cudaMalloc(&p, n) != cudaSuccess) {
+      p = nullptr;
+      return kErrOOM;
+    }
+    bytes = n;
+    return 0;
+  }
+  template <typename T>
+  T* as() const { return reinterpret_cast<T*>(p); }
+};
+
+// A linear weight prepared for the tensor-core GEMM: B operand [N][Kpad] f16
+// (K-major), plus the bias and, for quantised files, the raw blocks.
+struct Linear {
+  int N = 0, K = 0, Kpad = 0;
+  int file_dtype = 0;
+  std::shared_ptr<DevBuf> w;     // f16 [N][Kpad]
+  std::shared_ptr<DevBuf> b;     // f32 [N] (may be null)
+  std::shared_ptr<DevBuf> raw;   // raw quantised rows as in the file (q4_0/q4_1/q8_0), else null
+};
+
+struct Vec {
+  std::shared_ptr<DevBuf> d;  // f32
+  int n = 0;
+  const float* ptr() const { return d ? d->as<float>() : nullptr; }
+};
+
+struct VitBlock {
+  Vec n1w, n1b, n2w, n2b;
+  Linear qkv, proj, fc1, fc2;
+  std::shared_ptr<DevBuf> rope;  // f32 [N][32][2]
+  int rope_n = 0;
+  bool global = false;
+};
+
+struct NeckScale {
+  Linear dc1, dc2, c1, c3;  // deconv1/2 as [4*Cout][Cin], conv1x1 [Cout][Cin], conv3x3 [Cout][9*Cin]
+  bool has_dc1 = false, has_dc2 = false;
+};
+
+struct HieraBlock {
+  Vec n1w, n1b, n2w, n2b;
+  Linear qkv, proj, fc1, fc2, dim_proj;
+  int dim_in = 0, dim_out = 0, heads = 0, window = 0, stage = 0;
+  bool q_stride = false, has_dim_proj = false;
+};
+
+struct MemAttnLayer {
+  Vec n1w, n1b, n2w, n2b, n3w, n3b;
+  Linear sa_qkv, sa_out, ca_q, ca_k, ca_v, ca_out, fc1, fc2;
+};
+
+struct Model {
+  HParams hp;
+  bool loaded = false;
+  // SAM 3 ViT
+  Linear patch;                      // [1024][Kpad=592]
+  std::shared_ptr<DevBuf> pos_tiled; // f32 [72*72][1024]
+  Vec ln_pre_w, ln_pre_b;
+  std::vector<VitBlock> vit;
+  NeckScale neck_trk[4], neck_det[4];
+  bool has_neck_trk = false, has_neck_det = false;
+  // SAM 2 Hiera
+  Linear hpatch;                     // [E0][Kpad=152]
+  std::vector<float> pos_bkg, pos_win;  // host copies (CHW) for the PE
+  std::vector<HieraBlock> hiera;
+  int stage_ends[4] = {0, 0, 0, 0};
+  Linear fpn[4];
+  // memory attention
+  std::vector<MemAttnLayer> mem;
+  Vec mem_norm_w, mem_norm_b;
+  bool has_mem_attn = false;
+  std::vector<float> maskmem_tpos;   // [num_maskmem][64]
+  std::vector<float> obj_ptr_tpos_w, obj_ptr_tpos_b;  // [64][256], [64]
+  size_t device_bytes = 0;
+};
+
+// Per-frame outputs of one encode call (device, channel-last f32 maps).
+struct Outputs {
+  int n_frames = 0;
+  int img_size = 0;
+  std::shared_ptr<DevBuf> backbone;  // ViT output [F][72][72][1024] or null
+  std::shared_ptr<DevBuf> fpn[4];    // neck_trk / fpn levels [F][S][S][256]
+  int fpn_size[4] = {0, 0, 0, 0};
+  int n_fpn = 0;
+  std::shared_ptr<DevBuf> det[4];    // neck_det (SAM 3, non visual-only)
+  int n_det = 0;
+  std::map<int, std::shared_ptr<DevBuf>> pe_cache;  // sinusoidal PE per size, [S][S][256]
+};
+
+}  // namespace s3b
+
+// Opaque context of the C-ABI (one per device).
+struct s3b_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  int* d_err = nullptr;  // device error word of the bounded waits
+  std::string last_error;
+  s3b::Model model;
+  s3b::Outputs out;
+  // workspace (grown on demand, reused across calls)
+  std::map<std::string, std::shared_ptr<s3b::DevBuf>> ws;
+  int max_frames_per_pass = 8;
+  // per-kernel timing instrumentation (optional)
+  bool timing = false;
+  std::vector<std::pair<std::string, float>> timings;
+
+  s3b::DevBuf* buf(const std::string& name, size_t bytes, int* rc);
+};
+
+namespace s3b {
+int set_error(s3b_ctx* ctx, int code, const char* fmt, ...);
+int check_device(s3b_ctx* ctx, const char* where);
+
+// weight preparation (model.cpp)
+int load_model(s3b_ctx* ctx, const std::string& path);
+int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Linear& L, int kpad_to = 8);
+
+// encoders
+int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);
+int hiera_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);
+
+}  // namespace s3b

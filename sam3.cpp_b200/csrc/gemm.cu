@@ -1,0 +1,436 @@
+// Persistent warp-specialised tensor-core GEMM for sm_100a.
+//
+//   C[M,N] = A[M,K] * B[N,K]^T, A/B f16 K-major, f32 accumulation in TMEM.
+//
+// This kernel replaces ggml_mul_mat + ggml_add(bias) (+ activation,
+// + residual add, + the permute/cont copies that follow) on the encoder hot
+// path: ViT blocks sam3.cpp:3738-3798, Hiera blocks sam3.cpp:4317-4454,
+// memory attention sam3.cpp:9250-9325, and the convolutions lowered to
+// GEMMs (patch embed 3815/4470, neck 3880-3918, FPN 4547).
+//
+// Roles (320 threads, one CTA per SM, persistent over output tiles):
+//   warp 0     TMA producer: 128x64 A tile + BNx64 B tile per stage (SW128)
+//   warp 1     MMA issuer: 4 x tcgen05.mma (K=16) per stage into TMEM;
+//              owns the TMEM allocation (2 accumulators of BN columns)
+//   warps 2-9  epilogue: tcgen05.ld -> bias/act/residual -> global stores;
+//              warps w and w+4 share TMEM lane quarter (w % 4) and split the
+//              columns in halves.
+// The accumulator is double-buffered so the epilogue of tile i overlaps the
+// main loop of tile i+1.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <mutex>
+
+namespace s3b {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + kEpiWarps * 32;
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  switch (act) {
+    case ACT_GELU_ERF: return gelu_erf(v);
+    case ACT_GELU_TANH: return gelu_tanh(v);
+    case ACT_RELU: return v > 0.f ? v : 0.f;
+    default: return v;
+  }
+}
+
+__device__ __forceinline__ void store16(void* base, long long idx, int is_f32, const float (&v)[16], int n_valid,
+                                        bool vec_ok) {
+  if (is_f32) {
+    float* p = reinterpret_cast<float*>(base) + idx;
+    if (vec_ok && n_valid == 16) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+      for (int i = 0; i < n_valid; ++i) p[i] = v[i];
+    }
+  } else {
+    __half* p = reinterpret_cast<__half*>(base) + idx;
+    if (vec_ok && n_valid == 16) {
+      __align__(16) __half2 h[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(&h[0]);
+      *reinterpret_cast<uint4*>(p + 8) = *reinterpret_cast<const uint4*>(&h[4]);
+    } else {
+      for (int i = 0; i < n_valid; ++i) p[i] = __float2half_rn(v[i]);
+    }
+  }
+}
+
+// Epilogue for 16 consecutive accumulator columns [gc, gc+16) of row gr.
+__device__ __forceinline__ void epilogue16(const EpiParams& ep, long long gr, int gc, int N, const uint32_t (&r)[16]) {
+  float v[16];
+  const int n_valid = min(16, N - gc);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  if (ep.bias) {
+    if (ep.mode == EPI_DECONV2) {
+      for (int i = 0; i < n_valid; ++i) v[i] += __ldg(ep.bias + (gc + i) % ep.cout);
+    } else {
+      for (int i = 0; i < n_valid; ++i) v[i] += __ldg(ep.bias + gc + i);
+    }
+  }
+  if (ep.act != ACT_NONE) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = apply_act(v[i], ep.act);
+  }
+
+  if (ep.mode == EPI_STORE) {
+    const long long orow = map_row(ep.map, gr);
+    if (orow < 0) return;
+    if (ep.rope && gr < ep.rope_rows) {
+      const float* rt = ep.rope + ((gr % ep.rope_mod) * (N / 2) + gc / 2) * 2;
+      for (int i = 0; i + 1 < n_valid; i += 2) {
+        const float c = __ldg(rt + i), sn = __ldg(rt + i + 1);
+        const float a = v[i], b = v[i + 1];
+        v[i] = a * c - b * sn;
+        v[i + 1] = a * sn + b * c;
+      }
+    }
+    if (ep.out_scale != 1.0f) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] *= ep.out_scale;
+    }
+    if (ep.resid) {
+      long long rrow;
+      if (ep.resid_up) {
+        const long long HW = (long long)ep.map.H * ep.map.W;
+        const long long f = orow / HW;
+        const int rem = (int)(orow - f * HW);
+        const int y = rem / ep.map.W, x = rem - (rem / ep.map.W) * ep.map.W;
+        const int W2 = ep.map.W / 2, H2 = ep.map.H / 2;
+        rrow = (f * H2 + y / 2) * W2 + x / 2;
+      } else {
+        rrow = ep.resid_mod ? orow % ep.resid_mod : orow;
+      }
+      const float* rp = ep.resid + rrow * ep.ldr + gc;
+      if (n_valid == 16 && (ep.ldr % 4) == 0) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 t = *reinterpret_cast<const float4*>(rp + i);
+          v[i] += t.x; v[i + 1] += t.y; v[i + 2] += t.z; v[i + 3] += t.w;
+        }
+      } else {
+        for (int i = 0; i < n_valid; ++i) v[i] += rp[i];
+      }
+    }
+    const bool vec_ok = (ep.ldo % 16) == 0;
+    store16(ep.out, orow * ep.ldo + gc, ep.out_f32, v, n_valid, vec_ok);
+    return;
+  }
+
+  if (ep.mode == EPI_QKV) {
+    const long long win = gr / ep.ntok;
+    const int l = (int)(gr - win * ep.ntok);
+    if ((ep.D % 16) == 0) {
+      const int s = gc / ep.C;
+      const int cc = gc - s * ep.C;
+      const int h = cc / ep.D;
+      const int d0 = cc - h * ep.D;
+      if (s < 2 && ep.rope) {
+        const float* rt = ep.rope + ((long long)l * (ep.D / 2) + d0 / 2) * 2;
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float c = __ldg(rt + i), sn = __ldg(rt + i + 1);
+          const float a = v[i], b = v[i + 1];
+          v[i] = a * c - b * sn;
+          v[i + 1] = a * sn + b * c;
+        }
+      }
+      if (s == 0) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] *= ep.qscale;
+      }
+      __half* base = s == 0 ? ep.q : (s == 1 ? ep.k : ep.v);
+      const long long idx = ((win * ep.heads + h) * ep.ntok + l) * (long long)ep.D + d0;
+      store16(base, idx, 0, v, 16, true);
+    } else {
+      // head dim not a multiple of 16 (e.g. 72): per-pair path
+      for (int i = 0; i < n_valid; i += 2) {
+        const int n = gc + i;
+        const int s = n / ep.C;
+        const int cc = n - s * ep.C;
+        const int h = cc / ep.D;
+        const int d = cc - h * ep.D;
+        float a = v[i], b = v[i + 1];
+        if (s < 2 && ep.rope) {
+          const float* rt = ep.rope + ((long long)l * (ep.D / 2) + d / 2) * 2;
+          const float c = rt[0], sn = rt[1];
+          const float a2 = a * c - b * sn, b2 = a * sn + b * c;
+          a = a2; b = b2;
+        }
+        if (s == 0) { a *= ep.qscale; b *= ep.qscale; }
+        __half* base = s == 0 ? ep.q : (s == 1 ? ep.k : ep.v);
+        const long long idx = ((win * ep.heads + h) * ep.ntok + l) * (long long)ep.D + d;
+        *reinterpret_cast<__half2*>(base + idx) = __floats2half2_rn(a, b);
+      }
+    }
+    return;
+  }
+
+  if (ep.mode == EPI_DECONV2) {
+    const long long HW = (long long)ep.map.H * ep.map.W;
+    const long long f = gr / HW;
+    const int rem = (int)(gr - f * HW);
+    const int y = rem / ep.map.W, x = rem - y * ep.map.W;
+    const int kpos = gc / ep.cout;
+    const int co = gc - kpos * ep.cout;
+    const int ky = kpos >> 1, kx = kpos & 1;
+    const long long opix = (f * 2 * ep.map.H + 2 * y + ky) * (2LL * ep.map.W) + 2 * x + kx;
+    const bool vec_ok = (ep.cout % 16) == 0 && (ep.ldo % 16) == 0;
+    store16(ep.out, opix * ep.ldo + co, ep.out_f32, v, n_valid, vec_ok);
+  }
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
+}
+
+// Waits for a phase without looking at the abort flag (used only to drain).
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitNs) {
+      if (err) atomicCAS(err, 0, kErrWaitDrain);
+      return;
+    }
+  }
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                       int K, EpiParams ep, int* err) {
+  constexpr uint32_t A_BYTES = kBM * kBK * 2;
+  constexpr uint32_t B_BYTES = BN * kBK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512 || TMEM_COLS == 128, "TMEM columns must be a power of 2");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (M + kBM - 1) / kBM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int n_tiles = tiles_m * tiles_n;
+  const int nk = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], kEpiWarps);
+    }
+    mbar_init(mma_done, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0;             // bit s: stage s has been armed at least once
+      uint32_t armed_phase = 0;       // bit s: parity of the last arming of stage s
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+        const int m0 = (t / tiles_n) * kBM;
+        const int n0 = (t % tiles_n) * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, m0);
+          tma_load_2d(&tmB, &full[stage], sB + stage * B_BYTES, kb * kBK, n0);
+          armed |= 1u << stage;
+          armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Every issued copy lands before the CTA may exit.
+      for (int s = 0; s < STAGES; ++s)
+        if (armed & (1u << s)) mbar_wait_drain(&full[s], (armed_phase >> s) & 1u, err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(kBM, BN, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t aphase = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], aphase ^ 1, s_abort, err, kErrWaitTmemEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], phase, s_abort, err, kErrWaitFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t da = sdesc_k_sw128(smem_u32(sA + stage * A_BYTES));
+          const uint64_t db = sdesc_k_sw128(smem_u32(sB + stage * B_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc_mma_f16(d_tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (kb | kk) != 0 ? 1u : 0u);
+          issued = true;
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; aphase ^= 1; }
+      }
+      // All MMAs of this CTA complete before TMEM is released.
+      if (issued) {
+        tc_commit(mma_done);
+        mbar_wait_drain(mma_done, 0, err);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    int acc = 0;
+    uint32_t aphase = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+      const int m0 = (t / tiles_n) * kBM;
+      const int n0 = (t % tiles_n) * BN;
+      if (!mbar_wait(&tfull[acc], aphase, s_abort, err, kErrWaitTmemFull)) break;
+      tc_fence_after();
+      const long long gr = (long long)m0 + row;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * (BN / 2));
+#pragma unroll 1
+      for (int c = 0; c < BN / 2; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(tbase + (uint32_t)c, r);
+        tc_wait_ld();
+        const int gc = n0 + half * (BN / 2) + c;
+        if (gr < M && gc < N) epilogue16(ep, gr, gc, N, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; aphase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2D f16 tensor map over a row-major [rows][ld] matrix, box = box_rows x 64, SW128.
+int make_map_2d(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return -10;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0) return -11;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -12;
+}
+
+template <int BN, int STAGES>
+int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
+                const EpiParams& ep, int* err, cudaStream_t st) {
+  CUtensorMap ma, mb;
+  int rc = make_map_2d(&ma, A, M, K, lda, kBM);
+  if (rc) return rc;
+  rc = make_map_2d(&mb, B, N, K, ldb, BN);
+  if (rc) return rc;
+  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN) * kBK * 2 + (2 * STAGES + 5) * 8 + 16;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(gemm_f16_tc_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return -13;
+    attr_set = true;
+  }
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_f16_tc_kernel<BN, STAGES><<<grid, kThreads, smem, st>>>(ma, mb, M, N, K, ep, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -14;
+}
+
+}  // namespace
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
+             const EpiParams& ep, int* err, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || K <= 0) return -1;
+  if (lda < K || ldb < K) return -2;
+  if (ep.mode == EPI_QKV && (ep.C * 3 != N || ep.D <= 0 || ep.C % ep.D != 0 || ep.ntok <= 0 || (ep.D & 1)))
+    return -3;
+  if (ep.mode == EPI_DECONV2 && (ep.cout <= 0 || N != 4 * ep.cout)) return -3;
+  if (N <= 128) return launch_gemm<128, 6>(A, lda, B, ldb, M, N, K, ep, err, st);
+  return launch_gemm<256, 4>(A, lda, B, ldb, M, N, K, ep, err, st);
+}
+
+}  // namespace s3b

@@ -1,0 +1,137 @@
+// Host-visible launchers and parameter blocks of the sm_100a kernels.
+// Every launcher returns 0 on success or a negative error code and never
+// allocates device memory; buffers are owned by the caller (engine.cpp).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace s3b {
+
+// Maps a row of a GEMM / attention operand, in "work order", to a row of a
+// spatial token map [frames][H][W] (or -1 for a padding row that is dropped).
+//   kind 0: identity.
+//   kind 1: work rows are window-partitioned: frame-major, then windows in
+//           (wy, wx) order, then tokens (ly, lx) inside a ws x ws window; the
+//           spatial grid is padded up to (nwh*ws, nww*ws) and padded
+//           positions map to -1 (sam3.cpp:4190-4277 window partition).
+struct RowMap {
+  int kind = 0;
+  int ws = 0;
+  int nww = 0, nwh = 0;
+  int W = 0, H = 0;  // spatial grid of the token map (unpadded)
+};
+
+__host__ __device__ inline long long map_row(const RowMap& m, long long r) {
+  if (m.kind == 0) return r;
+  const long long per_win = (long long)m.ws * m.ws;
+  const long long per_frame = per_win * m.nww * m.nwh;
+  const long long f = r / per_frame;
+  const long long rr = r - f * per_frame;
+  const int win = (int)(rr / per_win);
+  const int l = (int)(rr - (long long)win * per_win);
+  const int wy = win / m.nww, wx = win - wy * m.nww;
+  const int y = wy * m.ws + l / m.ws, x = wx * m.ws + l % m.ws;
+  if (y >= m.H || x >= m.W) return -1;
+  return (f * m.H + y) * m.W + x;
+}
+
+enum EpiMode : int { EPI_STORE = 0, EPI_QKV = 1, EPI_DECONV2 = 2 };
+enum Act : int { ACT_NONE = 0, ACT_GELU_ERF = 1, ACT_GELU_TANH = 2, ACT_RELU = 3 };
+
+// Epilogue of the tensor-core GEMM C[M,N] = A[M,K] * B[N,K]^T (f32 acc):
+//   v = act(C + bias[n]) (+ resid)  then a mode-specific store.
+struct EpiParams {
+  int mode = EPI_STORE;
+  int act = ACT_NONE;
+  const float* bias = nullptr;  // [N] (EPI_DECONV2: [cout])
+  void* out = nullptr;          // EPI_STORE / EPI_DECONV2 destination
+  int out_f32 = 0;              // 1: f32 output, 0: f16 output
+  long long ldo = 0;            // row stride of `out` (elements)
+  RowMap map;                   // EPI_STORE: GEMM row -> output row
+  // residual (f32) added after the activation, indexed by the output row:
+  //   resid_up == 0: row' = (resid_mod ? row % resid_mod : row)
+  //   resid_up == 1: nearest 2x upsample of a (W/2, H/2) map (FPN top-down)
+  const float* resid = nullptr;
+  long long ldr = 0;
+  long long resid_mod = 0;
+  int resid_up = 0;
+  // EPI_STORE only: out = v * out_scale; RoPE on column pairs for GEMM rows
+  // < rope_rows, table row (row % rope_mod), table [rows][N/2][2] (cos, sin).
+  float out_scale = 1.0f;
+  long long rope_rows = 0, rope_mod = 1;
+  // EPI_QKV: columns [0,C) -> q, [C,2C) -> k, [2C,3C) -> v; each stored as
+  // [win][head][ntok][D] f16; RoPE (pairs (2i,2i+1), table [ntok][D/2][2])
+  // on q and k when `rope` is set; q multiplied by qscale.
+  __half* q = nullptr;
+  __half* k = nullptr;
+  __half* v = nullptr;
+  int C = 0, D = 0, heads = 0, ntok = 0;
+  const float* rope = nullptr;
+  float qscale = 1.0f;
+  // EPI_DECONV2: row = input pixel (f, y, x) of a (map.W x map.H) grid,
+  // column = (ky*2 + kx)*cout + co, stored at pixel (2y+ky, 2x+kx).
+  int cout = 0;
+};
+
+// Tensor-core GEMM (tcgen05 + TMA): A f16 [M][lda] K-major, B f16 [N][ldb]
+// K-major. lda, ldb multiples of 8; pointers 16-byte aligned.
+int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
+             const EpiParams& ep, int* err, cudaStream_t st);
+
+// Flash attention (online softmax, f16 in / f32 acc / f16 out).
+struct AttnParams {
+  const __half* q = nullptr;
+  const __half* k = nullptr;
+  const __half* v = nullptr;
+  __half* o = nullptr;
+  long long q_bh = 0, q_n = 0;  // element strides: batch*head, token
+  long long k_bh = 0, k_n = 0;
+  long long v_bh = 0, v_n = 0;
+  int heads = 1;
+  int nq = 0, nk = 0;
+  long long o_b = 0, o_n = 0;  // out: o + b*o_b + n*o_n + h*D + d
+  float scale = 1.0f;          // softmax scale applied to q.k
+};
+int attention(const AttnParams& p, int D, int batch_heads, cudaStream_t st);
+
+// LayerNorm over the last dim (C) of f32 rows, eps as given; out f16 or f32.
+// Output row r reads input row map_row(map, r) (or writes zeros for -1).
+int layernorm(const float* x, long long ldx, void* y, int y_f32, long long ldy, long long rows, int C,
+              const float* gamma, const float* beta, float eps, const RowMap& map, cudaStream_t st);
+
+// im2col for a stride-s convolution over an f32 CHW image batch [B][3][H][W]:
+// out f16 [B*OH*OW][Kpad], column = (ci*k + ky)*k + kx, zeros beyond K.
+int im2col_image(const float* img, int B, int Cin, int H, int W, int k, int stride, int pad, int OH, int OW,
+                 __half* out, int Kpad, cudaStream_t st);
+
+// im2col for a 3x3 / pad 1 / stride 1 convolution over channel-last f16
+// maps [B][H][W][C]: out [B*H*W][9*C], column = (ky*3 + kx)*C + ci.
+int im2col_3x3_cl(const __half* x, int B, int H, int W, int C, __half* out, cudaStream_t st);
+
+// 2x2 / stride 2 max pool over channel-last maps [B][H][W][C].
+int maxpool2_cl_f16(const __half* x, int B, int H, int W, int C, __half* y, cudaStream_t st);
+int maxpool2_cl_f32(const float* x, int B, int H, int W, int C, float* y, cudaStream_t st);
+
+// Q pooling inside windows: q [nwin*heads][ws*ws][D] -> [nwin*heads][(ws/2)^2][D].
+int qpool_windows(const __half* q, long long nbh, int ws, int D, __half* out, cudaStream_t st);
+
+// uint8 HWC frames -> f32 CHW normalised ((p/255 - mean)/std).
+int preprocess_u8(const uint8_t* img, int B, int H, int W, const float mean[3], const float stdv[3], float* out,
+                  cudaStream_t st);
+
+int cast_f32_f16(const float* x, long long n, __half* y, cudaStream_t st);
+int add_scaled_f32(const float* a, const float* b, float s, long long n, float* y, cudaStream_t st);
+
+// ggml block formats (32 values per block along the row).
+enum QType : int { QT_F32 = 0, QT_F16 = 1, QT_Q4_0 = 2, QT_Q4_1 = 3, QT_Q8_0 = 8 };
+long long qtype_row_bytes(int qtype, long long ne0);
+// Dequantise `nrows` rows of `ne0` values: raw blocks -> f32 (bit-exact ggml
+// semantics) or -> f16 (rounded from the exact f32 value).
+int dequant_rows(const void* src, int qtype, long long ne0, long long nrows, void* dst, int dst_f32,
+                 long long ld_dst, cudaStream_t st);
+
+// Returns the number of SMs of the current device (cached).
+int num_sms();
+
+}  // namespace s3b

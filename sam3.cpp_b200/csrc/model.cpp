@@ -1,0 +1,656 @@
+// .ggml model file parsing and device weight preparation (host, C++14).
+//
+// File format (sam3.cpp:3200-3344 loader, convert_sam3_to_ggml.py:160-240 and
+// convert_sam2_to_ggml.py:206-318 writers): u32 magic, i32 version, i32 ftype,
+// i32 n_tensors, the model's i32 hyper-parameters, then records
+//   i32 n_dims, i32 name_len, i32 dtype, i32 ne[n_dims] (ggml order), name,
+//   zero padding to a 32-byte file offset, raw data.
+// Unlike sam3_load_tensors (sam3.cpp:3091-3194), tensors the encoder engine
+// does not use are skipped instead of rejected, so full model files load.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <fstream>
+
+#include "engine.h"
+
+namespace s3b {
+
+static constexpr uint32_t kMagicSam3 = 0x73616D33;
+static constexpr uint32_t kMagicSam2 = 0x73616D32;
+
+int set_error(s3b_ctx* ctx, int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (ctx) ctx->last_error = buf;
+  fprintf(stderr, "s3b: %s\n", buf);
+  return code;
+}
+
+int check_device(s3b_ctx* ctx, const char* where) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(ctx, kErrCuda, "%s: %s", where, cudaGetErrorString(e));
+  return kOk;
+}
+
+static float h2f(uint16_t h) {
+  __half_raw r;
+  r.x = h;
+  return __half2float(__half(r));
+}
+
+// Host restatement of the block dequantisers (same values as the device kernel).
+static void dequant_row_host(int dtype, const uint8_t* p, int64_t n, float* y) {
+  const int64_t nb = n / 32;
+  for (int64_t b = 0; b < nb; ++b) {
+    if (dtype == QT_Q4_0) {
+      const uint8_t* q = p + b * 18;
+      uint16_t dh;
+      memcpy(&dh, q, 2);
+      const float d = h2f(dh);
+      for (int j = 0; j < 16; ++j) {
+        y[b * 32 + j] = (float)((int)(q[2 + j] & 0x0F) - 8) * d;
+        y[b * 32 + j + 16] = (float)((int)(q[2 + j] >> 4) - 8) * d;
+      }
+    } else if (dtype == QT_Q4_1) {
+      const uint8_t* q = p + b * 20;
+      uint16_t dh, mh;
+      memcpy(&dh, q, 2);
+      memcpy(&mh, q + 2, 2);
+      const float d = h2f(dh), m = h2f(mh);
+      for (int j = 0; j < 16; ++j) {
+        volatile float a = (float)(q[4 + j] & 0x0F) * d;
+        volatile float c = (float)(q[4 + j] >> 4) * d;
+        y[b * 32 + j] = a + m;
+        y[b * 32 + j + 16] = c + m;
+      }
+    } else {
+      const uint8_t* q = p + b * 34;
+      uint16_t dh;
+      memcpy(&dh, q, 2);
+      const float d = h2f(dh);
+      for (int j = 0; j < 32; ++j) y[b * 32 + j] = (float)((const int8_t*)(q + 2))[j] * d;
+    }
+  }
+}
+
+void tensor_to_f32(const FileTensor& t, std::vector<float>& out) {
+  const int64_t n = t.nelements();
+  out.resize(n);
+  if (t.dtype == QT_F32) {
+    memcpy(out.data(), t.data.data(), n * 4);
+  } else if (t.dtype == QT_F16) {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(t.data.data());
+    for (int64_t i = 0; i < n; ++i) out[i] = h2f(h[i]);
+  } else {
+    const int64_t rows = n / t.ne[0];
+    const long long rb = qtype_row_bytes(t.dtype, t.ne[0]);
+    for (int64_t r = 0; r < rows; ++r) dequant_row_host(t.dtype, t.data.data() + r * rb, t.ne[0], out.data() + r * t.ne[0]);
+  }
+}
+
+static bool rd32(std::ifstream& f, int32_t& v) {
+  f.read(reinterpret_cast<char*>(&v), 4);
+  return !f.fail();
+}
+
+int read_ggml_file(const std::string& path, HParams& hp, std::vector<FileTensor>& tensors, std::string& err) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) {
+    err = "cannot open " + path;
+    return kErrIO;
+  }
+  uint32_t magic = 0;
+  f.read(reinterpret_cast<char*>(&magic), 4);
+  int32_t version = 0, ftype = 0, n_tensors = 0;
+  rd32(f, version);
+  rd32(f, ftype);
+  rd32(f, n_tensors);
+  if (f.fail() || (magic != kMagicSam3 && magic != kMagicSam2)) {
+    err = "bad magic in " + path;
+    return kErrFormat;
+  }
+  hp.ftype = ftype;
+  int32_t v;
+  auto rd = [&](int& dst) {
+    rd32(f, v);
+    dst = v;
+  };
+  if (magic == kMagicSam3) {
+    // sam3_load_hparams (sam3.cpp:1477-1520)
+    hp.is_sam2 = 0;
+    int dummy;
+    rd(hp.img_size);
+    rd(hp.patch_size);
+    rd(hp.vit_embed_dim);
+    rd(hp.vit_depth);
+    rd(hp.vit_num_heads);
+    int mlp_ratio_x1000;
+    rd(mlp_ratio_x1000);
+    hp.vit_mlp_dim = (int)(hp.vit_embed_dim * (mlp_ratio_x1000 / 1000.0f));
+    rd(hp.vit_window_size);
+    rd(hp.n_global_attn);
+    for (int i = 0; i < hp.n_global_attn && i < 4; ++i) rd(hp.global_attn_idx[i]);
+    for (int i = 0; i < 6; ++i) rd(dummy);  // text_width..text_out_dim
+    rd(hp.neck_dim);
+    for (int i = 0; i < 11; ++i) rd(dummy);  // fenc (3), ddec (4), geom, presence, geom queries
+    for (int i = 0; i < 4; ++i) rd(dummy);   // sam decoder
+    rd(hp.mem_out_dim);
+    rd(hp.mem_attn_layers);
+    rd(hp.num_maskmem);
+    rd(hp.max_obj_ptrs);
+    rd(dummy);  // n_amb_experts
+    rd(hp.visual_only);
+  } else {
+    // sam2_load_hparams (sam3.cpp:1564-1626)
+    hp.is_sam2 = 1;
+    int dummy;
+    rd(hp.img_size);
+    rd(hp.backbone_type);
+    rd(hp.hiera_embed_dim);
+    rd(hp.hiera_num_heads);
+    rd(hp.hiera_num_stages);
+    for (int i = 0; i < 4; ++i) rd(hp.hiera_stages[i]);
+    rd(hp.hiera_global_n);
+    for (int i = 0; i < 8; ++i) rd(hp.hiera_global_idx[i]);
+    rd(hp.hiera_q_pool);
+    for (int i = 0; i < 4; ++i) rd(hp.hiera_window_spec[i]);
+    rd(hp.bkg_h);
+    rd(hp.bkg_w);
+    rd(hp.scalp);
+    rd(hp.neck_dim);
+    rd(hp.fpn_top_down_n);
+    for (int i = 0; i < 4; ++i) rd(hp.fpn_top_down_levels[i]);
+    for (int i = 0; i < 4; ++i) rd(dummy);  // sam decoder
+    rd(hp.mem_out_dim);
+    rd(hp.mem_attn_layers);
+    rd(hp.num_maskmem);
+    rd(hp.max_obj_ptrs);
+    for (int i = 0; i < 2 + 15; ++i) rd(dummy);  // sigmoid scale/bias + tracking flags
+    if (hp.backbone_type != 1) {
+      err = "only the Hiera backbone (backbone_type 1) is supported by the encoder engine";
+      return kErrUnsupported;
+    }
+  }
+  if (f.fail()) {
+    err = "truncated header";
+    return kErrFormat;
+  }
+  tensors.clear();
+  tensors.reserve(n_tensors);
+  for (int t = 0; t < n_tensors; ++t) {
+    int32_t n_dims, name_len, dtype;
+    if (!rd32(f, n_dims) || !rd32(f, name_len) || !rd32(f, dtype)) {
+      err = "truncated tensor header";
+      return kErrFormat;
+    }
+    if (n_dims < 1 || n_dims > 4 || name_len <= 0 || name_len > 512) {
+      err = "corrupt tensor header";
+      return kErrFormat;
+    }
+    FileTensor ft;
+    ft.n_dims = n_dims;
+    ft.dtype = dtype;
+    for (int i = 0; i < n_dims; ++i) {
+      int32_t d;
+      rd32(f, d);
+      if (d <= 0) {
+        err = "corrupt tensor shape";
+        return kErrFormat;
+      }
+      ft.ne[i] = d;
+    }
+    ft.name.resize(name_len);
+    f.read(&ft.name[0], name_len);
+    const size_t pos = (size_t)f.tellg();
+    const size_t pad = (32 - pos % 32) % 32;
+    if (pad) f.seekg(pad, std::ios::cur);
+    int64_t bytes;
+    if (dtype == QT_F32 || dtype == QT_F16) {
+      bytes = ft.nelements() * (dtype == QT_F16 ? 2 : 4);
+    } else if (dtype == QT_Q4_0 || dtype == QT_Q4_1 || dtype == QT_Q8_0) {
+      if (ft.ne[0] % 32) {
+        err = "quantised tensor with ne0 % 32 != 0: " + ft.name;
+        return kErrFormat;
+      }
+      bytes = qtype_row_bytes(dtype, ft.ne[0]) * (ft.nelements() / ft.ne[0]);
+    } else {
+      err = "unsupported dtype in " + ft.name;
+      return kErrFormat;
+    }
+    ft.data.resize(bytes);
+    f.read(reinterpret_cast<char*>(ft.data.data()), bytes);
+    if (f.fail()) {
+      err = "failed to read tensor " + ft.name;
+      return kErrIO;
+    }
+    tensors.push_back(std::move(ft));
+  }
+  return kOk;
+}
+
+// ---------------------------------------------------------------- uploads
+static std::shared_ptr<DevBuf> upload_bytes(s3b_ctx* ctx, const void* src, size_t bytes, int* rc) {
+  auto b = std::make_shared<DevBuf>();
+  if (b->reserve(bytes) != 0) {
+    *rc = set_error(ctx, kErrOOM, "cudaMalloc(%zu) failed", bytes);
+    return nullptr;
+  }
+  if (cudaMemcpy(b->p, src, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+    *rc = set_error(ctx, kErrCuda, "upload of %zu bytes failed", bytes);
+    return nullptr;
+  }
+  ctx->model.device_bytes += bytes;
+  return b;
+}
+
+static Vec upload_vec(s3b_ctx* ctx, const FileTensor& t, int* rc) {
+  std::vector<float> f;
+  tensor_to_f32(t, f);
+  Vec v;
+  v.n = (int)f.size();
+  v.d = upload_bytes(ctx, f.data(), f.size() * 4, rc);
+  return v;
+}
+
+// Uploads a GEMM B operand given as f32 [N][K] (row-major), padded to Kpad.
+static int upload_b_operand(s3b_ctx* ctx, const std::vector<float>& w, int N, int K, int kpad_to, Linear& L) {
+  L.N = N;
+  L.K = K;
+  L.Kpad = ((K + kpad_to - 1) / kpad_to) * kpad_to;
+  std::vector<__half> h((size_t)N * L.Kpad, __float2half_rn(0.f));
+  for (int n = 0; n < N; ++n)
+    for (int k = 0; k < K; ++k) h[(size_t)n * L.Kpad + k] = __float2half_rn(w[(size_t)n * K + k]);
+  int rc = 0;
+  L.w = upload_bytes(ctx, h.data(), h.size() * 2, &rc);
+  return rc;
+}
+
+int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Linear& L, int kpad_to) {
+  // ggml weight [K, N] (ne0 = K contiguous) == row-major [N][K]
+  const int K = (int)t.ne[0];
+  const int N = (int)(t.nelements() / t.ne[0]);
+  std::vector<float> w;
+  tensor_to_f32(t, w);
+  int rc = upload_b_operand(ctx, w, N, K, kpad_to, L);
+  if (rc) return rc;
+  L.file_dtype = t.dtype;
+  if (t.dtype == QT_Q4_0 || t.dtype == QT_Q4_1 || t.dtype == QT_Q8_0) {
+    L.raw = upload_bytes(ctx, t.data.data(), t.data.size(), &rc);
+    if (rc) return rc;
+  }
+  if (bias) {
+    std::vector<float> b;
+    tensor_to_f32(*bias, b);
+    if ((int)b.size() != N) return set_error(ctx, kErrFormat, "bias size mismatch for %s", t.name.c_str());
+    L.b = upload_bytes(ctx, b.data(), b.size() * 4, &rc);
+  }
+  return rc;
+}
+
+// ConvTranspose2d k=2 s=2, ggml [2, 2, Cout, Cin] -> B[(ky*2+kx)*Cout + co][ci].
+static int upload_deconv(s3b_ctx* ctx, const FileTensor& t, const FileTensor& bias, Linear& L) {
+  const int Cout = (int)t.ne[2], Cin = (int)t.ne[3];
+  std::vector<float> w, r((size_t)4 * Cout * Cin);
+  tensor_to_f32(t, w);
+  for (int ci = 0; ci < Cin; ++ci)
+    for (int co = 0; co < Cout; ++co)
+      for (int ky = 0; ky < 2; ++ky)
+        for (int kx = 0; kx < 2; ++kx)
+          r[(size_t)((ky * 2 + kx) * Cout + co) * Cin + ci] = w[(size_t)kx + 2 * (ky + 2 * (co + (size_t)Cout * ci))];
+  int rc = upload_b_operand(ctx, r, 4 * Cout, Cin, 8, L);
+  if (rc) return rc;
+  std::vector<float> b;
+  tensor_to_f32(bias, b);
+  L.b = upload_bytes(ctx, b.data(), b.size() * 4, &rc);
+  L.file_dtype = t.dtype;
+  return rc;
+}
+
+// Conv2d kxk, ggml [k, k, Cin, Cout] -> B[co][(ky*k + kx)*Cin + ci] (channel-last im2col order).
+static int upload_conv_cl(s3b_ctx* ctx, const FileTensor& t, const FileTensor& bias, Linear& L) {
+  const int k = (int)t.ne[0], Cin = (int)t.ne[2], Cout = (int)t.ne[3];
+  std::vector<float> w, r((size_t)Cout * k * k * Cin);
+  tensor_to_f32(t, w);
+  for (int co = 0; co < Cout; ++co)
+    for (int ci = 0; ci < Cin; ++ci)
+      for (int ky = 0; ky < k; ++ky)
+        for (int kx = 0; kx < k; ++kx)
+          r[(size_t)co * k * k * Cin + (size_t)(ky * k + kx) * Cin + ci] =
+              w[(size_t)kx + k * (ky + (size_t)k * (ci + (size_t)Cin * co))];
+  int rc = upload_b_operand(ctx, r, Cout, k * k * Cin, 8, L);
+  if (rc) return rc;
+  std::vector<float> b;
+  tensor_to_f32(bias, b);
+  L.b = upload_bytes(ctx, b.data(), b.size() * 4, &rc);
+  L.file_dtype = t.dtype;
+  return rc;
+}
+
+// ---------------------------------------------------------------- model build
+namespace {
+struct Index {
+  std::map<std::string, const FileTensor*> m;
+  const FileTensor* get(const std::string& n) const {
+    auto it = m.find(n);
+    return it == m.end() ? nullptr : it->second;
+  }
+};
+}  // namespace
+
+#define NEED(var, name)                                                                   \
+  const FileTensor* var = idx.get(name);                                                  \
+  if (!var) return set_error(ctx, kErrFormat, "missing tensor '%s'", std::string(name).c_str());
+
+static int load_neck(s3b_ctx* ctx, const Index& idx, const std::string& pfx, NeckScale* sc) {
+  int rc;
+  {
+    NEED(w0, pfx + "0.dconv_2x2_0.weight");
+    NEED(b0, pfx + "0.dconv_2x2_0.bias");
+    NEED(w1, pfx + "0.dconv_2x2_1.weight");
+    NEED(b1, pfx + "0.dconv_2x2_1.bias");
+    if ((rc = upload_deconv(ctx, *w0, *b0, sc[0].dc1))) return rc;
+    if ((rc = upload_deconv(ctx, *w1, *b1, sc[0].dc2))) return rc;
+    sc[0].has_dc1 = sc[0].has_dc2 = true;
+  }
+  {
+    NEED(w, pfx + "1.dconv_2x2.weight");
+    NEED(b, pfx + "1.dconv_2x2.bias");
+    if ((rc = upload_deconv(ctx, *w, *b, sc[1].dc1))) return rc;
+    sc[1].has_dc1 = true;
+  }
+  for (int s = 0; s < 4; ++s) {
+    const std::string p = pfx + std::to_string(s);
+    NEED(w1, p + ".conv_1x1.weight");
+    NEED(b1, p + ".conv_1x1.bias");
+    NEED(w3, p + ".conv_3x3.weight");
+    NEED(b3, p + ".conv_3x3.bias");
+    if ((rc = upload_conv_cl(ctx, *w1, *b1, sc[s].c1))) return rc;
+    if ((rc = upload_conv_cl(ctx, *w3, *b3, sc[s].c3))) return rc;
+  }
+  return kOk;
+}
+
+static int load_mem_attn(s3b_ctx* ctx, const Index& idx) {
+  Model& M = ctx->model;
+  const HParams& hp = M.hp;
+  if (!idx.get("mem_attn.layers.0.sa.q_proj.weight")) return kOk;  // optional
+  int rc = 0;
+  M.mem.resize(hp.mem_attn_layers);
+  for (int i = 0; i < hp.mem_attn_layers; ++i) {
+    MemAttnLayer& L = M.mem[i];
+    const std::string p = "mem_attn.layers." + std::to_string(i);
+    NEED(n1w, p + ".norm1.weight");
+    NEED(n1b, p + ".norm1.bias");
+    NEED(n2w, p + ".norm2.weight");
+    NEED(n2b, p + ".norm2.bias");
+    NEED(n3w, p + ".norm3.weight");
+    NEED(n3b, p + ".norm3.bias");
+    L.n1w = upload_vec(ctx, *n1w, &rc);
+    L.n1b = upload_vec(ctx, *n1b, &rc);
+    L.n2w = upload_vec(ctx, *n2w, &rc);
+    L.n2b = upload_vec(ctx, *n2b, &rc);
+    L.n3w = upload_vec(ctx, *n3w, &rc);
+    L.n3b = upload_vec(ctx, *n3b, &rc);
+    // self-attention q/k/v concatenated into one [3*D][D] GEMM
+    {
+      NEED(qw, p + ".sa.q_proj.weight");
+      NEED(kw, p + ".sa.k_proj.weight");
+      NEED(vw, p + ".sa.v_proj.weight");
+      NEED(qb, p + ".sa.q_proj.bias");
+      NEED(kb, p + ".sa.k_proj.bias");
+      NEED(vb, p + ".sa.v_proj.bias");
+      std::vector<float> a, b, c, w;
+      tensor_to_f32(*qw, a);
+      tensor_to_f32(*kw, b);
+      tensor_to_f32(*vw, c);
+      const int D = (int)qw->ne[0];
+      w.reserve(a.size() * 3);
+      w.insert(w.end(), a.begin(), a.end());
+      w.insert(w.end(), b.begin(), b.end());
+      w.insert(w.end(), c.begin(), c.end());
+      if ((rc = upload_b_operand(ctx, w, 3 * D, D, 8, L.sa_qkv))) return rc;
+      std::vector<float> ba, bb, bc;
+      tensor_to_f32(*qb, ba);
+      tensor_to_f32(*kb, bb);
+      tensor_to_f32(*vb, bc);
+      ba.insert(ba.end(), bb.begin(), bb.end());
+      ba.insert(ba.end(), bc.begin(), bc.end());
+      L.sa_qkv.b = upload_bytes(ctx, ba.data(), ba.size() * 4, &rc);
+    }
+    {
+      NEED(w, p + ".sa.out_proj.weight");
+      NEED(b, p + ".sa.out_proj.bias");
+      if ((rc = upload_linear(ctx, *w, b, L.sa_out))) return rc;
+    }
+    {
+      NEED(w, p + ".ca.q_proj.weight");
+      NEED(b, p + ".ca.q_proj.bias");
+      if ((rc = upload_linear(ctx, *w, b, L.ca_q))) return rc;
+    }
+    {
+      NEED(w, p + ".ca.k_proj.weight");
+      NEED(b, p + ".ca.k_proj.bias");
+      if ((rc = upload_linear(ctx, *w, b, L.ca_k))) return rc;
+    }
+    {
+      NEED(w, p + ".ca.v_proj.weight");
+      NEED(b, p + ".ca.v_proj.bias");
+      if ((rc = upload_linear(ctx, *w, b, L.ca_v))) return rc;
+    }
+    {
+      NEED(w, p + ".ca.out_proj.weight");
+      NEED(b, p + ".ca.out_proj.bias");
+      if ((rc = upload_linear(ctx, *w, b, L.ca_out))) return rc;
+    }
+    {
+      NEED(w, p + ".linear1.weight");
+      NEED(b, p + ".linear1.bias");
+      if ((rc = upload_linear(ctx, *w, b, L.fc1))) return rc;
+    }
+    {
+      NEED(w, p + ".linear2.weight");
+      NEED(b, p + ".linear2.bias");
+      if ((rc = upload_linear(ctx, *w, b, L.fc2))) return rc;
+    }
+  }
+  NEED(nw, "mem_attn.norm.weight");
+  NEED(nb, "mem_attn.norm.bias");
+  M.mem_norm_w = upload_vec(ctx, *nw, &rc);
+  M.mem_norm_b = upload_vec(ctx, *nb, &rc);
+  if (const FileTensor* t = idx.get("mem_enc.tpos_enc")) tensor_to_f32(*t, M.maskmem_tpos);
+  if (const FileTensor* t = idx.get("obj_ptr_tpos_proj.weight")) tensor_to_f32(*t, M.obj_ptr_tpos_w);
+  if (const FileTensor* t = idx.get("obj_ptr_tpos_proj.bias")) tensor_to_f32(*t, M.obj_ptr_tpos_b);
+  M.has_mem_attn = true;
+  return rc;
+}
+
+static int load_sam3(s3b_ctx* ctx, const Index& idx) {
+  Model& M = ctx->model;
+  const HParams& hp = M.hp;
+  const int E = hp.vit_embed_dim;
+  int rc = 0;
+  {
+    NEED(pw, "vit.patch_embed.proj.weight");
+    // ggml [p, p, 3, E] == [E][3][p][p]: row co, column (ci*p + ky)*p + kx (the im2col order)
+    if ((rc = upload_linear(ctx, *pw, nullptr, M.patch, 16))) return rc;
+  }
+  {
+    NEED(pos, "vit.pos_embed");
+    std::vector<float> p;
+    tensor_to_f32(*pos, p);
+    const int G = (int)pos->ne[1], H = hp.n_img_embd();
+    std::vector<float> tiled((size_t)H * H * E);
+    // ggml_repeat of [E, G, G] to [E, H, H] (sam3.cpp:3817-3822)
+    for (int y = 0; y < H; ++y)
+      for (int x = 0; x < H; ++x)
+        memcpy(&tiled[((size_t)y * H + x) * E], &p[((size_t)(y % G) * G + (x % G)) * E], E * 4);
+    M.pos_tiled = upload_bytes(ctx, tiled.data(), tiled.size() * 4, &rc);
+    if (rc) return rc;
+  }
+  {
+    NEED(w, "vit.ln_pre.weight");
+    NEED(b, "vit.ln_pre.bias");
+    M.ln_pre_w = upload_vec(ctx, *w, &rc);
+    M.ln_pre_b = upload_vec(ctx, *b, &rc);
+  }
+  M.vit.resize(hp.vit_depth);
+  for (int i = 0; i < hp.vit_depth; ++i) {
+    VitBlock& B = M.vit[i];
+    const std::string p = "vit.blocks." + std::to_string(i);
+    NEED(n1w, p + ".norm1.weight");
+    NEED(n1b, p + ".norm1.bias");
+    NEED(n2w, p + ".norm2.weight");
+    NEED(n2b, p + ".norm2.bias");
+    B.n1w = upload_vec(ctx, *n1w, &rc);
+    B.n1b = upload_vec(ctx, *n1b, &rc);
+    B.n2w = upload_vec(ctx, *n2w, &rc);
+    B.n2b = upload_vec(ctx, *n2b, &rc);
+    NEED(qw, p + ".attn.qkv.weight");
+    NEED(qb, p + ".attn.qkv.bias");
+    NEED(pw, p + ".attn.proj.weight");
+    NEED(pb, p + ".attn.proj.bias");
+    NEED(f1w, p + ".mlp.lin1.weight");
+    NEED(f1b, p + ".mlp.lin1.bias");
+    NEED(f2w, p + ".mlp.lin2.weight");
+    NEED(f2b, p + ".mlp.lin2.bias");
+    if ((rc = upload_linear(ctx, *qw, qb, B.qkv))) return rc;
+    if ((rc = upload_linear(ctx, *pw, pb, B.proj))) return rc;
+    if ((rc = upload_linear(ctx, *f1w, f1b, B.fc1))) return rc;
+    if ((rc = upload_linear(ctx, *f2w, f2b, B.fc2))) return rc;
+    B.global = hp.is_global(i);
+    if (const FileTensor* fc = idx.get(p + ".attn.freqs_cis")) {
+      std::vector<float> f;
+      tensor_to_f32(*fc, f);
+      B.rope_n = (int)fc->ne[2];
+      B.rope = upload_bytes(ctx, f.data(), f.size() * 4, &rc);
+    }
+  }
+  if (idx.get("neck.trk.0.conv_1x1.weight")) {
+    if ((rc = load_neck(ctx, idx, "neck.trk.", M.neck_trk))) return rc;
+    M.has_neck_trk = true;
+  }
+  if (!hp.visual_only && idx.get("neck.det.0.conv_1x1.weight")) {
+    if ((rc = load_neck(ctx, idx, "neck.det.", M.neck_det))) return rc;
+    M.has_neck_det = true;
+  }
+  return load_mem_attn(ctx, idx);
+}
+
+// Per-block Hiera metadata (sam2_precompute_hiera_metadata, sam3.cpp:1676-1742):
+// stage dims double at stage starts, q-stride on the first block of stages
+// 1..q_pool, and the window size "lags" one block at stage transitions.
+static void hiera_metadata(Model& M) {
+  const HParams& hp = M.hp;
+  int total = 0;
+  for (int s = 0; s < hp.hiera_num_stages; ++s) total += hp.hiera_stages[s];
+  M.hiera.resize(total);
+  int cum = 0;
+  for (int s = 0; s < hp.hiera_num_stages; ++s) {
+    cum += hp.hiera_stages[s];
+    M.stage_ends[s] = cum - 1;
+  }
+  std::vector<int> qpool_blocks;
+  for (int s = 0; s < hp.hiera_num_stages - 1 && (int)qpool_blocks.size() < hp.hiera_q_pool; ++s)
+    qpool_blocks.push_back(M.stage_ends[s] + 1);
+  int cur_stage = 0, embed = hp.hiera_embed_dim, heads = hp.hiera_num_heads;
+  for (int i = 0; i < total; ++i) {
+    HieraBlock& B = M.hiera[i];
+    int ws = hp.hiera_window_spec[cur_stage];
+    if (hp.is_hiera_global(i)) ws = 0;
+    B.window = ws;
+    int dout = embed;
+    if (i > 0 && i - 1 == M.stage_ends[cur_stage]) {
+      dout = embed * 2;
+      heads *= 2;
+      cur_stage++;
+    }
+    B.stage = cur_stage;
+    B.dim_in = embed;
+    B.dim_out = dout;
+    B.heads = heads;
+    B.q_stride = false;
+    for (int qb : qpool_blocks)
+      if (qb == i) B.q_stride = true;
+    embed = dout;
+  }
+}
+
+static int load_sam2(s3b_ctx* ctx, const Index& idx) {
+  Model& M = ctx->model;
+  const HParams& hp = M.hp;
+  int rc = 0;
+  hiera_metadata(M);
+  {
+    NEED(w, "hiera.patch_embed.weight");
+    NEED(b, "hiera.patch_embed.bias");
+    if ((rc = upload_linear(ctx, *w, b, M.hpatch, 8))) return rc;
+  }
+  {
+    NEED(pb, "hiera.pos_embed");
+    NEED(pw, "hiera.pos_embed_window");
+    tensor_to_f32(*pb, M.pos_bkg);
+    tensor_to_f32(*pw, M.pos_win);
+  }
+  for (size_t i = 0; i < M.hiera.size(); ++i) {
+    HieraBlock& B = M.hiera[i];
+    const std::string p = "hiera.blocks." + std::to_string(i);
+    NEED(n1w, p + ".norm1.weight");
+    NEED(n1b, p + ".norm1.bias");
+    NEED(n2w, p + ".norm2.weight");
+    NEED(n2b, p + ".norm2.bias");
+    B.n1w = upload_vec(ctx, *n1w, &rc);
+    B.n1b = upload_vec(ctx, *n1b, &rc);
+    B.n2w = upload_vec(ctx, *n2w, &rc);
+    B.n2b = upload_vec(ctx, *n2b, &rc);
+    NEED(qw, p + ".attn.qkv.weight");
+    NEED(qb, p + ".attn.qkv.bias");
+    NEED(pw, p + ".attn.proj.weight");
+    NEED(pb, p + ".attn.proj.bias");
+    NEED(f1w, p + ".mlp.fc1.weight");
+    NEED(f1b, p + ".mlp.fc1.bias");
+    NEED(f2w, p + ".mlp.fc2.weight");
+    NEED(f2b, p + ".mlp.fc2.bias");
+    if ((rc = upload_linear(ctx, *qw, qb, B.qkv))) return rc;
+    if ((rc = upload_linear(ctx, *pw, pb, B.proj))) return rc;
+    if ((rc = upload_linear(ctx, *f1w, f1b, B.fc1))) return rc;
+    if ((rc = upload_linear(ctx, *f2w, f2b, B.fc2))) return rc;
+    if (B.dim_in != B.dim_out) {
+      NEED(dw, p + ".proj.weight");
+      NEED(db, p + ".proj.bias");
+      if ((rc = upload_linear(ctx, *dw, db, B.dim_proj))) return rc;
+      B.has_dim_proj = true;
+    }
+  }
+  for (int i = 0; i < 4; ++i) {
+    const std::string p = "fpn.convs." + std::to_string(i);
+    NEED(w, p + ".weight");
+    NEED(b, p + ".bias");
+    if ((rc = upload_linear(ctx, *w, b, M.fpn[i]))) return rc;
+  }
+  return load_mem_attn(ctx, idx);
+}
+
+int load_model(s3b_ctx* ctx, const std::string& path) {
+  HParams hp;
+  std::vector<FileTensor> tensors;
+  std::string err;
+  int rc = read_ggml_file(path, hp, tensors, err);
+  if (rc) return set_error(ctx, rc, "%s", err.c_str());
+  ctx->model = Model();
+  ctx->model.hp = hp;
+  Index idx;
+  for (const FileTensor& t : tensors) idx.m[t.name] = &t;
+  cudaSetDevice(ctx->device);
+  rc = hp.is_sam2 ? load_sam2(ctx, idx) : load_sam3(ctx, idx);
+  if (rc) return rc;
+  ctx->model.loaded = true;
+  return kOk;
+}
+
+}  // namespace s3b

@@ -1,0 +1,253 @@
+// SAM 3 image encoder on B200: ViT backbone + SimpleFPN neck (host
+// orchestration, C++14). Replaces sam3_build_vit_graph (sam3.cpp:3835-3849),
+// sam3_build_vit_prefix_graph (3806-3830), sam3_vit_block_forward (3710-3801)
+// and sam3_build_neck_graph (3863-3921) with a fixed sequence of kernel
+// launches on the context's stream; nothing is re-planned per frame.
+//
+// Activation layout: token-major, channel-last (ggml [C, W, H, B] memory),
+// rows = frame * H*W + y*W + x. The residual stream stays f32; GEMM inputs
+// are f16; window partition / unpartition are folded into the LayerNorm row
+// gather and the projection epilogue's row map.
+#include <math.h>
+#include <string.h>
+
+#include "engine.h"
+
+namespace s3b {
+
+#define CK(call)                                                                               \
+  do {                                                                                         \
+    int _rc = (call);                                                                          \
+    if (_rc) return set_error(ctx, _rc < -9 ? kErrCuda : kErrArg, "%s failed (%d) at %s:%d", #call, _rc, \
+                              __FILE__, __LINE__);                                             \
+  } while (0)
+
+static int gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long long M, const EpiParams& ep) {
+  return gemm_f16(A, lda, L.w->as<__half>(), L.Kpad, (int)M, L.N, L.Kpad, ep, ctx->d_err, ctx->stream);
+}
+
+static EpiParams epi_store(const Linear& L, void* out, int out_f32, long long ldo, int act = ACT_NONE) {
+  EpiParams ep;
+  ep.mode = EPI_STORE;
+  ep.bias = L.b ? L.b->as<float>() : nullptr;
+  ep.out = out;
+  ep.out_f32 = out_f32;
+  ep.ldo = ldo;
+  ep.act = act;
+  return ep;
+}
+
+// One ViT block (sam3_vit_block_forward, sam3.cpp:3710-3801) on T tokens.
+static int vit_block(s3b_ctx* ctx, const VitBlock& B, int F, float* x, __half* xn, __half* q, __half* k, __half* v,
+                     __half* ao, __half* hbuf) {
+  const HParams& hp = ctx->model.hp;
+  const int E = hp.vit_embed_dim, NH = hp.vit_num_heads, HD = E / NH, G = hp.n_img_embd();
+  const long long T = (long long)F * G * G;
+  RowMap wmap;
+  int ntok, nwin;
+  if (!B.global) {
+    const int ws = hp.vit_window_size;
+    const int nw = (G + ws - 1) / ws;
+    wmap.kind = 1;
+    wmap.ws = ws;
+    wmap.nww = wmap.nwh = nw;
+    wmap.W = wmap.H = G;
+    ntok = ws * ws;
+    nwin = F * nw * nw;
+  } else {
+    ntok = G * G;
+    nwin = F;
+  }
+  const long long Tw = (long long)nwin * ntok;  // rows in window order (>= T when padded)
+  // norm1 + window partition (ggml_win_part, sam3.cpp:3730)
+  CK(layernorm(x, E, xn, 0, E, Tw, E, B.n1w.ptr(), B.n1b.ptr(), 1e-5f, wmap, ctx->stream));
+  // qkv + bias + split + RoPE(q, k) (sam3.cpp:3738-3771)
+  EpiParams ep;
+  ep.mode = EPI_QKV;
+  ep.bias = B.qkv.b->as<float>();
+  ep.q = q;
+  ep.k = k;
+  ep.v = v;
+  ep.C = E;
+  ep.D = HD;
+  ep.heads = NH;
+  ep.ntok = ntok;
+  ep.rope = B.rope ? B.rope->as<float>() : nullptr;
+  if (ep.rope && B.rope_n != ntok)
+    return set_error(ctx, kErrFormat, "freqs_cis has %d positions, attention has %d", B.rope_n, ntok);
+  ep.qscale = 1.0f;
+  CK(gemm(ctx, xn, E, B.qkv, Tw, ep));
+  // flash attention, scale 1/sqrt(HD) (sam3.cpp:3773-3774); output rows in window order
+  AttnParams ap;
+  ap.q = q;
+  ap.k = k;
+  ap.v = v;
+  ap.o = ao;
+  ap.q_bh = ap.k_bh = ap.v_bh = (long long)ntok * HD;
+  ap.q_n = ap.k_n = ap.v_n = HD;
+  ap.heads = NH;
+  ap.nq = ap.nk = ntok;
+  ap.o_b = (long long)ntok * E;
+  ap.o_n = E;
+  ap.scale = 1.0f / sqrtf((float)HD);
+  CK(attention(ap, HD, nwin * NH, ctx->stream));
+  // proj + bias + window unpartition + residual (sam3.cpp:3779-3787)
+  EpiParams pe = epi_store(B.proj, x, 1, E);
+  pe.map = wmap;
+  pe.resid = x;
+  pe.ldr = E;
+  CK(gemm(ctx, ao, E, B.proj, Tw, pe));
+  // norm2 -> fc1 + GELU(erf) -> fc2 + residual (sam3.cpp:3789-3798)
+  RowMap id;
+  CK(layernorm(x, E, xn, 0, E, T, E, B.n2w.ptr(), B.n2b.ptr(), 1e-5f, id, ctx->stream));
+  const int MLP = B.fc1.N;
+  CK(gemm(ctx, xn, E, B.fc1, T, epi_store(B.fc1, hbuf, 0, MLP, ACT_GELU_ERF)));
+  EpiParams f2 = epi_store(B.fc2, x, 1, E);
+  f2.resid = x;
+  f2.ldr = E;
+  CK(gemm(ctx, hbuf, MLP, B.fc2, T, f2));
+  return kOk;
+}
+
+// conv 3x3 (pad 1) as im2col + GEMM, channel-last f16 in -> f32 out.
+static int conv3x3(s3b_ctx* ctx, const Linear& L, const __half* in, int F, int S, float* out, __half* col) {
+  CK(im2col_3x3_cl(in, F, S, S, L.K / 9, col, ctx->stream));
+  CK(gemm(ctx, col, L.Kpad, L, (long long)F * S * S, epi_store(L, out, 1, L.N)));
+  return kOk;
+}
+
+// One SimpleFPN path (sam3_build_neck_graph, sam3.cpp:3863-3921) for F frames.
+static int vit_neck(s3b_ctx* ctx, const NeckScale* sc, const __half* xh, int F, float* const outs[4]) {
+  const HParams& hp = ctx->model.hp;
+  const int G = hp.n_img_embd();
+  int rc = 0;
+  const long long T = (long long)F * G * G;
+  const int c_mid = sc[0].dc1.N / 4;  // 512
+  const int D = sc[0].c1.N;           // 256
+  DevBuf* d1 = ctx->buf("neck_d1", (size_t)T * 4 * c_mid * 2, &rc);
+  DevBuf* d2 = ctx->buf("neck_d2", (size_t)T * 16 * D * 2, &rc);
+  DevBuf* c1 = ctx->buf("neck_c1", (size_t)T * 16 * D * 2, &rc);
+  DevBuf* col = ctx->buf("neck_col", (size_t)T * 16 * 9 * D * 2, &rc);
+  DevBuf* mp = ctx->buf("neck_mp", (size_t)T / 4 * hp.vit_embed_dim * 2, &rc);
+  if (rc) return rc;
+  // scale 0: deconv(E->512) + GELU(erf) -> deconv(512->D) -> 1x1 -> 3x3  (4x)
+  {
+    EpiParams e1 = epi_store(sc[0].dc1, d1->p, 0, c_mid, ACT_GELU_ERF);
+    e1.mode = EPI_DECONV2;
+    e1.cout = c_mid;
+    e1.map.W = e1.map.H = G;
+    CK(gemm(ctx, xh, hp.vit_embed_dim, sc[0].dc1, T, e1));
+    EpiParams e2 = epi_store(sc[0].dc2, d2->p, 0, D);
+    e2.mode = EPI_DECONV2;
+    e2.cout = D;
+    e2.map.W = e2.map.H = 2 * G;
+    CK(gemm(ctx, d1->as<__half>(), c_mid, sc[0].dc2, T * 4, e2));
+    CK(gemm(ctx, d2->as<__half>(), D, sc[0].c1, T * 16, epi_store(sc[0].c1, c1->p, 0, D)));
+    if ((rc = conv3x3(ctx, sc[0].c3, c1->as<__half>(), F, 4 * G, outs[0], col->as<__half>()))) return rc;
+  }
+  // scale 1: deconv(E->512) -> 1x1 (512->D) -> 3x3  (2x)
+  {
+    EpiParams e1 = epi_store(sc[1].dc1, d1->p, 0, c_mid);
+    e1.mode = EPI_DECONV2;
+    e1.cout = c_mid;
+    e1.map.W = e1.map.H = G;
+    CK(gemm(ctx, xh, hp.vit_embed_dim, sc[1].dc1, T, e1));
+    CK(gemm(ctx, d1->as<__half>(), c_mid, sc[1].c1, T * 4, epi_store(sc[1].c1, c1->p, 0, D)));
+    if ((rc = conv3x3(ctx, sc[1].c3, c1->as<__half>(), F, 2 * G, outs[1], col->as<__half>()))) return rc;
+  }
+  // scale 2: 1x1 (E->D) -> 3x3  (1x)
+  {
+    CK(gemm(ctx, xh, hp.vit_embed_dim, sc[2].c1, T, epi_store(sc[2].c1, c1->p, 0, D)));
+    if ((rc = conv3x3(ctx, sc[2].c3, c1->as<__half>(), F, G, outs[2], col->as<__half>()))) return rc;
+  }
+  // scale 3: maxpool 2x2 -> 1x1 -> 3x3  (0.5x)
+  {
+    CK(maxpool2_cl_f16(xh, F, G, G, hp.vit_embed_dim, mp->as<__half>(), ctx->stream));
+    CK(gemm(ctx, mp->as<__half>(), hp.vit_embed_dim, sc[3].c1, T / 4, epi_store(sc[3].c1, c1->p, 0, D)));
+    if ((rc = conv3x3(ctx, sc[3].c3, c1->as<__half>(), F, G / 2, outs[3], col->as<__half>()))) return rc;
+  }
+  return kOk;
+}
+
+int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
+  Model& M = ctx->model;
+  const HParams& hp = M.hp;
+  const int E = hp.vit_embed_dim, G = hp.n_img_embd(), P = hp.patch_size, S = hp.img_size;
+  const long long tok_per_frame = (long long)G * G;
+  int rc = 0;
+  Outputs& O = ctx->out;
+  const bool want_neck = !(flags & 1) && M.has_neck_trk;
+  const bool want_det = want_neck && M.has_neck_det && !(flags & 2);
+  // outputs
+  if (O.n_frames != n_frames || O.img_size != S || !O.backbone) {
+    O = Outputs();
+    O.n_frames = n_frames;
+    O.img_size = S;
+    O.backbone = std::make_shared<DevBuf>();
+    if (O.backbone->reserve((size_t)n_frames * tok_per_frame * E * 4)) return set_error(ctx, kErrOOM, "out alloc");
+  }
+  const int sizes[4] = {4 * G, 2 * G, G, G / 2};
+  if (want_neck) {
+    O.n_fpn = 4;
+    for (int i = 0; i < 4; ++i) {
+      O.fpn_size[i] = sizes[i];
+      if (!O.fpn[i]) O.fpn[i] = std::make_shared<DevBuf>();
+      if (O.fpn[i]->reserve((size_t)n_frames * sizes[i] * sizes[i] * hp.neck_dim * 4))
+        return set_error(ctx, kErrOOM, "out alloc");
+      if (want_det) {
+        if (!O.det[i]) O.det[i] = std::make_shared<DevBuf>();
+        if (O.det[i]->reserve((size_t)n_frames * sizes[i] * sizes[i] * hp.neck_dim * 4))
+          return set_error(ctx, kErrOOM, "out alloc");
+      }
+    }
+    O.n_det = want_det ? 4 : 0;
+  }
+  const int FB = ctx->max_frames_per_pass;
+  const long long Tmax = (long long)FB * tok_per_frame;
+  const int Kp = M.patch.Kpad;
+  // workspace (window order never exceeds T for the ViT: 72 = 3 x 24)
+  DevBuf* col = ctx->buf("vit_col", (size_t)Tmax * Kp * 2, &rc);
+  DevBuf* xp = ctx->buf("vit_xp", (size_t)Tmax * E * 4, &rc);
+  DevBuf* xn = ctx->buf("vit_xn", (size_t)Tmax * E * 2, &rc);
+  DevBuf* q = ctx->buf("vit_q", (size_t)Tmax * E * 2, &rc);
+  DevBuf* k = ctx->buf("vit_k", (size_t)Tmax * E * 2, &rc);
+  DevBuf* v = ctx->buf("vit_v", (size_t)Tmax * E * 2, &rc);
+  DevBuf* ao = ctx->buf("vit_ao", (size_t)Tmax * E * 2, &rc);
+  DevBuf* hb = ctx->buf("vit_h", (size_t)Tmax * hp.vit_mlp_dim * 2, &rc);
+  if (rc) return rc;
+  for (int f0 = 0; f0 < n_frames; f0 += FB) {
+    const int F = (n_frames - f0) < FB ? (n_frames - f0) : FB;
+    const long long T = (long long)F * tok_per_frame;
+    float* x = O.backbone->as<float>() + (size_t)f0 * tok_per_frame * E;
+    // patch embed (conv 14x14/s14, no bias) + tiled abs pos (sam3.cpp:3815-3822)
+    CK(im2col_image(d_chw + (size_t)f0 * 3 * S * S, F, 3, S, S, P, P, 0, G, G, col->as<__half>(), Kp, ctx->stream));
+    EpiParams pe = epi_store(M.patch, xp->p, 1, E);
+    pe.resid = M.pos_tiled->as<float>();
+    pe.ldr = E;
+    pe.resid_mod = tok_per_frame;
+    CK(gemm(ctx, col->as<__half>(), Kp, M.patch, T, pe));
+    // ln_pre (sam3.cpp:3825-3827)
+    RowMap id;
+    CK(layernorm(xp->as<float>(), E, x, 1, E, T, E, M.ln_pre_w.ptr(), M.ln_pre_b.ptr(), 1e-5f, id, ctx->stream));
+    for (int b = 0; b < hp.vit_depth; ++b) {
+      if ((rc = vit_block(ctx, M.vit[b], F, x, xn->as<__half>(), q->as<__half>(), k->as<__half>(), v->as<__half>(),
+                          ao->as<__half>(), hb->as<__half>())))
+        return rc;
+    }
+    if (want_neck) {
+      // neck input in f16 (ggml converts the conv input to the f16 kernel type)
+      __half* xh = xn->as<__half>();
+      CK(cast_f32_f16(x, T * E, xh, ctx->stream));
+      float* outs[4];
+      for (int i = 0; i < 4; ++i) outs[i] = O.fpn[i]->as<float>() + (size_t)f0 * sizes[i] * sizes[i] * hp.neck_dim;
+      if ((rc = vit_neck(ctx, M.neck_trk, xh, F, outs))) return rc;
+      if (want_det) {
+        for (int i = 0; i < 4; ++i) outs[i] = O.det[i]->as<float>() + (size_t)f0 * sizes[i] * sizes[i] * hp.neck_dim;
+        if ((rc = vit_neck(ctx, M.neck_det, xh, F, outs))) return rc;
+      }
+    }
+  }
+  return check_device(ctx, "vit_encode");
+}
+
+}  // namespace s3b

@@ -1,0 +1,236 @@
+"""Seeded synthetic models and frames in sam3.cpp's .ggml format.
+
+There are no checkpoints on this machine, so benchmarks and parity tests use
+random-init weights of the reference architectures: every weight and bias
+N(0, 0.02), LayerNorm gamma = 1, beta = 0 (or a seeded random affine for
+tests), drawn from numpy.random.default_rng(seed) in file-record order.
+Values are rounded to the file dtype chosen by the reference converter
+(convert_sam3_to_ggml.py write_tensor) and, for q4_0 / q4_1 / q8_0 models,
+quantised with the reference quantiser's selection rule
+(examples/quantize.cpp:195-223). RoPE tables (`attn.freqs_cis`) are not
+random: they follow compute_axial_cis (sam3.cpp:3555-3586; window blocks
+scale 1, global blocks scale window/grid).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import ggml_io
+
+
+# ---------------------------------------------------------------- configs
+@dataclass
+class Sam3Config:
+    img_size: int = 1008
+    patch: int = 14
+    embed: int = 1024
+    depth: int = 32
+    heads: int = 16
+    mlp_ratio_x1000: int = 4625
+    window: int = 24
+    global_idx: tuple = (7, 15, 23, 31)
+    neck_dim: int = 256
+    neck_mid: int = 512
+    visual_only: int = 1
+    with_mem_attn: bool = False
+    mem_out_dim: int = 64
+    mem_attn_layers: int = 4
+    num_maskmem: int = 7
+    max_obj_ptrs: int = 16
+    mem_ffn: int = 2048
+
+    @property
+    def grid(self) -> int:
+        return self.img_size // self.patch
+
+    @property
+    def mlp(self) -> int:
+        return int(np.float32(self.embed) * np.float32(self.mlp_ratio_x1000 / 1000.0))
+
+    @property
+    def pretrain_grid(self) -> int:
+        return self.grid // 3 if self.grid % 3 == 0 else self.grid
+
+    def hparams(self) -> list[int]:
+        # sam3_load_hparams order (sam3.cpp:1477-1520); n_global entries of global_attn_idx
+        hp = [self.img_size, self.patch, self.embed, self.depth, self.heads, self.mlp_ratio_x1000, self.window,
+              len(self.global_idx), *self.global_idx]
+        hp += [1024, 16, 24, 32, 49408, 256]              # text encoder (unused by the engine)
+        hp += [self.neck_dim]
+        hp += [6, 8, 2048, 6, 8, 2048, 200, 3, 1, 4]      # fenc, ddec, geom, presence, geom queries
+        hp += [256, 2, 3, 3]                              # sam decoder
+        hp += [self.mem_out_dim, self.mem_attn_layers, self.num_maskmem, self.max_obj_ptrs]
+        hp += [2, self.visual_only]                       # n_amb_experts, visual_only
+        return hp
+
+
+SAM3_VIT_L = Sam3Config()
+
+
+# ---------------------------------------------------------------- RoPE / PE
+def axial_cis(dim: int, end_x: int, end_y: int, theta: float = 10000.0, scale: float = 1.0) -> np.ndarray:
+    """compute_axial_cis as (cos, sin) pairs: [end_x*end_y, dim//2, 2] f32."""
+    q = dim // 4
+    freqs = (1.0 / (np.float32(theta) ** (np.arange(0, dim, 4, dtype=np.float32)[:q] / np.float32(dim)))).astype(np.float32)
+    t = np.arange(end_x * end_y, dtype=np.float32)
+    tx = (t % end_x).astype(np.float32) * np.float32(scale)
+    ty = np.floor(t / end_x).astype(np.float32) * np.float32(scale)
+    ax = np.outer(tx, freqs).astype(np.float32)
+    ay = np.outer(ty, freqs).astype(np.float32)
+    ang = np.concatenate([ax, ay], axis=1)
+    return np.stack([np.cos(ang), np.sin(ang)], axis=-1).astype(np.float32)
+
+
+# ---------------------------------------------------------------- tensors
+class _Gen:
+    def __init__(self, seed: int, ln_random: bool):
+        self.rng = np.random.default_rng(seed)
+        self.ln_random = ln_random
+
+    def w(self, *shape, std=0.02):
+        return (self.rng.standard_normal(shape, dtype=np.float32) * np.float32(std)).astype(np.float32)
+
+    def ln(self, n):
+        if self.ln_random:
+            g = 1.0 + self.w(n, std=0.1)
+            b = self.w(n, std=0.1)
+            return g.astype(np.float32), b
+        return np.ones(n, np.float32), np.zeros(n, np.float32)
+
+
+def _neck(g: _Gen, T: dict, pfx: str, E: int, D: int, mid: int):
+    T[pfx + "0.dconv_2x2_0.weight"] = g.w(E, mid, 2, 2)       # ConvTranspose2d [Cin, Cout, kH, kW]
+    T[pfx + "0.dconv_2x2_0.bias"] = g.w(mid)
+    T[pfx + "0.dconv_2x2_1.weight"] = g.w(mid, D, 2, 2)
+    T[pfx + "0.dconv_2x2_1.bias"] = g.w(D)
+    T[pfx + "0.conv_1x1.weight"] = g.w(D, D, 1, 1)
+    T[pfx + "0.conv_1x1.bias"] = g.w(D)
+    T[pfx + "0.conv_3x3.weight"] = g.w(D, D, 3, 3)
+    T[pfx + "0.conv_3x3.bias"] = g.w(D)
+    T[pfx + "1.dconv_2x2.weight"] = g.w(E, mid, 2, 2)
+    T[pfx + "1.dconv_2x2.bias"] = g.w(mid)
+    T[pfx + "1.conv_1x1.weight"] = g.w(D, mid, 1, 1)
+    T[pfx + "1.conv_1x1.bias"] = g.w(D)
+    T[pfx + "1.conv_3x3.weight"] = g.w(D, D, 3, 3)
+    T[pfx + "1.conv_3x3.bias"] = g.w(D)
+    for s in (2, 3):
+        T[pfx + f"{s}.conv_1x1.weight"] = g.w(D, E, 1, 1)
+        T[pfx + f"{s}.conv_1x1.bias"] = g.w(D)
+        T[pfx + f"{s}.conv_3x3.weight"] = g.w(D, D, 3, 3)
+        T[pfx + f"{s}.conv_3x3.bias"] = g.w(D)
+
+
+def _mem_attn(g: _Gen, T: dict, D: int, MD: int, layers: int, ffn: int, num_maskmem: int):
+    for i in range(layers):
+        p = f"mem_attn.layers.{i}"
+        for a in ("sa.q_proj", "sa.k_proj", "sa.v_proj", "sa.out_proj", "ca.q_proj"):
+            T[f"{p}.{a}.weight"] = g.w(D, D)
+            T[f"{p}.{a}.bias"] = g.w(D)
+        T[f"{p}.ca.k_proj.weight"] = g.w(D, MD)
+        T[f"{p}.ca.k_proj.bias"] = g.w(D)
+        T[f"{p}.ca.v_proj.weight"] = g.w(D, MD)
+        T[f"{p}.ca.v_proj.bias"] = g.w(D)
+        T[f"{p}.ca.out_proj.weight"] = g.w(D, D)
+        T[f"{p}.ca.out_proj.bias"] = g.w(D)
+        T[f"{p}.linear1.weight"] = g.w(ffn, D)
+        T[f"{p}.linear1.bias"] = g.w(ffn)
+        T[f"{p}.linear2.weight"] = g.w(D, ffn)
+        T[f"{p}.linear2.bias"] = g.w(D)
+        for n in ("norm1", "norm2", "norm3"):
+            T[f"{p}.{n}.weight"], T[f"{p}.{n}.bias"] = g.ln(D)
+    T["mem_attn.norm.weight"], T["mem_attn.norm.bias"] = g.ln(D)
+    T["mem_enc.tpos_enc"] = g.w(num_maskmem, 1, 1, MD)
+    T["obj_ptr_tpos_proj.weight"] = g.w(MD, D)
+    T["obj_ptr_tpos_proj.bias"] = g.w(MD)
+
+
+def sam3_tensors(cfg: Sam3Config, seed: int = 0, ln_random: bool = False, neck_det: bool = False) -> dict:
+    """name -> f32 array (PyTorch shape) of a SAM 3 image encoder (+ optional memory attention)."""
+    g = _Gen(seed, ln_random)
+    E, G, W = cfg.embed, cfg.grid, cfg.window
+    T: dict[str, np.ndarray] = {}
+    T["vit.patch_embed.proj.weight"] = g.w(E, 3, cfg.patch, cfg.patch)
+    T["vit.pos_embed"] = g.w(cfg.pretrain_grid, cfg.pretrain_grid, E)
+    T["vit.ln_pre.weight"], T["vit.ln_pre.bias"] = g.ln(E)
+    for i in range(cfg.depth):
+        p = f"vit.blocks.{i}"
+        T[f"{p}.norm1.weight"], T[f"{p}.norm1.bias"] = g.ln(E)
+        T[f"{p}.attn.qkv.weight"] = g.w(3 * E, E)
+        T[f"{p}.attn.qkv.bias"] = g.w(3 * E)
+        T[f"{p}.attn.proj.weight"] = g.w(E, E)
+        T[f"{p}.attn.proj.bias"] = g.w(E)
+        T[f"{p}.norm2.weight"], T[f"{p}.norm2.bias"] = g.ln(E)
+        T[f"{p}.mlp.lin1.weight"] = g.w(cfg.mlp, E)
+        T[f"{p}.mlp.lin1.bias"] = g.w(cfg.mlp)
+        T[f"{p}.mlp.lin2.weight"] = g.w(E, cfg.mlp)
+        T[f"{p}.mlp.lin2.bias"] = g.w(E)
+        hd = E // cfg.heads
+        if i in cfg.global_idx:
+            T[f"{p}.attn.freqs_cis"] = axial_cis(hd, G, G, scale=W / G)
+        else:
+            T[f"{p}.attn.freqs_cis"] = axial_cis(hd, W, W, scale=1.0)
+    if neck_det and not cfg.visual_only:
+        _neck(g, T, "neck.det.", E, cfg.neck_dim, cfg.neck_mid)
+    _neck(g, T, "neck.trk.", E, cfg.neck_dim, cfg.neck_mid)
+    if cfg.with_mem_attn:
+        _mem_attn(g, T, cfg.neck_dim, cfg.mem_out_dim, cfg.mem_attn_layers, cfg.mem_ffn, cfg.num_maskmem)
+    return T
+
+
+# ---------------------------------------------------------------- files
+def _round_to_dtype(name: str, a: np.ndarray, ftype: int) -> tuple[int, np.ndarray]:
+    dt = ggml_io.file_dtype(name, a.ndim, ftype)
+    if dt == ggml_io.F16:
+        a = a.astype(np.float16).astype(np.float32)
+    return dt, a
+
+
+def stored_values(T: dict, ftype: int = 1, qtype: int | None = None, quantize=None, dequantize=None) -> dict:
+    """The f32 values the engine sees after file-dtype rounding and quantisation."""
+    out = {}
+    for name, a in T.items():
+        dt, v = _round_to_dtype(name, a, ftype)
+        if qtype is not None and ggml_io.quantisable(name, v.shape, dt):
+            raw = quantize(qtype, v.reshape(-1, v.shape[-1]))
+            v = dequantize(qtype, raw, v.shape[-1]).reshape(v.shape)
+        out[name] = v
+    return out
+
+
+def write_model(path: str, T: dict, hparams: list[int], magic: int, version: int, ftype: int = 1,
+                qtype: int | None = None, quantize=None):
+    """Writes T (name -> f32 array, PyTorch shape) as a .ggml file.
+
+    ftype 0/1 follows the converter's dtype rule; with `qtype` the quantisable
+    tensors are then stored as q4_0 / q4_1 / q8_0 blocks (quantize(qtype, rows)
+    returns the raw blocks, e.g. sam3_b200.quantize_rows)."""
+    recs = []
+    for name, a in T.items():
+        dt, v = _round_to_dtype(name, a, ftype)
+        if qtype is not None and ggml_io.quantisable(name, v.shape, dt):
+            raw = quantize(qtype, v.reshape(-1, v.shape[-1]))
+            recs.append(ggml_io.Record(name, qtype, v.shape, raw.tobytes()))
+        elif dt == ggml_io.F16:
+            recs.append(ggml_io.Record(name, dt, v.shape, v.astype(np.float16).tobytes()))
+        else:
+            recs.append(ggml_io.Record(name, dt, v.shape, np.ascontiguousarray(v, np.float32).tobytes()))
+    file_ftype = qtype if qtype is not None else ftype
+    ggml_io.write(path, magic, version, file_ftype, hparams, recs)
+
+
+def write_sam3(path: str, cfg: Sam3Config, seed: int = 0, ftype: int = 1, qtype: int | None = None,
+               quantize=None, ln_random: bool = False, neck_det: bool = False) -> dict:
+    T = sam3_tensors(cfg, seed, ln_random=ln_random, neck_det=neck_det)
+    write_model(path, T, cfg.hparams(), ggml_io.MAGIC_SAM3, 3, ftype, qtype, quantize)
+    return T
+
+
+def frames_u8(n: int, size: int, base_seed: int = 1000) -> np.ndarray:
+    """Seeded uniform uint8 frames [n, size, size, 3] (frame i from default_rng(base_seed + i))."""
+    out = np.empty((n, size, size, 3), dtype=np.uint8)
+    for i in range(n):
+        out[i] = np.random.default_rng(base_seed + i).integers(0, 256, size=(size, size, 3), dtype=np.uint8)
+    return out

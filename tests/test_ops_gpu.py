@@ -1,0 +1,96 @@
+"""Kernel-level parity through the C ABI: tensor-core GEMM, flash attention,
+LayerNorm and block dequantisation against fp32 references on the same inputs."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _ref_gemm(A, B, bias, act, resid):
+    y = A.float() @ B.float().T
+    if bias is not None:
+        y = y + bias
+    if act == 1:
+        y = torch.nn.functional.gelu(y)
+    elif act == 2:
+        y = torch.nn.functional.gelu(y, approximate="tanh")
+    elif act == 3:
+        y = torch.relu(y)
+    if resid is not None:
+        y = y + resid
+    return y
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 96, 96), (5184, 3072, 1024), (1000, 4736, 1024),
+                                   (777, 1024, 4736), (64, 128, 592), (4097, 288, 152), (256, 512, 2304)])
+@pytest.mark.parametrize("act", [0, 1])
+def test_gemm(engine, M, N, K, act):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K + act)
+    A = (torch.randn(M, K, device="cuda", generator=g) * 0.5).half()
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    resid = torch.randn(M, N, device="cuda", generator=g) if act == 0 else None
+    out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    engine.gemm(A, B, out, bias=bias, act=act, resid=resid)
+    engine.sync()
+    ref = _ref_gemm(A, B, bias, act, resid)
+    err = (out - ref).abs().max().item()
+    tol = 2e-3 * max(1.0, ref.abs().max().item()) + 1e-4 * K ** 0.5
+    assert err < tol, f"max abs err {err} (tol {tol})"
+
+
+def test_gemm_f16_out_strided(engine):
+    M, N, K = 513, 640, 320
+    A_full = torch.randn(M, K + 64, device="cuda").half()
+    A = A_full[:, :K]
+    B = (torch.randn(N, K, device="cuda") * 0.05).half()
+    out = torch.zeros(M, N, device="cuda", dtype=torch.float16)
+    engine.gemm(A, B, out, act=3)
+    engine.sync()
+    ref = torch.relu(A.float() @ B.float().T)
+    assert (out.float() - ref).abs().max().item() < 1e-2
+
+
+@pytest.mark.parametrize("D,nq,nk,heads,batch", [(64, 576, 576, 16, 2), (64, 5184, 5184, 2, 1), (96, 49, 196, 8, 3),
+                                                 (96, 4096, 4096, 1, 1), (80, 100, 100, 2, 2),
+                                                 (256, 1000, 3000, 1, 1), (128, 70, 33, 3, 2)])
+def test_attention(engine, D, nq, nk, heads, batch):
+    g = torch.Generator(device="cuda").manual_seed(D + nq + nk)
+    q = torch.randn(batch, heads, nq, D, device="cuda", generator=g).half()
+    k = torch.randn(batch, heads, nk, D, device="cuda", generator=g).half()
+    v = torch.randn(batch, heads, nk, D, device="cuda", generator=g).half()
+    out = torch.empty(batch, nq, heads * D, device="cuda", dtype=torch.float16)
+    scale = 1.0 / D ** 0.5
+    engine.attention(q, k, v, out, scale)
+    engine.sync()
+    ref = torch.softmax((q.float() @ k.float().transpose(-1, -2)) * scale, dim=-1) @ v.float()
+    ref = ref.permute(0, 2, 1, 3).reshape(batch, nq, heads * D)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 2e-2, err
+
+
+@pytest.mark.parametrize("rows,C,f32", [(5184, 1024, 0), (1000, 96, 1), (37, 256, 0), (64, 1152, 1)])
+def test_layernorm(engine, rows, C, f32):
+    x = torch.randn(rows, C, device="cuda") * 3 + 1
+    g = torch.randn(C, device="cuda")
+    b = torch.randn(C, device="cuda")
+    out = torch.empty(rows, C, device="cuda", dtype=torch.float32 if f32 else torch.float16)
+    engine.layernorm(x, out, g, b, 1e-6)
+    engine.sync()
+    ref = torch.nn.functional.layer_norm(x, (C,), g, b, 1e-6)
+    assert (out.float() - ref).abs().max().item() < (2e-5 * C ** 0.5 + 1e-4 if f32 else 2e-2)
+
+
+@pytest.mark.parametrize("qtype", [2, 3, 8])
+def test_dequant_bit_exact(engine, s3b, qtype):
+    from oracle import quant
+    rng = np.random.default_rng(qtype)
+    x = rng.standard_normal((64, 4736)).astype(np.float32) * 0.02
+    raw = quant.quantize(qtype, x)
+    ref = quant.dequantize(qtype, raw, 4736)
+    d_raw = torch.from_numpy(raw).cuda()
+    out = torch.empty(64, 4736, device="cuda", dtype=torch.float32)
+    engine.dequantize(d_raw, qtype, 4736, 64, out)
+    engine.sync()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
