@@ -62,6 +62,15 @@ int s3b_sync(s3b_ctx* ctx);
 /* Options: "frames_per_pass" (encoder micro-batch, default 8). */
 int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value);
 
+/* Profiling (CUDA events on the context stream around every GEMM and
+ * attention launch; the reference times compute with std::chrono around
+ * ggml_backend_graph_compute, sam3.cpp:6118-6131). s3b_profile_end waits for
+ * the stream and writes out[0..8]: GEMM {launches, ms, flops, bytes},
+ * attention {launches, ms, flops, bytes}, and the total number of kernel
+ * launches since s3b_profile_begin. */
+int s3b_profile_begin(s3b_ctx* ctx, int with_events);
+int s3b_profile_end(s3b_ctx* ctx, double* out, int n);
+
 /* ---------------------------------------------------------------- model */
 
 /* Loads the encoder / memory-attention weights of a .ggml file (SAM 3 or
@@ -69,6 +78,13 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value);
  * Replaces sam3_load_model + sam3_load_tensors (sam3.cpp:3091-3344);
  * tensors outside the engine's scope are skipped. */
 int s3b_load_model(s3b_ctx* ctx, const char* path);
+
+/* Parses a .ggml file on the host only (no device needed) and checks every
+ * record: info[0] = 1 for SAM 2 else 0, info[1] = img_size, info[2] = number
+ * of tensor records, info[3] = file ftype, info[4] = backbone depth,
+ * info[5] = backbone embed dim, info[6] = records with quantised dtypes.
+ * Returns S3B_ERR_FORMAT / S3B_ERR_IO on corrupt or truncated files. */
+int s3b_inspect_model(const char* path, int32_t* info, int n, char* err, int err_len);
 
 /* info[0] = 1 for SAM 2 (Hiera) else 0, info[1] = img_size, info[2] = number
  * of backbone blocks, info[3] = backbone embed dim, info[4] = neck dim,

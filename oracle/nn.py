@@ -13,13 +13,14 @@ def f16r(x):
 
 def layer_norm(x, w, b, eps):
     """ggml_norm + mul + add over the last dim (sam3.cpp:1036-1060); f64 statistics."""
-    xd = x.astype(np.float64)
-    mean = xd.mean(axis=-1, keepdims=True)
-    var = ((xd - mean) ** 2).mean(axis=-1, keepdims=True)
-    y = (xd - mean) / np.sqrt(var + eps)
-    y = y * w.astype(np.float64)
+    x = np.asarray(x, np.float32)
+    mean = x.mean(axis=-1, keepdims=True, dtype=np.float64)
+    xc = x - mean.astype(np.float32)
+    var = np.square(xc).mean(axis=-1, keepdims=True, dtype=np.float64)
+    y = xc * (1.0 / np.sqrt(var + eps)).astype(np.float32)
+    y = y * w.astype(np.float32)
     if b is not None:
-        y = y + b.astype(np.float64)
+        y = y + b.astype(np.float32)
     return y.astype(np.float32)
 
 
@@ -35,8 +36,8 @@ def linear(x, w, b=None, f16_inputs=False):
 
 def gelu_erf(x):
     from scipy.special import erf
-    xd = x.astype(np.float64)
-    return (0.5 * xd * (1.0 + erf(xd / np.sqrt(2.0)))).astype(np.float32)
+    x = np.asarray(x, np.float32)
+    return (np.float32(0.5) * x * (np.float32(1.0) + erf(x * np.float32(0.7071067811865476)))).astype(np.float32)
 
 
 def gelu_tanh(x):

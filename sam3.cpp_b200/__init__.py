@@ -44,7 +44,10 @@ SYMBOLS = [
     ("s3b_set_stream", _I, [_P, _P]),
     ("s3b_sync", _I, [_P]),
     ("s3b_set_option", _I, [_P, _S, _I64]),
+    ("s3b_profile_begin", _I, [_P, _I]),
+    ("s3b_profile_end", _I, [_P, ctypes.POINTER(ctypes.c_double), _I]),
     ("s3b_load_model", _I, [_P, _S]),
+    ("s3b_inspect_model", _I, [_S, ctypes.POINTER(ctypes.c_int32), _I, _S, _I]),
     ("s3b_model_info", _I, [_P, ctypes.POINTER(ctypes.c_int32), _I]),
     ("s3b_encode_u8", _I, [_P, _P, _I, _I, _I]),
     ("s3b_encode_chw", _I, [_P, _P, _I, _I, _I]),
@@ -137,6 +140,17 @@ def dequantize_rows(qtype: int, raw: np.ndarray, ne0: int) -> np.ndarray:
     return out
 
 
+def inspect_model(path: str) -> dict:
+    """Host-only parse of a .ggml file (s3b_inspect_model); raises S3BError on corrupt files."""
+    info = (ctypes.c_int32 * 7)()
+    err = ctypes.create_string_buffer(512)
+    rc = lib().s3b_inspect_model(path.encode(), info, 7, err, 512)
+    if rc != 0:
+        raise S3BError(f"s3b_inspect_model: {ERRORS.get(rc, rc)}: {err.value.decode()}")
+    keys = ["is_sam2", "img_size", "n_tensors", "ftype", "depth", "embed_dim", "n_quantised"]
+    return dict(zip(keys, list(info)))
+
+
 # ---------------------------------------------------------------- engine
 class Engine:
     """One engine context on one CUDA device (s3b_create / s3b_destroy)."""
@@ -179,6 +193,17 @@ class Engine:
     def set_option(self, key: str, value: int):
         self._check(self._L.s3b_set_option(self.h, key.encode(), value), "s3b_set_option")
 
+    def profile_begin(self, with_events: bool = True):
+        self._check(self._L.s3b_profile_begin(self.h, 1 if with_events else 0), "s3b_profile_begin")
+
+    def profile_end(self) -> dict:
+        buf = (ctypes.c_double * 9)()
+        self._check(self._L.s3b_profile_end(self.h, buf, 9), "s3b_profile_end")
+        v = list(buf)
+        return {"gemm": {"launches": v[0], "ms": v[1], "flops": v[2], "bytes": v[3]},
+                "attention": {"launches": v[4], "ms": v[5], "flops": v[6], "bytes": v[7]},
+                "launches": int(v[8])}
+
     def load_model(self, path: str):
         self._check(self._L.s3b_load_model(self.h, path.encode()), "s3b_load_model")
 
@@ -214,10 +239,12 @@ class Engine:
         self._check(self._L.s3b_output_shape(self.h, name.encode(), ne), "s3b_output_shape")
         return tuple(ne)
 
-    def output(self, name: str, frame: int = 0) -> np.ndarray:
+    def output(self, name: str, frame: int = 0, out: np.ndarray | None = None) -> np.ndarray:
         """Frame `frame` of an output as numpy [H][W][C] (ggml [C, W, H])."""
         ne = self.output_shape(name)
-        out = np.empty((ne[2], ne[1], ne[0]), dtype=np.float32)
+        if out is None:
+            out = np.empty((ne[2], ne[1], ne[0]), dtype=np.float32)
+        assert out.dtype == np.float32 and out.flags.c_contiguous and out.size == ne[0] * ne[1] * ne[2]
         self._check(self._L.s3b_output_copy(self.h, name.encode(), frame, out.ctypes.data, out.size),
                     "s3b_output_copy")
         return out

@@ -187,6 +187,7 @@ void s3b_destroy(s3b_ctx* ctx) {
   ctx->ws.clear();
   ctx->out = Outputs();
   ctx->model = Model();
+  for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -228,12 +229,65 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
   return set_error(ctx, kErrArg, "unknown option '%s'", key);
 }
 
+int s3b_profile_begin(s3b_ctx* ctx, int with_events) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  ctx->prof = with_events != 0;
+  ctx->prof_entries.clear();
+  ctx->event_next = 0;
+  ctx->n_launches = 0;
+  return kOk;
+}
+
+int s3b_profile_end(s3b_ctx* ctx, double* out, int n) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return set_error(ctx, kErrCuda, "synchronize failed");
+  double v[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  for (const auto& e : ctx->prof_entries) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e.a, e.b);
+    const int base = e.kind == 0 ? 0 : 4;
+    v[base + 0] += 1;
+    v[base + 1] += ms;
+    v[base + 2] += e.flops;
+    v[base + 3] += e.bytes;
+  }
+  v[8] = (double)ctx->n_launches;
+  for (int i = 0; i < n && i < 9; ++i) out[i] = v[i];
+  ctx->prof = false;
+  ctx->prof_entries.clear();
+  ctx->event_next = 0;
+  return read_dev_err(ctx);
+}
+
 int s3b_load_model(s3b_ctx* ctx, const char* path) {
   int rc = ctx_enter(ctx);
   if (rc) return rc;
   if (!path) return set_error(ctx, kErrArg, "null path");
   ctx->out = Outputs();
   return load_model(ctx, path);
+}
+
+int s3b_inspect_model(const char* path, int32_t* info, int n, char* err, int err_len) {
+  if (!path) return kErrArg;
+  HParams hp;
+  std::vector<FileTensor> tensors;
+  std::string e;
+  const int rc = read_ggml_file(path, hp, tensors, e);
+  if (rc) {
+    if (err && err_len > 0) snprintf(err, err_len, "%s", e.c_str());
+    return rc;
+  }
+  int nq = 0;
+  for (const auto& t : tensors) nq += (t.dtype == QT_Q4_0 || t.dtype == QT_Q4_1 || t.dtype == QT_Q8_0) ? 1 : 0;
+  int depth = 0;
+  for (int s = 0; s < hp.hiera_num_stages && s < 4; ++s) depth += hp.hiera_stages[s];
+  const int32_t v[7] = {hp.is_sam2, hp.img_size, (int32_t)tensors.size(), hp.ftype,
+                        hp.is_sam2 ? depth : hp.vit_depth, hp.is_sam2 ? hp.hiera_embed_dim : hp.vit_embed_dim, nq};
+  for (int i = 0; i < n && i < 7; ++i) info[i] = v[i];
+  if (err && err_len > 0) err[0] = 0;
+  return kOk;
 }
 
 int s3b_model_info(s3b_ctx* ctx, int32_t* info, int n) {

@@ -207,9 +207,18 @@ struct s3b_ctx {
   // workspace (grown on demand, reused across calls)
   std::map<std::string, std::shared_ptr<s3b::DevBuf>> ws;
   int max_frames_per_pass = 8;
-  // per-kernel timing instrumentation (optional)
-  bool timing = false;
-  std::vector<std::pair<std::string, float>> timings;
+  // launch accounting + optional per-kernel CUDA-event timing (s3b_profile_*)
+  long long n_launches = 0;
+  bool prof = false;
+  struct Prof {
+    int kind;  // 0 GEMM, 1 attention, 2 other
+    double flops, bytes;
+    cudaEvent_t a, b;
+  };
+  std::vector<Prof> prof_entries;
+  std::vector<cudaEvent_t> event_pool;
+  size_t event_next = 0;
+  cudaEvent_t next_event();
 
   s3b::DevBuf* buf(const std::string& name, size_t bytes, int* rc);
 };
@@ -220,7 +229,15 @@ int check_device(s3b_ctx* ctx, const char* where);
 
 // weight preparation (model.cpp)
 int load_model(s3b_ctx* ctx, const std::string& path);
-int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Linear& L, int kpad_to = 8);
+int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Linear& L, int kpad_to = 8,
+                  int k_dims = 1);
+
+// launch helpers shared by the encoders (ops.cpp): count launches and, when
+// profiling is on, bracket the launch with CUDA events on the context stream.
+int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long long M, const EpiParams& ep);
+int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads);
+void count_launch(s3b_ctx* ctx, int n = 1);
+EpiParams epi_store(const Linear& L, void* out, int out_f32, long long ldo, int act = ACT_NONE);
 
 // encoders
 int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);

@@ -138,7 +138,7 @@ int read_ggml_file(const std::string& path, HParams& hp, std::vector<FileTensor>
     for (int i = 0; i < hp.n_global_attn && i < 4; ++i) rd(hp.global_attn_idx[i]);
     for (int i = 0; i < 6; ++i) rd(dummy);  // text_width..text_out_dim
     rd(hp.neck_dim);
-    for (int i = 0; i < 11; ++i) rd(dummy);  // fenc (3), ddec (4), geom, presence, geom queries
+    for (int i = 0; i < 10; ++i) rd(dummy);  // fenc (3), ddec (4), geom, presence, geom queries
     for (int i = 0; i < 4; ++i) rd(dummy);   // sam decoder
     rd(hp.mem_out_dim);
     rd(hp.mem_attn_layers);
@@ -271,10 +271,13 @@ static int upload_b_operand(s3b_ctx* ctx, const std::vector<float>& w, int N, in
   return rc;
 }
 
-int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Linear& L, int kpad_to) {
-  // ggml weight [K, N] (ne0 = K contiguous) == row-major [N][K]
-  const int K = (int)t.ne[0];
-  const int N = (int)(t.nelements() / t.ne[0]);
+int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Linear& L, int kpad_to, int k_dims) {
+  // ggml weight [K, N] (ne0 = K contiguous) == row-major [N][K]; a conv kernel
+  // [kW, kH, Cin, Cout] folds its first k_dims = 3 dims into K.
+  int64_t K64 = 1;
+  for (int i = 0; i < k_dims && i < 4; ++i) K64 *= t.ne[i];
+  const int K = (int)K64;
+  const int N = (int)(t.nelements() / K64);
   std::vector<float> w;
   tensor_to_f32(t, w);
   int rc = upload_b_operand(ctx, w, N, K, kpad_to, L);
@@ -478,7 +481,7 @@ static int load_sam3(s3b_ctx* ctx, const Index& idx) {
   {
     NEED(pw, "vit.patch_embed.proj.weight");
     // ggml [p, p, 3, E] == [E][3][p][p]: row co, column (ci*p + ky)*p + kx (the im2col order)
-    if ((rc = upload_linear(ctx, *pw, nullptr, M.patch, 16))) return rc;
+    if ((rc = upload_linear(ctx, *pw, nullptr, M.patch, 16, 3))) return rc;
   }
   {
     NEED(pos, "vit.pos_embed");
@@ -589,7 +592,7 @@ static int load_sam2(s3b_ctx* ctx, const Index& idx) {
   {
     NEED(w, "hiera.patch_embed.weight");
     NEED(b, "hiera.patch_embed.bias");
-    if ((rc = upload_linear(ctx, *w, b, M.hpatch, 8))) return rc;
+    if ((rc = upload_linear(ctx, *w, b, M.hpatch, 8, 3))) return rc;
   }
   {
     NEED(pb, "hiera.pos_embed");
@@ -631,7 +634,7 @@ static int load_sam2(s3b_ctx* ctx, const Index& idx) {
     const std::string p = "fpn.convs." + std::to_string(i);
     NEED(w, p + ".weight");
     NEED(b, p + ".bias");
-    if ((rc = upload_linear(ctx, *w, b, M.fpn[i]))) return rc;
+    if ((rc = upload_linear(ctx, *w, b, M.fpn[i], 8, 3))) return rc;
   }
   return load_mem_attn(ctx, idx);
 }

@@ -1,0 +1,67 @@
+// Launch helpers shared by the encoders: launch accounting and optional
+// CUDA-event timing of each GEMM / attention launch on the context stream.
+#include "engine.h"
+
+cudaEvent_t s3b_ctx::next_event() {
+  if (event_next == event_pool.size()) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    event_pool.push_back(e);
+  }
+  return event_pool[event_next++];
+}
+
+namespace s3b {
+
+void count_launch(s3b_ctx* ctx, int n) { ctx->n_launches += n; }
+
+EpiParams epi_store(const Linear& L, void* out, int out_f32, long long ldo, int act) {
+  EpiParams ep;
+  ep.mode = EPI_STORE;
+  ep.bias = L.b ? L.b->as<float>() : nullptr;
+  ep.out = out;
+  ep.out_f32 = out_f32;
+  ep.ldo = ldo;
+  ep.act = act;
+  return ep;
+}
+
+int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long long M, const EpiParams& ep) {
+  cudaEvent_t a = nullptr, b = nullptr;
+  if (ctx->prof) {
+    a = ctx->next_event();
+    b = ctx->next_event();
+    cudaEventRecord(a, ctx->stream);
+  }
+  const int rc = gemm_f16(A, lda, L.w->as<__half>(), L.Kpad, (int)M, L.N, L.Kpad, ep, ctx->d_err, ctx->stream);
+  count_launch(ctx);
+  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "gemm M=%lld N=%d K=%d failed (%d)", M, L.N, L.Kpad, rc);
+  if (ctx->prof) {
+    cudaEventRecord(b, ctx->stream);
+    // algorithmic work: 2*M*N*K flops; bytes: A + B (f16) + output
+    const double bytes = 2.0 * M * L.K + 2.0 * L.N * L.K + (ep.out_f32 ? 4.0 : 2.0) * M * L.N;
+    ctx->prof_entries.push_back({0, 2.0 * M * L.N * L.K, bytes, a, b});
+  }
+  return kOk;
+}
+
+int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
+  cudaEvent_t a = nullptr, b = nullptr;
+  if (ctx->prof) {
+    a = ctx->next_event();
+    b = ctx->next_event();
+    cudaEventRecord(a, ctx->stream);
+  }
+  const int rc = attention(p, D, batch_heads, ctx->stream);
+  count_launch(ctx);
+  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "attention D=%d failed (%d)", D, rc);
+  if (ctx->prof) {
+    cudaEventRecord(b, ctx->stream);
+    const double flops = 4.0 * p.nq * (double)p.nk * D * batch_heads;
+    const double bytes = 2.0 * batch_heads * D * (2.0 * p.nq + 2.0 * p.nk);
+    ctx->prof_entries.push_back({1, flops, bytes, a, b});
+  }
+  return kOk;
+}
+
+}  // namespace s3b

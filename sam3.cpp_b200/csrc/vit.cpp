@@ -15,26 +15,21 @@
 
 namespace s3b {
 
-#define CK(call)                                                                               \
-  do {                                                                                         \
-    int _rc = (call);                                                                          \
+#define CK(call)                                                                                          \
+  do {                                                                                                    \
+    int _rc = (call);                                                                                     \
+    count_launch(ctx);                                                                                    \
     if (_rc) return set_error(ctx, _rc < -9 ? kErrCuda : kErrArg, "%s failed (%d) at %s:%d", #call, _rc, \
-                              __FILE__, __LINE__);                                             \
+                              __FILE__, __LINE__);                                                        \
+  } while (0)
+#define CKG(call)                                                                                         \
+  do {                                                                                                    \
+    int _rc = (call);                                                                                     \
+    if (_rc) return _rc;                                                                                  \
   } while (0)
 
 static int gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long long M, const EpiParams& ep) {
-  return gemm_f16(A, lda, L.w->as<__half>(), L.Kpad, (int)M, L.N, L.Kpad, ep, ctx->d_err, ctx->stream);
-}
-
-static EpiParams epi_store(const Linear& L, void* out, int out_f32, long long ldo, int act = ACT_NONE) {
-  EpiParams ep;
-  ep.mode = EPI_STORE;
-  ep.bias = L.b ? L.b->as<float>() : nullptr;
-  ep.out = out;
-  ep.out_f32 = out_f32;
-  ep.ldo = ldo;
-  ep.act = act;
-  return ep;
+  return run_gemm(ctx, A, lda, L, M, ep);
 }
 
 // One ViT block (sam3_vit_block_forward, sam3.cpp:3710-3801) on T tokens.
@@ -76,7 +71,7 @@ static int vit_block(s3b_ctx* ctx, const VitBlock& B, int F, float* x, __half* x
   if (ep.rope && B.rope_n != ntok)
     return set_error(ctx, kErrFormat, "freqs_cis has %d positions, attention has %d", B.rope_n, ntok);
   ep.qscale = 1.0f;
-  CK(gemm(ctx, xn, E, B.qkv, Tw, ep));
+  CKG(gemm(ctx, xn, E, B.qkv, Tw, ep));
   // flash attention, scale 1/sqrt(HD) (sam3.cpp:3773-3774); output rows in window order
   AttnParams ap;
   ap.q = q;
@@ -90,29 +85,29 @@ static int vit_block(s3b_ctx* ctx, const VitBlock& B, int F, float* x, __half* x
   ap.o_b = (long long)ntok * E;
   ap.o_n = E;
   ap.scale = 1.0f / sqrtf((float)HD);
-  CK(attention(ap, HD, nwin * NH, ctx->stream));
+  CKG(run_attn(ctx, ap, HD, nwin * NH));
   // proj + bias + window unpartition + residual (sam3.cpp:3779-3787)
   EpiParams pe = epi_store(B.proj, x, 1, E);
   pe.map = wmap;
   pe.resid = x;
   pe.ldr = E;
-  CK(gemm(ctx, ao, E, B.proj, Tw, pe));
+  CKG(gemm(ctx, ao, E, B.proj, Tw, pe));
   // norm2 -> fc1 + GELU(erf) -> fc2 + residual (sam3.cpp:3789-3798)
   RowMap id;
   CK(layernorm(x, E, xn, 0, E, T, E, B.n2w.ptr(), B.n2b.ptr(), 1e-5f, id, ctx->stream));
   const int MLP = B.fc1.N;
-  CK(gemm(ctx, xn, E, B.fc1, T, epi_store(B.fc1, hbuf, 0, MLP, ACT_GELU_ERF)));
+  CKG(gemm(ctx, xn, E, B.fc1, T, epi_store(B.fc1, hbuf, 0, MLP, ACT_GELU_ERF)));
   EpiParams f2 = epi_store(B.fc2, x, 1, E);
   f2.resid = x;
   f2.ldr = E;
-  CK(gemm(ctx, hbuf, MLP, B.fc2, T, f2));
+  CKG(gemm(ctx, hbuf, MLP, B.fc2, T, f2));
   return kOk;
 }
 
 // conv 3x3 (pad 1) as im2col + GEMM, channel-last f16 in -> f32 out.
 static int conv3x3(s3b_ctx* ctx, const Linear& L, const __half* in, int F, int S, float* out, __half* col) {
   CK(im2col_3x3_cl(in, F, S, S, L.K / 9, col, ctx->stream));
-  CK(gemm(ctx, col, L.Kpad, L, (long long)F * S * S, epi_store(L, out, 1, L.N)));
+  CKG(gemm(ctx, col, L.Kpad, L, (long long)F * S * S, epi_store(L, out, 1, L.N)));
   return kOk;
 }
 
@@ -136,13 +131,13 @@ static int vit_neck(s3b_ctx* ctx, const NeckScale* sc, const __half* xh, int F, 
     e1.mode = EPI_DECONV2;
     e1.cout = c_mid;
     e1.map.W = e1.map.H = G;
-    CK(gemm(ctx, xh, hp.vit_embed_dim, sc[0].dc1, T, e1));
+    CKG(gemm(ctx, xh, hp.vit_embed_dim, sc[0].dc1, T, e1));
     EpiParams e2 = epi_store(sc[0].dc2, d2->p, 0, D);
     e2.mode = EPI_DECONV2;
     e2.cout = D;
     e2.map.W = e2.map.H = 2 * G;
-    CK(gemm(ctx, d1->as<__half>(), c_mid, sc[0].dc2, T * 4, e2));
-    CK(gemm(ctx, d2->as<__half>(), D, sc[0].c1, T * 16, epi_store(sc[0].c1, c1->p, 0, D)));
+    CKG(gemm(ctx, d1->as<__half>(), c_mid, sc[0].dc2, T * 4, e2));
+    CKG(gemm(ctx, d2->as<__half>(), D, sc[0].c1, T * 16, epi_store(sc[0].c1, c1->p, 0, D)));
     if ((rc = conv3x3(ctx, sc[0].c3, c1->as<__half>(), F, 4 * G, outs[0], col->as<__half>()))) return rc;
   }
   // scale 1: deconv(E->512) -> 1x1 (512->D) -> 3x3  (2x)
@@ -151,19 +146,19 @@ static int vit_neck(s3b_ctx* ctx, const NeckScale* sc, const __half* xh, int F, 
     e1.mode = EPI_DECONV2;
     e1.cout = c_mid;
     e1.map.W = e1.map.H = G;
-    CK(gemm(ctx, xh, hp.vit_embed_dim, sc[1].dc1, T, e1));
-    CK(gemm(ctx, d1->as<__half>(), c_mid, sc[1].c1, T * 4, epi_store(sc[1].c1, c1->p, 0, D)));
+    CKG(gemm(ctx, xh, hp.vit_embed_dim, sc[1].dc1, T, e1));
+    CKG(gemm(ctx, d1->as<__half>(), c_mid, sc[1].c1, T * 4, epi_store(sc[1].c1, c1->p, 0, D)));
     if ((rc = conv3x3(ctx, sc[1].c3, c1->as<__half>(), F, 2 * G, outs[1], col->as<__half>()))) return rc;
   }
   // scale 2: 1x1 (E->D) -> 3x3  (1x)
   {
-    CK(gemm(ctx, xh, hp.vit_embed_dim, sc[2].c1, T, epi_store(sc[2].c1, c1->p, 0, D)));
+    CKG(gemm(ctx, xh, hp.vit_embed_dim, sc[2].c1, T, epi_store(sc[2].c1, c1->p, 0, D)));
     if ((rc = conv3x3(ctx, sc[2].c3, c1->as<__half>(), F, G, outs[2], col->as<__half>()))) return rc;
   }
   // scale 3: maxpool 2x2 -> 1x1 -> 3x3  (0.5x)
   {
     CK(maxpool2_cl_f16(xh, F, G, G, hp.vit_embed_dim, mp->as<__half>(), ctx->stream));
-    CK(gemm(ctx, mp->as<__half>(), hp.vit_embed_dim, sc[3].c1, T / 4, epi_store(sc[3].c1, c1->p, 0, D)));
+    CKG(gemm(ctx, mp->as<__half>(), hp.vit_embed_dim, sc[3].c1, T / 4, epi_store(sc[3].c1, c1->p, 0, D)));
     if ((rc = conv3x3(ctx, sc[3].c3, c1->as<__half>(), F, G / 2, outs[3], col->as<__half>()))) return rc;
   }
   return kOk;
@@ -203,9 +198,11 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
     O.n_det = want_det ? 4 : 0;
   }
   const int FB = ctx->max_frames_per_pass;
-  const long long Tmax = (long long)FB * tok_per_frame;
+  // rows per frame in window order (>= G*G when the grid is padded to whole windows)
+  const int nwv = (G + hp.vit_window_size - 1) / hp.vit_window_size;
+  const long long win_per_frame = (long long)nwv * nwv * hp.vit_window_size * hp.vit_window_size;
+  const long long Tmax = (long long)FB * (win_per_frame > tok_per_frame ? win_per_frame : tok_per_frame);
   const int Kp = M.patch.Kpad;
-  // workspace (window order never exceeds T for the ViT: 72 = 3 x 24)
   DevBuf* col = ctx->buf("vit_col", (size_t)Tmax * Kp * 2, &rc);
   DevBuf* xp = ctx->buf("vit_xp", (size_t)Tmax * E * 4, &rc);
   DevBuf* xn = ctx->buf("vit_xn", (size_t)Tmax * E * 2, &rc);
@@ -225,7 +222,7 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
     pe.resid = M.pos_tiled->as<float>();
     pe.ldr = E;
     pe.resid_mod = tok_per_frame;
-    CK(gemm(ctx, col->as<__half>(), Kp, M.patch, T, pe));
+    CKG(gemm(ctx, col->as<__half>(), Kp, M.patch, T, pe));
     // ln_pre (sam3.cpp:3825-3827)
     RowMap id;
     CK(layernorm(xp->as<float>(), E, x, 1, E, T, E, M.ln_pre_w.ptr(), M.ln_pre_b.ptr(), 1e-5f, id, ctx->stream));
