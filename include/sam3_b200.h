@@ -154,6 +154,15 @@ int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, 
 int s3b_op_layernorm(s3b_ctx* ctx, const float* x, void* out, int out_f32, int64_t rows, int C, const float* g,
                      const float* b, float eps);
 
+/* 3x3 / stride 1 / pad 1 convolution on channel-last f16 maps x [B][H][W][C]
+ * with weights w f16 [Cout][3][3][C] (ky, kx, ci order, i.e. the ggml kernel
+ * [3, 3, C, Cout] repacked channel-last), bias f32 [Cout] or NULL, out f32
+ * [B][H][W][Cout]. Lowered to im2col (context workspace) + tensor-core GEMM.
+ * Replaces ggml_conv_2d_s1_ph + bias add (sam3.cpp:3887-3918). C and Cout
+ * multiples of 8. */
+int s3b_op_conv3x3(s3b_ctx* ctx, const void* x, int B, int H, int W, int C, const void* w, const float* bias,
+                   float* out, int Cout);
+
 /* Dequantises nrows rows of ne0 values of q4_0 / q4_1 / q8_0 blocks to f32,
  * bit-exactly as ggml's type-traits to_float (sam3.cpp:1076-1077). */
 int s3b_op_dequantize(s3b_ctx* ctx, const void* src, int type, int64_t ne0, int64_t nrows, float* dst);

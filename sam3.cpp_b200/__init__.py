@@ -60,6 +60,7 @@ SYMBOLS = [
     ("s3b_op_gemm", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _I, _P, _I, _I64, _P, _I64]),
     ("s3b_op_attention", _I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F]),
     ("s3b_op_layernorm", _I, [_P, _P, _P, _I, _I64, _I, _P, _P, _F]),
+    ("s3b_op_conv3x3", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),
     ("s3b_op_dequantize", _I, [_P, _P, _I, _I64, _I64, _P]),
     ("s3b_row_size", _I64, [_I, _I64]),
     ("s3b_quantize_rows", _I, [_I, _P, _I64, _I64, _P]),
@@ -300,6 +301,13 @@ class Engine:
         rc = self._L.s3b_op_layernorm(self.h, x.data_ptr(), out.data_ptr(), out_f32, rows, C, g.data_ptr(),
                                       _ptr(b), eps)
         self._check(rc, "s3b_op_layernorm")
+
+    def conv3x3(self, x, w, bias, out):
+        """x f16 [B,H,W,C], w f16 [Cout,3,3,C], bias f32 [Cout] or None, out f32 [B,H,W,Cout]."""
+        B, H, W, C = x.shape
+        Cout = w.shape[0]
+        rc = self._L.s3b_op_conv3x3(self.h, x.data_ptr(), B, H, W, C, w.data_ptr(), _ptr(bias), out.data_ptr(), Cout)
+        self._check(rc, "s3b_op_conv3x3")
 
     def dequantize(self, raw, qtype: int, ne0: int, nrows: int, out):
         rc = self._L.s3b_op_dequantize(self.h, raw.data_ptr(), qtype, ne0, nrows, out.data_ptr())

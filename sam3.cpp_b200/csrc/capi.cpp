@@ -452,6 +452,29 @@ int s3b_op_layernorm(s3b_ctx* ctx, const float* x, void* out, int out_f32, int64
   return kOk;
 }
 
+int s3b_op_conv3x3(s3b_ctx* ctx, const void* x, int B, int H, int W, int C, const void* w, const float* bias,
+                   float* out, int Cout) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!x || !w || !out || B <= 0 || H <= 0 || W <= 0 || C <= 0 || Cout <= 0 || C % 8 || Cout % 8)
+    return set_error(ctx, kErrArg, "bad conv3x3 arguments");
+  const long long M = (long long)B * H * W;
+  DevBuf* col = ctx->buf("op_conv_col", (size_t)M * 9 * C * 2, &rc);
+  if (rc) return rc;
+  rc = im2col_3x3_cl(reinterpret_cast<const __half*>(x), B, H, W, C, col->as<__half>(), ctx->stream);
+  if (rc) return set_error(ctx, kErrCuda, "im2col launch failed (%d)", rc);
+  EpiParams ep;
+  ep.mode = EPI_STORE;
+  ep.bias = bias;
+  ep.out = out;
+  ep.out_f32 = 1;
+  ep.ldo = Cout;
+  rc = gemm_f16(col->as<__half>(), 9LL * C, reinterpret_cast<const __half*>(w), 9LL * C, (int)M, Cout, 9 * C, ep,
+                ctx->d_err, ctx->stream);
+  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "conv gemm launch failed (%d)", rc);
+  return kOk;
+}
+
 int s3b_op_dequantize(s3b_ctx* ctx, const void* src, int type, int64_t ne0, int64_t nrows, float* dst) {
   int rc = ctx_enter(ctx);
   if (rc) return rc;

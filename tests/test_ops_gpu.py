@@ -82,6 +82,21 @@ def test_layernorm(engine, rows, C, f32):
     assert (out.float() - ref).abs().max().item() < (2e-5 * C ** 0.5 + 1e-4 if f32 else 2e-2)
 
 
+@pytest.mark.parametrize("B,H,W,C,Cout", [(1, 36, 36, 256, 256), (2, 17, 23, 64, 128), (1, 72, 72, 256, 256)])
+def test_conv3x3(engine, B, H, W, C, Cout):
+    g = torch.Generator(device="cuda").manual_seed(H * W + C)
+    x = torch.randn(B, H, W, C, device="cuda", generator=g).half()
+    w = (torch.randn(Cout, 3, 3, C, device="cuda", generator=g) * 0.05).half()
+    bias = torch.randn(Cout, device="cuda", generator=g) * 0.1
+    out = torch.empty(B, H, W, Cout, device="cuda", dtype=torch.float32)
+    engine.conv3x3(x, w, bias, out)
+    engine.sync()
+    ref = torch.nn.functional.conv2d(x.float().permute(0, 3, 1, 2), w.float().permute(0, 3, 1, 2), bias, padding=1)
+    ref = ref.permute(0, 2, 3, 1)
+    err = (out - ref).abs().max().item()
+    assert err < 2e-3 * max(1.0, ref.abs().max().item()), err
+
+
 @pytest.mark.parametrize("qtype", [2, 3, 8])
 def test_dequant_bit_exact(engine, s3b, qtype):
     from oracle import quant
