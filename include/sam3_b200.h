@@ -163,6 +163,27 @@ int s3b_op_layernorm(s3b_ctx* ctx, const float* x, void* out, int out_f32, int64
 int s3b_op_conv3x3(s3b_ctx* ctx, const void* x, int B, int H, int W, int C, const void* w, const float* bias,
                    float* out, int Cout);
 
+/* Size of the static device scratch used by s3b_conv3x3_noalloc (32 MiB). */
+#define S3B_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* Same computation as s3b_op_conv3x3, for callers that cannot allocate
+ * device memory (a host whose GPU memory is pre-sized and owned by another
+ * allocator, a plugin whose CUDA context forbids cudaMalloc, or a real-time
+ * thread where cudaMalloc/cudaFree would synchronise the device). It needs no
+ * s3b_ctx and calls no cudaMalloc, cudaFree or allocating library routine:
+ * the im2col workspace and the kernels' error word live in one file-scope
+ * __device__ array of S3B_NOALLOC_SCRATCH_BYTES (+256) bytes that every GPU
+ * loading the library holds until exit. The caller passes inputs, outputs
+ * and a cudaStream_t (NULL = legacy default stream); work is only enqueued.
+ * B*H*W*9*C*2 must not exceed S3B_NOALLOC_SCRATCH_BYTES (S3B_ERR_ARG and a
+ * message on stderr otherwise). The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress), so make it before any
+ * stream capture. All calls share the array: calls that overlap on the GPU
+ * race and must be ordered by the caller.
+ * No counterpart in the reference (sam3.cpp always allocates through ggml). */
+int s3b_conv3x3_noalloc(const void* x, int B, int H, int W, int C, const void* w, const float* bias, float* out,
+                        int Cout, void* cuda_stream);
+
 /* Dequantises nrows rows of ne0 values of q4_0 / q4_1 / q8_0 blocks to f32,
  * bit-exactly as ggml's type-traits to_float (sam3.cpp:1076-1077). */
 int s3b_op_dequantize(s3b_ctx* ctx, const void* src, int type, int64_t ne0, int64_t nrows, float* dst);

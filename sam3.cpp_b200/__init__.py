@@ -61,6 +61,7 @@ SYMBOLS = [
     ("s3b_op_attention", _I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F]),
     ("s3b_op_layernorm", _I, [_P, _P, _P, _I, _I64, _I, _P, _P, _F]),
     ("s3b_op_conv3x3", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),
+    ("s3b_conv3x3_noalloc", _I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _P]),
     ("s3b_op_dequantize", _I, [_P, _P, _I, _I64, _I64, _P]),
     ("s3b_row_size", _I64, [_I, _I64]),
     ("s3b_quantize_rows", _I, [_I, _P, _I64, _I64, _P]),
