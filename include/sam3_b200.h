@@ -55,8 +55,11 @@ enum {
 int s3b_create(int device, s3b_ctx** out);
 void s3b_destroy(s3b_ctx* ctx);
 const char* s3b_last_error(const s3b_ctx* ctx);
-/* Uses `cuda_stream` (a cudaStream_t, or NULL for the context's own) for all work. */
+/* Uses `cuda_stream` (a cudaStream_t; NULL = the legacy default stream) for
+ * all work of the context; s3b_reset_stream returns to a stream owned by the
+ * context. */
 int s3b_set_stream(s3b_ctx* ctx, void* cuda_stream);
+int s3b_reset_stream(s3b_ctx* ctx);
 /* Waits for all work of the context and checks the device error word. */
 int s3b_sync(s3b_ctx* ctx);
 /* Options: "frames_per_pass" (encoder micro-batch, default 8). */
@@ -142,6 +145,15 @@ int s3b_mem_attn(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat
  * (+ activation) pairs such as sam3.cpp:3738-3739, 3792-3796. */
 int s3b_op_gemm(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
                 const float* bias, int act, void* out, int out_f32, int64_t ldo, const float* resid, int64_t ldr);
+
+/* Fused projection + 2D RoPE: out = A B^T + bias, then columns < rope_cols
+ * are rotated in pairs (2i, 2i+1) by table [positions][rope_d/2][2] (cos,
+ * sin) at position (row % rope_mod) and pair ((col % rope_d) / 2). This is
+ * the qkv projection of a ViT block followed by sam3_apply_rope on q and k
+ * (sam3.cpp:3738-3771, 3667-3706). */
+int s3b_op_gemm_rope(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
+                     const float* bias, const float* table, int rope_d, int rope_cols, int64_t rope_mod, void* out,
+                     int out_f32, int64_t ldo);
 
 /* softmax(q k^T * scale) v for q [B*H][nq][d], k/v [B*H][nk][d] (f16),
  * out [B][nq][H*d] f16. Replaces ggml_flash_attn_ext (sam3.cpp:3774, 4395,

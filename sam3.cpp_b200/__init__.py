@@ -42,6 +42,7 @@ SYMBOLS = [
     ("s3b_destroy", None, [_P]),
     ("s3b_last_error", _S, [_P]),
     ("s3b_set_stream", _I, [_P, _P]),
+    ("s3b_reset_stream", _I, [_P]),
     ("s3b_sync", _I, [_P]),
     ("s3b_set_option", _I, [_P, _S, _I64]),
     ("s3b_profile_begin", _I, [_P, _I]),
@@ -58,6 +59,7 @@ SYMBOLS = [
     ("s3b_output_device_ptr", _I, [_P, _S, _I, ctypes.POINTER(_P)]),
     ("s3b_mem_attn", _I, [_P, _P, _P, _I, _P, _P, _I, _I, _P, _I]),
     ("s3b_op_gemm", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _I, _P, _I, _I64, _P, _I64]),
+    ("s3b_op_gemm_rope", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _I, _I, _I64, _P, _I, _I64]),
     ("s3b_op_attention", _I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F]),
     ("s3b_op_layernorm", _I, [_P, _P, _P, _I, _I64, _I, _P, _P, _F]),
     ("s3b_op_conv3x3", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),
@@ -187,7 +189,12 @@ class Engine:
         return m.decode() if m else ""
 
     def set_stream(self, stream_handle: int | None):
-        self._check(self._L.s3b_set_stream(self.h, stream_handle), "s3b_set_stream")
+        """Runs on `stream_handle` (a cudaStream_t value; 0 = legacy default stream);
+        None returns to a stream owned by the context."""
+        if stream_handle is None:
+            self._check(self._L.s3b_reset_stream(self.h), "s3b_reset_stream")
+        else:
+            self._check(self._L.s3b_set_stream(self.h, stream_handle), "s3b_set_stream")
 
     def sync(self):
         self._check(self._L.s3b_sync(self.h), "s3b_sync")
@@ -288,6 +295,15 @@ class Engine:
                                  out.data_ptr(), out_f32, out.stride(0), _ptr(resid),
                                  resid.stride(0) if resid is not None else 0)
         self._check(rc, "s3b_op_gemm")
+
+    def gemm_rope(self, A, B, out, bias, table, rope_d: int, rope_cols: int, rope_mod: int):
+        M, lda = A.shape[0], A.stride(0)
+        N, ldb = B.shape[0], B.stride(0)
+        out_f32 = 1 if out.dtype.itemsize == 4 else 0
+        rc = self._L.s3b_op_gemm_rope(self.h, A.data_ptr(), lda, B.data_ptr(), ldb, M, N, A.shape[1], _ptr(bias),
+                                      table.data_ptr(), rope_d, rope_cols, rope_mod, out.data_ptr(), out_f32,
+                                      out.stride(0))
+        self._check(rc, "s3b_op_gemm_rope")
 
     def attention(self, q, k, v, out, scale: float):
         B, H, nq, d = q.shape

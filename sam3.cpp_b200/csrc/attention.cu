@@ -79,9 +79,9 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
   const int bh = blockIdx.y;
   const int b = bh / p.heads, h = bh - (bh / p.heads) * p.heads;
   const int q0 = blockIdx.x * kBQ;
-  const __half* Qg = p.q + (long long)bh * p.q_bh + (long long)q0 * p.q_n;
-  const __half* Kg = p.k + (long long)bh * p.k_bh;
-  const __half* Vg = p.v + (long long)bh * p.v_bh;
+  const __half* Qg = p.q + (long long)b * p.q_b + (long long)h * p.q_h + (long long)q0 * p.q_n;
+  const __half* Kg = p.k + (long long)b * p.k_b + (long long)h * p.k_h;
+  const __half* Vg = p.v + (long long)b * p.v_b + (long long)h * p.v_h;
 
   load_tile<D>(sQ, Qg, p.q_n, p.nq - q0, tid);
   load_tile<D>(sK, Kg, p.k_n, p.nk, tid);
@@ -203,14 +203,16 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
   const float inv0 = 1.f / l0, inv1 = 1.f / l1;
   const int r0 = q0 + warp * 16 + g, r1 = r0 + 8;
-  __half* ob = p.o + (long long)b * p.o_b + (long long)h * D;
+  const long long orow0 = r0 < p.nq ? map_row(p.omap, (long long)b * p.nq + r0) : -1;
+  const long long orow1 = r1 < p.nq ? map_row(p.omap, (long long)b * p.nq + r1) : -1;
+  __half* ob = p.o + (long long)h * D;
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
     const int c = n * 8 + 2 * t4;
-    if (r0 < p.nq)
-      *reinterpret_cast<__half2*>(ob + (long long)r0 * p.o_n + c) = __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
-    if (r1 < p.nq)
-      *reinterpret_cast<__half2*>(ob + (long long)r1 * p.o_n + c) = __floats2half2_rn(o[n][2] * inv1, o[n][3] * inv1);
+    if (orow0 >= 0)
+      *reinterpret_cast<__half2*>(ob + orow0 * p.o_n + c) = __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
+    if (orow1 >= 0)
+      *reinterpret_cast<__half2*>(ob + orow1 * p.o_n + c) = __floats2half2_rn(o[n][2] * inv1, o[n][3] * inv1);
   }
 }
 
@@ -226,14 +228,16 @@ int launch_attn(const AttnParams& p, int batch_heads, cudaStream_t st) {
   }
   dim3 grid((p.nq + kBQ - 1) / kBQ, batch_heads);
   attn_fwd_kernel<D><<<grid, 128, smem, st>>>(p);
-  return cudaGetLastError() == cudaSuccess ? 0 : -14;
+  return launch_status("attention");
 }
 
 }  // namespace
 
 int attention(const AttnParams& p, int D, int batch_heads, cudaStream_t st) {
   if (p.nq <= 0 || p.nk <= 0 || batch_heads <= 0 || p.heads <= 0) return -1;
-  if ((p.q_n % 8) || (p.k_n % 8) || (p.v_n % 8) || (p.q_bh % 8) || (p.k_bh % 8) || (p.v_bh % 8)) return -2;
+  if ((p.q_n % 8) || (p.k_n % 8) || (p.v_n % 8) || (p.q_b % 8) || (p.k_b % 8) || (p.v_b % 8) || (p.q_h % 8) ||
+      (p.k_h % 8) || (p.v_h % 8) || (p.o_n % 2))
+    return -2;
   switch (D) {
     case 64: return launch_attn<64>(p, batch_heads, st);
     case 80: return launch_attn<80>(p, batch_heads, st);

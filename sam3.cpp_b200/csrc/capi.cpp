@@ -199,14 +199,20 @@ int s3b_set_stream(s3b_ctx* ctx, void* stream) {
   int rc = ctx_enter(ctx);
   if (rc) return rc;
   cudaStreamSynchronize(ctx->stream);
-  if (stream) {
-    if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
-    ctx->own_stream = false;
-    ctx->stream = reinterpret_cast<cudaStream_t>(stream);
-  } else if (!ctx->own_stream) {
-    cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
-    ctx->own_stream = true;
-  }
+  if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+  ctx->own_stream = false;
+  ctx->stream = reinterpret_cast<cudaStream_t>(stream);
+  return kOk;
+}
+
+int s3b_reset_stream(s3b_ctx* ctx) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (ctx->own_stream) return kOk;
+  cudaStreamSynchronize(ctx->stream);
+  if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "stream creation failed");
+  ctx->own_stream = true;
   return kOk;
 }
 
@@ -417,6 +423,30 @@ int s3b_op_gemm(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, int64_t
   return kOk;
 }
 
+int s3b_op_gemm_rope(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
+                     const float* bias, const float* table, int rope_d, int rope_cols, int64_t rope_mod, void* out,
+                     int out_f32, int64_t ldo) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!A || !B || !out || !table || M <= 0 || N <= 0 || K <= 0 || rope_d <= 0 || (rope_d & 1) || rope_mod <= 0)
+    return set_error(ctx, kErrArg, "bad gemm_rope arguments");
+  EpiParams ep;
+  ep.mode = EPI_STORE;
+  ep.bias = bias;
+  ep.out = out;
+  ep.out_f32 = out_f32;
+  ep.ldo = ldo;
+  ep.rope = table;
+  ep.rope_D = rope_d;
+  ep.rope_cols = rope_cols;
+  ep.rope_rows = M;
+  ep.rope_mod = rope_mod;
+  rc = gemm_f16(reinterpret_cast<const __half*>(A), lda, reinterpret_cast<const __half*>(B), ldb, M, N, K, ep,
+                ctx->d_err, ctx->stream);
+  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "gemm_rope launch failed (%d)", rc);
+  return kOk;
+}
+
 int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, void* out, int batch, int heads,
                      int nq, int nk, int d, float scale) {
   int rc = ctx_enter(ctx);
@@ -427,13 +457,14 @@ int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, 
   p.k = reinterpret_cast<const __half*>(k);
   p.v = reinterpret_cast<const __half*>(v);
   p.o = reinterpret_cast<__half*>(out);
-  p.q_bh = (long long)nq * d;
-  p.k_bh = p.v_bh = (long long)nk * d;
+  p.q_b = (long long)heads * nq * d;
+  p.q_h = (long long)nq * d;
+  p.k_b = p.v_b = (long long)heads * nk * d;
+  p.k_h = p.v_h = (long long)nk * d;
   p.q_n = p.k_n = p.v_n = d;
   p.heads = heads;
   p.nq = nq;
   p.nk = nk;
-  p.o_b = (long long)nq * heads * d;
   p.o_n = (long long)heads * d;
   p.scale = scale;
   rc = attention(p, d, batch * heads, ctx->stream);

@@ -246,7 +246,7 @@ inline int grid_for(long long n, int threads) {
   return (int)g;
 }
 
-inline int launch_ok() { return cudaGetLastError() == cudaSuccess ? 0 : -14; }
+inline int launch_ok() { return launch_status("elementwise kernel"); }
 
 }  // namespace
 

@@ -2,8 +2,8 @@
 //
 //   C[M,N] = A[M,K] * B[N,K]^T, A/B f16 K-major, f32 accumulation in TMEM.
 //
-// This kernel replaces ggml_mul_mat + ggml_add(bias) (+ activation,
-// + residual add, + the permute/cont copies that follow) on the encoder hot
+// This kernel replaces ggml_mul_mat + ggml_add(bias) (+ activation, RoPE,
+// residual add, and the permute/cont copies around them) on the encoder hot
 // path: ViT blocks sam3.cpp:3738-3798, Hiera blocks sam3.cpp:4317-4454,
 // memory attention sam3.cpp:9250-9325, and the convolutions lowered to
 // GEMMs (patch embed 3815/4470, neck 3880-3918, FPN 4547).
@@ -12,13 +12,22 @@
 //   warp 0     TMA producer: 128x64 A tile + BNx64 B tile per stage (SW128)
 //   warp 1     MMA issuer: 4 x tcgen05.mma (K=16) per stage into TMEM;
 //              owns the TMEM allocation (2 accumulators of BN columns)
-//   warps 2-9  epilogue: tcgen05.ld -> bias/act/residual -> global stores;
-//              warps w and w+4 share TMEM lane quarter (w % 4) and split the
-//              columns in halves.
+//   warps 2-9  epilogue: warps w and w+4 share TMEM lane quarter (w % 4) and
+//              split the tile's columns in halves.
 // The accumulator is double-buffered so the epilogue of tile i overlaps the
 // main loop of tile i+1.
+//
+// Epilogue, TMA path (plain row-major outputs): each 128-row column chunk of
+// 128 bytes is moved TMEM -> registers (bias, activation, RoPE) -> a 128B-
+// swizzled shared staging buffer (double-buffered per half) -> global by one
+// TMA tensor store. When the residual is the output itself (x += f(x)) the
+// chunk of x is first TMA-loaded into the same staging buffer and added in
+// registers. Other layouts (deconvolution pixel scatter, row remaps,
+// broadcast residuals) use direct per-row stores.
 #include "common.cuh"
 #include "kernels.h"
+
+#include <stdio.h>
 
 #include <mutex>
 
@@ -30,6 +39,7 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + kEpiWarps * 32;
+constexpr uint32_t kStageBufBytes = 16384;  // 128 rows x 128 B
 
 __device__ __forceinline__ float apply_act(float v, int act) {
   switch (act) {
@@ -64,15 +74,18 @@ __device__ __forceinline__ void store16(void* base, long long idx, int is_f32, c
   }
 }
 
-// Epilogue for 16 consecutive accumulator columns [gc, gc+16) of row gr.
-__device__ __forceinline__ void epilogue16(const EpiParams& ep, long long gr, int gc, int N, const uint32_t (&r)[16]) {
-  float v[16];
+// bias + activation + RoPE + scale on 16 consecutive columns [gc, gc+16) of row gr.
+__device__ __forceinline__ void epi_math16(const EpiParams& ep, long long gr, int gc, int N, float (&v)[16]) {
   const int n_valid = min(16, N - gc);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
   if (ep.bias) {
     if (ep.mode == EPI_DECONV2) {
       for (int i = 0; i < n_valid; ++i) v[i] += __ldg(ep.bias + (gc + i) % ep.cout);
+    } else if (n_valid == 16 && ((reinterpret_cast<uintptr_t>(ep.bias + gc) & 15) == 0)) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(ep.bias + gc + i));
+        v[i] += b.x; v[i + 1] += b.y; v[i + 2] += b.z; v[i + 3] += b.w;
+      }
     } else {
       for (int i = 0; i < n_valid; ++i) v[i] += __ldg(ep.bias + gc + i);
     }
@@ -81,23 +94,29 @@ __device__ __forceinline__ void epilogue16(const EpiParams& ep, long long gr, in
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = apply_act(v[i], ep.act);
   }
+  if (ep.rope && gc < ep.rope_cols && gr < ep.rope_rows) {
+    const int half_d = ep.rope_D >> 1;
+    const long long pos = gr % ep.rope_mod;
+    for (int i = 0; i + 1 < n_valid; i += 2) {
+      const int d = (gc + i) % ep.rope_D;
+      const float2 cs = __ldg(reinterpret_cast<const float2*>(ep.rope + (pos * half_d + (d >> 1)) * 2));
+      const float a = v[i], b = v[i + 1];
+      v[i] = a * cs.x - b * cs.y;
+      v[i + 1] = a * cs.y + b * cs.x;
+    }
+  }
+  if (ep.out_scale != 1.0f) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] *= ep.out_scale;
+  }
+}
 
+// Direct-store epilogue for 16 columns (row remaps, broadcast residuals, deconvolution scatter).
+__device__ __forceinline__ void epi_store_direct16(const EpiParams& ep, long long gr, int gc, int N, float (&v)[16]) {
+  const int n_valid = min(16, N - gc);
   if (ep.mode == EPI_STORE) {
     const long long orow = map_row(ep.map, gr);
     if (orow < 0) return;
-    if (ep.rope && gr < ep.rope_rows) {
-      const float* rt = ep.rope + ((gr % ep.rope_mod) * (N / 2) + gc / 2) * 2;
-      for (int i = 0; i + 1 < n_valid; i += 2) {
-        const float c = __ldg(rt + i), sn = __ldg(rt + i + 1);
-        const float a = v[i], b = v[i + 1];
-        v[i] = a * c - b * sn;
-        v[i + 1] = a * sn + b * c;
-      }
-    }
-    if (ep.out_scale != 1.0f) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] *= ep.out_scale;
-    }
     if (ep.resid) {
       long long rrow;
       if (ep.resid_up) {
@@ -121,60 +140,9 @@ __device__ __forceinline__ void epilogue16(const EpiParams& ep, long long gr, in
         for (int i = 0; i < n_valid; ++i) v[i] += rp[i];
       }
     }
-    const bool vec_ok = (ep.ldo % 16) == 0;
-    store16(ep.out, orow * ep.ldo + gc, ep.out_f32, v, n_valid, vec_ok);
+    store16(ep.out, orow * ep.ldo + gc, ep.out_f32, v, n_valid, (ep.ldo % 16) == 0);
     return;
   }
-
-  if (ep.mode == EPI_QKV) {
-    const long long win = gr / ep.ntok;
-    const int l = (int)(gr - win * ep.ntok);
-    if ((ep.D % 16) == 0) {
-      const int s = gc / ep.C;
-      const int cc = gc - s * ep.C;
-      const int h = cc / ep.D;
-      const int d0 = cc - h * ep.D;
-      if (s < 2 && ep.rope) {
-        const float* rt = ep.rope + ((long long)l * (ep.D / 2) + d0 / 2) * 2;
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const float c = __ldg(rt + i), sn = __ldg(rt + i + 1);
-          const float a = v[i], b = v[i + 1];
-          v[i] = a * c - b * sn;
-          v[i + 1] = a * sn + b * c;
-        }
-      }
-      if (s == 0) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] *= ep.qscale;
-      }
-      __half* base = s == 0 ? ep.q : (s == 1 ? ep.k : ep.v);
-      const long long idx = ((win * ep.heads + h) * ep.ntok + l) * (long long)ep.D + d0;
-      store16(base, idx, 0, v, 16, true);
-    } else {
-      // head dim not a multiple of 16 (e.g. 72): per-pair path
-      for (int i = 0; i < n_valid; i += 2) {
-        const int n = gc + i;
-        const int s = n / ep.C;
-        const int cc = n - s * ep.C;
-        const int h = cc / ep.D;
-        const int d = cc - h * ep.D;
-        float a = v[i], b = v[i + 1];
-        if (s < 2 && ep.rope) {
-          const float* rt = ep.rope + ((long long)l * (ep.D / 2) + d / 2) * 2;
-          const float c = rt[0], sn = rt[1];
-          const float a2 = a * c - b * sn, b2 = a * sn + b * c;
-          a = a2; b = b2;
-        }
-        if (s == 0) { a *= ep.qscale; b *= ep.qscale; }
-        __half* base = s == 0 ? ep.q : (s == 1 ? ep.k : ep.v);
-        const long long idx = ((win * ep.heads + h) * ep.ntok + l) * (long long)ep.D + d;
-        *reinterpret_cast<__half2*>(base + idx) = __floats2half2_rn(a, b);
-      }
-    }
-    return;
-  }
-
   if (ep.mode == EPI_DECONV2) {
     const long long HW = (long long)ep.map.H * ep.map.W;
     const long long f = gr / HW;
@@ -188,6 +156,16 @@ __device__ __forceinline__ void epilogue16(const EpiParams& ep, long long gr, in
     store16(ep.out, opix * ep.ldo + co, ep.out_f32, v, n_valid, vec_ok);
   }
 }
+
+// 16 TMEM columns into R[o..o+15] (o a compile-time constant keeps R in registers).
+#define TMEM_LD16(taddr, R, o)                                                                              \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "                                                    \
+               "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"                            \
+               : "=r"(R[o + 0]), "=r"(R[o + 1]), "=r"(R[o + 2]), "=r"(R[o + 3]), "=r"(R[o + 4]),           \
+                 "=r"(R[o + 5]), "=r"(R[o + 6]), "=r"(R[o + 7]), "=r"(R[o + 8]), "=r"(R[o + 9]),           \
+                 "=r"(R[o + 10]), "=r"(R[o + 11]), "=r"(R[o + 12]), "=r"(R[o + 13]), "=r"(R[o + 14]),      \
+                 "=r"(R[o + 15])                                                                            \
+               : "r"(taddr))
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -204,27 +182,43 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   }
 }
 
-template <int BN, int STAGES>
+__device__ __forceinline__ void named_bar(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const void* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+template <int BN, int STAGES, bool TMA_EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                       int K, EpiParams ep, int* err) {
+    gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmC, int M, int N, int K, EpiParams ep,
+                       int resid_in_place, int* err) {
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
   constexpr uint32_t B_BYTES = BN * kBK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = 2 * BN;
-  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+  constexpr uint32_t STAGING = TMA_EPI ? 4 * kStageBufBytes : 0;
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512 || TMEM_COLS == 128, "TMEM columns must be a power of 2");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sC = sB + STAGES * B_BYTES;  // staging (TMA epilogue only), 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(sC + STAGING);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* mma_done = tempty + 2;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* rfull = mma_done + 1;  // [half*2 + buf]: residual chunk landed in its staging buffer
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(rfull + 4);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -244,11 +238,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[a], kEpiWarps);
     }
     mbar_init(mma_done, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&rfull[i], 1);
     *s_abort = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (TMA_EPI) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(s_tmem, TMEM_COLS);
@@ -263,8 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t armed = 0;             // bit s: stage s has been armed at least once
-      uint32_t armed_phase = 0;       // bit s: parity of the last arming of stage s
+      uint32_t armed = 0;        // bit s: stage s has been armed at least once
+      uint32_t armed_phase = 0;  // bit s: parity of the last arming of stage s
       bool ok = true;
       for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
         const int m0 = (t / tiles_n) * kBM;
@@ -322,8 +318,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row = q * 32 + lane;
+    const bool leader = (warp - 2) == 4 * half && lane == 0;  // issues this half's TMA copies
     int acc = 0;
     uint32_t aphase = 0;
+    uint32_t chunk_ctr = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
       const int m0 = (t / tiles_n) * kBM;
       const int n0 = (t % tiles_n) * BN;
@@ -331,19 +329,110 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const long long gr = (long long)m0 + row;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * (BN / 2));
+      if (TMA_EPI) {
+        // chunk = 128 B of columns: 32 f32 or 64 f16
+        const int cw = ep.out_f32 ? 32 : 64;
+        bool ok = true;
+        for (int c0 = 0; c0 < BN / 2; c0 += cw) {
+          const int gcb = n0 + half * (BN / 2) + c0;
+          const int bsel = half * 2 + (int)(chunk_ctr & 1);
+          uint8_t* buf = sC + bsel * kStageBufBytes;
+          if (resid_in_place && leader) {
+            // residual chunk -> staging buffer, once the store that last used it has read it
+            bulk_wait_read1();
+            if (gcb < N) {
+              mbar_arrive_expect_tx(&rfull[bsel], kStageBufBytes);
+              tma_load_2d(&tmC, &rfull[bsel], buf, gcb, m0);
+            } else {
+              mbar_arrive(&rfull[bsel]);
+            }
+          }
+          uint32_t r[64];
+          TMEM_LD16(tbase + (uint32_t)c0, r, 0);
+          TMEM_LD16(tbase + (uint32_t)(c0 + 16), r, 16);
+          if (cw == 64) {
+            TMEM_LD16(tbase + (uint32_t)(c0 + 32), r, 32);
+            TMEM_LD16(tbase + (uint32_t)(c0 + 48), r, 48);
+          }
+          tc_wait_ld();
+          if (c0 + cw >= BN / 2) {
+            // accumulator fully read: hand TMEM back to the MMA warp early
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+          }
+          if (resid_in_place) {
+            // parity of this buffer's residual barrier = number of its earlier uses & 1
+            if (!mbar_wait(&rfull[bsel], (chunk_ctr >> 1) & 1u, s_abort, err, kErrWaitMisc)) { ok = false; break; }
+          } else {
+            if (leader) bulk_wait_read1();  // the store that last used `buf` has read it
+            named_bar(1 + half, 128);
+          }
+          uint8_t* rowp = buf + row * 128;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (j * 16 < cw) {
+              float v[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[j * 16 + i]);
+              const int gc = gcb + j * 16;
+              if (gc < N) epi_math16(ep, gr, gc, N, v);
+              if (ep.out_f32) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const int unit = j * 4 + u;  // 16-byte unit within the 128-byte row
+                  float4* sp = reinterpret_cast<float4*>(rowp + ((unit ^ (row & 7)) << 4));
+                  if (resid_in_place) {
+                    const float4 rv = *sp;
+                    v[4 * u] += rv.x; v[4 * u + 1] += rv.y; v[4 * u + 2] += rv.z; v[4 * u + 3] += rv.w;
+                  }
+                  *sp = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                }
+              } else {
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  const int unit = j * 2 + u;
+                  __align__(16) __half2 h[4];
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[8 * u + 2 * e], v[8 * u + 2 * e + 1]);
+                  *reinterpret_cast<uint4*>(rowp + ((unit ^ (row & 7)) << 4)) = *reinterpret_cast<const uint4*>(h);
+                }
+              }
+            }
+          }
+          fence_proxy_async_smem();
+          named_bar(1 + half, 128);
+          if (leader && gcb < N) {
+            tma_store_2d(&tmC, buf, gcb, m0);
+            bulk_commit();
+          }
+          ++chunk_ctr;
+        }
+        if (!ok) break;
+      } else {
 #pragma unroll 1
-      for (int c = 0; c < BN / 2; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(tbase + (uint32_t)c, r);
-        tc_wait_ld();
-        const int gc = n0 + half * (BN / 2) + c;
-        if (gr < M && gc < N) epilogue16(ep, gr, gc, N, r);
+        for (int c = 0; c < BN / 2; c += 16) {
+          uint32_t r[16];
+          TMEM_LD16(tbase + (uint32_t)c, r, 0);
+          tc_wait_ld();
+          if (c + 16 >= BN / 2) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+          }
+          const int gc = n0 + half * (BN / 2) + c;
+          if (gr < M && gc < N) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+            epi_math16(ep, gr, gc, N, v);
+            epi_store_direct16(ep, gr, gc, N, v);
+          }
+        }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) { acc = 0; aphase ^= 1; }
     }
+    if (TMA_EPI && leader) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -372,44 +461,60 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 2D f16 tensor map over a row-major [rows][ld] matrix, box = box_rows x 64, SW128.
-int make_map_2d(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld, int box_rows) {
+// 2D tensor map over a row-major [rows][ld] matrix, box = box_rows x (128 B), SW128.
+int make_map_2d(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld, int box_rows,
+                int elem_bytes) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return -10;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0) return -11;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * elem_bytes) % 16 != 0) return -11;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * elem_bytes)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -12;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool TMA_EPI>
 int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
-                const EpiParams& ep, int* err, cudaStream_t st) {
-  CUtensorMap ma, mb;
-  int rc = make_map_2d(&ma, A, M, K, lda, kBM);
+                const EpiParams& ep, int resid_in_place, int* err, cudaStream_t st) {
+  CUtensorMap ma, mb, mc;
+  int rc = make_map_2d(&ma, A, M, K, lda, kBM, 2);
   if (rc) return rc;
-  rc = make_map_2d(&mb, B, N, K, ldb, BN);
+  rc = make_map_2d(&mb, B, N, K, ldb, BN, 2);
   if (rc) return rc;
-  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN) * kBK * 2 + (2 * STAGES + 5) * 8 + 16;
+  if (TMA_EPI) {
+    rc = make_map_2d(&mc, ep.out, M, N, ep.ldo, kBM, ep.out_f32 ? 4 : 2);
+    if (rc) return rc;
+  } else {
+    mc = ma;  // unused
+  }
+  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN) * kBK * 2 + (TMA_EPI ? 4 * kStageBufBytes : 0) +
+                          (2 * STAGES + 9) * 8 + 16;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_f16_tc_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_f16_tc_kernel<BN, STAGES, TMA_EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
       return -13;
     attr_set = true;
   }
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_f16_tc_kernel<BN, STAGES><<<grid, kThreads, smem, st>>>(ma, mb, M, N, K, ep, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -14;
+  gemm_f16_tc_kernel<BN, STAGES, TMA_EPI><<<grid, kThreads, smem, st>>>(ma, mb, mc, M, N, K, ep, resid_in_place,
+                                                                        err);
+  return launch_status("gemm");
 }
 
 }  // namespace
+
+int launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return 0;
+  fprintf(stderr, "s3b: CUDA error at %s launch: %s (%d)\n", what, cudaGetErrorString(e), (int)e);
+  return -14;
+}
 
 int num_sms() {
   static int n = 0;
@@ -426,11 +531,22 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
              const EpiParams& ep, int* err, cudaStream_t st) {
   if (M <= 0 || N <= 0 || K <= 0) return -1;
   if (lda < K || ldb < K) return -2;
-  if (ep.mode == EPI_QKV && (ep.C * 3 != N || ep.D <= 0 || ep.C % ep.D != 0 || ep.ntok <= 0 || (ep.D & 1)))
-    return -3;
   if (ep.mode == EPI_DECONV2 && (ep.cout <= 0 || N != 4 * ep.cout)) return -3;
-  if (N <= 128) return launch_gemm<128, 6>(A, lda, B, ldb, M, N, K, ep, err, st);
-  return launch_gemm<256, 4>(A, lda, B, ldb, M, N, K, ep, err, st);
+  if (ep.mode != EPI_STORE && ep.mode != EPI_DECONV2) return -3;
+  if (ep.rope && (ep.rope_D <= 0 || (ep.rope_D & 1) || ep.rope_mod <= 0)) return -3;
+  const int eb = ep.out_f32 ? 4 : 2;
+  // TMA epilogue: plain row-major output, residual absent or the output itself
+  const bool tma_epi = ep.mode == EPI_STORE && ep.map.kind == 0 && !ep.resid_up && ep.resid_mod == 0 &&
+                       (ep.resid == nullptr ||
+                        (static_cast<const void*>(ep.resid) == ep.out && ep.ldr == ep.ldo && ep.out_f32)) &&
+                       (reinterpret_cast<uintptr_t>(ep.out) & 15) == 0 && (ep.ldo * eb) % 16 == 0 && ep.ldo >= N;
+  const int resid_in_place = (tma_epi && ep.resid) ? 1 : 0;
+  if (tma_epi) {
+    if (N <= 128) return launch_gemm<128, 4, true>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
+    return launch_gemm<256, 3, true>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
+  }
+  if (N <= 128) return launch_gemm<128, 6, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
+  return launch_gemm<256, 4, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
 }
 
 }  // namespace s3b

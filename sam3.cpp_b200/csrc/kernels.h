@@ -36,7 +36,7 @@ __host__ __device__ inline long long map_row(const RowMap& m, long long r) {
   return (f * m.H + y) * m.W + x;
 }
 
-enum EpiMode : int { EPI_STORE = 0, EPI_QKV = 1, EPI_DECONV2 = 2 };
+enum EpiMode : int { EPI_STORE = 0, EPI_DECONV2 = 2 };
 enum Act : int { ACT_NONE = 0, ACT_GELU_ERF = 1, ACT_GELU_TANH = 2, ACT_RELU = 3 };
 
 // Epilogue of the tensor-core GEMM C[M,N] = A[M,K] * B[N,K]^T (f32 acc):
@@ -56,19 +56,13 @@ struct EpiParams {
   long long ldr = 0;
   long long resid_mod = 0;
   int resid_up = 0;
-  // EPI_STORE only: out = v * out_scale; RoPE on column pairs for GEMM rows
-  // < rope_rows, table row (row % rope_mod), table [rows][N/2][2] (cos, sin).
+  // EPI_STORE only: out = v * out_scale; RoPE on column pairs (2i, 2i+1) of
+  // columns < rope_cols and GEMM rows < rope_rows: head dim rope_D, position
+  // (row % rope_mod), table [positions][rope_D/2][2] (cos, sin).
   float out_scale = 1.0f;
-  long long rope_rows = 0, rope_mod = 1;
-  // EPI_QKV: columns [0,C) -> q, [C,2C) -> k, [2C,3C) -> v; each stored as
-  // [win][head][ntok][D] f16; RoPE (pairs (2i,2i+1), table [ntok][D/2][2])
-  // on q and k when `rope` is set; q multiplied by qscale.
-  __half* q = nullptr;
-  __half* k = nullptr;
-  __half* v = nullptr;
-  int C = 0, D = 0, heads = 0, ntok = 0;
   const float* rope = nullptr;
-  float qscale = 1.0f;
+  int rope_D = 0, rope_cols = 0;
+  long long rope_rows = 0, rope_mod = 1;
   // EPI_DECONV2: row = input pixel (f, y, x) of a (map.W x map.H) grid,
   // column = (ky*2 + kx)*cout + co, stored at pixel (2y+ky, 2x+kx).
   int cout = 0;
@@ -85,13 +79,16 @@ struct AttnParams {
   const __half* k = nullptr;
   const __half* v = nullptr;
   __half* o = nullptr;
-  long long q_bh = 0, q_n = 0;  // element strides: batch*head, token
-  long long k_bh = 0, k_n = 0;
-  long long v_bh = 0, v_n = 0;
+  // element strides: q + b*q_b + h*q_h + n*q_n (same for k, v)
+  long long q_b = 0, q_h = 0, q_n = 0;
+  long long k_b = 0, k_h = 0, k_n = 0;
+  long long v_b = 0, v_h = 0, v_n = 0;
   int heads = 1;
   int nq = 0, nk = 0;
-  long long o_b = 0, o_n = 0;  // out: o + b*o_b + n*o_n + h*D + d
-  float scale = 1.0f;          // softmax scale applied to q.k
+  // out row = map_row(omap, b*nq + n): o + row*o_n + h*D + d (rows mapped to -1 are dropped)
+  long long o_n = 0;
+  RowMap omap;
+  float scale = 1.0f;  // softmax scale applied to q.k
 };
 int attention(const AttnParams& p, int D, int batch_heads, cudaStream_t st);
 
@@ -133,5 +130,9 @@ int dequant_rows(const void* src, int qtype, long long ne0, long long nrows, voi
 
 // Returns the number of SMs of the current device (cached).
 int num_sms();
+
+// Status of the last launch: 0, or -14 after printing the CUDA error (a
+// failed launch, or an earlier asynchronous fault reported at this point).
+int launch_status(const char* what);
 
 }  // namespace s3b

@@ -33,8 +33,8 @@ static int gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, l
 }
 
 // One ViT block (sam3_vit_block_forward, sam3.cpp:3710-3801) on T tokens.
-static int vit_block(s3b_ctx* ctx, const VitBlock& B, int F, float* x, __half* xn, __half* q, __half* k, __half* v,
-                     __half* ao, __half* hbuf) {
+static int vit_block(s3b_ctx* ctx, const VitBlock& B, int F, float* x, __half* xn, __half* qkv, __half* ao,
+                     __half* hbuf) {
   const HParams& hp = ctx->model.hp;
   const int E = hp.vit_embed_dim, NH = hp.vit_num_heads, HD = E / NH, G = hp.n_img_embd();
   const long long T = (long long)F * G * G;
@@ -56,42 +56,40 @@ static int vit_block(s3b_ctx* ctx, const VitBlock& B, int F, float* x, __half* x
   const long long Tw = (long long)nwin * ntok;  // rows in window order (>= T when padded)
   // norm1 + window partition (ggml_win_part, sam3.cpp:3730)
   CK(layernorm(x, E, xn, 0, E, Tw, E, B.n1w.ptr(), B.n1b.ptr(), 1e-5f, wmap, ctx->stream));
-  // qkv + bias + split + RoPE(q, k) (sam3.cpp:3738-3771)
-  EpiParams ep;
-  ep.mode = EPI_QKV;
-  ep.bias = B.qkv.b->as<float>();
-  ep.q = q;
-  ep.k = k;
-  ep.v = v;
-  ep.C = E;
-  ep.D = HD;
-  ep.heads = NH;
-  ep.ntok = ntok;
-  ep.rope = B.rope ? B.rope->as<float>() : nullptr;
-  if (ep.rope && B.rope_n != ntok)
-    return set_error(ctx, kErrFormat, "freqs_cis has %d positions, attention has %d", B.rope_n, ntok);
-  ep.qscale = 1.0f;
+  // qkv + bias + RoPE(q, k) into [Tw][3E] f16 (sam3.cpp:3738-3771); the attention
+  // kernel reads q / k / v of each (window, head) with strides, so no split copies
+  EpiParams ep = epi_store(B.qkv, qkv, 0, 3LL * E);
+  if (B.rope) {
+    if (B.rope_n != ntok)
+      return set_error(ctx, kErrFormat, "freqs_cis has %d positions, attention has %d", B.rope_n, ntok);
+    ep.rope = B.rope->as<float>();
+    ep.rope_D = HD;
+    ep.rope_cols = 2 * E;
+    ep.rope_rows = Tw;
+    ep.rope_mod = ntok;
+  }
   CKG(gemm(ctx, xn, E, B.qkv, Tw, ep));
-  // flash attention, scale 1/sqrt(HD) (sam3.cpp:3773-3774); output rows in window order
+  // flash attention, scale 1/sqrt(HD) (sam3.cpp:3773-3774); rows leave in spatial
+  // order (window unpartition, sam3.cpp:3784) so the projection needs no remap
   AttnParams ap;
-  ap.q = q;
-  ap.k = k;
-  ap.v = v;
+  ap.q = qkv;
+  ap.k = qkv + E;
+  ap.v = qkv + 2 * E;
   ap.o = ao;
-  ap.q_bh = ap.k_bh = ap.v_bh = (long long)ntok * HD;
-  ap.q_n = ap.k_n = ap.v_n = HD;
+  ap.q_b = ap.k_b = ap.v_b = (long long)ntok * 3 * E;
+  ap.q_h = ap.k_h = ap.v_h = HD;
+  ap.q_n = ap.k_n = ap.v_n = 3LL * E;
   ap.heads = NH;
   ap.nq = ap.nk = ntok;
-  ap.o_b = (long long)ntok * E;
   ap.o_n = E;
+  ap.omap = wmap;
   ap.scale = 1.0f / sqrtf((float)HD);
   CKG(run_attn(ctx, ap, HD, nwin * NH));
-  // proj + bias + window unpartition + residual (sam3.cpp:3779-3787)
+  // proj + bias, residual added in place (x chunk TMA-loaded in the epilogue) (sam3.cpp:3779-3787)
   EpiParams pe = epi_store(B.proj, x, 1, E);
-  pe.map = wmap;
   pe.resid = x;
   pe.ldr = E;
-  CKG(gemm(ctx, ao, E, B.proj, Tw, pe));
+  CKG(gemm(ctx, ao, E, B.proj, T, pe));
   // norm2 -> fc1 + GELU(erf) -> fc2 + residual (sam3.cpp:3789-3798)
   RowMap id;
   CK(layernorm(x, E, xn, 0, E, T, E, B.n2w.ptr(), B.n2b.ptr(), 1e-5f, id, ctx->stream));
@@ -206,9 +204,7 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
   DevBuf* col = ctx->buf("vit_col", (size_t)Tmax * Kp * 2, &rc);
   DevBuf* xp = ctx->buf("vit_xp", (size_t)Tmax * E * 4, &rc);
   DevBuf* xn = ctx->buf("vit_xn", (size_t)Tmax * E * 2, &rc);
-  DevBuf* q = ctx->buf("vit_q", (size_t)Tmax * E * 2, &rc);
-  DevBuf* k = ctx->buf("vit_k", (size_t)Tmax * E * 2, &rc);
-  DevBuf* v = ctx->buf("vit_v", (size_t)Tmax * E * 2, &rc);
+  DevBuf* qkv = ctx->buf("vit_qkv", (size_t)Tmax * 3 * E * 2, &rc);
   DevBuf* ao = ctx->buf("vit_ao", (size_t)Tmax * E * 2, &rc);
   DevBuf* hb = ctx->buf("vit_h", (size_t)Tmax * hp.vit_mlp_dim * 2, &rc);
   if (rc) return rc;
@@ -227,8 +223,8 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
     RowMap id;
     CK(layernorm(xp->as<float>(), E, x, 1, E, T, E, M.ln_pre_w.ptr(), M.ln_pre_b.ptr(), 1e-5f, id, ctx->stream));
     for (int b = 0; b < hp.vit_depth; ++b) {
-      if ((rc = vit_block(ctx, M.vit[b], F, x, xn->as<__half>(), q->as<__half>(), k->as<__half>(), v->as<__half>(),
-                          ao->as<__half>(), hb->as<__half>())))
+      if ((rc = vit_block(ctx, M.vit[b], F, x, xn->as<__half>(), qkv->as<__half>(), ao->as<__half>(),
+                          hb->as<__half>())))
         return rc;
     }
     if (want_neck) {

@@ -39,5 +39,9 @@ def engine(s3b):
         pytest.skip("no CUDA device")
     torch.cuda.init()
     e = s3b.Engine(0)
+    # run the engine on torch's stream so inputs made by torch are ready and
+    # in-place outputs are not raced by torch's own reference computations
+    e.set_stream(torch.cuda.current_stream().cuda_stream)
     yield e
+    e.set_stream(None)
     e.close()

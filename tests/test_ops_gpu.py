@@ -40,6 +40,44 @@ def test_gemm(engine, M, N, K, act):
     assert err < tol, f"max abs err {err} (tol {tol})"
 
 
+@pytest.mark.parametrize("M,N,K", [(5184, 1024, 1024), (1000, 96, 256), (333, 1024, 4736)])
+def test_gemm_inplace_residual(engine, M, N, K):
+    """out += A B^T + bias with the residual being the output itself (the
+    epilogue loads the residual chunk by TMA into its staging buffer)."""
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    A = torch.randn(M, K, device="cuda", generator=g).half()
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
+    bias = torch.randn(N, device="cuda", generator=g)
+    x = torch.randn(M, N, device="cuda", generator=g)
+    ref = x + A.float() @ B.float().T + bias
+    engine.gemm(A, B, x, bias=bias, resid=x)
+    engine.sync()
+    assert (x - ref).abs().max().item() < 2e-3 * max(1.0, ref.abs().max().item())
+
+
+def test_gemm_rope_f16(engine):
+    """RoPE on the first 2*E columns (q, k) of a fused qkv projection, f16 TMA-store epilogue."""
+    M, E, HD = 576 * 2, 256, 64
+    g = torch.Generator(device="cuda").manual_seed(7)
+    A = torch.randn(M, E, device="cuda", generator=g).half()
+    B = (torch.randn(3 * E, E, device="cuda", generator=g) * 0.05).half()
+    bias = torch.randn(3 * E, device="cuda", generator=g) * 0.1
+    ang = torch.rand(576, HD // 2, device="cuda", generator=g) * 6.28
+    table = torch.stack([ang.cos(), ang.sin()], -1).contiguous()
+    out = torch.empty(M, 3 * E, device="cuda", dtype=torch.float16)
+    engine.gemm_rope(A, B, out, bias, table, HD, 2 * E, 576)
+    engine.sync()
+    y = A.float() @ B.float().T + bias
+    pos = torch.arange(M, device="cuda") % 576
+    c = table[pos, :, 0].repeat(1, 2 * E // HD)
+    s = table[pos, :, 1].repeat(1, 2 * E // HD)
+    a, b = y[:, 0:2 * E:2], y[:, 1:2 * E:2]
+    ref = y.clone()
+    ref[:, 0:2 * E:2] = a * c - b * s
+    ref[:, 1:2 * E:2] = a * s + b * c
+    assert (out.float() - ref).abs().max().item() < 2e-2
+
+
 def test_gemm_f16_out_strided(engine):
     M, N, K = 513, 640, 320
     A_full = torch.randn(M, K + 64, device="cuda").half()
