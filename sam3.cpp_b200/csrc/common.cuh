@@ -171,10 +171,32 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_fmt) {
 }
 
 // ---------------------------------------------------------------- math
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// erf by Abramowitz & Stegun, Handbook of Mathematical Functions, eq. 7.1.26:
+//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),
+//   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7 (odd extension for z < 0).
+// Branch-free (one reciprocal, one exponential, five FMAs): the GEMM
+// epilogue evaluates it for every element of the MLP hidden layer.
+__device__ __forceinline__ float erf_as7126(float x) {
+  const float z = fabsf(x);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  const float r = 1.0f - poly * __expf(-z * z);
+  return copysignf(r, x);
+}
+// GELU with the erf form (ggml_gelu_erf, sam3.cpp:3794 / 3882).
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f));
+}
+// GELU with the tanh form (ggml_gelu, sam3.cpp:4449); tanh(u) = 1 - 2 / (exp(2u) + 1).
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+  const float u = fminf(fmaxf(k0 * fmaf(k1 * x * x, x, x), -10.0f), 10.0f);  // tanh(+-10) == +-1 in f32
+  const float th = 1.0f - __fdividef(2.0f, __expf(2.0f * u) + 1.0f);
+  return 0.5f * x * (1.0f + th);
 }
 
 }  // namespace s3b

@@ -41,15 +41,16 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr uint32_t kStageBufBytes = 16384;  // 128 rows x 128 B
 
-__device__ __forceinline__ float apply_act(float v, int act) {
-  switch (act) {
-    case ACT_GELU_ERF: return gelu_erf(v);
-    case ACT_GELU_TANH: return gelu_tanh(v);
-    case ACT_RELU: return v > 0.f ? v : 0.f;
-    default: return v;
-  }
+
+// Two f32 -> one packed f16x2 register (lo in the low half), round to nearest even.
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
+// All loops over the 16 values below are fully unrolled with compile-time
+// indices (tails are predicated), so v[] stays in registers.
 __device__ __forceinline__ void store16(void* base, long long idx, int is_f32, const float (&v)[16], int n_valid,
                                         bool vec_ok) {
   if (is_f32) {
@@ -58,28 +59,35 @@ __device__ __forceinline__ void store16(void* base, long long idx, int is_f32, c
 #pragma unroll
       for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
     } else {
-      for (int i = 0; i < n_valid; ++i) p[i] = v[i];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < n_valid) p[i] = v[i];
     }
   } else {
     __half* p = reinterpret_cast<__half*>(base) + idx;
     if (vec_ok && n_valid == 16) {
-      __align__(16) __half2 h[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-      *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(&h[0]);
-      *reinterpret_cast<uint4*>(p + 8) = *reinterpret_cast<const uint4*>(&h[4]);
+      *reinterpret_cast<uint4*>(p) = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]),
+                                                pack_h2(v[6], v[7]));
+      *reinterpret_cast<uint4*>(p + 8) = make_uint4(pack_h2(v[8], v[9]), pack_h2(v[10], v[11]),
+                                                    pack_h2(v[12], v[13]), pack_h2(v[14], v[15]));
     } else {
-      for (int i = 0; i < n_valid; ++i) p[i] = __float2half_rn(v[i]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < n_valid) p[i] = __float2half_rn(v[i]);
     }
   }
 }
 
-// bias + activation + RoPE + scale on 16 consecutive columns [gc, gc+16) of row gr.
-__device__ __forceinline__ void epi_math16(const EpiParams& ep, long long gr, int gc, int N, float (&v)[16]) {
+// bias + activation + RoPE + scale on 16 consecutive columns [gc, gc+16) of
+// row gr; rope_pos = RoPE position of the row (gr % rope_mod), or -1 for none.
+__device__ __forceinline__ void epi_math16(const EpiParams& ep, int rope_pos, int gc, int N, float (&v)[16]) {
   const int n_valid = min(16, N - gc);
   if (ep.bias) {
     if (ep.mode == EPI_DECONV2) {
-      for (int i = 0; i < n_valid; ++i) v[i] += __ldg(ep.bias + (gc + i) % ep.cout);
+      const int c0 = gc % ep.cout;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < n_valid) v[i] += __ldg(ep.bias + (c0 + i) % ep.cout);
     } else if (n_valid == 16 && ((reinterpret_cast<uintptr_t>(ep.bias + gc) & 15) == 0)) {
 #pragma unroll
       for (int i = 0; i < 16; i += 4) {
@@ -87,22 +95,49 @@ __device__ __forceinline__ void epi_math16(const EpiParams& ep, long long gr, in
         v[i] += b.x; v[i + 1] += b.y; v[i + 2] += b.z; v[i + 3] += b.w;
       }
     } else {
-      for (int i = 0; i < n_valid; ++i) v[i] += __ldg(ep.bias + gc + i);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < n_valid) v[i] += __ldg(ep.bias + gc + i);
     }
   }
-  if (ep.act != ACT_NONE) {
+  // one uniform branch per activation, so the 16 independent evaluations interleave
+  if (ep.act == ACT_GELU_ERF) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = apply_act(v[i], ep.act);
+    for (int i = 0; i < 16; ++i) v[i] = gelu_erf(v[i]);
+  } else if (ep.act == ACT_GELU_TANH) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = gelu_tanh(v[i]);
+  } else if (ep.act == ACT_RELU) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = fmaxf(v[i], 0.0f);
   }
-  if (ep.rope && gc < ep.rope_cols && gr < ep.rope_rows) {
+  if (rope_pos >= 0 && gc < ep.rope_cols) {
     const int half_d = ep.rope_D >> 1;
-    const long long pos = gr % ep.rope_mod;
-    for (int i = 0; i + 1 < n_valid; i += 2) {
-      const int d = (gc + i) % ep.rope_D;
-      const float2 cs = __ldg(reinterpret_cast<const float2*>(ep.rope + (pos * half_d + (d >> 1)) * 2));
-      const float a = v[i], b = v[i + 1];
-      v[i] = a * cs.x - b * cs.y;
-      v[i + 1] = a * cs.y + b * cs.x;
+    const float* tb = ep.rope + (size_t)rope_pos * half_d * 2;
+    const int d0 = gc % ep.rope_D;  // even: gc and rope_D are even
+    if ((ep.rope_D & 15) == 0 && (ep.rope_cols & 15) == 0 && n_valid == 16) {
+      // the 16 columns lie inside one head: 8 consecutive (cos, sin) pairs
+      const float4* t4 = reinterpret_cast<const float4*>(tb + d0);
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        const float4 cs = __ldg(t4 + (i >> 2));
+        const float a0 = v[i], b0 = v[i + 1], a1 = v[i + 2], b1 = v[i + 3];
+        v[i] = a0 * cs.x - b0 * cs.y;
+        v[i + 1] = a0 * cs.y + b0 * cs.x;
+        v[i + 2] = a1 * cs.z - b1 * cs.w;
+        v[i + 3] = a1 * cs.w + b1 * cs.z;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        if (i + 1 < n_valid && gc + i < ep.rope_cols) {
+          const int d = (d0 + i) % ep.rope_D;
+          const float2 cs = __ldg(reinterpret_cast<const float2*>(tb + d));
+          const float a = v[i], b = v[i + 1];
+          v[i] = a * cs.x - b * cs.y;
+          v[i + 1] = a * cs.y + b * cs.x;
+        }
+      }
     }
   }
   if (ep.out_scale != 1.0f) {
@@ -137,7 +172,9 @@ __device__ __forceinline__ void epi_store_direct16(const EpiParams& ep, long lon
           v[i] += t.x; v[i + 1] += t.y; v[i + 2] += t.z; v[i + 3] += t.w;
         }
       } else {
-        for (int i = 0; i < n_valid; ++i) v[i] += rp[i];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < n_valid) v[i] += rp[i];
       }
     }
     store16(ep.out, orow * ep.ldo + gc, ep.out_f32, v, n_valid, (ep.ldo % 16) == 0);
@@ -322,31 +359,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t aphase = 0;
     uint32_t chunk_ctr = 0;
+    uint32_t r_issued0 = 0, r_issued1 = 0, r_used0 = 0, r_used1 = 0;  // residual loads per staging buffer
+    const int cw = ep.out_f32 ? 32 : 64;                // chunk = 128 B of columns: 32 f32 or 64 f16
+    // Residual chunk `ctr` (columns gcb.., rows m0..) -> its staging buffer, once
+    // the TMA store that last used that buffer has finished reading it.
+    auto issue_resid = [&](uint32_t ctr, int gcb, int m0) {
+      const int b = (int)(ctr & 1);
+      const int bsel = half * 2 + b;
+      bulk_wait_read1();
+      if (gcb < N) {
+        mbar_arrive_expect_tx(&rfull[bsel], kStageBufBytes);
+        tma_load_2d(&tmC, &rfull[bsel], sC + bsel * kStageBufBytes, gcb, m0);
+      } else {
+        mbar_arrive(&rfull[bsel]);
+      }
+      if (b) ++r_issued1; else ++r_issued0;
+    };
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
       const int m0 = (t / tiles_n) * kBM;
       const int n0 = (t % tiles_n) * BN;
+      // the first residual chunk does not depend on the accumulator: fetch it during the main loop
+      if (TMA_EPI && resid_in_place && leader) issue_resid(chunk_ctr, n0 + half * (BN / 2), m0);
       if (!mbar_wait(&tfull[acc], aphase, s_abort, err, kErrWaitTmemFull)) break;
       tc_fence_after();
       const long long gr = (long long)m0 + row;
+      const int rope_pos = (ep.rope && gr < ep.rope_rows) ? (int)(gr % ep.rope_mod) : -1;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * (BN / 2));
       if (TMA_EPI) {
-        // chunk = 128 B of columns: 32 f32 or 64 f16
-        const int cw = ep.out_f32 ? 32 : 64;
         bool ok = true;
         for (int c0 = 0; c0 < BN / 2; c0 += cw) {
           const int gcb = n0 + half * (BN / 2) + c0;
           const int bsel = half * 2 + (int)(chunk_ctr & 1);
           uint8_t* buf = sC + bsel * kStageBufBytes;
-          if (resid_in_place && leader) {
-            // residual chunk -> staging buffer, once the store that last used it has read it
-            bulk_wait_read1();
-            if (gcb < N) {
-              mbar_arrive_expect_tx(&rfull[bsel], kStageBufBytes);
-              tma_load_2d(&tmC, &rfull[bsel], buf, gcb, m0);
-            } else {
-              mbar_arrive(&rfull[bsel]);
-            }
-          }
           uint32_t r[64];
           TMEM_LD16(tbase + (uint32_t)c0, r, 0);
           TMEM_LD16(tbase + (uint32_t)(c0 + 16), r, 16);
@@ -364,6 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (resid_in_place) {
             // parity of this buffer's residual barrier = number of its earlier uses & 1
             if (!mbar_wait(&rfull[bsel], (chunk_ctr >> 1) & 1u, s_abort, err, kErrWaitMisc)) { ok = false; break; }
+            if (chunk_ctr & 1) ++r_used1; else ++r_used0;
           } else {
             if (leader) bulk_wait_read1();  // the store that last used `buf` has read it
             named_bar(1 + half, 128);
@@ -376,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[j * 16 + i]);
               const int gc = gcb + j * 16;
-              if (gc < N) epi_math16(ep, gr, gc, N, v);
+              if (gc < N) epi_math16(ep, rope_pos, gc, N, v);
               if (ep.out_f32) {
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
@@ -392,10 +437,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
                   const int unit = j * 2 + u;
-                  __align__(16) __half2 h[4];
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[8 * u + 2 * e], v[8 * u + 2 * e + 1]);
-                  *reinterpret_cast<uint4*>(rowp + ((unit ^ (row & 7)) << 4)) = *reinterpret_cast<const uint4*>(h);
+                  *reinterpret_cast<uint4*>(rowp + ((unit ^ (row & 7)) << 4)) =
+                      make_uint4(pack_h2(v[8 * u], v[8 * u + 1]), pack_h2(v[8 * u + 2], v[8 * u + 3]),
+                                 pack_h2(v[8 * u + 4], v[8 * u + 5]), pack_h2(v[8 * u + 6], v[8 * u + 7]));
                 }
               }
             }
@@ -406,6 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_store_2d(&tmC, buf, gcb, m0);
             bulk_commit();
           }
+          if (resid_in_place && leader && c0 + cw < BN / 2) issue_resid(chunk_ctr + 1, gcb + cw, m0);
           ++chunk_ctr;
         }
         if (!ok) break;
@@ -425,14 +470,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-            epi_math16(ep, gr, gc, N, v);
+            epi_math16(ep, rope_pos, gc, N, v);
             epi_store_direct16(ep, gr, gc, N, v);
           }
         }
       }
       if (++acc == 2) { acc = 0; aphase ^= 1; }
     }
-    if (TMA_EPI && leader) bulk_wait_all();
+    if (TMA_EPI && leader) {
+      bulk_wait_all();
+      // a residual load issued but never consumed (only after an abort) lands before exit
+      if (r_issued0 > r_used0) mbar_wait_drain(&rfull[half * 2 + 0], (r_issued0 - 1) & 1u, err);
+      if (r_issued1 > r_used1) mbar_wait_drain(&rfull[half * 2 + 1], (r_issued1 - 1) & 1u, err);
+    }
   }
 
   tc_fence_before();

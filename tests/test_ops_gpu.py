@@ -78,6 +78,25 @@ def test_gemm_rope_f16(engine):
     assert (out.float() - ref).abs().max().item() < 2e-2
 
 
+@pytest.mark.parametrize("act", [1, 2])
+def test_gemm_activation_accuracy(engine, act):
+    """The epilogue GELUs (erf by Abramowitz-Stegun 7.1.26; tanh via exp) against
+    float64 references: A holds f16-exact inputs, B = I, so out = act(x) exactly up
+    to the activation's own error (bound 2e-6 absolute + 1e-6 relative)."""
+    x = torch.linspace(-9.0, 9.0, 128 * 64, device="cuda").half().reshape(-1, 64)
+    eye = torch.eye(64, device="cuda").half()
+    out = torch.empty(x.shape[0], 64, device="cuda", dtype=torch.float32)
+    engine.gemm(x, eye, out, act=act)
+    engine.sync()
+    xd = x.double()
+    if act == 1:
+        ref = 0.5 * xd * (1 + torch.erf(xd / 2 ** 0.5))
+    else:
+        ref = 0.5 * xd * (1 + torch.tanh(0.7978845608028654 * (xd + 0.044715 * xd ** 3)))
+    err = (out.double() - ref).abs()
+    assert (err <= 2e-6 + 1e-6 * ref.abs()).all(), err.max().item()
+
+
 def test_gemm_f16_out_strided(engine):
     M, N, K = 513, 640, 320
     A_full = torch.randn(M, K + 64, device="cuda").half()
