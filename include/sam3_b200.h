@@ -62,7 +62,10 @@ int s3b_set_stream(s3b_ctx* ctx, void* cuda_stream);
 int s3b_reset_stream(s3b_ctx* ctx);
 /* Waits for all work of the context and checks the device error word. */
 int s3b_sync(s3b_ctx* ctx);
-/* Options: "frames_per_pass" (encoder micro-batch, default 8). */
+/* Options: "frames_per_pass" (encoder micro-batch, default 8);
+ * "stop_after_blocks" (test hook: run only the first n backbone blocks and
+ * no neck, -1 = all; the stage runners of sam3.h:441-496 play this role in
+ * the reference). */
 int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value);
 
 /* Profiling (CUDA events on the context stream around every GEMM and

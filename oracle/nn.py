@@ -62,18 +62,22 @@ def rope(x, cis):
 
 
 def attention(q, k, v, scale, f16_inputs=False):
-    """softmax(q k^T * scale) v for q [B, Nq, D], k/v [B, Nk, D] (no mask), f32 / f64 softmax."""
+    """softmax(q k^T * scale) v for q [B, Nq, D], k/v [B, Nk, D] (no mask), f32 softmax."""
     if f16_inputs:
         q, k, v = f16r(q), f16r(k), f16r(v)
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    v = np.asarray(v, np.float32)
     out = np.empty((q.shape[0], q.shape[1], v.shape[2]), np.float32)
     for b in range(q.shape[0]):
         # chunk queries to bound memory for the global / memory-attention sizes
         for s in range(0, q.shape[1], 2048):
-            sc = np.matmul(q[b, s:s + 2048], k[b].T).astype(np.float64) * scale
+            sc = np.matmul(q[b, s:s + 2048], k[b].T)
+            sc *= np.float32(scale)
             sc -= sc.max(axis=-1, keepdims=True)
-            p = np.exp(sc)
-            p /= p.sum(axis=-1, keepdims=True)
-            out[b, s:s + 2048] = np.matmul(p.astype(np.float32), v[b])
+            np.exp(sc, out=sc)
+            sc /= sc.sum(axis=-1, keepdims=True, dtype=np.float64).astype(np.float32)
+            out[b, s:s + 2048] = np.matmul(sc, v[b])
     return out
 
 

@@ -232,6 +232,11 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     ctx->max_frames_per_pass = (int)value;
     return kOk;
   }
+  if (k == "stop_after_blocks") {
+    if (value < -1 || value > 1024) return set_error(ctx, kErrArg, "stop_after_blocks out of range");
+    ctx->stop_after_blocks = (int)value;
+    return kOk;
+  }
   return set_error(ctx, kErrArg, "unknown option '%s'", key);
 }
 

@@ -191,6 +191,12 @@ __global__ void add_scaled_kernel(const float* __restrict__ a, const float* __re
     y[i] = a[i] + s * b[i];
 }
 
+__global__ void add_scaled_to_f16_kernel(const float* __restrict__ a, const float* __restrict__ b, float s,
+                                         long long n, __half* __restrict__ y) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    y[i] = __float2half_rn(b ? a[i] + s * b[i] : a[i]);
+}
+
 // One thread per 32-value block. Values are produced exactly as ggml's
 // dequantisers define them: q4_0 (q - 8) * d, q4_1 q * d + m (multiply then
 // add, both rounded to f32), q8_0 q * d, with d and m the f16 fields.
@@ -306,6 +312,11 @@ int cast_f32_f16(const float* x, long long n, __half* y, cudaStream_t st) {
 
 int add_scaled_f32(const float* a, const float* b, float s, long long n, float* y, cudaStream_t st) {
   add_scaled_kernel<<<grid_for(n, 256), 256, 0, st>>>(a, b, s, n, y);
+  return launch_ok();
+}
+
+int add_scaled_to_f16(const float* a, const float* b, float s, long long n, __half* y, cudaStream_t st) {
+  add_scaled_to_f16_kernel<<<grid_for(n, 256), 256, 0, st>>>(a, b, s, n, y);
   return launch_ok();
 }
 

@@ -119,6 +119,8 @@ int preprocess_u8(const uint8_t* img, int B, int H, int W, const float mean[3], 
 
 int cast_f32_f16(const float* x, long long n, __half* y, cudaStream_t st);
 int add_scaled_f32(const float* a, const float* b, float s, long long n, float* y, cudaStream_t st);
+// y = f16(a + s*b) (b may be null: y = f16(a)).
+int add_scaled_to_f16(const float* a, const float* b, float s, long long n, __half* y, cudaStream_t st);
 
 // ggml block formats (32 values per block along the row).
 enum QType : int { QT_F32 = 0, QT_F16 = 1, QT_Q4_0 = 2, QT_Q4_1 = 3, QT_Q8_0 = 8 };

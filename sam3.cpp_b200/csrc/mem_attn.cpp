@@ -1,12 +1,171 @@
-// Memory attention on B200 (host orchestration).
+// Memory attention on B200 (host orchestration, C++14).
+//
+// Replaces sam3_build_mem_attn_graph (sam3.cpp:9224-9337) and its ggml
+// compute inside sam3_propagate_single (sam3.cpp:11171-11453): per layer a
+// single-head (d = 256) RoPE self-attention over the N = feat^2 current
+// tokens, a RoPE cross-attention to the M memory tokens (K projected from
+// prompt + prompt_pos, V from prompt; RoPE on the spatial keys only, their
+// table repeated per memory slot), and a ReLU FFN, each pre-normed with a
+// residual; a final LayerNorm. The RoPE table follows
+// sam3_ensure_tracker_pe_caches (sam3.cpp:11126-11169) and is cached on the
+// device per feature size.
+#include <math.h>
+
+#include <vector>
+
 #include "engine.h"
 
 namespace s3b {
 
+#define CKL(call)                                                                                          \
+  do {                                                                                                     \
+    int _rc = (call);                                                                                      \
+    count_launch(ctx);                                                                                     \
+    if (_rc) return set_error(ctx, _rc < -9 ? kErrCuda : kErrArg, "%s failed (%d)", #call, _rc);          \
+  } while (0)
+#define CKR(call)           \
+  do {                      \
+    int _rc = (call);       \
+    if (_rc) return _rc;    \
+  } while (0)
+
+// Axial RoPE table (sam3_compute_axial_cis, sam3.cpp:3555-3586) as [N][dim/2][2].
+static void axial_cis(int dim, int end_x, int end_y, float theta, float scale, std::vector<float>& out) {
+  const int q = dim / 4;
+  std::vector<float> freqs(q);
+  for (int i = 0; i < q; ++i) freqs[i] = 1.0f / powf(theta, (float)(i * 4) / (float)dim);
+  const int N = end_x * end_y;
+  out.assign((size_t)N * dim, 0.f);
+  for (int idx = 0; idx < N; ++idx) {
+    const float tx = (float)(idx % end_x) * scale, ty = (float)(idx / end_x) * scale;
+    for (int i = 0; i < q; ++i) {
+      out[(size_t)idx * dim + 2 * i] = cosf(tx * freqs[i]);
+      out[(size_t)idx * dim + 2 * i + 1] = sinf(tx * freqs[i]);
+      out[(size_t)idx * dim + 2 * q + 2 * i] = cosf(ty * freqs[i]);
+      out[(size_t)idx * dim + 2 * q + 2 * i + 1] = sinf(ty * freqs[i]);
+    }
+  }
+}
+
+static const float* rope_table(s3b_ctx* ctx, int feat, int D, int* rc) {
+  const std::string key = "ma_rope_" + std::to_string(feat) + "_" + std::to_string(D);
+  auto it = ctx->ws.find(key);
+  if (it != ctx->ws.end() && it->second) return it->second->as<float>();
+  std::vector<float> t;
+  axial_cis(D, feat, feat, 10000.0f, 1.0f, t);
+  DevBuf* b = ctx->buf(key, t.size() * 4, rc);
+  if (*rc) return nullptr;
+  if (cudaMemcpy(b->p, t.data(), t.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    *rc = set_error(ctx, kErrCuda, "RoPE table upload failed");
+    return nullptr;
+  }
+  return b->as<float>();
+}
+
 int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const float* prompt,
                  const float* prompt_pos, int m_total, int n_ptr, float* out) {
-  (void)curr; (void)src_pos; (void)feat; (void)prompt; (void)prompt_pos; (void)m_total; (void)n_ptr; (void)out;
-  return set_error(ctx, kErrUnsupported, "memory attention not built yet");
+  const Model& M = ctx->model;
+  const int D = M.hp.neck_dim, MD = M.hp.mem_out_dim;
+  const long long N = (long long)feat * feat;
+  const long long Mt = m_total, m_sp = m_total - n_ptr;
+  if (M.mem.empty()) return set_error(ctx, kErrState, "no memory-attention layers");
+  if (M.mem[0].ca_k.K != MD) return set_error(ctx, kErrFormat, "cross-attention kv dim %d != %d", M.mem[0].ca_k.K, MD);
+  int rc = 0;
+  const float* rope = rope_table(ctx, feat, D, &rc);
+  if (rc) return rc;
+  const int FFN = M.mem[0].fc1.N;
+  DevBuf* x = ctx->buf("ma_x", (size_t)N * D * 4, &rc);
+  DevBuf* xn = ctx->buf("ma_xn", (size_t)N * D * 2, &rc);
+  DevBuf* qkv = ctx->buf("ma_qkv", (size_t)N * 3 * D * 2, &rc);
+  DevBuf* ao = ctx->buf("ma_ao", (size_t)N * D * 2, &rc);
+  DevBuf* hb = ctx->buf("ma_h", (size_t)N * FFN * 2, &rc);
+  DevBuf* kvin = ctx->buf("ma_kvin", (size_t)Mt * MD * 2, &rc);
+  DevBuf* pin = ctx->buf("ma_pin", (size_t)Mt * MD * 2, &rc);
+  DevBuf* kb = ctx->buf("ma_k", (size_t)Mt * D * 2, &rc);
+  DevBuf* vb = ctx->buf("ma_v", (size_t)Mt * D * 2, &rc);
+  if (rc) return rc;
+  float* X = x->as<float>();
+  __half* XN = xn->as<__half>();
+  RowMap id;
+  // pos_enc_at_input: x = curr + 0.1 * src_pos (sam3.cpp:9243)
+  CKL(add_scaled_f32(curr, src_pos, 0.1f, N * D, X, ctx->stream));
+  // memory keys see prompt + prompt_pos, values see prompt (sam3.cpp:9278-9283)
+  CKL(add_scaled_to_f16(prompt, prompt_pos, 1.0f, Mt * MD, kvin->as<__half>(), ctx->stream));
+  CKL(add_scaled_to_f16(prompt, nullptr, 0.0f, Mt * MD, pin->as<__half>(), ctx->stream));
+  const float scale = 1.0f / sqrtf((float)D);
+
+  for (size_t l = 0; l < M.mem.size(); ++l) {
+    const MemAttnLayer& L = M.mem[l];
+    // self-attention with RoPE on q and k (sam3.cpp:9247-9271)
+    CKL(layernorm(X, D, XN, 0, D, N, D, L.n1w.ptr(), L.n1b.ptr(), 1e-5f, id, ctx->stream));
+    EpiParams e = epi_store(L.sa_qkv, qkv->p, 0, 3LL * D);
+    e.rope = rope;
+    e.rope_D = D;
+    e.rope_cols = 2 * D;
+    e.rope_rows = N;
+    e.rope_mod = N;
+    CKR(run_gemm(ctx, XN, D, L.sa_qkv, N, e));
+    AttnParams a;
+    a.q = qkv->as<__half>();
+    a.k = a.q + D;
+    a.v = a.q + 2 * D;
+    a.q_n = a.k_n = a.v_n = 3LL * D;
+    a.heads = 1;
+    a.nq = a.nk = (int)N;
+    a.o = ao->as<__half>();
+    a.o_n = D;
+    a.scale = scale;
+    CKR(run_attn(ctx, a, D, 1));
+    EpiParams r = epi_store(L.sa_out, X, 1, D);
+    r.resid = X;
+    r.ldr = D;
+    CKR(run_gemm(ctx, ao->as<__half>(), D, L.sa_out, N, r));
+    // cross-attention to the memory (sam3.cpp:9274-9316)
+    CKL(layernorm(X, D, XN, 0, D, N, D, L.n2w.ptr(), L.n2b.ptr(), 1e-5f, id, ctx->stream));
+    EpiParams eq = epi_store(L.ca_q, qkv->p, 0, D);
+    eq.rope = rope;
+    eq.rope_D = D;
+    eq.rope_cols = D;
+    eq.rope_rows = N;
+    eq.rope_mod = N;
+    CKR(run_gemm(ctx, XN, D, L.ca_q, N, eq));
+    EpiParams ek = epi_store(L.ca_k, kb->p, 0, D);
+    if (m_sp > 0) {
+      ek.rope = rope;
+      ek.rope_D = D;
+      ek.rope_cols = D;
+      ek.rope_rows = m_sp;  // pointer tokens at the end get no RoPE
+      ek.rope_mod = N;      // the table repeats for every memory slot
+    }
+    CKR(run_gemm(ctx, kvin->as<__half>(), MD, L.ca_k, Mt, ek));
+    CKR(run_gemm(ctx, pin->as<__half>(), MD, L.ca_v, Mt, epi_store(L.ca_v, vb->p, 0, D)));
+    AttnParams c;
+    c.q = qkv->as<__half>();
+    c.k = kb->as<__half>();
+    c.v = vb->as<__half>();
+    c.q_n = c.k_n = c.v_n = D;
+    c.heads = 1;
+    c.nq = (int)N;
+    c.nk = (int)Mt;
+    c.o = ao->as<__half>();
+    c.o_n = D;
+    c.scale = scale;
+    CKR(run_attn(ctx, c, D, 1));
+    EpiParams r2 = epi_store(L.ca_out, X, 1, D);
+    r2.resid = X;
+    r2.ldr = D;
+    CKR(run_gemm(ctx, ao->as<__half>(), D, L.ca_out, N, r2));
+    // FFN (sam3.cpp:9318-9326)
+    CKL(layernorm(X, D, XN, 0, D, N, D, L.n3w.ptr(), L.n3b.ptr(), 1e-5f, id, ctx->stream));
+    CKR(run_gemm(ctx, XN, D, L.fc1, N, epi_store(L.fc1, hb->p, 0, FFN, ACT_RELU)));
+    EpiParams r3 = epi_store(L.fc2, X, 1, D);
+    r3.resid = X;
+    r3.ldr = D;
+    CKR(run_gemm(ctx, hb->as<__half>(), FFN, L.fc2, N, r3));
+  }
+  // final norm (sam3.cpp:9330-9334)
+  CKL(layernorm(X, D, out, 1, D, N, D, M.mem_norm_w.ptr(), M.mem_norm_b.ptr(), 1e-5f, id, ctx->stream));
+  return check_device(ctx, "mem_attn");
 }
 
 }  // namespace s3b

@@ -169,7 +169,7 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
   const long long tok_per_frame = (long long)G * G;
   int rc = 0;
   Outputs& O = ctx->out;
-  const bool want_neck = !(flags & 1) && M.has_neck_trk;
+  const bool want_neck = !(flags & 1) && M.has_neck_trk && ctx->stop_after_blocks < 0;
   const bool want_det = want_neck && M.has_neck_det && !(flags & 2);
   // outputs
   if (O.n_frames != n_frames || O.img_size != S || !O.backbone) {
@@ -222,7 +222,11 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
     // ln_pre (sam3.cpp:3825-3827)
     RowMap id;
     CK(layernorm(xp->as<float>(), E, x, 1, E, T, E, M.ln_pre_w.ptr(), M.ln_pre_b.ptr(), 1e-5f, id, ctx->stream));
-    for (int b = 0; b < hp.vit_depth; ++b) {
+    // stage runner (test hook, like sam3_test_run_vit_block_stage): stop after `stop_after_blocks`
+    const int n_blocks = ctx->stop_after_blocks >= 0 && ctx->stop_after_blocks < hp.vit_depth
+                             ? ctx->stop_after_blocks
+                             : hp.vit_depth;
+    for (int b = 0; b < n_blocks; ++b) {
       if ((rc = vit_block(ctx, M.vit[b], F, x, xn->as<__half>(), qkv->as<__half>(), ao->as<__half>(),
                           hb->as<__half>())))
         return rc;

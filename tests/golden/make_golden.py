@@ -1,0 +1,191 @@
+#!/usr/bin/env python3
+"""Generates the golden fixtures in tests/golden/ from the reference's own code.
+
+Run in a container that has the reference checkout (read-only) and torch:
+
+    python tests/golden/make_golden.py --reference /path/to/sam3.cpp
+
+1. vit_golden.npz — the reference's PyTorch ViT + SimpleFPN forward
+   (tests/dump_vit_reference.py main(), run unmodified as a subprocess) on a
+   seeded synthetic checkpoint whose tensors are exactly the values a f16
+   .ggml file written by sam3_b200.synth stores (same seed, same rounding),
+   and on a seeded 1008x1008 uint8 frame. The script's detector neck
+   ("convs.*") is given the tracker neck weights ("neck.trk.*" in .ggml
+   naming), so its outputs are the engine's neck_trk_0..3.
+2. mem_attn_golden.npz — run_memory_attention() imported from the
+   reference's tests/dump_phase7_reference.py on seeded synthetic tracker
+   weights, current features, memory prompt and prompt PE.
+
+Each dumped tensor is stored as deterministic samples (indices + values)
+plus summary statistics, so the fixtures stay small; tests regenerate the
+same weights from the seeds and compare.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+N_SAMPLES = 4096
+
+VIT_SEED = 2024
+FRAME_SEED = 1000
+MEM_SEED = 77
+MEM_FRAMES = 2
+MEM_PTRS = 2
+
+
+def load_pkg():
+    name = "sam3_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg = os.path.join(ROOT, "sam3.cpp_b200")
+    spec = importlib.util.spec_from_file_location(name, os.path.join(pkg, "__init__.py"),
+                                                  submodule_search_locations=[pkg])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def sample(arr: np.ndarray, key: str, seed: int):
+    flat = np.ascontiguousarray(arr, np.float32).ravel()
+    rng = np.random.default_rng(seed)
+    idx = np.sort(rng.choice(flat.size, size=min(N_SAMPLES, flat.size), replace=False)).astype(np.int64)
+    return {f"{key}__shape": np.array(arr.shape, np.int64), f"{key}__idx": idx, f"{key}__val": flat[idx],
+            f"{key}__stats": np.array([flat.mean(dtype=np.float64), flat.std(dtype=np.float64),
+                                       np.abs(flat).mean(dtype=np.float64), np.abs(flat).max()], np.float64)}
+
+
+def vit_checkpoint(W: dict):
+    """.ggml-named stored values -> the state dict keys dump_vit_reference.py reads."""
+    import torch
+    sd = {}
+    tp = "detector.backbone.vision_backbone.trunk."
+    for k, v in W.items():
+        if k.startswith("vit."):
+            name = k[len("vit."):].replace(".mlp.lin1.", ".mlp.fc1.").replace(".mlp.lin2.", ".mlp.fc2.")
+            t = torch.from_numpy(np.ascontiguousarray(v))
+            if name == "pos_embed":  # [g, g, E] -> [1, 1 + g*g, E] with a (unused) cls slot
+                g, _, E = v.shape
+                t = torch.cat([torch.zeros(1, 1, E), t.reshape(1, g * g, E)], dim=1)
+            elif name.endswith("attn.freqs_cis"):  # [N, 32, 2] (cos, sin) -> complex [N, 32]
+                t = torch.complex(t[..., 0].contiguous(), t[..., 1].contiguous())
+            sd[tp + name] = t
+        elif k.startswith("neck.trk."):
+            sd["detector.backbone.vision_backbone.convs." + k[len("neck.trk."):]] = torch.from_numpy(
+                np.ascontiguousarray(v))
+    return sd
+
+
+def make_vit(reference: str, out_path: str):
+    import torch
+    from PIL import Image
+    s3b = load_pkg()
+    from sam3_b200 import synth
+    cfg = synth.SAM3_VIT_L
+    T = synth.sam3_tensors(cfg, seed=VIT_SEED, ln_random=True)
+    W = synth.stored_values(T, 1, None)
+    frame = synth.frames_u8(1, cfg.img_size, base_seed=FRAME_SEED)[0]
+    with tempfile.TemporaryDirectory() as d:
+        ck = os.path.join(d, "synthetic_sam3.pt")
+        torch.save(vit_checkpoint(W), ck)
+        img = os.path.join(d, "frame.png")
+        Image.fromarray(frame).save(img)
+        outdir = os.path.join(d, "ref")
+        script = os.path.join(reference, "tests", "dump_vit_reference.py")
+        subprocess.run([sys.executable, script, "--checkpoint", ck, "--image", img, "--outdir", outdir],
+                       check=True, cwd=d)
+
+        def load(name):
+            shape = tuple(int(x) for x in open(os.path.join(outdir, name + ".shape")).read().split(","))
+            return np.fromfile(os.path.join(outdir, name + ".bin"), dtype=np.float32).reshape(shape)
+
+        out = {}
+        taps = ["preprocessed", "after_ln_pre", "block_0_out", "block_7_out", "vit_final",
+                "neck_det_0", "neck_det_1", "neck_det_2", "neck_det_3"]
+        for i, name in enumerate(taps):
+            a = load(name)
+            if name.startswith("neck_det_"):
+                a = a[0].transpose(1, 2, 0)  # [1, C, H, W] -> channel-last [H, W, C]
+            elif name == "preprocessed":
+                a = a[0]
+            else:
+                a = a[0]  # [H, W, C]
+            out.update(sample(a, name, 100 + i))
+    meta = {"weights_seed": VIT_SEED, "frame_seed": FRAME_SEED, "ln_random": True, "ftype": 1,
+            "generator": "tests/dump_vit_reference.py main() of the reference, unmodified",
+            "config": "SAM 3 ViT-L 1008^2 (synth.SAM3_VIT_L), tracker neck weights as the script's convs.*"}
+    np.savez_compressed(out_path, meta=json.dumps(meta), **out)
+    print("wrote", out_path)
+
+
+def mem_attn_tracker_weights(T: dict):
+    import torch
+    sd = {}
+    for k, v in T.items():
+        if not k.startswith("mem_attn."):
+            continue
+        name = k.replace("mem_attn.layers.", "transformer.encoder.layers.").replace("mem_attn.norm.",
+                                                                                   "transformer.encoder.norm.")
+        name = name.replace(".sa.", ".self_attn.").replace(".ca.", ".cross_attn_image.")
+        sd[name] = torch.from_numpy(np.ascontiguousarray(v))
+    return sd
+
+
+def mem_inputs(seed: int, H: int = 72):
+    """Seeded current features, memory prompt (MEM_FRAMES spatial slots + MEM_PTRS pointers x 4 tokens)."""
+    sys.path.insert(0, ROOT)
+    from oracle.mem_attn import golden_inputs
+    return golden_inputs({"feat": H, "inputs_seed": seed, "mem_frames": MEM_FRAMES, "ptrs": MEM_PTRS})
+
+
+def make_mem_attn(reference: str, out_path: str):
+    import torch
+    s3b = load_pkg()
+    from sam3_b200 import synth
+    cfg = synth.Sam3Config(depth=1, global_idx=(), with_mem_attn=True)
+    T = synth.sam3_tensors(cfg, seed=MEM_SEED, ln_random=True)
+    W = synth.stored_values({k: v for k, v in T.items() if k.startswith("mem_attn.")}, 1, None)
+    spec = importlib.util.spec_from_file_location("dump_phase7_reference",
+                                                  os.path.join(reference, "tests", "dump_phase7_reference.py"))
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    curr, prompt, prompt_pos, n_ptr = mem_inputs(MEM_SEED + 1)
+    curr_nchw = torch.from_numpy(curr.reshape(72, 72, 256).transpose(2, 0, 1).copy())[None]
+    with torch.no_grad():
+        res = ref.run_memory_attention(mem_attn_tracker_weights(W), curr_nchw,
+                                       torch.from_numpy(prompt)[:, None, :], torch.from_numpy(prompt_pos)[:, None, :],
+                                       n_ptr)
+    out = {}
+    for i, key in enumerate(["input", "layer0_after_sa", "layer0_after_ca", "layer0_after_ffn", "output"]):
+        a = res[key].numpy()  # batch-first [1, N, 256]
+        assert a.shape == (1, 72 * 72, 256), a.shape
+        out.update(sample(a[0], key, 200 + i))
+    meta = {"weights_seed": MEM_SEED, "inputs_seed": MEM_SEED + 1, "mem_frames": MEM_FRAMES, "ptrs": MEM_PTRS,
+            "feat": 72, "generator": "run_memory_attention() of the reference's tests/dump_phase7_reference.py"}
+    np.savez_compressed(out_path, meta=json.dumps(meta), **out)
+    print("wrote", out_path)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of the sam3.cpp checkout (read-only)")
+    ap.add_argument("--only", choices=["vit", "mem_attn"], default=None)
+    a = ap.parse_args()
+    if a.only in (None, "vit"):
+        make_vit(a.reference, os.path.join(HERE, "vit_golden.npz"))
+    if a.only in (None, "mem_attn"):
+        make_mem_attn(a.reference, os.path.join(HERE, "mem_attn_golden.npz"))
+
+
+if __name__ == "__main__":
+    main()
