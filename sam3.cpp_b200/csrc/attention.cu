@@ -55,10 +55,10 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 
 // Loads `rows` x D halves (row stride `ld` elements in global) into a padded
 // shared tile; rows at or beyond `valid_rows` are zero-filled.
-template <int D>
+template <int D, int DR>
 __device__ __forceinline__ void load_tile(__half* s, const __half* g, long long ld, int valid_rows, int tid) {
   constexpr int LD = D + 8;
-  constexpr int CH = D / 8;
+  constexpr int CH = DR / 8;  // only the DR real columns come from global memory
   for (int i = tid; i < kBKV * CH; i += 128) {
     const int r = i / CH, c = i - r * CH;
     const bool ok = r < valid_rows;
@@ -66,7 +66,10 @@ __device__ __forceinline__ void load_tile(__half* s, const __half* g, long long 
   }
 }
 
-template <int D>
+// D: compute head dim (multiple of 16); DR: real head dim (multiple of 8). For
+// DR < D (Hiera-L's 72 -> 80) the pad columns stay zero in shared memory, which
+// leaves q.k unchanged and gives zero output columns that are not stored.
+template <int D, int DR>
 __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
   constexpr int LD = D + 8;
   constexpr int NT = D / 8;  // n-tiles of the output
@@ -83,9 +86,16 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
   const __half* Kg = p.k + (long long)b * p.k_b + (long long)h * p.k_h;
   const __half* Vg = p.v + (long long)b * p.v_b + (long long)h * p.v_h;
 
-  load_tile<D>(sQ, Qg, p.q_n, p.nq - q0, tid);
-  load_tile<D>(sK, Kg, p.k_n, p.nk, tid);
-  load_tile<D>(sV, Vg, p.v_n, p.nk, tid);
+  if constexpr (DR < D) {
+    constexpr int PADC = (DR < D) ? D - DR : 1;
+    for (int i = tid; i < (kBQ + 4 * kBKV) * PADC; i += 128) {
+      const int r = i / PADC, c = DR + i % PADC;
+      sQ[r * LD + c] = __float2half_rn(0.f);
+    }
+  }
+  load_tile<D, DR>(sQ, Qg, p.q_n, p.nq - q0, tid);
+  load_tile<D, DR>(sK, Kg, p.k_n, p.nk, tid);
+  load_tile<D, DR>(sV, Vg, p.v_n, p.nk, tid);
   cp_async_commit();
 
   float o[NT][4];
@@ -102,8 +112,8 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
     const int buf = j & 1;
     if (j + 1 < nkt) {
       const int nb = buf ^ 1;
-      load_tile<D>(sK + nb * kBKV * LD, Kg + (long long)(j + 1) * kBKV * p.k_n, p.k_n, p.nk - (j + 1) * kBKV, tid);
-      load_tile<D>(sV + nb * kBKV * LD, Vg + (long long)(j + 1) * kBKV * p.v_n, p.v_n, p.nk - (j + 1) * kBKV, tid);
+      load_tile<D, DR>(sK + nb * kBKV * LD, Kg + (long long)(j + 1) * kBKV * p.k_n, p.k_n, p.nk - (j + 1) * kBKV, tid);
+      load_tile<D, DR>(sV + nb * kBKV * LD, Vg + (long long)(j + 1) * kBKV * p.v_n, p.v_n, p.nk - (j + 1) * kBKV, tid);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -205,10 +215,11 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
   const int r0 = q0 + warp * 16 + g, r1 = r0 + 8;
   const long long orow0 = r0 < p.nq ? map_row(p.omap, (long long)b * p.nq + r0) : -1;
   const long long orow1 = r1 < p.nq ? map_row(p.omap, (long long)b * p.nq + r1) : -1;
-  __half* ob = p.o + (long long)h * D;
+  __half* ob = p.o + (long long)h * DR;
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
     const int c = n * 8 + 2 * t4;
+    if (c >= DR) continue;
     if (orow0 >= 0)
       *reinterpret_cast<__half2*>(ob + orow0 * p.o_n + c) = __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
     if (orow1 >= 0)
@@ -216,18 +227,18 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
   }
 }
 
-template <int D>
+template <int D, int DR>
 int launch_attn(const AttnParams& p, int batch_heads, cudaStream_t st) {
   constexpr size_t smem = (size_t)(kBQ + 4 * kBKV) * (D + 8) * 2;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(attn_fwd_kernel<D, DR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
       return -13;
     attr = true;
   }
   dim3 grid((p.nq + kBQ - 1) / kBQ, batch_heads);
-  attn_fwd_kernel<D><<<grid, 128, smem, st>>>(p);
+  attn_fwd_kernel<D, DR><<<grid, 128, smem, st>>>(p);
   return launch_status("attention");
 }
 
@@ -239,11 +250,12 @@ int attention(const AttnParams& p, int D, int batch_heads, cudaStream_t st) {
       (p.k_h % 8) || (p.v_h % 8) || (p.o_n % 2))
     return -2;
   switch (D) {
-    case 64: return launch_attn<64>(p, batch_heads, st);
-    case 80: return launch_attn<80>(p, batch_heads, st);
-    case 96: return launch_attn<96>(p, batch_heads, st);
-    case 128: return launch_attn<128>(p, batch_heads, st);
-    case 256: return launch_attn<256>(p, batch_heads, st);
+    case 64: return launch_attn<64, 64>(p, batch_heads, st);
+    case 72: return launch_attn<80, 72>(p, batch_heads, st);
+    case 80: return launch_attn<80, 80>(p, batch_heads, st);
+    case 96: return launch_attn<96, 96>(p, batch_heads, st);
+    case 128: return launch_attn<128, 128>(p, batch_heads, st);
+    case 256: return launch_attn<256, 256>(p, batch_heads, st);
     default: return -3;
   }
 }

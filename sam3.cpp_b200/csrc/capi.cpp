@@ -83,7 +83,14 @@ int resolve_output(s3b_ctx* ctx, const char* name, OutRef& r) {
   const HParams& hp = ctx->model.hp;
   std::string n(name ? name : "");
   if (O.n_frames <= 0) return set_error(ctx, kErrState, "no encode has run");
-  if (n == "vit_output" && O.backbone && !hp.is_sam2) {
+  if (n == "backbone" && O.backbone && hp.is_sam2 && O.backbone_c > 0) {
+    r.dev = O.backbone->as<float>();
+    r.ne[0] = O.backbone_c;
+    r.ne[1] = r.ne[2] = O.backbone_s;
+    r.frame_elems = (int64_t)O.backbone_s * O.backbone_s * O.backbone_c;
+    return kOk;
+  }
+  if ((n == "vit_output" || n == "backbone") && O.backbone && !hp.is_sam2) {
     const int G = hp.n_img_embd();
     r.dev = O.backbone->as<float>();
     r.ne[0] = hp.vit_embed_dim;

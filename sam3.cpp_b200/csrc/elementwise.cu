@@ -149,20 +149,33 @@ __global__ void maxpool2_cl_kernel(const T* __restrict__ x, int B, int H, int W,
   }
 }
 
-__global__ void qpool_kernel(const __half* __restrict__ q, long long nbh, int ws, int D, __half* __restrict__ out) {
+// 2x2 max pool of the (ws x ws) token grid of each window; 8 channels per thread.
+__global__ void qpool_kernel(const __half* __restrict__ q, long long ld, long long nwin, int ws, int C,
+                             __half* __restrict__ out) {
   const int wo = ws / 2;
-  const long long total = nbh * wo * wo * D;
+  const int c8n = C / 8;
+  const long long total = nwin * wo * wo * c8n;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int d = (int)(i % D);
-    const long long t = i / D;
+    const int c8 = (int)(i % c8n);
+    const long long t = i / c8n;
     const int l = (int)(t % (wo * wo));
-    const long long bh = t / (wo * wo);
+    const long long w = t / (wo * wo);
     const int oy = l / wo, ox = l - (l / wo) * wo;
-    const __half* p = q + bh * ws * ws * D;
-    const int i00 = (2 * oy) * ws + 2 * ox;
-    __half m = __hmax(__hmax(p[(long long)i00 * D + d], p[(long long)(i00 + 1) * D + d]),
-                      __hmax(p[(long long)(i00 + ws) * D + d], p[(long long)(i00 + ws + 1) * D + d]));
-    out[i] = m;
+    const long long r00 = w * ws * ws + (long long)(2 * oy) * ws + 2 * ox;
+    const __half* p = q + c8 * 8;
+    const uint4 a = *reinterpret_cast<const uint4*>(p + r00 * ld);
+    const uint4 b = *reinterpret_cast<const uint4*>(p + (r00 + 1) * ld);
+    const uint4 c = *reinterpret_cast<const uint4*>(p + (r00 + ws) * ld);
+    const uint4 d = *reinterpret_cast<const uint4*>(p + (r00 + ws + 1) * ld);
+    const __half2* ha = reinterpret_cast<const __half2*>(&a);
+    const __half2* hb = reinterpret_cast<const __half2*>(&b);
+    const __half2* hc = reinterpret_cast<const __half2*>(&c);
+    const __half2* hd = reinterpret_cast<const __half2*>(&d);
+    uint4 o;
+    __half2* ho = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ho[e] = __hmax2(__hmax2(ha[e], hb[e]), __hmax2(hc[e], hd[e]));
+    *reinterpret_cast<uint4*>(out + t * C + c8 * 8) = o;
   }
 }
 
@@ -291,9 +304,10 @@ int maxpool2_cl_f32(const float* x, int B, int H, int W, int C, float* y, cudaSt
   return launch_ok();
 }
 
-int qpool_windows(const __half* q, long long nbh, int ws, int D, __half* out, cudaStream_t st) {
-  const long long n = nbh * (ws / 2) * (ws / 2) * D;
-  qpool_kernel<<<grid_for(n, 256), 256, 0, st>>>(q, nbh, ws, D, out);
+int qpool_windows(const __half* q, long long ld, long long nwin, int ws, int C, __half* out, cudaStream_t st) {
+  if (C % 8 || ld % 8) return -1;
+  const long long n = nwin * (ws / 2) * (ws / 2) * (C / 8);
+  qpool_kernel<<<grid_for(n, 256), 256, 0, st>>>(q, ld, nwin, ws, C, out);
   return launch_ok();
 }
 

@@ -168,6 +168,8 @@ struct Model {
   // SAM 2 Hiera
   Linear hpatch;                     // [E0][Kpad=152]
   std::vector<float> pos_bkg, pos_win;  // host copies (CHW) for the PE
+  std::shared_ptr<DevBuf> hiera_pe;     // f32 [S][S][E0], S = img_size / 4 (computed at load)
+  int hiera_pe_size = 0;
   std::vector<HieraBlock> hiera;
   int stage_ends[4] = {0, 0, 0, 0};
   Linear fpn[4];
@@ -184,7 +186,8 @@ struct Model {
 struct Outputs {
   int n_frames = 0;
   int img_size = 0;
-  std::shared_ptr<DevBuf> backbone;  // ViT output [F][72][72][1024] or null
+  std::shared_ptr<DevBuf> backbone;  // ViT output [F][72][72][1024], or the Hiera state (stage runner)
+  int backbone_c = 0, backbone_s = 0;  // Hiera stage-runner state: channels, spatial size
   std::shared_ptr<DevBuf> fpn[4];    // neck_trk / fpn levels [F][S][S][256]
   int fpn_size[4] = {0, 0, 0, 0};
   int n_fpn = 0;

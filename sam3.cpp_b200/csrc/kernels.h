@@ -110,8 +110,9 @@ int im2col_3x3_cl(const __half* x, int B, int H, int W, int C, __half* out, cuda
 int maxpool2_cl_f16(const __half* x, int B, int H, int W, int C, __half* y, cudaStream_t st);
 int maxpool2_cl_f32(const float* x, int B, int H, int W, int C, float* y, cudaStream_t st);
 
-// Q pooling inside windows: q [nwin*heads][ws*ws][D] -> [nwin*heads][(ws/2)^2][D].
-int qpool_windows(const __half* q, long long nbh, int ws, int D, __half* out, cudaStream_t st);
+// Q pooling inside windows (sam3.cpp:4363-4371): rows w*ws*ws + (y*ws + x) of
+// q (row stride ld elements, C channels) -> out [nwin][(ws/2)^2][C] contiguous.
+int qpool_windows(const __half* q, long long ld, long long nwin, int ws, int C, __half* out, cudaStream_t st);
 
 // uint8 HWC frames -> f32 CHW normalised ((p/255 - mean)/std).
 int preprocess_u8(const uint8_t* img, int B, int H, int W, const float mean[3], const float stdv[3], float* out,

@@ -12,6 +12,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <fstream>
 
 #include "engine.h"
@@ -548,6 +549,44 @@ static int load_sam3(s3b_ctx* ctx, const Index& idx) {
 // Per-block Hiera metadata (sam2_precompute_hiera_metadata, sam3.cpp:1676-1742):
 // stage dims double at stage starts, q-stride on the first block of stages
 // 1..q_pool, and the window size "lags" one block at stage transitions.
+// Keys cubic convolution (a = -0.75), half-pixel centres, clamped taps: the
+// resampling of sam2_bicubic_interpolate_cpu (sam3.cpp:4072-4109).
+static float cubic_w(float x) {
+  x = fabsf(x);
+  if (x < 1.0f) return (1.25f * x - 2.25f) * x * x + 1.0f;
+  if (x < 2.0f) return ((-0.75f * x + 3.75f) * x - 6.0f) * x + 3.0f;
+  return 0.0f;
+}
+
+// Hiera PE (sam2_compute_pos_embed, sam3.cpp:4114-4171): background PE
+// [E][bh][bw] resized to S x S plus the window PE [E][ws][ws] tiled, written
+// channel-last [S][S][E].
+void hiera_pos_embed(const std::vector<float>& bkg, int bh, int bw, const std::vector<float>& win, int ws, int E,
+                     int S, std::vector<float>& pe) {
+  pe.assign((size_t)S * S * E, 0.f);
+  for (int y = 0; y < S; ++y) {
+    const float fy = ((float)y + 0.5f) * (float)bh / (float)S - 0.5f;
+    const int iy = (int)floorf(fy);
+    const float dy = fy - iy;
+    for (int x = 0; x < S; ++x) {
+      const float fx = ((float)x + 0.5f) * (float)bw / (float)S - 0.5f;
+      const int ix = (int)floorf(fx);
+      const float dx = fx - ix;
+      float* dst = &pe[((size_t)y * S + x) * E];
+      for (int jj = -1; jj <= 2; ++jj) {
+        const float wy = cubic_w(dy - jj);
+        const int sy = std::min(std::max(iy + jj, 0), bh - 1);
+        for (int ii = -1; ii <= 2; ++ii) {
+          const float wx = cubic_w(dx - ii);
+          const int sx = std::min(std::max(ix + ii, 0), bw - 1);
+          for (int e = 0; e < E; ++e) dst[e] += wy * wx * bkg[((size_t)e * bh + sy) * bw + sx];
+        }
+      }
+      for (int e = 0; e < E; ++e) dst[e] += win[((size_t)e * ws + (y % ws)) * ws + (x % ws)];
+    }
+  }
+}
+
 static void hiera_metadata(Model& M) {
   const HParams& hp = M.hp;
   int total = 0;
@@ -599,6 +638,14 @@ static int load_sam2(s3b_ctx* ctx, const Index& idx) {
     NEED(pw, "hiera.pos_embed_window");
     tensor_to_f32(*pb, M.pos_bkg);
     tensor_to_f32(*pw, M.pos_win);
+    // The PE is the same for every frame of a given size: computed once here
+    // instead of per frame (sam3.cpp:5928-5934 recomputes it on the host each frame).
+    const int E0 = hp.hiera_embed_dim, S = hp.img_size / 4;
+    std::vector<float> pe;
+    hiera_pos_embed(M.pos_bkg, (int)pb->ne[1], (int)pb->ne[0], M.pos_win, (int)pw->ne[0], E0, S, pe);
+    M.hiera_pe = upload_bytes(ctx, pe.data(), pe.size() * 4, &rc);
+    if (rc) return rc;
+    M.hiera_pe_size = S;
   }
   for (size_t i = 0; i < M.hiera.size(); ++i) {
     HieraBlock& B = M.hiera[i];

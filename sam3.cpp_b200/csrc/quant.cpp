@@ -16,8 +16,10 @@
 namespace s3b {
 
 static uint16_t f2h(float f) {
-  __half h = __float2half_rn(f);
-  return reinterpret_cast<__half_raw&>(h).x;
+  const __half h = __float2half_rn(f);
+  uint16_t u;
+  memcpy(&u, &h, 2);
+  return u;
 }
 
 void quantize_row_host(int type, const float* x, int64_t n, uint8_t* dst) {

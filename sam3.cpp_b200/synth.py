@@ -70,6 +70,100 @@ class Sam3Config:
 SAM3_VIT_L = Sam3Config()
 
 
+@dataclass
+class Sam2Config:
+    """SAM 2 / 2.1 Hiera image encoder + FPN neck (+ optional memory attention)."""
+    img_size: int = 1024
+    embed: int = 96
+    heads: int = 1
+    stages: tuple = (1, 2, 7, 2)
+    global_idx: tuple = (5, 7, 9)
+    q_pool: int = 3
+    window_spec: tuple = (8, 4, 14, 7)
+    bkg: tuple = (7, 7)
+    scalp: int = 1
+    neck_dim: int = 256
+    fpn_top_down_levels: tuple = (2, 3)
+    with_mem_attn: bool = False
+    mem_out_dim: int = 64
+    mem_attn_layers: int = 4
+    num_maskmem: int = 7
+    max_obj_ptrs: int = 16
+    mem_ffn: int = 2048
+
+    def hparams(self) -> list[int]:
+        # sam2_load_hparams order (sam3.cpp:1564-1626), 57 fields for the Hiera backbone
+        g = list(self.global_idx) + [0] * (8 - len(self.global_idx))
+        td = list(self.fpn_top_down_levels) + [0] * (4 - len(self.fpn_top_down_levels))
+        hp = [self.img_size, 1, self.embed, self.heads, len(self.stages), *self.stages, len(self.global_idx), *g,
+              self.q_pool, *self.window_spec, self.bkg[0], self.bkg[1], self.scalp, self.neck_dim,
+              len(self.fpn_top_down_levels), *td]
+        hp += [256, 2, 3, 3]                                       # sam decoder
+        hp += [self.mem_out_dim, self.mem_attn_layers, self.num_maskmem, self.max_obj_ptrs]
+        hp += [2000, -1000]                                        # sigmoid scale / bias x100
+        hp += [1, 1, 1, 1, 1, 1, 0, 1, 0, 1, 1, 1, 1, 1, 1]        # tracking flags, is_sam2_1 = 1
+        return hp
+
+    def blocks(self):
+        """Per-block (dim_in, dim_out, heads, window, q_stride) following sam3.cpp:1676-1742."""
+        ends, cum = [], 0
+        for s in self.stages:
+            cum += s
+            ends.append(cum - 1)
+        qpool_blocks = [ends[s] + 1 for s in range(len(self.stages) - 1)][:self.q_pool]
+        out, cur, embed, heads = [], 0, self.embed, self.heads
+        for i in range(sum(self.stages)):
+            ws = 0 if i in self.global_idx else self.window_spec[cur]
+            dout = embed
+            if i > 0 and i - 1 == ends[cur]:
+                dout = embed * 2
+                heads *= 2
+                cur += 1
+            out.append((embed, dout, heads, ws, i in qpool_blocks))
+            embed = dout
+        return out
+
+    def stage_dims(self):
+        return [self.embed * (2 ** s) for s in range(len(self.stages))]
+
+
+HIERA_T = Sam2Config()
+HIERA_L = Sam2Config(embed=144, heads=2, stages=(2, 6, 36, 4), global_idx=(23, 33, 43), window_spec=(8, 4, 16, 8))
+
+
+def sam2_tensors(cfg: Sam2Config, seed: int = 0, ln_random: bool = False) -> dict:
+    """name -> f32 array (PyTorch shape) of a SAM 2.1 Hiera image encoder + FPN neck."""
+    g = _Gen(seed, ln_random)
+    E0 = cfg.embed
+    T: dict[str, np.ndarray] = {}
+    T["hiera.patch_embed.weight"] = g.w(E0, 3, 7, 7)
+    T["hiera.patch_embed.bias"] = g.w(E0)
+    T["hiera.pos_embed"] = g.w(1, E0, cfg.bkg[0], cfg.bkg[1])
+    T["hiera.pos_embed_window"] = g.w(1, E0, cfg.window_spec[0], cfg.window_spec[0])
+    for i, (din, dout, heads, ws, qs) in enumerate(cfg.blocks()):
+        p = f"hiera.blocks.{i}"
+        T[f"{p}.norm1.weight"], T[f"{p}.norm1.bias"] = g.ln(din)
+        T[f"{p}.attn.qkv.weight"] = g.w(3 * dout, din)
+        T[f"{p}.attn.qkv.bias"] = g.w(3 * dout)
+        T[f"{p}.attn.proj.weight"] = g.w(dout, dout)
+        T[f"{p}.attn.proj.bias"] = g.w(dout)
+        T[f"{p}.norm2.weight"], T[f"{p}.norm2.bias"] = g.ln(dout)
+        T[f"{p}.mlp.fc1.weight"] = g.w(4 * dout, dout)
+        T[f"{p}.mlp.fc1.bias"] = g.w(4 * dout)
+        T[f"{p}.mlp.fc2.weight"] = g.w(dout, 4 * dout)
+        T[f"{p}.mlp.fc2.bias"] = g.w(dout)
+        if din != dout:
+            T[f"{p}.proj.weight"] = g.w(dout, din)
+            T[f"{p}.proj.bias"] = g.w(dout)
+    dims = cfg.stage_dims()
+    for i in range(4):
+        T[f"fpn.convs.{i}.weight"] = g.w(cfg.neck_dim, dims[3 - i], 1, 1)
+        T[f"fpn.convs.{i}.bias"] = g.w(cfg.neck_dim)
+    if cfg.with_mem_attn:
+        _mem_attn(g, T, cfg.neck_dim, cfg.mem_out_dim, cfg.mem_attn_layers, cfg.mem_ffn, cfg.num_maskmem)
+    return T
+
+
 # ---------------------------------------------------------------- RoPE / PE
 def axial_cis(dim: int, end_x: int, end_y: int, theta: float = 10000.0, scale: float = 1.0) -> np.ndarray:
     """compute_axial_cis as (cos, sin) pairs: [end_x*end_y, dim//2, 2] f32."""
@@ -225,6 +319,13 @@ def write_sam3(path: str, cfg: Sam3Config, seed: int = 0, ftype: int = 1, qtype:
                quantize=None, ln_random: bool = False, neck_det: bool = False) -> dict:
     T = sam3_tensors(cfg, seed, ln_random=ln_random, neck_det=neck_det)
     write_model(path, T, cfg.hparams(), ggml_io.MAGIC_SAM3, 3, ftype, qtype, quantize)
+    return T
+
+
+def write_sam2(path: str, cfg: Sam2Config, seed: int = 0, ftype: int = 1, qtype: int | None = None,
+               quantize=None, ln_random: bool = False) -> dict:
+    T = sam2_tensors(cfg, seed, ln_random=ln_random)
+    write_model(path, T, cfg.hparams(), ggml_io.MAGIC_SAM2, 1, ftype, qtype, quantize)
     return T
 
 

@@ -1,0 +1,96 @@
+"""SAM 2 / 2.1 Hiera encoder: oracle checks on CPU and the B200 engine against
+the oracle on GPU (through the C ABI).
+
+The SAM 2 reference dump (tests/dump_sam2_reference.py) needs the external
+sam2 package, so the Hiera oracle is pinned component-wise: its bicubic PE
+resampling against PyTorch's bicubic (the op the reference's C++ bicubic
+reproduces, sam3.cpp:4070-4109), and through the shared building blocks that
+the ViT / memory-attention fixtures pin."""
+import numpy as np
+import pytest
+
+from oracle import hiera as oh
+from oracle import quant as oq
+from parity import assert_close
+
+
+def test_oracle_bicubic_matches_torch():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(0)
+    src = rng.standard_normal((16, 7, 7)).astype(np.float32)
+    for H, W in ((256, 256), (64, 64), (37, 50)):
+        ref = torch.nn.functional.interpolate(torch.from_numpy(src)[None], size=(H, W), mode="bicubic",
+                                              align_corners=False)[0].numpy()
+        np.testing.assert_allclose(oh.bicubic(src, H, W), ref, rtol=1e-5, atol=1e-5)
+
+
+def test_hiera_block_metadata(s3b):
+    """Per-block dims / heads / windows / q-stride of Hiera-T (sam3.cpp:1676-1742)."""
+    from sam3_b200 import synth
+    b = synth.HIERA_T.blocks()
+    assert [x[3] for x in b] == [8, 8, 4, 4, 14, 0, 14, 0, 14, 0, 14, 7]
+    assert [i for i, x in enumerate(b) if x[4]] == [1, 3, 10]
+    assert [x[1] for x in b] == [96, 192, 192, 384, 384, 384, 384, 384, 384, 384, 768, 768]
+
+
+def small_cfgs(synth):
+    return {
+        # hd 96, padded windows at stage 2 (16 -> 28), q-stride with padded unpartition at block 5, one global block
+        "t": synth.Sam2Config(img_size=256, embed=96, heads=1, stages=(1, 2, 2, 1), global_idx=(4,),
+                              window_spec=(8, 4, 14, 7)),
+        # Hiera-L-like head dim 72
+        "l": synth.Sam2Config(img_size=256, embed=144, heads=2, stages=(1, 2, 2, 1), global_idx=(3,),
+                              window_spec=(8, 4, 16, 8)),
+    }
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,qtype", [("t", None), ("t", 2), ("l", 8)])
+def test_hiera_small_vs_oracle(engine, s3b, tmp_path, name, qtype):
+    from sam3_b200 import synth
+    cfg = small_cfgs(synth)[name]
+    path = str(tmp_path / "h.ggml")
+    T = synth.write_sam2(path, cfg, seed=4, ftype=1, qtype=qtype, quantize=s3b.quantize_rows, ln_random=True)
+    W = synth.stored_values(T, 1, qtype, oq.quantize, oq.dequantize)
+    engine.load_model(path)
+    frames = synth.frames_u8(2, cfg.img_size, base_seed=31)
+    chw = oh.preprocess_u8(frames)
+    stages = oh.backbone(W, chw, cfg)
+    fpn = oh.fpn(W, stages, cfg)
+    engine.encode_u8(frames)
+    for f in range(2):
+        for i in range(3):
+            got = engine.output(f"neck_trk_{i}", f)
+            assert got.shape == fpn[i][f].shape, (got.shape, fpn[i][f].shape)
+            assert_close(got, fpn[i][f], 0.9999, 0.01, 0.05, f"{name} fpn {i} frame {f}")
+    # backbone state after every block (stage runner)
+    ends = np.cumsum(cfg.stages) - 1
+    for nb in range(1, sum(cfg.stages) + 1):
+        if nb - 1 not in ends:
+            continue
+        engine.set_option("stop_after_blocks", nb)
+        try:
+            engine.encode_u8(frames[:1])
+            got = engine.output("backbone", 0)
+        finally:
+            engine.set_option("stop_after_blocks", -1)
+        ref = stages[list(ends).index(nb - 1)][0]
+        assert_close(got, ref, 0.9999, 0.01, 0.05, f"{name} stage after block {nb - 1}")
+
+
+@pytest.mark.gpu
+def test_hiera_t_full_vs_oracle(engine, s3b, tmp_path):
+    """SAM 2.1 Hiera-Tiny at 1024^2 (BASELINE configs[0] shape), f16 weights, one frame."""
+    from sam3_b200 import synth
+    cfg = synth.HIERA_T
+    path = str(tmp_path / "hiera_t.ggml")
+    T = synth.write_sam2(path, cfg, seed=0, ftype=1, ln_random=True)
+    W = synth.stored_values(T, 1, None)
+    engine.load_model(path)
+    frames = synth.frames_u8(1, 1024, base_seed=1000)
+    engine.encode_u8(frames)
+    fpn = oh.fpn(W, oh.backbone(W, oh.preprocess_u8(frames), cfg), cfg)
+    for i in range(3):
+        got = engine.output(f"neck_trk_{i}", 0)
+        assert got.shape == (256 >> i, 256 >> i, 256)
+        print(assert_close(got, fpn[i][0], 0.9999, 0.01, 0.05, f"hiera-t fpn {i}"))
