@@ -63,6 +63,8 @@ int s3b_reset_stream(s3b_ctx* ctx);
 /* Waits for all work of the context and checks the device error word. */
 int s3b_sync(s3b_ctx* ctx);
 /* Options: "frames_per_pass" (encoder micro-batch, default 8);
+ * "attention_impl" (0: tcgen05 flash attention where eligible, 1: always the
+ * mma.sync kernel);
  * "stop_after_blocks" (test hook: run only the first n backbone blocks and
  * no neck, -1 = all; the stage runners of sam3.h:441-496 play this role in
  * the reference). */
@@ -163,6 +165,15 @@ int s3b_op_gemm_rope(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, in
  * 9267, 9312) with no mask. d in {64, 80, 96, 128, 256}. */
 int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, void* out, int batch, int heads,
                      int nq, int nk, int d, float scale);
+
+/* Attention over a fused qkv buffer, the layout the ViT blocks use:
+ * q / k / v of head h of window w at qkv[(w*ntok + n)*ld + {0, E, 2E} + h*d]
+ * with E = heads*d (ld >= 3E), nq = nk = ntok; out [nwin*ntok][ld_out] f16 at
+ * columns h*d. d = 64 runs the tcgen05 kernel (unless the context option
+ * "attention_impl" is 1), other d the mma.sync kernel. Replaces the
+ * qkv split + permute + ggml_flash_attn_ext of sam3.cpp:3738-3774. */
+int s3b_op_attention_qkv(s3b_ctx* ctx, const void* qkv, int64_t ld, void* out, int64_t ld_out, int nwin, int heads,
+                         int ntok, int d, float scale);
 
 /* LayerNorm over C of f32 rows: out = (x-mean)/sqrt(var+eps)*g + b, f16 or
  * f32 out. Replaces ggml_norm + mul + add (sam3.cpp:1036-1060). */

@@ -61,6 +61,7 @@ SYMBOLS = [
     ("s3b_op_gemm", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _I, _P, _I, _I64, _P, _I64]),
     ("s3b_op_gemm_rope", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _I, _I, _I64, _P, _I, _I64]),
     ("s3b_op_attention", _I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F]),
+    ("s3b_op_attention_qkv", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _I, _F]),
     ("s3b_op_layernorm", _I, [_P, _P, _P, _I, _I64, _I, _P, _P, _F]),
     ("s3b_op_conv3x3", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),
     ("s3b_conv3x3_noalloc", _I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _P]),
@@ -311,6 +312,12 @@ class Engine:
         rc = self._L.s3b_op_attention(self.h, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, H, nq,
                                       nk, d, scale)
         self._check(rc, "s3b_op_attention")
+
+    def attention_qkv(self, qkv, out, nwin: int, heads: int, ntok: int, d: int, scale: float):
+        """qkv f16 [nwin*ntok][ld] (q | k | v, heads*d each), out f16 [nwin*ntok][ld_out]."""
+        rc = self._L.s3b_op_attention_qkv(self.h, qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), nwin,
+                                          heads, ntok, d, scale)
+        self._check(rc, "s3b_op_attention_qkv")
 
     def layernorm(self, x, out, g, b, eps: float):
         rows, C = x.shape

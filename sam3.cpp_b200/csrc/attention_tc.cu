@@ -1,0 +1,382 @@
+// Tensor-core (tcgen05 / TMEM / TMA) flash attention for head dim 64: the
+// ViT windowed and global attention of sam3_vit_block_forward
+// (ggml_flash_attn_ext at sam3.cpp:3774; softmax(q k^T / 8) v, no mask).
+//
+// One CTA = one 128-query tile of one (window, head); 6 warps, 2 CTAs / SM:
+//   warp 0     TMA: Q tile once, then K_j, V_j through a 3-slot ring. The
+//              tensor map is 3-D (channels, token, window) over the fused
+//              [tokens][3E] qkv buffer, so a tile never reads another window
+//              (rows past the window are zero-filled by TMA).
+//   warp 1     MMA: S = Q K_j^T (M=128, N=128, K=64) into TMEM; after the
+//              softmax wrote P_j: O_j = P_j V_j (M=128, N=64, K=128, V as an
+//              MN-major operand) into one of two TMEM O buffers.
+//   warps 2-5  softmax, one query row per thread (TMEM lane): two passes over
+//              the S row (max, then exp2 / sum / f16 P into 128B-swizzled
+//              shared memory), and the running output kept in registers:
+//              acc = acc * 2^(m_old - m_new) + O_j.
+// Every wait is bounded; a timeout records an error code and unwinds.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace s3b {
+namespace {
+
+constexpr int kD = 64;
+constexpr int kBQ = 128;
+constexpr int kBK = 128;
+constexpr int kSlots = 3;
+constexpr uint32_t kTileBytes = kBK * kD * 2;  // 16 KB: 128 rows x 128 B
+constexpr uint32_t kPBytes = kBQ * kBK * 2;    // 32 KB: two 128 x 64 swizzled halves
+constexpr int kThreads = 192;
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
+}
+
+// MN-major, 128B-swizzled operand (rows of 64 f16 along N, consecutive rows
+// along K): SBO = 1024 B between 8-row groups, LBO = stride between 64-wide N
+// atoms (a single atom here).
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(kTileBytes >> 4) << 16;  // LBO (unused: N == 64)
+  d |= (uint64_t)(1024u >> 4) << 32;       // SBO
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+#define TMEM_LD32(taddr, R)                                                                                  \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "                                                     \
+               "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"                                     \
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                    \
+               : "=r"(R[0]), "=r"(R[1]), "=r"(R[2]), "=r"(R[3]), "=r"(R[4]), "=r"(R[5]), "=r"(R[6]),         \
+                 "=r"(R[7]), "=r"(R[8]), "=r"(R[9]), "=r"(R[10]), "=r"(R[11]), "=r"(R[12]), "=r"(R[13]),     \
+                 "=r"(R[14]), "=r"(R[15]), "=r"(R[16]), "=r"(R[17]), "=r"(R[18]), "=r"(R[19]), "=r"(R[20]),  \
+                 "=r"(R[21]), "=r"(R[22]), "=r"(R[23]), "=r"(R[24]), "=r"(R[25]), "=r"(R[26]), "=r"(R[27]),  \
+                 "=r"(R[28]), "=r"(R[29]), "=r"(R[30]), "=r"(R[31])                                          \
+               : "r"(taddr))
+
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitNs) {
+      if (err) atomicCAS(err, 0, kErrWaitDrain);
+      return;
+    }
+  }
+}
+
+struct TcAttnArgs {
+  int heads, ntok, nwin;
+  int q_col, k_col, v_col;  // column offsets (elements) of q / k / v of head 0 in a row
+  __half* o;
+  long long o_n;
+  RowMap omap;
+  float sl2;  // softmax scale * log2(e)
+};
+
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tm, TcAttnArgs a, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sQ = smem;                          // 16 KB
+  uint8_t* sKV = sQ + kTileBytes;              // kSlots x 16 KB
+  uint8_t* sP = sKV + kSlots * kTileBytes;     // 32 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;                // [kSlots]
+  uint64_t* kv_empty = kv_full + kSlots;       // [kSlots]
+  uint64_t* s_full = kv_empty + kSlots;
+  uint64_t* s_empty = s_full + 1;
+  uint64_t* p_full = s_empty + 1;
+  uint64_t* p_empty = p_full + 1;
+  uint64_t* o_full = p_empty + 1;              // [2]
+  uint64_t* o_empty = o_full + 2;              // [2]
+  uint64_t* mma_done = o_empty + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int w = bh / a.heads, h = bh - w * a.heads;
+  const int nkb = (a.ntok + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 4);
+    mbar_init(p_full, 4);
+    mbar_init(p_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&o_full[b], 1);
+      mbar_init(&o_empty[b], 4);
+    }
+    mbar_init(mma_done, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    tma_prefetch_desc(&tm);
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, 256);  // S: columns [0,128), O buffers: [128,192), [192,256)
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // Q once, then K_0, V_0, K_1, V_1, ... through the ring
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_3d(&tm, q_full, sQ, a.q_col + h * kD, qb * kBQ, w);
+      uint32_t armed = 0, armed_phase = 0;
+      bool ok = true;
+      for (int t = 0; t < 2 * nkb && ok; ++t) {
+        const int s = t % kSlots;
+        const uint32_t use = (uint32_t)(t / kSlots);
+        if (!mbar_wait(&kv_empty[s], (use & 1) ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
+        mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
+        const int j = t >> 1;
+        const int col = ((t & 1) ? a.v_col : a.k_col) + h * kD;
+        tma_load_3d(&tm, &kv_full[s], sKV + s * kTileBytes, col, j * kBK, w);
+        armed |= 1u << s;
+        armed_phase = (armed_phase & ~(1u << s)) | ((use & 1) << s);
+      }
+      mbar_wait_drain(q_full, 0, err);
+      for (int s = 0; s < kSlots; ++s)
+        if (armed & (1u << s)) mbar_wait_drain(&kv_full[s], (armed_phase >> s) & 1u, err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16(kBQ, kBK, 0);                    // both K-major
+      constexpr uint32_t idesc_o = idesc_f16(kBQ, kD, 0) | (1u << 16);        // B (V) MN-major
+      bool ok = mbar_wait(q_full, 0, s_abort, err, kErrWaitFull);
+      tc_fence_after();
+      const uint64_t dq = sdesc_k_sw128(smem_u32(sQ));
+      bool issued = false;
+      // S_0
+      auto issue_s = [&](int j) -> bool {
+        const int t = 2 * j, s = t % kSlots;
+        if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) return false;
+        if (j > 0 && !mbar_wait(s_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc)) return false;
+        tc_fence_after();
+        const uint64_t dk = sdesc_k_sw128(smem_u32(sKV + s * kTileBytes));
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) tc_mma_f16(tmem, dq + (uint64_t)(kk * 2), dk + (uint64_t)(kk * 2), idesc_s, kk != 0);
+        tc_commit(s_full);
+        tc_commit(&kv_empty[s]);
+        issued = true;
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < nkb && ok; ++j) {
+        if (j + 1 < nkb && !issue_s(j + 1)) break;
+        // O_j = P_j V_j
+        const int t = 2 * j + 1, s = t % kSlots, ob = j & 1;
+        if (!mbar_wait(p_full, (uint32_t)j & 1, s_abort, err, kErrWaitMisc)) break;
+        if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) break;
+        if (j >= 2 && !mbar_wait(&o_empty[ob], (uint32_t)((j - 2) >> 1) & 1, s_abort, err, kErrWaitMisc)) break;
+        tc_fence_after();
+        const uint32_t pa = smem_u32(sP), va = smem_u32(sKV + s * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          // P: two 128 x 64 K-major halves (32 B per K step inside a half); V: 16 key rows = 2048 B per K step
+          const uint64_t dp = sdesc_k_sw128(pa + (uint32_t)((kk >> 2) * (kBQ * 128) + (kk & 3) * 32));
+          const uint64_t dv = sdesc_mn_sw128(va + (uint32_t)(kk * 2048));
+          tc_mma_f16(tmem + 128 + ob * 64, dp, dv, idesc_o, kk != 0);
+        }
+        tc_commit(&o_full[ob]);
+        tc_commit(&kv_empty[s]);
+        tc_commit(p_empty);
+      }
+      if (issued) {
+        tc_commit(mma_done);
+        mbar_wait_drain(mma_done, 0, err);
+      }
+    }
+  } else {
+    // softmax warps: warp w owns TMEM lanes 32*(w%4) .. +31 = query rows
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    float acc[kD];
+#pragma unroll
+    for (int i = 0; i < kD; ++i) acc[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      if (!mbar_wait(s_full, (uint32_t)j & 1, s_abort, err, kErrWaitTmemFull)) { ok = false; break; }
+      tc_fence_after();
+      const int kvalid = a.ntok - j * kBK;  // keys at or past this count are tiling padding
+      // pass 1: row max
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBK; c += 32) {
+        uint32_t r[32];
+        TMEM_LD32(tmem + lane_off + (uint32_t)c, r);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c + i < kvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
+      }
+      const float m_new = fmaxf(m, mx * a.sl2);
+      const float alpha = ex2(m - m_new);
+      // P buffer free (the previous P V has read it)
+      if (j > 0 && !mbar_wait(p_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
+      // pass 2: p = 2^(s*sl2 - m_new), row sum, f16 P into the swizzled A-operand layout
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBK; c += 32) {
+        uint32_t r[32];
+        TMEM_LD32(tmem + lane_off + (uint32_t)c, r);
+        tc_wait_ld();
+        uint8_t* half = sP + (c >> 6) * (kBQ * 128) + row * 128;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float p[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int i = 8 * u + e;
+            p[e] = (c + i < kvalid) ? ex2(fmaf(__uint_as_float(r[i]), a.sl2, -m_new)) : 0.f;
+            sum += p[e];
+          }
+          const int unit = ((c & 63) >> 3) + u;  // 16-byte unit (8 keys) inside the 128-byte row
+          *reinterpret_cast<uint4*>(half + ((unit ^ (row & 7)) << 4)) =
+              make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
+        }
+      }
+      l = l * alpha + sum;
+      m = m_new;
+      // S row fully read; P written
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(s_empty);
+        mbar_arrive(p_full);
+      }
+      // fold O_{j-1} into the register accumulator
+      if (j > 0) {
+        const int ob = (j - 1) & 1;
+        if (!mbar_wait(&o_full[ob], (uint32_t)((j - 1) >> 1) & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < kD; c += 32) {
+          TMEM_LD32(tmem + lane_off + 128 + ob * 64 + (uint32_t)c, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c + i] = fmaf(acc[c + i], alpha_prev, __uint_as_float(r[i]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_empty[ob]);
+      }
+      alpha_prev = alpha;
+    }
+    if (ok) {
+      const int ob = (nkb - 1) & 1;
+      if (mbar_wait(&o_full[ob], (uint32_t)((nkb - 1) >> 1) & 1, s_abort, err, kErrWaitMisc)) {
+        tc_fence_after();
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < kD; c += 32) {
+          TMEM_LD32(tmem + lane_off + 128 + ob * 64 + (uint32_t)c, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c + i] = fmaf(acc[c + i], alpha_prev, __uint_as_float(r[i]));
+        }
+        const int qi = qb * kBQ + row;
+        if (qi < a.ntok) {
+          const long long orow = map_row(a.omap, (long long)w * a.ntok + qi);
+          if (orow >= 0) {
+            const float inv = 1.0f / l;
+            uint4* op = reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * kD);
+#pragma unroll
+            for (int u = 0; u < kD / 8; ++u)
+              op[u] = make_uint4(pack_h2(acc[8 * u] * inv, acc[8 * u + 1] * inv),
+                                 pack_h2(acc[8 * u + 2] * inv, acc[8 * u + 3] * inv),
+                                 pack_h2(acc[8 * u + 4] * inv, acc[8 * u + 5] * inv),
+                                 pack_h2(acc[8 * u + 6] * inv, acc[8 * u + 7] * inv));
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+}  // namespace
+
+void* tensor_map_encoder();  // gemm.cu
+
+// q, k, v of head h of window w: base[w*ntok + n][col + h*64], one row stride for all three.
+int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v_col, int heads, int ntok, int nwin,
+                   __half* o, long long o_n, const RowMap& omap, float scale, int* err, cudaStream_t st) {
+  EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!enc) return -10;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16 || (q_col % 8) || (k_col % 8) || (v_col % 8) ||
+      (o_n % 8) || (reinterpret_cast<uintptr_t>(o) & 15))
+    return -2;
+  CUtensorMap tm;
+  cuuint64_t dims[3] = {(cuuint64_t)ld, (cuuint64_t)ntok, (cuuint64_t)nwin};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(ld * 2 * ntok)};
+  cuuint32_t box[3] = {(cuuint32_t)kD, (cuuint32_t)kBK, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return -12;
+  TcAttnArgs a;
+  a.heads = heads;
+  a.ntok = ntok;
+  a.nwin = nwin;
+  a.q_col = q_col;
+  a.k_col = k_col;
+  a.v_col = v_col;
+  a.o = o;
+  a.o_n = o_n;
+  a.omap = omap;
+  a.sl2 = scale * 1.4426950408889634f;
+  constexpr size_t smem = 1024 + kTileBytes * (1 + kSlots) + kPBytes + 16 * 8 + 16;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return -13;
+    attr = true;
+  }
+  dim3 grid((ntok + kBQ - 1) / kBQ, nwin * heads);
+  attn_tc_kernel<<<grid, kThreads, smem, st>>>(tm, a, err);
+  return launch_status("attention_tc64");
+}
+
+}  // namespace s3b

@@ -239,6 +239,11 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     ctx->max_frames_per_pass = (int)value;
     return kOk;
   }
+  if (k == "attention_impl") {
+    if (value < 0 || value > 1) return set_error(ctx, kErrArg, "attention_impl must be 0 or 1");
+    ctx->attention_impl = (int)value;
+    return kOk;
+  }
   if (k == "stop_after_blocks") {
     if (value < -1 || value > 1024) return set_error(ctx, kErrArg, "stop_after_blocks out of range");
     ctx->stop_after_blocks = (int)value;
@@ -482,6 +487,27 @@ int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, 
   rc = attention(p, d, batch * heads, ctx->stream);
   if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "attention launch failed (%d)", rc);
   return kOk;
+}
+
+int s3b_op_attention_qkv(s3b_ctx* ctx, const void* qkv, int64_t ld, void* out, int64_t ld_out, int nwin, int heads,
+                         int ntok, int d, float scale) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!qkv || !out || nwin <= 0 || heads <= 0 || ntok <= 0 || d <= 0 || ld < 3LL * heads * d || ld_out < (int64_t)heads * d)
+    return set_error(ctx, kErrArg, "bad attention_qkv arguments");
+  AttnParams p;
+  p.q = reinterpret_cast<const __half*>(qkv);
+  p.k = p.q + (long long)heads * d;
+  p.v = p.q + 2LL * heads * d;
+  p.q_b = p.k_b = p.v_b = (long long)ntok * ld;
+  p.q_h = p.k_h = p.v_h = d;
+  p.q_n = p.k_n = p.v_n = ld;
+  p.heads = heads;
+  p.nq = p.nk = ntok;
+  p.o = reinterpret_cast<__half*>(out);
+  p.o_n = ld_out;
+  p.scale = scale;
+  return run_attn(ctx, p, d, nwin * heads);
 }
 
 int s3b_op_layernorm(s3b_ctx* ctx, const float* x, void* out, int out_f32, int64_t rows, int C, const float* g,

@@ -211,6 +211,7 @@ struct s3b_ctx {
   std::map<std::string, std::shared_ptr<s3b::DevBuf>> ws;
   int max_frames_per_pass = 8;
   int stop_after_blocks = -1;  // test hook: run only the first n backbone blocks (-1: all)
+  int attention_impl = 0;      // 0: tcgen05 where eligible, 1: always the mma.sync kernel
   // launch accounting + optional per-kernel CUDA-event timing (s3b_profile_*)
   long long n_launches = 0;
   bool prof = false;

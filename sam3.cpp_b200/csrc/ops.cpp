@@ -52,7 +52,15 @@ int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
     b = ctx->next_event();
     cudaEventRecord(a, ctx->stream);
   }
-  const int rc = attention(p, D, batch_heads, ctx->stream);
+  // the tcgen05 kernel serves d = 64 attention over one fused qkv buffer (the ViT blocks)
+  const long long kq = p.k - p.q, vq = p.v - p.q;
+  const bool tc_ok = ctx->attention_impl != 1 && D == 64 && p.nq == p.nk && p.q_n == p.k_n && p.q_n == p.v_n &&
+                     p.q_b == p.k_b && p.q_b == p.v_b && p.q_b == (long long)p.nq * p.q_n && p.q_h == 64 &&
+                     p.k_h == 64 && p.v_h == 64 && kq > 0 && vq > 0 && kq + 64LL * p.heads <= p.q_n &&
+                     vq + 64LL * p.heads <= p.q_n && batch_heads % p.heads == 0;
+  const int rc = tc_ok ? attention_tc64(p.q, p.q_n, 0, (int)kq, (int)vq, p.heads, p.nq, batch_heads / p.heads, p.o,
+                                        p.o_n, p.omap, p.scale, ctx->d_err, ctx->stream)
+                       : attention(p, D, batch_heads, ctx->stream);
   count_launch(ctx);
   if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "attention D=%d failed (%d)", D, rc);
   if (ctx->prof) {

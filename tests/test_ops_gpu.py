@@ -128,6 +128,51 @@ def test_attention(engine, D, nq, nk, heads, batch):
     assert err < 2e-2, err
 
 
+def _ref_attention_qkv(qkv, nwin, heads, ntok, d, scale):
+    E = heads * d
+    x = qkv[:, :3 * E].float().view(nwin, ntok, 3, heads, d).permute(2, 0, 3, 1, 4)
+    q, k, v = x[0], x[1], x[2]
+    o = torch.softmax((q @ k.transpose(-1, -2)) * scale, dim=-1) @ v
+    return o.permute(0, 2, 1, 3).reshape(nwin * ntok, E)
+
+
+# d = 64 over one fused qkv buffer runs the tcgen05 kernel (ViT window / global
+# attention shapes, ragged token counts, padded row strides); other d use the
+# mma.sync kernel through the same entry point.
+@pytest.mark.parametrize("nwin,heads,ntok,d,pad", [(9, 16, 576, 64, 0), (1, 16, 5184, 64, 0), (3, 2, 64, 64, 0),
+                                                   (2, 3, 200, 64, 64), (5, 1, 129, 64, 8), (1, 4, 1, 64, 0),
+                                                   (4, 2, 300, 72, 0), (2, 2, 256, 96, 32)])
+def test_attention_qkv(engine, nwin, heads, ntok, d, pad):
+    g = torch.Generator(device="cuda").manual_seed(nwin * 1000 + heads * 10 + ntok)
+    E = heads * d
+    qkv = (torch.randn(nwin * ntok, 3 * E + pad, device="cuda", generator=g) * 1.5).half()
+    out = torch.full((nwin * ntok, E + pad), 7.0, device="cuda", dtype=torch.float16)
+    scale = 1.0 / d ** 0.5
+    engine.attention_qkv(qkv, out, nwin, heads, ntok, d, scale)
+    engine.sync()
+    ref = _ref_attention_qkv(qkv, nwin, heads, ntok, d, scale)
+    err = (out[:, :E].float() - ref).abs().max().item()
+    assert err < 2e-2, err
+    if pad:
+        assert torch.all(out[:, E:] == 7.0), "wrote past the head columns"
+
+
+def test_attention_qkv_impls_agree(engine):
+    """The tcgen05 kernel and the mma.sync kernel on the same ViT-window input."""
+    nwin, heads, ntok, d = 4, 16, 576, 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    qkv = (torch.randn(nwin * ntok, 3 * heads * d, device="cuda", generator=g) * 2).half()
+    outs = []
+    for impl in (0, 1):
+        engine.set_option("attention_impl", impl)
+        out = torch.empty(nwin * ntok, heads * d, device="cuda", dtype=torch.float16)
+        engine.attention_qkv(qkv, out, nwin, heads, ntok, d, 0.125)
+        engine.sync()
+        outs.append(out.float())
+    engine.set_option("attention_impl", 0)
+    assert (outs[0] - outs[1]).abs().max().item() < 1e-2
+
+
 @pytest.mark.parametrize("rows,C,f32", [(5184, 1024, 0), (1000, 96, 1), (37, 256, 0), (64, 1152, 1)])
 def test_layernorm(engine, rows, C, f32):
     x = torch.randn(rows, C, device="cuda") * 3 + 1
