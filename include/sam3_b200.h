@@ -65,6 +65,9 @@ int s3b_sync(s3b_ctx* ctx);
 /* Options: "frames_per_pass" (encoder micro-batch, default 8);
  * "attention_impl" (0: tcgen05 flash attention where eligible, 1: always the
  * mma.sync kernel);
+ * "attention_exp_poly" (0-4: of every 8 softmax exponentials in the tcgen05
+ * kernel, how many are evaluated by a polynomial on the FMA pipe instead of
+ * the MUFU unit; a tuning knob, results agree to f16 rounding);
  * "stop_after_blocks" (test hook: run only the first n backbone blocks and
  * no neck, -1 = all; the stage runners of sam3.h:441-496 play this role in
  * the reference). */

@@ -52,6 +52,22 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, for x <= 0 (the softmax exponent), to take part of the
+// exponentials off the MUFU unit, which bounds a d = 64 tile (16384 exp2 per
+// 128 x 128 tile against 2 x 2.1 MFLOP of MMA). Cody-Waite range reduction
+// x = n + f, n = rint(x) taken from the low mantissa bits of x + 1.5*2^23,
+// f in [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted here for minimum
+// maximum relative error on that interval (7.5e-5, below the f16 half ulp of
+// P); 2^n added to the exponent field. x is clamped at -126 so the exponent
+// stays in range (P rounds to 0 in f16 there anyway).
+__device__ __forceinline__ float exp2_poly3(float x) {
+  x = fmaxf(x, -126.f);
+  const float j = x + 12582912.f;
+  const float f = x - (j - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.0551716685f, f, 0.2426111251f), f, 0.6932609677f), f, 0.9999280572f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -88,6 +104,8 @@ struct TcAttnArgs {
   float sl2;  // softmax scale * log2(e)
 };
 
+// NPOLY of every 8 softmax exponentials use exp2_poly3, the rest MUFU ex2.
+template <int NPOLY>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm, TcAttnArgs a, int* err) {
   extern __shared__ uint8_t smem_raw[];
@@ -169,20 +187,22 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(kBQ, kBK, 0);                    // both K-major
+      constexpr uint32_t idesc_s64 = idesc_f16(kBQ, kBK / 2, 0);              // ragged last key tile
       constexpr uint32_t idesc_o = idesc_f16(kBQ, kD, 0) | (1u << 16);        // B (V) MN-major
       bool ok = mbar_wait(q_full, 0, s_abort, err, kErrWaitFull);
       tc_fence_after();
       const uint64_t dq = sdesc_k_sw128(smem_u32(sQ));
       bool issued = false;
-      // S_0
+      // S_j = Q K_j^T; only the first 64 key columns when at most 64 keys of the tile are real
       auto issue_s = [&](int j) -> bool {
         const int t = 2 * j, s = t % kSlots;
         if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) return false;
         if (j > 0 && !mbar_wait(s_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc)) return false;
         tc_fence_after();
         const uint64_t dk = sdesc_k_sw128(smem_u32(sKV + s * kTileBytes));
+        const uint32_t ids = (a.ntok - j * kBK <= kBK / 2) ? idesc_s64 : idesc_s;
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) tc_mma_f16(tmem, dq + (uint64_t)(kk * 2), dk + (uint64_t)(kk * 2), idesc_s, kk != 0);
+        for (int kk = 0; kk < kD / 16; ++kk) tc_mma_f16(tmem, dq + (uint64_t)(kk * 2), dk + (uint64_t)(kk * 2), ids, kk != 0);
         tc_commit(s_full);
         tc_commit(&kv_empty[s]);
         issued = true;
@@ -198,8 +218,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (j >= 2 && !mbar_wait(&o_empty[ob], (uint32_t)((j - 2) >> 1) & 1, s_abort, err, kErrWaitMisc)) break;
         tc_fence_after();
         const uint32_t pa = smem_u32(sP), va = smem_u32(sKV + s * kTileBytes);
+        // K steps that hold a real key (the softmax writes P only up to the chunk holding the last key)
+        const int nk16 = min(kBK / 16, (a.ntok - j * kBK + 15) / 16);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
+          if (kk >= nk16) break;
           // P: two 128 x 64 K-major halves (32 B per K step inside a half); V: 16 key rows = 2048 B per K step
           const uint64_t dp = sdesc_k_sw128(pa + (uint32_t)((kk >> 2) * (kBQ * 128) + (kk & 3) * 32));
           const uint64_t dv = sdesc_mn_sw128(va + (uint32_t)(kk * 2048));
@@ -223,50 +246,75 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int i = 0; i < kD; ++i) acc[i] = 0.f;
     float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    // a warp whose 32 query rows are all tiling padding only keeps the barrier protocol
+    const bool rows_live = qb * kBQ + q4 * 32 < a.ntok;
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
       if (!mbar_wait(s_full, (uint32_t)j & 1, s_abort, err, kErrWaitTmemFull)) { ok = false; break; }
       tc_fence_after();
       const int kvalid = a.ntok - j * kBK;  // keys at or past this count are tiling padding
-      // pass 1: row max
-      float mx = -INFINITY;
+      float alpha = 1.f;
+      if (rows_live) {
+        // pass 1: row max (4 independent chains; 32-key chunks past the last key are skipped)
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kBK; c += 32) {
-        uint32_t r[32];
-        TMEM_LD32(tmem + lane_off + (uint32_t)c, r);
-        tc_wait_ld();
+        for (int c = 0; c < kBK; c += 32) {
+          if (c >= kvalid) break;
+          uint32_t r[32];
+          TMEM_LD32(tmem + lane_off + (uint32_t)c, r);
+          tc_wait_ld();
+          if (c + 32 <= kvalid) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c + i < kvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
+            for (int i = 0; i < 32; i += 4) {
+              mx0 = fmaxf(mx0, __uint_as_float(r[i]));
+              mx1 = fmaxf(mx1, __uint_as_float(r[i + 1]));
+              mx2 = fmaxf(mx2, __uint_as_float(r[i + 2]));
+              mx3 = fmaxf(mx3, __uint_as_float(r[i + 3]));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c + i < kvalid) mx0 = fmaxf(mx0, __uint_as_float(r[i]));
+          }
+        }
+        const float m_new = fmaxf(m, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.sl2);
+        alpha = ex2(m - m_new);
+        m = m_new;
       }
-      const float m_new = fmaxf(m, mx * a.sl2);
-      const float alpha = ex2(m - m_new);
       // P buffer free (the previous P V has read it)
       if (j > 0 && !mbar_wait(p_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
-      // pass 2: p = 2^(s*sl2 - m_new), row sum, f16 P into the swizzled A-operand layout
-      float sum = 0.f;
+      if (rows_live) {
+        // pass 2: p = 2^(s*sl2 - m), row sum, f16 P into the swizzled A-operand layout; padding keys
+        // inside the last chunk get p = 0 (the P V product reads up to the end of that chunk)
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-      for (int c = 0; c < kBK; c += 32) {
-        uint32_t r[32];
-        TMEM_LD32(tmem + lane_off + (uint32_t)c, r);
-        tc_wait_ld();
-        uint8_t* half = sP + (c >> 6) * (kBQ * 128) + row * 128;
+        for (int c = 0; c < kBK; c += 32) {
+          if (c >= kvalid) break;
+          uint32_t r[32];
+          TMEM_LD32(tmem + lane_off + (uint32_t)c, r);
+          tc_wait_ld();
+          const bool whole = c + 32 <= kvalid;
+          uint8_t* half = sP + (c >> 6) * (kBQ * 128) + row * 128;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          float p[8];
+          for (int u = 0; u < 4; ++u) {
+            float p[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int i = 8 * u + e;
-            p[e] = (c + i < kvalid) ? ex2(fmaf(__uint_as_float(r[i]), a.sl2, -m_new)) : 0.f;
-            sum += p[e];
+            for (int e = 0; e < 8; ++e) {
+              const int i = 8 * u + e;
+              const float x = fmaf(__uint_as_float(r[i]), a.sl2, -m);
+              p[e] = (whole || c + i < kvalid) ? (e < NPOLY ? exp2_poly3(x) : ex2(x)) : 0.f;
+            }
+            s0 += p[0] + p[4];
+            s1 += p[1] + p[5];
+            s2 += p[2] + p[6];
+            s3 += p[3] + p[7];
+            const int unit = ((c & 63) >> 3) + u;  // 16-byte unit (8 keys) inside the 128-byte row
+            *reinterpret_cast<uint4*>(half + ((unit ^ (row & 7)) << 4)) =
+                make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
           }
-          const int unit = ((c & 63) >> 3) + u;  // 16-byte unit (8 keys) inside the 128-byte row
-          *reinterpret_cast<uint4*>(half + ((unit ^ (row & 7)) << 4)) =
-              make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
         }
+        l = l * alpha + ((s0 + s1) + (s2 + s3));
       }
-      l = l * alpha + sum;
-      m = m_new;
       // S row fully read; P written
       tc_fence_before();
       fence_proxy_async_smem();
@@ -280,13 +328,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int ob = (j - 1) & 1;
         if (!mbar_wait(&o_full[ob], (uint32_t)((j - 1) >> 1) & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
         tc_fence_after();
-        uint32_t r[32];
+        if (rows_live) {
+          uint32_t r[32];
 #pragma unroll
-        for (int c = 0; c < kD; c += 32) {
-          TMEM_LD32(tmem + lane_off + 128 + ob * 64 + (uint32_t)c, r);
-          tc_wait_ld();
+          for (int c = 0; c < kD; c += 32) {
+            TMEM_LD32(tmem + lane_off + 128 + ob * 64 + (uint32_t)c, r);
+            tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c + i] = fmaf(acc[c + i], alpha_prev, __uint_as_float(r[i]));
+            for (int i = 0; i < 32; ++i) acc[c + i] = fmaf(acc[c + i], alpha_prev, __uint_as_float(r[i]));
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -294,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       alpha_prev = alpha;
     }
-    if (ok) {
+    if (ok && rows_live) {
       const int ob = (nkb - 1) & 1;
       if (mbar_wait(&o_full[ob], (uint32_t)((nkb - 1) >> 1) & 1, s_abort, err, kErrWaitMisc)) {
         tc_fence_after();
@@ -341,7 +391,12 @@ void* tensor_map_encoder();  // gemm.cu
 
 // q, k, v of head h of window w: base[w*ntok + n][col + h*64], one row stride for all three.
 int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v_col, int heads, int ntok, int nwin,
-                   __half* o, long long o_n, const RowMap& omap, float scale, int* err, cudaStream_t st) {
+                   __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int* err,
+                   cudaStream_t st) {
+  typedef void (*KernelFn)(const CUtensorMap, TcAttnArgs, int*);
+  static const KernelFn kernels[5] = {attn_tc_kernel<0>, attn_tc_kernel<1>, attn_tc_kernel<2>, attn_tc_kernel<3>,
+                                      attn_tc_kernel<4>};
+  if (exp_poly < 0 || exp_poly > 4) return -2;
   EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!enc) return -10;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16 || (q_col % 8) || (k_col % 8) || (v_col % 8) ||
@@ -368,14 +423,14 @@ int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v
   a.omap = omap;
   a.sl2 = scale * 1.4426950408889634f;
   constexpr size_t smem = 1024 + kTileBytes * (1 + kSlots) + kPBytes + 16 * 8 + 16;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return -13;
-    attr = true;
+  static bool attr[5] = {false, false, false, false, false};
+  const KernelFn kfn = kernels[exp_poly];
+  if (!attr[exp_poly]) {
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -13;
+    attr[exp_poly] = true;
   }
   dim3 grid((ntok + kBQ - 1) / kBQ, nwin * heads);
-  attn_tc_kernel<<<grid, kThreads, smem, st>>>(tm, a, err);
+  kfn<<<grid, kThreads, smem, st>>>(tm, a, err);
   return launch_status("attention_tc64");
 }
 

@@ -244,6 +244,11 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     ctx->attention_impl = (int)value;
     return kOk;
   }
+  if (k == "attention_exp_poly") {
+    if (value < 0 || value > 4) return set_error(ctx, kErrArg, "attention_exp_poly must be in [0, 4]");
+    ctx->attention_exp_poly = (int)value;
+    return kOk;
+  }
   if (k == "stop_after_blocks") {
     if (value < -1 || value > 1024) return set_error(ctx, kErrArg, "stop_after_blocks out of range");
     ctx->stop_after_blocks = (int)value;

@@ -59,7 +59,7 @@ int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
                      p.k_h == 64 && p.v_h == 64 && kq > 0 && vq > 0 && kq + 64LL * p.heads <= p.q_n &&
                      vq + 64LL * p.heads <= p.q_n && batch_heads % p.heads == 0;
   const int rc = tc_ok ? attention_tc64(p.q, p.q_n, 0, (int)kq, (int)vq, p.heads, p.nq, batch_heads / p.heads, p.o,
-                                        p.o_n, p.omap, p.scale, ctx->d_err, ctx->stream)
+                                        p.o_n, p.omap, p.scale, ctx->attention_exp_poly, ctx->d_err, ctx->stream)
                        : attention(p, D, batch_heads, ctx->stream);
   count_launch(ctx);
   if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "attention D=%d failed (%d)", D, rc);

@@ -158,19 +158,22 @@ def test_attention_qkv(engine, nwin, heads, ntok, d, pad):
 
 
 def test_attention_qkv_impls_agree(engine):
-    """The tcgen05 kernel and the mma.sync kernel on the same ViT-window input."""
+    """The mma.sync kernel and the tcgen05 kernel (MUFU-only and polynomial exponentials) agree."""
     nwin, heads, ntok, d = 4, 16, 576, 64
     g = torch.Generator(device="cuda").manual_seed(5)
     qkv = (torch.randn(nwin * ntok, 3 * heads * d, device="cuda", generator=g) * 2).half()
     outs = []
-    for impl in (0, 1):
+    for impl, poly in ((1, 0), (0, 0), (0, 2), (0, 4)):
         engine.set_option("attention_impl", impl)
+        engine.set_option("attention_exp_poly", poly)
         out = torch.empty(nwin * ntok, heads * d, device="cuda", dtype=torch.float16)
         engine.attention_qkv(qkv, out, nwin, heads, ntok, d, 0.125)
         engine.sync()
         outs.append(out.float())
     engine.set_option("attention_impl", 0)
-    assert (outs[0] - outs[1]).abs().max().item() < 1e-2
+    engine.set_option("attention_exp_poly", 0)
+    for o in outs[1:]:
+        assert (o - outs[0]).abs().max().item() < 1e-2
 
 
 @pytest.mark.parametrize("rows,C,f32", [(5184, 1024, 0), (1000, 96, 1), (37, 256, 0), (64, 1152, 1)])
