@@ -5,6 +5,8 @@ Workload: SAM 3 ViT image encoder + tracker
 SimpleFPN neck, q4_0 weights (seeded synthetic, random-init), 64 seeded
 1008x1008 frames sharded over N GPUs (64/N frames per GPU, one process per
 GPU, no data-path collective). One step = encode all frames of the rank.
+The same line carries `hiera_t_q4_0` (configs[1]: SAM 2.1 Hiera-T + FPN
+neck, q4_0, 16 seeded 1024x1024 frames per GPU), timed the same way.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload vit_q4_0|vit_f16]
   python bench.py --impl reference ...   # CPU restatement (oracle) of the same path
@@ -48,6 +50,74 @@ def load_pkg():
     sys.modules[name] = mod
     spec.loader.exec_module(mod)
     return mod
+
+
+def shard_frames(total: int, rank: int, world: int) -> tuple[int, int]:
+    """Frames [first, first + count) encoded by `rank`: contiguous blocks whose
+    sizes differ by at most one; frame f keeps its seed on any world size."""
+    first = total * rank // world
+    return first, total * (rank + 1) // world - first
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    """Max of a per-rank time over all ranks (the job's time); identity on one rank."""
+    if world <= 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+HIERA_FRAMES_PER_GPU = 16
+
+
+def bench_hiera(s3b, local: int, rank: int, world: int, steps: int, warmup: int, stream, device) -> dict:
+    """SAM 2.1 Hiera-T image encoder + FPN neck, q4_0 weights, a batch of 16 seeded
+    1024^2 frames per GPU (device-resident), CUDA events on the engine stream, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from sam3_b200 import synth
+    path = os.path.join(tempfile.gettempdir(), "s3b_bench_hiera_t_q4_0.ggml")
+    if local == 0 and not os.path.exists(path):
+        synth.write_sam2(path + ".tmp", synth.HIERA_T, seed=0, ftype=1, qtype=2, quantize=s3b.quantize_rows)
+        os.replace(path + ".tmp", path)
+    if world > 1:
+        dist.barrier()
+    eng = s3b.Engine(local)
+    eng.set_option("frames_per_pass", HIERA_FRAMES_PER_GPU)
+    eng.load_model(path)
+    n = HIERA_FRAMES_PER_GPU
+    frames = torch.from_numpy(synth.frames_u8(n, 1024, base_seed=1000 + rank * n)).to(device)
+    for _ in range(warmup):
+        eng.encode_u8(frames)
+    eng.sync()
+    eng.set_stream(stream.cuda_stream)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    eng.profile_begin(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        eng.encode_u8(frames)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prof = eng.profile_end()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+    g, a = prof["gemm"], prof["attention"]
+    eng.set_stream(None)
+    eng.close()
+    return {"workload": f"configs[1]: SAM 2.1 Hiera-T image encoder + FPN neck, q4_0 weights, {n} seeded 1024^2 "
+                        f"frames per GPU (device-resident) x {world} GPU(s)",
+            "value": n * world / (ms / 1000.0), "unit": "frames/s", "ms_per_step": ms,
+            "gemm_tflops": g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0,
+            "gemm_ms_per_step": g["ms"] / steps,
+            "attention_tflops": a["flops"] / (a["ms"] / 1000.0) / 1e12 if a["ms"] > 0 else 0.0,
+            "attention_ms_per_step": a["ms"] / steps,
+            "algorithmic_tflop_per_step": (g["flops"] + a["flops"]) / steps / 1e12,
+            "gpu_launches_per_step": prof["launches"] / steps}
 
 
 def vit_flops_per_frame(cfg, with_neck=True):
@@ -173,6 +243,7 @@ def main():
     ap.add_argument("--frames", type=int, default=FRAMES_TOTAL)
     ap.add_argument("--frames-per-pass", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-hiera", action="store_true", help="skip the Hiera-T (configs[1]) measurement")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -182,7 +253,8 @@ def main():
     metric = "encoder frames/sec (SAM 3 ViT 1008^2 + SimpleFPN neck)"
     cfg_json = {"workload": f"configs[3]: SAM 3 ViT-L encoder + tracker neck, {args.workload.split('_', 1)[1]} "
                             f"weights, {args.frames} seeded 1008^2 frames sharded over {n_gpus} GPU(s)",
-                "frames_total": args.frames, "frames_per_gpu": args.frames // n_gpus, "img_size": 1008,
+                "frames_total": args.frames, "frames_per_gpu": shard_frames(args.frames, 0, n_gpus)[1],
+                "img_size": 1008,
                 "parallelism": f"frame-sharded x{n_gpus} (no collective)",
                 "l2_flush": "inputs + activations per step >> 126 MB L2"}
 
@@ -233,8 +305,7 @@ def main():
     eng.load_model(path)
     load_s = time.time() - t0
 
-    nf = args.frames // n_gpus
-    first = rank * nf
+    first, nf = shard_frames(args.frames, rank, n_gpus)
     host = synth.frames_u8(nf, cfg.img_size, base_seed=1000 + first)
     host_t = torch.from_numpy(host).pin_memory()
     dev = host_t.cuda()
@@ -264,11 +335,7 @@ def main():
     torch.cuda.synchronize()
     prof = eng.profile_end()
     clk = clocks.stop()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world, "cuda")
     value = args.frames / (ms / 1000.0)
 
     # --- end-to-end through the public API with host buffers
@@ -286,11 +353,7 @@ def main():
             eng.output("neck_trk_2", f, out=out_np[f])
     ev3.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = ev2.elapsed_time(ev3) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(ev2.elapsed_time(ev3) / args.steps, world, "cuda")
     e2e = args.frames / (e2e_ms / 1000.0)
 
     # --- roofline of the dominant kernel (tensor-core GEMM)
@@ -298,6 +361,7 @@ def main():
     g = prof["gemm"]
     gemm_tflops = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0
     a = prof["attention"]
+    ln = prof["layernorm"]
     attn_tflops = a["flops"] / (a["ms"] / 1000.0) / 1e12 if a["ms"] > 0 else 0.0
     fl_gemm, fl_attn, fl_neck = vit_flops_per_frame(cfg)
     total_tflops = (fl_gemm + fl_attn + fl_neck) * value / 1e12
@@ -318,9 +382,18 @@ def main():
                          "gemm_ms_per_step": g["ms"] / args.steps, "gemm_launches_per_step": g["launches"] / args.steps},
             "attention": {"achieved_tflops": attn_tflops, "ms_per_step": a["ms"] / args.steps,
                           "frac_of_peak": attn_tflops / peak_sust},
+            "layernorm": {"achieved_gbs": ln["bytes"] / (ln["ms"] / 1000.0) / 1e9 if ln["ms"] > 0 else 0.0,
+                          "peak_gbs": hbm, "frac_of_peak": (ln["bytes"] / (ln["ms"] / 1000.0) / 1e9 / hbm)
+                          if ln["ms"] > 0 else 0.0, "ms_per_step": ln["ms"] / args.steps,
+                          "launches_per_step": ln["launches"] / args.steps,
+                          "bound": "hbm (algorithmic bytes: f32 rows in + f16 rows out)"},
             "whole_step_tflops": total_tflops, "flops_per_frame": fl_gemm + fl_attn + fl_neck,
             "gpu_launches": int(prof["launches"]), "clocks": clk,
             "setup": {"model_gen_s": gen_s, "load_s": load_s, "weights_mib": eng.model_info()["weights_mib"]}}
+    eng.set_stream(None)
+    eng.close()
+    if not args.no_hiera:
+        line["hiera_t_q4_0"] = bench_hiera(s3b, local, rank, world, args.steps, args.warmup, stream, "cuda")
     if rank == 0 and not args.no_cpu_baseline and world == 1:
         v, parts = cpu_sample(args.workload, 1)
         line["cpu_baseline"] = {"value": v, "unit": "frames/s", "cores": os.cpu_count(), "kind": "port",
@@ -328,8 +401,6 @@ def main():
                                           f"tracker neck, extrapolated to 28+4 blocks; {parts}"}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    eng.set_stream(None)
-    eng.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

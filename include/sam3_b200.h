@@ -73,12 +73,14 @@ int s3b_sync(s3b_ctx* ctx);
  * the reference). */
 int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value);
 
-/* Profiling (CUDA events on the context stream around every GEMM and
- * attention launch; the reference times compute with std::chrono around
+/* Profiling (CUDA events on the context stream around every GEMM, attention
+ * and LayerNorm launch; the reference times compute with std::chrono around
  * ggml_backend_graph_compute, sam3.cpp:6118-6131). s3b_profile_end waits for
- * the stream and writes out[0..8]: GEMM {launches, ms, flops, bytes},
- * attention {launches, ms, flops, bytes}, and the total number of kernel
- * launches since s3b_profile_begin. */
+ * the stream and writes the first n (up to 13) of: out[0..3] GEMM {launches,
+ * ms, flops, bytes}, out[4..7] attention {launches, ms, flops, bytes},
+ * out[8] the total number of kernel launches since s3b_profile_begin,
+ * out[9..12] LayerNorm {launches, ms, 0, bytes}. Bytes and flops are
+ * algorithmic (operands and results once). */
 int s3b_profile_begin(s3b_ctx* ctx, int with_events);
 int s3b_profile_end(s3b_ctx* ctx, double* out, int n);
 

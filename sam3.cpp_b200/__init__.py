@@ -207,11 +207,12 @@ class Engine:
         self._check(self._L.s3b_profile_begin(self.h, 1 if with_events else 0), "s3b_profile_begin")
 
     def profile_end(self) -> dict:
-        buf = (ctypes.c_double * 9)()
-        self._check(self._L.s3b_profile_end(self.h, buf, 9), "s3b_profile_end")
+        buf = (ctypes.c_double * 13)()
+        self._check(self._L.s3b_profile_end(self.h, buf, 13), "s3b_profile_end")
         v = list(buf)
         return {"gemm": {"launches": v[0], "ms": v[1], "flops": v[2], "bytes": v[3]},
                 "attention": {"launches": v[4], "ms": v[5], "flops": v[6], "bytes": v[7]},
+                "layernorm": {"launches": v[9], "ms": v[10], "bytes": v[12]},
                 "launches": int(v[8])}
 
     def load_model(self, path: str):

@@ -79,9 +79,11 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
   __half* sV = sK + 2 * kBKV * LD;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.y;
+  // 1-D grid, query tile fastest: the tiles of one (batch, head) run together and share K/V in L2
+  const int n_qt = (p.nq + kBQ - 1) / kBQ;
+  const int bh = (int)(blockIdx.x / n_qt);
   const int b = bh / p.heads, h = bh - (bh / p.heads) * p.heads;
-  const int q0 = blockIdx.x * kBQ;
+  const int q0 = (int)(blockIdx.x - (unsigned)bh * n_qt) * kBQ;
   const __half* Qg = p.q + (long long)b * p.q_b + (long long)h * p.q_h + (long long)q0 * p.q_n;
   const __half* Kg = p.k + (long long)b * p.k_b + (long long)h * p.k_h;
   const __half* Vg = p.v + (long long)b * p.v_b + (long long)h * p.v_h;
@@ -237,8 +239,9 @@ int launch_attn(const AttnParams& p, int batch_heads, cudaStream_t st) {
       return -13;
     attr = true;
   }
-  dim3 grid((p.nq + kBQ - 1) / kBQ, batch_heads);
-  attn_fwd_kernel<D, DR><<<grid, 128, smem, st>>>(p);
+  const long long n_cta = (long long)((p.nq + kBQ - 1) / kBQ) * batch_heads;
+  if (n_cta > 0x7fffffffLL) return -2;
+  attn_fwd_kernel<D, DR><<<(unsigned)n_cta, 128, smem, st>>>(p);
   return launch_status("attention");
 }
 

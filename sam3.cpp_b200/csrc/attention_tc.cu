@@ -128,8 +128,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = blockIdx.x;
-  const int bh = blockIdx.y;
+  // 1-D grid, query tile fastest: the tiles of one (window, head) run together and share K/V in L2
+  const int n_qt = (a.ntok + kBQ - 1) / kBQ;
+  const int bh = (int)(blockIdx.x / n_qt);
+  const int qb = (int)(blockIdx.x - (unsigned)bh * n_qt);
   const int w = bh / a.heads, h = bh - w * a.heads;
   const int nkb = (a.ntok + kBK - 1) / kBK;
 
@@ -429,8 +431,9 @@ int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v
     if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -13;
     attr[exp_poly] = true;
   }
-  dim3 grid((ntok + kBQ - 1) / kBQ, nwin * heads);
-  kfn<<<grid, kThreads, smem, st>>>(tm, a, err);
+  const long long n_cta = (long long)((ntok + kBQ - 1) / kBQ) * nwin * heads;
+  if (n_cta > 0x7fffffffLL) return -2;
+  kfn<<<(unsigned)n_cta, kThreads, smem, st>>>(tm, a, err);
   return launch_status("attention_tc64");
 }
 

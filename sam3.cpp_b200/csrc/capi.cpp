@@ -271,18 +271,18 @@ int s3b_profile_end(s3b_ctx* ctx, double* out, int n) {
   int rc = ctx_enter(ctx);
   if (rc) return rc;
   if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return set_error(ctx, kErrCuda, "synchronize failed");
-  double v[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  double v[13] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
   for (const auto& e : ctx->prof_entries) {
     float ms = 0.f;
     cudaEventElapsedTime(&ms, e.a, e.b);
-    const int base = e.kind == 0 ? 0 : 4;
+    const int base = e.kind == 0 ? 0 : e.kind == 1 ? 4 : 9;
     v[base + 0] += 1;
     v[base + 1] += ms;
     v[base + 2] += e.flops;
     v[base + 3] += e.bytes;
   }
   v[8] = (double)ctx->n_launches;
-  for (int i = 0; i < n && i < 9; ++i) out[i] = v[i];
+  for (int i = 0; i < n && i < 13; ++i) out[i] = v[i];
   ctx->prof = false;
   ctx->prof_entries.clear();
   ctx->event_next = 0;

@@ -217,7 +217,7 @@ struct s3b_ctx {
   long long n_launches = 0;
   bool prof = false;
   struct Prof {
-    int kind;  // 0 GEMM, 1 attention, 2 other
+    int kind;  // 0 GEMM, 1 attention, 2 LayerNorm
     double flops, bytes;
     cudaEvent_t a, b;
   };
@@ -242,6 +242,9 @@ int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Lin
 // profiling is on, bracket the launch with CUDA events on the context stream.
 int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long long M, const EpiParams& ep);
 int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads);
+// layernorm() on the context stream, timed when profiling; returns layernorm's status (the caller counts the launch)
+int run_ln(s3b_ctx* ctx, const float* x, long long ldx, void* y, int y_f32, long long ldy, long long rows, int C,
+           const float* g, const float* b, float eps, const RowMap& map);
 void count_launch(s3b_ctx* ctx, int n = 1);
 EpiParams epi_store(const Linear& L, void* out, int out_f32, long long ldo, int act = ACT_NONE);
 

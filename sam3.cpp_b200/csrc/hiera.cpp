@@ -82,7 +82,7 @@ static int hiera_block(s3b_ctx* ctx, const HieraBlock& B, int F, int S, float* x
   // shortcut (sam3.cpp:4312-4327): dim projection of the normed input and/or 2x2 max pool
   float* xnew = x;
   if (din != dout) {
-    CKH(layernorm(x, din, xn, 0, din, T, din, B.n1w.ptr(), B.n1b.ptr(), 1e-6f, id, ctx->stream));
+    CKH(run_ln(ctx, x, din, xn, 0, din, T, din, B.n1w.ptr(), B.n1b.ptr(), 1e-6f, id));
     xnew = xalt;
     if (B.q_stride) {
       CKR(run_gemm(ctx, xn, din, B.dim_proj, T, epi_store(B.dim_proj, tmp, 1, dout)));
@@ -95,7 +95,7 @@ static int hiera_block(s3b_ctx* ctx, const HieraBlock& B, int F, int S, float* x
     CKH(maxpool2_cl_f32(x, F, S, S, dout, xnew, ctx->stream));
   }
   // norm1 + zero-padded window partition (sam3.cpp:4306-4337)
-  CKH(layernorm(x, din, xw, 0, din, Tw, din, B.n1w.ptr(), B.n1b.ptr(), 1e-6f, g.wmap, ctx->stream));
+  CKH(run_ln(ctx, x, din, xw, 0, din, Tw, din, B.n1w.ptr(), B.n1b.ptr(), 1e-6f, g.wmap));
   // qkv (sam3.cpp:4344-4357)
   CKR(run_gemm(ctx, xw, din, B.qkv, Tw, epi_store(B.qkv, qkv, 0, 3LL * dout)));
   AttnParams a;
@@ -130,7 +130,7 @@ static int hiera_block(s3b_ctx* ctx, const HieraBlock& B, int F, int S, float* x
   pr.ldr = dout;
   CKR(run_gemm(ctx, ao, dout, B.proj, T2, pr));
   // MLP with tanh GELU + residual (sam3.cpp:4440-4454)
-  CKH(layernorm(xnew, dout, xn, 0, dout, T2, dout, B.n2w.ptr(), B.n2b.ptr(), 1e-6f, id, ctx->stream));
+  CKH(run_ln(ctx, xnew, dout, xn, 0, dout, T2, dout, B.n2w.ptr(), B.n2b.ptr(), 1e-6f, id));
   CKR(run_gemm(ctx, xn, dout, B.fc1, T2, epi_store(B.fc1, hbuf, 0, 4LL * dout, ACT_GELU_TANH)));
   EpiParams f2 = epi_store(B.fc2, xnew, 1, dout);
   f2.resid = xnew;

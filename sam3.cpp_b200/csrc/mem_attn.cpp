@@ -97,7 +97,7 @@ int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat
   for (size_t l = 0; l < M.mem.size(); ++l) {
     const MemAttnLayer& L = M.mem[l];
     // self-attention with RoPE on q and k (sam3.cpp:9247-9271)
-    CKL(layernorm(X, D, XN, 0, D, N, D, L.n1w.ptr(), L.n1b.ptr(), 1e-5f, id, ctx->stream));
+    CKL(run_ln(ctx, X, D, XN, 0, D, N, D, L.n1w.ptr(), L.n1b.ptr(), 1e-5f, id));
     EpiParams e = epi_store(L.sa_qkv, qkv->p, 0, 3LL * D);
     e.rope = rope;
     e.rope_D = D;
@@ -121,7 +121,7 @@ int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat
     r.ldr = D;
     CKR(run_gemm(ctx, ao->as<__half>(), D, L.sa_out, N, r));
     // cross-attention to the memory (sam3.cpp:9274-9316)
-    CKL(layernorm(X, D, XN, 0, D, N, D, L.n2w.ptr(), L.n2b.ptr(), 1e-5f, id, ctx->stream));
+    CKL(run_ln(ctx, X, D, XN, 0, D, N, D, L.n2w.ptr(), L.n2b.ptr(), 1e-5f, id));
     EpiParams eq = epi_store(L.ca_q, qkv->p, 0, D);
     eq.rope = rope;
     eq.rope_D = D;
@@ -156,7 +156,7 @@ int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat
     r2.ldr = D;
     CKR(run_gemm(ctx, ao->as<__half>(), D, L.ca_out, N, r2));
     // FFN (sam3.cpp:9318-9326)
-    CKL(layernorm(X, D, XN, 0, D, N, D, L.n3w.ptr(), L.n3b.ptr(), 1e-5f, id, ctx->stream));
+    CKL(run_ln(ctx, X, D, XN, 0, D, N, D, L.n3w.ptr(), L.n3b.ptr(), 1e-5f, id));
     CKR(run_gemm(ctx, XN, D, L.fc1, N, epi_store(L.fc1, hb->p, 0, FFN, ACT_RELU)));
     EpiParams r3 = epi_store(L.fc2, X, 1, D);
     r3.resid = X;
@@ -164,7 +164,7 @@ int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat
     CKR(run_gemm(ctx, hb->as<__half>(), FFN, L.fc2, N, r3));
   }
   // final norm (sam3.cpp:9330-9334)
-  CKL(layernorm(X, D, out, 1, D, N, D, M.mem_norm_w.ptr(), M.mem_norm_b.ptr(), 1e-5f, id, ctx->stream));
+  CKL(run_ln(ctx, X, D, out, 1, D, N, D, M.mem_norm_w.ptr(), M.mem_norm_b.ptr(), 1e-5f, id));
   return check_device(ctx, "mem_attn");
 }
 

@@ -45,6 +45,24 @@ int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long
   return kOk;
 }
 
+// LayerNorm (HBM-bound): algorithmic bytes = f32 rows in + rows out (f16 / f32) + gamma, beta.
+int run_ln(s3b_ctx* ctx, const float* x, long long ldx, void* y, int y_f32, long long ldy, long long rows, int C,
+           const float* g, const float* b, float eps, const RowMap& map) {
+  cudaEvent_t ea = nullptr, eb = nullptr;
+  if (ctx->prof) {
+    ea = ctx->next_event();
+    eb = ctx->next_event();
+    cudaEventRecord(ea, ctx->stream);
+  }
+  const int rc = layernorm(x, ldx, y, y_f32, ldy, rows, C, g, b, eps, map, ctx->stream);
+  if (!rc && ctx->prof) {
+    cudaEventRecord(eb, ctx->stream);
+    const double bytes = (4.0 + (y_f32 ? 4.0 : 2.0)) * rows * C + 8.0 * C;
+    ctx->prof_entries.push_back({2, 0.0, bytes, ea, eb});
+  }
+  return rc;
+}
+
 int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
   cudaEvent_t a = nullptr, b = nullptr;
   if (ctx->prof) {

@@ -55,7 +55,7 @@ static int vit_block(s3b_ctx* ctx, const VitBlock& B, int F, float* x, __half* x
   }
   const long long Tw = (long long)nwin * ntok;  // rows in window order (>= T when padded)
   // norm1 + window partition (ggml_win_part, sam3.cpp:3730)
-  CK(layernorm(x, E, xn, 0, E, Tw, E, B.n1w.ptr(), B.n1b.ptr(), 1e-5f, wmap, ctx->stream));
+  CK(run_ln(ctx, x, E, xn, 0, E, Tw, E, B.n1w.ptr(), B.n1b.ptr(), 1e-5f, wmap));
   // qkv + bias + RoPE(q, k) into [Tw][3E] f16 (sam3.cpp:3738-3771); the attention
   // kernel reads q / k / v of each (window, head) with strides, so no split copies
   EpiParams ep = epi_store(B.qkv, qkv, 0, 3LL * E);
@@ -92,7 +92,7 @@ static int vit_block(s3b_ctx* ctx, const VitBlock& B, int F, float* x, __half* x
   CKG(gemm(ctx, ao, E, B.proj, T, pe));
   // norm2 -> fc1 + GELU(erf) -> fc2 + residual (sam3.cpp:3789-3798)
   RowMap id;
-  CK(layernorm(x, E, xn, 0, E, T, E, B.n2w.ptr(), B.n2b.ptr(), 1e-5f, id, ctx->stream));
+  CK(run_ln(ctx, x, E, xn, 0, E, T, E, B.n2w.ptr(), B.n2b.ptr(), 1e-5f, id));
   const int MLP = B.fc1.N;
   CKG(gemm(ctx, xn, E, B.fc1, T, epi_store(B.fc1, hbuf, 0, MLP, ACT_GELU_ERF)));
   EpiParams f2 = epi_store(B.fc2, x, 1, E);
@@ -221,7 +221,7 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
     CKG(gemm(ctx, col->as<__half>(), Kp, M.patch, T, pe));
     // ln_pre (sam3.cpp:3825-3827)
     RowMap id;
-    CK(layernorm(xp->as<float>(), E, x, 1, E, T, E, M.ln_pre_w.ptr(), M.ln_pre_b.ptr(), 1e-5f, id, ctx->stream));
+    CK(run_ln(ctx, xp->as<float>(), E, x, 1, E, T, E, M.ln_pre_w.ptr(), M.ln_pre_b.ptr(), 1e-5f, id));
     // stage runner (test hook, like sam3_test_run_vit_block_stage): stop after `stop_after_blocks`
     const int n_blocks = ctx->stop_after_blocks >= 0 && ctx->stop_after_blocks < hp.vit_depth
                              ? ctx->stop_after_blocks

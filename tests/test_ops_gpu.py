@@ -112,7 +112,10 @@ def test_gemm_f16_out_strided(engine):
 @pytest.mark.parametrize("D,nq,nk,heads,batch", [(64, 576, 576, 16, 2), (64, 5184, 5184, 2, 1), (96, 49, 196, 8, 3),
                                                  (96, 4096, 4096, 1, 1), (80, 100, 100, 2, 2),
                                                  (256, 1000, 3000, 1, 1), (128, 70, 33, 3, 2),
-                                                 (72, 196, 196, 2, 3), (72, 49, 196, 16, 2)])
+                                                 (72, 196, 196, 2, 3), (72, 49, 196, 16, 2),
+                                                 # more (batch, head) pairs than a grid's y extent (Hiera-T
+                                                 # stage-1 windows at 16 frames per pass)
+                                                 (96, 16, 16, 4, 16400)])
 def test_attention(engine, D, nq, nk, heads, batch):
     g = torch.Generator(device="cuda").manual_seed(D + nq + nk)
     q = torch.randn(batch, heads, nq, D, device="cuda", generator=g).half()
