@@ -16,9 +16,15 @@ namespace {
 
 constexpr int kMaxVec = 16;  // float4 per lane -> C <= 2048
 
-__global__ void layernorm_kernel(const float* __restrict__ x, long long ldx, void* __restrict__ y, int y_f32,
-                                 long long ldy, long long rows, int C, const float* __restrict__ gamma,
-                                 const float* __restrict__ beta, float eps, RowMap map) {
+// One warp per row, NV = ceil(C / 128) float4 per lane held in registers (so
+// the register footprint, and with it the number of rows in flight per SM,
+// follows the row width). The row is streamed (read once), the output is
+// left in L2 for the GEMM that consumes it next.
+template <int NV>
+__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, long long ldx,
+                                                        void* __restrict__ y, int y_f32, long long ldy, long long rows,
+                                                        int C, const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta, float eps, RowMap map) {
   const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -36,22 +42,21 @@ __global__ void layernorm_kernel(const float* __restrict__ x, long long ldx, voi
   }
   const float* xr = x + src * ldx;
   const int nvec = C >> 2;
-  float4 v[kMaxVec];
+  float4 v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int vi = lane + 32 * i;
+    v[i] = vi < nvec ? __ldcs(reinterpret_cast<const float4*>(xr + 4 * vi)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   float sum = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
-    const int vi = lane + 32 * i;
-    if (vi < nvec) {
-      v[i] = *reinterpret_cast<const float4*>(xr + 4 * vi);
-      sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-    }
-  }
+  for (int i = 0; i < NV; ++i) sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
 #pragma unroll
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   const float mean = sum / (float)C;
   float var = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < NV; ++i) {
     const int vi = lane + 32 * i;
     if (vi < nvec) {
       const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
@@ -62,7 +67,7 @@ __global__ void layernorm_kernel(const float* __restrict__ x, long long ldx, voi
   for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
   const float rstd = rsqrtf(var / (float)C + eps);
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < NV; ++i) {
     const int vi = lane + 32 * i;
     if (vi < nvec) {
       const float4 g = *reinterpret_cast<const float4*>(gamma + 4 * vi);
@@ -274,7 +279,21 @@ int layernorm(const float* x, long long ldx, void* y, int y_f32, long long ldy, 
   if (C % 4 || C > 4 * 32 * kMaxVec || ldx % 4 || ldy % 4 || rows <= 0) return -1;
   const int warps = 8;
   const long long blocks = (rows + warps - 1) / warps;
-  layernorm_kernel<<<(unsigned)blocks, warps * 32, 0, st>>>(x, ldx, y, y_f32, ldy, rows, C, gamma, beta, eps, map);
+  if (blocks > 0x7fffffffLL) return -1;
+  const int nv = (C + 127) / 128;
+#define S3B_LN_CASE(N)                                                                                            \
+  case N:                                                                                                        \
+    layernorm_kernel<N><<<(unsigned)blocks, warps * 32, 0, st>>>(x, ldx, y, y_f32, ldy, rows, C, gamma, beta, eps, \
+                                                                  map);                                          \
+    break;
+  switch (nv) {
+    S3B_LN_CASE(1) S3B_LN_CASE(2) S3B_LN_CASE(3) S3B_LN_CASE(4) S3B_LN_CASE(5) S3B_LN_CASE(6) S3B_LN_CASE(7)
+    S3B_LN_CASE(8) S3B_LN_CASE(9) S3B_LN_CASE(10) S3B_LN_CASE(11) S3B_LN_CASE(12) S3B_LN_CASE(13)
+    S3B_LN_CASE(14) S3B_LN_CASE(15) S3B_LN_CASE(16)
+    default:
+      return -1;
+  }
+#undef S3B_LN_CASE
   return launch_ok();
 }
 

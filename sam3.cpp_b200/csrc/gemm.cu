@@ -41,6 +41,8 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr uint32_t kStageBufBytes = 16384;  // 128 rows x 128 B
 
+bool g_gemm_pairs = true;  // 256-row tiles on SM pairs for the wide TMA-epilogue GEMMs
+
 
 // Two f32 -> one packed f16x2 register (lo in the low half), round to nearest even.
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
@@ -231,13 +233,23 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-template <int BN, int STAGES, bool TMA_EPI>
+// PAIR: clusters of 2 CTAs on two SMs share one 256 x BN tile (cta_group::2):
+// each CTA loads its 128 rows of A and BN/2 rows of B per stage (so a stage
+// is 32 KB instead of 48 KB at BN = 256 and more stages fit), the even CTA
+// issues M = 256 MMAs over both CTAs' shared memory into both TMEMs, and
+// each CTA runs the epilogue of its own 128 rows. Stage completion is counted
+// on the leader's `full` barrier; the leader's commits arrive on `empty` /
+// `tfull` of both CTAs; both epilogues release accumulators on the leader's
+// `tempty`.
+template <int BN, int STAGES, bool TMA_EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, int M, int N, int K, EpiParams ep,
                        int resid_in_place, int* err) {
+  constexpr int BN_CTA = PAIR ? BN / 2 : BN;  // rows of B this CTA loads per stage
+  constexpr int TM = PAIR ? 2 * kBM : kBM;    // output rows per tile
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
-  constexpr uint32_t B_BYTES = BN * kBK * 2;
+  constexpr uint32_t B_BYTES = BN_CTA * kBK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = 2 * BN;
   constexpr uint32_t STAGING = TMA_EPI ? 4 * kStageBufBytes : 0;
@@ -260,7 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles_m = (M + kBM - 1) / kBM;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;  // CTA within the pair; 0 issues the MMAs
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int tiles_m = (M + TM - 1) / TM;
   const int tiles_n = (N + BN - 1) / BN;
   const int n_tiles = tiles_m * tiles_n;
   const int nk = (K + kBK - 1) / kBK;
@@ -272,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps);
+      mbar_init(&tempty[a], PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     mbar_init(mma_done, 1);
     for (int i = 0; i < 4; ++i) mbar_init(&rfull[i], 1);
@@ -284,11 +299,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (TMA_EPI) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
-    tmem_alloc(s_tmem, TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(s_tmem, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(s_tmem, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
 
@@ -299,33 +320,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t armed = 0;        // bit s: stage s has been armed at least once
       uint32_t armed_phase = 0;  // bit s: parity of the last arming of stage s
       bool ok = true;
-      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-        const int m0 = (t / tiles_n) * kBM;
-        const int n0 = (t % tiles_n) * BN;
+      for (int t = unit; t < n_tiles && ok; t += n_units) {
+        const int m0 = (t / tiles_n) * TM + (int)rank * kBM;
+        const int n0 = (t % tiles_n) * BN + (int)rank * BN_CTA;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, m0);
-          tma_load_2d(&tmB, &full[stage], sB + stage * B_BYTES, kb * kBK, n0);
+          if (PAIR) {
+            // both CTAs' bytes complete the leader's barrier; only the leader arms it
+            const uint32_t fb = cluster_addr(smem_u32(&full[stage]), 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+            tma_load_2d_pair(&tmA, fb, sA + stage * A_BYTES, kb * kBK, m0);
+            tma_load_2d_pair(&tmB, fb, sB + stage * B_BYTES, kb * kBK, n0);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+            tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, m0);
+            tma_load_2d(&tmB, &full[stage], sB + stage * B_BYTES, kb * kBK, n0);
+          }
           armed |= 1u << stage;
           armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
-      // Every issued copy lands before the CTA may exit.
+      // Every issued copy lands before the CTA may exit. With pairs the copies
+      // are counted on the leader, so wait instead for the MMA's release of
+      // each stage's last use (which also makes every commit that targets this
+      // CTA's `empty` barriers land before exit).
       for (int s = 0; s < STAGES; ++s)
-        if (armed & (1u << s)) mbar_wait_drain(&full[s], (armed_phase >> s) & 1u, err);
+        if (armed & (1u << s)) mbar_wait_drain(PAIR ? &empty[s] : &full[s], (armed_phase >> s) & 1u, err);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(kBM, BN, 0);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f16(TM, BN, 0);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t aphase = 0;
       bool ok = true;
       bool issued = false;
-      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+      for (int t = unit; t < n_tiles && ok; t += n_units) {
         if (!mbar_wait(&tempty[acc], aphase ^ 1, s_abort, err, kErrWaitTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -335,19 +367,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t da = sdesc_k_sw128(smem_u32(sA + stage * A_BYTES));
           const uint64_t db = sdesc_k_sw128(smem_u32(sB + stage * B_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            tc_mma_f16(d_tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (kb | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            if (PAIR)
+              tc_mma_f16_pair(d_tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (kb | kk) != 0 ? 1u : 0u);
+            else
+              tc_mma_f16(d_tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
           issued = true;
-          tc_commit(&empty[stage]);
+          if (PAIR) tc_commit_pair(&empty[stage], 3); else tc_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        tc_commit(&tfull[acc]);
+        if (PAIR) tc_commit_pair(&tfull[acc], 3); else tc_commit(&tfull[acc]);
         if (++acc == 2) { acc = 0; aphase ^= 1; }
       }
-      // All MMAs of this CTA complete before TMEM is released.
+      // All MMAs complete before TMEM is released.
       if (issued) {
-        tc_commit(mma_done);
+        if (PAIR) tc_commit_pair(mma_done, 1); else tc_commit(mma_done);
         mbar_wait_drain(mma_done, 0, err);
       }
     }
@@ -375,8 +411,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (b) ++r_issued1; else ++r_issued0;
     };
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
-      const int m0 = (t / tiles_n) * kBM;
+    // this CTA's epilogue warps release an accumulator on the MMA-issuing CTA's barrier
+    auto release_acc = [&](int a) {
+      if (PAIR)
+        mbar_arrive_cluster(cluster_addr(smem_u32(&tempty[a]), 0));
+      else
+        mbar_arrive(&tempty[a]);
+    };
+    for (int t = unit; t < n_tiles; t += n_units) {
+      const int m0 = (t / tiles_n) * TM + (int)rank * kBM;
       const int n0 = (t % tiles_n) * BN;
       // the first residual chunk does not depend on the accumulator: fetch it during the main loop
       if (TMA_EPI && resid_in_place && leader) issue_resid(chunk_ctr, n0 + half * (BN / 2), m0);
@@ -403,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // accumulator fully read: hand TMEM back to the MMA warp early
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
+            if (lane == 0) release_acc(acc);
           }
           if (resid_in_place) {
             // parity of this buffer's residual barrier = number of its earlier uses & 1
@@ -463,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (c + 16 >= BN / 2) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
+            if (lane == 0) release_acc(acc);
           }
           const int gc = n0 + half * (BN / 2) + c;
           if (gr < M && gc < N) {
@@ -487,9 +530,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // pairs: the leader's MMAs (which read the peer's shared memory and write its
+  // TMEM) and all remote arrives are complete before either CTA frees or exits
+  if (PAIR) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -527,13 +576,14 @@ int make_map_2d(CUtensorMap* map, const void* base, long long rows, long long co
   return r == CUDA_SUCCESS ? 0 : -12;
 }
 
-template <int BN, int STAGES, bool TMA_EPI>
+template <int BN, int STAGES, bool TMA_EPI, bool PAIR>
 int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
                 const EpiParams& ep, int resid_in_place, int* err, cudaStream_t st) {
+  constexpr int BN_CTA = PAIR ? BN / 2 : BN;
   CUtensorMap ma, mb, mc;
   int rc = make_map_2d(&ma, A, M, K, lda, kBM, 2);
   if (rc) return rc;
-  rc = make_map_2d(&mb, B, N, K, ldb, BN, 2);
+  rc = make_map_2d(&mb, B, N, K, ldb, BN_CTA, 2);
   if (rc) return rc;
   if (TMA_EPI) {
     rc = make_map_2d(&mc, ep.out, M, N, ep.ldo, kBM, ep.out_f32 ? 4 : 2);
@@ -541,20 +591,60 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
   } else {
     mc = ma;  // unused
   }
-  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN) * kBK * 2 + (TMA_EPI ? 4 * kStageBufBytes : 0) +
+  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN_CTA) * kBK * 2 + (TMA_EPI ? 4 * kStageBufBytes : 0) +
                           (2 * STAGES + 9) * 8 + 16;
+  static_assert(smem <= 232448, "shared memory per CTA");
+  auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR>;
   static bool attr_set = false;
+  static int max_units = 0;  // co-resident CTAs (or pairs)
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_f16_tc_kernel<BN, STAGES, TMA_EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return -13;
+    max_units = num_sms();
+    if (PAIR) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * (num_sms() / 2));
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) return -13;
+      max_units = n;
+    }
     attr_set = true;
   }
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_f16_tc_kernel<BN, STAGES, TMA_EPI><<<grid, kThreads, smem, st>>>(ma, mb, mc, M, N, K, ep, resid_in_place,
-                                                                        err);
-  return launch_status("gemm");
+  const int tm = PAIR ? 2 * kBM : kBM;
+  const int tiles = ((M + tm - 1) / tm) * ((N + BN - 1) / BN);
+  const int units = tiles < max_units ? tiles : max_units;
+  if (!PAIR) {
+    kernel<<<units, kThreads, smem, st>>>(ma, mb, mc, M, N, K, ep, resid_in_place, err);
+    return launch_status("gemm");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * units);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, M, N, K, ep, resid_in_place, err);
+  if (e != cudaSuccess) {
+    fprintf(stderr, "s3b: CUDA error at gemm (pair) launch: %s (%d)\n", cudaGetErrorString(e), (int)e);
+    cudaGetLastError();
+    return -14;
+  }
+  return launch_status("gemm (pair)");
 }
 
 }  // namespace
@@ -594,11 +684,16 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
                        (reinterpret_cast<uintptr_t>(ep.out) & 15) == 0 && (ep.ldo * eb) % 16 == 0 && ep.ldo >= N;
   const int resid_in_place = (tma_epi && ep.resid) ? 1 : 0;
   if (tma_epi) {
-    if (N <= 128) return launch_gemm<128, 4, true>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
-    return launch_gemm<256, 3, true>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
+    if (N <= 128) return launch_gemm<128, 4, true, false>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
+    // 256-row tiles on SM pairs once there are enough rows to keep the pairs busy
+    if (g_gemm_pairs && M > 2 * kBM)
+      return launch_gemm<256, 5, true, true>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
+    return launch_gemm<256, 3, true, false>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
   }
-  if (N <= 128) return launch_gemm<128, 6, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
-  return launch_gemm<256, 4, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
+  if (N <= 128) return launch_gemm<128, 6, false, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
+  return launch_gemm<256, 4, false, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
 }
+
+void set_gemm_pairs(bool on) { g_gemm_pairs = on; }
 
 }  // namespace s3b

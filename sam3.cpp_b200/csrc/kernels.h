@@ -72,6 +72,8 @@ struct EpiParams {
 // K-major. lda, ldb multiples of 8; pointers 16-byte aligned.
 int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
              const EpiParams& ep, int* err, cudaStream_t st);
+// Process-wide: whether wide TMA-epilogue GEMMs use 256-row tiles on SM pairs (default on).
+void set_gemm_pairs(bool on);
 
 // Flash attention (online softmax, f16 in / f32 acc / f16 out).
 struct AttnParams {

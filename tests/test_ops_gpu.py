@@ -40,6 +40,33 @@ def test_gemm(engine, M, N, K, act):
     assert err < tol, f"max abs err {err} (tol {tol})"
 
 
+@pytest.mark.parametrize("pairs", [0, 1])
+@pytest.mark.parametrize("M,N,K,resid", [(41472 // 8 + 130, 3072, 1024, False), (1000, 4736, 1024, False),
+                                         (5184, 1024, 4736, True), (4097, 288, 152, True), (257, 512, 64, True)])
+def test_gemm_pairs_and_single(engine, pairs, M, N, K, resid):
+    """256-row tiles on SM pairs (cta_group::2) and 128-row tiles on single SMs, with ragged M / N / K
+    tails, f16 and f32 (in-place residual) outputs, against the fp32 reference."""
+    engine.set_option("gemm_pairs", pairs)
+    try:
+        g = torch.Generator(device="cuda").manual_seed(M + N + K + pairs)
+        A = (torch.randn(M, K, device="cuda", generator=g) * 0.5).half()
+        B = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
+        bias = torch.randn(N, device="cuda", generator=g) * 0.1
+        if resid:
+            out = torch.randn(M, N, device="cuda", generator=g)
+            ref = out + A.float() @ B.float().T + bias
+            engine.gemm(A, B, out, bias=bias, resid=out)
+        else:
+            out = torch.empty(M, N, device="cuda", dtype=torch.float16)
+            ref = A.float() @ B.float().T + bias
+            engine.gemm(A, B, out, bias=bias)
+        engine.sync()
+        err = (out.float() - ref).abs().max().item()
+        assert err < 2e-3 * max(1.0, ref.abs().max().item()) + 1e-4 * K ** 0.5 + (0 if resid else 1e-2), err
+    finally:
+        engine.set_option("gemm_pairs", 1)
+
+
 @pytest.mark.parametrize("M,N,K", [(5184, 1024, 1024), (1000, 96, 256), (333, 1024, 4736)])
 def test_gemm_inplace_residual(engine, M, N, K):
     """out += A B^T + bias with the residual being the output itself (the
