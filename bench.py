@@ -242,6 +242,8 @@ def main():
     ap.add_argument("--workload", default="vit_q4_0", choices=["vit_q4_0", "vit_q8_0", "vit_f16"])
     ap.add_argument("--frames", type=int, default=FRAMES_TOTAL)
     ap.add_argument("--frames-per-pass", type=int, default=8)
+    ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1],
+                    help="1: 256-row GEMM tiles on SM pairs (default); 0: 128-row tiles on single SMs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-hiera", action="store_true", help="skip the Hiera-T (configs[1]) measurement")
     args = ap.parse_args()
@@ -301,6 +303,7 @@ def main():
     gen_s = time.time() - t0
     eng = s3b.Engine(local)
     eng.set_option("frames_per_pass", args.frames_per_pass)
+    eng.set_option("gemm_pairs", args.gemm_pairs)
     t0 = time.time()
     eng.load_model(path)
     load_s = time.time() - t0

@@ -685,8 +685,10 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
   const int resid_in_place = (tma_epi && ep.resid) ? 1 : 0;
   if (tma_epi) {
     if (N <= 128) return launch_gemm<128, 4, true, false>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
-    // 256-row tiles on SM pairs once there are enough rows to keep the pairs busy
-    if (g_gemm_pairs && M > 2 * kBM)
+    // 256-row tiles on SM pairs where the main loop dominates (long K): measured faster for
+    // K = 4736 (ViT fc2), slower for K = 1024 GEMMs whose epilogue (GELU, RoPE, residual)
+    // already takes longer than their main loop
+    if (g_gemm_pairs && M > 2 * kBM && K >= 2048)
       return launch_gemm<256, 5, true, true>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
     return launch_gemm<256, 3, true, false>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
   }
