@@ -68,6 +68,8 @@ int s3b_sync(s3b_ctx* ctx);
  * "gemm_pairs" (1, default: the wide GEMMs run 256-row tiles on pairs of
  * SMs, tcgen05 cta_group::2; 0: 128-row tiles on single SMs; applies to
  * every context of the process);
+ * "gemm_wide_epilogue" (1, default: short-K GEMMs with f16 outputs run 16
+ * epilogue warps; 0: 8; process-wide);
  * "attention_exp_poly" (0-4: of every 8 softmax exponentials in the tcgen05
  * kernel, how many are evaluated by a polynomial on the FMA pipe instead of
  * the MUFU unit; a tuning knob, results agree to f16 rounding);

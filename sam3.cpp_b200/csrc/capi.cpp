@@ -249,6 +249,11 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     set_gemm_pairs(value != 0);
     return kOk;
   }
+  if (k == "gemm_wide_epilogue") {
+    if (value < 0 || value > 1) return set_error(ctx, kErrArg, "gemm_wide_epilogue must be 0 or 1");
+    set_gemm_wide_epilogue(value != 0);
+    return kOk;
+  }
   if (k == "attention_exp_poly") {
     if (value < 0 || value > 4) return set_error(ctx, kErrArg, "attention_exp_poly must be in [0, 4]");
     ctx->attention_exp_poly = (int)value;

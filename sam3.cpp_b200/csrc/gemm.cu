@@ -37,11 +37,12 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + kEpiWarps * 32;
+// threads of a CTA with `ew` epilogue warps (plus the TMA and MMA warps)
+constexpr int gemm_threads(int ew) { return 64 + 32 * ew; }
 constexpr uint32_t kStageBufBytes = 16384;  // 128 rows x 128 B
 
-bool g_gemm_pairs = true;  // 256-row tiles on SM pairs for the wide TMA-epilogue GEMMs
+bool g_gemm_pairs = true;     // 256-row tiles on SM pairs for the wide TMA-epilogue GEMMs
+bool g_gemm_wide_epi = true;  // 16 epilogue warps for short-K GEMMs with f16 outputs
 
 
 // Two f32 -> one packed f16x2 register (lo in the low half), round to nearest even.
@@ -231,6 +232,7 @@ __device__ __forceinline__ void tma_store_2d(const void* map, const void* src, i
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // PAIR: clusters of 2 CTAs on two SMs share one 256 x BN tile (cta_group::2):
@@ -241,8 +243,10 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // on the leader's `full` barrier; the leader's commits arrive on `empty` /
 // `tfull` of both CTAs; both epilogues release accumulators on the leader's
 // `tempty`.
-template <int BN, int STAGES, bool TMA_EPI, bool PAIR>
-__global__ void __launch_bounds__(kThreads, 1)
+// EW: epilogue warps, 8 (2 column groups) or 16 (4 column groups, for epilogues
+// that would otherwise outlast the main loop).
+template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW>
+__global__ void __launch_bounds__(gemm_threads(EW), 1)
     gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, int M, int N, int K, EpiParams ep,
                        int resid_in_place, int* err) {
@@ -287,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], PAIR ? 2 * kEpiWarps : kEpiWarps);
+      mbar_init(&tempty[a], PAIR ? 2 * EW : EW);
     }
     mbar_init(mma_done, 1);
     for (int i = 0; i < 4; ++i) mbar_init(&rfull[i], 1);
@@ -388,28 +392,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
+    // Epilogue: EW warps in G = EW/4 column groups; the 4 warps of a group cover
+    // the 4 TMEM lane quarters (the tile's 128 rows) of the group's CG columns.
+    // The 4 staging buffers (16 KB) are split NBUF per group.
+    constexpr int G = EW / 4;
+    constexpr int CG = BN / G;
+    constexpr int NBUF = 4 / G;
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int grp = (warp - 2) >> 2;
     const int row = q * 32 + lane;
-    const bool leader = (warp - 2) == 4 * half && lane == 0;  // issues this half's TMA copies
+    const bool leader = ((warp - 2) & 3) == 0 && lane == 0;  // issues this group's TMA copies
     int acc = 0;
     uint32_t aphase = 0;
     uint32_t chunk_ctr = 0;
     uint32_t r_issued0 = 0, r_issued1 = 0, r_used0 = 0, r_used1 = 0;  // residual loads per staging buffer
-    const int cw = ep.out_f32 ? 32 : 64;                // chunk = 128 B of columns: 32 f32 or 64 f16
+    // the 16-warp variant serves f16 outputs without a residual only (fewer live registers)
+    constexpr bool kF16Only = EW == 16;
+    const bool out_f32 = kF16Only ? false : (ep.out_f32 != 0);
+    const int rip = kF16Only ? 0 : resid_in_place;
+    const int cw = out_f32 ? 32 : 64;                   // chunk = 128 B of columns: 32 f32 or 64 f16
+    // staging buffer of chunk `ctr`, and how many chunks used that buffer before it
+    auto buf_of = [&](uint32_t ctr) -> int { return grp * NBUF + (NBUF == 1 ? 0 : (int)(ctr & 1)); };
+    auto buf_uses = [&](uint32_t ctr) -> uint32_t { return NBUF == 1 ? ctr : (ctr >> 1); };
+    // the TMA store that last used the buffer has read it
+    auto wait_buf_read = [&]() {
+      if (NBUF == 1) bulk_wait_read0(); else bulk_wait_read1();
+    };
     // Residual chunk `ctr` (columns gcb.., rows m0..) -> its staging buffer, once
     // the TMA store that last used that buffer has finished reading it.
     auto issue_resid = [&](uint32_t ctr, int gcb, int m0) {
-      const int b = (int)(ctr & 1);
-      const int bsel = half * 2 + b;
-      bulk_wait_read1();
+      const int bsel = buf_of(ctr);
+      wait_buf_read();
       if (gcb < N) {
         mbar_arrive_expect_tx(&rfull[bsel], kStageBufBytes);
         tma_load_2d(&tmC, &rfull[bsel], sC + bsel * kStageBufBytes, gcb, m0);
       } else {
         mbar_arrive(&rfull[bsel]);
       }
-      if (b) ++r_issued1; else ++r_issued0;
+      if (NBUF == 1 || !(ctr & 1)) ++r_issued0; else ++r_issued1;
     };
     // this CTA's epilogue warps release an accumulator on the MMA-issuing CTA's barrier
     auto release_acc = [&](int a) {
@@ -422,93 +442,102 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = (t / tiles_n) * TM + (int)rank * kBM;
       const int n0 = (t % tiles_n) * BN;
       // the first residual chunk does not depend on the accumulator: fetch it during the main loop
-      if (TMA_EPI && resid_in_place && leader) issue_resid(chunk_ctr, n0 + half * (BN / 2), m0);
+      if (TMA_EPI && rip && leader) issue_resid(chunk_ctr, n0 + grp * CG, m0);
       if (!mbar_wait(&tfull[acc], aphase, s_abort, err, kErrWaitTmemFull)) break;
       tc_fence_after();
       const long long gr = (long long)m0 + row;
       const int rope_pos = (ep.rope && gr < ep.rope_rows) ? (int)(gr % ep.rope_mod) : -1;
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * (BN / 2));
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + grp * CG);
       if (TMA_EPI) {
         bool ok = true;
-        for (int c0 = 0; c0 < BN / 2; c0 += cw) {
-          const int gcb = n0 + half * (BN / 2) + c0;
-          const int bsel = half * 2 + (int)(chunk_ctr & 1);
+        for (int c0 = 0; c0 < CG; c0 += cw) {
+          const int gcb = n0 + grp * CG + c0;
+          const int bsel = buf_of(chunk_ctr);
           uint8_t* buf = sC + bsel * kStageBufBytes;
-          uint32_t r[64];
+          // the chunk goes through registers 32 columns at a time; the first 32 are
+          // loaded from TMEM while the staging buffer is awaited
+          uint32_t r[32];
           TMEM_LD16(tbase + (uint32_t)c0, r, 0);
           TMEM_LD16(tbase + (uint32_t)(c0 + 16), r, 16);
-          if (cw == 64) {
-            TMEM_LD16(tbase + (uint32_t)(c0 + 32), r, 32);
-            TMEM_LD16(tbase + (uint32_t)(c0 + 48), r, 48);
-          }
-          tc_wait_ld();
-          if (c0 + cw >= BN / 2) {
-            // accumulator fully read: hand TMEM back to the MMA warp early
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) release_acc(acc);
-          }
-          if (resid_in_place) {
+          if (rip) {
             // parity of this buffer's residual barrier = number of its earlier uses & 1
-            if (!mbar_wait(&rfull[bsel], (chunk_ctr >> 1) & 1u, s_abort, err, kErrWaitMisc)) { ok = false; break; }
-            if (chunk_ctr & 1) ++r_used1; else ++r_used0;
+            if (!mbar_wait(&rfull[bsel], buf_uses(chunk_ctr) & 1u, s_abort, err, kErrWaitMisc)) {
+              tc_wait_ld();
+              ok = false;
+              break;
+            }
+            if (NBUF == 1 || !(chunk_ctr & 1)) ++r_used0; else ++r_used1;
           } else {
-            if (leader) bulk_wait_read1();  // the store that last used `buf` has read it
-            named_bar(1 + half, 128);
+            if (leader) wait_buf_read();
+            named_bar(1 + grp, 128);
           }
           uint8_t* rowp = buf + row * 128;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (j * 16 < cw) {
-              float v[16];
+          for (int s0 = 0; s0 < 64; s0 += 32) {
+            if (s0 < cw) {
+              if (s0 > 0) {
+                TMEM_LD16(tbase + (uint32_t)(c0 + s0), r, 0);
+                TMEM_LD16(tbase + (uint32_t)(c0 + s0 + 16), r, 16);
+              }
+              tc_wait_ld();
+              if (c0 + cw >= CG && s0 + 32 >= cw) {
+                // accumulator fully read: hand TMEM back to the MMA warp early
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) release_acc(acc);
+              }
 #pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[j * 16 + i]);
-              const int gc = gcb + j * 16;
-              if (gc < N) epi_math16(ep, rope_pos, gc, N, v);
-              if (ep.out_f32) {
+              for (int j = 0; j < 2; ++j) {
+                float v[16];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  const int unit = j * 4 + u;  // 16-byte unit within the 128-byte row
-                  float4* sp = reinterpret_cast<float4*>(rowp + ((unit ^ (row & 7)) << 4));
-                  if (resid_in_place) {
-                    const float4 rv = *sp;
-                    v[4 * u] += rv.x; v[4 * u + 1] += rv.y; v[4 * u + 2] += rv.z; v[4 * u + 3] += rv.w;
+                for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[j * 16 + i]);
+                const int gc = gcb + s0 + j * 16;
+                if (gc < N) epi_math16(ep, rope_pos, gc, N, v);
+                if (out_f32) {
+#pragma unroll
+                  for (int u = 0; u < 4; ++u) {
+                    const int unit = (s0 + j * 16) / 4 + u;  // 16-byte unit within the 128-byte row
+                    float4* sp = reinterpret_cast<float4*>(rowp + ((unit ^ (row & 7)) << 4));
+                    if (rip) {
+                      const float4 rv = *sp;
+                      v[4 * u] += rv.x; v[4 * u + 1] += rv.y; v[4 * u + 2] += rv.z; v[4 * u + 3] += rv.w;
+                    }
+                    *sp = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
                   }
-                  *sp = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-                }
-              } else {
+                } else {
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                  const int unit = j * 2 + u;
-                  *reinterpret_cast<uint4*>(rowp + ((unit ^ (row & 7)) << 4)) =
-                      make_uint4(pack_h2(v[8 * u], v[8 * u + 1]), pack_h2(v[8 * u + 2], v[8 * u + 3]),
-                                 pack_h2(v[8 * u + 4], v[8 * u + 5]), pack_h2(v[8 * u + 6], v[8 * u + 7]));
+                  for (int u = 0; u < 2; ++u) {
+                    const int unit = (s0 + j * 16) / 8 + u;
+                    *reinterpret_cast<uint4*>(rowp + ((unit ^ (row & 7)) << 4)) =
+                        make_uint4(pack_h2(v[8 * u], v[8 * u + 1]), pack_h2(v[8 * u + 2], v[8 * u + 3]),
+                                   pack_h2(v[8 * u + 4], v[8 * u + 5]), pack_h2(v[8 * u + 6], v[8 * u + 7]));
+                  }
                 }
               }
             }
           }
           fence_proxy_async_smem();
-          named_bar(1 + half, 128);
+          named_bar(1 + grp, 128);
           if (leader && gcb < N) {
             tma_store_2d(&tmC, buf, gcb, m0);
             bulk_commit();
           }
-          if (resid_in_place && leader && c0 + cw < BN / 2) issue_resid(chunk_ctr + 1, gcb + cw, m0);
+          if (rip && leader && c0 + cw < CG) issue_resid(chunk_ctr + 1, gcb + cw, m0);
           ++chunk_ctr;
         }
         if (!ok) break;
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 16) {
+        for (int c = 0; c < CG; c += 16) {
           uint32_t r[16];
           TMEM_LD16(tbase + (uint32_t)c, r, 0);
           tc_wait_ld();
-          if (c + 16 >= BN / 2) {
+          if (c + 16 >= CG) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) release_acc(acc);
           }
-          const int gc = n0 + half * (BN / 2) + c;
+          const int gc = n0 + grp * CG + c;
           if (gr < M && gc < N) {
             float v[16];
 #pragma unroll
@@ -523,8 +552,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (TMA_EPI && leader) {
       bulk_wait_all();
       // a residual load issued but never consumed (only after an abort) lands before exit
-      if (r_issued0 > r_used0) mbar_wait_drain(&rfull[half * 2 + 0], (r_issued0 - 1) & 1u, err);
-      if (r_issued1 > r_used1) mbar_wait_drain(&rfull[half * 2 + 1], (r_issued1 - 1) & 1u, err);
+      if (r_issued0 > r_used0) mbar_wait_drain(&rfull[grp * NBUF + 0], (r_issued0 - 1) & 1u, err);
+      if (NBUF == 2 && r_issued1 > r_used1) mbar_wait_drain(&rfull[grp * NBUF + 1], (r_issued1 - 1) & 1u, err);
     }
   }
 
@@ -576,7 +605,7 @@ int make_map_2d(CUtensorMap* map, const void* base, long long rows, long long co
   return r == CUDA_SUCCESS ? 0 : -12;
 }
 
-template <int BN, int STAGES, bool TMA_EPI, bool PAIR>
+template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW = 8>
 int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
                 const EpiParams& ep, int resid_in_place, int* err, cudaStream_t st) {
   constexpr int BN_CTA = PAIR ? BN / 2 : BN;
@@ -594,7 +623,8 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
   constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN_CTA) * kBK * 2 + (TMA_EPI ? 4 * kStageBufBytes : 0) +
                           (2 * STAGES + 9) * 8 + 16;
   static_assert(smem <= 232448, "shared memory per CTA");
-  auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR>;
+  auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR, EW>;
+  constexpr int kThreads = gemm_threads(EW);
   static bool attr_set = false;
   static int max_units = 0;  // co-resident CTAs (or pairs)
   if (!attr_set) {
@@ -685,6 +715,10 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
   const int resid_in_place = (tma_epi && ep.resid) ? 1 : 0;
   if (tma_epi) {
     if (N <= 128) return launch_gemm<128, 4, true, false>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
+    // f16 outputs of short-K GEMMs (QKV + RoPE, MLP fc1 + GELU): their epilogue outlasts the main loop
+    // with 8 epilogue warps, so they run 16
+    if (!resid_in_place && !ep.out_f32 && K < 2048 && g_gemm_wide_epi)
+      return launch_gemm<256, 3, true, false, 16>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
     // 256-row tiles on SM pairs where the main loop dominates (long K): measured faster for
     // K = 4736 (ViT fc2), slower for K = 1024 GEMMs whose epilogue (GELU, RoPE, residual)
     // already takes longer than their main loop
@@ -697,5 +731,6 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
 }
 
 void set_gemm_pairs(bool on) { g_gemm_pairs = on; }
+void set_gemm_wide_epilogue(bool on) { g_gemm_wide_epi = on; }
 
 }  // namespace s3b

@@ -74,6 +74,8 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
              const EpiParams& ep, int* err, cudaStream_t st);
 // Process-wide: whether wide TMA-epilogue GEMMs use 256-row tiles on SM pairs (default on).
 void set_gemm_pairs(bool on);
+// Process-wide: whether short-K GEMMs with f16 outputs use 16 epilogue warps (default on).
+void set_gemm_wide_epilogue(bool on);
 
 // Flash attention (online softmax, f16 in / f32 acc / f16 out).
 struct AttnParams {

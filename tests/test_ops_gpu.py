@@ -67,6 +67,54 @@ def test_gemm_pairs_and_single(engine, pairs, M, N, K, resid):
         engine.set_option("gemm_pairs", 1)
 
 
+@pytest.mark.parametrize("wide", [0, 1])
+@pytest.mark.parametrize("M,N,K,act", [(5184, 4736, 1024, 1), (1000, 3072, 256, 0), (777, 288, 96, 2),
+                                       (130, 1000, 1024, 3)])
+def test_gemm_f16_epilogue_warps(engine, wide, M, N, K, act):
+    """f16-output GEMMs with 8 or 16 epilogue warps (column groups of 128 or 64), ragged M / N."""
+    engine.set_option("gemm_wide_epilogue", wide)
+    try:
+        g = torch.Generator(device="cuda").manual_seed(M * 3 + N + act)
+        A = (torch.randn(M, K, device="cuda", generator=g) * 0.5).half()
+        B = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
+        bias = torch.randn(N, device="cuda", generator=g) * 0.1
+        out = torch.full((M, N), 3.0, device="cuda", dtype=torch.float16)
+        engine.gemm(A, B, out, bias=bias, act=act)
+        engine.sync()
+        ref = _ref_gemm(A, B, bias, act, None)
+        assert (out.float() - ref).abs().max().item() < 1e-2 * max(1.0, ref.abs().max().item())
+    finally:
+        engine.set_option("gemm_wide_epilogue", 1)
+
+
+@pytest.mark.parametrize("wide", [0, 1])
+def test_gemm_rope_epilogue_warps(engine, wide):
+    """QKV-shaped GEMM with RoPE on q, k (ViT window layout) with 8 or 16 epilogue warps."""
+    engine.set_option("gemm_wide_epilogue", wide)
+    try:
+        M, E, HD = 576 * 9, 1024, 64
+        g = torch.Generator(device="cuda").manual_seed(11)
+        A = torch.randn(M, E, device="cuda", generator=g).half()
+        B = (torch.randn(3 * E, E, device="cuda", generator=g) * 0.03).half()
+        bias = torch.randn(3 * E, device="cuda", generator=g) * 0.1
+        ang = torch.rand(576, HD // 2, device="cuda", generator=g) * 6.28
+        table = torch.stack([ang.cos(), ang.sin()], -1).contiguous()
+        out = torch.empty(M, 3 * E, device="cuda", dtype=torch.float16)
+        engine.gemm_rope(A, B, out, bias, table, HD, 2 * E, 576)
+        engine.sync()
+        y = A.float() @ B.float().T + bias
+        pos = torch.arange(M, device="cuda") % 576
+        c = table[pos, :, 0].repeat(1, 2 * E // HD)
+        s = table[pos, :, 1].repeat(1, 2 * E // HD)
+        a, b = y[:, 0:2 * E:2], y[:, 1:2 * E:2]
+        ref = y.clone()
+        ref[:, 0:2 * E:2] = a * c - b * s
+        ref[:, 1:2 * E:2] = a * s + b * c
+        assert (out.float() - ref).abs().max().item() < 2e-2
+    finally:
+        engine.set_option("gemm_wide_epilogue", 1)
+
+
 @pytest.mark.parametrize("M,N,K", [(5184, 1024, 1024), (1000, 96, 256), (333, 1024, 4736)])
 def test_gemm_inplace_residual(engine, M, N, K):
     """out += A B^T + bias with the residual being the output itself (the
