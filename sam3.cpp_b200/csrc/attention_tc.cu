@@ -2,19 +2,27 @@
 // ViT windowed and global attention of sam3_vit_block_forward
 // (ggml_flash_attn_ext at sam3.cpp:3774; softmax(q k^T / 8) v, no mask).
 //
-// One CTA = one 128-query tile of one (window, head); 6 warps, 2 CTAs / SM:
+// One CTA = one 128-query tile of one (window, head); 10 warps, 2 CTAs / SM:
 //   warp 0     TMA: Q tile once, then K_j, V_j through a 3-slot ring. The
 //              tensor map is 3-D (channels, token, window) over the fused
 //              [tokens][3E] qkv buffer, so a tile never reads another window
 //              (rows past the window are zero-filled by TMA).
 //   warp 1     MMA: S = Q K_j^T (M=128, N=128, K=64) into TMEM; after the
-//              softmax wrote P_j: O_j = P_j V_j (M=128, N=64, K=128, V as an
-//              MN-major operand) into one of two TMEM O buffers.
-//   warps 2-5  softmax, one query row per thread (TMEM lane): two passes over
-//              the S row (max, then exp2 / sum / f16 P into 128B-swizzled
-//              shared memory), and the running output kept in registers:
-//              acc = acc * 2^(m_old - m_new) + O_j.
-// Every wait is bounded; a timeout records an error code and unwinds.
+//              softmax wrote P_j: O += P_j V_j (M=128, N=64, K=128, V as an
+//              MN-major operand) into one TMEM accumulator kept across tiles.
+//   warps 2-9  softmax. Each query row (TMEM lane) is shared by two threads,
+//              one per 64-key half of the tile: row max over its half (two
+//              32-column TMEM reads), one exchange of the partial maxima
+//              through shared memory, then p = 2^(s*scale*log2e - m) written
+//              as f16 into the 128B-swizzled A operand of the P V product.
+//              The reference max m only moves when the row max grows by more
+//              than 2^8 (so P <= 256, exact enough in f16); only then are the
+//              row's running sum and its O row in TMEM rescaled, which after
+//              the first tiles is rare. Each thread keeps its half's sum; the
+//              two are added once at the end, when O is read, divided by the
+//              sum and stored (32 columns per thread).
+// Every wait is bounded; a timeout records an error code and the CTA unwinds
+// without skipping any named barrier.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -27,7 +35,10 @@ constexpr int kBK = 128;
 constexpr int kSlots = 3;
 constexpr uint32_t kTileBytes = kBK * kD * 2;  // 16 KB: 128 rows x 128 B
 constexpr uint32_t kPBytes = kBQ * kBK * 2;    // 32 KB: two 128 x 64 swizzled halves
-constexpr int kThreads = 192;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kThreads = 64 + 32 * kSoftmaxWarps;
+constexpr float kLazyMax = 8.0f;  // log2 of the largest P value before the reference max moves
+constexpr int kXchgBytes = (2 * 2 * kBQ + 2 * kBQ) * 4;  // partial maxima (2 slots x 2 halves) + final sums
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -52,14 +63,13 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, for x <= 0 (the softmax exponent), to take part of the
-// exponentials off the MUFU unit, which bounds a d = 64 tile (16384 exp2 per
-// 128 x 128 tile against 2 x 2.1 MFLOP of MMA). Cody-Waite range reduction
-// x = n + f, n = rint(x) taken from the low mantissa bits of x + 1.5*2^23,
-// f in [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted here for minimum
-// maximum relative error on that interval (7.5e-5, below the f16 half ulp of
-// P); 2^n added to the exponent field. x is clamped at -126 so the exponent
-// stays in range (P rounds to 0 in f16 there anyway).
+// 2^x on the FMA pipe, for x <= 8 (the softmax exponent), to take part of the
+// exponentials off the MUFU unit. Cody-Waite range reduction x = n + f,
+// n = rint(x) taken from the low mantissa bits of x + 1.5*2^23, f in
+// [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted here for minimum maximum
+// relative error on that interval (7.5e-5, below the f16 half ulp of P); 2^n
+// added to the exponent field. x is clamped at -126 so the exponent stays in
+// range (P rounds to 0 in f16 there anyway).
 __device__ __forceinline__ float exp2_poly3(float x) {
   x = fmaxf(x, -126.f);
   const float j = x + 12582912.f;
@@ -74,6 +84,11 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   return r;
 }
 
+__device__ __forceinline__ void named_bar(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 #define TMEM_LD32(taddr, R)                                                                                  \
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "                                                     \
                "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"                                     \
@@ -84,6 +99,17 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
                  "=r"(R[21]), "=r"(R[22]), "=r"(R[23]), "=r"(R[24]), "=r"(R[25]), "=r"(R[26]), "=r"(R[27]),  \
                  "=r"(R[28]), "=r"(R[29]), "=r"(R[30]), "=r"(R[31])                                          \
                : "r"(taddr))
+
+#define TMEM_ST32(taddr, R)                                                                                  \
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "                                               \
+               "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"                                    \
+               "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),             \
+               "r"(R[0]), "r"(R[1]), "r"(R[2]), "r"(R[3]), "r"(R[4]), "r"(R[5]), "r"(R[6]), "r"(R[7]),       \
+               "r"(R[8]), "r"(R[9]), "r"(R[10]), "r"(R[11]), "r"(R[12]), "r"(R[13]), "r"(R[14]), "r"(R[15]), \
+               "r"(R[16]), "r"(R[17]), "r"(R[18]), "r"(R[19]), "r"(R[20]), "r"(R[21]), "r"(R[22]),           \
+               "r"(R[23]), "r"(R[24]), "r"(R[25]), "r"(R[26]), "r"(R[27]), "r"(R[28]), "r"(R[29]),           \
+               "r"(R[30]), "r"(R[31])                                                                        \
+               : "memory")
 
 __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err) {
   const unsigned long long t0 = globaltimer_ns();
@@ -113,7 +139,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* sQ = smem;                          // 16 KB
   uint8_t* sKV = sQ + kTileBytes;              // kSlots x 16 KB
   uint8_t* sP = sKV + kSlots * kTileBytes;     // 32 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  float* xmax = reinterpret_cast<float*>(sP + kPBytes);  // [2 slots][2 halves][128 rows]
+  float* xsum = xmax + 4 * kBQ;                          // [2 halves][128 rows]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xsum + 2 * kBQ);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;                // [kSlots]
   uint64_t* kv_empty = kv_full + kSlots;       // [kSlots]
@@ -121,9 +149,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* s_empty = s_full + 1;
   uint64_t* p_full = s_empty + 1;
   uint64_t* p_empty = p_full + 1;
-  uint64_t* o_full = p_empty + 1;              // [2]
-  uint64_t* o_empty = o_full + 2;              // [2]
-  uint64_t* mma_done = o_empty + 2;
+  uint64_t* o_done = p_empty + 1;
+  uint64_t* mma_done = o_done + 1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
@@ -142,13 +169,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&kv_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_empty, 4);
-    mbar_init(p_full, 4);
+    mbar_init(s_empty, kSoftmaxWarps);
+    mbar_init(p_full, kSoftmaxWarps);
     mbar_init(p_empty, 1);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&o_full[b], 1);
-      mbar_init(&o_empty[b], 4);
-    }
+    mbar_init(o_done, 1);
     mbar_init(mma_done, 1);
     *s_abort = 0;
     fence_mbar_init();
@@ -156,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     tma_prefetch_desc(&tm);
   }
   if (warp == 1) {
-    tmem_alloc(s_tmem, 256);  // S: columns [0,128), O buffers: [128,192), [192,256)
+    tmem_alloc(s_tmem, 256);  // S: columns [0,128), O: [128,192)
     tmem_relinquish();
   }
   tc_fence_before();
@@ -212,12 +236,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; j < nkb && ok; ++j) {
-        if (j + 1 < nkb && !issue_s(j + 1)) break;
-        // O_j = P_j V_j
-        const int t = 2 * j + 1, s = t % kSlots, ob = j & 1;
-        if (!mbar_wait(p_full, (uint32_t)j & 1, s_abort, err, kErrWaitMisc)) break;
-        if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) break;
-        if (j >= 2 && !mbar_wait(&o_empty[ob], (uint32_t)((j - 2) >> 1) & 1, s_abort, err, kErrWaitMisc)) break;
+        if (j + 1 < nkb && !issue_s(j + 1)) { ok = false; break; }
+        // O += P_j V_j (after the softmax wrote P_j and, where needed, rescaled O)
+        const int t = 2 * j + 1, s = t % kSlots;
+        if (!mbar_wait(p_full, (uint32_t)j & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
+        if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
         tc_fence_after();
         const uint32_t pa = smem_u32(sP), va = smem_u32(sKV + s * kTileBytes);
         // K steps that hold a real key (the softmax writes P only up to the chunk holding the last key)
@@ -228,44 +251,45 @@ __global__ void __launch_bounds__(kThreads, 2)
           // P: two 128 x 64 K-major halves (32 B per K step inside a half); V: 16 key rows = 2048 B per K step
           const uint64_t dp = sdesc_k_sw128(pa + (uint32_t)((kk >> 2) * (kBQ * 128) + (kk & 3) * 32));
           const uint64_t dv = sdesc_mn_sw128(va + (uint32_t)(kk * 2048));
-          tc_mma_f16(tmem + 128 + ob * 64, dp, dv, idesc_o, kk != 0);
+          tc_mma_f16(tmem + 128, dp, dv, idesc_o, (j > 0 || kk != 0) ? 1u : 0u);
         }
-        tc_commit(&o_full[ob]);
         tc_commit(&kv_empty[s]);
         tc_commit(p_empty);
       }
+      if (ok) tc_commit(o_done);
       if (issued) {
         tc_commit(mma_done);
         mbar_wait_drain(mma_done, 0, err);
       }
     }
   } else {
-    // softmax warps: warp w owns TMEM lanes 32*(w%4) .. +31 = query rows
+    // softmax: warp w owns TMEM lanes 32*(w%4) .. +31 (query rows) and key half hsel of every tile
     const int q4 = warp & 3;
+    const int hsel = (warp - 2) >> 2;
     const int row = q4 * 32 + lane;
+    const int cbase = hsel * (kBK / 2);
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    float acc[kD];
-#pragma unroll
-    for (int i = 0; i < kD; ++i) acc[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    const uint32_t o_addr = tmem + lane_off + 128 + (uint32_t)(hsel * (kD / 2));
     // a warp whose 32 query rows are all tiling padding only keeps the barrier protocol
     const bool rows_live = qb * kBQ + q4 * 32 < a.ntok;
+    float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkb && ok; ++j) {
-      if (!mbar_wait(s_full, (uint32_t)j & 1, s_abort, err, kErrWaitTmemFull)) { ok = false; break; }
+    for (int j = 0; j < nkb; ++j) {  // every softmax warp runs every iteration (named barriers)
+      if (ok) ok = mbar_wait(s_full, (uint32_t)j & 1, s_abort, err, kErrWaitTmemFull);
+      ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
       const int kvalid = a.ntok - j * kBK;  // keys at or past this count are tiling padding
-      float alpha = 1.f;
-      if (rows_live) {
-        // pass 1: row max (4 independent chains; 32-key chunks past the last key are skipped)
+      // partial row max over this thread's key half (4 independent chains)
+      float pm = -INFINITY;
+      if (ok && rows_live) {
         float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kBK; c += 32) {
-          if (c >= kvalid) break;
+        for (int c = 0; c < kBK / 2; c += 32) {
+          if (cbase + c >= kvalid) break;
           uint32_t r[32];
-          TMEM_LD32(tmem + lane_off + (uint32_t)c, r);
+          TMEM_LD32(tmem + lane_off + (uint32_t)(cbase + c), r);
           tc_wait_ld();
-          if (c + 32 <= kvalid) {
+          if (cbase + c + 32 <= kvalid) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
               mx0 = fmaxf(mx0, __uint_as_float(r[i]));
@@ -276,48 +300,74 @@ __global__ void __launch_bounds__(kThreads, 2)
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (c + i < kvalid) mx0 = fmaxf(mx0, __uint_as_float(r[i]));
+              if (cbase + c + i < kvalid) mx0 = fmaxf(mx0, __uint_as_float(r[i]));
           }
         }
-        const float m_new = fmaxf(m, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.sl2);
-        alpha = ex2(m - m_new);
-        m = m_new;
+        pm = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.sl2;
       }
-      // P buffer free (the previous P V has read it)
-      if (j > 0 && !mbar_wait(p_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
-      if (rows_live) {
-        // pass 2: p = 2^(s*sl2 - m), row sum, f16 P into the swizzled A-operand layout; padding keys
-        // inside the last chunk get p = 0 (the P V product reads up to the end of that chunk)
+      // exchange the partial maxima of the two halves of each row (slot j & 1 is rewritten
+      // two tiles later, after the partner has passed the next barrier)
+      xmax[((j & 1) * 2 + hsel) * kBQ + row] = pm;
+      named_bar(1, 32 * kSoftmaxWarps);
+      const float m_tile = fmaxf(pm, xmax[((j & 1) * 2 + (hsel ^ 1)) * kBQ + row]);
+      // lazy reference max: move it only when the row max grows by more than 2^kLazyMax
+      // (always at the first tile); both threads of a row take the same decision
+      float alpha = 1.f;
+      bool resc = false;
+      if (m_tile > m_ref + kLazyMax) {
+        alpha = ex2(m_ref - m_tile);  // 0 at the first tile
+        resc = j > 0;
+        m_ref = m_tile;
+        l *= alpha;
+      }
+      // P buffer free and O final for tile j-1 (the previous P V has completed)
+      if (ok && j > 0) ok = mbar_wait(p_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok && rows_live) {
+        tc_fence_after();
+        // p = 2^(s*sl2 - m_ref), row sum, f16 P into the swizzled A operand (half hsel of sP);
+        // padding keys inside the last chunk get p = 0 (the P V product reads up to its end)
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        uint8_t* prow = sP + hsel * (kBQ * 128) + row * 128;
 #pragma unroll
-        for (int c = 0; c < kBK; c += 32) {
-          if (c >= kvalid) break;
+        for (int c = 0; c < kBK / 2; c += 32) {
+          if (cbase + c >= kvalid) break;
           uint32_t r[32];
-          TMEM_LD32(tmem + lane_off + (uint32_t)c, r);
+          TMEM_LD32(tmem + lane_off + (uint32_t)(cbase + c), r);
           tc_wait_ld();
-          const bool whole = c + 32 <= kvalid;
-          uint8_t* half = sP + (c >> 6) * (kBQ * 128) + row * 128;
+          const bool whole = cbase + c + 32 <= kvalid;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             float p[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               const int i = 8 * u + e;
-              const float x = fmaf(__uint_as_float(r[i]), a.sl2, -m);
-              p[e] = (whole || c + i < kvalid) ? (e < NPOLY ? exp2_poly3(x) : ex2(x)) : 0.f;
+              const float x = fmaf(__uint_as_float(r[i]), a.sl2, -m_ref);
+              p[e] = (whole || cbase + c + i < kvalid) ? (e < NPOLY ? exp2_poly3(x) : ex2(x)) : 0.f;
             }
             s0 += p[0] + p[4];
             s1 += p[1] + p[5];
             s2 += p[2] + p[6];
             s3 += p[3] + p[7];
-            const int unit = ((c & 63) >> 3) + u;  // 16-byte unit (8 keys) inside the 128-byte row
-            *reinterpret_cast<uint4*>(half + ((unit ^ (row & 7)) << 4)) =
+            const int unit = (c >> 3) + u;  // 16-byte unit (8 keys) inside the 128-byte row
+            *reinterpret_cast<uint4*>(prow + ((unit ^ (row & 7)) << 4)) =
                 make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
           }
         }
-        l = l * alpha + ((s0 + s1) + (s2 + s3));
+        l += (s0 + s1) + (s2 + s3);
+        // the reference max moved: rescale this thread's 32 columns of the row's running O
+        if (__any_sync(0xffffffffu, resc)) {
+          uint32_t o[32];
+          TMEM_LD32(o_addr, o);
+          tc_wait_ld();
+          const float f = resc ? alpha : 1.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          TMEM_ST32(o_addr, o);
+          tc_wait_st();
+        }
       }
-      // S row fully read; P written
+      // S read, P written, O rescaled: hand all three to the MMA warp
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
@@ -325,52 +375,30 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_arrive(s_empty);
         mbar_arrive(p_full);
       }
-      // fold O_{j-1} into the register accumulator
-      if (j > 0) {
-        const int ob = (j - 1) & 1;
-        if (!mbar_wait(&o_full[ob], (uint32_t)((j - 1) >> 1) & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
-        tc_fence_after();
-        if (rows_live) {
-          uint32_t r[32];
-#pragma unroll
-          for (int c = 0; c < kD; c += 32) {
-            TMEM_LD32(tmem + lane_off + 128 + ob * 64 + (uint32_t)c, r);
-            tc_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) acc[c + i] = fmaf(acc[c + i], alpha_prev, __uint_as_float(r[i]));
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&o_empty[ob]);
-      }
-      alpha_prev = alpha;
     }
+    // all P V products complete
+    if (ok) ok = mbar_wait(o_done, 0, s_abort, err, kErrWaitMisc);
+    ok = __all_sync(0xffffffffu, ok);
+    xsum[hsel * kBQ + row] = l;
+    named_bar(1, 32 * kSoftmaxWarps);
+    const float lt = l + xsum[(hsel ^ 1) * kBQ + row];
     if (ok && rows_live) {
-      const int ob = (nkb - 1) & 1;
-      if (mbar_wait(&o_full[ob], (uint32_t)((nkb - 1) >> 1) & 1, s_abort, err, kErrWaitMisc)) {
-        tc_fence_after();
-        uint32_t r[32];
+      tc_fence_after();
+      uint32_t o[32];
+      TMEM_LD32(o_addr, o);
+      tc_wait_ld();
+      const int qi = qb * kBQ + row;
+      if (qi < a.ntok) {
+        const long long orow = map_row(a.omap, (long long)w * a.ntok + qi);
+        if (orow >= 0) {
+          const float inv = 1.0f / lt;
+          uint4* op = reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * kD + hsel * (kD / 2));
 #pragma unroll
-        for (int c = 0; c < kD; c += 32) {
-          TMEM_LD32(tmem + lane_off + 128 + ob * 64 + (uint32_t)c, r);
-          tc_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c + i] = fmaf(acc[c + i], alpha_prev, __uint_as_float(r[i]));
-        }
-        const int qi = qb * kBQ + row;
-        if (qi < a.ntok) {
-          const long long orow = map_row(a.omap, (long long)w * a.ntok + qi);
-          if (orow >= 0) {
-            const float inv = 1.0f / l;
-            uint4* op = reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * kD);
-#pragma unroll
-            for (int u = 0; u < kD / 8; ++u)
-              op[u] = make_uint4(pack_h2(acc[8 * u] * inv, acc[8 * u + 1] * inv),
-                                 pack_h2(acc[8 * u + 2] * inv, acc[8 * u + 3] * inv),
-                                 pack_h2(acc[8 * u + 4] * inv, acc[8 * u + 5] * inv),
-                                 pack_h2(acc[8 * u + 6] * inv, acc[8 * u + 7] * inv));
-          }
+          for (int u = 0; u < 4; ++u)
+            op[u] = make_uint4(pack_h2(__uint_as_float(o[8 * u]) * inv, __uint_as_float(o[8 * u + 1]) * inv),
+                               pack_h2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv),
+                               pack_h2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv),
+                               pack_h2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv));
         }
       }
     }
@@ -424,7 +452,7 @@ int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v
   a.o_n = o_n;
   a.omap = omap;
   a.sl2 = scale * 1.4426950408889634f;
-  constexpr size_t smem = 1024 + kTileBytes * (1 + kSlots) + kPBytes + 16 * 8 + 16;
+  constexpr size_t smem = 1024 + kTileBytes * (1 + kSlots) + kPBytes + kXchgBytes + 16 * 8 + 16;
   static bool attr[5] = {false, false, false, false, false};
   const KernelFn kfn = kernels[exp_poly];
   if (!attr[exp_poly]) {
