@@ -242,8 +242,8 @@ def main():
     ap.add_argument("--workload", default="vit_q4_0", choices=["vit_q4_0", "vit_q8_0", "vit_f16"])
     ap.add_argument("--frames", type=int, default=FRAMES_TOTAL)
     ap.add_argument("--frames-per-pass", type=int, default=8)
-    ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1],
-                    help="1: 256-row GEMM tiles on SM pairs (default); 0: 128-row tiles on single SMs")
+    ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1, 2],
+                    help="256-row GEMM tiles on SM pairs: 1 (default) for K >= 2048, 2 for all, 0 never")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-hiera", action="store_true", help="skip the Hiera-T (configs[1]) measurement")
     args = ap.parse_args()

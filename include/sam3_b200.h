@@ -65,9 +65,10 @@ int s3b_sync(s3b_ctx* ctx);
 /* Options: "frames_per_pass" (encoder micro-batch, default 8);
  * "attention_impl" (0: tcgen05 flash attention where eligible, 1: always the
  * mma.sync kernel);
- * "gemm_pairs" (1, default: the wide GEMMs run 256-row tiles on pairs of
- * SMs, tcgen05 cta_group::2; 0: 128-row tiles on single SMs; applies to
- * every context of the process);
+ * "gemm_pairs" (which wide GEMMs run 256-row tiles on pairs of SMs, tcgen05
+ * cta_group::2: 1, default, those with K >= 2048 and the f16-output ones
+ * with 16 epilogue warps; 2 all; 0 none, 128-row tiles on single SMs;
+ * applies to every context of the process);
  * "gemm_wide_epilogue" (1, default: short-K GEMMs with f16 outputs run 16
  * epilogue warps; 0: 8; process-wide);
  * "attention_exp_poly" (0-4: of every 8 softmax exponentials in the tcgen05

@@ -121,6 +121,72 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   }
 }
 
+// Max over this thread's 64 keys of the tile (TMEM columns [cbase, cbase+64) of
+// its lane), in log2 units; MASKED: keys at or past kvalid are tiling padding.
+template <bool MASKED>
+__device__ __forceinline__ float half_row_max(uint32_t taddr, int cbase, int kvalid, float sl2) {
+  float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < kBK / 2; c += 32) {
+    if (MASKED && cbase + c >= kvalid) break;
+    uint32_t r[32];
+    TMEM_LD32(taddr + (uint32_t)c, r);
+    tc_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
+      float v2 = __uint_as_float(r[i + 2]), v3 = __uint_as_float(r[i + 3]);
+      if (MASKED) {
+        const int k = cbase + c + i;
+        v0 = k < kvalid ? v0 : -INFINITY;
+        v1 = k + 1 < kvalid ? v1 : -INFINITY;
+        v2 = k + 2 < kvalid ? v2 : -INFINITY;
+        v3 = k + 3 < kvalid ? v3 : -INFINITY;
+      }
+      mx0 = fmaxf(mx0, v0);
+      mx1 = fmaxf(mx1, v1);
+      mx2 = fmaxf(mx2, v2);
+      mx3 = fmaxf(mx3, v3);
+    }
+  }
+  return fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+}
+
+// p = 2^(s*sl2 - m) over this thread's 64 keys, written as f16 into its row of
+// the 128B-swizzled P half (`prow`), returns the row sum; MASKED: padding keys
+// inside the last 32-key chunk get p = 0 (the P V product reads to its end).
+template <bool MASKED, int NPOLY>
+__device__ __forceinline__ float half_row_p(uint32_t taddr, int cbase, int kvalid, float sl2, float m, uint8_t* prow,
+                                            int row) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+  for (int c = 0; c < kBK / 2; c += 32) {
+    if (MASKED && cbase + c >= kvalid) break;
+    uint32_t r[32];
+    TMEM_LD32(taddr + (uint32_t)c, r);
+    tc_wait_ld();
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float p[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = 8 * u + e;
+        const float x = fmaf(__uint_as_float(r[i]), sl2, -m);
+        p[e] = e < NPOLY ? exp2_poly3(x) : ex2(x);
+        if (MASKED) p[e] = cbase + c + i < kvalid ? p[e] : 0.f;
+      }
+      s0 += p[0] + p[4];
+      s1 += p[1] + p[5];
+      s2 += p[2] + p[6];
+      s3 += p[3] + p[7];
+      const int unit = (c >> 3) + u;  // 16-byte unit (8 keys) inside the 128-byte row
+      *reinterpret_cast<uint4*>(prow + ((unit ^ (row & 7)) << 4)) =
+          make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
+    }
+  }
+  return (s0 + s1) + (s2 + s3);
+}
+
 struct TcAttnArgs {
   int heads, ntok, nwin;
   int q_col, k_col, v_col;  // column offsets (elements) of q / k / v of head 0 in a row
@@ -280,31 +346,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_after();
       const int kvalid = a.ntok - j * kBK;  // keys at or past this count are tiling padding
       // partial row max over this thread's key half (4 independent chains)
+      const bool full_tile = kvalid >= kBK;  // every tile but a ragged last one
+      const uint32_t s_addr = tmem + lane_off + (uint32_t)cbase;
       float pm = -INFINITY;
-      if (ok && rows_live) {
-        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < kBK / 2; c += 32) {
-          if (cbase + c >= kvalid) break;
-          uint32_t r[32];
-          TMEM_LD32(tmem + lane_off + (uint32_t)(cbase + c), r);
-          tc_wait_ld();
-          if (cbase + c + 32 <= kvalid) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              mx0 = fmaxf(mx0, __uint_as_float(r[i]));
-              mx1 = fmaxf(mx1, __uint_as_float(r[i + 1]));
-              mx2 = fmaxf(mx2, __uint_as_float(r[i + 2]));
-              mx3 = fmaxf(mx3, __uint_as_float(r[i + 3]));
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (cbase + c + i < kvalid) mx0 = fmaxf(mx0, __uint_as_float(r[i]));
-          }
-        }
-        pm = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.sl2;
-      }
+      if (ok && rows_live)
+        pm = full_tile ? half_row_max<false>(s_addr, cbase, kvalid, a.sl2)
+                       : half_row_max<true>(s_addr, cbase, kvalid, a.sl2);
       // exchange the partial maxima of the two halves of each row (slot j & 1 is rewritten
       // two tiles later, after the partner has passed the next barrier)
       xmax[((j & 1) * 2 + hsel) * kBQ + row] = pm;
@@ -325,36 +372,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       ok = __all_sync(0xffffffffu, ok);
       if (ok && rows_live) {
         tc_fence_after();
-        // p = 2^(s*sl2 - m_ref), row sum, f16 P into the swizzled A operand (half hsel of sP);
-        // padding keys inside the last chunk get p = 0 (the P V product reads up to its end)
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        // p = 2^(s*sl2 - m_ref), row sum, f16 P into the swizzled A operand (half hsel of sP)
         uint8_t* prow = sP + hsel * (kBQ * 128) + row * 128;
-#pragma unroll
-        for (int c = 0; c < kBK / 2; c += 32) {
-          if (cbase + c >= kvalid) break;
-          uint32_t r[32];
-          TMEM_LD32(tmem + lane_off + (uint32_t)(cbase + c), r);
-          tc_wait_ld();
-          const bool whole = cbase + c + 32 <= kvalid;
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float p[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int i = 8 * u + e;
-              const float x = fmaf(__uint_as_float(r[i]), a.sl2, -m_ref);
-              p[e] = (whole || cbase + c + i < kvalid) ? (e < NPOLY ? exp2_poly3(x) : ex2(x)) : 0.f;
-            }
-            s0 += p[0] + p[4];
-            s1 += p[1] + p[5];
-            s2 += p[2] + p[6];
-            s3 += p[3] + p[7];
-            const int unit = (c >> 3) + u;  // 16-byte unit (8 keys) inside the 128-byte row
-            *reinterpret_cast<uint4*>(prow + ((unit ^ (row & 7)) << 4)) =
-                make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
-          }
-        }
-        l += (s0 + s1) + (s2 + s3);
+        l += full_tile ? half_row_p<false, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row)
+                       : half_row_p<true, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row);
         // the reference max moved: rescale this thread's 32 columns of the row's running O
         if (__any_sync(0xffffffffu, resc)) {
           uint32_t o[32];

@@ -245,8 +245,8 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     return kOk;
   }
   if (k == "gemm_pairs") {
-    if (value < 0 || value > 1) return set_error(ctx, kErrArg, "gemm_pairs must be 0 or 1");
-    set_gemm_pairs(value != 0);
+    if (value < 0 || value > 2) return set_error(ctx, kErrArg, "gemm_pairs must be 0, 1 or 2");
+    set_gemm_pairs((int)value);
     return kOk;
   }
   if (k == "gemm_wide_epilogue") {

@@ -41,7 +41,7 @@ constexpr int kBK = 64;
 constexpr int gemm_threads(int ew) { return 64 + 32 * ew; }
 constexpr uint32_t kStageBufBytes = 16384;  // 128 rows x 128 B
 
-bool g_gemm_pairs = true;     // 256-row tiles on SM pairs for the wide TMA-epilogue GEMMs
+int g_gemm_pairs = 1;         // 256-row tiles on SM pairs: 0 never, 1 long-K GEMMs, 2 every wide GEMM
 bool g_gemm_wide_epi = true;  // 16 epilogue warps for short-K GEMMs with f16 outputs
 
 
@@ -717,12 +717,16 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
     if (N <= 128) return launch_gemm<128, 4, true, false>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
     // f16 outputs of short-K GEMMs (QKV + RoPE, MLP fc1 + GELU): their epilogue outlasts the main loop
     // with 8 epilogue warps, so they run 16
-    if (!resid_in_place && !ep.out_f32 && K < 2048 && g_gemm_wide_epi)
+    if (!resid_in_place && !ep.out_f32 && K < 2048 && g_gemm_wide_epi) {
+      // with 16 epilogue warps the pair main loop pays off (measured 3-4% on QKV + RoPE)
+      if (g_gemm_pairs >= 1 && M > 2 * kBM)
+        return launch_gemm<256, 5, true, true, 16>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
       return launch_gemm<256, 3, true, false, 16>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
+    }
     // 256-row tiles on SM pairs where the main loop dominates (long K): measured faster for
     // K = 4736 (ViT fc2), slower for K = 1024 GEMMs whose epilogue (GELU, RoPE, residual)
     // already takes longer than their main loop
-    if (g_gemm_pairs && M > 2 * kBM && K >= 2048)
+    if (g_gemm_pairs && M > 2 * kBM && (K >= 2048 || g_gemm_pairs == 2))
       return launch_gemm<256, 5, true, true>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
     return launch_gemm<256, 3, true, false>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
   }
@@ -730,7 +734,7 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
   return launch_gemm<256, 4, false, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
 }
 
-void set_gemm_pairs(bool on) { g_gemm_pairs = on; }
+void set_gemm_pairs(int mode) { g_gemm_pairs = mode; }
 void set_gemm_wide_epilogue(bool on) { g_gemm_wide_epi = on; }
 
 }  // namespace s3b

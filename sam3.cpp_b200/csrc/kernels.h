@@ -72,8 +72,9 @@ struct EpiParams {
 // K-major. lda, ldb multiples of 8; pointers 16-byte aligned.
 int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
              const EpiParams& ep, int* err, cudaStream_t st);
-// Process-wide: whether wide TMA-epilogue GEMMs use 256-row tiles on SM pairs (default on).
-void set_gemm_pairs(bool on);
+// Process-wide: which wide TMA-epilogue GEMMs use 256-row tiles on SM pairs:
+// 0 none, 1 (default) those with K >= 2048 or f16 outputs on 16 epilogue warps, 2 all.
+void set_gemm_pairs(int mode);
 // Process-wide: whether short-K GEMMs with f16 outputs use 16 epilogue warps (default on).
 void set_gemm_wide_epilogue(bool on);
 

@@ -67,12 +67,15 @@ def test_gemm_pairs_and_single(engine, pairs, M, N, K, resid):
         engine.set_option("gemm_pairs", 1)
 
 
+@pytest.mark.parametrize("pairs", [1, 2])
 @pytest.mark.parametrize("wide", [0, 1])
 @pytest.mark.parametrize("M,N,K,act", [(5184, 4736, 1024, 1), (1000, 3072, 256, 0), (777, 288, 96, 2),
                                        (130, 1000, 1024, 3)])
-def test_gemm_f16_epilogue_warps(engine, wide, M, N, K, act):
-    """f16-output GEMMs with 8 or 16 epilogue warps (column groups of 128 or 64), ragged M / N."""
+def test_gemm_f16_epilogue_warps(engine, pairs, wide, M, N, K, act):
+    """f16-output GEMMs with 8 or 16 epilogue warps (column groups of 128 or 64), on single SMs
+    or SM pairs, ragged M / N."""
     engine.set_option("gemm_wide_epilogue", wide)
+    engine.set_option("gemm_pairs", pairs)
     try:
         g = torch.Generator(device="cuda").manual_seed(M * 3 + N + act)
         A = (torch.randn(M, K, device="cuda", generator=g) * 0.5).half()
@@ -85,6 +88,7 @@ def test_gemm_f16_epilogue_warps(engine, wide, M, N, K, act):
         assert (out.float() - ref).abs().max().item() < 1e-2 * max(1.0, ref.abs().max().item())
     finally:
         engine.set_option("gemm_wide_epilogue", 1)
+        engine.set_option("gemm_pairs", 1)
 
 
 @pytest.mark.parametrize("wide", [0, 1])
