@@ -33,10 +33,10 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 FRAMES_TOTAL = 64
-# measured with ncu (profiles/gemm_attention_vit_block0_ncu.md): mean DRAM read+write per launch of the
+# measured with ncu (one --set full capture of ViT block 0): mean DRAM read+write per launch of the
 # qkv / proj / fc1 / fc2 GEMMs of a ViT block at 8 frames per pass, and their algorithmic bytes
-GEMM_TRAFFIC_BYTES = 4.61e8
-GEMM_ALG_BYTES = 5.01e8
+GEMM_TRAFFIC_BYTES = 4.656e8
+GEMM_ALG_BYTES = 5.006e8
 
 
 def load_pkg():
@@ -378,7 +378,7 @@ def main():
             "roofline": {"bound": "tensor", "achieved": gemm_tflops, "peak": peak_sust, "unit": "TFLOP/s",
                          "frac": gemm_tflops / peak_sust,
                          # DRAM bytes per GEMM launch (read + write), mean of the four block-0 GEMMs at 8 frames
-                         # from one ncu capture (profiles/gemm_attention_vit_block0_ncu.md); algorithmic 5.0e8
+                         # from one ncu capture of ViT block 0; algorithmic 5.0e8
                          "traffic": GEMM_TRAFFIC_BYTES, "traffic_algorithmic": GEMM_ALG_BYTES,
                          "kernel": "gemm_f16_tc_kernel (tcgen05/TMEM, TMA)",
                          "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
