@@ -6,7 +6,9 @@ SimpleFPN neck, q4_0 weights (seeded synthetic, random-init), 64 seeded
 1008x1008 frames sharded over N GPUs (64/N frames per GPU, one process per
 GPU, no data-path collective). One step = encode all frames of the rank.
 The same line carries `hiera_t_q4_0` (configs[1]: SAM 2.1 Hiera-T + FPN
-neck, q4_0, 16 seeded 1024x1024 frames per GPU), timed the same way.
+neck, q4_0, 16 seeded 1024x1024 frames per GPU) and `video_hiera_l_q8_0`
+(configs[4]: Hiera-L q8_0 on 64 frames sharded over the GPUs, then memory
+attention per frame on GPU 0), timed the same way.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload vit_q4_0|vit_f16]
   python bench.py --impl reference ...   # CPU restatement (oracle) of the same path
@@ -118,6 +120,80 @@ def bench_hiera(s3b, local: int, rank: int, world: int, steps: int, warmup: int,
             "attention_ms_per_step": a["ms"] / steps,
             "algorithmic_tflop_per_step": (g["flops"] + a["flops"]) / steps / 1e12,
             "gpu_launches_per_step": prof["launches"] / steps}
+
+
+def bench_video(s3b, local: int, rank: int, world: int, steps: int, warmup: int, stream, device) -> dict:
+    """SAM 2.1 Hiera-L image encoder + FPN neck, q8_0 weights, 64 seeded 1024^2 frames
+    sharded over the GPUs (frames/s of the job, max over ranks); then, on rank 0 (the tracking GPU), memory
+    attention per frame: 4 layers, d = 256, 64x64 current tokens from the encoder's level-2 map, cross-attention
+    to 7 memory frames of 64x64 tokens + 16 object pointers x 4 tokens (M = 28736, random memory bank)."""
+    import dataclasses
+
+    import torch
+    import torch.distributed as dist
+    from sam3_b200 import synth
+    cfg = dataclasses.replace(synth.HIERA_L, with_mem_attn=True)
+    path = os.path.join(tempfile.gettempdir(), "s3b_bench_hiera_l_q8_0.ggml")
+    if local == 0 and not os.path.exists(path):
+        synth.write_sam2(path + ".tmp", cfg, seed=0, ftype=1, qtype=8, quantize=s3b.quantize_rows)
+        os.replace(path + ".tmp", path)
+    if world > 1:
+        dist.barrier()
+    eng = s3b.Engine(local)
+    eng.load_model(path)
+    first, nf = shard_frames(FRAMES_TOTAL, rank, world)
+    frames = torch.from_numpy(synth.frames_u8(nf, 1024, base_seed=1000 + first)).to(device)
+    for _ in range(warmup):
+        eng.encode_u8(frames)
+    eng.sync()
+    eng.set_stream(stream.cuda_stream)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    eng.profile_begin(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        eng.encode_u8(frames)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prof = eng.profile_end()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+    g, a = prof["gemm"], prof["attention"]
+    out = {"workload": f"configs[4]: SAM 2.1 Hiera-L image encoder + FPN neck, q8_0 weights, {FRAMES_TOTAL} seeded "
+                       f"1024^2 frames sharded over {world} GPU(s); memory attention per frame on GPU 0",
+           "encoder_frames_per_s": FRAMES_TOTAL / (ms / 1000.0), "encoder_ms_per_step": ms,
+           "encoder_gemm_tflops": g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0,
+           "encoder_attention_tflops": a["flops"] / (a["ms"] / 1000.0) / 1e12 if a["ms"] > 0 else 0.0}
+    if rank == 0:
+        # current frame = frame 0 of this rank's batch, its PE; random memory bank and pointer tokens
+        curr = torch.from_numpy(eng.output("neck_trk_2", 0).reshape(-1, 256)).to(device)
+        pos = torch.from_numpy(eng.output("neck_trk_pe_2", 0).reshape(-1, 256)).to(device)
+        g2 = torch.Generator(device=device).manual_seed(5)
+        m_total, n_ptr = cfg.num_maskmem * 4096 + cfg.max_obj_ptrs * 4, cfg.max_obj_ptrs * 4
+        prompt = torch.randn(m_total, 64, device=device, generator=g2)
+        prompt_pos = torch.randn(m_total, 64, device=device, generator=g2) * 0.1
+        res = torch.empty_like(curr)
+        for _ in range(warmup):
+            eng.mem_attn(curr, pos, 64, prompt, prompt_pos, n_ptr, out=res)
+        torch.cuda.synchronize()
+        eng.profile_begin(True)
+        e0.record(stream)
+        for _ in range(steps):
+            eng.mem_attn(curr, pos, 64, prompt, prompt_pos, n_ptr, out=res)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        p2 = eng.profile_end()
+        mms = e0.elapsed_time(e1) / steps
+        fl = (p2["gemm"]["flops"] + p2["attention"]["flops"]) / steps
+        out.update({"mem_attn_ms_per_frame": mms, "mem_attn_tflop_per_frame": fl / 1e12,
+                    "mem_attn_tflops": fl / (mms / 1000.0) / 1e12,
+                    "mem_attn_attention_tflops": p2["attention"]["flops"] / (p2["attention"]["ms"] / 1000.0) / 1e12
+                    if p2["attention"]["ms"] > 0 else 0.0,
+                    "mem_attn_memory_tokens": m_total})
+    eng.set_stream(None)
+    eng.close()
+    return out
 
 
 def vit_flops_per_frame(cfg, with_neck=True):
@@ -246,6 +322,8 @@ def main():
                     help="256-row GEMM tiles on SM pairs: 1 (default) for K >= 2048, 2 for all, 0 never")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-hiera", action="store_true", help="skip the Hiera-T (configs[1]) measurement")
+    ap.add_argument("--no-video", action="store_true",
+                    help="skip the Hiera-L + memory attention (configs[4]) measurement")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -397,6 +475,8 @@ def main():
     eng.close()
     if not args.no_hiera:
         line["hiera_t_q4_0"] = bench_hiera(s3b, local, rank, world, args.steps, args.warmup, stream, "cuda")
+    if not args.no_video:
+        line["video_hiera_l_q8_0"] = bench_video(s3b, local, rank, world, args.steps, args.warmup, stream, "cuda")
     if rank == 0 and not args.no_cpu_baseline and world == 1:
         v, parts = cpu_sample(args.workload, 1)
         line["cpu_baseline"] = {"value": v, "unit": "frames/s", "cores": os.cpu_count(), "kind": "port",
