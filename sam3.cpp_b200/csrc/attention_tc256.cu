@@ -1,0 +1,584 @@
+// Tensor-core (tcgen05 / TMEM / TMA) flash attention for head dim 256: the
+// memory attention of the video tracker (sam3_build_mem_attn_graph,
+// ggml_flash_attn_ext at sam3.cpp:9267 and 9312; one head, d = 256, scale
+// 1/16): self-attention over the 64x64 current tokens and cross-attention to
+// the memory bank (7 x 4096 spatial + pointer tokens).
+//
+// One CTA = one 128-query tile of one (batch, head); 6 warps, 1 CTA / SM
+// (TMEM: two 64-column S buffers + a 256-column O accumulator = 512 columns):
+//   warp 0     TMA: Q tile once (4 boxes of 64 columns), then K_j, V_j (64 keys
+//              x 256, 32 KB each) through a 3-slot ring. Q, K and V have their
+//              own 3-D tensor maps (columns, rows, batch), so they may live in
+//              separate buffers with different row counts and strides.
+//   warp 1     MMA: S_j = Q K_j^T (M=128, N=64, K=256) into S buffer j&1; after
+//              the softmax wrote P_j: O += P_j V_j (M=128, N=256, K=64, V as
+//              an MN-major operand). S_{j+2} is issued right after P_j V_j, so
+//              the tensor core computes the next scores while the softmax
+//              threads work on the current ones.
+//   warps 2-5  softmax, one query row per thread (TMEM lane): row max over the
+//              64 keys, p = 2^(s*scale*log2e - m) as f16 into the 128B-swizzled
+//              A operand; the reference max m moves only when the row max grows
+//              by more than 2^8, and only then are the sum and the row of O in
+//              TMEM rescaled. At the end O is read, divided by the sum and
+//              stored (256 columns per row).
+// Every wait is bounded; a timeout records an error code and the CTA unwinds.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace s3b {
+namespace {
+
+constexpr int kD = 256;
+constexpr int kAtoms = kD / 64;                          // 64-column (128-byte) swizzle atoms per row
+constexpr int kBQ = 128;
+constexpr int kBK = 64;
+constexpr int kSlots = 3;
+constexpr uint32_t kQBytes = kBQ * kD * 2;               // 64 KB: 4 atoms of 128 rows x 128 B
+constexpr uint32_t kKVAtom = kBK * 128;                  // 8 KB: 64 rows x 128 B
+constexpr uint32_t kKVBytes = kBK * kD * 2;              // 32 KB
+constexpr uint32_t kPBytes = kBQ * kBK * 2;              // 16 KB: one atom of 128 rows x 128 B
+constexpr int kThreads = 192;
+constexpr float kLazyMax = 8.0f;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kOCol = 256;                          // O at TMEM columns [256, 512)
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
+}
+
+// MN-major SW128 operand (V: rows = keys along K, 64 values of d per 128-byte
+// row): SBO = 1024 B between 8-key groups, LBO = 8 KB between 64-wide d atoms.
+__device__ __forceinline__ uint64_t sdesc_mn_sw128_v(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(kKVAtom >> 4) << 16;  // LBO
+  d |= (uint64_t)(1024u >> 4) << 32;    // SBO
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+#define TMEM_LD32(taddr, R)                                                                                  \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "                                                     \
+               "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"                                     \
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                    \
+               : "=r"(R[0]), "=r"(R[1]), "=r"(R[2]), "=r"(R[3]), "=r"(R[4]), "=r"(R[5]), "=r"(R[6]),         \
+                 "=r"(R[7]), "=r"(R[8]), "=r"(R[9]), "=r"(R[10]), "=r"(R[11]), "=r"(R[12]), "=r"(R[13]),     \
+                 "=r"(R[14]), "=r"(R[15]), "=r"(R[16]), "=r"(R[17]), "=r"(R[18]), "=r"(R[19]), "=r"(R[20]),  \
+                 "=r"(R[21]), "=r"(R[22]), "=r"(R[23]), "=r"(R[24]), "=r"(R[25]), "=r"(R[26]), "=r"(R[27]),  \
+                 "=r"(R[28]), "=r"(R[29]), "=r"(R[30]), "=r"(R[31])                                          \
+               : "r"(taddr))
+
+#define TMEM_ST32(taddr, R)                                                                                  \
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "                                               \
+               "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"                                    \
+               "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),             \
+               "r"(R[0]), "r"(R[1]), "r"(R[2]), "r"(R[3]), "r"(R[4]), "r"(R[5]), "r"(R[6]), "r"(R[7]),       \
+               "r"(R[8]), "r"(R[9]), "r"(R[10]), "r"(R[11]), "r"(R[12]), "r"(R[13]), "r"(R[14]), "r"(R[15]), \
+               "r"(R[16]), "r"(R[17]), "r"(R[18]), "r"(R[19]), "r"(R[20]), "r"(R[21]), "r"(R[22]),           \
+               "r"(R[23]), "r"(R[24]), "r"(R[25]), "r"(R[26]), "r"(R[27]), "r"(R[28]), "r"(R[29]),           \
+               "r"(R[30]), "r"(R[31])                                                                        \
+               : "memory")
+
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitNs) {
+      if (err) atomicCAS(err, 0, kErrWaitDrain);
+      return;
+    }
+  }
+}
+
+struct Tc256Args {
+  int heads, nq, nk;
+  int head_rows;      // 1: head h of batch b is row block b*heads + h (layout [B][H][n][d]); 0: columns h*x_h
+  int q_h, k_h, v_h;  // column offset (elements) of head h = h * x_h (head_rows == 0)
+  __half* o;
+  long long o_n;      // output row stride; row = map_row(omap, b*nq + i), head h at column h*256
+  RowMap omap;
+  float sl2;          // softmax scale * log2(e)
+  // key split: CTA `split` of a query tile covers key tiles [split*tiles_per, +tiles_per); with
+  // n_split > 1 it writes its unnormalised O, reference max and sum to ws_o / ws_ml for the combine
+  int n_split, tiles_per;
+  float* ws_o;   // [bh][split][nq][256]
+  float* ws_ml;  // [bh][split][nq][2]
+};
+
+// Max over the 64 keys of the tile (TMEM columns [0, 64) of this lane's S
+// buffer), in log2 units; MASKED: keys at or past kvalid are padding.
+template <bool MASKED>
+__device__ __forceinline__ float row_max64(uint32_t taddr, int kvalid, float sl2) {
+  float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < kBK; c += 32) {
+    if (MASKED && c >= kvalid) break;
+    uint32_t r[32];
+    TMEM_LD32(taddr + (uint32_t)c, r);
+    tc_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
+      float v2 = __uint_as_float(r[i + 2]), v3 = __uint_as_float(r[i + 3]);
+      if (MASKED) {
+        v0 = c + i < kvalid ? v0 : -INFINITY;
+        v1 = c + i + 1 < kvalid ? v1 : -INFINITY;
+        v2 = c + i + 2 < kvalid ? v2 : -INFINITY;
+        v3 = c + i + 3 < kvalid ? v3 : -INFINITY;
+      }
+      mx0 = fmaxf(mx0, v0);
+      mx1 = fmaxf(mx1, v1);
+      mx2 = fmaxf(mx2, v2);
+      mx3 = fmaxf(mx3, v3);
+    }
+  }
+  return fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+}
+
+// p = 2^(s*sl2 - m) over the 64 keys into this thread's row of the swizzled P
+// atom; returns the row sum. MASKED: padding keys inside the last 32-key chunk
+// get p = 0 (the P V product reads to the end of that chunk).
+template <bool MASKED>
+__device__ __forceinline__ float row_p64(uint32_t taddr, int kvalid, float sl2, float m, uint8_t* prow, int row) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+  for (int c = 0; c < kBK; c += 32) {
+    if (MASKED && c >= kvalid) break;
+    uint32_t r[32];
+    TMEM_LD32(taddr + (uint32_t)c, r);
+    tc_wait_ld();
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float p[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = 8 * u + e;
+        p[e] = ex2(fmaf(__uint_as_float(r[i]), sl2, -m));
+        if (MASKED) p[e] = c + i < kvalid ? p[e] : 0.f;
+      }
+      s0 += p[0] + p[4];
+      s1 += p[1] + p[5];
+      s2 += p[2] + p[6];
+      s3 += p[3] + p[7];
+      const int unit = (c >> 3) + u;  // 16-byte unit (8 keys) inside the 128-byte row
+      *reinterpret_cast<uint4*>(prow + ((unit ^ (row & 7)) << 4)) =
+          make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
+    }
+  }
+  return (s0 + s1) + (s2 + s3);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                      const __grid_constant__ CUtensorMap tv, Tc256Args a, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sQ = smem;                           // 64 KB
+  uint8_t* sKV = sQ + kQBytes;                  // kSlots x 32 KB
+  uint8_t* sP = sKV + kSlots * kKVBytes;        // 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;                 // [kSlots]
+  uint64_t* kv_empty = kv_full + kSlots;        // [kSlots]
+  uint64_t* s_full = kv_empty + kSlots;         // [2]
+  uint64_t* s_empty = s_full + 2;               // [2]
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* p_empty = p_full + 1;
+  uint64_t* o_done = p_empty + 1;
+  uint64_t* mma_done = o_done + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // 1-D grid, query tile fastest: the tiles of one (batch, head) run together and share K/V in L2
+  const int n_qt = (a.nq + kBQ - 1) / kBQ;
+  const int qb = (int)(blockIdx.x % (unsigned)n_qt);
+  const int rest = (int)(blockIdx.x / (unsigned)n_qt);
+  const int split = rest % a.n_split;
+  const int bh = rest / a.n_split;
+  const int b = bh / a.heads, h = bh - b * a.heads;
+  const int rb = a.head_rows ? bh : b;  // row block (batch coordinate of the maps)
+  const int hc = a.head_rows ? 0 : h;   // head index used for the column offset
+  // this CTA's key tiles: global tiles j0 .. j0 + nkb - 1 (local index j below); never empty
+  const int j0 = split * a.tiles_per;
+  const int nkb = min((a.nk + kBK - 1) / kBK - j0, a.tiles_per);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(p_empty, 1);
+    mbar_init(o_done, 1);
+    mbar_init(mma_done, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, kTmemCols);  // S buffers: [0,64), [64,128); O: [256,512)
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kQBytes);
+#pragma unroll
+      for (int at = 0; at < kAtoms; ++at)
+        tma_load_3d(&tq, q_full, sQ + at * (kBQ * 128), hc * a.q_h + at * 64, qb * kBQ, rb);
+      uint32_t armed = 0, armed_phase = 0;
+      bool ok = true;
+      for (int t = 0; t < 2 * nkb && ok; ++t) {  // K_0, V_0, K_1, V_1, ...
+        const int s = t % kSlots;
+        const uint32_t use = (uint32_t)(t / kSlots);
+        if (!mbar_wait(&kv_empty[s], (use & 1) ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
+        mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
+        const int j = t >> 1;
+        const CUtensorMap* map = (t & 1) ? &tv : &tk;
+        const int col0 = hc * ((t & 1) ? a.v_h : a.k_h);
+#pragma unroll
+        for (int at = 0; at < kAtoms; ++at)
+          tma_load_3d(map, &kv_full[s], sKV + s * kKVBytes + at * kKVAtom, col0 + at * 64, (j0 + j) * kBK, rb);
+        armed |= 1u << s;
+        armed_phase = (armed_phase & ~(1u << s)) | ((use & 1) << s);
+      }
+      mbar_wait_drain(q_full, 0, err);
+      for (int s = 0; s < kSlots; ++s)
+        if (armed & (1u << s)) mbar_wait_drain(&kv_full[s], (armed_phase >> s) & 1u, err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16(kBQ, kBK, 0);                 // Q, K both K-major
+      constexpr uint32_t idesc_o = idesc_f16(kBQ, kD, 0) | (1u << 16);     // B (V) MN-major
+      bool ok = mbar_wait(q_full, 0, s_abort, err, kErrWaitFull);
+      tc_fence_after();
+      const uint32_t qa = smem_u32(sQ);
+      bool issued = false;
+      // S_j = Q K_j^T into S buffer j & 1 (free once the softmax released S_{j-2})
+      auto issue_s = [&](int j) -> bool {
+        const int t = 2 * j, s = t % kSlots, sb = j & 1;
+        if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) return false;
+        if (j >= 2 && !mbar_wait(&s_empty[sb], (uint32_t)((j - 2) >> 1) & 1, s_abort, err, kErrWaitMisc))
+          return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sKV + s * kKVBytes);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk & 3) * 32);
+          const uint64_t dq = sdesc_k_sw128(qa + (uint32_t)((kk >> 2) * (kBQ * 128)) + off);
+          const uint64_t dk = sdesc_k_sw128(ka + (uint32_t)((kk >> 2) * kKVAtom) + off);
+          tc_mma_f16(tmem + (uint32_t)(sb * kBK), dq, dk, idesc_s, kk != 0);
+        }
+        tc_commit(&s_full[sb]);
+        tc_commit(&kv_empty[s]);
+        issued = true;
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && nkb > 1) ok = issue_s(1);
+      for (int j = 0; j < nkb && ok; ++j) {
+        // O += P_j V_j (after the softmax wrote P_j and, where needed, rescaled O)
+        const int t = 2 * j + 1, s = t % kSlots;
+        if (!mbar_wait(p_full, (uint32_t)j & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
+        if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t pa = smem_u32(sP), va = smem_u32(sKV + s * kKVBytes);
+        const int nk16 = min(kBK / 16, (a.nk - (j0 + j) * kBK + 15) / 16);  // K steps holding a real key
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          if (kk >= nk16) break;
+          const uint64_t dp = sdesc_k_sw128(pa + (uint32_t)(kk * 32));
+          const uint64_t dv = sdesc_mn_sw128_v(va + (uint32_t)(kk * 2048));  // 16 key rows per K step
+          tc_mma_f16(tmem + kOCol, dp, dv, idesc_o, (j > 0 || kk != 0) ? 1u : 0u);
+        }
+        tc_commit(&kv_empty[s]);
+        tc_commit(p_empty);
+        if (j + 2 < nkb && !issue_s(j + 2)) { ok = false; break; }
+      }
+      if (ok) tc_commit(o_done);
+      if (issued) {
+        tc_commit(mma_done);
+        mbar_wait_drain(mma_done, 0, err);
+      }
+    }
+  } else {
+    // softmax: warp w owns TMEM lanes 32*(w%4) .. +31 (query rows)
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const bool rows_live = qb * kBQ + q4 * 32 < a.nq;  // else only the barrier protocol
+    uint8_t* prow = sP + row * 128;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&s_full[sb], (uint32_t)(j >> 1) & 1, s_abort, err, kErrWaitTmemFull)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int kvalid = a.nk - (j0 + j) * kBK;
+      const bool full_tile = kvalid >= kBK;
+      const uint32_t s_addr = tmem + lane_off + (uint32_t)(sb * kBK);
+      float alpha = 1.f;
+      bool resc = false;
+      if (rows_live) {
+        const float m_tile = full_tile ? row_max64<false>(s_addr, kvalid, a.sl2) : row_max64<true>(s_addr, kvalid, a.sl2);
+        if (m_tile > m_ref + kLazyMax) {  // always at the first tile
+          alpha = ex2(m_ref - m_tile);
+          resc = j > 0;
+          m_ref = m_tile;
+          l *= alpha;
+        }
+      }
+      // P buffer free and O final for tile j-1
+      if (j > 0 && !mbar_wait(p_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      if (rows_live) {
+        tc_fence_after();
+        l += full_tile ? row_p64<false>(s_addr, kvalid, a.sl2, m_ref, prow, row)
+                       : row_p64<true>(s_addr, kvalid, a.sl2, m_ref, prow, row);
+        if (__any_sync(0xffffffffu, resc)) {
+          const float f = resc ? alpha : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < kD; c += 32) {
+            uint32_t o[32];
+            TMEM_LD32(tmem + lane_off + kOCol + (uint32_t)c, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            TMEM_ST32(tmem + lane_off + kOCol + (uint32_t)c, o);
+          }
+          tc_wait_st();
+        }
+      }
+      // S_j read, P_j written, O rescaled: hand them to the MMA warp
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_empty[sb]);
+        mbar_arrive(p_full);
+      }
+    }
+    if (ok) ok = mbar_wait(o_done, 0, s_abort, err, kErrWaitMisc);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok && rows_live) {
+      tc_fence_after();
+      const int qi = qb * kBQ + row;
+      if (a.n_split > 1) {
+        // partial result of this key split: O relative to 2^m_ref, the reference max and the sum
+        const size_t prow_idx = ((size_t)bh * a.n_split + split) * a.nq + qi;
+#pragma unroll 1
+        for (int c = 0; c < kD; c += 32) {
+          uint32_t o[32];
+          TMEM_LD32(tmem + lane_off + kOCol + (uint32_t)c, o);
+          tc_wait_ld();
+          if (qi < a.nq) {
+            float4* op = reinterpret_cast<float4*>(a.ws_o + prow_idx * kD + c);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              op[u] = make_float4(__uint_as_float(o[4 * u]), __uint_as_float(o[4 * u + 1]),
+                                  __uint_as_float(o[4 * u + 2]), __uint_as_float(o[4 * u + 3]));
+          }
+        }
+        if (qi < a.nq) *reinterpret_cast<float2*>(a.ws_ml + prow_idx * 2) = make_float2(m_ref, l);
+      } else {
+        const long long orow = qi < a.nq ? map_row(a.omap, (long long)b * a.nq + qi) : -1;
+        const float inv = 1.0f / l;
+#pragma unroll 1
+        for (int c = 0; c < kD; c += 32) {
+          uint32_t o[32];
+          TMEM_LD32(tmem + lane_off + kOCol + (uint32_t)c, o);
+          tc_wait_ld();
+          if (orow >= 0) {
+            uint4* op = reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * kD + c);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              op[u] = make_uint4(pack_h2(__uint_as_float(o[8 * u]) * inv, __uint_as_float(o[8 * u + 1]) * inv),
+                                 pack_h2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv),
+                                 pack_h2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv),
+                                 pack_h2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv));
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Merges the key splits of each query row: M = max of the splits' reference
+// maxima, O = sum_s 2^(m_s - M) O_s, l = sum_s 2^(m_s - M) l_s, out = O / l
+// (f16). One warp per row, 8 columns per lane.
+__global__ void __launch_bounds__(256) attn_combine256_kernel(Tc256Args a, long long rows) {
+  const long long r = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const int bh = (int)(r / a.nq), qi = (int)(r - (long long)bh * a.nq);
+  const int b = bh / a.heads, h = bh - b * a.heads;
+  float mmax = -INFINITY;
+  for (int s = 0; s < a.n_split; ++s)
+    mmax = fmaxf(mmax, a.ws_ml[(((size_t)bh * a.n_split + s) * a.nq + qi) * 2]);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float lsum = 0.f;
+  for (int s = 0; s < a.n_split; ++s) {
+    const size_t pr = ((size_t)bh * a.n_split + s) * a.nq + qi;
+    const float2 ml = *reinterpret_cast<const float2*>(a.ws_ml + pr * 2);
+    const float w = ml.x == -INFINITY ? 0.f : ex2(ml.x - mmax);
+    lsum += w * ml.y;
+    const float4* op = reinterpret_cast<const float4*>(a.ws_o + pr * kD + lane * 8);
+    const float4 x0 = op[0], x1 = op[1];
+    acc[0] += w * x0.x; acc[1] += w * x0.y; acc[2] += w * x0.z; acc[3] += w * x0.w;
+    acc[4] += w * x1.x; acc[5] += w * x1.y; acc[6] += w * x1.z; acc[7] += w * x1.w;
+  }
+  const long long orow = map_row(a.omap, (long long)b * a.nq + qi);
+  if (orow < 0) return;
+  const float inv = 1.0f / lsum;
+  *reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * kD + lane * 8) =
+      make_uint4(pack_h2(acc[0] * inv, acc[1] * inv), pack_h2(acc[2] * inv, acc[3] * inv),
+                 pack_h2(acc[4] * inv, acc[5] * inv), pack_h2(acc[6] * inv, acc[7] * inv));
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// 3-D map (columns, rows, batch) over x[b*xb + n*xn + col], box = 64 columns x box_rows x 1, SW128.
+int map3(EncodeTiledFn enc, CUtensorMap* m, const __half* x, long long xn, long long xb, int rows, int batch,
+         int box_rows) {
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (xn % 8) || (xb % 8)) return -2;
+  cuuint64_t dims[3] = {(cuuint64_t)xn, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(xn * 2), (cuuint64_t)(xb * 2)};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(x), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? 0
+             : -12;
+}
+
+}  // namespace
+
+void* tensor_map_encoder();  // gemm.cu
+
+size_t attention_tc256_ws_bytes(int n_split, int batch_heads, int nq) {
+  return (size_t)n_split * batch_heads * nq * (kD + 2) * sizeof(float);
+}
+
+int attention_tc256(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes, int* err, cudaStream_t st) {
+  EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!enc) return -10;
+  if (p.heads <= 0 || batch_heads % p.heads || p.nq <= 0 || p.nk <= 0) return -2;
+  if ((p.o_n % 8) || (reinterpret_cast<uintptr_t>(p.o) & 15)) return -2;
+  // heads either as column offsets inside a row (fused projections) or as
+  // consecutive row blocks ([B][H][n][d]); anything else is not supported here
+  const bool head_rows = p.heads > 1 && p.q_h >= (long long)p.nq * p.q_n;
+  int blocks;
+  long long qb, kb, vb;
+  if (head_rows) {
+    if (p.k_h < (long long)p.nk * p.k_n || p.v_h < (long long)p.nk * p.v_n) return -2;
+    if (batch_heads > p.heads &&
+        (p.q_b != p.heads * p.q_h || p.k_b != p.heads * p.k_h || p.v_b != p.heads * p.v_h))
+      return -2;
+    blocks = batch_heads;
+    qb = p.q_h;
+    kb = p.k_h;
+    vb = p.v_h;
+    if (p.q_n < kD || p.k_n < kD || p.v_n < kD) return -2;
+  } else {
+    if ((p.q_h % 8) || (p.k_h % 8) || (p.v_h % 8)) return -2;
+    if ((long long)(p.heads - 1) * p.q_h + kD > p.q_n || (long long)(p.heads - 1) * p.k_h + kD > p.k_n ||
+        (long long)(p.heads - 1) * p.v_h + kD > p.v_n)
+      return -2;
+    blocks = batch_heads / p.heads;
+    // a single batch may carry any batch stride; use one that satisfies the map's rules
+    qb = blocks > 1 ? p.q_b : (long long)p.nq * p.q_n;
+    kb = blocks > 1 ? p.k_b : (long long)p.nk * p.k_n;
+    vb = blocks > 1 ? p.v_b : (long long)p.nk * p.v_n;
+  }
+  CUtensorMap tq, tk, tv;
+  int rc = map3(enc, &tq, p.q, p.q_n, qb, p.nq, blocks, kBQ);
+  if (!rc) rc = map3(enc, &tk, p.k, p.k_n, kb, p.nk, blocks, kBK);
+  if (!rc) rc = map3(enc, &tv, p.v, p.v_n, vb, p.nk, blocks, kBK);
+  if (rc) return rc;
+  Tc256Args a;
+  a.heads = p.heads;
+  a.head_rows = head_rows ? 1 : 0;
+  a.nq = p.nq;
+  a.nk = p.nk;
+  a.q_h = (int)p.q_h;
+  a.k_h = (int)p.k_h;
+  a.v_h = (int)p.v_h;
+  a.o = p.o;
+  a.o_n = p.o_n;
+  a.omap = p.omap;
+  a.sl2 = p.scale * 1.4426950408889634f;
+  // split the keys over CTAs when the query tiles alone leave SMs idle (e.g. one head of 4096 queries:
+  // 32 tiles on 148 SMs), keeping at least 4 key tiles per split and no split empty
+  const int n_qt = (p.nq + kBQ - 1) / kBQ;
+  const long long units = (long long)n_qt * batch_heads;
+  const int nkb = (p.nk + kBK - 1) / kBK;
+  int n_split = 1;
+  if (ws && units < num_sms()) n_split = (int)std::max(1LL, std::min((long long)num_sms() / units, (long long)nkb / 4));
+  int tiles_per = (nkb + n_split - 1) / n_split;
+  n_split = (nkb + tiles_per - 1) / tiles_per;
+  if (n_split > 1 && ws_bytes < attention_tc256_ws_bytes(n_split, batch_heads, p.nq)) n_split = 1, tiles_per = nkb;
+  a.n_split = n_split;
+  a.tiles_per = tiles_per;
+  a.ws_o = ws;
+  a.ws_ml = ws ? ws + (size_t)n_split * batch_heads * p.nq * kD : nullptr;
+  constexpr size_t smem = 1024 + kQBytes + kSlots * kKVBytes + kPBytes + 16 * 8 + 16;
+  static_assert(smem <= 232448, "shared memory per CTA");
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_tc256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return -13;
+    attr = true;
+  }
+  const long long n_cta = units * n_split;
+  if (n_cta > 0x7fffffffLL) return -2;
+  attn_tc256_kernel<<<(unsigned)n_cta, kThreads, smem, st>>>(tq, tk, tv, a, err);
+  int rc2 = launch_status("attention_tc256");
+  if (rc2 || n_split == 1) return rc2;
+  const long long rows = (long long)batch_heads * p.nq;
+  attn_combine256_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(a, rows);
+  return launch_status("attention_tc256 combine");
+}
+
+}  // namespace s3b

@@ -76,9 +76,29 @@ int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
                      p.q_b == p.k_b && p.q_b == p.v_b && p.q_b == (long long)p.nq * p.q_n && p.q_h == 64 &&
                      p.k_h == 64 && p.v_h == 64 && kq > 0 && vq > 0 && kq + 64LL * p.heads <= p.q_n &&
                      vq + 64LL * p.heads <= p.q_n && batch_heads % p.heads == 0;
-  const int rc = tc_ok ? attention_tc64(p.q, p.q_n, 0, (int)kq, (int)vq, p.heads, p.nq, batch_heads / p.heads, p.o,
-                                        p.o_n, p.omap, p.scale, ctx->attention_exp_poly, ctx->d_err, ctx->stream)
-                       : attention(p, D, batch_heads, ctx->stream);
+  int rc;
+  if (tc_ok) {
+    rc = attention_tc64(p.q, p.q_n, 0, (int)kq, (int)vq, p.heads, p.nq, batch_heads / p.heads, p.o, p.o_n, p.omap,
+                        p.scale, ctx->attention_exp_poly, ctx->d_err, ctx->stream);
+  } else {
+    // d = 256 (memory attention) on the tcgen05 kernel when its layout rules hold, else mma.sync
+    rc = -2;
+    if (ctx->attention_impl != 1 && D == 256) {
+      // workspace for key splits (used when the query tiles leave SMs idle)
+      const long long units = (long long)((p.nq + 127) / 128) * batch_heads;
+      float* ws = nullptr;
+      size_t ws_bytes = 0;
+      if (units < num_sms()) {
+        ws_bytes = attention_tc256_ws_bytes((int)(num_sms() / units), batch_heads, p.nq);
+        int brc = 0;
+        DevBuf* buf = ctx->buf("attn_tc256_split", ws_bytes, &brc);
+        if (brc) return brc;
+        ws = buf->as<float>();
+      }
+      rc = attention_tc256(p, batch_heads, ws, ws_bytes, ctx->d_err, ctx->stream);
+    }
+    if (rc == -2) rc = attention(p, D, batch_heads, ctx->stream);
+  }
   count_launch(ctx);
   if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "attention D=%d failed (%d)", D, rc);
   if (ctx->prof) {

@@ -194,7 +194,9 @@ def test_gemm_f16_out_strided(engine):
                                                  (72, 196, 196, 2, 3), (72, 49, 196, 16, 2),
                                                  # more (batch, head) pairs than a grid's y extent (Hiera-T
                                                  # stage-1 windows at 16 frames per pass)
-                                                 (96, 16, 16, 4, 16400)])
+                                                 (96, 16, 16, 4, 16400),
+                                                 # d = 256 on the tcgen05 kernel: heads as row blocks, ragged keys
+                                                 (256, 300, 500, 2, 2), (256, 128, 64, 1, 3), (256, 1, 77, 3, 1)])
 def test_attention(engine, D, nq, nk, heads, batch):
     g = torch.Generator(device="cuda").manual_seed(D + nq + nk)
     q = torch.randn(batch, heads, nq, D, device="cuda", generator=g).half()
