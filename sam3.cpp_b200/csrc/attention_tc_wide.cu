@@ -1,27 +1,37 @@
-// Tensor-core (tcgen05 / TMEM / TMA) flash attention for head dim 256: the
-// memory attention of the video tracker (sam3_build_mem_attn_graph,
-// ggml_flash_attn_ext at sam3.cpp:9267 and 9312; one head, d = 256, scale
-// 1/16): self-attention over the 64x64 current tokens and cross-attention to
-// the memory bank (7 x 4096 spatial + pointer tokens).
+// Tensor-core (tcgen05 / TMEM / TMA) flash attention for head dims 72, 96 and
+// 256 with separate q / k / v operands:
+//   d = 256  memory attention of the video tracker (sam3_build_mem_attn_graph,
+//            ggml_flash_attn_ext at sam3.cpp:9267 and 9312; one head, scale
+//            1/16): self-attention over the 64x64 current tokens and
+//            cross-attention to the memory bank (7 x 4096 + pointer tokens);
+//   d = 96   SAM 2.1 Hiera-T blocks, d = 72 Hiera-L blocks
+//            (sam2_hiera_block_forward, ggml_flash_attn_ext at sam3.cpp:4395),
+//            windowed and global, heads as column offsets of the fused qkv
+//            buffer, windows as the batch.
 //
-// One CTA = one 128-query tile of one (batch, head); 6 warps, 1 CTA / SM
-// (TMEM: two 64-column S buffers + a 256-column O accumulator = 512 columns):
-//   warp 0     TMA: Q tile once (4 boxes of 64 columns), then K_j, V_j (64 keys
-//              x 256, 32 KB each) through a 3-slot ring. Q, K and V have their
-//              own 3-D tensor maps (columns, rows, batch), so they may live in
-//              separate buffers with different row counts and strides.
-//   warp 1     MMA: S_j = Q K_j^T (M=128, N=64, K=256) into S buffer j&1; after
-//              the softmax wrote P_j: O += P_j V_j (M=128, N=256, K=64, V as
-//              an MN-major operand). S_{j+2} is issued right after P_j V_j, so
-//              the tensor core computes the next scores while the softmax
-//              threads work on the current ones.
+// One CTA = one 128-query tile of one (batch, head) and one range of key tiles
+// (64 keys each); 6 warps:
+//   warp 0     TMA: the Q tile once, then K_j, V_j through a 3-slot ring, in
+//              64-column (128-byte, SW128) boxes; Q, K and V have their own 3-D
+//              tensor maps (columns, rows, batch) whose column extent ends at the
+//              tensor's last head, so padded boxes read zeros, never a
+//              neighbour's or a row's end.
+//   warp 1     MMA: S_j = Q K_j^T (M=128, N=64, K = d rounded up to 16) into S
+//              buffer j&1; after the softmax wrote P_j: O += P_j V_j (M=128,
+//              N = d rounded up to 16, K=64, V as an MN-major operand). S_{j+2}
+//              is issued right after P_j V_j, so scores for the next tiles are
+//              computed while the softmax threads work on the current one.
 //   warps 2-5  softmax, one query row per thread (TMEM lane): row max over the
 //              64 keys, p = 2^(s*scale*log2e - m) as f16 into the 128B-swizzled
 //              A operand; the reference max m moves only when the row max grows
 //              by more than 2^8, and only then are the sum and the row of O in
-//              TMEM rescaled. At the end O is read, divided by the sum and
-//              stored (256 columns per row).
-// Every wait is bounded; a timeout records an error code and the CTA unwinds.
+//              TMEM rescaled. At the end O is divided by the sum and stored, or,
+//              when the keys are split over several CTAs, written unnormalised
+//              with m and the sum for a combine kernel.
+// d = 72: the S product runs K = 80, so the 8 padding columns of the Q tile are
+// zeroed in shared memory before the first MMA (the matching K columns then
+// contribute nothing). Every wait is bounded; a timeout records an error code
+// and the CTA unwinds.
 #include <algorithm>
 
 #include "common.cuh"
@@ -30,19 +40,25 @@
 namespace s3b {
 namespace {
 
-constexpr int kD = 256;
-constexpr int kAtoms = kD / 64;                          // 64-column (128-byte) swizzle atoms per row
 constexpr int kBQ = 128;
 constexpr int kBK = 64;
 constexpr int kSlots = 3;
-constexpr uint32_t kQBytes = kBQ * kD * 2;               // 64 KB: 4 atoms of 128 rows x 128 B
-constexpr uint32_t kKVAtom = kBK * 128;                  // 8 KB: 64 rows x 128 B
-constexpr uint32_t kKVBytes = kBK * kD * 2;              // 32 KB
-constexpr uint32_t kPBytes = kBQ * kBK * 2;              // 16 KB: one atom of 128 rows x 128 B
+constexpr uint32_t kPBytes = kBQ * kBK * 2;  // 16 KB: one atom of 128 rows x 128 B
 constexpr int kThreads = 192;
 constexpr float kLazyMax = 8.0f;
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kOCol = 256;                          // O at TMEM columns [256, 512)
+constexpr uint32_t kOCol = 128;              // S buffers at TMEM columns [0,64), [64,128); O from 128
+
+template <int D>
+struct WideCfg {
+  static constexpr int DK = (D + 15) / 16 * 16;              // K of Q K^T and N of P V
+  static constexpr int NA = (DK + 63) / 64;                  // 64-column swizzle atoms loaded per row
+  static constexpr uint32_t QBytes = kBQ * NA * 128;         // Q tile: NA atoms of 128 rows x 128 B
+  static constexpr uint32_t KVAtom = kBK * 128;              // 8 KB: 64 rows x 128 B
+  static constexpr uint32_t KVBytes = NA * KVAtom;
+  static constexpr uint32_t TmemCols = kOCol + DK <= 256 ? 256 : 512;
+  static constexpr int MinBlocks = TmemCols <= 256 ? 2 : 1;  // CTAs per SM (TMEM, shared memory)
+  static constexpr size_t Smem = 1024 + QBytes + kSlots * KVBytes + kPBytes + 16 * 8 + 16;
+};
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -53,8 +69,8 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 __device__ __forceinline__ uint64_t sdesc_mn_sw128_v(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)(kKVAtom >> 4) << 16;  // LBO
-  d |= (uint64_t)(1024u >> 4) << 32;    // SBO
+  d |= (uint64_t)((kBK * 128) >> 4) << 16;  // LBO
+  d |= (uint64_t)(1024u >> 4) << 32;        // SBO
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;
   return d;
@@ -85,15 +101,19 @@ __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sy
                  "=r"(R[28]), "=r"(R[29]), "=r"(R[30]), "=r"(R[31])                                          \
                : "r"(taddr))
 
-#define TMEM_ST32(taddr, R)                                                                                  \
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "                                               \
-               "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"                                    \
-               "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),             \
+#define TMEM_LD16(taddr, R)                                                                                  \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "                                                     \
+               "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"                             \
+               : "=r"(R[0]), "=r"(R[1]), "=r"(R[2]), "=r"(R[3]), "=r"(R[4]), "=r"(R[5]), "=r"(R[6]),         \
+                 "=r"(R[7]), "=r"(R[8]), "=r"(R[9]), "=r"(R[10]), "=r"(R[11]), "=r"(R[12]), "=r"(R[13]),     \
+                 "=r"(R[14]), "=r"(R[15])                                                                    \
+               : "r"(taddr))
+
+#define TMEM_ST16(taddr, R)                                                                                  \
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "                                               \
+               "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),                     \
                "r"(R[0]), "r"(R[1]), "r"(R[2]), "r"(R[3]), "r"(R[4]), "r"(R[5]), "r"(R[6]), "r"(R[7]),       \
-               "r"(R[8]), "r"(R[9]), "r"(R[10]), "r"(R[11]), "r"(R[12]), "r"(R[13]), "r"(R[14]), "r"(R[15]), \
-               "r"(R[16]), "r"(R[17]), "r"(R[18]), "r"(R[19]), "r"(R[20]), "r"(R[21]), "r"(R[22]),           \
-               "r"(R[23]), "r"(R[24]), "r"(R[25]), "r"(R[26]), "r"(R[27]), "r"(R[28]), "r"(R[29]),           \
-               "r"(R[30]), "r"(R[31])                                                                        \
+               "r"(R[8]), "r"(R[9]), "r"(R[10]), "r"(R[11]), "r"(R[12]), "r"(R[13]), "r"(R[14]), "r"(R[15])  \
                : "memory")
 
 __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err) {
@@ -106,18 +126,18 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   }
 }
 
-struct Tc256Args {
+struct WideArgs {
   int heads, nq, nk;
   int head_rows;      // 1: head h of batch b is row block b*heads + h (layout [B][H][n][d]); 0: columns h*x_h
   int q_h, k_h, v_h;  // column offset (elements) of head h = h * x_h (head_rows == 0)
   __half* o;
-  long long o_n;      // output row stride; row = map_row(omap, b*nq + i), head h at column h*256
+  long long o_n;      // output row stride; row = map_row(omap, b*nq + i), head h at column h*d
   RowMap omap;
   float sl2;          // softmax scale * log2(e)
   // key split: CTA `split` of a query tile covers key tiles [split*tiles_per, +tiles_per); with
   // n_split > 1 it writes its unnormalised O, reference max and sum to ws_o / ws_ml for the combine
   int n_split, tiles_per;
-  float* ws_o;   // [bh][split][nq][256]
+  float* ws_o;   // [bh][split][nq][d]
   float* ws_ml;  // [bh][split][nq][2]
 };
 
@@ -184,14 +204,18 @@ __device__ __forceinline__ float row_p64(uint32_t taddr, int kvalid, float sl2, 
   return (s0 + s1) + (s2 + s3);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    attn_tc256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                      const __grid_constant__ CUtensorMap tv, Tc256Args a, int* err) {
+template <int D>
+__global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
+    attn_wide_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                     const __grid_constant__ CUtensorMap tv, WideArgs a, int* err) {
+  using C = WideCfg<D>;
+  constexpr int DK = C::DK, NA = C::NA;
+  constexpr bool kPadQ = DK > D;  // Q columns [D, DK) must read as zero
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* sQ = smem;                           // 64 KB
-  uint8_t* sKV = sQ + kQBytes;                  // kSlots x 32 KB
-  uint8_t* sP = sKV + kSlots * kKVBytes;        // 16 KB
+  uint8_t* sQ = smem;                           // NA atoms of 16 KB
+  uint8_t* sKV = sQ + C::QBytes;                // kSlots x NA x 8 KB
+  uint8_t* sP = sKV + kSlots * C::KVBytes;      // 16 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;                 // [kSlots]
@@ -202,7 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_empty = p_full + 1;
   uint64_t* o_done = p_empty + 1;
   uint64_t* mma_done = o_done + 1;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* q_ready = mma_done + 1;             // Q padding zeroed (d = 72)
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(q_ready + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -233,6 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(p_empty, 1);
     mbar_init(o_done, 1);
     mbar_init(mma_done, 1);
+    mbar_init(q_ready, 4);
     *s_abort = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -241,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tv);
   }
   if (warp == 1) {
-    tmem_alloc(s_tmem, kTmemCols);  // S buffers: [0,64), [64,128); O: [256,512)
+    tmem_alloc(s_tmem, C::TmemCols);  // S buffers: [0,64), [64,128); O: [128, 128 + DK)
     tmem_relinquish();
   }
   tc_fence_before();
@@ -251,9 +277,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, kQBytes);
+      mbar_arrive_expect_tx(q_full, C::QBytes);
 #pragma unroll
-      for (int at = 0; at < kAtoms; ++at)
+      for (int at = 0; at < NA; ++at)
         tma_load_3d(&tq, q_full, sQ + at * (kBQ * 128), hc * a.q_h + at * 64, qb * kBQ, rb);
       uint32_t armed = 0, armed_phase = 0;
       bool ok = true;
@@ -261,13 +287,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = t % kSlots;
         const uint32_t use = (uint32_t)(t / kSlots);
         if (!mbar_wait(&kv_empty[s], (use & 1) ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
-        mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
+        mbar_arrive_expect_tx(&kv_full[s], C::KVBytes);
         const int j = t >> 1;
         const CUtensorMap* map = (t & 1) ? &tv : &tk;
         const int col0 = hc * ((t & 1) ? a.v_h : a.k_h);
 #pragma unroll
-        for (int at = 0; at < kAtoms; ++at)
-          tma_load_3d(map, &kv_full[s], sKV + s * kKVBytes + at * kKVAtom, col0 + at * 64, (j0 + j) * kBK, rb);
+        for (int at = 0; at < NA; ++at)
+          tma_load_3d(map, &kv_full[s], sKV + s * C::KVBytes + at * C::KVAtom, col0 + at * 64, (j0 + j) * kBK, rb);
         armed |= 1u << s;
         armed_phase = (armed_phase & ~(1u << s)) | ((use & 1) << s);
       }
@@ -278,8 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(kBQ, kBK, 0);                 // Q, K both K-major
-      constexpr uint32_t idesc_o = idesc_f16(kBQ, kD, 0) | (1u << 16);     // B (V) MN-major
-      bool ok = mbar_wait(q_full, 0, s_abort, err, kErrWaitFull);
+      constexpr uint32_t idesc_o = idesc_f16(kBQ, DK, 0) | (1u << 16);     // B (V) MN-major
+      bool ok = mbar_wait(kPadQ ? q_ready : q_full, 0, s_abort, err, kErrWaitFull);
       tc_fence_after();
       const uint32_t qa = smem_u32(sQ);
       bool issued = false;
@@ -290,12 +316,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j >= 2 && !mbar_wait(&s_empty[sb], (uint32_t)((j - 2) >> 1) & 1, s_abort, err, kErrWaitMisc))
           return false;
         tc_fence_after();
-        const uint32_t ka = smem_u32(sKV + s * kKVBytes);
+        const uint32_t ka = smem_u32(sKV + s * C::KVBytes);
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
+        for (int kk = 0; kk < DK / 16; ++kk) {
           const uint32_t off = (uint32_t)((kk & 3) * 32);
           const uint64_t dq = sdesc_k_sw128(qa + (uint32_t)((kk >> 2) * (kBQ * 128)) + off);
-          const uint64_t dk = sdesc_k_sw128(ka + (uint32_t)((kk >> 2) * kKVAtom) + off);
+          const uint64_t dk = sdesc_k_sw128(ka + (uint32_t)((kk >> 2) * C::KVAtom) + off);
           tc_mma_f16(tmem + (uint32_t)(sb * kBK), dq, dk, idesc_s, kk != 0);
         }
         tc_commit(&s_full[sb]);
@@ -311,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(p_full, (uint32_t)j & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
         if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t pa = smem_u32(sP), va = smem_u32(sKV + s * kKVBytes);
+        const uint32_t pa = smem_u32(sP), va = smem_u32(sKV + s * C::KVBytes);
         const int nk16 = min(kBK / 16, (a.nk - (j0 + j) * kBK + 15) / 16);  // K steps holding a real key
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
@@ -339,6 +365,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* prow = sP + row * 128;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
+    if constexpr (kPadQ) {
+      // zero this row's Q columns [D, DK) (one 16-byte unit of the last atom)
+      ok = mbar_wait(q_full, 0, s_abort, err, kErrWaitFull);
+      if (ok) {
+        constexpr int col = D % 64;  // first padding column inside its atom
+        static_assert(DK - D == 8 && col % 8 == 0, "d = 72-like padding: one 16-byte unit");
+        uint8_t* qrow = sQ + (D / 64) * (kBQ * 128) + row * 128;
+        *reinterpret_cast<uint4*>(qrow + (((col >> 3) ^ (row & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+      ok = __all_sync(0xffffffffu, ok);
+    }
     for (int j = 0; j < nkb && ok; ++j) {
       const int sb = j & 1;
       if (!mbar_wait(&s_full[sb], (uint32_t)(j >> 1) & 1, s_abort, err, kErrWaitTmemFull)) ok = false;
@@ -370,13 +410,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (__any_sync(0xffffffffu, resc)) {
           const float f = resc ? alpha : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < kD; c += 32) {
-            uint32_t o[32];
-            TMEM_LD32(tmem + lane_off + kOCol + (uint32_t)c, o);
+          for (int c = 0; c < DK; c += 16) {
+            uint32_t o[16];
+            TMEM_LD16(tmem + lane_off + kOCol + (uint32_t)c, o);
             tc_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            TMEM_ST32(tmem + lane_off + kOCol + (uint32_t)c, o);
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            TMEM_ST16(tmem + lane_off + kOCol + (uint32_t)c, o);
           }
           tc_wait_st();
         }
@@ -397,37 +437,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int qi = qb * kBQ + row;
       if (a.n_split > 1) {
         // partial result of this key split: O relative to 2^m_ref, the reference max and the sum
-        const size_t prow_idx = ((size_t)bh * a.n_split + split) * a.nq + qi;
+        const size_t pidx = ((size_t)bh * a.n_split + split) * a.nq + qi;
 #pragma unroll 1
-        for (int c = 0; c < kD; c += 32) {
-          uint32_t o[32];
-          TMEM_LD32(tmem + lane_off + kOCol + (uint32_t)c, o);
+        for (int c = 0; c < DK; c += 16) {
+          uint32_t o[16];
+          TMEM_LD16(tmem + lane_off + kOCol + (uint32_t)c, o);
           tc_wait_ld();
           if (qi < a.nq) {
-            float4* op = reinterpret_cast<float4*>(a.ws_o + prow_idx * kD + c);
+            float4* op = reinterpret_cast<float4*>(a.ws_o + pidx * D + c);
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-              op[u] = make_float4(__uint_as_float(o[4 * u]), __uint_as_float(o[4 * u + 1]),
-                                  __uint_as_float(o[4 * u + 2]), __uint_as_float(o[4 * u + 3]));
+            for (int u = 0; u < 4; ++u)
+              if (c + 4 * u < D)
+                op[u] = make_float4(__uint_as_float(o[4 * u]), __uint_as_float(o[4 * u + 1]),
+                                    __uint_as_float(o[4 * u + 2]), __uint_as_float(o[4 * u + 3]));
           }
         }
-        if (qi < a.nq) *reinterpret_cast<float2*>(a.ws_ml + prow_idx * 2) = make_float2(m_ref, l);
+        if (qi < a.nq) *reinterpret_cast<float2*>(a.ws_ml + pidx * 2) = make_float2(m_ref, l);
       } else {
         const long long orow = qi < a.nq ? map_row(a.omap, (long long)b * a.nq + qi) : -1;
         const float inv = 1.0f / l;
 #pragma unroll 1
-        for (int c = 0; c < kD; c += 32) {
-          uint32_t o[32];
-          TMEM_LD32(tmem + lane_off + kOCol + (uint32_t)c, o);
+        for (int c = 0; c < DK; c += 16) {
+          uint32_t o[16];
+          TMEM_LD16(tmem + lane_off + kOCol + (uint32_t)c, o);
           tc_wait_ld();
           if (orow >= 0) {
-            uint4* op = reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * kD + c);
+            uint4* op = reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * D + c);
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              op[u] = make_uint4(pack_h2(__uint_as_float(o[8 * u]) * inv, __uint_as_float(o[8 * u + 1]) * inv),
-                                 pack_h2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv),
-                                 pack_h2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv),
-                                 pack_h2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv));
+            for (int u = 0; u < 2; ++u)
+              if (c + 8 * u < D)
+                op[u] = make_uint4(pack_h2(__uint_as_float(o[8 * u]) * inv, __uint_as_float(o[8 * u + 1]) * inv),
+                                   pack_h2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv),
+                                   pack_h2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv),
+                                   pack_h2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv));
           }
         }
       }
@@ -437,14 +479,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, C::TmemCols);
   }
 }
 
 // Merges the key splits of each query row: M = max of the splits' reference
 // maxima, O = sum_s 2^(m_s - M) O_s, l = sum_s 2^(m_s - M) l_s, out = O / l
-// (f16). One warp per row, 8 columns per lane.
-__global__ void __launch_bounds__(256) attn_combine256_kernel(Tc256Args a, long long rows) {
+// (f16). One warp per row.
+template <int D>
+__global__ void __launch_bounds__(256) attn_wide_combine_kernel(WideArgs a, long long rows) {
   const long long r = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -453,35 +496,41 @@ __global__ void __launch_bounds__(256) attn_combine256_kernel(Tc256Args a, long 
   float mmax = -INFINITY;
   for (int s = 0; s < a.n_split; ++s)
     mmax = fmaxf(mmax, a.ws_ml[(((size_t)bh * a.n_split + s) * a.nq + qi) * 2]);
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  constexpr int PER = (D + 31) / 32;  // columns lane + 32*i
+  float acc[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
   float lsum = 0.f;
   for (int s = 0; s < a.n_split; ++s) {
     const size_t pr = ((size_t)bh * a.n_split + s) * a.nq + qi;
     const float2 ml = *reinterpret_cast<const float2*>(a.ws_ml + pr * 2);
     const float w = ml.x == -INFINITY ? 0.f : ex2(ml.x - mmax);
     lsum += w * ml.y;
-    const float4* op = reinterpret_cast<const float4*>(a.ws_o + pr * kD + lane * 8);
-    const float4 x0 = op[0], x1 = op[1];
-    acc[0] += w * x0.x; acc[1] += w * x0.y; acc[2] += w * x0.z; acc[3] += w * x0.w;
-    acc[4] += w * x1.x; acc[5] += w * x1.y; acc[6] += w * x1.z; acc[7] += w * x1.w;
+    const float* op = a.ws_o + pr * D;
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (lane + 32 * i < D) acc[i] += w * op[lane + 32 * i];
   }
   const long long orow = map_row(a.omap, (long long)b * a.nq + qi);
   if (orow < 0) return;
   const float inv = 1.0f / lsum;
-  *reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * kD + lane * 8) =
-      make_uint4(pack_h2(acc[0] * inv, acc[1] * inv), pack_h2(acc[2] * inv, acc[3] * inv),
-                 pack_h2(acc[4] * inv, acc[5] * inv), pack_h2(acc[6] * inv, acc[7] * inv));
+  __half* o = a.o + orow * a.o_n + h * D;
+#pragma unroll
+  for (int i = 0; i < PER; ++i)
+    if (lane + 32 * i < D) o[lane + 32 * i] = __float2half_rn(acc[i] * inv);
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// 3-D map (columns, rows, batch) over x[b*xb + n*xn + col], box = 64 columns x box_rows x 1, SW128.
-int map3(EncodeTiledFn enc, CUtensorMap* m, const __half* x, long long xn, long long xb, int rows, int batch,
-         int box_rows) {
-  if ((reinterpret_cast<uintptr_t>(x) & 15) || (xn % 8) || (xb % 8)) return -2;
-  cuuint64_t dims[3] = {(cuuint64_t)xn, (cuuint64_t)rows, (cuuint64_t)batch};
+// 3-D map (columns, rows, batch) over x[b*xb + n*xn + col] with `cols` columns
+// (the tensor's own extent: reads past it return zeros), box = 64 columns x
+// box_rows x 1, SW128.
+int map3(EncodeTiledFn enc, CUtensorMap* m, const __half* x, long long cols, long long xn, long long xb, int rows,
+         int batch, int box_rows) {
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (xn % 8) || (xb % 8) || cols <= 0 || cols > xn) return -2;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)(xn * 2), (cuuint64_t)(xb * 2)};
   cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
@@ -492,24 +541,18 @@ int map3(EncodeTiledFn enc, CUtensorMap* m, const __half* x, long long xn, long 
              : -12;
 }
 
-}  // namespace
-
-void* tensor_map_encoder();  // gemm.cu
-
-size_t attention_tc256_ws_bytes(int n_split, int batch_heads, int nq) {
-  return (size_t)n_split * batch_heads * nq * (kD + 2) * sizeof(float);
-}
-
-int attention_tc256(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes, int* err, cudaStream_t st) {
+template <int D>
+int launch_wide(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes, int* err, cudaStream_t st) {
+  using C = WideCfg<D>;
   EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!enc) return -10;
   if (p.heads <= 0 || batch_heads % p.heads || p.nq <= 0 || p.nk <= 0) return -2;
-  if ((p.o_n % 8) || (reinterpret_cast<uintptr_t>(p.o) & 15)) return -2;
+  if ((p.o_n % 8) || (reinterpret_cast<uintptr_t>(p.o) & 15) || ((long long)p.heads * D > p.o_n)) return -2;
   // heads either as column offsets inside a row (fused projections) or as
   // consecutive row blocks ([B][H][n][d]); anything else is not supported here
   const bool head_rows = p.heads > 1 && p.q_h >= (long long)p.nq * p.q_n;
   int blocks;
-  long long qb, kb, vb;
+  long long qb, kb, vb, qc, kc, vc;  // batch strides and column extents
   if (head_rows) {
     if (p.k_h < (long long)p.nk * p.k_n || p.v_h < (long long)p.nk * p.v_n) return -2;
     if (batch_heads > p.heads &&
@@ -519,24 +562,24 @@ int attention_tc256(const AttnParams& p, int batch_heads, float* ws, size_t ws_b
     qb = p.q_h;
     kb = p.k_h;
     vb = p.v_h;
-    if (p.q_n < kD || p.k_n < kD || p.v_n < kD) return -2;
+    qc = kc = vc = D;
   } else {
     if ((p.q_h % 8) || (p.k_h % 8) || (p.v_h % 8)) return -2;
-    if ((long long)(p.heads - 1) * p.q_h + kD > p.q_n || (long long)(p.heads - 1) * p.k_h + kD > p.k_n ||
-        (long long)(p.heads - 1) * p.v_h + kD > p.v_n)
-      return -2;
     blocks = batch_heads / p.heads;
     // a single batch may carry any batch stride; use one that satisfies the map's rules
     qb = blocks > 1 ? p.q_b : (long long)p.nq * p.q_n;
     kb = blocks > 1 ? p.k_b : (long long)p.nk * p.k_n;
     vb = blocks > 1 ? p.v_b : (long long)p.nk * p.v_n;
+    qc = (long long)(p.heads - 1) * p.q_h + D;
+    kc = (long long)(p.heads - 1) * p.k_h + D;
+    vc = (long long)(p.heads - 1) * p.v_h + D;
   }
   CUtensorMap tq, tk, tv;
-  int rc = map3(enc, &tq, p.q, p.q_n, qb, p.nq, blocks, kBQ);
-  if (!rc) rc = map3(enc, &tk, p.k, p.k_n, kb, p.nk, blocks, kBK);
-  if (!rc) rc = map3(enc, &tv, p.v, p.v_n, vb, p.nk, blocks, kBK);
+  int rc = map3(enc, &tq, p.q, qc, p.q_n, qb, p.nq, blocks, kBQ);
+  if (!rc) rc = map3(enc, &tk, p.k, kc, p.k_n, kb, p.nk, blocks, kBK);
+  if (!rc) rc = map3(enc, &tv, p.v, vc, p.v_n, vb, p.nk, blocks, kBK);
   if (rc) return rc;
-  Tc256Args a;
+  WideArgs a;
   a.heads = p.heads;
   a.head_rows = head_rows ? 1 : 0;
   a.nq = p.nq;
@@ -552,33 +595,57 @@ int attention_tc256(const AttnParams& p, int batch_heads, float* ws, size_t ws_b
   // 32 tiles on 148 SMs), keeping at least 4 key tiles per split and no split empty
   const int n_qt = (p.nq + kBQ - 1) / kBQ;
   const long long units = (long long)n_qt * batch_heads;
+  const long long slots = (long long)num_sms() * C::MinBlocks;
   const int nkb = (p.nk + kBK - 1) / kBK;
   int n_split = 1;
-  if (ws && units < num_sms()) n_split = (int)std::max(1LL, std::min((long long)num_sms() / units, (long long)nkb / 4));
+  if (ws && units < slots) n_split = (int)std::max(1LL, std::min(slots / units, (long long)nkb / 4));
   int tiles_per = (nkb + n_split - 1) / n_split;
   n_split = (nkb + tiles_per - 1) / tiles_per;
-  if (n_split > 1 && ws_bytes < attention_tc256_ws_bytes(n_split, batch_heads, p.nq)) n_split = 1, tiles_per = nkb;
+  if (n_split > 1 && ws_bytes < attention_wide_ws_bytes(D, n_split, batch_heads, p.nq)) {
+    n_split = 1;
+    tiles_per = nkb;
+  }
   a.n_split = n_split;
   a.tiles_per = tiles_per;
   a.ws_o = ws;
-  a.ws_ml = ws ? ws + (size_t)n_split * batch_heads * p.nq * kD : nullptr;
-  constexpr size_t smem = 1024 + kQBytes + kSlots * kKVBytes + kPBytes + 16 * 8 + 16;
-  static_assert(smem <= 232448, "shared memory per CTA");
+  a.ws_ml = ws ? ws + (size_t)n_split * batch_heads * p.nq * D : nullptr;
+  static_assert(C::Smem <= 232448, "shared memory per CTA");
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(attn_tc256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(attn_wide_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::Smem) !=
         cudaSuccess)
       return -13;
     attr = true;
   }
   const long long n_cta = units * n_split;
   if (n_cta > 0x7fffffffLL) return -2;
-  attn_tc256_kernel<<<(unsigned)n_cta, kThreads, smem, st>>>(tq, tk, tv, a, err);
-  int rc2 = launch_status("attention_tc256");
+  attn_wide_kernel<D><<<(unsigned)n_cta, kThreads, C::Smem, st>>>(tq, tk, tv, a, err);
+  int rc2 = launch_status("attention_wide");
   if (rc2 || n_split == 1) return rc2;
   const long long rows = (long long)batch_heads * p.nq;
-  attn_combine256_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(a, rows);
-  return launch_status("attention_tc256 combine");
+  attn_wide_combine_kernel<D><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(a, rows);
+  return launch_status("attention_wide combine");
+}
+
+}  // namespace
+
+size_t attention_wide_ws_bytes(int d, int n_split, int batch_heads, int nq) {
+  return (size_t)n_split * batch_heads * nq * (d + 2) * sizeof(float);
+}
+
+int attention_wide_max_split(int d, long long units) {
+  const long long slots = (long long)num_sms() * (d == 256 ? 1 : 2);
+  return units < slots ? (int)(slots / units) : 1;
+}
+
+int attention_wide(const AttnParams& p, int d, int batch_heads, float* ws, size_t ws_bytes, int* err,
+                   cudaStream_t st) {
+  switch (d) {
+    case 72: return launch_wide<72>(p, batch_heads, ws, ws_bytes, err, st);
+    case 96: return launch_wide<96>(p, batch_heads, ws, ws_bytes, err, st);
+    case 256: return launch_wide<256>(p, batch_heads, ws, ws_bytes, err, st);
+    default: return -2;
+  }
 }
 
 }  // namespace s3b

@@ -103,15 +103,18 @@ int attention(const AttnParams& p, int D, int batch_heads, cudaStream_t st);
 int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v_col, int heads, int ntok, int nwin,
                    __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int* err,
                    cudaStream_t st);
-// Tensor-core (tcgen05) flash attention, head dim 256 (memory attention):
-// q / k / v with their own row strides and row counts (nq, nk), heads as
-// column offsets (q_h etc. < row length) or as row blocks ([B][H][n][d]).
-// Returns -2 for layouts it does not take. When the query tiles alone would
-// leave SMs idle, the keys are split over several CTAs whose partial results
-// (in `ws`, attention_tc256_ws_bytes(n_split, ...) bytes for n_split up to
-// SMs / query tiles) a second kernel merges; ws = NULL disables splitting.
-int attention_tc256(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes, int* err, cudaStream_t st);
-size_t attention_tc256_ws_bytes(int n_split, int batch_heads, int nq);
+// Tensor-core (tcgen05) flash attention for head dims d = 72, 96, 256
+// (Hiera-L, Hiera-T, memory attention): q / k / v with their own row strides
+// and row counts (nq, nk), heads as column offsets (q_h etc. < row length) or
+// as row blocks ([B][H][n][d]). Returns -2 for layouts or d it does not take.
+// When the query tiles alone would leave SMs idle, the keys are split over
+// several CTAs whose partial results (in `ws`: attention_wide_ws_bytes(d,
+// n_split, ...) bytes for n_split up to attention_wide_max_split(d, query
+// tiles x batch_heads)) a second kernel merges; ws = NULL disables splitting.
+int attention_wide(const AttnParams& p, int d, int batch_heads, float* ws, size_t ws_bytes, int* err,
+                   cudaStream_t st);
+size_t attention_wide_ws_bytes(int d, int n_split, int batch_heads, int nq);
+int attention_wide_max_split(int d, long long units);
 void* tensor_map_encoder();
 
 // LayerNorm over the last dim (C) of f32 rows, eps as given; out f16 or f32.

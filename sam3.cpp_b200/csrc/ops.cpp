@@ -81,21 +81,23 @@ int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
     rc = attention_tc64(p.q, p.q_n, 0, (int)kq, (int)vq, p.heads, p.nq, batch_heads / p.heads, p.o, p.o_n, p.omap,
                         p.scale, ctx->attention_exp_poly, ctx->d_err, ctx->stream);
   } else {
-    // d = 256 (memory attention) on the tcgen05 kernel when its layout rules hold, else mma.sync
+    // d = 256 (memory attention) and d = 72 / 96 (Hiera) with at least one full query tile on the
+    // tcgen05 kernel when its layout rules hold, else mma.sync
     rc = -2;
-    if (ctx->attention_impl != 1 && D == 256) {
+    if (ctx->attention_impl != 1 && (D == 256 || ((D == 72 || D == 96) && p.nq >= 128))) {
       // workspace for key splits (used when the query tiles leave SMs idle)
       const long long units = (long long)((p.nq + 127) / 128) * batch_heads;
+      const int max_split = attention_wide_max_split(D, units);
       float* ws = nullptr;
       size_t ws_bytes = 0;
-      if (units < num_sms()) {
-        ws_bytes = attention_tc256_ws_bytes((int)(num_sms() / units), batch_heads, p.nq);
+      if (max_split > 1) {
+        ws_bytes = attention_wide_ws_bytes(D, max_split, batch_heads, p.nq);
         int brc = 0;
-        DevBuf* buf = ctx->buf("attn_tc256_split", ws_bytes, &brc);
+        DevBuf* buf = ctx->buf("attn_wide_split", ws_bytes, &brc);
         if (brc) return brc;
         ws = buf->as<float>();
       }
-      rc = attention_tc256(p, batch_heads, ws, ws_bytes, ctx->d_err, ctx->stream);
+      rc = attention_wide(p, D, batch_heads, ws, ws_bytes, ctx->d_err, ctx->stream);
     }
     if (rc == -2) rc = attention(p, D, batch_heads, ctx->stream);
   }

@@ -196,7 +196,9 @@ def test_gemm_f16_out_strided(engine):
                                                  # stage-1 windows at 16 frames per pass)
                                                  (96, 16, 16, 4, 16400),
                                                  # d = 256 on the tcgen05 kernel: heads as row blocks, ragged keys
-                                                 (256, 300, 500, 2, 2), (256, 128, 64, 1, 3), (256, 1, 77, 3, 1)])
+                                                 (256, 300, 500, 2, 2), (256, 128, 64, 1, 3), (256, 1, 77, 3, 1),
+                                                 # d = 72 / 96 with a full query tile on the tcgen05 kernel
+                                                 (72, 300, 500, 3, 2), (96, 1000, 300, 2, 1), (72, 4096, 4096, 1, 1)])
 def test_attention(engine, D, nq, nk, heads, batch):
     g = torch.Generator(device="cuda").manual_seed(D + nq + nk)
     q = torch.randn(batch, heads, nq, D, device="cuda", generator=g).half()
