@@ -641,6 +641,7 @@ int attention_wide_max_split(int d, long long units) {
 int attention_wide(const AttnParams& p, int d, int batch_heads, float* ws, size_t ws_bytes, int* err,
                    cudaStream_t st) {
   switch (d) {
+    case 64: return launch_wide<64>(p, batch_heads, ws, ws_bytes, err, st);
     case 72: return launch_wide<72>(p, batch_heads, ws, ws_bytes, err, st);
     case 96: return launch_wide<96>(p, batch_heads, ws, ws_bytes, err, st);
     case 256: return launch_wide<256>(p, batch_heads, ws, ws_bytes, err, st);

@@ -72,7 +72,7 @@ int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
   }
   // the tcgen05 kernel serves d = 64 attention over one fused qkv buffer (the ViT blocks)
   const long long kq = p.k - p.q, vq = p.v - p.q;
-  const bool tc_ok = ctx->attention_impl != 1 && D == 64 && p.nq == p.nk && p.q_n == p.k_n && p.q_n == p.v_n &&
+  const bool tc_ok = ctx->attention_impl == 0 && D == 64 && p.nq == p.nk && p.q_n == p.k_n && p.q_n == p.v_n &&
                      p.q_b == p.k_b && p.q_b == p.v_b && p.q_b == (long long)p.nq * p.q_n && p.q_h == 64 &&
                      p.k_h == 64 && p.v_h == 64 && kq > 0 && vq > 0 && kq + 64LL * p.heads <= p.q_n &&
                      vq + 64LL * p.heads <= p.q_n && batch_heads % p.heads == 0;
@@ -84,7 +84,8 @@ int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
     // d = 256 (memory attention) and d = 72 / 96 (Hiera) with at least one full query tile on the
     // tcgen05 kernel when its layout rules hold, else mma.sync
     rc = -2;
-    if (ctx->attention_impl != 1 && (D == 256 || ((D == 72 || D == 96) && p.nq >= 128))) {
+    if (ctx->attention_impl != 1 &&
+        (D == 256 || ((D == 72 || D == 96 || (D == 64 && ctx->attention_impl == 2)) && p.nq >= 128))) {
       // workspace for key splits (used when the query tiles leave SMs idle)
       const long long units = (long long)((p.nq + 127) / 128) * batch_heads;
       const int max_split = attention_wide_max_split(D, units);
