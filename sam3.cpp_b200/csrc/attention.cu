@@ -229,8 +229,161 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
   }
 }
 
+// Small windows (nq <= 16, nk <= NKP <= 64; Hiera's pooled and stage-1/2
+// windows, e.g. 16 queries x 16 keys): one warp per (batch, head), four per
+// CTA, each with its own Q (16 rows), K and V (NKP rows) in shared memory; S,
+// the softmax and P V of the single key tile stay in registers.
+template <int D, int DR, int NKP>
+__global__ void __launch_bounds__(128) attn_small_kernel(AttnParams p, int batch_heads) {
+  constexpr int LD = D + 8;
+  constexpr int NT = D / 8;
+  constexpr int WROWS = 16 + 2 * NKP;  // Q, K, V rows of one warp
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x * 4 + warp;
+  if (bh >= batch_heads) return;  // whole warp; no CTA-wide barrier below
+  __half* sQ = reinterpret_cast<__half*>(smem_raw) + warp * WROWS * LD;
+  __half* sK = sQ + 16 * LD;
+  __half* sV = sK + NKP * LD;
+  const int b = bh / p.heads, h = bh - (bh / p.heads) * p.heads;
+  const __half* Qg = p.q + (long long)b * p.q_b + (long long)h * p.q_h;
+  const __half* Kg = p.k + (long long)b * p.k_b + (long long)h * p.k_h;
+  const __half* Vg = p.v + (long long)b * p.v_b + (long long)h * p.v_h;
+  if constexpr (DR < D) {
+    constexpr int PADC = (DR < D) ? D - DR : 1;
+    for (int i = lane; i < WROWS * PADC; i += 32) sQ[(i / PADC) * LD + DR + i % PADC] = __float2half_rn(0.f);
+  }
+  constexpr int CH = DR / 8;  // 16-byte chunks per row
+  for (int i = lane; i < 16 * CH; i += 32) {
+    const int r = i / CH, c = i - r * CH;
+    const bool ok = r < p.nq;
+    cp_async16(sQ + r * LD + c * 8, ok ? (const void*)(Qg + (long long)r * p.q_n + c * 8) : (const void*)Qg, ok);
+  }
+  for (int i = lane; i < NKP * CH; i += 32) {
+    const int r = i / CH, c = i - r * CH;
+    const bool ok = r < p.nk;
+    cp_async16(sK + r * LD + c * 8, ok ? (const void*)(Kg + (long long)r * p.k_n + c * 8) : (const void*)Kg, ok);
+    cp_async16(sV + r * LD + c * 8, ok ? (const void*)(Vg + (long long)r * p.v_n + c * 8) : (const void*)Vg, ok);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncwarp();
+
+  const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+  const int g = lane >> 2, t4 = lane & 3;
+  float s[NKP / 8][4];
+#pragma unroll
+  for (int n = 0; n < NKP / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    uint32_t a0, a1, a2, a3;
+    {
+      const int r = (lane & 7) + 8 * ((lane >> 3) & 1);
+      const int c = kk * 16 + 8 * (lane >> 4);
+      ldsm_x4(sQa + (uint32_t)((r * LD + c) * 2), a0, a1, a2, a3);
+    }
+#pragma unroll
+    for (int np = 0; np < NKP / 16; ++np) {
+      uint32_t b0, b1, b2, b3;
+      const int r = np * 16 + (lane & 7) + 8 * (lane >> 4);
+      const int c = kk * 16 + 8 * ((lane >> 3) & 1);
+      ldsm_x4(sKa + (uint32_t)((r * LD + c) * 2), b0, b1, b2, b3);
+      mma16816(s[2 * np], a0, a1, a2, a3, b0, b1);
+      mma16816(s[2 * np + 1], a0, a1, a2, a3, b2, b3);
+    }
+  }
+  // softmax over the nk real keys (rows g and g+8)
+  const float sl2 = p.scale * 1.4426950408889634f;
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int n = 0; n < NKP / 8; ++n) {
+    const int key = n * 8 + 2 * t4;
+    if (key >= p.nk) { s[n][0] = -INFINITY; s[n][2] = -INFINITY; }
+    if (key + 1 >= p.nk) { s[n][1] = -INFINITY; s[n][3] = -INFINITY; }
+    mx0 = fmaxf(mx0, fmaxf(s[n][0], s[n][1]));
+    mx1 = fmaxf(mx1, fmaxf(s[n][2], s[n][3]));
+  }
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  const float mn0 = mx0 * sl2, mn1 = mx1 * sl2;
+  float l0 = 0.f, l1 = 0.f;
+  uint32_t pa[NKP / 8][2];
+#pragma unroll
+  for (int n = 0; n < NKP / 8; ++n) {
+    const float p0 = exp2f(s[n][0] * sl2 - mn0), p1 = exp2f(s[n][1] * sl2 - mn0);
+    const float p2 = exp2f(s[n][2] * sl2 - mn1), p3 = exp2f(s[n][3] * sl2 - mn1);
+    l0 += p0 + p1;
+    l1 += p2 + p3;
+    pa[n][0] = pack_h2(p0, p1);
+    pa[n][1] = pack_h2(p2, p3);
+  }
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < NKP / 16; ++kk) {
+    const uint32_t a0 = pa[2 * kk][0], a1 = pa[2 * kk][1], a2 = pa[2 * kk + 1][0], a3 = pa[2 * kk + 1][1];
+#pragma unroll
+    for (int dp = 0; dp < NT / 2; ++dp) {
+      uint32_t b0, b1, b2, b3;
+      const int r = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+      const int c = dp * 16 + 8 * (lane >> 4);
+      ldsm_x4_t(sVa + (uint32_t)((r * LD + c) * 2), b0, b1, b2, b3);
+      mma16816(o[2 * dp], a0, a1, a2, a3, b0, b1);
+      mma16816(o[2 * dp + 1], a0, a1, a2, a3, b2, b3);
+    }
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+  const int r0 = g, r1 = g + 8;
+  const long long orow0 = r0 < p.nq ? map_row(p.omap, (long long)b * p.nq + r0) : -1;
+  const long long orow1 = r1 < p.nq ? map_row(p.omap, (long long)b * p.nq + r1) : -1;
+  __half* ob = p.o + (long long)h * DR;
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int c = n * 8 + 2 * t4;
+    if (c >= DR) continue;
+    if (orow0 >= 0)
+      *reinterpret_cast<__half2*>(ob + orow0 * p.o_n + c) = __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
+    if (orow1 >= 0)
+      *reinterpret_cast<__half2*>(ob + orow1 * p.o_n + c) = __floats2half2_rn(o[n][2] * inv1, o[n][3] * inv1);
+  }
+}
+
+template <int D, int DR, int NKP>
+int launch_small(const AttnParams& p, int batch_heads, cudaStream_t st) {
+  constexpr size_t smem = (size_t)4 * (16 + 2 * NKP) * (D + 8) * 2;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_small_kernel<D, DR, NKP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return -13;
+    attr = true;
+  }
+  const long long n_cta = ((long long)batch_heads + 3) / 4;
+  if (n_cta > 0x7fffffffLL) return -2;
+  attn_small_kernel<D, DR, NKP><<<(unsigned)n_cta, 128, smem, st>>>(p, batch_heads);
+  return launch_status("attention (small windows)");
+}
+
+template <int D, int DR>
+int launch_small_nk(const AttnParams& p, int batch_heads, cudaStream_t st) {
+  if (p.nk <= 16) return launch_small<D, DR, 16>(p, batch_heads, st);
+  if (p.nk <= 32) return launch_small<D, DR, 32>(p, batch_heads, st);
+  if (p.nk <= 48) return launch_small<D, DR, 48>(p, batch_heads, st);
+  return launch_small<D, DR, 64>(p, batch_heads, st);
+}
+
 template <int D, int DR>
 int launch_attn(const AttnParams& p, int batch_heads, cudaStream_t st) {
+  if constexpr (D <= 128) {
+    if (p.nq <= 16 && p.nk <= 64) return launch_small_nk<D, DR>(p, batch_heads, st);
+  }
   constexpr size_t smem = (size_t)(kBQ + 4 * kBKV) * (D + 8) * 2;
   static bool attr = false;
   if (!attr) {

@@ -16,99 +16,140 @@ namespace {
 
 constexpr int kMaxVec = 16;  // float4 per lane -> C <= 2048
 
-// One warp per row, NV = ceil(C / 128) float4 per lane held in registers (so
-// the register footprint, and with it the number of rows in flight per SM,
-// follows the row width). The row is streamed (read once), the output is
-// left in L2 for the GEMM that consumes it next.
-template <int NV>
+// One warp per R rows, NV = ceil(C / 128) float4 per lane and row held in
+// registers (so the register footprint, and with it the number of rows in
+// flight per SM, follows the row width; narrow rows are batched R to a warp so
+// their loads overlap). The row is streamed (read once), the output is left in
+// L2 for the GEMM that consumes it next.
+template <int NV, int R>
 __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, long long ldx,
                                                         void* __restrict__ y, int y_f32, long long ldy, long long rows,
                                                         int C, const float* __restrict__ gamma,
                                                         const float* __restrict__ beta, float eps, RowMap map) {
-  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const long long row0 = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * R;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const long long src = map_row(map, row);
-  if (src < 0) {
-    // padding row of a window partition: zeros (sam3.cpp:4199-4207 pads after the norm)
-    if (y_f32) {
-      float* yo = reinterpret_cast<float*>(y) + row * ldy;
-      for (int c = lane; c < C; c += 32) yo[c] = 0.f;
-    } else {
-      __half* yo = reinterpret_cast<__half*>(y) + row * ldy;
-      for (int c = lane; c < C; c += 32) yo[c] = __float2half_rn(0.f);
-    }
-    return;
-  }
-  const float* xr = x + src * ldx;
   const int nvec = C >> 2;
-  float4 v[NV];
+  float4 v[R][NV];
+  long long src[R];  // input row; -1: padding row of a window partition; -2: past the last row
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int vi = lane + 32 * i;
-    v[i] = vi < nvec ? __ldcs(reinterpret_cast<const float4*>(xr + 4 * vi)) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  float sum = 0.f;
+  for (int r = 0; r < R; ++r) {
+    src[r] = row0 + r < rows ? map_row(map, row0 + r) : -2;
+    const float* xr = x + (src[r] > 0 ? src[r] : 0) * ldx;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float mean = sum / (float)C;
-  float var = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int vi = lane + 32 * i;
-    if (vi < nvec) {
-      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-      var += (a * a + b * b) + (c * c + d * d);
+    for (int i = 0; i < NV; ++i) {
+      const int vi = lane + 32 * i;
+      v[r][i] = (src[r] >= 0 && vi < nvec) ? __ldcs(reinterpret_cast<const float4*>(xr + 4 * vi))
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
+  float mean[R], rstd[R];
 #pragma unroll
-  for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-  const float rstd = rsqrtf(var / (float)C + eps);
+  for (int r = 0; r < R; ++r) {
+    float sum = 0.f;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int vi = lane + 32 * i;
-    if (vi < nvec) {
-      const float4 g = *reinterpret_cast<const float4*>(gamma + 4 * vi);
-      const float4 b = beta ? *reinterpret_cast<const float4*>(beta + 4 * vi) : make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 o;
-      o.x = (v[i].x - mean) * rstd * g.x + b.x;
-      o.y = (v[i].y - mean) * rstd * g.y + b.y;
-      o.z = (v[i].z - mean) * rstd * g.z + b.z;
-      o.w = (v[i].w - mean) * rstd * g.w + b.w;
+    for (int i = 0; i < NV; ++i) sum += (v[r][i].x + v[r][i].y) + (v[r][i].z + v[r][i].w);
+    mean[r] = sum;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < R; ++r) mean[r] += __shfl_xor_sync(0xffffffffu, mean[r], o);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    mean[r] /= (float)C;
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+        const float a = v[r][i].x - mean[r], b = v[r][i].y - mean[r], c = v[r][i].z - mean[r], d = v[r][i].w - mean[r];
+        var += (a * a + b * b) + (c * c + d * d);
+      }
+    }
+    rstd[r] = var;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < R; ++r) rstd[r] += __shfl_xor_sync(0xffffffffu, rstd[r], o);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (src[r] == -2) continue;
+    const long long row = row0 + r;
+    if (src[r] < 0) {
+      // padding row of a window partition: zeros (sam3.cpp:4199-4207 pads after the norm)
       if (y_f32) {
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + row * ldy + 4 * vi) = o;
+        float* yo = reinterpret_cast<float*>(y) + row * ldy;
+        for (int c = lane; c < C; c += 32) yo[c] = 0.f;
       } else {
-        __half2 h0 = __floats2half2_rn(o.x, o.y), h1 = __floats2half2_rn(o.z, o.w);
-        uint2 u;
-        u.x = *reinterpret_cast<uint32_t*>(&h0);
-        u.y = *reinterpret_cast<uint32_t*>(&h1);
-        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(y) + row * ldy + 4 * vi) = u;
+        __half* yo = reinterpret_cast<__half*>(y) + row * ldy;
+        for (int c = lane; c < C; c += 32) yo[c] = __float2half_rn(0.f);
+      }
+      continue;
+    }
+    const float rs = rsqrtf(rstd[r] / (float)C + eps);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+        const float4 g = *reinterpret_cast<const float4*>(gamma + 4 * vi);
+        const float4 b = beta ? *reinterpret_cast<const float4*>(beta + 4 * vi) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 o;
+        o.x = (v[r][i].x - mean[r]) * rs * g.x + b.x;
+        o.y = (v[r][i].y - mean[r]) * rs * g.y + b.y;
+        o.z = (v[r][i].z - mean[r]) * rs * g.z + b.z;
+        o.w = (v[r][i].w - mean[r]) * rs * g.w + b.w;
+        if (y_f32) {
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + row * ldy + 4 * vi) = o;
+        } else {
+          __half2 h0 = __floats2half2_rn(o.x, o.y), h1 = __floats2half2_rn(o.z, o.w);
+          uint2 u;
+          u.x = *reinterpret_cast<uint32_t*>(&h0);
+          u.y = *reinterpret_cast<uint32_t*>(&h1);
+          *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(y) + row * ldy + 4 * vi) = u;
+        }
       }
     }
   }
 }
 
+// One thread per 8 consecutive columns of an output row (one 16-byte store):
+// 32-bit index math once per thread, then (ci, ky, kx) advance column by
+// column without divisions; consecutive threads take consecutive column
+// groups, so their reads run along the input rows.
 __global__ void im2col_image_kernel(const float* __restrict__ img, int B, int Cin, int H, int W, int k, int stride,
                                     int pad, int OH, int OW, __half* __restrict__ out, int Kpad) {
-  const long long total = (long long)B * OH * OW * Kpad;
-  const int K = Cin * k * k;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / Kpad;
-    const int col = (int)(i - row * Kpad);
-    float val = 0.f;
-    if (col < K) {
-      const int ci = col / (k * k);
-      const int rem = col - ci * k * k;
-      const int ky = rem / k, kx = rem - (rem / k) * k;
-      const long long b = row / ((long long)OH * OW);
-      const int pix = (int)(row - b * OH * OW);
-      const int oy = pix / OW, ox = pix - (pix / OW) * OW;
-      const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
-      if (iy >= 0 && iy < H && ix >= 0 && ix < W) val = img[((b * Cin + ci) * H + iy) * (long long)W + ix];
+  const int vpr = Kpad >> 3;  // 8-column groups per output row
+  const int total = B * OH * OW * vpr;
+  const int K = Cin * k * k, kk = k * k, ohw = OH * OW;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+    const int row = t / vpr, v = t - row * vpr;
+    const int b = row / ohw, pix = row - b * ohw;
+    const int oy = pix / OW, ox = pix - oy * OW;
+    const int iy0 = oy * stride - pad, ix0 = ox * stride - pad;
+    const int col0 = v * 8;
+    int ci = col0 / kk;
+    const int rem = col0 - ci * kk;
+    int ky = rem / k, kx = rem - ky * k;
+    float val[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      val[e] = 0.f;
+      const int iy = iy0 + ky, ix = ix0 + kx;
+      if (col0 + e < K && iy >= 0 && iy < H && ix >= 0 && ix < W)
+        val[e] = __ldg(img + (((long long)b * Cin + ci) * H + iy) * (long long)W + ix);
+      if (++kx == k) {
+        kx = 0;
+        if (++ky == k) {
+          ky = 0;
+          ++ci;
+        }
+      }
     }
-    out[i] = __float2half_rn(val);
+    __half2 h[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(val[2 * e], val[2 * e + 1]);
+    *reinterpret_cast<uint4*>(out + (long long)row * Kpad + col0) = *reinterpret_cast<const uint4*>(h);
   }
 }
 
@@ -278,13 +319,14 @@ int layernorm(const float* x, long long ldx, void* y, int y_f32, long long ldy, 
               const float* gamma, const float* beta, float eps, const RowMap& map, cudaStream_t st) {
   if (C % 4 || C > 4 * 32 * kMaxVec || ldx % 4 || ldy % 4 || rows <= 0) return -1;
   const int warps = 8;
-  const long long blocks = (rows + warps - 1) / warps;
-  if (blocks > 0x7fffffffLL) return -1;
   const int nv = (C + 127) / 128;
+  const int rpw = nv <= 2 ? 4 : nv == 3 ? 2 : 1;  // rows per warp
+  const long long blocks = (rows + (long long)warps * rpw - 1) / ((long long)warps * rpw);
+  if (blocks > 0x7fffffffLL) return -1;
 #define S3B_LN_CASE(N)                                                                                            \
   case N:                                                                                                        \
-    layernorm_kernel<N><<<(unsigned)blocks, warps * 32, 0, st>>>(x, ldx, y, y_f32, ldy, rows, C, gamma, beta, eps, \
-                                                                  map);                                          \
+    layernorm_kernel<N, (N <= 2 ? 4 : N == 3 ? 2 : 1)><<<(unsigned)blocks, warps * 32, 0, st>>>(                 \
+        x, ldx, y, y_f32, ldy, rows, C, gamma, beta, eps, map);                                                  \
     break;
   switch (nv) {
     S3B_LN_CASE(1) S3B_LN_CASE(2) S3B_LN_CASE(3) S3B_LN_CASE(4) S3B_LN_CASE(5) S3B_LN_CASE(6) S3B_LN_CASE(7)
@@ -299,8 +341,9 @@ int layernorm(const float* x, long long ldx, void* y, int y_f32, long long ldy, 
 
 int im2col_image(const float* img, int B, int Cin, int H, int W, int k, int stride, int pad, int OH, int OW,
                  __half* out, int Kpad, cudaStream_t st) {
-  if (Kpad < Cin * k * k) return -1;
-  const long long n = (long long)B * OH * OW * Kpad;
+  if (Kpad < Cin * k * k || Kpad % 8 || (reinterpret_cast<uintptr_t>(out) & 15)) return -1;
+  const long long n = (long long)B * OH * OW * (Kpad / 8);  // threads: one per 8 output columns
+  if (n > 0x7fffffffLL) return -1;
   im2col_image_kernel<<<grid_for(n, 256), 256, 0, st>>>(img, B, Cin, H, W, k, stride, pad, OH, OW, out, Kpad);
   return launch_ok();
 }

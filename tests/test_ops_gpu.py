@@ -198,7 +198,11 @@ def test_gemm_f16_out_strided(engine):
                                                  # d = 256 on the tcgen05 kernel: heads as row blocks, ragged keys
                                                  (256, 300, 500, 2, 2), (256, 128, 64, 1, 3), (256, 1, 77, 3, 1),
                                                  # d = 72 / 96 with a full query tile on the tcgen05 kernel
-                                                 (72, 300, 500, 3, 2), (96, 1000, 300, 2, 1), (72, 4096, 4096, 1, 1)])
+                                                 (72, 300, 500, 3, 2), (96, 1000, 300, 2, 1), (72, 4096, 4096, 1, 1),
+                                                 # small windows, one warp per (batch, head): every key padding
+                                                 # (16 / 32 / 48 / 64), ragged query counts, pad d = 72
+                                                 (96, 16, 16, 2, 301), (96, 4, 16, 4, 99), (72, 16, 64, 2, 50),
+                                                 (64, 9, 40, 3, 7), (128, 1, 5, 2, 3), (72, 4, 16, 8, 33)])
 def test_attention(engine, D, nq, nk, heads, batch):
     g = torch.Generator(device="cuda").manual_seed(D + nq + nk)
     q = torch.randn(batch, heads, nq, D, device="cuda", generator=g).half()
