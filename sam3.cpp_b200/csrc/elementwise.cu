@@ -182,16 +182,27 @@ __device__ __forceinline__ __half tmax<__half>(__half a, __half b) { return __hm
 
 template <typename T>
 __global__ void maxpool2_cl_kernel(const T* __restrict__ x, int B, int H, int W, int C, T* __restrict__ y) {
-  const int OH = H / 2, OW = W / 2;
-  const long long total = (long long)B * OH * OW * C;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % C);
-    const long long pix = i / C;
-    const long long b = pix / ((long long)OH * OW);
-    const int rem = (int)(pix - b * OH * OW);
-    const int oy = rem / OW, ox = rem - (rem / OW) * OW;
-    const T* p = x + ((b * H + 2 * oy) * W + 2 * ox) * C + c;
-    y[i] = tmax(tmax(p[0], p[C]), tmax(p[(long long)W * C], p[(long long)W * C + C]));
+  // 16 bytes (4 f32 or 8 f16 channels) per thread; 32-bit index math (the
+  // launcher checks the element count)
+  constexpr int V = 16 / sizeof(T);
+  const int OH = H / 2, OW = W / 2, cv = C / V, ohw = OH * OW;
+  const int total = B * ohw * cv;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int c = i % cv, pix = i / cv;
+    const int b = pix / ohw, rem = pix - b * ohw;
+    const int oy = rem / OW, ox = rem - oy * OW;
+    const uint4* p = reinterpret_cast<const uint4*>(x + (((long long)b * H + 2 * oy) * W + 2 * ox) * C) + c;
+    const long long wr = (long long)W * cv;  // one input row, in 16-byte units
+    uint4 q[4] = {__ldcs(p), __ldcs(p + cv), __ldcs(p + wr), __ldcs(p + wr + cv)};
+    uint4 r;
+    const T* a0 = reinterpret_cast<const T*>(&q[0]);
+    const T* a1 = reinterpret_cast<const T*>(&q[1]);
+    const T* a2 = reinterpret_cast<const T*>(&q[2]);
+    const T* a3 = reinterpret_cast<const T*>(&q[3]);
+    T* o = reinterpret_cast<T*>(&r);
+#pragma unroll
+    for (int e = 0; e < V; ++e) o[e] = tmax(tmax(a0[e], a1[e]), tmax(a2[e], a3[e]));
+    reinterpret_cast<uint4*>(y)[i] = r;
   }
 }
 
@@ -239,9 +250,15 @@ __global__ void preprocess_kernel(const uint8_t* __restrict__ img, int B, int H,
   }
 }
 
+// 4 values per thread (n4 = n / 4 float4 groups), then the n % 4 tail.
 __global__ void cast_kernel(const float* __restrict__ x, long long n, __half* __restrict__ y) {
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-    y[i] = __float2half_rn(x[i]);
+  const long long n4 = n >> 2;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const float4 v = __ldcs(reinterpret_cast<const float4*>(x) + i);
+    __half2 h[2] = {__floats2half2_rn(v.x, v.y), __floats2half2_rn(v.z, v.w)};
+    reinterpret_cast<uint2*>(y)[i] = *reinterpret_cast<const uint2*>(h);
+  }
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) y[4 * n4 + threadIdx.x] = __float2half_rn(x[4 * n4 + threadIdx.x]);
 }
 
 __global__ void add_scaled_kernel(const float* __restrict__ a, const float* __restrict__ b, float s, long long n,
@@ -356,12 +373,16 @@ int im2col_3x3_cl(const __half* x, int B, int H, int W, int C, __half* out, cuda
 }
 
 int maxpool2_cl_f16(const __half* x, int B, int H, int W, int C, __half* y, cudaStream_t st) {
-  const long long n = (long long)B * (H / 2) * (W / 2) * C;
+  const long long n = (long long)B * (H / 2) * (W / 2) * (C / 8);  // 16-byte groups
+  if (C % 8 || n > 0x7fffffffLL || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
+    return -1;
   maxpool2_cl_kernel<__half><<<grid_for(n, 256), 256, 0, st>>>(x, B, H, W, C, y);
   return launch_ok();
 }
 int maxpool2_cl_f32(const float* x, int B, int H, int W, int C, float* y, cudaStream_t st) {
-  const long long n = (long long)B * (H / 2) * (W / 2) * C;
+  const long long n = (long long)B * (H / 2) * (W / 2) * (C / 4);  // 16-byte groups
+  if (C % 4 || n > 0x7fffffffLL || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
+    return -1;
   maxpool2_cl_kernel<float><<<grid_for(n, 256), 256, 0, st>>>(x, B, H, W, C, y);
   return launch_ok();
 }
@@ -382,7 +403,8 @@ int preprocess_u8(const uint8_t* img, int B, int H, int W, const float mean[3], 
 }
 
 int cast_f32_f16(const float* x, long long n, __half* y, cudaStream_t st) {
-  cast_kernel<<<grid_for(n, 256), 256, 0, st>>>(x, n, y);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 7)) return -1;
+  cast_kernel<<<grid_for((n + 3) / 4, 256), 256, 0, st>>>(x, n, y);
   return launch_ok();
 }
 

@@ -248,8 +248,8 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW>
 __global__ void __launch_bounds__(gemm_threads(EW), 1)
     gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       const __grid_constant__ CUtensorMap tmC, int M, int N, int K, EpiParams ep,
-                       int resid_in_place, int* err) {
+                       const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M,
+                       int N, int K, EpiParams ep, int resid_in_place, int* err) {
   constexpr int BN_CTA = PAIR ? BN / 2 : BN;  // rows of B this CTA loads per stage
   constexpr int TM = PAIR ? 2 * kBM : kBM;    // output rows per tile
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
@@ -301,6 +301,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (TMA_EPI) tma_prefetch_desc(&tmC);
+    if (TMA_EPI && resid_in_place) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) {
     if (PAIR) {
@@ -425,7 +426,10 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       wait_buf_read();
       if (gcb < N) {
         mbar_arrive_expect_tx(&rfull[bsel], kStageBufBytes);
-        tma_load_2d(&tmC, &rfull[bsel], sC + bsel * kStageBufBytes, gcb, m0);
+        // the residual's row: the output row itself, or (resid_mod: a table repeated every
+        // resid_mod rows, a multiple of the 128-row tile) its row inside the table
+        const int rrow = ep.resid_mod ? (int)((long long)m0 % ep.resid_mod) : m0;
+        tma_load_2d(&tmR, &rfull[bsel], sC + bsel * kStageBufBytes, gcb, rrow);
       } else {
         mbar_arrive(&rfull[bsel]);
       }
@@ -609,7 +613,7 @@ template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW = 8>
 int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
                 const EpiParams& ep, int resid_in_place, int* err, cudaStream_t st) {
   constexpr int BN_CTA = PAIR ? BN / 2 : BN;
-  CUtensorMap ma, mb, mc;
+  CUtensorMap ma, mb, mc, mr;
   int rc = make_map_2d(&ma, A, M, K, lda, kBM, 2);
   if (rc) return rc;
   rc = make_map_2d(&mb, B, N, K, ldb, BN_CTA, 2);
@@ -619,6 +623,13 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
     if (rc) return rc;
   } else {
     mc = ma;  // unused
+  }
+  if (TMA_EPI && resid_in_place && static_cast<const void*>(ep.resid) != ep.out) {
+    // a separate f32 residual (resid_mod rows repeated, or M rows)
+    rc = make_map_2d(&mr, ep.resid, ep.resid_mod ? ep.resid_mod : M, N, ep.ldr, kBM, 4);
+    if (rc) return rc;
+  } else {
+    mr = mc;
   }
   constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN_CTA) * kBK * 2 + (TMA_EPI ? 4 * kStageBufBytes : 0) +
                           (2 * STAGES + 9) * 8 + 16;
@@ -653,7 +664,7 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
   const int tiles = ((M + tm - 1) / tm) * ((N + BN - 1) / BN);
   const int units = tiles < max_units ? tiles : max_units;
   if (!PAIR) {
-    kernel<<<units, kThreads, smem, st>>>(ma, mb, mc, M, N, K, ep, resid_in_place, err);
+    kernel<<<units, kThreads, smem, st>>>(ma, mb, mc, mr, M, N, K, ep, resid_in_place, err);
     return launch_status("gemm");
   }
   cudaLaunchConfig_t cfg = {};
@@ -668,7 +679,7 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, M, N, K, ep, resid_in_place, err);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, mr, M, N, K, ep, resid_in_place, err);
   if (e != cudaSuccess) {
     fprintf(stderr, "s3b: CUDA error at gemm (pair) launch: %s (%d)\n", cudaGetErrorString(e), (int)e);
     cudaGetLastError();
@@ -707,10 +718,17 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
   if (ep.mode != EPI_STORE && ep.mode != EPI_DECONV2) return -3;
   if (ep.rope && (ep.rope_D <= 0 || (ep.rope_D & 1) || ep.rope_mod <= 0)) return -3;
   const int eb = ep.out_f32 ? 4 : 2;
-  // TMA epilogue: plain row-major output, residual absent or the output itself
-  const bool tma_epi = ep.mode == EPI_STORE && ep.map.kind == 0 && !ep.resid_up && ep.resid_mod == 0 &&
-                       (ep.resid == nullptr ||
-                        (static_cast<const void*>(ep.resid) == ep.out && ep.ldr == ep.ldo && ep.out_f32)) &&
+  // TMA epilogue: plain row-major output; the residual (f32 outputs) absent, the output itself, or a
+  // separate f32 matrix, possibly a table repeated every resid_mod rows (a multiple of the 128-row tile,
+  // so no tile straddles a repeat), loaded by TMA into the staging buffer
+  const bool resid_sep = ep.resid != nullptr && static_cast<const void*>(ep.resid) != ep.out;
+  const bool resid_ok =
+      ep.resid == nullptr ||
+      (ep.out_f32 && !ep.resid_up &&
+       (resid_sep ? ((ep.resid_mod == 0 || ep.resid_mod % kBM == 0) && (ep.ldr * 4) % 16 == 0 && ep.ldr >= N &&
+                     (reinterpret_cast<uintptr_t>(ep.resid) & 15) == 0)
+                  : (ep.resid_mod == 0 && ep.ldr == ep.ldo)));
+  const bool tma_epi = ep.mode == EPI_STORE && ep.map.kind == 0 && resid_ok &&
                        (reinterpret_cast<uintptr_t>(ep.out) & 15) == 0 && (ep.ldo * eb) % 16 == 0 && ep.ldo >= N;
   const int resid_in_place = (tma_epi && ep.resid) ? 1 : 0;
   if (tma_epi) {
