@@ -69,8 +69,8 @@ int s3b_sync(s3b_ctx* ctx);
  * cta_group::2: 1, default, those with K >= 2048 and the f16-output ones
  * with 16 epilogue warps; 2 all; 0 none, 128-row tiles on single SMs;
  * applies to every context of the process);
- * "gemm_wide_epilogue" (1, default: short-K GEMMs with f16 outputs run 16
- * epilogue warps; 0: 8; process-wide);
+ * "gemm_wide_epilogue" (1, default: GEMMs with K < 2048 run 16 epilogue
+ * warps instead of 8; 0: all run 8; process-wide);
  * "attention_exp_poly" (0-4: of every 8 softmax exponentials in the tcgen05
  * kernel, how many are evaluated by a polynomial on the FMA pipe instead of
  * the MUFU unit; a tuning knob, results agree to f16 rounding);

@@ -251,7 +251,7 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
   }
   if (k == "gemm_wide_epilogue") {
     if (value < 0 || value > 1) return set_error(ctx, kErrArg, "gemm_wide_epilogue must be 0 or 1");
-    set_gemm_wide_epilogue(value != 0);
+    set_gemm_wide_epilogue((int)value);
     return kOk;
   }
   if (k == "attention_exp_poly") {

@@ -42,7 +42,7 @@ constexpr int gemm_threads(int ew) { return 64 + 32 * ew; }
 constexpr uint32_t kStageBufBytes = 16384;  // 128 rows x 128 B
 
 int g_gemm_pairs = 1;         // 256-row tiles on SM pairs: 0 never, 1 long-K GEMMs, 2 every wide GEMM
-bool g_gemm_wide_epi = true;  // 16 epilogue warps for short-K GEMMs with f16 outputs
+int g_gemm_wide_epi = 1;      // 16 epilogue warps for short-K GEMMs: 0 never, 1 always
 
 
 // Two f32 -> one packed f16x2 register (lo in the low half), round to nearest even.
@@ -407,10 +407,10 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
     uint32_t aphase = 0;
     uint32_t chunk_ctr = 0;
     uint32_t r_issued0 = 0, r_issued1 = 0, r_used0 = 0, r_used1 = 0;  // residual loads per staging buffer
-    // the 16-warp variant serves f16 outputs without a residual only (fewer live registers)
-    constexpr bool kF16Only = EW == 16;
-    const bool out_f32 = kF16Only ? false : (ep.out_f32 != 0);
-    const int rip = kF16Only ? 0 : resid_in_place;
+    // residual chunks are TMA-loaded into the staging buffers (two per group with 8 warps, one
+    // with 16: the second chunk of a group then waits for the first chunk's store to read it)
+    const bool out_f32 = ep.out_f32 != 0;
+    const int rip = resid_in_place;
     const int cw = out_f32 ? 32 : 64;                   // chunk = 128 B of columns: 32 f32 or 64 f16
     // staging buffer of chunk `ctr`, and how many chunks used that buffer before it
     auto buf_of = [&](uint32_t ctr) -> int { return grp * NBUF + (NBUF == 1 ? 0 : (int)(ctr & 1)); };
@@ -733,13 +733,14 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
   const int resid_in_place = (tma_epi && ep.resid) ? 1 : 0;
   if (tma_epi) {
     if (N <= 128) return launch_gemm<128, 4, true, false>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
-    // f16 outputs of short-K GEMMs (QKV + RoPE, MLP fc1 + GELU): their epilogue outlasts the main loop
-    // with 8 epilogue warps, so they run 16
-    if (!resid_in_place && !ep.out_f32 && K < 2048 && g_gemm_wide_epi) {
+    // short-K GEMMs (QKV + RoPE, MLP fc1 + GELU, attention proj + residual): their epilogue outlasts
+    // the main loop with 8 epilogue warps, so they run 16 (measured 4-12% faster on the f32
+    // in-place-residual proj, 2-20% on the f16 ones)
+    if (K < 2048 && g_gemm_wide_epi) {
       // with 16 epilogue warps the pair main loop pays off (measured 3-4% on QKV + RoPE)
-      if (g_gemm_pairs >= 1 && M > 2 * kBM)
-        return launch_gemm<256, 5, true, true, 16>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
-      return launch_gemm<256, 3, true, false, 16>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
+      if (M > 2 * kBM && (g_gemm_pairs == 2 || (g_gemm_pairs == 1 && !ep.out_f32)))
+        return launch_gemm<256, 5, true, true, 16>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
+      return launch_gemm<256, 3, true, false, 16>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
     }
     // 256-row tiles on SM pairs where the main loop dominates (long K): measured faster for
     // K = 4736 (ViT fc2), slower for K = 1024 GEMMs whose epilogue (GELU, RoPE, residual)
@@ -753,6 +754,6 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
 }
 
 void set_gemm_pairs(int mode) { g_gemm_pairs = mode; }
-void set_gemm_wide_epilogue(bool on) { g_gemm_wide_epi = on; }
+void set_gemm_wide_epilogue(int mode) { g_gemm_wide_epi = mode; }
 
 }  // namespace s3b

@@ -75,8 +75,9 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
 // Process-wide: which wide TMA-epilogue GEMMs use 256-row tiles on SM pairs:
 // 0 none, 1 (default) those with K >= 2048 or f16 outputs on 16 epilogue warps, 2 all.
 void set_gemm_pairs(int mode);
-// Process-wide: whether short-K GEMMs with f16 outputs use 16 epilogue warps (default on).
-void set_gemm_wide_epilogue(bool on);
+// Process-wide: which short-K (K < 2048) GEMMs use 16 epilogue warps: 0 none,
+// 1 (default) those with f16 outputs, 2 all.
+void set_gemm_wide_epilogue(int mode);
 
 // Flash attention (online softmax, f16 in / f32 acc / f16 out).
 struct AttnParams {

@@ -40,13 +40,17 @@ def test_gemm(engine, M, N, K, act):
     assert err < tol, f"max abs err {err} (tol {tol})"
 
 
-@pytest.mark.parametrize("pairs", [0, 1])
+@pytest.mark.parametrize("wide", [0, 1])
+@pytest.mark.parametrize("pairs", [0, 1, 2])
 @pytest.mark.parametrize("M,N,K,resid", [(41472 // 8 + 130, 3072, 1024, False), (1000, 4736, 1024, False),
-                                         (5184, 1024, 4736, True), (4097, 288, 152, True), (257, 512, 64, True)])
-def test_gemm_pairs_and_single(engine, pairs, M, N, K, resid):
-    """256-row tiles on SM pairs (cta_group::2) and 128-row tiles on single SMs, with ragged M / N / K
-    tails, f16 and f32 (in-place residual) outputs, against the fp32 reference."""
+                                         (5184, 1024, 4736, True), (4097, 288, 152, True), (257, 512, 64, True),
+                                         (5184, 1024, 1024, True)])
+def test_gemm_pairs_and_single(engine, wide, pairs, M, N, K, resid):
+    """256-row tiles on SM pairs (cta_group::2) and 128-row tiles on single SMs, 8 or 16 epilogue warps
+    (16: one staging buffer per column group), ragged M / N / K tails, f16 and f32 (in-place residual)
+    outputs, against the fp32 reference."""
     engine.set_option("gemm_pairs", pairs)
+    engine.set_option("gemm_wide_epilogue", wide)
     try:
         g = torch.Generator(device="cuda").manual_seed(M + N + K + pairs)
         A = (torch.randn(M, K, device="cuda", generator=g) * 0.5).half()
@@ -65,6 +69,7 @@ def test_gemm_pairs_and_single(engine, pairs, M, N, K, resid):
         assert err < 2e-3 * max(1.0, ref.abs().max().item()) + 1e-4 * K ** 0.5 + (0 if resid else 1e-2), err
     finally:
         engine.set_option("gemm_pairs", 1)
+        engine.set_option("gemm_wide_epilogue", 1)
 
 
 @pytest.mark.parametrize("pairs", [1, 2])
