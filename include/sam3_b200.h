@@ -64,7 +64,8 @@ int s3b_reset_stream(s3b_ctx* ctx);
 int s3b_sync(s3b_ctx* ctx);
 /* Options: "frames_per_pass" (encoder micro-batch, default 8);
  * "attention_impl" (0: tcgen05 flash attention where eligible, 1: always the
- * mma.sync kernel, 2: as 0 but d = 64 on the 64-key-tile tcgen05 kernel);
+ * mma.sync kernel, 2: as 0 but d = 64 on the 64-key-tile tcgen05 kernel,
+ * 3: as 0 but the d = 64 kernel stages P in shared memory instead of TMEM);
  * "gemm_pairs" (which wide GEMMs run 256-row tiles on pairs of SMs, tcgen05
  * cta_group::2: 1, default, those with K >= 2048 and the f16-output ones
  * with 16 epilogue warps; 2 all; 0 none, 128-row tiles on single SMs;

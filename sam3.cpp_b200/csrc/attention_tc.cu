@@ -2,19 +2,23 @@
 // ViT windowed and global attention of sam3_vit_block_forward
 // (ggml_flash_attn_ext at sam3.cpp:3774; softmax(q k^T / 8) v, no mask).
 //
-// One CTA = one 128-query tile of one (window, head); 10 warps, 2 CTAs / SM:
-//   warp 0     TMA: Q tile once, then K_j, V_j through a 3-slot ring. The
-//              tensor map is 3-D (channels, token, window) over the fused
-//              [tokens][3E] qkv buffer, so a tile never reads another window
-//              (rows past the window are zero-filled by TMA).
+// One CTA = one 128-query tile of one (window, head); 10 warps, 2 CTAs / SM.
+// TMEM (256 columns): S [0,128), O [128,192), P [192,256).
+//   warp 0     TMA: Q tile once, then K_j, V_j through a 5-slot ring (two key
+//              tiles of look-ahead). The tensor map is 3-D (channels, token,
+//              window) over the fused [tokens][3E] qkv buffer, so a tile never
+//              reads another window (rows past the window are zero-filled).
 //   warp 1     MMA: S = Q K_j^T (M=128, N=128, K=64) into TMEM; after the
-//              softmax wrote P_j: O += P_j V_j (M=128, N=64, K=128, V as an
-//              MN-major operand) into one TMEM accumulator kept across tiles.
+//              softmax wrote P_j: O += P_j V_j (M=128, N=64, K=128; A = P read
+//              from TMEM, B = V as an MN-major shared-memory operand) into one
+//              TMEM accumulator kept across tiles.
 //   warps 2-9  softmax. Each query row (TMEM lane) is shared by two threads,
 //              one per 64-key half of the tile: row max over its half (two
 //              32-column TMEM reads), one exchange of the partial maxima
 //              through shared memory, then p = 2^(s*scale*log2e - m) written
-//              as f16 into the 128B-swizzled A operand of the P V product.
+//              to TMEM as f16 pairs (the A operand of the P V product).
+//              TMEMP = false (a tuning option) keeps the earlier layout: P in
+//              a 128B-swizzled shared-memory operand and a 3-slot ring.
 //              The reference max m only moves when the row max grows by more
 //              than 2^8 (so P <= 256, exact enough in f16); only then are the
 //              row's running sum and its O row in TMEM rescaled, which after
@@ -99,6 +103,13 @@ __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sy
                  "=r"(R[21]), "=r"(R[22]), "=r"(R[23]), "=r"(R[24]), "=r"(R[25]), "=r"(R[26]), "=r"(R[27]),  \
                  "=r"(R[28]), "=r"(R[29]), "=r"(R[30]), "=r"(R[31])                                          \
                : "r"(taddr))
+
+#define TMEM_ST16(taddr, R)                                                                                  \
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "                                               \
+               "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),                     \
+               "r"(R[0]), "r"(R[1]), "r"(R[2]), "r"(R[3]), "r"(R[4]), "r"(R[5]), "r"(R[6]), "r"(R[7]),       \
+               "r"(R[8]), "r"(R[9]), "r"(R[10]), "r"(R[11]), "r"(R[12]), "r"(R[13]), "r"(R[14]), "r"(R[15])  \
+               : "memory")
 
 #define TMEM_ST32(taddr, R)                                                                                  \
   asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "                                               \
@@ -187,6 +198,41 @@ __device__ __forceinline__ float half_row_p(uint32_t taddr, int cbase, int kvali
   return (s0 + s1) + (s2 + s3);
 }
 
+// As half_row_p, but P goes to TMEM (the A operand of the P V product): this thread's 64 keys as
+// 32 columns of f16 pairs of its lane, starting at p_taddr.
+template <bool MASKED, int NPOLY>
+__device__ __forceinline__ float half_row_p_tmem(uint32_t taddr, int cbase, int kvalid, float sl2, float m,
+                                                 uint32_t p_taddr) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+  for (int c = 0; c < kBK / 2; c += 32) {
+    if (MASKED && cbase + c >= kvalid) break;
+    uint32_t r[32];
+    TMEM_LD32(taddr + (uint32_t)c, r);
+    tc_wait_ld();
+    uint32_t pk[16];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float p[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = 8 * u + e;
+        const float x = fmaf(__uint_as_float(r[i]), sl2, -m);
+        p[e] = e < NPOLY ? exp2_poly3(x) : ex2(x);
+        if (MASKED) p[e] = cbase + c + i < kvalid ? p[e] : 0.f;
+      }
+      s0 += p[0] + p[4];
+      s1 += p[1] + p[5];
+      s2 += p[2] + p[6];
+      s3 += p[3] + p[7];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pk[4 * u + e] = pack_h2(p[2 * e], p[2 * e + 1]);
+    }
+    TMEM_ST16(p_taddr + (uint32_t)(c / 2), pk);
+  }
+  return (s0 + s1) + (s2 + s3);
+}
+
 struct TcAttnArgs {
   int heads, ntok, nwin;
   int q_col, k_col, v_col;  // column offsets (elements) of q / k / v of head 0 in a row
@@ -197,21 +243,23 @@ struct TcAttnArgs {
 };
 
 // NPOLY of every 8 softmax exponentials use exp2_poly3, the rest MUFU ex2.
-template <int NPOLY>
+template <int NPOLY, bool TMEMP>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm, TcAttnArgs a, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem;                          // 16 KB
-  uint8_t* sKV = sQ + kTileBytes;              // kSlots x 16 KB
-  uint8_t* sP = sKV + kSlots * kTileBytes;     // 32 KB
-  float* xmax = reinterpret_cast<float*>(sP + kPBytes);  // [2 slots][2 halves][128 rows]
+  // TMEMP: P lives in TMEM (columns [192,256)) and its 32 KB of shared memory go to two more K/V slots
+  constexpr int kSl = TMEMP ? 5 : kSlots;
+  uint8_t* sKV = sQ + kTileBytes;              // kSl x 16 KB
+  uint8_t* sP = sKV + kSl * kTileBytes;        // 32 KB (shared-memory P only)
+  float* xmax = reinterpret_cast<float*>(sP + (TMEMP ? 0 : kPBytes));  // [2 slots][2 halves][128 rows]
   float* xsum = xmax + 4 * kBQ;                          // [2 halves][128 rows]
   uint64_t* bars = reinterpret_cast<uint64_t*>(xsum + 2 * kBQ);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;                // [kSlots]
-  uint64_t* kv_empty = kv_full + kSlots;       // [kSlots]
-  uint64_t* s_full = kv_empty + kSlots;
+  uint64_t* kv_full = bars + 1;                // [kSl]
+  uint64_t* kv_empty = kv_full + kSl;          // [kSl]
+  uint64_t* s_full = kv_empty + kSl;
   uint64_t* s_empty = s_full + 1;
   uint64_t* p_full = s_empty + 1;
   uint64_t* p_empty = p_full + 1;
@@ -230,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kSlots; ++s) {
+    for (int s = 0; s < kSl; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
@@ -262,8 +310,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint32_t armed = 0, armed_phase = 0;
       bool ok = true;
       for (int t = 0; t < 2 * nkb && ok; ++t) {
-        const int s = t % kSlots;
-        const uint32_t use = (uint32_t)(t / kSlots);
+        const int s = t % kSl;
+        const uint32_t use = (uint32_t)(t / kSl);
         if (!mbar_wait(&kv_empty[s], (use & 1) ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
         mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
         const int j = t >> 1;
@@ -273,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         armed_phase = (armed_phase & ~(1u << s)) | ((use & 1) << s);
       }
       mbar_wait_drain(q_full, 0, err);
-      for (int s = 0; s < kSlots; ++s)
+      for (int s = 0; s < kSl; ++s)
         if (armed & (1u << s)) mbar_wait_drain(&kv_full[s], (armed_phase >> s) & 1u, err);
     }
   } else if (warp == 1) {
@@ -287,8 +335,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       bool issued = false;
       // S_j = Q K_j^T; only the first 64 key columns when at most 64 keys of the tile are real
       auto issue_s = [&](int j) -> bool {
-        const int t = 2 * j, s = t % kSlots;
-        if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) return false;
+        const int t = 2 * j, s = t % kSl;
+        if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSl) & 1, s_abort, err, kErrWaitFull)) return false;
         if (j > 0 && !mbar_wait(s_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc)) return false;
         tc_fence_after();
         const uint64_t dk = sdesc_k_sw128(smem_u32(sKV + s * kTileBytes));
@@ -304,9 +352,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int j = 0; j < nkb && ok; ++j) {
         if (j + 1 < nkb && !issue_s(j + 1)) { ok = false; break; }
         // O += P_j V_j (after the softmax wrote P_j and, where needed, rescaled O)
-        const int t = 2 * j + 1, s = t % kSlots;
+        const int t = 2 * j + 1, s = t % kSl;
         if (!mbar_wait(p_full, (uint32_t)j & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
-        if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
+        if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSl) & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
         tc_fence_after();
         const uint32_t pa = smem_u32(sP), va = smem_u32(sKV + s * kTileBytes);
         // K steps that hold a real key (the softmax writes P only up to the chunk holding the last key)
@@ -315,9 +363,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int kk = 0; kk < kBK / 16; ++kk) {
           if (kk >= nk16) break;
           // P: two 128 x 64 K-major halves (32 B per K step inside a half); V: 16 key rows = 2048 B per K step
-          const uint64_t dp = sdesc_k_sw128(pa + (uint32_t)((kk >> 2) * (kBQ * 128) + (kk & 3) * 32));
           const uint64_t dv = sdesc_mn_sw128(va + (uint32_t)(kk * 2048));
-          tc_mma_f16(tmem + 128, dp, dv, idesc_o, (j > 0 || kk != 0) ? 1u : 0u);
+          if (TMEMP) {
+            // P from TMEM: 8 columns (16 keys as f16 pairs) per K step
+            tc_mma_f16_ts(tmem + 128, tmem + 192 + (uint32_t)(kk * 8), dv, idesc_o, (j > 0 || kk != 0) ? 1u : 0u);
+          } else {
+            const uint64_t dp = sdesc_k_sw128(pa + (uint32_t)((kk >> 2) * (kBQ * 128) + (kk & 3) * 32));
+            tc_mma_f16(tmem + 128, dp, dv, idesc_o, (j > 0 || kk != 0) ? 1u : 0u);
+          }
         }
         tc_commit(&kv_empty[s]);
         tc_commit(p_empty);
@@ -373,9 +426,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (ok && rows_live) {
         tc_fence_after();
         // p = 2^(s*sl2 - m_ref), row sum, f16 P into the swizzled A operand (half hsel of sP)
-        uint8_t* prow = sP + hsel * (kBQ * 128) + row * 128;
-        l += full_tile ? half_row_p<false, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row)
-                       : half_row_p<true, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row);
+        if (TMEMP) {
+          const uint32_t p_addr = tmem + lane_off + 192 + (uint32_t)(hsel * (kBK / 4));
+          l += full_tile ? half_row_p_tmem<false, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, p_addr)
+                         : half_row_p_tmem<true, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, p_addr);
+        } else {
+          uint8_t* prow = sP + hsel * (kBQ * 128) + row * 128;
+          l += full_tile ? half_row_p<false, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row)
+                         : half_row_p<true, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row);
+        }
         // the reference max moved: rescale this thread's 32 columns of the row's running O
         if (__any_sync(0xffffffffu, resc)) {
           uint32_t o[32];
@@ -389,8 +448,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       // S read, P written, O rescaled: hand all three to the MMA warp
+      if (TMEMP) tc_wait_st();
       tc_fence_before();
-      fence_proxy_async_smem();
+      if (!TMEMP) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(s_empty);
@@ -442,12 +502,15 @@ void* tensor_map_encoder();  // gemm.cu
 
 // q, k, v of head h of window w: base[w*ntok + n][col + h*64], one row stride for all three.
 int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v_col, int heads, int ntok, int nwin,
-                   __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int* err,
-                   cudaStream_t st) {
+                   __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int p_tmem,
+                   int* err, cudaStream_t st) {
   typedef void (*KernelFn)(const CUtensorMap, TcAttnArgs, int*);
-  static const KernelFn kernels[5] = {attn_tc_kernel<0>, attn_tc_kernel<1>, attn_tc_kernel<2>, attn_tc_kernel<3>,
-                                      attn_tc_kernel<4>};
-  if (exp_poly < 0 || exp_poly > 4) return -2;
+  static const KernelFn kernels[2][5] = {
+      {attn_tc_kernel<0, false>, attn_tc_kernel<1, false>, attn_tc_kernel<2, false>, attn_tc_kernel<3, false>,
+       attn_tc_kernel<4, false>},
+      {attn_tc_kernel<0, true>, attn_tc_kernel<1, true>, attn_tc_kernel<2, true>, attn_tc_kernel<3, true>,
+       attn_tc_kernel<4, true>}};
+  if (exp_poly < 0 || exp_poly > 4 || p_tmem < 0 || p_tmem > 1) return -2;
   EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!enc) return -10;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16 || (q_col % 8) || (k_col % 8) || (v_col % 8) ||
@@ -473,12 +536,13 @@ int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v
   a.o_n = o_n;
   a.omap = omap;
   a.sl2 = scale * 1.4426950408889634f;
-  constexpr size_t smem = 1024 + kTileBytes * (1 + kSlots) + kPBytes + kXchgBytes + 16 * 8 + 16;
-  static bool attr[5] = {false, false, false, false, false};
-  const KernelFn kfn = kernels[exp_poly];
-  if (!attr[exp_poly]) {
+  const size_t smem = p_tmem ? 1024 + kTileBytes * (1 + 5) + kXchgBytes + 24 * 8 + 16
+                             : 1024 + kTileBytes * (1 + kSlots) + kPBytes + kXchgBytes + 24 * 8 + 16;
+  static bool attr[2][5] = {};
+  const KernelFn kfn = kernels[p_tmem][exp_poly];
+  if (!attr[p_tmem][exp_poly]) {
     if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -13;
-    attr[exp_poly] = true;
+    attr[p_tmem][exp_poly] = true;
   }
   const long long n_cta = (long long)((ntok + kBQ - 1) / kBQ) * nwin * heads;
   if (n_cta > 0x7fffffffLL) return -2;

@@ -240,7 +240,7 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     return kOk;
   }
   if (k == "attention_impl") {
-    if (value < 0 || value > 2) return set_error(ctx, kErrArg, "attention_impl must be 0, 1 or 2");
+    if (value < 0 || value > 3) return set_error(ctx, kErrArg, "attention_impl must be 0, 1, 2 or 3");
     ctx->attention_impl = (int)value;
     return kOk;
   }

@@ -138,6 +138,17 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (f16/bf16 in, f32 acc).
+// A operand read from TMEM (K-major: lane = row, each 32-bit column holds two consecutive K
+// elements, 8 columns per K = 16 step), B from shared memory
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
   asm volatile(

@@ -211,7 +211,8 @@ struct s3b_ctx {
   std::map<std::string, std::shared_ptr<s3b::DevBuf>> ws;
   int max_frames_per_pass = 8;
   int stop_after_blocks = -1;  // test hook: run only the first n backbone blocks (-1: all)
-  int attention_impl = 0;      // 0: tcgen05 where eligible, 1: always mma.sync, 2: d = 64 on the wide tcgen05 kernel
+  int attention_impl = 0;      // 0: tcgen05 where eligible, 1: always mma.sync, 2: d = 64 on the wide tcgen05 kernel,
+                               // 3: as 0, d = 64 with P in shared memory
   int attention_exp_poly = 0;  // of every 8 softmax exponentials in the tcgen05 kernel, how many use the FMA pipe
   // launch accounting + optional per-kernel CUDA-event timing (s3b_profile_*)
   long long n_launches = 0;

@@ -237,14 +237,20 @@ def _ref_attention_qkv(qkv, nwin, heads, ntok, d, scale):
 @pytest.mark.parametrize("nwin,heads,ntok,d,pad", [(9, 16, 576, 64, 0), (1, 16, 5184, 64, 0), (3, 2, 64, 64, 0),
                                                    (2, 3, 200, 64, 64), (5, 1, 129, 64, 8), (1, 4, 1, 64, 0),
                                                    (4, 2, 300, 72, 0), (2, 2, 256, 96, 32)])
-def test_attention_qkv(engine, nwin, heads, ntok, d, pad):
+@pytest.mark.parametrize("impl", [0, 3])
+def test_attention_qkv(engine, nwin, heads, ntok, d, pad, impl):
+    """impl 0: the d = 64 softmax splits each row over two warps; 3: over two threads of one warp."""
     g = torch.Generator(device="cuda").manual_seed(nwin * 1000 + heads * 10 + ntok)
     E = heads * d
     qkv = (torch.randn(nwin * ntok, 3 * E + pad, device="cuda", generator=g) * 1.5).half()
     out = torch.full((nwin * ntok, E + pad), 7.0, device="cuda", dtype=torch.float16)
     scale = 1.0 / d ** 0.5
-    engine.attention_qkv(qkv, out, nwin, heads, ntok, d, scale)
-    engine.sync()
+    engine.set_option("attention_impl", impl)
+    try:
+        engine.attention_qkv(qkv, out, nwin, heads, ntok, d, scale)
+        engine.sync()
+    finally:
+        engine.set_option("attention_impl", 0)
     ref = _ref_attention_qkv(qkv, nwin, heads, ntok, d, scale)
     err = (out[:, :E].float() - ref).abs().max().item()
     assert err < 2e-2, err
@@ -258,7 +264,7 @@ def test_attention_qkv_impls_agree(engine):
     g = torch.Generator(device="cuda").manual_seed(5)
     qkv = (torch.randn(nwin * ntok, 3 * heads * d, device="cuda", generator=g) * 2).half()
     outs = []
-    for impl, poly in ((1, 0), (0, 0), (0, 2), (0, 4)):
+    for impl, poly in ((1, 0), (0, 0), (0, 2), (0, 4), (3, 0), (3, 3)):
         engine.set_option("attention_impl", impl)
         engine.set_option("attention_exp_poly", poly)
         out = torch.empty(nwin * ntok, heads * d, device="cuda", dtype=torch.float16)
@@ -269,6 +275,30 @@ def test_attention_qkv_impls_agree(engine):
     engine.set_option("attention_exp_poly", 0)
     for o in outs[1:]:
         assert (o - outs[0]).abs().max().item() < 1e-2
+
+
+@pytest.mark.parametrize("impl", [0, 3])
+def test_attention_qkv_growing_max(engine, impl):
+    """Keys whose logits grow tile by tile, so the running reference max of the d = 64 kernel moves
+    after the first key tile and the running O rows are rescaled in TMEM (both softmax layouts)."""
+    nwin, heads, ntok, d = 2, 4, 600, 64
+    E = heads * d
+    g = torch.Generator(device="cuda").manual_seed(21)
+    x = torch.randn(nwin, ntok, 3, heads, d, device="cuda", generator=g)
+    grow = 1.0 + torch.arange(ntok, device="cuda").float() / 128.0  # key tile j scaled by about 1 + j
+    x[:, :, 1] *= grow.view(1, ntok, 1, 1) * 3.0
+    x[:, :, 0] *= 3.0
+    qkv = x.reshape(nwin * ntok, 3 * E).half()
+    out = torch.empty(nwin * ntok, E, device="cuda", dtype=torch.float16)
+    engine.set_option("attention_impl", impl)
+    try:
+        engine.attention_qkv(qkv, out, nwin, heads, ntok, d, 0.125)
+        engine.sync()
+    finally:
+        engine.set_option("attention_impl", 0)
+    ref = _ref_attention_qkv(qkv, nwin, heads, ntok, d, 0.125)
+    assert torch.isfinite(out).all()
+    assert (out.float() - ref).abs().max().item() < 3e-2
 
 
 @pytest.mark.parametrize("rows,C,f32", [(5184, 1024, 0), (1000, 96, 1), (37, 256, 0), (64, 1152, 1)])
