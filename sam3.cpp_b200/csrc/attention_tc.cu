@@ -199,17 +199,25 @@ __device__ __forceinline__ float half_row_p(uint32_t taddr, int cbase, int kvali
 }
 
 // As half_row_p, but P goes to TMEM (the A operand of the P V product): this thread's 64 keys as
-// 32 columns of f16 pairs of its lane, starting at p_taddr.
+// 32 columns of f16 pairs of its lane, starting at p_taddr. The warp arrives on s_empty right after
+// its last read of S, so the MMA warp computes the next S while the exponentials run.
 template <bool MASKED, int NPOLY>
 __device__ __forceinline__ float half_row_p_tmem(uint32_t taddr, int cbase, int kvalid, float sl2, float m,
-                                                 uint32_t p_taddr) {
+                                                 uint32_t p_taddr, uint64_t* s_empty) {
   float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  bool released = false;
 #pragma unroll
   for (int c = 0; c < kBK / 2; c += 32) {
     if (MASKED && cbase + c >= kvalid) break;
     uint32_t r[32];
     TMEM_LD32(taddr + (uint32_t)c, r);
     tc_wait_ld();
+    if (c + 32 >= kBK / 2 || (MASKED && cbase + c + 32 >= kvalid)) {  // this warp's last read of S
+      tc_fence_before();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(s_empty);
+      released = true;
+    }
     uint32_t pk[16];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -229,6 +237,11 @@ __device__ __forceinline__ float half_row_p_tmem(uint32_t taddr, int cbase, int 
       for (int e = 0; e < 4; ++e) pk[4 * u + e] = pack_h2(p[2 * e], p[2 * e + 1]);
     }
     TMEM_ST16(p_taddr + (uint32_t)(c / 2), pk);
+  }
+  if (!released) {  // no key of this half is real: S was not read
+    tc_fence_before();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(s_empty);
   }
   return (s0 + s1) + (s2 + s3);
 }
@@ -423,13 +436,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       // P buffer free and O final for tile j-1 (the previous P V has completed)
       if (ok && j > 0) ok = mbar_wait(p_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc);
       ok = __all_sync(0xffffffffu, ok);
-      if (ok && rows_live) {
+      const bool p_pass = ok && rows_live;  // the TMEM P pass releases S itself
+      if (p_pass) {
         tc_fence_after();
         // p = 2^(s*sl2 - m_ref), row sum, f16 P into the swizzled A operand (half hsel of sP)
         if (TMEMP) {
           const uint32_t p_addr = tmem + lane_off + 192 + (uint32_t)(hsel * (kBK / 4));
-          l += full_tile ? half_row_p_tmem<false, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, p_addr)
-                         : half_row_p_tmem<true, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, p_addr);
+          l += full_tile ? half_row_p_tmem<false, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, p_addr, s_empty)
+                         : half_row_p_tmem<true, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, p_addr, s_empty);
         } else {
           uint8_t* prow = sP + hsel * (kBQ * 128) + row * 128;
           l += full_tile ? half_row_p<false, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row)
@@ -447,13 +461,13 @@ __global__ void __launch_bounds__(kThreads, 2)
           tc_wait_st();
         }
       }
-      // S read, P written, O rescaled: hand all three to the MMA warp
+      // S read (unless already released by the P pass), P written, O rescaled: hand them to the MMA warp
       if (TMEMP) tc_wait_st();
       tc_fence_before();
       if (!TMEMP) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(s_empty);
+        if (!(TMEMP && p_pass)) mbar_arrive(s_empty);
         mbar_arrive(p_full);
       }
     }
