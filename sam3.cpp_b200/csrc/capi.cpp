@@ -462,13 +462,23 @@ int s3b_op_gemm_rope(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, in
   if (rc) return rc;
   if (!A || !B || !out || !table || M <= 0 || N <= 0 || K <= 0 || rope_d <= 0 || (rope_d & 1) || rope_mod <= 0)
     return set_error(ctx, kErrArg, "bad gemm_rope arguments");
+  // the epilogue reads the table position-major: re-lay the caller's [positions][rope_d/2][2] table
+  // into a context buffer, one strided copy per frequency
+  const int half_d = rope_d / 2;
+  DevBuf* tb = ctx->buf("gemm_rope_table", (size_t)rope_mod * half_d * 8, &rc);
+  if (rc) return rc;
+  for (int i = 0; i < half_d; ++i) {
+    if (cudaMemcpy2DAsync(static_cast<char*>(tb->p) + (size_t)i * rope_mod * 8, 8, table + 2 * i, (size_t)half_d * 8, 8,
+                          (size_t)rope_mod, cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess)
+      return set_error(ctx, kErrCuda, "gemm_rope: table copy failed");
+  }
   EpiParams ep;
   ep.mode = EPI_STORE;
   ep.bias = bias;
   ep.out = out;
   ep.out_f32 = out_f32;
   ep.ldo = ldo;
-  ep.rope = table;
+  ep.rope = tb->as<float>();
   ep.rope_D = rope_d;
   ep.rope_cols = rope_cols;
   ep.rope_rows = M;

@@ -133,7 +133,7 @@ struct Vec {
 struct VitBlock {
   Vec n1w, n1b, n2w, n2b;
   Linear qkv, proj, fc1, fc2;
-  std::shared_ptr<DevBuf> rope;  // f32 [N][32][2]
+  std::shared_ptr<DevBuf> rope;  // f32 [32][N][2] (position-major)
   int rope_n = 0;
   bool global = false;
 };
@@ -248,6 +248,8 @@ int run_ln(s3b_ctx* ctx, const float* x, long long ldx, void* y, int y_f32, long
            const float* g, const float* b, float eps, const RowMap& map);
 void count_launch(s3b_ctx* ctx, int n = 1);
 EpiParams epi_store(const Linear& L, void* out, int out_f32, long long ldo, int act = ACT_NONE);
+// RoPE table [npos][half_d][2] (cos, sin) -> the position-major [half_d][npos][2] the GEMM epilogue reads
+void rope_position_major(const std::vector<float>& in, int npos, int half_d, std::vector<float>& out);
 
 // encoders
 int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);

@@ -115,27 +115,27 @@ __device__ __forceinline__ void epi_math16(const EpiParams& ep, int rope_pos, in
     for (int i = 0; i < 16; ++i) v[i] = fmaxf(v[i], 0.0f);
   }
   if (rope_pos >= 0 && gc < ep.rope_cols) {
-    const int half_d = ep.rope_D >> 1;
-    const float* tb = ep.rope + (size_t)rope_pos * half_d * 2;
+    // position-major table: the (cos, sin) pairs of one frequency for consecutive positions are
+    // adjacent, so the 32 rows (positions) of a warp read one contiguous 256-byte run per pair
+    const float2* tb = reinterpret_cast<const float2*>(ep.rope) + rope_pos;
+    const long long pstride = ep.rope_mod;
     const int d0 = gc % ep.rope_D;  // even: gc and rope_D are even
     if ((ep.rope_D & 15) == 0 && (ep.rope_cols & 15) == 0 && n_valid == 16) {
-      // the 16 columns lie inside one head: 8 consecutive (cos, sin) pairs
-      const float4* t4 = reinterpret_cast<const float4*>(tb + d0);
+      // the 16 columns lie inside one head: 8 consecutive frequencies
+      const float2* t2 = tb + (long long)(d0 >> 1) * pstride;
 #pragma unroll
-      for (int i = 0; i < 16; i += 4) {
-        const float4 cs = __ldg(t4 + (i >> 2));
-        const float a0 = v[i], b0 = v[i + 1], a1 = v[i + 2], b1 = v[i + 3];
-        v[i] = a0 * cs.x - b0 * cs.y;
-        v[i + 1] = a0 * cs.y + b0 * cs.x;
-        v[i + 2] = a1 * cs.z - b1 * cs.w;
-        v[i + 3] = a1 * cs.w + b1 * cs.z;
+      for (int i = 0; i < 16; i += 2) {
+        const float2 cs = __ldg(t2 + (long long)(i >> 1) * pstride);
+        const float a = v[i], b = v[i + 1];
+        v[i] = a * cs.x - b * cs.y;
+        v[i + 1] = a * cs.y + b * cs.x;
       }
     } else {
 #pragma unroll
       for (int i = 0; i < 16; i += 2) {
         if (i + 1 < n_valid && gc + i < ep.rope_cols) {
           const int d = (d0 + i) % ep.rope_D;
-          const float2 cs = __ldg(reinterpret_cast<const float2*>(tb + d));
+          const float2 cs = __ldg(tb + (long long)(d >> 1) * pstride);
           const float a = v[i], b = v[i + 1];
           v[i] = a * cs.x - b * cs.y;
           v[i + 1] = a * cs.y + b * cs.x;

@@ -58,7 +58,7 @@ struct EpiParams {
   int resid_up = 0;
   // EPI_STORE only: out = v * out_scale; RoPE on column pairs (2i, 2i+1) of
   // columns < rope_cols and GEMM rows < rope_rows: head dim rope_D, position
-  // (row % rope_mod), table [positions][rope_D/2][2] (cos, sin).
+  // (row % rope_mod), position-major table [rope_D/2][rope_mod][2] (cos, sin).
   float out_scale = 1.0f;
   const float* rope = nullptr;
   int rope_D = 0, rope_cols = 0;

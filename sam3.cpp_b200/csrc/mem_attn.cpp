@@ -51,8 +51,9 @@ static const float* rope_table(s3b_ctx* ctx, int feat, int D, int* rc) {
   const std::string key = "ma_rope_" + std::to_string(feat) + "_" + std::to_string(D);
   auto it = ctx->ws.find(key);
   if (it != ctx->ws.end() && it->second) return it->second->as<float>();
-  std::vector<float> t;
-  axial_cis(D, feat, feat, 10000.0f, 1.0f, t);
+  std::vector<float> t0, t;
+  axial_cis(D, feat, feat, 10000.0f, 1.0f, t0);
+  rope_position_major(t0, feat * feat, D / 2, t);
   DevBuf* b = ctx->buf(key, t.size() * 4, rc);
   if (*rc) return nullptr;
   if (cudaMemcpy(b->p, t.data(), t.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {

@@ -529,10 +529,12 @@ static int load_sam3(s3b_ctx* ctx, const Index& idx) {
     if ((rc = upload_linear(ctx, *f2w, f2b, B.fc2))) return rc;
     B.global = hp.is_global(i);
     if (const FileTensor* fc = idx.get(p + ".attn.freqs_cis")) {
-      std::vector<float> f;
+      std::vector<float> f, fp;
       tensor_to_f32(*fc, f);
       B.rope_n = (int)fc->ne[2];
-      B.rope = upload_bytes(ctx, f.data(), f.size() * 4, &rc);
+      if (f.size() % ((size_t)B.rope_n * 2)) return set_error(ctx, kErrFormat, "%s: bad freqs_cis shape", p.c_str());
+      rope_position_major(f, B.rope_n, (int)(f.size() / ((size_t)B.rope_n * 2)), fp);
+      B.rope = upload_bytes(ctx, fp.data(), fp.size() * 4, &rc);
     }
   }
   if (idx.get("neck.trk.0.conv_1x1.weight")) {

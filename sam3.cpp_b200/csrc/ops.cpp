@@ -13,6 +13,15 @@ cudaEvent_t s3b_ctx::next_event() {
 
 namespace s3b {
 
+void rope_position_major(const std::vector<float>& in, int npos, int half_d, std::vector<float>& out) {
+  out.resize((size_t)npos * half_d * 2);
+  for (int p = 0; p < npos; ++p)
+    for (int i = 0; i < half_d; ++i) {
+      out[((size_t)i * npos + p) * 2] = in[((size_t)p * half_d + i) * 2];
+      out[((size_t)i * npos + p) * 2 + 1] = in[((size_t)p * half_d + i) * 2 + 1];
+    }
+}
+
 void count_launch(s3b_ctx* ctx, int n) { ctx->n_launches += n; }
 
 EpiParams epi_store(const Linear& L, void* out, int out_f32, long long ldo, int act) {
