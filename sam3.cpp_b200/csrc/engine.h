@@ -139,8 +139,10 @@ struct VitBlock {
 };
 
 struct NeckScale {
-  Linear dc1, dc2, c1, c3;  // deconv1/2 as [4*Cout][Cin], conv1x1 [Cout][Cin], conv3x3 [Cout][9*Cin]
-  bool has_dc1 = false, has_dc2 = false;
+  // dc1: first deconvolution of scale 0 as [4*Cout][Cin]; dcf: the last deconvolution of scales 0 / 1
+  // with the following 1x1 conv folded in, [4*D][Cin]; c1: 1x1 conv of scales 2 / 3 [D][Cin];
+  // c3: 3x3 conv [D][9*D]
+  Linear dc1, dcf, c1, c3;
 };
 
 struct HieraBlock {

@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <fstream>
+#include <thread>
 
 #include "engine.h"
 
@@ -298,15 +299,56 @@ int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Lin
 }
 
 // ConvTranspose2d k=2 s=2, ggml [2, 2, Cout, Cin] -> B[(ky*2+kx)*Cout + co][ci].
-static int upload_deconv(s3b_ctx* ctx, const FileTensor& t, const FileTensor& bias, Linear& L) {
+// ConvTranspose2d 2x2 stride 2, ggml [2, 2, Cout, Cin] -> rows [(ky*2 + kx)*Cout + co][ci].
+static void deconv_rows(const FileTensor& t, std::vector<float>& r) {
   const int Cout = (int)t.ne[2], Cin = (int)t.ne[3];
-  std::vector<float> w, r((size_t)4 * Cout * Cin);
+  std::vector<float> w;
+  r.assign((size_t)4 * Cout * Cin, 0.f);
   tensor_to_f32(t, w);
   for (int ci = 0; ci < Cin; ++ci)
     for (int co = 0; co < Cout; ++co)
       for (int ky = 0; ky < 2; ++ky)
         for (int kx = 0; kx < 2; ++kx)
           r[(size_t)((ky * 2 + kx) * Cout + co) * Cin + ci] = w[(size_t)kx + 2 * (ky + 2 * (co + (size_t)Cout * ci))];
+}
+
+// A 1x1 conv (c [Co][Cd], bias bc) applied to the output of a 2x2 deconvolution (rows d [4*Cd][Cin],
+// bias bd) is one deconvolution: rows f[p*Co + o] = sum_c c[o][c] d[p*Cd + c], bias
+// bf[o] = bc[o] + sum_c c[o][c] bd[c] (the deconvolution bias is the same at every kernel position).
+// Computed in f32 on the host threads at load.
+static void fold_1x1_into_deconv(const std::vector<float>& d, const std::vector<float>& bd, int Cd, int Cin,
+                                 const std::vector<float>& c, const std::vector<float>& bc, int Co,
+                                 std::vector<float>& f, std::vector<float>& bf) {
+  f.assign((size_t)4 * Co * Cin, 0.f);
+  bf.assign(Co, 0.f);
+  for (int o = 0; o < Co; ++o) {
+    double acc = bc[o];
+    for (int k = 0; k < Cd; ++k) acc += (double)c[(size_t)o * Cd + k] * bd[k];
+    bf[o] = (float)acc;
+  }
+  const int n_rows = 4 * Co;
+  unsigned nt = std::thread::hardware_concurrency();
+  nt = std::max(1u, std::min(nt, 32u));
+  std::vector<std::thread> th;
+  for (unsigned t = 0; t < nt; ++t)
+    th.emplace_back([&, t]() {
+      for (int row = (int)t; row < n_rows; row += (int)nt) {
+        const int p = row / Co, o = row % Co;
+        float* out = f.data() + (size_t)row * Cin;
+        for (int k = 0; k < Cd; ++k) {
+          const float s = c[(size_t)o * Cd + k];
+          const float* in = d.data() + (size_t)(p * Cd + k) * Cin;
+          for (int i = 0; i < Cin; ++i) out[i] += s * in[i];
+        }
+      }
+    });
+  for (auto& x : th) x.join();
+}
+
+static int upload_deconv(s3b_ctx* ctx, const FileTensor& t, const FileTensor& bias, Linear& L) {
+  const int Cout = (int)t.ne[2], Cin = (int)t.ne[3];
+  std::vector<float> r;
+  deconv_rows(t, r);
   int rc = upload_b_operand(ctx, r, 4 * Cout, Cin, 8, L);
   if (rc) return rc;
   std::vector<float> b;
@@ -316,10 +358,11 @@ static int upload_deconv(s3b_ctx* ctx, const FileTensor& t, const FileTensor& bi
   return rc;
 }
 
-// Conv2d kxk, ggml [k, k, Cin, Cout] -> B[co][(ky*k + kx)*Cin + ci] (channel-last im2col order).
-static int upload_conv_cl(s3b_ctx* ctx, const FileTensor& t, const FileTensor& bias, Linear& L) {
+// Conv2d kxk, ggml [k, k, Cin, Cout] -> rows [co][(ky*k + kx)*Cin + ci] (channel-last im2col order).
+static void conv_rows(const FileTensor& t, std::vector<float>& r) {
   const int k = (int)t.ne[0], Cin = (int)t.ne[2], Cout = (int)t.ne[3];
-  std::vector<float> w, r((size_t)Cout * k * k * Cin);
+  std::vector<float> w;
+  r.assign((size_t)Cout * k * k * Cin, 0.f);
   tensor_to_f32(t, w);
   for (int co = 0; co < Cout; ++co)
     for (int ci = 0; ci < Cin; ++ci)
@@ -327,6 +370,12 @@ static int upload_conv_cl(s3b_ctx* ctx, const FileTensor& t, const FileTensor& b
         for (int kx = 0; kx < k; ++kx)
           r[(size_t)co * k * k * Cin + (size_t)(ky * k + kx) * Cin + ci] =
               w[(size_t)kx + k * (ky + (size_t)k * (ci + (size_t)Cin * co))];
+}
+
+static int upload_conv_cl(s3b_ctx* ctx, const FileTensor& t, const FileTensor& bias, Linear& L) {
+  const int k = (int)t.ne[0], Cin = (int)t.ne[2], Cout = (int)t.ne[3];
+  std::vector<float> r;
+  conv_rows(t, r);
   int rc = upload_b_operand(ctx, r, Cout, k * k * Cin, 8, L);
   if (rc) return rc;
   std::vector<float> b;
@@ -351,30 +400,51 @@ struct Index {
   const FileTensor* var = idx.get(name);                                                  \
   if (!var) return set_error(ctx, kErrFormat, "missing tensor '%s'", std::string(name).c_str());
 
+// The last deconvolution of scales 0 and 1 is followed by the 1x1 conv with nothing in between, so
+// the two are uploaded as one deconvolution (fold_1x1_into_deconv); scales 2 and 3 keep the 1x1 conv.
 static int load_neck(s3b_ctx* ctx, const Index& idx, const std::string& pfx, NeckScale* sc) {
   int rc;
+  auto fold = [&](const FileTensor& dw, const FileTensor& db, const std::string& conv, Linear& L) -> int {
+    NEED(cw, conv + ".conv_1x1.weight");
+    NEED(cb, conv + ".conv_1x1.bias");
+    const int Cd = (int)dw.ne[2], Cin = (int)dw.ne[3], Co = (int)cw->ne[3];
+    if ((int)cw->ne[2] != Cd || cw->ne[0] != 1 || cw->ne[1] != 1)
+      return set_error(ctx, kErrFormat, "%s: 1x1 conv does not follow the deconvolution", conv.c_str());
+    std::vector<float> d, bd, c, bc, f, bf;
+    deconv_rows(dw, d);
+    tensor_to_f32(db, bd);
+    conv_rows(*cw, c);
+    tensor_to_f32(*cb, bc);
+    if ((int)bd.size() != Cd || (int)bc.size() != Co) return set_error(ctx, kErrFormat, "%s: bias size", conv.c_str());
+    fold_1x1_into_deconv(d, bd, Cd, Cin, c, bc, Co, f, bf);
+    int r = upload_b_operand(ctx, f, 4 * Co, Cin, 8, L);
+    if (r) return r;
+    L.b = upload_bytes(ctx, bf.data(), bf.size() * 4, &r);
+    L.file_dtype = dw.dtype;
+    return r;
+  };
   {
     NEED(w0, pfx + "0.dconv_2x2_0.weight");
     NEED(b0, pfx + "0.dconv_2x2_0.bias");
     NEED(w1, pfx + "0.dconv_2x2_1.weight");
     NEED(b1, pfx + "0.dconv_2x2_1.bias");
     if ((rc = upload_deconv(ctx, *w0, *b0, sc[0].dc1))) return rc;
-    if ((rc = upload_deconv(ctx, *w1, *b1, sc[0].dc2))) return rc;
-    sc[0].has_dc1 = sc[0].has_dc2 = true;
+    if ((rc = fold(*w1, *b1, pfx + "0", sc[0].dcf))) return rc;
   }
   {
     NEED(w, pfx + "1.dconv_2x2.weight");
     NEED(b, pfx + "1.dconv_2x2.bias");
-    if ((rc = upload_deconv(ctx, *w, *b, sc[1].dc1))) return rc;
-    sc[1].has_dc1 = true;
+    if ((rc = fold(*w, *b, pfx + "1", sc[1].dcf))) return rc;
   }
   for (int s = 0; s < 4; ++s) {
     const std::string p = pfx + std::to_string(s);
-    NEED(w1, p + ".conv_1x1.weight");
-    NEED(b1, p + ".conv_1x1.bias");
     NEED(w3, p + ".conv_3x3.weight");
     NEED(b3, p + ".conv_3x3.bias");
-    if ((rc = upload_conv_cl(ctx, *w1, *b1, sc[s].c1))) return rc;
+    if (s >= 2) {
+      NEED(w1, p + ".conv_1x1.weight");
+      NEED(b1, p + ".conv_1x1.bias");
+      if ((rc = upload_conv_cl(ctx, *w1, *b1, sc[s].c1))) return rc;
+    }
     if ((rc = upload_conv_cl(ctx, *w3, *b3, sc[s].c3))) return rc;
   }
   return kOk;

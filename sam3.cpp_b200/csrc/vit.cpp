@@ -116,36 +116,33 @@ static int vit_neck(s3b_ctx* ctx, const NeckScale* sc, const __half* xh, int F, 
   int rc = 0;
   const long long T = (long long)F * G * G;
   const int c_mid = sc[0].dc1.N / 4;  // 512
-  const int D = sc[0].c1.N;           // 256
+  const int D = sc[0].c3.N;           // 256
   DevBuf* d1 = ctx->buf("neck_d1", (size_t)T * 4 * c_mid * 2, &rc);
-  DevBuf* d2 = ctx->buf("neck_d2", (size_t)T * 16 * D * 2, &rc);
   DevBuf* c1 = ctx->buf("neck_c1", (size_t)T * 16 * D * 2, &rc);
   DevBuf* col = ctx->buf("neck_col", (size_t)T * 16 * 9 * D * 2, &rc);
   DevBuf* mp = ctx->buf("neck_mp", (size_t)T / 4 * hp.vit_embed_dim * 2, &rc);
   if (rc) return rc;
-  // scale 0: deconv(E->512) + GELU(erf) -> deconv(512->D) -> 1x1 -> 3x3  (4x)
+  // scale 0: deconv(E->512) + GELU(erf) -> [deconv(512->D) -> 1x1, folded into one deconv] -> 3x3  (4x)
   {
     EpiParams e1 = epi_store(sc[0].dc1, d1->p, 0, c_mid, ACT_GELU_ERF);
     e1.mode = EPI_DECONV2;
     e1.cout = c_mid;
     e1.map.W = e1.map.H = G;
     CKG(gemm(ctx, xh, hp.vit_embed_dim, sc[0].dc1, T, e1));
-    EpiParams e2 = epi_store(sc[0].dc2, d2->p, 0, D);
+    EpiParams e2 = epi_store(sc[0].dcf, c1->p, 0, D);
     e2.mode = EPI_DECONV2;
     e2.cout = D;
     e2.map.W = e2.map.H = 2 * G;
-    CKG(gemm(ctx, d1->as<__half>(), c_mid, sc[0].dc2, T * 4, e2));
-    CKG(gemm(ctx, d2->as<__half>(), D, sc[0].c1, T * 16, epi_store(sc[0].c1, c1->p, 0, D)));
+    CKG(gemm(ctx, d1->as<__half>(), c_mid, sc[0].dcf, T * 4, e2));
     if ((rc = conv3x3(ctx, sc[0].c3, c1->as<__half>(), F, 4 * G, outs[0], col->as<__half>()))) return rc;
   }
-  // scale 1: deconv(E->512) -> 1x1 (512->D) -> 3x3  (2x)
+  // scale 1: [deconv(E->512) -> 1x1 (512->D), folded into one deconv] -> 3x3  (2x)
   {
-    EpiParams e1 = epi_store(sc[1].dc1, d1->p, 0, c_mid);
+    EpiParams e1 = epi_store(sc[1].dcf, c1->p, 0, D);
     e1.mode = EPI_DECONV2;
-    e1.cout = c_mid;
+    e1.cout = D;
     e1.map.W = e1.map.H = G;
-    CKG(gemm(ctx, xh, hp.vit_embed_dim, sc[1].dc1, T, e1));
-    CKG(gemm(ctx, d1->as<__half>(), c_mid, sc[1].c1, T * 4, epi_store(sc[1].c1, c1->p, 0, D)));
+    CKG(gemm(ctx, xh, hp.vit_embed_dim, sc[1].dcf, T, e1));
     if ((rc = conv3x3(ctx, sc[1].c3, c1->as<__half>(), F, 2 * G, outs[1], col->as<__half>()))) return rc;
   }
   // scale 2: 1x1 (E->D) -> 3x3  (1x)
