@@ -72,6 +72,9 @@ int s3b_sync(s3b_ctx* ctx);
  * applies to every context of the process);
  * "gemm_wide_epilogue" (1, default: GEMMs with K < 2048 run 16 epilogue
  * warps instead of 8; 0: all run 8; process-wide);
+ * "conv_implicit" (1, default: 3x3 convolutions with C a multiple of 64 run
+ * as implicit GEMMs whose TMA loads fetch the shifted pixel blocks, no
+ * column matrix; 0: im2col + GEMM);
  * "attention_exp_poly" (0-4: of every 8 softmax exponentials in the tcgen05
  * kernel, how many are evaluated by a polynomial on the FMA pipe instead of
  * the MUFU unit; a tuning knob, results agree to f16 rounding);
@@ -195,7 +198,8 @@ int s3b_op_layernorm(s3b_ctx* ctx, const float* x, void* out, int out_f32, int64
 /* 3x3 / stride 1 / pad 1 convolution on channel-last f16 maps x [B][H][W][C]
  * with weights w f16 [Cout][3][3][C] (ky, kx, ci order, i.e. the ggml kernel
  * [3, 3, C, Cout] repacked channel-last), bias f32 [Cout] or NULL, out f32
- * [B][H][W][Cout]. Lowered to im2col (context workspace) + tensor-core GEMM.
+ * [B][H][W][Cout]. An implicit tensor-core GEMM (C a multiple of 64), else
+ * im2col (context workspace) + GEMM.
  * Replaces ggml_conv_2d_s1_ph + bias add (sam3.cpp:3887-3918). C and Cout
  * multiples of 8. */
 int s3b_op_conv3x3(s3b_ctx* ctx, const void* x, int B, int H, int W, int C, const void* w, const float* bias,

@@ -254,6 +254,11 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     set_gemm_wide_epilogue((int)value);
     return kOk;
   }
+  if (k == "conv_implicit") {
+    if (value < 0 || value > 1) return set_error(ctx, kErrArg, "conv_implicit must be 0 or 1");
+    ctx->conv_implicit = (int)value;
+    return kOk;
+  }
   if (k == "attention_exp_poly") {
     if (value < 0 || value > 4) return set_error(ctx, kErrArg, "attention_exp_poly must be in [0, 4]");
     ctx->attention_exp_poly = (int)value;
@@ -553,16 +558,25 @@ int s3b_op_conv3x3(s3b_ctx* ctx, const void* x, int B, int H, int W, int C, cons
   if (!x || !w || !out || B <= 0 || H <= 0 || W <= 0 || C <= 0 || Cout <= 0 || C % 8 || Cout % 8)
     return set_error(ctx, kErrArg, "bad conv3x3 arguments");
   const long long M = (long long)B * H * W;
-  DevBuf* col = ctx->buf("op_conv_col", (size_t)M * 9 * C * 2, &rc);
-  if (rc) return rc;
-  rc = im2col_3x3_cl(reinterpret_cast<const __half*>(x), B, H, W, C, col->as<__half>(), ctx->stream);
-  if (rc) return set_error(ctx, kErrCuda, "im2col launch failed (%d)", rc);
   EpiParams ep;
   ep.mode = EPI_STORE;
   ep.bias = bias;
   ep.out = out;
   ep.out_f32 = 1;
   ep.ldo = Cout;
+  if (ctx->conv_implicit && C % 64 == 0) {
+    // implicit GEMM: no column matrix
+    rc = gemm_conv3x3(reinterpret_cast<const __half*>(x), B, H, W, C, reinterpret_cast<const __half*>(w), 9LL * C,
+                      Cout, ep, ctx->d_err, ctx->stream);
+    if (rc != -2) {
+      if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "implicit conv3x3 launch failed (%d)", rc);
+      return kOk;
+    }
+  }
+  DevBuf* col = ctx->buf("op_conv_col", (size_t)M * 9 * C * 2, &rc);
+  if (rc) return rc;
+  rc = im2col_3x3_cl(reinterpret_cast<const __half*>(x), B, H, W, C, col->as<__half>(), ctx->stream);
+  if (rc) return set_error(ctx, kErrCuda, "im2col launch failed (%d)", rc);
   rc = gemm_f16(col->as<__half>(), 9LL * C, reinterpret_cast<const __half*>(w), 9LL * C, (int)M, Cout, 9 * C, ep,
                 ctx->d_err, ctx->stream);
   if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "conv gemm launch failed (%d)", rc);

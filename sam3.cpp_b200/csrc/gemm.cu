@@ -230,6 +230,11 @@ __device__ __forceinline__ void tma_store_2d(const void* map, const void* src, i
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+__device__ __forceinline__ void tma_store_4d(const void* map, const void* src, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -245,7 +250,25 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // `tempty`.
 // EW: epilogue warps, 8 (2 column groups) or 16 (4 column groups, for epilogues
 // that would otherwise outlast the main loop).
-template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW>
+// CONV: implicit 3x3 / pad 1 convolution over the channel-last f16 map
+// [conv_F][conv_H][conv_W][conv_C] (A never materialised): a tile's 128 rows are an
+// 8 x 16 pixel block (the pair's two CTAs take vertically adjacent blocks), and
+// k-block kb = (tap, 64-channel block) is one 4-D TMA load of the block shifted by
+// the tap; TMA zero-fills the taps outside the map, which is the padding. The
+// output tile goes out through a 4-D TMA store that clips at the map's edges.
+template <int CONV_TY_BLOCKS>
+__device__ __forceinline__ void conv_tile_origin(int mt, const EpiParams& ep, uint32_t rank, int* x0, int* y0,
+                                                 int* f) {
+  const int txn = (ep.conv_W + 15) / 16;
+  const int tyn = (ep.conv_H + 8 * CONV_TY_BLOCKS - 1) / (8 * CONV_TY_BLOCKS);
+  const int tx = mt % txn, r = mt / txn;
+  const int ty = r % tyn;
+  *f = r / tyn;
+  *x0 = tx * 16;
+  *y0 = ty * 8 * CONV_TY_BLOCKS + (int)rank * 8;
+}
+
+template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW, bool CONV = false>
 __global__ void __launch_bounds__(gemm_threads(EW), 1)
     gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M,
@@ -258,6 +281,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
   constexpr uint32_t TMEM_COLS = 2 * BN;
   constexpr uint32_t STAGING = TMA_EPI ? 4 * kStageBufBytes : 0;
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
+  static_assert(!CONV || TMA_EPI, "the implicit convolution stores through TMA");
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512 || TMEM_COLS == 128, "TMEM columns must be a power of 2");
 
   extern __shared__ uint8_t smem_raw[];
@@ -325,20 +349,33 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       uint32_t armed = 0;        // bit s: stage s has been armed at least once
       uint32_t armed_phase = 0;  // bit s: parity of the last arming of stage s
       bool ok = true;
+      const int cbn = CONV ? ep.conv_C / kBK : 1;  // 64-channel blocks per tap
       for (int t = unit; t < n_tiles && ok; t += n_units) {
         const int m0 = (t / tiles_n) * TM + (int)rank * kBM;
         const int n0 = (t % tiles_n) * BN + (int)rank * BN_CTA;
+        int cx = 0, cy = 0, cf = 0;
+        if (CONV) conv_tile_origin<PAIR ? 2 : 1>(t / tiles_n, ep, rank, &cx, &cy, &cf);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
+          // CONV: k-block kb = tap (ky, kx) x channel block cb; the block shifted by (kx - 1, ky - 1)
+          const int tap = CONV ? kb / cbn : 0;
+          const int cb = CONV ? kb - tap * cbn : 0;
+          const int ky = tap / 3, kx = tap - 3 * (tap / 3);
           if (PAIR) {
             // both CTAs' bytes complete the leader's barrier; only the leader arms it
             const uint32_t fb = cluster_addr(smem_u32(&full[stage]), 0);
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
-            tma_load_2d_pair(&tmA, fb, sA + stage * A_BYTES, kb * kBK, m0);
+            if (CONV)
+              tma_load_4d_pair(&tmA, fb, sA + stage * A_BYTES, cb * kBK, cx + kx - 1, cy + ky - 1, cf);
+            else
+              tma_load_2d_pair(&tmA, fb, sA + stage * A_BYTES, kb * kBK, m0);
             tma_load_2d_pair(&tmB, fb, sB + stage * B_BYTES, kb * kBK, n0);
           } else {
             mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-            tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, m0);
+            if (CONV)
+              tma_load_4d(&tmA, &full[stage], sA + stage * A_BYTES, cb * kBK, cx + kx - 1, cy + ky - 1, cf);
+            else
+              tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, m0);
             tma_load_2d(&tmB, &full[stage], sB + stage * B_BYTES, kb * kBK, n0);
           }
           armed |= 1u << stage;
@@ -445,6 +482,8 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
     for (int t = unit; t < n_tiles; t += n_units) {
       const int m0 = (t / tiles_n) * TM + (int)rank * kBM;
       const int n0 = (t % tiles_n) * BN;
+      int cx = 0, cy = 0, cf = 0;
+      if (CONV) conv_tile_origin<PAIR ? 2 : 1>(t / tiles_n, ep, rank, &cx, &cy, &cf);
       // the first residual chunk does not depend on the accumulator: fetch it during the main loop
       if (TMA_EPI && rip && leader) issue_resid(chunk_ctr, n0 + grp * CG, m0);
       if (!mbar_wait(&tfull[acc], aphase, s_abort, err, kErrWaitTmemFull)) break;
@@ -523,7 +562,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
           fence_proxy_async_smem();
           named_bar(1 + grp, 128);
           if (leader && gcb < N) {
-            tma_store_2d(&tmC, buf, gcb, m0);
+            if (CONV) tma_store_4d(&tmC, buf, gcb, cx, cy, cf); else tma_store_2d(&tmC, buf, gcb, m0);
             bulk_commit();
           }
           if (rip && leader && c0 + cw < CG) issue_resid(chunk_ctr + 1, gcb + cw, m0);
@@ -609,17 +648,39 @@ int make_map_2d(CUtensorMap* map, const void* base, long long rows, long long co
   return r == CUDA_SUCCESS ? 0 : -12;
 }
 
-template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW = 8>
+// 4-D tensor map over a channel-last [F][H][W][C] map, box = (128 B of channels) x 16 x 8 x 1
+// (an 8 x 16 pixel block, 128 rows of 128 B in the SW128 layout of a 2-D tile), SW128;
+// coordinates outside the map read as zero (loads) or are not written (stores).
+int make_map_conv(CUtensorMap* map, const void* base, int F, int H, int W, int C, int elem_bytes) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return -10;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || ((long long)C * elem_bytes) % 16 != 0) return -11;
+  cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)F};
+  cuuint64_t strides[3] = {(cuuint64_t)C * elem_bytes, (cuuint64_t)W * C * elem_bytes,
+                           (cuuint64_t)H * W * C * elem_bytes};
+  cuuint32_t box[4] = {(cuuint32_t)(128 / elem_bytes), 16, 8, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -12;
+}
+
+// CONV: A is the channel-last input map of gemm_conv3x3 (geometry in ep.conv_*) and M the number of
+// pixel-block tiles x the tile rows.
+template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW = 8, bool CONV = false>
 int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
                 const EpiParams& ep, int resid_in_place, int* err, cudaStream_t st) {
   constexpr int BN_CTA = PAIR ? BN / 2 : BN;
   CUtensorMap ma, mb, mc, mr;
-  int rc = make_map_2d(&ma, A, M, K, lda, kBM, 2);
+  int rc = CONV ? make_map_conv(&ma, A, ep.conv_F, ep.conv_H, ep.conv_W, ep.conv_C, 2)
+                : make_map_2d(&ma, A, M, K, lda, kBM, 2);
   if (rc) return rc;
   rc = make_map_2d(&mb, B, N, K, ldb, BN_CTA, 2);
   if (rc) return rc;
   if (TMA_EPI) {
-    rc = make_map_2d(&mc, ep.out, M, N, ep.ldo, kBM, ep.out_f32 ? 4 : 2);
+    rc = CONV ? make_map_conv(&mc, ep.out, ep.conv_F, ep.conv_H, ep.conv_W, N, ep.out_f32 ? 4 : 2)
+              : make_map_2d(&mc, ep.out, M, N, ep.ldo, kBM, ep.out_f32 ? 4 : 2);
     if (rc) return rc;
   } else {
     mc = ma;  // unused
@@ -634,7 +695,7 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
   constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN_CTA) * kBK * 2 + (TMA_EPI ? 4 * kStageBufBytes : 0) +
                           (2 * STAGES + 9) * 8 + 16;
   static_assert(smem <= 232448, "shared memory per CTA");
-  auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR, EW>;
+  auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR, EW, CONV>;
   constexpr int kThreads = gemm_threads(EW);
   static bool attr_set = false;
   static int max_units = 0;  // co-resident CTAs (or pairs)
@@ -751,6 +812,26 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
   }
   if (N <= 128) return launch_gemm<128, 6, false, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
   return launch_gemm<256, 4, false, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
+}
+
+int gemm_conv3x3(const __half* x, int F, int H, int W, int C, const __half* Bw, long long ldb, int N,
+                 const EpiParams& ep_in, int* err, cudaStream_t st) {
+  if (F <= 0 || H <= 0 || W <= 0 || C <= 0 || N <= 0 || C % kBK) return -2;
+  // plain stores of the whole [F][H][W][N] output: no residual, RoPE, row map or strided rows
+  if (ep_in.mode != EPI_STORE || ep_in.map.kind != 0 || ep_in.resid || ep_in.rope || ep_in.ldo != N) return -2;
+  if ((reinterpret_cast<uintptr_t>(ep_in.out) & 15) || ((long long)N * (ep_in.out_f32 ? 4 : 2)) % 16) return -2;
+  EpiParams ep = ep_in;
+  ep.conv_F = F;
+  ep.conv_H = H;
+  ep.conv_W = W;
+  ep.conv_C = C;
+  const int K = 9 * C;
+  const bool pair = g_gemm_pairs != 0;
+  const long long tiles = (long long)F * ((W + 15) / 16) * ((H + (pair ? 15 : 7)) / (pair ? 16 : 8));
+  const long long m_virtual = tiles * (pair ? 2 * kBM : kBM);
+  if (m_virtual > 0x7fffffffLL) return -2;
+  if (pair) return launch_gemm<256, 5, true, true, 8, true>(x, C, Bw, ldb, (int)m_virtual, N, K, ep, 0, err, st);
+  return launch_gemm<256, 3, true, false, 8, true>(x, C, Bw, ldb, (int)m_virtual, N, K, ep, 0, err, st);
 }
 
 void set_gemm_pairs(int mode) { g_gemm_pairs = mode; }

@@ -66,12 +66,20 @@ struct EpiParams {
   // EPI_DECONV2: row = input pixel (f, y, x) of a (map.W x map.H) grid,
   // column = (ky*2 + kx)*cout + co, stored at pixel (2y+ky, 2x+kx).
   int cout = 0;
+  // implicit 3x3 convolution (gemm_conv3x3 sets these): channel-last f16 input [F][H][W][C]
+  int conv_F = 0, conv_H = 0, conv_W = 0, conv_C = 0;
 };
 
 // Tensor-core GEMM (tcgen05 + TMA): A f16 [M][lda] K-major, B f16 [N][ldb]
 // K-major. lda, ldb multiples of 8; pointers 16-byte aligned.
 int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
              const EpiParams& ep, int* err, cudaStream_t st);
+// 3x3 / stride 1 / pad 1 convolution as an implicit GEMM (no column matrix): x channel-last f16
+// [F][H][W][C] (C a multiple of 64), weights Bw [N][9*C] in (ky, kx, c) order, output
+// [F][H][W][N] through ep (EPI_STORE with ldo == N, bias / activation / f16 or f32; no residual,
+// RoPE or row map). Returns -2 when those conditions do not hold (callers fall back to im2col).
+int gemm_conv3x3(const __half* x, int F, int H, int W, int C, const __half* Bw, long long ldb, int N,
+                 const EpiParams& ep, int* err, cudaStream_t st);
 // Process-wide: which wide TMA-epilogue GEMMs use 256-row tiles on SM pairs:
 // 0 none, 1 (default) those with K >= 2048 or f16 outputs on 16 epilogue warps, 2 all.
 void set_gemm_pairs(int mode);

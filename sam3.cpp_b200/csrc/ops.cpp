@@ -54,6 +54,38 @@ int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long
   return kOk;
 }
 
+// 3x3 / pad 1 conv of a channel-last f16 map as an implicit GEMM when the option and the shapes allow,
+// else im2col into `col` + GEMM. Counted and timed as a GEMM (algorithmic flops 2*pixels*N*9C).
+int run_conv3x3(s3b_ctx* ctx, const Linear& L, const __half* x, int F, int H, int W, const EpiParams& ep,
+                __half* col) {
+  const int C = L.K / 9;
+  const long long M = (long long)F * H * W;
+  if (ctx->conv_implicit && L.Kpad == L.K && C % 64 == 0) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (ctx->prof) {
+      a = ctx->next_event();
+      b = ctx->next_event();
+      cudaEventRecord(a, ctx->stream);
+    }
+    const int rc = gemm_conv3x3(x, F, H, W, C, L.w->as<__half>(), L.Kpad, L.N, ep, ctx->d_err, ctx->stream);
+    if (rc != -2) {
+      count_launch(ctx);
+      if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "implicit conv3x3 failed (%d)", rc);
+      if (ctx->prof) {
+        cudaEventRecord(b, ctx->stream);
+        const double bytes = 2.0 * M * C + 2.0 * L.N * L.K + (ep.out_f32 ? 4.0 : 2.0) * M * L.N;
+        ctx->prof_entries.push_back({0, 2.0 * M * L.N * L.K, bytes, a, b});
+      }
+      return kOk;
+    }
+  }
+  if (!col) return set_error(ctx, kErrArg, "conv3x3: no column workspace for the im2col path");
+  int rc = im2col_3x3_cl(x, F, H, W, C, col, ctx->stream);
+  count_launch(ctx);
+  if (rc) return set_error(ctx, kErrCuda, "im2col_3x3 failed (%d)", rc);
+  return run_gemm(ctx, col, L.Kpad, L, M, ep);
+}
+
 // LayerNorm (HBM-bound): algorithmic bytes = f32 rows in + rows out (f16 / f32) + gamma, beta.
 int run_ln(s3b_ctx* ctx, const float* x, long long ldx, void* y, int y_f32, long long ldy, long long rows, int C,
            const float* g, const float* b, float eps, const RowMap& map) {

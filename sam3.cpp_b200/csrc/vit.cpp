@@ -102,11 +102,9 @@ static int vit_block(s3b_ctx* ctx, const VitBlock& B, int F, float* x, __half* x
   return kOk;
 }
 
-// conv 3x3 (pad 1) as im2col + GEMM, channel-last f16 in -> f32 out.
+// conv 3x3 (pad 1), channel-last f16 in -> f32 out: implicit GEMM (im2col + GEMM when disabled).
 static int conv3x3(s3b_ctx* ctx, const Linear& L, const __half* in, int F, int S, float* out, __half* col) {
-  CK(im2col_3x3_cl(in, F, S, S, L.K / 9, col, ctx->stream));
-  CKG(gemm(ctx, col, L.Kpad, L, (long long)F * S * S, epi_store(L, out, 1, L.N)));
-  return kOk;
+  return run_conv3x3(ctx, L, in, F, S, S, epi_store(L, out, 1, L.N), col);
 }
 
 // One SimpleFPN path (sam3_build_neck_graph, sam3.cpp:3863-3921) for F frames.
@@ -119,7 +117,9 @@ static int vit_neck(s3b_ctx* ctx, const NeckScale* sc, const __half* xh, int F, 
   const int D = sc[0].c3.N;           // 256
   DevBuf* d1 = ctx->buf("neck_d1", (size_t)T * 4 * c_mid * 2, &rc);
   DevBuf* c1 = ctx->buf("neck_c1", (size_t)T * 16 * D * 2, &rc);
-  DevBuf* col = ctx->buf("neck_col", (size_t)T * 16 * 9 * D * 2, &rc);
+  // im2col workspace only when the implicit convolution is switched off
+  DevBuf* col = ctx->conv_implicit ? nullptr : ctx->buf("neck_col", (size_t)T * 16 * 9 * D * 2, &rc);
+  __half* colp = col ? col->as<__half>() : nullptr;
   DevBuf* mp = ctx->buf("neck_mp", (size_t)T / 4 * hp.vit_embed_dim * 2, &rc);
   if (rc) return rc;
   // scale 0: deconv(E->512) + GELU(erf) -> [deconv(512->D) -> 1x1, folded into one deconv] -> 3x3  (4x)
@@ -134,7 +134,7 @@ static int vit_neck(s3b_ctx* ctx, const NeckScale* sc, const __half* xh, int F, 
     e2.cout = D;
     e2.map.W = e2.map.H = 2 * G;
     CKG(gemm(ctx, d1->as<__half>(), c_mid, sc[0].dcf, T * 4, e2));
-    if ((rc = conv3x3(ctx, sc[0].c3, c1->as<__half>(), F, 4 * G, outs[0], col->as<__half>()))) return rc;
+    if ((rc = conv3x3(ctx, sc[0].c3, c1->as<__half>(), F, 4 * G, outs[0], colp))) return rc;
   }
   // scale 1: [deconv(E->512) -> 1x1 (512->D), folded into one deconv] -> 3x3  (2x)
   {
@@ -143,18 +143,18 @@ static int vit_neck(s3b_ctx* ctx, const NeckScale* sc, const __half* xh, int F, 
     e1.cout = D;
     e1.map.W = e1.map.H = G;
     CKG(gemm(ctx, xh, hp.vit_embed_dim, sc[1].dcf, T, e1));
-    if ((rc = conv3x3(ctx, sc[1].c3, c1->as<__half>(), F, 2 * G, outs[1], col->as<__half>()))) return rc;
+    if ((rc = conv3x3(ctx, sc[1].c3, c1->as<__half>(), F, 2 * G, outs[1], colp))) return rc;
   }
   // scale 2: 1x1 (E->D) -> 3x3  (1x)
   {
     CKG(gemm(ctx, xh, hp.vit_embed_dim, sc[2].c1, T, epi_store(sc[2].c1, c1->p, 0, D)));
-    if ((rc = conv3x3(ctx, sc[2].c3, c1->as<__half>(), F, G, outs[2], col->as<__half>()))) return rc;
+    if ((rc = conv3x3(ctx, sc[2].c3, c1->as<__half>(), F, G, outs[2], colp))) return rc;
   }
   // scale 3: maxpool 2x2 -> 1x1 -> 3x3  (0.5x)
   {
     CK(maxpool2_cl_f16(xh, F, G, G, hp.vit_embed_dim, mp->as<__half>(), ctx->stream));
     CKG(gemm(ctx, mp->as<__half>(), hp.vit_embed_dim, sc[3].c1, T / 4, epi_store(sc[3].c1, c1->p, 0, D)));
-    if ((rc = conv3x3(ctx, sc[3].c3, c1->as<__half>(), F, G / 2, outs[3], col->as<__half>()))) return rc;
+    if ((rc = conv3x3(ctx, sc[3].c3, c1->as<__half>(), F, G / 2, outs[3], colp))) return rc;
   }
   return kOk;
 }

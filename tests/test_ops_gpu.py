@@ -313,19 +313,47 @@ def test_layernorm(engine, rows, C, f32):
     assert (out.float() - ref).abs().max().item() < (2e-5 * C ** 0.5 + 1e-4 if f32 else 2e-2)
 
 
-@pytest.mark.parametrize("B,H,W,C,Cout", [(1, 36, 36, 256, 256), (2, 17, 23, 64, 128), (1, 72, 72, 256, 256)])
-def test_conv3x3(engine, B, H, W, C, Cout):
+@pytest.mark.parametrize("implicit,pairs", [(1, 1), (1, 0), (0, 1)])
+@pytest.mark.parametrize("B,H,W,C,Cout", [(1, 36, 36, 256, 256), (2, 17, 23, 64, 128), (1, 72, 72, 256, 256),
+                                          (3, 9, 40, 128, 64), (1, 5, 7, 64, 256), (2, 144, 144, 256, 256)])
+def test_conv3x3(engine, implicit, pairs, B, H, W, C, Cout):
+    """3x3 / pad 1 conv: implicit GEMM (8 x 16 pixel blocks by 4-D TMA, zero-filled border taps, clipped
+    stores at ragged edges) on single SMs or SM pairs, and im2col + GEMM, against the fp32 reference."""
     g = torch.Generator(device="cuda").manual_seed(H * W + C)
     x = torch.randn(B, H, W, C, device="cuda", generator=g).half()
     w = (torch.randn(Cout, 3, 3, C, device="cuda", generator=g) * 0.05).half()
     bias = torch.randn(Cout, device="cuda", generator=g) * 0.1
-    out = torch.empty(B, H, W, Cout, device="cuda", dtype=torch.float32)
-    engine.conv3x3(x, w, bias, out)
-    engine.sync()
+    out = torch.full((B, H, W, Cout), float("nan"), device="cuda", dtype=torch.float32)
+    engine.set_option("conv_implicit", implicit)
+    engine.set_option("gemm_pairs", pairs)
+    try:
+        engine.conv3x3(x, w, bias, out)
+        engine.sync()
+    finally:
+        engine.set_option("conv_implicit", 1)
+        engine.set_option("gemm_pairs", 1)
     ref = torch.nn.functional.conv2d(x.float().permute(0, 3, 1, 2), w.float().permute(0, 3, 1, 2), bias, padding=1)
     ref = ref.permute(0, 2, 3, 1)
     err = (out - ref).abs().max().item()
     assert err < 2e-3 * max(1.0, ref.abs().max().item()), err
+
+
+def test_conv3x3_implicit_equals_im2col(engine):
+    """The implicit GEMM reads the same products in the same K order (tap, channel) as the GEMM over
+    the column matrix, so both paths give the same bits."""
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(2, 40, 56, 256, device="cuda", generator=g).half()
+    w = (torch.randn(256, 3, 3, 256, device="cuda", generator=g) * 0.05).half()
+    bias = torch.randn(256, device="cuda", generator=g) * 0.1
+    outs = []
+    for implicit in (1, 0):
+        engine.set_option("conv_implicit", implicit)
+        out = torch.empty(2, 40, 56, 256, device="cuda", dtype=torch.float32)
+        engine.conv3x3(x, w, bias, out)
+        engine.sync()
+        outs.append(out)
+    engine.set_option("conv_implicit", 1)
+    assert torch.equal(outs[0], outs[1])
 
 
 @pytest.mark.parametrize("qtype", [2, 3, 8])
