@@ -3,12 +3,13 @@
 
 Workload: SAM 3 ViT image encoder + tracker
 SimpleFPN neck, q4_0 weights (seeded synthetic, random-init), 64 seeded
-1008x1008 frames sharded over N GPUs (64/N frames per GPU, one process per
-GPU, no data-path collective). One step = encode all frames of the rank.
+1008x1008 frames per GPU (rank r encodes frames [64 r, 64 r + 64): weak
+scaling, one process per GPU, no data-path collective). One step = encode
+all frames of the rank; `value` = all ranks' frames / the slowest rank's time.
 The same line carries `hiera_t_q4_0` (configs[1]: SAM 2.1 Hiera-T + FPN
 neck, q4_0, 16 seeded 1024x1024 frames per GPU) and `video_hiera_l_q8_0`
-(configs[4]: Hiera-L q8_0 on 64 frames sharded over the GPUs, then memory
-attention per frame on GPU 0), timed the same way.
+(configs[4]: Hiera-L q8_0 on 64 frames per GPU, then memory attention per
+frame on GPU 0), timed the same way.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload vit_q4_0|vit_f16]
   python bench.py --impl reference ...   # CPU restatement (oracle) of the same path
@@ -52,6 +53,12 @@ def load_pkg():
     sys.modules[name] = mod
     spec.loader.exec_module(mod)
     return mod
+
+
+def rank_frames(per_gpu: int, rank: int) -> tuple[int, int]:
+    """Frames [first, first + per_gpu) encoded by `rank` (weak scaling: every rank encodes per_gpu frames
+    of its own; frame f keeps its seed on any world size)."""
+    return rank * per_gpu, per_gpu
 
 
 def shard_frames(total: int, rank: int, world: int) -> tuple[int, int]:
@@ -141,7 +148,7 @@ def bench_video(s3b, local: int, rank: int, world: int, steps: int, warmup: int,
         dist.barrier()
     eng = s3b.Engine(local)
     eng.load_model(path)
-    first, nf = shard_frames(FRAMES_TOTAL, rank, world)
+    first, nf = rank_frames(FRAMES_TOTAL, rank)
     frames = torch.from_numpy(synth.frames_u8(nf, 1024, base_seed=1000 + first)).to(device)
     for _ in range(warmup):
         eng.encode_u8(frames)
@@ -161,8 +168,8 @@ def bench_video(s3b, local: int, rank: int, world: int, steps: int, warmup: int,
     ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
     g, a = prof["gemm"], prof["attention"]
     out = {"workload": f"configs[4]: SAM 2.1 Hiera-L image encoder + FPN neck, q8_0 weights, {FRAMES_TOTAL} seeded "
-                       f"1024^2 frames sharded over {world} GPU(s); memory attention per frame on GPU 0",
-           "encoder_frames_per_s": FRAMES_TOTAL / (ms / 1000.0), "encoder_ms_per_step": ms,
+                       f"1024^2 frames per GPU x {world} GPU(s); memory attention per frame on GPU 0",
+           "encoder_frames_per_s": FRAMES_TOTAL * world / (ms / 1000.0), "encoder_ms_per_step": ms,
            "encoder_gemm_tflops": g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0,
            "encoder_attention_tflops": a["flops"] / (a["ms"] / 1000.0) / 1e12 if a["ms"] > 0 else 0.0}
     if rank == 0:
@@ -316,7 +323,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="vit_q4_0", choices=["vit_q4_0", "vit_q8_0", "vit_f16"])
-    ap.add_argument("--frames", type=int, default=FRAMES_TOTAL)
+    ap.add_argument("--frames", type=int, default=FRAMES_TOTAL, help="frames per GPU")
     ap.add_argument("--frames-per-pass", type=int, default=8)
     ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1, 2],
                     help="256-row GEMM tiles on SM pairs: 1 (default) for K >= 2048, 2 for all, 0 never")
@@ -332,8 +339,8 @@ def main():
     n_gpus = max(world, 1)
     metric = "encoder frames/sec (SAM 3 ViT 1008^2 + SimpleFPN neck)"
     cfg_json = {"workload": f"configs[3]: SAM 3 ViT-L encoder + tracker neck, {args.workload.split('_', 1)[1]} "
-                            f"weights, {args.frames} seeded 1008^2 frames sharded over {n_gpus} GPU(s)",
-                "frames_total": args.frames, "frames_per_gpu": shard_frames(args.frames, 0, n_gpus)[1],
+                            f"weights, {args.frames} seeded 1008^2 frames per GPU x {n_gpus} GPU(s)",
+                "frames_total": args.frames * n_gpus, "frames_per_gpu": args.frames,
                 "img_size": 1008,
                 "parallelism": f"frame-sharded x{n_gpus} (no collective)",
                 "l2_flush": "inputs + activations per step >> 126 MB L2"}
@@ -348,7 +355,7 @@ def main():
         t0 = time.perf_counter()
         v, parts = cpu_sample(args.workload, steps)
         elapsed = time.perf_counter() - t0
-        ms = 1000.0 * FRAMES_TOTAL / v / n_gpus
+        ms = 1000.0 * args.frames / v
         line = {"impl": "reference", "metric": metric, "value": v, "unit": "frames/s", "n_gpus": n_gpus,
                 "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": ms, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init)",
@@ -386,7 +393,7 @@ def main():
     eng.load_model(path)
     load_s = time.time() - t0
 
-    first, nf = shard_frames(args.frames, rank, n_gpus)
+    first, nf = rank_frames(args.frames, rank)
     host = synth.frames_u8(nf, cfg.img_size, base_seed=1000 + first)
     host_t = torch.from_numpy(host).pin_memory()
     dev = host_t.cuda()
@@ -417,7 +424,7 @@ def main():
     prof = eng.profile_end()
     clk = clocks.stop()
     ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world, "cuda")
-    value = args.frames / (ms / 1000.0)
+    value = args.frames * n_gpus / (ms / 1000.0)
 
     # --- end-to-end through the public API with host buffers
     if world > 1:
@@ -435,7 +442,7 @@ def main():
     ev3.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(ev2.elapsed_time(ev3) / args.steps, world, "cuda")
-    e2e = args.frames / (e2e_ms / 1000.0)
+    e2e = args.frames * n_gpus / (e2e_ms / 1000.0)
 
     # --- roofline of the dominant kernel (tensor-core GEMM)
     peak_burst, peak_sust, hbm, src = measured_peaks()

@@ -20,14 +20,14 @@ def load(name, path):
 
 
 def main():
-    outdir, total = sys.argv[1], int(sys.argv[2])
+    outdir, per_gpu = sys.argv[1], int(sys.argv[2])
     import torch.distributed as dist
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
     bench = load("bench_under_test", os.path.join(ROOT, "bench.py"))
     bench.load_pkg()
     from sam3_b200 import synth
-    first, n = bench.shard_frames(total, rank, world)
+    first, n = bench.rank_frames(per_gpu, rank)
     frames = synth.frames_u8(n, 8, base_seed=1000 + first)
     digests = [hashlib.sha256(f.tobytes()).hexdigest() for f in frames]
     # each rank reports a different "time"; every rank must see the max
