@@ -74,7 +74,8 @@ int s3b_sync(s3b_ctx* ctx);
  * warps instead of 8; 0: all run 8; process-wide);
  * "conv_implicit" (1, default: 3x3 convolutions with C a multiple of 64 run
  * as implicit GEMMs whose TMA loads fetch the shifted pixel blocks, no
- * column matrix; 0: im2col + GEMM);
+ * column matrix, and the neck's 2x2 deconvolutions store their outputs
+ * through 5-D TMA; 0: im2col + GEMM and scattered deconvolution stores);
  * "attention_exp_poly" (0-4: of every 8 softmax exponentials in the tcgen05
  * kernel, how many are evaluated by a polynomial on the FMA pipe instead of
  * the MUFU unit; a tuning knob, results agree to f16 rounding);
@@ -204,6 +205,18 @@ int s3b_op_layernorm(s3b_ctx* ctx, const float* x, void* out, int out_f32, int64
  * multiples of 8. */
 int s3b_op_conv3x3(s3b_ctx* ctx, const void* x, int B, int H, int W, int C, const void* w, const float* bias,
                    float* out, int Cout);
+
+/* 2x2 / stride 2 transposed convolution on channel-last f16 maps x
+ * [B][H][W][Cin] with weights w f16 [2][2][Cout][Cin] (rows (ky*2 + kx)*Cout +
+ * co of Cin values, i.e. the ggml kernel [2, 2, Cout, Cin] repacked), bias
+ * f32 [Cout] or NULL, act 0 (none) or 1 (GELU, erf form), out f16 (out_f32 =
+ * 0) or f32 [B][2H][2W][Cout]. Cin a multiple of 8, Cout of 32. A GEMM over
+ * 8 x 16 input-pixel blocks whose outputs leave through 5-D TMA stores
+ * (option "conv_implicit" = 0: scattered stores). Replaces
+ * ggml_conv_transpose_2d_p0 + bias (+ ggml_gelu_erf) of the SimpleFPN
+ * neck (sam3_build_neck_graph, sam3.cpp:3863-3921). */
+int s3b_op_deconv2x2(s3b_ctx* ctx, const void* x, int B, int H, int W, int Cin, const void* w, const float* bias,
+                     int act, void* out, int out_f32, int Cout);
 
 /* Size of the static device scratch used by s3b_conv3x3_noalloc (32 MiB). */
 #define S3B_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)

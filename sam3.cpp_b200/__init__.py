@@ -64,6 +64,7 @@ SYMBOLS = [
     ("s3b_op_attention_qkv", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _I, _F]),
     ("s3b_op_layernorm", _I, [_P, _P, _P, _I, _I64, _I, _P, _P, _F]),
     ("s3b_op_conv3x3", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),
+    ("s3b_op_deconv2x2", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _I, _P, _I, _I]),
     ("s3b_conv3x3_noalloc", _I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _P]),
     ("s3b_op_dequantize", _I, [_P, _P, _I, _I64, _I64, _P]),
     ("s3b_row_size", _I64, [_I, _I64]),
@@ -333,6 +334,14 @@ class Engine:
         Cout = w.shape[0]
         rc = self._L.s3b_op_conv3x3(self.h, x.data_ptr(), B, H, W, C, w.data_ptr(), _ptr(bias), out.data_ptr(), Cout)
         self._check(rc, "s3b_op_conv3x3")
+
+    def deconv2x2(self, x, w, bias, out, act: int = 0):
+        """x f16 [B,H,W,Cin], w f16 [2,2,Cout,Cin], bias f32 [Cout] or None, out f16 / f32 [B,2H,2W,Cout]."""
+        B, H, W, Cin = x.shape
+        Cout = w.shape[2]
+        rc = self._L.s3b_op_deconv2x2(self.h, x.data_ptr(), B, H, W, Cin, w.data_ptr(), _ptr(bias), act,
+                                      out.data_ptr(), 1 if out.dtype.itemsize == 4 else 0, Cout)
+        self._check(rc, "s3b_op_deconv2x2")
 
     def dequantize(self, raw, qtype: int, ne0: int, nrows: int, out):
         rc = self._L.s3b_op_dequantize(self.h, raw.data_ptr(), qtype, ne0, nrows, out.data_ptr())

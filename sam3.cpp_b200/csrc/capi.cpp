@@ -583,6 +583,39 @@ int s3b_op_conv3x3(s3b_ctx* ctx, const void* x, int B, int H, int W, int C, cons
   return kOk;
 }
 
+int s3b_op_deconv2x2(s3b_ctx* ctx, const void* x, int B, int H, int W, int Cin, const void* w, const float* bias,
+                     int act, void* out, int out_f32, int Cout) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!x || !w || !out || B <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0 || Cin % 8 || Cout % 32 ||
+      (act != 0 && act != 1))
+    return set_error(ctx, kErrArg, "bad deconv2x2 arguments");
+  EpiParams ep;
+  ep.mode = EPI_STORE;
+  ep.bias = bias;
+  ep.act = act ? ACT_GELU_ERF : ACT_NONE;
+  ep.out = out;
+  ep.out_f32 = out_f32 ? 1 : 0;
+  ep.ldo = Cout;
+  const __half* xh = reinterpret_cast<const __half*>(x);
+  const __half* wh = reinterpret_cast<const __half*>(w);
+  if (ctx->conv_implicit) {
+    rc = gemm_deconv2x2(xh, B, H, W, Cin, wh, Cin, Cout, ep, ctx->d_err, ctx->stream);
+    if (rc != -2) {
+      if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "deconv2x2 launch failed (%d)", rc);
+      return kOk;
+    }
+  }
+  // scattered 16-value stores of each (ky, kx) group at pixel (2y + ky, 2x + kx)
+  ep.mode = EPI_DECONV2;
+  ep.cout = Cout;
+  ep.map.W = W;
+  ep.map.H = H;
+  rc = gemm_f16(xh, Cin, wh, Cin, B * H * W, 4 * Cout, Cin, ep, ctx->d_err, ctx->stream);
+  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "deconv2x2 gemm launch failed (%d)", rc);
+  return kOk;
+}
+
 int s3b_op_dequantize(s3b_ctx* ctx, const void* src, int type, int64_t ne0, int64_t nrows, float* dst) {
   int rc = ctx_enter(ctx);
   if (rc) return rc;

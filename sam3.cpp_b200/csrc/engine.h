@@ -215,7 +215,7 @@ struct s3b_ctx {
   int stop_after_blocks = -1;  // test hook: run only the first n backbone blocks (-1: all)
   int attention_impl = 0;      // 0: tcgen05 where eligible, 1: always mma.sync, 2: d = 64 on the wide tcgen05 kernel,
                                // 3: as 0, d = 64 with P in shared memory
-  int conv_implicit = 1;       // 3x3 convs as implicit GEMMs (0: im2col + GEMM)
+  int conv_implicit = 1;       // pixel-block GEMMs: implicit 3x3 convs, TMA-stored deconvs (0: im2col / scatter)
   int attention_exp_poly = 0;  // of every 8 softmax exponentials in the tcgen05 kernel, how many use the FMA pipe
   // launch accounting + optional per-kernel CUDA-event timing (s3b_profile_*)
   long long n_launches = 0;
@@ -248,6 +248,7 @@ int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long
 int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads);
 int run_conv3x3(s3b_ctx* ctx, const Linear& L, const __half* x, int F, int H, int W, const EpiParams& ep,
                 __half* col);
+int run_deconv2x2(s3b_ctx* ctx, const Linear& L, const __half* x, int F, int H, int W, EpiParams ep);
 // layernorm() on the context stream, timed when profiling; returns layernorm's status (the caller counts the launch)
 int run_ln(s3b_ctx* ctx, const float* x, long long ldx, void* y, int y_f32, long long ldy, long long rows, int C,
            const float* g, const float* b, float eps, const RowMap& map);

@@ -235,6 +235,11 @@ __device__ __forceinline__ void tma_store_4d(const void* map, const void* src, i
                "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
                : "memory");
 }
+__device__ __forceinline__ void tma_store_5d(const void* map, const void* src, int x, int y, int z, int w, int v) {
+  asm volatile("cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -250,12 +255,16 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // `tempty`.
 // EW: epilogue warps, 8 (2 column groups) or 16 (4 column groups, for epilogues
 // that would otherwise outlast the main loop).
-// CONV: implicit 3x3 / pad 1 convolution over the channel-last f16 map
-// [conv_F][conv_H][conv_W][conv_C] (A never materialised): a tile's 128 rows are an
-// 8 x 16 pixel block (the pair's two CTAs take vertically adjacent blocks), and
-// k-block kb = (tap, 64-channel block) is one 4-D TMA load of the block shifted by
-// the tap; TMA zero-fills the taps outside the map, which is the padding. The
-// output tile goes out through a 4-D TMA store that clips at the map's edges.
+// BLK (pixel-block tiling of a channel-last f16 input map [conv_F][conv_H][conv_W][conv_C]):
+// a tile's 128 rows are an 8 x 16 pixel block (the pair's two CTAs take vertically adjacent
+// blocks), loaded by 4-D TMA.
+//   BLK 1, implicit 3x3 / pad 1 convolution (A never materialised): k-block kb = (tap, 64-channel
+//     block) is the block shifted by the tap; TMA zero-fills the taps outside the map, which is
+//     the padding. The output tile goes out through a 4-D TMA store that clips at the map's edges.
+//   BLK 2, 2x2 / stride 2 deconvolution (EPI_DECONV2 columns (ky*2 + kx)*cout + co): for one ky,
+//     the columns (kx, co) of the block's pixels are a regular box of the [F][2H][2W][cout]
+//     output, (kx*cout + co, x, ky, y, f) with strides (1, 2 cout, 2W cout, 4W cout, 4HW cout):
+//     one 5-D TMA store per chunk instead of scattered 16-value stores.
 template <int CONV_TY_BLOCKS>
 __device__ __forceinline__ void conv_tile_origin(int mt, const EpiParams& ep, uint32_t rank, int* x0, int* y0,
                                                  int* f) {
@@ -268,7 +277,7 @@ __device__ __forceinline__ void conv_tile_origin(int mt, const EpiParams& ep, ui
   *y0 = ty * 8 * CONV_TY_BLOCKS + (int)rank * 8;
 }
 
-template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW, bool CONV = false>
+template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW, int BLK = 0>
 __global__ void __launch_bounds__(gemm_threads(EW), 1)
     gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M,
@@ -281,7 +290,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
   constexpr uint32_t TMEM_COLS = 2 * BN;
   constexpr uint32_t STAGING = TMA_EPI ? 4 * kStageBufBytes : 0;
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
-  static_assert(!CONV || TMA_EPI, "the implicit convolution stores through TMA");
+  static_assert(BLK == 0 || TMA_EPI, "pixel-block tiles store through TMA");
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512 || TMEM_COLS == 128, "TMEM columns must be a power of 2");
 
   extern __shared__ uint8_t smem_raw[];
@@ -349,30 +358,31 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       uint32_t armed = 0;        // bit s: stage s has been armed at least once
       uint32_t armed_phase = 0;  // bit s: parity of the last arming of stage s
       bool ok = true;
-      const int cbn = CONV ? ep.conv_C / kBK : 1;  // 64-channel blocks per tap
+      const int cbn = BLK == 1 ? ep.conv_C / kBK : 1;  // 64-channel blocks per tap
       for (int t = unit; t < n_tiles && ok; t += n_units) {
         const int m0 = (t / tiles_n) * TM + (int)rank * kBM;
         const int n0 = (t % tiles_n) * BN + (int)rank * BN_CTA;
         int cx = 0, cy = 0, cf = 0;
-        if (CONV) conv_tile_origin<PAIR ? 2 : 1>(t / tiles_n, ep, rank, &cx, &cy, &cf);
+        if (BLK) conv_tile_origin<PAIR ? 2 : 1>(t / tiles_n, ep, rank, &cx, &cy, &cf);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
-          // CONV: k-block kb = tap (ky, kx) x channel block cb; the block shifted by (kx - 1, ky - 1)
-          const int tap = CONV ? kb / cbn : 0;
-          const int cb = CONV ? kb - tap * cbn : 0;
+          // BLK 1: k-block kb = tap (ky, kx) x channel block cb, the block shifted by (kx - 1, ky - 1);
+          // BLK 2: channel block kb of the block itself
+          const int tap = BLK == 1 ? kb / cbn : 4;
+          const int cb = BLK == 1 ? kb - tap * cbn : kb;
           const int ky = tap / 3, kx = tap - 3 * (tap / 3);
           if (PAIR) {
             // both CTAs' bytes complete the leader's barrier; only the leader arms it
             const uint32_t fb = cluster_addr(smem_u32(&full[stage]), 0);
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
-            if (CONV)
+            if (BLK)
               tma_load_4d_pair(&tmA, fb, sA + stage * A_BYTES, cb * kBK, cx + kx - 1, cy + ky - 1, cf);
             else
               tma_load_2d_pair(&tmA, fb, sA + stage * A_BYTES, kb * kBK, m0);
             tma_load_2d_pair(&tmB, fb, sB + stage * B_BYTES, kb * kBK, n0);
           } else {
             mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-            if (CONV)
+            if (BLK)
               tma_load_4d(&tmA, &full[stage], sA + stage * A_BYTES, cb * kBK, cx + kx - 1, cy + ky - 1, cf);
             else
               tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, m0);
@@ -483,7 +493,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       const int m0 = (t / tiles_n) * TM + (int)rank * kBM;
       const int n0 = (t % tiles_n) * BN;
       int cx = 0, cy = 0, cf = 0;
-      if (CONV) conv_tile_origin<PAIR ? 2 : 1>(t / tiles_n, ep, rank, &cx, &cy, &cf);
+      if (BLK) conv_tile_origin<PAIR ? 2 : 1>(t / tiles_n, ep, rank, &cx, &cy, &cf);
       // the first residual chunk does not depend on the accumulator: fetch it during the main loop
       if (TMA_EPI && rip && leader) issue_resid(chunk_ctr, n0 + grp * CG, m0);
       if (!mbar_wait(&tfull[acc], aphase, s_abort, err, kErrWaitTmemFull)) break;
@@ -562,7 +572,14 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
           fence_proxy_async_smem();
           named_bar(1 + grp, 128);
           if (leader && gcb < N) {
-            if (CONV) tma_store_4d(&tmC, buf, gcb, cx, cy, cf); else tma_store_2d(&tmC, buf, gcb, m0);
+            if (BLK == 1) {
+              tma_store_4d(&tmC, buf, gcb, cx, cy, cf);
+            } else if (BLK == 2) {
+              const int ky = gcb / (2 * ep.cout);  // a chunk never straddles a ky (2 cout is a multiple of 64)
+              tma_store_5d(&tmC, buf, gcb - ky * 2 * ep.cout, cx, ky, cy, cf);
+            } else {
+              tma_store_2d(&tmC, buf, gcb, m0);
+            }
             bulk_commit();
           }
           if (rip && leader && c0 + cw < CG) issue_resid(chunk_ctr + 1, gcb + cw, m0);
@@ -666,21 +683,42 @@ int make_map_conv(CUtensorMap* map, const void* base, int F, int H, int W, int C
   return r == CUDA_SUCCESS ? 0 : -12;
 }
 
-// CONV: A is the channel-last input map of gemm_conv3x3 (geometry in ep.conv_*) and M the number of
-// pixel-block tiles x the tile rows.
-template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW = 8, bool CONV = false>
+// 5-D tensor map over the [F][2H][2W][cout] output of a 2x2 / stride 2 deconvolution seen as
+// (kx*cout + co, x, ky, y, f), box = (128 B) x 16 x 1 x 8 x 1 (the 8 x 16 input-pixel block's
+// outputs for one ky and 128 B of (kx, co)), SW128.
+int make_map_deconv_out(CUtensorMap* map, const void* base, int F, int H, int W, int cout, int elem_bytes) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return -10;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || ((long long)cout * elem_bytes) % 16 != 0) return -11;
+  const cuuint64_t c = (cuuint64_t)cout, eb = (cuuint64_t)elem_bytes;
+  cuuint64_t dims[5] = {2 * c, (cuuint64_t)W, 2, (cuuint64_t)H, (cuuint64_t)F};
+  cuuint64_t strides[4] = {2 * c * eb, 2 * (cuuint64_t)W * c * eb, 4 * (cuuint64_t)W * c * eb,
+                           4 * (cuuint64_t)H * W * c * eb};
+  cuuint32_t box[5] = {(cuuint32_t)(128 / elem_bytes), 16, 1, 8, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -12;
+}
+
+// BLK 1 / 2: A is the channel-last input map (geometry in ep.conv_*) of gemm_conv3x3 /
+// gemm_deconv2x2 and M the number of pixel-block tiles x the tile rows.
+template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW = 8, int BLK = 0>
 int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
                 const EpiParams& ep, int resid_in_place, int* err, cudaStream_t st) {
   constexpr int BN_CTA = PAIR ? BN / 2 : BN;
   CUtensorMap ma, mb, mc, mr;
-  int rc = CONV ? make_map_conv(&ma, A, ep.conv_F, ep.conv_H, ep.conv_W, ep.conv_C, 2)
-                : make_map_2d(&ma, A, M, K, lda, kBM, 2);
+  int rc = BLK ? make_map_conv(&ma, A, ep.conv_F, ep.conv_H, ep.conv_W, ep.conv_C, 2)
+               : make_map_2d(&ma, A, M, K, lda, kBM, 2);
   if (rc) return rc;
   rc = make_map_2d(&mb, B, N, K, ldb, BN_CTA, 2);
   if (rc) return rc;
   if (TMA_EPI) {
-    rc = CONV ? make_map_conv(&mc, ep.out, ep.conv_F, ep.conv_H, ep.conv_W, N, ep.out_f32 ? 4 : 2)
-              : make_map_2d(&mc, ep.out, M, N, ep.ldo, kBM, ep.out_f32 ? 4 : 2);
+    const int eb = ep.out_f32 ? 4 : 2;
+    if (BLK == 1) rc = make_map_conv(&mc, ep.out, ep.conv_F, ep.conv_H, ep.conv_W, N, eb);
+    else if (BLK == 2) rc = make_map_deconv_out(&mc, ep.out, ep.conv_F, ep.conv_H, ep.conv_W, ep.cout, eb);
+    else rc = make_map_2d(&mc, ep.out, M, N, ep.ldo, kBM, eb);
     if (rc) return rc;
   } else {
     mc = ma;  // unused
@@ -695,7 +733,7 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
   constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN_CTA) * kBK * 2 + (TMA_EPI ? 4 * kStageBufBytes : 0) +
                           (2 * STAGES + 9) * 8 + 16;
   static_assert(smem <= 232448, "shared memory per CTA");
-  auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR, EW, CONV>;
+  auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR, EW, BLK>;
   constexpr int kThreads = gemm_threads(EW);
   static bool attr_set = false;
   static int max_units = 0;  // co-resident CTAs (or pairs)
@@ -830,8 +868,29 @@ int gemm_conv3x3(const __half* x, int F, int H, int W, int C, const __half* Bw, 
   const long long tiles = (long long)F * ((W + 15) / 16) * ((H + (pair ? 15 : 7)) / (pair ? 16 : 8));
   const long long m_virtual = tiles * (pair ? 2 * kBM : kBM);
   if (m_virtual > 0x7fffffffLL) return -2;
-  if (pair) return launch_gemm<256, 5, true, true, 8, true>(x, C, Bw, ldb, (int)m_virtual, N, K, ep, 0, err, st);
-  return launch_gemm<256, 3, true, false, 8, true>(x, C, Bw, ldb, (int)m_virtual, N, K, ep, 0, err, st);
+  if (pair) return launch_gemm<256, 5, true, true, 8, 1>(x, C, Bw, ldb, (int)m_virtual, N, K, ep, 0, err, st);
+  return launch_gemm<256, 3, true, false, 8, 1>(x, C, Bw, ldb, (int)m_virtual, N, K, ep, 0, err, st);
+}
+
+int gemm_deconv2x2(const __half* x, int F, int H, int W, int Cin, const __half* Bw, long long ldb, int cout,
+                   const EpiParams& ep_in, int* err, cudaStream_t st) {
+  if (F <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cin % 8 || cout <= 0 || cout % 32) return -2;
+  if (ep_in.resid || ep_in.rope || ep_in.map.kind != 0) return -2;
+  if ((reinterpret_cast<uintptr_t>(ep_in.out) & 15) || (reinterpret_cast<uintptr_t>(x) & 15)) return -2;
+  EpiParams ep = ep_in;
+  ep.mode = EPI_DECONV2;
+  ep.cout = cout;
+  ep.conv_F = F;
+  ep.conv_H = H;
+  ep.conv_W = W;
+  ep.conv_C = Cin;
+  const int N = 4 * cout, K = Cin;
+  const bool pair = g_gemm_pairs != 0;
+  const long long tiles = (long long)F * ((W + 15) / 16) * ((H + (pair ? 15 : 7)) / (pair ? 16 : 8));
+  const long long m_virtual = tiles * (pair ? 2 * kBM : kBM);
+  if (m_virtual > 0x7fffffffLL) return -2;
+  if (pair) return launch_gemm<256, 5, true, true, 16, 2>(x, Cin, Bw, ldb, (int)m_virtual, N, K, ep, 0, err, st);
+  return launch_gemm<256, 3, true, false, 16, 2>(x, Cin, Bw, ldb, (int)m_virtual, N, K, ep, 0, err, st);
 }
 
 void set_gemm_pairs(int mode) { g_gemm_pairs = mode; }

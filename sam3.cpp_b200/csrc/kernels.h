@@ -80,6 +80,12 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
 // RoPE or row map). Returns -2 when those conditions do not hold (callers fall back to im2col).
 int gemm_conv3x3(const __half* x, int F, int H, int W, int C, const __half* Bw, long long ldb, int N,
                  const EpiParams& ep, int* err, cudaStream_t st);
+// 2x2 / stride 2 deconvolution (ConvTranspose2d) as a GEMM over pixel blocks whose outputs leave
+// through 5-D TMA stores: x channel-last f16 [F][H][W][Cin] (Cin a multiple of 8), weights Bw
+// [4*cout][Cin] with rows (ky*2 + kx)*cout + co, output [F][2H][2W][cout] (cout a multiple of 32)
+// through ep (bias per co, activation, f16 or f32). Returns -2 when the conditions do not hold.
+int gemm_deconv2x2(const __half* x, int F, int H, int W, int Cin, const __half* Bw, long long ldb, int cout,
+                   const EpiParams& ep, int* err, cudaStream_t st);
 // Process-wide: which wide TMA-epilogue GEMMs use 256-row tiles on SM pairs:
 // 0 none, 1 (default) those with K >= 2048 or f16 outputs on 16 epilogue warps, 2 all.
 void set_gemm_pairs(int mode);

@@ -86,6 +86,38 @@ int run_conv3x3(s3b_ctx* ctx, const Linear& L, const __half* x, int F, int H, in
   return run_gemm(ctx, col, L.Kpad, L, M, ep);
 }
 
+// 2x2 / stride 2 deconvolution of a channel-last f16 map [F][H][W][Cin] into [F][2H][2W][cout]
+// (cout = L.N / 4): pixel-block GEMM with 5-D TMA output stores when the option and the shapes
+// allow, else the GEMM with scattered 16-value stores (EPI_DECONV2). Counted and timed as a GEMM.
+int run_deconv2x2(s3b_ctx* ctx, const Linear& L, const __half* x, int F, int H, int W, EpiParams ep) {
+  const int cout = L.N / 4;
+  const long long M = (long long)F * H * W;
+  if (ctx->conv_implicit && L.Kpad == L.K) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (ctx->prof) {
+      a = ctx->next_event();
+      b = ctx->next_event();
+      cudaEventRecord(a, ctx->stream);
+    }
+    const int rc = gemm_deconv2x2(x, F, H, W, L.K, L.w->as<__half>(), L.Kpad, cout, ep, ctx->d_err, ctx->stream);
+    if (rc != -2) {
+      count_launch(ctx);
+      if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "deconv2x2 failed (%d)", rc);
+      if (ctx->prof) {
+        cudaEventRecord(b, ctx->stream);
+        const double bytes = 2.0 * M * L.K + 2.0 * L.N * L.K + (ep.out_f32 ? 4.0 : 2.0) * M * L.N;
+        ctx->prof_entries.push_back({0, 2.0 * M * L.N * L.K, bytes, a, b});
+      }
+      return kOk;
+    }
+  }
+  ep.mode = EPI_DECONV2;
+  ep.cout = cout;
+  ep.map.W = W;
+  ep.map.H = H;
+  return run_gemm(ctx, x, L.Kpad, L, M, ep);
+}
+
 // LayerNorm (HBM-bound): algorithmic bytes = f32 rows in + rows out (f16 / f32) + gamma, beta.
 int run_ln(s3b_ctx* ctx, const float* x, long long ldx, void* y, int y_f32, long long ldy, long long rows, int C,
            const float* g, const float* b, float eps, const RowMap& map) {

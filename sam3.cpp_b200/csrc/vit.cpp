@@ -124,25 +124,15 @@ static int vit_neck(s3b_ctx* ctx, const NeckScale* sc, const __half* xh, int F, 
   if (rc) return rc;
   // scale 0: deconv(E->512) + GELU(erf) -> [deconv(512->D) -> 1x1, folded into one deconv] -> 3x3  (4x)
   {
-    EpiParams e1 = epi_store(sc[0].dc1, d1->p, 0, c_mid, ACT_GELU_ERF);
-    e1.mode = EPI_DECONV2;
-    e1.cout = c_mid;
-    e1.map.W = e1.map.H = G;
-    CKG(gemm(ctx, xh, hp.vit_embed_dim, sc[0].dc1, T, e1));
-    EpiParams e2 = epi_store(sc[0].dcf, c1->p, 0, D);
-    e2.mode = EPI_DECONV2;
-    e2.cout = D;
-    e2.map.W = e2.map.H = 2 * G;
-    CKG(gemm(ctx, d1->as<__half>(), c_mid, sc[0].dcf, T * 4, e2));
+    if ((rc = run_deconv2x2(ctx, sc[0].dc1, xh, F, G, G, epi_store(sc[0].dc1, d1->p, 0, c_mid, ACT_GELU_ERF))))
+      return rc;
+    if ((rc = run_deconv2x2(ctx, sc[0].dcf, d1->as<__half>(), F, 2 * G, 2 * G, epi_store(sc[0].dcf, c1->p, 0, D))))
+      return rc;
     if ((rc = conv3x3(ctx, sc[0].c3, c1->as<__half>(), F, 4 * G, outs[0], colp))) return rc;
   }
   // scale 1: [deconv(E->512) -> 1x1 (512->D), folded into one deconv] -> 3x3  (2x)
   {
-    EpiParams e1 = epi_store(sc[1].dcf, c1->p, 0, D);
-    e1.mode = EPI_DECONV2;
-    e1.cout = D;
-    e1.map.W = e1.map.H = G;
-    CKG(gemm(ctx, xh, hp.vit_embed_dim, sc[1].dcf, T, e1));
+    if ((rc = run_deconv2x2(ctx, sc[1].dcf, xh, F, G, G, epi_store(sc[1].dcf, c1->p, 0, D)))) return rc;
     if ((rc = conv3x3(ctx, sc[1].c3, c1->as<__half>(), F, 2 * G, outs[1], colp))) return rc;
   }
   // scale 2: 1x1 (E->D) -> 3x3  (1x)

@@ -338,6 +338,36 @@ def test_conv3x3(engine, implicit, pairs, B, H, W, C, Cout):
     assert err < 2e-3 * max(1.0, ref.abs().max().item()), err
 
 
+@pytest.mark.parametrize("blocks,pairs", [(1, 1), (1, 0), (0, 1)])
+@pytest.mark.parametrize("B,H,W,Cin,Cout,act,f32", [(1, 72, 72, 1024, 512, 1, 0), (2, 17, 23, 64, 256, 0, 0),
+                                                    (1, 36, 40, 512, 256, 0, 1), (3, 9, 5, 96, 64, 1, 1)])
+def test_deconv2x2(engine, blocks, pairs, B, H, W, Cin, Cout, act, f32):
+    """2x2 / stride 2 transposed conv: pixel-block GEMM with 5-D TMA output stores (ragged blocks
+    clipped) on single SMs or SM pairs, and the scattered-store GEMM, against the fp32 reference."""
+    g = torch.Generator(device="cuda").manual_seed(H * W + Cin + Cout)
+    x = torch.randn(B, H, W, Cin, device="cuda", generator=g).half()
+    w = (torch.randn(2, 2, Cout, Cin, device="cuda", generator=g) * (0.5 / Cin ** 0.5)).half()
+    bias = torch.randn(Cout, device="cuda", generator=g) * 0.1
+    out = torch.full((B, 2 * H, 2 * W, Cout), float("nan"), device="cuda",
+                     dtype=torch.float32 if f32 else torch.float16)
+    engine.set_option("conv_implicit", blocks)
+    engine.set_option("gemm_pairs", pairs)
+    try:
+        engine.deconv2x2(x, w, bias, out, act)
+        engine.sync()
+    finally:
+        engine.set_option("conv_implicit", 1)
+        engine.set_option("gemm_pairs", 1)
+    # torch weight layout for conv_transpose2d: [Cin][Cout][kh][kw]
+    wt = w.float().permute(3, 2, 0, 1).contiguous()
+    ref = torch.nn.functional.conv_transpose2d(x.float().permute(0, 3, 1, 2), wt, bias, stride=2)
+    if act:
+        ref = torch.nn.functional.gelu(ref)
+    ref = ref.permute(0, 2, 3, 1)
+    err = (out.float() - ref).abs().max().item()
+    assert err < (2e-3 if f32 else 1e-2) * max(1.0, ref.abs().max().item()), err
+
+
 def test_conv3x3_implicit_equals_im2col(engine):
     """The implicit GEMM reads the same products in the same K order (tap, channel) as the GEMM over
     the column matrix, so both paths give the same bits."""
