@@ -162,7 +162,7 @@ struct Model {
   bool loaded = false;
   // SAM 3 ViT
   Linear patch;                      // [1024][Kpad=592]
-  std::shared_ptr<DevBuf> pos_tiled; // f32 [72*72][1024]
+  std::shared_ptr<DevBuf> pos_tiled; // f32 [72*72 + 128][1024] (last 128 rows repeat the first)
   Vec ln_pre_w, ln_pre_b;
   std::vector<VitBlock> vit;
   NeckScale neck_trk[4], neck_det[4];

@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       if (gcb < N) {
         mbar_arrive_expect_tx(&rfull[bsel], kStageBufBytes);
         // the residual's row: the output row itself, or (resid_mod: a table repeated every
-        // resid_mod rows, a multiple of the 128-row tile) its row inside the table
+        // resid_mod rows, a multiple of the 128-row tile or wrap-padded) its row inside the table
         const int rrow = ep.resid_mod ? (int)((long long)m0 % ep.resid_mod) : m0;
         tma_load_2d(&tmR, &rfull[bsel], sC + bsel * kStageBufBytes, gcb, rrow);
       } else {
@@ -725,7 +725,7 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
   }
   if (TMA_EPI && resid_in_place && static_cast<const void*>(ep.resid) != ep.out) {
     // a separate f32 residual (resid_mod rows repeated, or M rows)
-    rc = make_map_2d(&mr, ep.resid, ep.resid_mod ? ep.resid_mod : M, N, ep.ldr, kBM, 4);
+    rc = make_map_2d(&mr, ep.resid, ep.resid_mod ? ep.resid_mod + (ep.resid_wrap_pad ? kBM : 0) : M, N, ep.ldr, kBM, 4);
     if (rc) return rc;
   } else {
     mr = mc;
@@ -819,12 +819,13 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
   const int eb = ep.out_f32 ? 4 : 2;
   // TMA epilogue: plain row-major output; the residual (f32 outputs) absent, the output itself, or a
   // separate f32 matrix, possibly a table repeated every resid_mod rows (a multiple of the 128-row tile,
-  // so no tile straddles a repeat), loaded by TMA into the staging buffer
+  // so no tile straddles a repeat, or wrap-padded by 128 rows), loaded by TMA into the staging buffer
   const bool resid_sep = ep.resid != nullptr && static_cast<const void*>(ep.resid) != ep.out;
   const bool resid_ok =
       ep.resid == nullptr ||
       (ep.out_f32 && !ep.resid_up &&
-       (resid_sep ? ((ep.resid_mod == 0 || ep.resid_mod % kBM == 0) && (ep.ldr * 4) % 16 == 0 && ep.ldr >= N &&
+       (resid_sep ? ((ep.resid_mod == 0 || ep.resid_mod % kBM == 0 || ep.resid_wrap_pad) && (ep.ldr * 4) % 16 == 0 &&
+                     ep.ldr >= N &&
                      (reinterpret_cast<uintptr_t>(ep.resid) & 15) == 0)
                   : (ep.resid_mod == 0 && ep.ldr == ep.ldo)));
   const bool tma_epi = ep.mode == EPI_STORE && ep.map.kind == 0 && resid_ok &&

@@ -56,6 +56,9 @@ struct EpiParams {
   long long ldr = 0;
   long long resid_mod = 0;
   int resid_up = 0;
+  // resid_mod tables only: the table holds resid_mod + 128 rows, the last 128 repeating the first
+  // (a 128-row output tile then reads its rows contiguously even across the repeat)
+  int resid_wrap_pad = 0;
   // EPI_STORE only: out = v * out_scale; RoPE on column pairs (2i, 2i+1) of
   // columns < rope_cols and GEMM rows < rope_rows: head dim rope_D, position
   // (row % rope_mod), position-major table [rope_D/2][rope_mod][2] (cos, sin).

@@ -559,11 +559,14 @@ static int load_sam3(s3b_ctx* ctx, const Index& idx) {
     std::vector<float> p;
     tensor_to_f32(*pos, p);
     const int G = (int)pos->ne[1], H = hp.n_img_embd();
-    std::vector<float> tiled((size_t)H * H * E);
-    // ggml_repeat of [E, G, G] to [E, H, H] (sam3.cpp:3817-3822)
+    // ggml_repeat of [E, G, G] to [E, H, H] (sam3.cpp:3817-3822), plus 128 rows repeating the first
+    // (the patch-embedding GEMM adds it per frame as a wrap-padded residual table)
+    std::vector<float> tiled(((size_t)H * H + 128) * E);
     for (int y = 0; y < H; ++y)
       for (int x = 0; x < H; ++x)
         memcpy(&tiled[((size_t)y * H + x) * E], &p[((size_t)(y % G) * G + (x % G)) * E], E * 4);
+    for (int r = 0; r < 128; ++r)
+      memcpy(&tiled[((size_t)H * H + r) * E], &tiled[(size_t)(r % (H * H)) * E], E * 4);
     M.pos_tiled = upload_bytes(ctx, tiled.data(), tiled.size() * 4, &rc);
     if (rc) return rc;
   }

@@ -205,6 +205,7 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
     pe.resid = M.pos_tiled->as<float>();
     pe.ldr = E;
     pe.resid_mod = tok_per_frame;
+    pe.resid_wrap_pad = 1;
     CKG(gemm(ctx, col->as<__half>(), Kp, M.patch, T, pe));
     // ln_pre (sam3.cpp:3825-3827)
     RowMap id;
