@@ -204,7 +204,9 @@ __device__ __forceinline__ float half_row_p(uint32_t taddr, int cbase, int kvali
 template <bool MASKED, int NPOLY>
 __device__ __forceinline__ float half_row_p_tmem(uint32_t taddr, int cbase, int kvalid, float sl2, float m,
                                                  uint32_t p_taddr, uint64_t* s_empty) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  // the scale-and-shift and the row sum run two-wide (packed f32x2); the exponentials one by one
+  const unsigned long long sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m, -m);
+  unsigned long long acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
   bool released = false;
 #pragma unroll
   for (int c = 0; c < kBK / 2; c += 32) {
@@ -223,16 +225,19 @@ __device__ __forceinline__ float half_row_p_tmem(uint32_t taddr, int cbase, int 
     for (int u = 0; u < 4; ++u) {
       float p[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
+      for (int e = 0; e < 8; e += 2) {
         const int i = 8 * u + e;
-        const float x = fmaf(__uint_as_float(r[i]), sl2, -m);
-        p[e] = e < NPOLY ? exp2_poly3(x) : ex2(x);
-        if (MASKED) p[e] = cbase + c + i < kvalid ? p[e] : 0.f;
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2x2, negm2), x0, x1);
+        p[e] = e < NPOLY ? exp2_poly3(x0) : ex2(x0);
+        p[e + 1] = e + 1 < NPOLY ? exp2_poly3(x1) : ex2(x1);
+        if (MASKED) {
+          p[e] = cbase + c + i < kvalid ? p[e] : 0.f;
+          p[e + 1] = cbase + c + i + 1 < kvalid ? p[e + 1] : 0.f;
+        }
       }
-      s0 += p[0] + p[4];
-      s1 += p[1] + p[5];
-      s2 += p[2] + p[6];
-      s3 += p[3] + p[7];
+      acc0 = f2_add(acc0, f2_add(f2_pack(p[0], p[1]), f2_pack(p[4], p[5])));
+      acc1 = f2_add(acc1, f2_add(f2_pack(p[2], p[3]), f2_pack(p[6], p[7])));
 #pragma unroll
       for (int e = 0; e < 4; ++e) pk[4 * u + e] = pack_h2(p[2 * e], p[2 * e + 1]);
     }
@@ -243,7 +248,10 @@ __device__ __forceinline__ float half_row_p_tmem(uint32_t taddr, int cbase, int 
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(s_empty);
   }
-  return (s0 + s1) + (s2 + s3);
+  float a0, a1, b0, b1;
+  f2_unpack(acc0, a0, a1);
+  f2_unpack(acc1, b0, b1);
+  return (a0 + a1) + (b0 + b1);
 }
 
 struct TcAttnArgs {

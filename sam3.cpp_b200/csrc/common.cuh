@@ -312,4 +312,50 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + th);
 }
 
+// Packed two-wide f32 arithmetic (sm_100: one instruction for two lanes of a 64-bit register pair).
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// gelu_erf on a pair of values: the degree-6 polynomial and the four squarings run two-wide.
+__device__ __forceinline__ void gelu_erf2(float& a, float& b) {
+  const unsigned long long ax = f2_pack(fabsf(a), fabsf(b));
+  unsigned long long q = f2_fma(f2_pack(5.6212996640e-06f, 5.6212996640e-06f), ax,
+                                f2_pack(5.1055209009e-05f, 5.1055209009e-05f));
+  q = f2_fma(q, ax, f2_pack(3.9686137011e-05f, 3.9686137011e-05f));
+  q = f2_fma(q, ax, f2_pack(3.4227392389e-03f, 3.4227392389e-03f));
+  q = f2_fma(q, ax, f2_pack(2.2076998457e-02f, 2.2076998457e-02f));
+  q = f2_fma(q, ax, f2_pack(5.2075163037e-02f, 5.2075163037e-02f));
+  q = f2_fma(q, ax, f2_pack(1.0442737824e+00f, 1.0442737824e+00f));
+  q = f2_mul(q, q);
+  q = f2_mul(q, q);
+  q = f2_mul(q, q);
+  q = f2_mul(q, q);
+  float qa, qb;
+  f2_unpack(q, qa, qb);
+  const float ha = rcp_approx(qa), hb = rcp_approx(qb);
+  a *= a >= 0.0f ? 1.0f - ha : ha;
+  b *= b >= 0.0f ? 1.0f - hb : hb;
+}
+
 }  // namespace s3b

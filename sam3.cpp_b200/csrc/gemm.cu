@@ -95,7 +95,8 @@ __device__ __forceinline__ void epi_math16(const EpiParams& ep, int rope_pos, in
 #pragma unroll
       for (int i = 0; i < 16; i += 4) {
         const float4 b = __ldg(reinterpret_cast<const float4*>(ep.bias + gc + i));
-        v[i] += b.x; v[i + 1] += b.y; v[i + 2] += b.z; v[i + 3] += b.w;
+        f2_unpack(f2_add(f2_pack(v[i], v[i + 1]), f2_pack(b.x, b.y)), v[i], v[i + 1]);
+        f2_unpack(f2_add(f2_pack(v[i + 2], v[i + 3]), f2_pack(b.z, b.w)), v[i + 2], v[i + 3]);
       }
     } else {
 #pragma unroll
@@ -106,7 +107,7 @@ __device__ __forceinline__ void epi_math16(const EpiParams& ep, int rope_pos, in
   // one uniform branch per activation, so the 16 independent evaluations interleave
   if (ep.act == ACT_GELU_ERF) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = gelu_erf(v[i]);
+    for (int i = 0; i < 16; i += 2) gelu_erf2(v[i], v[i + 1]);
   } else if (ep.act == ACT_GELU_TANH) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = gelu_tanh(v[i]);
@@ -553,7 +554,9 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
                     float4* sp = reinterpret_cast<float4*>(rowp + ((unit ^ (row & 7)) << 4));
                     if (rip) {
                       const float4 rv = *sp;
-                      v[4 * u] += rv.x; v[4 * u + 1] += rv.y; v[4 * u + 2] += rv.z; v[4 * u + 3] += rv.w;
+                      f2_unpack(f2_add(f2_pack(v[4 * u], v[4 * u + 1]), f2_pack(rv.x, rv.y)), v[4 * u], v[4 * u + 1]);
+                      f2_unpack(f2_add(f2_pack(v[4 * u + 2], v[4 * u + 3]), f2_pack(rv.z, rv.w)), v[4 * u + 2],
+                                v[4 * u + 3]);
                     }
                     *sp = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
                   }
