@@ -172,9 +172,46 @@ def bench_video(s3b, local: int, rank: int, world: int, steps: int, warmup: int,
            "encoder_frames_per_s": FRAMES_TOTAL * world / (ms / 1000.0), "encoder_ms_per_step": ms,
            "encoder_gemm_tflops": g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0,
            "encoder_attention_tflops": a["flops"] / (a["ms"] / 1000.0) / 1e12 if a["ms"] > 0 else 0.0}
+    # hand-off of per-frame features to the tracking GPU (rank 0): every other rank copies its frame 0's
+    # neck_trk_2 (the memory-attention input) into its slot of a rank-0 buffer opened through CUDA IPC
+    # (s3b_peer_copy_output over NVLink); rank 0 then runs memory attention on the frame rank 1 encoded
+    ne = eng.output_shape("neck_trk_2")
+    fbytes = ne[0] * ne[1] * ne[2] * 4
+    recv = None
+    if world > 1:
+        import torch.distributed as dist
+        if rank == 0:
+            recv = eng.device_alloc(fbytes * (world - 1))
+            handle = [eng.ipc_export(recv)]
+        else:
+            handle = [None]
+        dist.broadcast_object_list(handle, src=0)
+        ms_copy = 0.0
+        if rank > 0:
+            ptr = eng.ipc_open(handle[0])
+            dst = ptr + (rank - 1) * fbytes
+            for _ in range(warmup):
+                eng.peer_copy_output("neck_trk_2", 0, dst, 0, fbytes)
+            eng.sync()
+            e0.record(stream)
+            for _ in range(steps):
+                eng.peer_copy_output("neck_trk_2", 0, dst, 0, fbytes)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms_copy = e0.elapsed_time(e1) / steps
+            eng.ipc_close(ptr)
+        dist.barrier()
+        t = max_over_ranks(ms_copy, world, device)
+        out["p2p_neck_trk_2"] = {"bytes_per_frame": fbytes, "senders": world - 1, "ms_per_copy_max": t,
+                                 "gbs_per_sender": fbytes / (t / 1000.0) / 1e9 if t > 0 else None,
+                                 "path": "s3b_peer_copy_output into a rank-0 buffer opened with s3b_ipc_open"}
     if rank == 0:
-        # current frame = frame 0 of this rank's batch, its PE; random memory bank and pointer tokens
-        curr = torch.from_numpy(eng.output("neck_trk_2", 0).reshape(-1, 256)).to(device)
+        # current frame = frame 0 of rank 1 (received above) or of this rank's own batch; its PE; random
+        # memory bank and pointer tokens
+        if recv is not None:
+            curr = torch.as_tensor(_CudaArray(recv, fbytes // 4), device=device).view(-1, 256)
+        else:
+            curr = torch.from_numpy(eng.output("neck_trk_2", 0).reshape(-1, 256)).to(device)
         pos = torch.from_numpy(eng.output("neck_trk_pe_2", 0).reshape(-1, 256)).to(device)
         g2 = torch.Generator(device=device).manual_seed(5)
         m_total, n_ptr = cfg.num_maskmem * 4096 + cfg.max_obj_ptrs * 4, cfg.max_obj_ptrs * 4
@@ -197,10 +234,20 @@ def bench_video(s3b, local: int, rank: int, world: int, steps: int, warmup: int,
                     "mem_attn_tflops": fl / (mms / 1000.0) / 1e12,
                     "mem_attn_attention_tflops": p2["attention"]["flops"] / (p2["attention"]["ms"] / 1000.0) / 1e12
                     if p2["attention"]["ms"] > 0 else 0.0,
-                    "mem_attn_memory_tokens": m_total})
+                    "mem_attn_memory_tokens": m_total,
+                    "mem_attn_input": "frame 0 of rank 1 (peer-copied)" if recv is not None else "own frame 0"})
+        if recv is not None:
+            eng.device_free(recv)
     eng.set_stream(None)
     eng.close()
     return out
+
+
+class _CudaArray:
+    """Zero-copy view of engine-owned device memory for torch.as_tensor (the CUDA array interface)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
 
 
 def vit_flops_per_frame(cfg, with_neck=True):

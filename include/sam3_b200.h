@@ -142,6 +142,33 @@ int s3b_output_copy(s3b_ctx* ctx, const char* name, int frame, float* dst, int64
 /* Device pointer of frame `frame` of an output (valid until the next encode). */
 int s3b_output_device_ptr(s3b_ctx* ctx, const char* name, int frame, const float** dptr);
 
+/* ---------------------------------------------------------------- features to the tracking GPU */
+
+/* Copies frame `frame` of output `name` (as s3b_output_device_ptr) into
+ * device memory `dst` of GPU `dst_device`: over NVLink peer access
+ * (cudaMemcpyPeerAsync, peer access enabled on first use) when dst_device is
+ * not the context's GPU, else a device-to-device copy. dst may be another
+ * GPU's buffer of this process or a pointer from s3b_ipc_open (one process
+ * per GPU). Enqueued on the context stream after the encode that produced
+ * the output; s3b_sync(ctx) waits for it. dst_bytes must hold the frame's
+ * output. This is the hand-off of per-frame features from an encoding GPU to
+ * the tracking GPU, which the reference does through host copies of
+ * state.neck_trk (sam3_propagate_single, sam3.cpp:11378-11391). */
+int s3b_peer_copy_output(s3b_ctx* ctx, const char* name, int frame, void* dst, int dst_device, int64_t dst_bytes);
+
+/* Device memory owned by the context's GPU (cudaMalloc'd, so it has its own
+ * base address and can be shared by s3b_ipc_export), freed by
+ * s3b_device_free or with the context. */
+int s3b_device_alloc(s3b_ctx* ctx, int64_t bytes, void** dptr);
+int s3b_device_free(s3b_ctx* ctx, void* dptr);
+/* CUDA IPC for the one-process-per-GPU layout: export writes the 64-byte
+ * handle of an allocation made by s3b_device_alloc; another process opens it
+ * (its context on any GPU of the box) and gets a device pointer it can pass
+ * to s3b_peer_copy_output; close releases the mapping. */
+int s3b_ipc_export(s3b_ctx* ctx, const void* dptr, void* handle64);
+int s3b_ipc_open(s3b_ctx* ctx, const void* handle64, void** dptr);
+int s3b_ipc_close(s3b_ctx* ctx, void* dptr);
+
 /* ---------------------------------------------------------------- memory attention */
 
 /* Memory attention (sam3_build_mem_attn_graph, sam3.cpp:9224-9337) on one

@@ -57,6 +57,12 @@ SYMBOLS = [
     ("s3b_output_shape", _I, [_P, _S, ctypes.POINTER(_I64)]),
     ("s3b_output_copy", _I, [_P, _S, _I, _P, _I64]),
     ("s3b_output_device_ptr", _I, [_P, _S, _I, ctypes.POINTER(_P)]),
+    ("s3b_peer_copy_output", _I, [_P, _S, _I, _P, _I, _I64]),
+    ("s3b_device_alloc", _I, [_P, _I64, ctypes.POINTER(_P)]),
+    ("s3b_device_free", _I, [_P, _P]),
+    ("s3b_ipc_export", _I, [_P, _P, _P]),
+    ("s3b_ipc_open", _I, [_P, _P, ctypes.POINTER(_P)]),
+    ("s3b_ipc_close", _I, [_P, _P]),
     ("s3b_mem_attn", _I, [_P, _P, _P, _I, _P, _P, _I, _I, _P, _I]),
     ("s3b_op_gemm", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _I, _P, _I, _I64, _P, _I64]),
     ("s3b_op_gemm_rope", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _I, _I, _I64, _P, _I, _I64]),
@@ -266,6 +272,34 @@ class Engine:
         self._check(self._L.s3b_output_device_ptr(self.h, name.encode(), frame, ctypes.byref(p)),
                     "s3b_output_device_ptr")
         return int(p.value)
+
+    # -- per-frame features to the tracking GPU
+    def peer_copy_output(self, name: str, frame: int, dst_ptr: int, dst_device: int, dst_bytes: int):
+        self._check(self._L.s3b_peer_copy_output(self.h, name.encode(), frame, dst_ptr, dst_device, dst_bytes),
+                    "s3b_peer_copy_output")
+
+    def device_alloc(self, nbytes: int) -> int:
+        p = ctypes.c_void_p()
+        self._check(self._L.s3b_device_alloc(self.h, nbytes, ctypes.byref(p)), "s3b_device_alloc")
+        return int(p.value)
+
+    def device_free(self, ptr: int):
+        self._check(self._L.s3b_device_free(self.h, ptr), "s3b_device_free")
+
+    def ipc_export(self, ptr: int) -> bytes:
+        h = ctypes.create_string_buffer(64)
+        self._check(self._L.s3b_ipc_export(self.h, ptr, h), "s3b_ipc_export")
+        return h.raw
+
+    def ipc_open(self, handle: bytes) -> int:
+        assert len(handle) == 64
+        p = ctypes.c_void_p()
+        self._check(self._L.s3b_ipc_open(self.h, ctypes.create_string_buffer(handle, 64), ctypes.byref(p)),
+                    "s3b_ipc_open")
+        return int(p.value)
+
+    def ipc_close(self, ptr: int):
+        self._check(self._L.s3b_ipc_close(self.h, ptr), "s3b_ipc_close")
 
     # -- memory attention
     def mem_attn(self, curr, src_pos, feat: int, prompt, prompt_pos, n_ptr_tokens: int, out=None):

@@ -191,6 +191,9 @@ void s3b_destroy(s3b_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  for (void* p : ctx->ipc_mapped) cudaIpcCloseMemHandle(p);
+  ctx->ipc_mapped.clear();
+  ctx->user_allocs.clear();
   ctx->ws.clear();
   ctx->out = Outputs();
   ctx->model = Model();
@@ -413,6 +416,100 @@ int s3b_output_device_ptr(s3b_ctx* ctx, const char* name, int frame, const float
   if (r.is_pe) return set_error(ctx, kErrArg, "PE outputs are host-computed; use s3b_output_copy");
   if (frame < 0 || frame >= ctx->out.n_frames) return set_error(ctx, kErrArg, "frame out of range");
   *dptr = r.dev + (size_t)frame * r.frame_elems;
+  return kOk;
+}
+
+int s3b_peer_copy_output(s3b_ctx* ctx, const char* name, int frame, void* dst, int dst_device, int64_t dst_bytes) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!dst || dst_device < 0) return set_error(ctx, kErrArg, "bad peer copy destination");
+  OutRef r;
+  if ((rc = resolve_output(ctx, name, r))) return rc;
+  if (r.is_pe) return set_error(ctx, kErrArg, "PE outputs are host-computed; use s3b_output_copy");
+  if (frame < 0 || frame >= ctx->out.n_frames) return set_error(ctx, kErrArg, "frame out of range");
+  const size_t bytes = (size_t)r.frame_elems * sizeof(float);
+  if (dst_bytes < (int64_t)bytes) return set_error(ctx, kErrArg, "destination holds %lld bytes, need %zu",
+                                                   (long long)dst_bytes, bytes);
+  const float* src = r.dev + (size_t)frame * r.frame_elems;
+  cudaError_t e;
+  if (dst_device == ctx->device) {
+    e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, ctx->stream);
+  } else {
+    int can = 0;
+    if (cudaDeviceCanAccessPeer(&can, ctx->device, dst_device) != cudaSuccess)
+      return set_error(ctx, kErrCuda, "cudaDeviceCanAccessPeer(%d, %d)", ctx->device, dst_device);
+    if (can) {
+      const cudaError_t pe = cudaDeviceEnablePeerAccess(dst_device, 0);
+      if (pe != cudaSuccess && pe != cudaErrorPeerAccessAlreadyEnabled)
+        return set_error(ctx, kErrCuda, "cudaDeviceEnablePeerAccess(%d): %s", dst_device, cudaGetErrorString(pe));
+      cudaGetLastError();  // clears "already enabled"
+    }
+    // without peer access the driver stages the copy through host memory
+    e = cudaMemcpyPeerAsync(dst, dst_device, src, ctx->device, bytes, ctx->stream);
+  }
+  if (e != cudaSuccess) return set_error(ctx, kErrCuda, "peer copy: %s", cudaGetErrorString(e));
+  return kOk;
+}
+
+int s3b_device_alloc(s3b_ctx* ctx, int64_t bytes, void** dptr) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!dptr || bytes <= 0) return set_error(ctx, kErrArg, "bad allocation arguments");
+  auto b = std::make_shared<DevBuf>();
+  if (cudaMalloc(&b->p, (size_t)bytes) != cudaSuccess) {
+    b->p = nullptr;
+    cudaGetLastError();
+    return set_error(ctx, kErrCuda, "cudaMalloc(%lld) failed", (long long)bytes);
+  }
+  b->bytes = (size_t)bytes;
+  *dptr = b->p;
+  ctx->user_allocs[b->p] = b;
+  return kOk;
+}
+
+int s3b_device_free(s3b_ctx* ctx, void* dptr) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  auto it = ctx->user_allocs.find(dptr);
+  if (it == ctx->user_allocs.end()) return set_error(ctx, kErrArg, "not an s3b_device_alloc allocation");
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  ctx->user_allocs.erase(it);
+  return kOk;
+}
+
+int s3b_ipc_export(s3b_ctx* ctx, const void* dptr, void* handle64) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!handle64 || ctx->user_allocs.find(const_cast<void*>(dptr)) == ctx->user_allocs.end())
+    return set_error(ctx, kErrArg, "IPC export needs an s3b_device_alloc allocation");
+  cudaIpcMemHandle_t h;
+  static_assert(sizeof(h) == 64, "CUDA IPC handle size");
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(dptr)) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "cudaIpcGetMemHandle: %s", cudaGetErrorString(cudaGetLastError()));
+  memcpy(handle64, &h, sizeof(h));
+  return kOk;
+}
+
+int s3b_ipc_open(s3b_ctx* ctx, const void* handle64, void** dptr) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!handle64 || !dptr) return set_error(ctx, kErrArg, "bad IPC arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  if (cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(cudaGetLastError()));
+  ctx->ipc_mapped.insert(*dptr);
+  return kOk;
+}
+
+int s3b_ipc_close(s3b_ctx* ctx, void* dptr) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  auto it = ctx->ipc_mapped.find(dptr);
+  if (it == ctx->ipc_mapped.end()) return set_error(ctx, kErrArg, "not an s3b_ipc_open mapping");
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  cudaIpcCloseMemHandle(dptr);
+  ctx->ipc_mapped.erase(it);
   return kOk;
 }
 

@@ -12,6 +12,7 @@
 
 #include <map>
 #include <memory>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -211,6 +212,9 @@ struct s3b_ctx {
   s3b::Outputs out;
   // workspace (grown on demand, reused across calls)
   std::map<std::string, std::shared_ptr<s3b::DevBuf>> ws;
+  // s3b_device_alloc allocations and s3b_ipc_open mappings, released with the context
+  std::map<void*, std::shared_ptr<s3b::DevBuf>> user_allocs;
+  std::set<void*> ipc_mapped;
   int max_frames_per_pass = 8;
   int stop_after_blocks = -1;  // test hook: run only the first n backbone blocks (-1: all)
   int attention_impl = 0;      // 0: tcgen05 where eligible, 1: always mma.sync, 2: d = 64 on the wide tcgen05 kernel,
