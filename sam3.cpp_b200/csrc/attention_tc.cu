@@ -166,36 +166,56 @@ __device__ __forceinline__ float half_row_max(uint32_t taddr, int cbase, int kva
 // p = 2^(s*sl2 - m) over this thread's 64 keys, written as f16 into its row of
 // the 128B-swizzled P half (`prow`), returns the row sum; MASKED: padding keys
 // inside the last 32-key chunk get p = 0 (the P V product reads to its end).
+// The warp arrives on s_empty right after its last read of S (as half_row_p_tmem).
 template <bool MASKED, int NPOLY>
 __device__ __forceinline__ float half_row_p(uint32_t taddr, int cbase, int kvalid, float sl2, float m, uint8_t* prow,
-                                            int row) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                                            int row, uint64_t* s_empty) {
+  const unsigned long long sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m, -m);
+  unsigned long long acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
+  bool released = false;
 #pragma unroll
   for (int c = 0; c < kBK / 2; c += 32) {
     if (MASKED && cbase + c >= kvalid) break;
     uint32_t r[32];
     TMEM_LD32(taddr + (uint32_t)c, r);
     tc_wait_ld();
+    if (c + 32 >= kBK / 2 || (MASKED && cbase + c + 32 >= kvalid)) {  // this warp's last read of S
+      tc_fence_before();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(s_empty);
+      released = true;
+    }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       float p[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
+      for (int e = 0; e < 8; e += 2) {
         const int i = 8 * u + e;
-        const float x = fmaf(__uint_as_float(r[i]), sl2, -m);
-        p[e] = e < NPOLY ? exp2_poly3(x) : ex2(x);
-        if (MASKED) p[e] = cbase + c + i < kvalid ? p[e] : 0.f;
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2x2, negm2), x0, x1);
+        p[e] = e < NPOLY ? exp2_poly3(x0) : ex2(x0);
+        p[e + 1] = e + 1 < NPOLY ? exp2_poly3(x1) : ex2(x1);
+        if (MASKED) {
+          p[e] = cbase + c + i < kvalid ? p[e] : 0.f;
+          p[e + 1] = cbase + c + i + 1 < kvalid ? p[e + 1] : 0.f;
+        }
       }
-      s0 += p[0] + p[4];
-      s1 += p[1] + p[5];
-      s2 += p[2] + p[6];
-      s3 += p[3] + p[7];
+      acc0 = f2_add(acc0, f2_add(f2_pack(p[0], p[1]), f2_pack(p[4], p[5])));
+      acc1 = f2_add(acc1, f2_add(f2_pack(p[2], p[3]), f2_pack(p[6], p[7])));
       const int unit = (c >> 3) + u;  // 16-byte unit (8 keys) inside the 128-byte row
       *reinterpret_cast<uint4*>(prow + ((unit ^ (row & 7)) << 4)) =
           make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
     }
   }
-  return (s0 + s1) + (s2 + s3);
+  if (!released) {  // no key of this half is real: S was not read
+    tc_fence_before();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(s_empty);
+  }
+  float a0, a1, b0, b1;
+  f2_unpack(acc0, a0, a1);
+  f2_unpack(acc1, b0, b1);
+  return (a0 + a1) + (b0 + b1);
 }
 
 // As half_row_p, but P goes to TMEM (the A operand of the P V product): this thread's 64 keys as
@@ -264,17 +284,20 @@ struct TcAttnArgs {
 };
 
 // NPOLY of every 8 softmax exponentials use exp2_poly3, the rest MUFU ex2.
-template <int NPOLY, bool TMEMP>
+// PMODE (where P, the A operand of the P V product, lives): 1 TMEM (columns [192,256); its shared
+// memory goes to two more K/V slots); 0 a 128B-swizzled shared-memory operand. (Alternating the two
+// per tile, to double-buffer P, measured slower: the smaller K/V ring and the register spills cost
+// more than the wait for the previous P V that it removes.)
+template <int NPOLY, int PMODE>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm, TcAttnArgs a, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem;                          // 16 KB
-  // TMEMP: P lives in TMEM (columns [192,256)) and its 32 KB of shared memory go to two more K/V slots
-  constexpr int kSl = TMEMP ? 5 : kSlots;
+  constexpr int kSl = PMODE == 1 ? 5 : kSlots;
   uint8_t* sKV = sQ + kTileBytes;              // kSl x 16 KB
   uint8_t* sP = sKV + kSl * kTileBytes;        // 32 KB (shared-memory P only)
-  float* xmax = reinterpret_cast<float*>(sP + (TMEMP ? 0 : kPBytes));  // [2 slots][2 halves][128 rows]
+  float* xmax = reinterpret_cast<float*>(sP + (PMODE == 1 ? 0 : kPBytes));  // [2 slots][2 halves][128 rows]
   float* xsum = xmax + 4 * kBQ;                          // [2 halves][128 rows]
   uint64_t* bars = reinterpret_cast<uint64_t*>(xsum + 2 * kBQ);
   uint64_t* q_full = bars;
@@ -283,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* s_full = kv_empty + kSl;
   uint64_t* s_empty = s_full + 1;
   uint64_t* p_full = s_empty + 1;
-  uint64_t* p_empty = p_full + 1;
+  uint64_t* p_empty = p_full + 1;              // P buffer free (the previous P V has completed)
   uint64_t* o_done = p_empty + 1;
   uint64_t* mma_done = o_done + 1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -385,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (kk >= nk16) break;
           // P: two 128 x 64 K-major halves (32 B per K step inside a half); V: 16 key rows = 2048 B per K step
           const uint64_t dv = sdesc_mn_sw128(va + (uint32_t)(kk * 2048));
-          if (TMEMP) {
+          if (PMODE == 1) {
             // P from TMEM: 8 columns (16 keys as f16 pairs) per K step
             tc_mma_f16_ts(tmem + 128, tmem + 192 + (uint32_t)(kk * 8), dv, idesc_o, (j > 0 || kk != 0) ? 1u : 0u);
           } else {
@@ -444,18 +467,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       // P buffer free and O final for tile j-1 (the previous P V has completed)
       if (ok && j > 0) ok = mbar_wait(p_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc);
       ok = __all_sync(0xffffffffu, ok);
-      const bool p_pass = ok && rows_live;  // the TMEM P pass releases S itself
+      const bool p_pass = ok && rows_live;  // the P pass releases S itself
+      constexpr bool p_tmem = PMODE == 1;
       if (p_pass) {
         tc_fence_after();
-        // p = 2^(s*sl2 - m_ref), row sum, f16 P into the swizzled A operand (half hsel of sP)
-        if (TMEMP) {
+        // p = 2^(s*sl2 - m_ref), row sum, f16 P into the A operand (half hsel)
+        if (p_tmem) {
           const uint32_t p_addr = tmem + lane_off + 192 + (uint32_t)(hsel * (kBK / 4));
           l += full_tile ? half_row_p_tmem<false, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, p_addr, s_empty)
                          : half_row_p_tmem<true, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, p_addr, s_empty);
         } else {
           uint8_t* prow = sP + hsel * (kBQ * 128) + row * 128;
-          l += full_tile ? half_row_p<false, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row)
-                         : half_row_p<true, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row);
+          l += full_tile ? half_row_p<false, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row, s_empty)
+                         : half_row_p<true, NPOLY>(s_addr, cbase, kvalid, a.sl2, m_ref, prow, row, s_empty);
         }
         // the reference max moved: rescale this thread's 32 columns of the row's running O
         if (__any_sync(0xffffffffu, resc)) {
@@ -470,12 +494,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       // S read (unless already released by the P pass), P written, O rescaled: hand them to the MMA warp
-      if (TMEMP) tc_wait_st();
+      tc_wait_st();
       tc_fence_before();
-      if (!TMEMP) fence_proxy_async_smem();
+      if (!p_tmem) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        if (!(TMEMP && p_pass)) mbar_arrive(s_empty);
+        if (!p_pass) mbar_arrive(s_empty);
         mbar_arrive(p_full);
       }
     }
@@ -524,15 +548,13 @@ void* tensor_map_encoder();  // gemm.cu
 
 // q, k, v of head h of window w: base[w*ntok + n][col + h*64], one row stride for all three.
 int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v_col, int heads, int ntok, int nwin,
-                   __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int p_tmem,
+                   __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int p_mode,
                    int* err, cudaStream_t st) {
   typedef void (*KernelFn)(const CUtensorMap, TcAttnArgs, int*);
   static const KernelFn kernels[2][5] = {
-      {attn_tc_kernel<0, false>, attn_tc_kernel<1, false>, attn_tc_kernel<2, false>, attn_tc_kernel<3, false>,
-       attn_tc_kernel<4, false>},
-      {attn_tc_kernel<0, true>, attn_tc_kernel<1, true>, attn_tc_kernel<2, true>, attn_tc_kernel<3, true>,
-       attn_tc_kernel<4, true>}};
-  if (exp_poly < 0 || exp_poly > 4 || p_tmem < 0 || p_tmem > 1) return -2;
+      {attn_tc_kernel<0, 0>, attn_tc_kernel<1, 0>, attn_tc_kernel<2, 0>, attn_tc_kernel<3, 0>, attn_tc_kernel<4, 0>},
+      {attn_tc_kernel<0, 1>, attn_tc_kernel<1, 1>, attn_tc_kernel<2, 1>, attn_tc_kernel<3, 1>, attn_tc_kernel<4, 1>}};
+  if (exp_poly < 0 || exp_poly > 4 || p_mode < 0 || p_mode > 1) return -2;
   EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!enc) return -10;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16 || (q_col % 8) || (k_col % 8) || (v_col % 8) ||
@@ -558,13 +580,13 @@ int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v
   a.o_n = o_n;
   a.omap = omap;
   a.sl2 = scale * 1.4426950408889634f;
-  const size_t smem = p_tmem ? 1024 + kTileBytes * (1 + 5) + kXchgBytes + 24 * 8 + 16
-                             : 1024 + kTileBytes * (1 + kSlots) + kPBytes + kXchgBytes + 24 * 8 + 16;
+  const size_t smem = p_mode == 1 ? 1024 + kTileBytes * (1 + 5) + kXchgBytes + 24 * 8 + 16
+                                  : 1024 + kTileBytes * (1 + kSlots) + kPBytes + kXchgBytes + 24 * 8 + 16;
   static bool attr[2][5] = {};
-  const KernelFn kfn = kernels[p_tmem][exp_poly];
-  if (!attr[p_tmem][exp_poly]) {
+  const KernelFn kfn = kernels[p_mode][exp_poly];
+  if (!attr[p_mode][exp_poly]) {
     if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -13;
-    attr[p_tmem][exp_poly] = true;
+    attr[p_mode][exp_poly] = true;
   }
   const long long n_cta = (long long)((ntok + kBQ - 1) / kBQ) * nwin * heads;
   if (n_cta > 0x7fffffffLL) return -2;

@@ -119,7 +119,7 @@ int attention(const AttnParams& p, int D, int batch_heads, cudaStream_t st);
 // window w at base[(w*ntok + n)*ld + {q,k,v}_col + h*64] (one fused qkv
 // buffer), nq == nk == ntok; output rows map_row(omap, w*ntok + n).
 int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v_col, int heads, int ntok, int nwin,
-                   __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int p_tmem,
+                   __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int p_mode,
                    int* err, cudaStream_t st);
 // Tensor-core (tcgen05) flash attention for head dims d = 72, 96, 256
 // (Hiera-L, Hiera-T, memory attention): q / k / v with their own row strides
