@@ -330,12 +330,120 @@ inline int grid_for(long long n, int threads) {
 
 inline int launch_ok() { return launch_status("elementwise kernel"); }
 
+// Rows whose float4 count is not a multiple of 32 (Hiera widths 96, 144, 192, 288, 576): L lanes per
+// row (L = 4, 8 or 16, C = 4 L NV exactly), 32 / L rows per warp side by side, RI such groups per warp
+// loaded up front; the reductions are shuffles inside each L-lane group. No lane idles, and every load
+// instruction covers 32 / L contiguous 16 L-byte runs.
+template <int L, int NV, int RI>
+__global__ void __launch_bounds__(256) layernorm_sub_kernel(const float* __restrict__ x, long long ldx,
+                                                            void* __restrict__ y, int y_f32, long long ldy,
+                                                            long long rows, int C, const float* __restrict__ gamma,
+                                                            const float* __restrict__ beta, float eps, RowMap map) {
+  constexpr int G = 32 / L;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane / L, sl = lane % L;
+  const long long row0 = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * (G * RI);
+  float4 v[RI][NV];
+  long long src[RI];
+#pragma unroll
+  for (int r = 0; r < RI; ++r) {
+    const long long row = row0 + r * G + sub;
+    src[r] = row < rows ? map_row(map, row) : -2;
+    const float* xr = x + (src[r] > 0 ? src[r] : 0) * ldx;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+      v[r][i] = src[r] >= 0 ? __ldcs(reinterpret_cast<const float4*>(xr + 4 * (sl + L * i)))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mean[RI], var[RI];
+#pragma unroll
+  for (int r = 0; r < RI; ++r) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) s += (v[r][i].x + v[r][i].y) + (v[r][i].z + v[r][i].w);
+    mean[r] = s;
+  }
+#pragma unroll
+  for (int o = L / 2; o; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < RI; ++r) mean[r] += __shfl_xor_sync(0xffffffffu, mean[r], o);
+#pragma unroll
+  for (int r = 0; r < RI; ++r) {
+    mean[r] /= (float)C;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float a = v[r][i].x - mean[r], b = v[r][i].y - mean[r], c = v[r][i].z - mean[r], d = v[r][i].w - mean[r];
+      s += (a * a + b * b) + (c * c + d * d);
+    }
+    var[r] = s;
+  }
+#pragma unroll
+  for (int o = L / 2; o; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < RI; ++r) var[r] += __shfl_xor_sync(0xffffffffu, var[r], o);
+#pragma unroll
+  for (int r = 0; r < RI; ++r) {
+    if (src[r] == -2) continue;
+    const long long row = row0 + r * G + sub;
+    const float rs = rsqrtf(var[r] / (float)C + eps);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int vi = sl + L * i;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);  // padding row of a window partition: zeros
+      if (src[r] >= 0) {
+        const float4 g = *reinterpret_cast<const float4*>(gamma + 4 * vi);
+        const float4 b = beta ? *reinterpret_cast<const float4*>(beta + 4 * vi) : make_float4(0.f, 0.f, 0.f, 0.f);
+        o.x = (v[r][i].x - mean[r]) * rs * g.x + b.x;
+        o.y = (v[r][i].y - mean[r]) * rs * g.y + b.y;
+        o.z = (v[r][i].z - mean[r]) * rs * g.z + b.z;
+        o.w = (v[r][i].w - mean[r]) * rs * g.w + b.w;
+      }
+      if (y_f32) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + row * ldy + 4 * vi) = o;
+      } else {
+        __half2 h0 = __floats2half2_rn(o.x, o.y), h1 = __floats2half2_rn(o.z, o.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&h0);
+        u.y = *reinterpret_cast<uint32_t*>(&h1);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(y) + row * ldy + 4 * vi) = u;
+      }
+    }
+  }
+}
+
 }  // namespace
 
 int layernorm(const float* x, long long ldx, void* y, int y_f32, long long ldy, long long rows, int C,
               const float* gamma, const float* beta, float eps, const RowMap& map, cudaStream_t st) {
   if (C % 4 || C > 4 * 32 * kMaxVec || ldx % 4 || ldy % 4 || rows <= 0) return -1;
   const int warps = 8;
+  const int c4 = C / 4;
+  if (c4 % 32) {
+    // sub-warp rows: the largest L in {16, 8, 4} dividing C/4 with at most 12 float4 per lane
+    int L = 0;
+    for (int l = 16; l >= 4; l >>= 1)
+      if (c4 % l == 0 && c4 / l <= 12) { L = l; break; }
+    if (L) {
+      constexpr int RI = 2;
+      const long long rows_per_block = (long long)warps * (32 / L) * RI;
+      const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
+      if (blocks > 0x7fffffffLL) return -1;
+      const int nv = c4 / L;
+      bool launched = true;
+#define S3B_LNS(LL, NN)                                                                                          \
+  if (L == LL && nv == NN)                                                                                       \
+    layernorm_sub_kernel<LL, NN, RI><<<(unsigned)blocks, warps * 32, 0, st>>>(x, ldx, y, y_f32, ldy, rows, C,    \
+                                                                              gamma, beta, eps, map);            \
+  else
+      S3B_LNS(16, 1) S3B_LNS(16, 2) S3B_LNS(16, 3) S3B_LNS(16, 5) S3B_LNS(16, 6) S3B_LNS(16, 9)
+      S3B_LNS(8, 1) S3B_LNS(8, 3) S3B_LNS(8, 5) S3B_LNS(8, 7) S3B_LNS(8, 9) S3B_LNS(8, 11)
+      S3B_LNS(4, 1) S3B_LNS(4, 3) S3B_LNS(4, 5) S3B_LNS(4, 7) S3B_LNS(4, 9) S3B_LNS(4, 11)
+      launched = false;
+#undef S3B_LNS
+      if (launched) return launch_ok();
+    }
+  }
   const int nv = (C + 127) / 128;
   const int rpw = nv <= 2 ? 4 : nv == 3 ? 2 : 1;  // rows per warp
   const long long blocks = (rows + (long long)warps * rpw - 1) / ((long long)warps * rpw);

@@ -301,8 +301,12 @@ def test_attention_qkv_growing_max(engine, impl):
     assert (out.float() - ref).abs().max().item() < 3e-2
 
 
-@pytest.mark.parametrize("rows,C,f32", [(5184, 1024, 0), (1000, 96, 1), (37, 256, 0), (64, 1152, 1)])
+@pytest.mark.parametrize("rows,C,f32", [(5184, 1024, 0), (1000, 96, 1), (37, 256, 0), (64, 1152, 1), (5000, 144, 0),
+                                        (777, 192, 1), (301, 288, 0), (129, 576, 1), (65, 64, 0), (33, 80, 1),
+                                        (70001, 96, 0)])
 def test_layernorm(engine, rows, C, f32):
+    """Widths whose float4 count is a multiple of 32 run one row per warp; the others (Hiera's 96, 144,
+    192, 288, 576, ...) run L-lane row groups, several rows per warp."""
     x = torch.randn(rows, C, device="cuda") * 3 + 1
     g = torch.randn(C, device="cuda")
     b = torch.randn(C, device="cuda")
