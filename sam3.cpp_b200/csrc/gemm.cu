@@ -495,10 +495,20 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       const int n0 = (t % tiles_n) * BN;
       int cx = 0, cy = 0, cf = 0;
       if (BLK) conv_tile_origin<PAIR ? 2 : 1>(t / tiles_n, ep, rank, &cx, &cy, &cf);
+      // a column group wholly past N (the last column tile of an N that is not a multiple of BN) has
+      // nothing to store: it only takes part in the accumulator hand-over
+      const bool grp_live = n0 + grp * CG < N;
       // the first residual chunk does not depend on the accumulator: fetch it during the main loop
-      if (TMA_EPI && rip && leader) issue_resid(chunk_ctr, n0 + grp * CG, m0);
+      if (TMA_EPI && rip && leader && grp_live) issue_resid(chunk_ctr, n0 + grp * CG, m0);
       if (!mbar_wait(&tfull[acc], aphase, s_abort, err, kErrWaitTmemFull)) break;
       tc_fence_after();
+      if (!grp_live) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) release_acc(acc);
+        if (++acc == 2) { acc = 0; aphase ^= 1; }
+        continue;
+      }
       const long long gr = (long long)m0 + row;
       const int rope_pos = (ep.rope && gr < ep.rope_rows) ? (int)(gr % ep.rope_mod) : -1;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + grp * CG);
