@@ -124,6 +124,16 @@ int s3b_model_info(s3b_ctx* ctx, int32_t* info, int n);
  * (sam3.cpp:6024-6212, 5857-6018) for frames already at the model size. */
 int s3b_encode_u8(s3b_ctx* ctx, const uint8_t* frames_hwc, int n_frames, int img_size, int flags);
 
+/* Encodes n_frames uint8 HWC frames of width x height (host memory), resized
+ * on the device to the model size by the reference's bilinear (f64 weights,
+ * half-pixel centres, rounded to uint8: sam3_resize_bilinear,
+ * sam3.cpp:3441-3481) and normalised in the same pass; frames already at the
+ * model size skip the resize (sam3.cpp:3496). All frames share one size.
+ * Replaces sam3_encode_image (sam3.cpp:6024-6212, 5857-6018) for any image. */
+int s3b_encode_image_u8(s3b_ctx* ctx, const uint8_t* frames_hwc, int n_frames, int width, int height, int flags);
+int s3b_encode_image_u8_device(s3b_ctx* ctx, const uint8_t* d_frames_hwc, int n_frames, int width, int height,
+                               int flags);
+
 /* Same from preprocessed f32 CHW frames in host memory; replaces
  * sam3_encode_image_from_preprocessed (sam3.h:426-435, sam3.cpp:6997-7481). */
 int s3b_encode_chw(s3b_ctx* ctx, const float* frames_chw, int n_frames, int img_size, int flags);
@@ -217,6 +227,12 @@ int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, 
  * qkv split + permute + ggml_flash_attn_ext of sam3.cpp:3738-3774. */
 int s3b_op_attention_qkv(s3b_ctx* ctx, const void* qkv, int64_t ld, void* out, int64_t ld_out, int nwin, int heads,
                          int ntok, int d, float scale);
+
+/* Bilinear resize of uint8 HWC frames (device pointers) [n][src_h][src_w][3]
+ * -> [n][dst_h][dst_w][3]: sam3_resize_bilinear (sam3.cpp:3441-3481), f64
+ * arithmetic in the reference's order, (int)(v + 0.5) clamped to [0, 255]. */
+int s3b_op_resize_bilinear_u8(s3b_ctx* ctx, const uint8_t* src, int n_frames, int src_w, int src_h, uint8_t* dst,
+                              int dst_w, int dst_h);
 
 /* LayerNorm over C of f32 rows: out = (x-mean)/sqrt(var+eps)*g + b, f16 or
  * f32 out. Replaces ggml_norm + mul + add (sam3.cpp:1036-1060). */

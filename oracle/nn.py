@@ -163,3 +163,34 @@ def sine_pe_2d(H, W, d_model):
     pe[:, :, :half] = vy[:, None, :]
     pe[:, :, half:] = vx[None, :, :]
     return pe
+
+
+def resize_bilinear_u8(img, dst_w, dst_h):
+    """sam3_resize_bilinear (sam3.cpp:3441-3481): uint8 [H, W, 3] -> uint8 [dst_h, dst_w, 3].
+
+    Half-pixel centres (o + 0.5) * (src / dst) - 0.5 clamped at 0, the second tap clamped at
+    the last row / column, v = wy0 (wx0 p00 + wx p01) + wy (wx0 p10 + wx p11) in f64 with every
+    operation rounded on its own (numpy never fuses), then (int)(v + 0.5) clamped to [0, 255].
+    """
+    img = np.asarray(img, np.uint8)
+    H, W = img.shape[0], img.shape[1]
+
+    def taps(n_out, n_in):
+        s = np.float64(n_in) / np.float64(n_out)
+        f = (np.arange(n_out, dtype=np.float64) + 0.5) * s - 0.5
+        f = np.maximum(f, 0.0)
+        i0 = f.astype(np.int64)
+        i1 = np.where(i0 < n_in - 1, i0 + 1, i0)
+        return i0, i1, f - i0
+
+    y0, y1, wy = taps(dst_h, H)
+    x0, x1, wx = taps(dst_w, W)
+    src = img.astype(np.float64)
+    wy, wx = wy[:, None, None], wx[None, :, None]
+    wy0, wx0 = 1.0 - wy, 1.0 - wx
+    p00 = src[y0][:, x0]
+    p01 = src[y0][:, x1]
+    p10 = src[y1][:, x0]
+    p11 = src[y1][:, x1]
+    v = wy0 * (wx0 * p00 + wx * p01) + wy * (wx0 * p10 + wx * p11)
+    return np.clip((v + 0.5).astype(np.int64), 0, 255).astype(np.uint8)

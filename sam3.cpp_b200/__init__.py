@@ -54,6 +54,8 @@ SYMBOLS = [
     ("s3b_encode_chw", _I, [_P, _P, _I, _I, _I]),
     ("s3b_encode_u8_device", _I, [_P, _P, _I, _I, _I]),
     ("s3b_encode_chw_device", _I, [_P, _P, _I, _I, _I]),
+    ("s3b_encode_image_u8", _I, [_P, _P, _I, _I, _I, _I]),
+    ("s3b_encode_image_u8_device", _I, [_P, _P, _I, _I, _I, _I]),
     ("s3b_output_shape", _I, [_P, _S, ctypes.POINTER(_I64)]),
     ("s3b_output_copy", _I, [_P, _S, _I, _P, _I64]),
     ("s3b_output_device_ptr", _I, [_P, _S, _I, ctypes.POINTER(_P)]),
@@ -68,6 +70,7 @@ SYMBOLS = [
     ("s3b_op_gemm_rope", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _I, _I, _I64, _P, _I, _I64]),
     ("s3b_op_attention", _I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F]),
     ("s3b_op_attention_qkv", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _I, _F]),
+    ("s3b_op_resize_bilinear_u8", _I, [_P, _P, _I, _I, _I, _P, _I, _I]),
     ("s3b_op_layernorm", _I, [_P, _P, _P, _I, _I64, _I, _P, _P, _F]),
     ("s3b_op_conv3x3", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),
     ("s3b_op_deconv2x2", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _I, _P, _I, _I]),
@@ -242,6 +245,17 @@ class Engine:
             rc = self._L.s3b_encode_u8(self.h, frames.ctypes.data, n, S, flags)
         self._check(rc, "s3b_encode_u8")
 
+    def encode_image_u8(self, frames, flags: int = 0):
+        """frames: uint8 [n, H, W, 3] of any size, numpy (host) or torch CUDA tensor (device);
+        resized to the model size on the device unless already at it."""
+        n, H, W = int(frames.shape[0]), int(frames.shape[1]), int(frames.shape[2])
+        if hasattr(frames, "is_cuda") and frames.is_cuda:
+            rc = self._L.s3b_encode_image_u8_device(self.h, frames.data_ptr(), n, W, H, flags)
+        else:
+            frames = np.ascontiguousarray(frames, dtype=np.uint8)
+            rc = self._L.s3b_encode_image_u8(self.h, frames.ctypes.data, n, W, H, flags)
+        self._check(rc, "s3b_encode_image_u8")
+
     def encode_chw(self, frames, flags: int = 0):
         """frames: f32 [n, 3, S, S] numpy (host) or torch CUDA tensor (device)."""
         n, S = int(frames.shape[0]), int(frames.shape[2])
@@ -354,6 +368,13 @@ class Engine:
         rc = self._L.s3b_op_attention_qkv(self.h, qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), nwin,
                                           heads, ntok, d, scale)
         self._check(rc, "s3b_op_attention_qkv")
+
+    def resize_bilinear_u8(self, src, out):
+        """src uint8 CUDA [n, H, W, 3] -> out uint8 CUDA [n, H', W', 3]."""
+        n, H, W = int(src.shape[0]), int(src.shape[1]), int(src.shape[2])
+        rc = self._L.s3b_op_resize_bilinear_u8(self.h, src.data_ptr(), n, W, H, out.data_ptr(), int(out.shape[2]),
+                                               int(out.shape[1]))
+        self._check(rc, "s3b_op_resize_bilinear_u8")
 
     def layernorm(self, x, out, g, b, eps: float):
         rows, C = x.shape

@@ -138,6 +138,10 @@ int stage_host(s3b_ctx* ctx, const T* host, size_t n, const char* name, T** dev)
   return kOk;
 }
 
+// SAM 3 normalisation (p/255 - 0.5)/0.5 (sam3.cpp:3505-3511); SAM 2 ImageNet mean/std (3519-3520).
+const float kMeanSam3[3] = {0.5f, 0.5f, 0.5f}, kStdSam3[3] = {0.5f, 0.5f, 0.5f};
+const float kMeanSam2[3] = {0.485f, 0.456f, 0.406f}, kStdSam2[3] = {0.229f, 0.224f, 0.225f};
+
 int encode_device_chw(s3b_ctx* ctx, const float* d_chw, int n_frames, int img_size, int flags) {
   if (!ctx->model.loaded) return set_error(ctx, kErrState, "no model loaded");
   if (n_frames <= 0) return set_error(ctx, kErrArg, "n_frames must be > 0");
@@ -153,13 +157,29 @@ int encode_device_u8(s3b_ctx* ctx, const uint8_t* d_u8, int n_frames, int img_si
   int rc = 0;
   DevBuf* chw = ctx->buf("frames_chw", (size_t)n_frames * 3 * img_size * img_size * 4, &rc);
   if (rc) return rc;
-  static const float m3[3] = {0.5f, 0.5f, 0.5f}, s3[3] = {0.5f, 0.5f, 0.5f};
-  static const float m2[3] = {0.485f, 0.456f, 0.406f}, s2[3] = {0.229f, 0.224f, 0.225f};
   const bool sam2 = ctx->model.hp.is_sam2 != 0;
-  rc = preprocess_u8(d_u8, n_frames, img_size, img_size, sam2 ? m2 : m3, sam2 ? s2 : s3, chw->as<float>(),
-                     ctx->stream);
+  rc = preprocess_u8(d_u8, n_frames, img_size, img_size, sam2 ? kMeanSam2 : kMeanSam3, sam2 ? kStdSam2 : kStdSam3,
+                     chw->as<float>(), ctx->stream);
   if (rc) return set_error(ctx, kErrCuda, "preprocess launch failed");
   return encode_device_chw(ctx, chw->as<float>(), n_frames, img_size, flags);
+}
+
+// Frames of any size: resized on the device to the model size and normalised in the same pass
+// (sam3_preprocess_image / sam2_preprocess_image, sam3.cpp:3486-3544); frames already at the
+// model size skip the resize, as the reference does (3496).
+int encode_device_image_u8(s3b_ctx* ctx, const uint8_t* d_u8, int n_frames, int width, int height, int flags) {
+  if (!ctx->model.loaded) return set_error(ctx, kErrState, "no model loaded");
+  if (n_frames <= 0 || width <= 0 || height <= 0) return set_error(ctx, kErrArg, "bad frame count / size");
+  const int S = ctx->model.hp.img_size;
+  if (width == S && height == S) return encode_device_u8(ctx, d_u8, n_frames, S, flags);
+  int rc = 0;
+  DevBuf* chw = ctx->buf("frames_chw", (size_t)n_frames * 3 * S * S * 4, &rc);
+  if (rc) return rc;
+  const bool sam2 = ctx->model.hp.is_sam2 != 0;
+  rc = resize_bilinear_u8(d_u8, n_frames, height, width, S, S, sam2 ? kMeanSam2 : kMeanSam3,
+                          sam2 ? kStdSam2 : kStdSam3, chw->p, ctx->stream);
+  if (rc) return set_error(ctx, kErrCuda, "resize launch failed");
+  return encode_device_chw(ctx, chw->as<float>(), n_frames, S, flags);
 }
 
 }  // namespace
@@ -355,6 +375,23 @@ int s3b_encode_u8(s3b_ctx* ctx, const uint8_t* frames, int n_frames, int img_siz
   uint8_t* d = nullptr;
   if ((rc = stage_host(ctx, frames, (size_t)n_frames * img_size * img_size * 3, "frames_u8", &d))) return rc;
   return encode_device_u8(ctx, d, n_frames, img_size, flags);
+}
+
+int s3b_encode_image_u8(s3b_ctx* ctx, const uint8_t* frames, int n_frames, int width, int height, int flags) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!frames || n_frames <= 0 || width <= 0 || height <= 0) return set_error(ctx, kErrArg, "bad arguments");
+  uint8_t* d = nullptr;
+  if ((rc = stage_host(ctx, frames, (size_t)n_frames * width * height * 3, "frames_u8", &d))) return rc;
+  return encode_device_image_u8(ctx, d, n_frames, width, height, flags);
+}
+
+int s3b_encode_image_u8_device(s3b_ctx* ctx, const uint8_t* d_frames, int n_frames, int width, int height,
+                               int flags) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!d_frames) return set_error(ctx, kErrArg, "null frames");
+  return encode_device_image_u8(ctx, d_frames, n_frames, width, height, flags);
 }
 
 int s3b_encode_chw(s3b_ctx* ctx, const float* chw, int n_frames, int img_size, int flags) {
@@ -635,6 +672,17 @@ int s3b_op_attention_qkv(s3b_ctx* ctx, const void* qkv, int64_t ld, void* out, i
   p.o_n = ld_out;
   p.scale = scale;
   return run_attn(ctx, p, d, nwin * heads);
+}
+
+int s3b_op_resize_bilinear_u8(s3b_ctx* ctx, const uint8_t* src, int n_frames, int src_w, int src_h, uint8_t* dst,
+                              int dst_w, int dst_h) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!src || !dst || n_frames <= 0 || src_w <= 0 || src_h <= 0 || dst_w <= 0 || dst_h <= 0)
+    return set_error(ctx, kErrArg, "bad resize arguments");
+  rc = resize_bilinear_u8(src, n_frames, src_h, src_w, dst_h, dst_w, nullptr, nullptr, dst, ctx->stream);
+  if (rc) return set_error(ctx, kErrCuda, "resize launch failed (%d)", rc);
+  return kOk;
 }
 
 int s3b_op_layernorm(s3b_ctx* ctx, const float* x, void* out, int out_f32, int64_t rows, int C, const float* g,

@@ -250,6 +250,65 @@ __global__ void preprocess_kernel(const uint8_t* __restrict__ img, int B, int H,
   }
 }
 
+// Source taps of output index o along one axis (sam3.cpp:3449-3462): half-pixel centre
+// (o + 0.5) * s - 0.5 clamped at 0, the next tap clamped at the last index, weight of the next
+// tap = the fraction. f64 with every operation rounded on its own (no contraction), as the
+// reference's host code does.
+__device__ __forceinline__ void bilinear_taps(int o, double s, int n, int& i0, int& i1, double& w) {
+  double f = __dadd_rn(__dmul_rn(__dadd_rn((double)o, 0.5), s), -0.5);
+  if (f < 0.0) f = 0.0;
+  i0 = (int)f;
+  i1 = i0 < n - 1 ? i0 + 1 : i0;
+  w = __dadd_rn(f, -(double)i0);
+}
+
+// Bilinear resize of uint8 HWC frames [B][SH][SW][3] to [B][DH][DW] (sam3.cpp:3441-3481):
+// v = wy0 (wx0 p00 + wx p01) + wy (wx0 p10 + wx p11) in f64, then (int)(v + 0.5) clamped to
+// [0, 255]. NORM = false stores uint8 HWC; NORM = true stores the normalised f32 CHW frame
+// ((q/255 - mean)/std, sam3.cpp:3505-3511 and 3535-3541) of the rounded value q.
+template <bool NORM>
+__global__ void resize_bilinear_kernel(const uint8_t* __restrict__ src, int B, int SH, int SW, int DH, int DW,
+                                       double sy, double sx, float m0, float m1, float m2, float s0, float s1,
+                                       float s2, void* __restrict__ out) {
+  const long long plane = (long long)DH * DW;
+  const long long total = (long long)B * plane;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long b = i / plane;
+    const long long pix = i - b * plane;
+    const int y = (int)(pix / DW), x = (int)(pix - (long long)y * DW);
+    int y0, y1, x0, x1;
+    double wy, wx;
+    bilinear_taps(y, sy, SH, y0, y1, wy);
+    bilinear_taps(x, sx, SW, x0, x1, wx);
+    const double wy0 = __dadd_rn(1.0, -wy), wx0 = __dadd_rn(1.0, -wx);
+    const uint8_t* f = src + b * SH * (long long)SW * 3;
+    const uint8_t* r0 = f + (long long)y0 * SW * 3;
+    const uint8_t* r1 = f + (long long)y1 * SW * 3;
+    uint8_t q[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const double p00 = r0[x0 * 3 + c], p01 = r0[x1 * 3 + c], p10 = r1[x0 * 3 + c], p11 = r1[x1 * 3 + c];
+      const double top = __dadd_rn(__dmul_rn(wx0, p00), __dmul_rn(wx, p01));
+      const double bot = __dadd_rn(__dmul_rn(wx0, p10), __dmul_rn(wx, p11));
+      const double v = __dadd_rn(__dmul_rn(wy0, top), __dmul_rn(wy, bot));
+      int iv = (int)__dadd_rn(v, 0.5);
+      iv = iv < 0 ? 0 : (iv > 255 ? 255 : iv);
+      q[c] = (uint8_t)iv;
+    }
+    if (NORM) {
+      float* o = static_cast<float*>(out);
+      o[(b * 3 + 0) * plane + pix] = ((float)q[0] / 255.0f - m0) / s0;
+      o[(b * 3 + 1) * plane + pix] = ((float)q[1] / 255.0f - m1) / s1;
+      o[(b * 3 + 2) * plane + pix] = ((float)q[2] / 255.0f - m2) / s2;
+    } else {
+      uint8_t* o = static_cast<uint8_t*>(out) + i * 3;
+      o[0] = q[0];
+      o[1] = q[1];
+      o[2] = q[2];
+    }
+  }
+}
+
 // 4 values per thread (n4 = n / 4 float4 groups), then the n % 4 tail.
 __global__ void cast_kernel(const float* __restrict__ x, long long n, __half* __restrict__ y) {
   const long long n4 = n >> 2;
@@ -507,6 +566,20 @@ int preprocess_u8(const uint8_t* img, int B, int H, int W, const float mean[3], 
   const long long n = (long long)B * H * W;
   preprocess_kernel<<<grid_for(n, 256), 256, 0, st>>>(img, B, H, W, mean[0], mean[1], mean[2], stdv[0], stdv[1],
                                                       stdv[2], out);
+  return launch_ok();
+}
+
+int resize_bilinear_u8(const uint8_t* src, int B, int SH, int SW, int DH, int DW, const float* mean,
+                       const float* stdv, void* out, cudaStream_t st) {
+  if (B <= 0 || SH <= 0 || SW <= 0 || DH <= 0 || DW <= 0) return -1;
+  const double sy = (double)SH / DH, sx = (double)SW / DW;
+  const long long n = (long long)B * DH * DW;
+  if (mean && stdv)
+    resize_bilinear_kernel<true><<<grid_for(n, 256), 256, 0, st>>>(src, B, SH, SW, DH, DW, sy, sx, mean[0], mean[1],
+                                                                   mean[2], stdv[0], stdv[1], stdv[2], out);
+  else
+    resize_bilinear_kernel<false><<<grid_for(n, 256), 256, 0, st>>>(src, B, SH, SW, DH, DW, sy, sx, 0.f, 0.f, 0.f,
+                                                                    1.f, 1.f, 1.f, out);
   return launch_ok();
 }
 

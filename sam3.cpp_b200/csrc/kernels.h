@@ -161,6 +161,12 @@ int qpool_windows(const __half* q, long long ld, long long nwin, int ws, int C, 
 int preprocess_u8(const uint8_t* img, int B, int H, int W, const float mean[3], const float stdv[3], float* out,
                   cudaStream_t st);
 
+// Bilinear resize of uint8 HWC frames [B][SH][SW][3] to DH x DW (sam3.cpp:3441-3481: half-pixel
+// centres, f64 weights, rounded to uint8). mean / stdv null: uint8 HWC out; else the rounded
+// frame normalised to f32 CHW [B][3][DH][DW] as preprocess_u8 does.
+int resize_bilinear_u8(const uint8_t* src, int B, int SH, int SW, int DH, int DW, const float* mean,
+                       const float* stdv, void* out, cudaStream_t st);
+
 int cast_f32_f16(const float* x, long long n, __half* y, cudaStream_t st);
 int add_scaled_f32(const float* a, const float* b, float s, long long n, float* y, cudaStream_t st);
 // y = f16(a + s*b) (b may be null: y = f16(a)).
