@@ -36,6 +36,9 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 FRAMES_TOTAL = 64
+# 1: q4_0 / q8_0 linear weights stay in block form in HBM and the GEMMs dequantise them in shared
+# memory (engine option weights_quantised); 0: dequantised to f16 at load (--weights-quantised)
+WEIGHTS_QUANTISED = 0
 # measured with ncu (one --set full capture of ViT block 0): mean DRAM read+write per launch of the
 # qkv / proj / fc1 / fc2 GEMMs of a ViT block at 8 frames per pass, and their algorithmic bytes
 GEMM_TRAFFIC_BYTES = 4.696e8
@@ -95,6 +98,7 @@ def bench_hiera(s3b, local: int, rank: int, world: int, steps: int, warmup: int,
     if world > 1:
         dist.barrier()
     eng = s3b.Engine(local)
+    eng.set_option("weights_quantised", WEIGHTS_QUANTISED)
     eng.set_option("frames_per_pass", HIERA_FRAMES_PER_GPU)
     eng.load_model(path)
     n = HIERA_FRAMES_PER_GPU
@@ -147,6 +151,7 @@ def bench_video(s3b, local: int, rank: int, world: int, steps: int, warmup: int,
     if world > 1:
         dist.barrier()
     eng = s3b.Engine(local)
+    eng.set_option("weights_quantised", WEIGHTS_QUANTISED)
     eng.load_model(path)
     first, nf = rank_frames(FRAMES_TOTAL, rank)
     frames = torch.from_numpy(synth.frames_u8(nf, 1024, base_seed=1000 + first)).to(device)
@@ -364,6 +369,7 @@ def cpu_sample(workload: str, steps: int = 1):
 
 
 def main():
+    global WEIGHTS_QUANTISED
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -374,11 +380,14 @@ def main():
     ap.add_argument("--frames-per-pass", type=int, default=8)
     ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1, 2],
                     help="256-row GEMM tiles on SM pairs: 1 (default) for K >= 2048, 2 for all, 0 never")
+    ap.add_argument("--weights-quantised", type=int, default=WEIGHTS_QUANTISED, choices=[0, 1],
+                    help="1: quantised weights stay in block form in HBM, dequantised inside the GEMMs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-hiera", action="store_true", help="skip the Hiera-T (configs[1]) measurement")
     ap.add_argument("--no-video", action="store_true",
                     help="skip the Hiera-L + memory attention (configs[4]) measurement")
     args = ap.parse_args()
+    WEIGHTS_QUANTISED = args.weights_quantised
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -390,6 +399,8 @@ def main():
                 "frames_total": args.frames * n_gpus, "frames_per_gpu": args.frames,
                 "img_size": 1008,
                 "parallelism": f"frame-sharded x{n_gpus} (no collective)",
+                "weights_in_hbm": ("block form, dequantised inside the GEMMs" if args.weights_quantised
+                                   else "f16, dequantised once at load"),
                 "l2_flush": "inputs + activations per step >> 126 MB L2"}
 
     if args.impl == "reference":
@@ -434,6 +445,7 @@ def main():
     cfg = synth.SAM3_VIT_L
     gen_s = time.time() - t0
     eng = s3b.Engine(local)
+    eng.set_option("weights_quantised", WEIGHTS_QUANTISED)
     eng.set_option("frames_per_pass", args.frames_per_pass)
     eng.set_option("gemm_pairs", args.gemm_pairs)
     t0 = time.time()

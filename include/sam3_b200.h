@@ -72,6 +72,10 @@ int s3b_sync(s3b_ctx* ctx);
  * applies to every context of the process);
  * "gemm_wide_epilogue" (1, default: GEMMs with K < 2048 run 16 epilogue
  * warps instead of 8; 0: all run 8; process-wide);
+ * "weights_quantised" (read by s3b_load_model; 1: q4_0 / q8_0 linear
+ * weights stay in block form in device memory and the GEMMs dequantise each
+ * weight tile in shared memory; 0, default: they are dequantised to f16 once
+ * at load; results are identical);
  * "conv_implicit" (1, default: 3x3 convolutions with C a multiple of 64 run
  * as implicit GEMMs whose TMA loads fetch the shifted pixel blocks, no
  * column matrix, and the neck's 2x2 deconvolutions store their outputs
@@ -281,6 +285,16 @@ int s3b_op_deconv2x2(s3b_ctx* ctx, const void* x, int B, int H, int W, int Cin, 
  * No counterpart in the reference (sam3.cpp always allocates through ggml). */
 int s3b_conv3x3_noalloc(const void* x, int B, int H, int W, int C, const void* w, const float* bias, float* out,
                         int Cout, void* cuda_stream);
+
+/* As s3b_op_gemm with B given as N rows of K values in q4_0 or q8_0 blocks
+ * (device memory, ggml row layout; K a multiple of 32, N of 8): the rows are
+ * split into a block-value plane and an f16 scale plane (context workspace)
+ * and the GEMM dequantises each weight tile in shared memory, so weights are
+ * read from HBM only in block form. Results equal s3b_op_gemm on the
+ * dequantised (f16-rounded) weights. Replaces ggml_mul_mat on a quantised
+ * weight (sam3.cpp:3738, 3792-3795, 4345, 4447-4450, 9250-9324). */
+int s3b_op_gemm_q(s3b_ctx* ctx, const void* A, int64_t lda, const void* blocks, int type, int M, int N, int K,
+                  const float* bias, int act, void* out, int out_f32, int64_t ldo, const float* resid, int64_t ldr);
 
 /* Dequantises nrows rows of ne0 values of q4_0 / q4_1 / q8_0 blocks to f32,
  * bit-exactly as ggml's type-traits to_float (sam3.cpp:1076-1077). */

@@ -68,6 +68,7 @@ SYMBOLS = [
     ("s3b_mem_attn", _I, [_P, _P, _P, _I, _P, _P, _I, _I, _P, _I]),
     ("s3b_op_gemm", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _I, _P, _I, _I64, _P, _I64]),
     ("s3b_op_gemm_rope", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _I, _I, _I64, _P, _I, _I64]),
+    ("s3b_op_gemm_q", _I, [_P, _P, _I64, _P, _I, _I, _I, _I, _P, _I, _P, _I, _I64, _P, _I64]),
     ("s3b_op_attention", _I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F]),
     ("s3b_op_attention_qkv", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _I, _F]),
     ("s3b_op_resize_bilinear_u8", _I, [_P, _P, _I, _I, _I, _P, _I, _I]),
@@ -346,6 +347,16 @@ class Engine:
                                  out.data_ptr(), out_f32, out.stride(0), _ptr(resid),
                                  resid.stride(0) if resid is not None else 0)
         self._check(rc, "s3b_op_gemm")
+
+    def gemm_q(self, A, blocks, qtype: int, N: int, out, bias=None, act=ACT_NONE, resid=None):
+        """out = A B^T (+ bias, act, resid) with B as N rows of q4_0 / q8_0 blocks (a uint8 CUDA tensor of
+        N * row_size(qtype, K) bytes, ggml row layout)."""
+        M, lda, K = A.shape[0], A.stride(0), A.shape[1]
+        out_f32 = 1 if out.dtype.itemsize == 4 else 0
+        rc = self._L.s3b_op_gemm_q(self.h, A.data_ptr(), lda, blocks.data_ptr(), qtype, M, N, K, _ptr(bias), act,
+                                   out.data_ptr(), out_f32, out.stride(0), _ptr(resid),
+                                   resid.stride(0) if resid is not None else 0)
+        self._check(rc, "s3b_op_gemm_q")
 
     def gemm_rope(self, A, B, out, bias, table, rope_d: int, rope_cols: int, rope_mod: int):
         M, lda = A.shape[0], A.stride(0)

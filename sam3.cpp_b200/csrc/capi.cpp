@@ -277,6 +277,11 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     set_gemm_wide_epilogue((int)value);
     return kOk;
   }
+  if (k == "weights_quantised") {
+    if (value < 0 || value > 1) return set_error(ctx, kErrArg, "weights_quantised must be 0 or 1");
+    ctx->weights_quantised = (int)value;
+    return kOk;
+  }
   if (k == "conv_implicit") {
     if (value < 0 || value > 1) return set_error(ctx, kErrArg, "conv_implicit must be 0 or 1");
     ctx->conv_implicit = (int)value;
@@ -758,6 +763,39 @@ int s3b_op_deconv2x2(s3b_ctx* ctx, const void* x, int B, int H, int W, int Cin, 
   ep.map.H = H;
   rc = gemm_f16(xh, Cin, wh, Cin, B * H * W, 4 * Cout, Cin, ep, ctx->d_err, ctx->stream);
   if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "deconv2x2 gemm launch failed (%d)", rc);
+  return kOk;
+}
+
+int s3b_op_gemm_q(s3b_ctx* ctx, const void* A, int64_t lda, const void* blocks, int type, int M, int N, int K,
+                  const float* bias, int act, void* out, int out_f32, int64_t ldo, const float* resid, int64_t ldr) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!A || !blocks || !out || M <= 0 || N <= 0 || K <= 0) return set_error(ctx, kErrArg, "bad gemm_q arguments");
+  if (type != QT_Q4_0 && type != QT_Q8_0) return set_error(ctx, kErrUnsupported, "gemm_q takes q4_0 or q8_0 rows");
+  if (K % 32 || N % 8) return set_error(ctx, kErrArg, "gemm_q needs K %% 32 == 0 and N %% 8 == 0");
+  // the rows are split into the value and scale planes in context workspaces, then multiplied
+  const size_t vbytes = (size_t)N * (type == QT_Q4_0 ? K / 2 : K);
+  DevBuf* qv = ctx->buf("gemm_q_values", vbytes, &rc);
+  if (rc) return rc;
+  DevBuf* qs = ctx->buf("gemm_q_scales", (size_t)N * (K / 32) * 2, &rc);
+  if (rc) return rc;
+  rc = repack_q_rows(blocks, type, N, K, qv->p, qs->as<__half>(), ctx->stream);
+  if (rc) return set_error(ctx, kErrArg, "gemm_q repack launch failed (%d)", rc);
+  EpiParams ep;
+  ep.mode = EPI_STORE;
+  ep.act = act;
+  ep.bias = bias;
+  ep.out = out;
+  ep.out_f32 = out_f32;
+  ep.ldo = ldo;
+  ep.resid = resid;
+  ep.ldr = ldr;
+  QWeight w;
+  w.type = type;
+  w.values = qv->p;
+  w.scales = qs->as<__half>();
+  rc = gemm_q(reinterpret_cast<const __half*>(A), lda, w, M, N, K, ep, ctx->d_err, ctx->stream);
+  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "gemm_q launch failed (%d)", rc);
   return kOk;
 }
 

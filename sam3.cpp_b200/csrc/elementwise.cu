@@ -610,6 +610,51 @@ long long qtype_row_bytes(int qtype, long long ne0) {
   }
 }
 
+// One thread per 32-value block of row n: the f16 scale goes to scales[blk][n]; q4_0 values to
+// 16 bytes of the nibble plane row n, as 4 words of 8 values each (value 2p of a word in nibble p,
+// value 2p + 1 in nibble p + 4); q8_0 values to 32 bytes of the int8 plane row n, in order.
+__global__ void repack_q_kernel(const uint8_t* __restrict__ src, int qtype, int N, int K, long long row_bytes,
+                                uint8_t* __restrict__ values, uint16_t* __restrict__ scales) {
+  const int nb = K / 32;
+  const long long total = (long long)nb * N;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(i / nb), blk = (int)(i - (long long)n * nb);
+    const uint8_t* p = src + n * row_bytes + (long long)blk * (qtype == QT_Q4_0 ? 18 : 34);
+    scales[(long long)blk * N + n] = (uint16_t)(p[0] | (p[1] << 8));
+    if (qtype == QT_Q4_0) {
+      uint8_t q[32];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        q[j] = p[2 + j] & 0x0F;
+        q[j + 16] = p[2 + j] >> 4;
+      }
+      uint32_t* o = reinterpret_cast<uint32_t*>(values + (long long)n * (K / 2) + blk * 16);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp)
+          w |= ((uint32_t)q[8 * g + 2 * pp] << (4 * pp)) | ((uint32_t)q[8 * g + 2 * pp + 1] << (16 + 4 * pp));
+        o[g] = w;
+      }
+    } else {
+      uint8_t* o = values + (long long)n * K + blk * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) o[j] = p[2 + j];
+    }
+  }
+}
+
+int repack_q_rows(const void* src, int qtype, int N, int K, void* values, __half* scales, cudaStream_t st) {
+  if (qtype != QT_Q4_0 && qtype != QT_Q8_0) return -1;
+  if (K % 32 || N <= 0 || K <= 0) return -2;
+  const long long n = (long long)(K / 32) * N;
+  repack_q_kernel<<<grid_for(n, 128), 128, 0, st>>>(reinterpret_cast<const uint8_t*>(src), qtype, N, K,
+                                                    qtype_row_bytes(qtype, K), reinterpret_cast<uint8_t*>(values),
+                                                    reinterpret_cast<uint16_t*>(scales));
+  return launch_ok();
+}
+
 int dequant_rows(const void* src, int qtype, long long ne0, long long nrows, void* dst, int dst_f32,
                  long long ld_dst, cudaStream_t st) {
   if (qtype != QT_Q4_0 && qtype != QT_Q4_1 && qtype != QT_Q8_0) return -1;

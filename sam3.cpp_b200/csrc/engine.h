@@ -117,12 +117,18 @@ struct DevBuf {
 
 // A linear weight prepared for the tensor-core GEMM: B operand [N][Kpad] f16
 // (K-major), plus the bias and, for quantised files, the raw blocks.
+// With the context option weights_quantised, a q4_0 / q8_0 weight keeps its block form on the
+// device instead (qtype != 0, w null): value plane qv and f16 scale plane qs in the QWeight
+// layout, dequantised inside the GEMM.
 struct Linear {
   int N = 0, K = 0, Kpad = 0;
   int file_dtype = 0;
   std::shared_ptr<DevBuf> w;     // f16 [N][Kpad]
   std::shared_ptr<DevBuf> b;     // f32 [N] (may be null)
   std::shared_ptr<DevBuf> raw;   // raw quantised rows as in the file (q4_0/q4_1/q8_0), else null
+  int qtype = 0;                 // QT_Q4_0 / QT_Q8_0 when the weight is kept in block form
+  std::shared_ptr<DevBuf> qv;    // q4_0 nibble plane [N][K/2] or q8_0 int8 plane [N][K]
+  std::shared_ptr<DevBuf> qs;    // f16 block scales [K/32][N]
 };
 
 struct Vec {
@@ -219,6 +225,7 @@ struct s3b_ctx {
   int stop_after_blocks = -1;  // test hook: run only the first n backbone blocks (-1: all)
   int attention_impl = 0;      // 0: tcgen05 where eligible, 1: always mma.sync, 2: d = 64 on the wide tcgen05 kernel,
                                // 3: as 0, d = 64 with P in shared memory
+  int weights_quantised = 0;   // q4_0 / q8_0 linear weights stay in block form, dequantised inside the GEMM
   int conv_implicit = 1;       // pixel-block GEMMs: implicit 3x3 convs, TMA-stored deconvs (0: im2col / scatter)
   int attention_exp_poly = 0;  // of every 8 softmax exponentials in the tcgen05 kernel, how many use the FMA pipe
   // launch accounting + optional per-kernel CUDA-event timing (s3b_profile_*)

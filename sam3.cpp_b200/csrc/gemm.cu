@@ -38,7 +38,10 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 // threads of a CTA with `ew` epilogue warps (plus the TMA and MMA warps)
-constexpr int gemm_threads(int ew) { return 64 + 32 * ew; }
+constexpr int gemm_threads(int ew, int dw = 0) { return 64 + 32 * (ew + dw); }
+// QB (quantised B operand): warps that dequantise each stage's weight tile (4 beside 16 epilogue
+// warps, 8 beside 8)
+constexpr int dequant_warps(int ew) { return ew >= 16 ? 4 : 8; }
 constexpr uint32_t kStageBufBytes = 16384;  // 128 rows x 128 B
 
 int g_gemm_pairs = 1;         // 256-row tiles on SM pairs: 0 never, 1 long-K GEMMs, 2 every wide GEMM
@@ -50,6 +53,51 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// ---- quantised B operand (QB 1: q4_0, QB 2: q8_0), dequantised in shared memory
+// A value v = q * d (q8_0) or (q - 8) * d (q4_0) with d the f16 block scale: the
+// integer becomes an exact f16 through the 0x6400 exponent trick (0x6400 | u is
+// 1024 + u for u < 1024), the offset is subtracted exactly, and one rounded f16
+// multiply by d gives round_f16(q * d), the value the load-time dequantisation
+// (f32 product, then f16 rounding) produces: the product of two f16 values is
+// exact in f32, so both round the same real number once.
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t byte_perm(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+// q4_0 plane word (8 values of one row): nibble p (bits 4p) holds value 2p and
+// nibble p + 4 (bits 16 + 4p) value 2p + 1, so pair p is (w >> 4p) & 0x000F000F.
+__device__ __forceinline__ uint4 dequant8_q4(uint32_t w, uint32_t d2) {
+  const uint32_t off = 0x64086408u;  // 1032 = 1024 + 8
+  uint4 o;
+  o.x = h2_mul(h2_sub((w & 0x000F000Fu) | 0x64006400u, off), d2);
+  o.y = h2_mul(h2_sub(((w >> 4) & 0x000F000Fu) | 0x64006400u, off), d2);
+  o.z = h2_mul(h2_sub(((w >> 8) & 0x000F000Fu) | 0x64006400u, off), d2);
+  o.w = h2_mul(h2_sub(((w >> 12) & 0x000F000Fu) | 0x64006400u, off), d2);
+  return o;
+}
+// q8_0: 8 int8 values in two words; q ^ 0x80 = q + 128 in [0, 255].
+__device__ __forceinline__ uint4 dequant8_q8(uint2 w, uint32_t d2) {
+  const uint32_t off = 0x64806480u;  // 1152 = 1024 + 128
+  const uint32_t u0 = w.x ^ 0x80808080u, u1 = w.y ^ 0x80808080u;
+  uint4 o;
+  o.x = h2_mul(h2_sub(byte_perm(u0, 0x64u, 0x4140u), off), d2);
+  o.y = h2_mul(h2_sub(byte_perm(u0, 0x64u, 0x4342u), off), d2);
+  o.z = h2_mul(h2_sub(byte_perm(u1, 0x64u, 0x4140u), off), d2);
+  o.w = h2_mul(h2_sub(byte_perm(u1, 0x64u, 0x4342u), off), d2);
+  return o;
 }
 
 // All loops over the 16 values below are fully unrolled with compile-time
@@ -278,11 +326,23 @@ __device__ __forceinline__ void conv_tile_origin(int mt, const EpiParams& ep, ui
   *y0 = ty * 8 * CONV_TY_BLOCKS + (int)rank * 8;
 }
 
-template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW, int BLK = 0>
-__global__ void __launch_bounds__(gemm_threads(EW), 1)
+// QB (quantised weights; 0: f16 B via TMA): the weight tile of a k-step arrives as
+// block values (QB 1, q4_0: 32 bytes of nibbles per row; QB 2, q8_0: 64 int8 per
+// row; tmB over the value plane) plus the two f16 block scales of each row (tmS
+// over the [K/32][N] scale plane) in one of QS landing buffers (a ring of its own,
+// `qfull` / `qempty`, filled by lane 1 of the producer warp up to QS k-steps ahead,
+// so that the load latency stays off the stage ring). The dequant_warps(EW) warps
+// after the epilogue warps wait for the stage's B buffer to be free (`empty`) and
+// for the landing buffer, write the f16 tile into the B buffer in the SW128 layout
+// the TMA would have produced, fence it for the async proxy, release the landing
+// buffer and arrive on `full` (with pairs: on the leader's `full`, whose count then
+// includes both CTAs' dequantising warps).
+template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW, int BLK = 0, int QB = 0, int QS = 0>
+__global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 1)
     gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M,
-                       int N, int K, EpiParams ep, int resid_in_place, int* err) {
+                       const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
+                       const __grid_constant__ CUtensorMap tmS, int M, int N, int K, EpiParams ep,
+                       int resid_in_place, int* err) {
   constexpr int BN_CTA = PAIR ? BN / 2 : BN;  // rows of B this CTA loads per stage
   constexpr int TM = PAIR ? 2 * kBM : kBM;    // output rows per tile
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
@@ -290,8 +350,14 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = 2 * BN;
   constexpr uint32_t STAGING = TMA_EPI ? 4 * kStageBufBytes : 0;
+  constexpr int DW = QB ? dequant_warps(EW) : 0;
+  constexpr uint32_t QROW = QB == 1 ? 32 : 64;              // value bytes per weight row per stage
+  constexpr uint32_t QV_BYTES = QB ? BN_CTA * QROW : 0;     // block values of the stage
+  constexpr uint32_t Q_BYTES = QB ? QV_BYTES + 4 * BN_CTA : 0;  // + 2 f16 scales per row
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(BLK == 0 || TMA_EPI, "pixel-block tiles store through TMA");
+  static_assert(QB == 0 || BLK == 0, "quantised weights: plain GEMMs only");
+  static_assert((QB == 0) == (QS == 0), "landing buffers exactly for quantised weights");
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512 || TMEM_COLS == 128, "TMEM columns must be a power of 2");
 
   extern __shared__ uint8_t smem_raw[];
@@ -299,13 +365,16 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sC = sB + STAGES * B_BYTES;  // staging (TMA epilogue only), 1024-aligned
-  uint64_t* full = reinterpret_cast<uint64_t*>(sC + STAGING);
+  uint8_t* sQ = sC + STAGING;           // QB landing buffers, 512-byte multiples
+  uint64_t* full = reinterpret_cast<uint64_t*>(sQ + QS * Q_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* mma_done = tempty + 2;
   uint64_t* rfull = mma_done + 1;  // [half*2 + buf]: residual chunk landed in its staging buffer
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(rfull + 4);
+  uint64_t* qfull = rfull + 4;     // [QS] (QB): a k-step's block values and scales landed
+  uint64_t* qempty = qfull + QS;   // [QS] (QB): the dequantising warps have read the landing buffer
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(qempty + QS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -320,8 +389,13 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      // QB: the producer's arrive (A bytes) + one arrive per dequantising warp (of both CTAs with pairs)
+      mbar_init(&full[s], QB ? 1 + (PAIR ? 2 : 1) * DW : 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < QS; ++s) {
+      mbar_init(&qfull[s], 1);
+      mbar_init(&qempty[s], DW);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
@@ -334,6 +408,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
     fence_proxy_async_smem();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (QB) tma_prefetch_desc(&tmS);
     if (TMA_EPI) tma_prefetch_desc(&tmC);
     if (TMA_EPI && resid_in_place) tma_prefetch_desc(&tmR);
   }
@@ -372,7 +447,17 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
           const int tap = BLK == 1 ? kb / cbn : 4;
           const int cb = BLK == 1 ? kb - tap * cbn : kb;
           const int ky = tap / 3, kx = tap - 3 * (tap / 3);
-          if (PAIR) {
+          if (QB) {
+            // A as usual (the weight tile comes through the landing ring, lane 1)
+            if (PAIR) {
+              const uint32_t fb = cluster_addr(smem_u32(&full[stage]), 0);
+              if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * A_BYTES);
+              tma_load_2d_pair(&tmA, fb, sA + stage * A_BYTES, kb * kBK, m0);
+            } else {
+              mbar_arrive_expect_tx(&full[stage], A_BYTES);
+              tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, m0);
+            }
+          } else if (PAIR) {
             // both CTAs' bytes complete the leader's barrier; only the leader arms it
             const uint32_t fb = cluster_addr(smem_u32(&full[stage]), 0);
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
@@ -400,6 +485,27 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       // CTA's `empty` barriers land before exit).
       for (int s = 0; s < STAGES; ++s)
         if (armed & (1u << s)) mbar_wait_drain(PAIR ? &empty[s] : &full[s], (armed_phase >> s) & 1u, err);
+    } else if (QB && lane == 1) {
+      // landing ring: the block values and scales of every k-step of this CTA's half of the weight
+      // tile, up to QS k-steps ahead of the dequantising warps
+      int qi = 0;
+      uint32_t qph = 0;
+      uint32_t armed = 0, armed_phase = 0;
+      bool ok = true;
+      for (int t = unit; t < n_tiles && ok; t += n_units) {
+        const int n0 = (t % tiles_n) * BN + (int)rank * BN_CTA;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&qempty[qi], qph ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&qfull[qi], Q_BYTES);
+          tma_load_2d(&tmB, &qfull[qi], sQ + qi * Q_BYTES, kb * (int)QROW, n0);
+          tma_load_2d(&tmS, &qfull[qi], sQ + qi * Q_BYTES + QV_BYTES, n0, kb * 2);
+          armed |= 1u << qi;
+          armed_phase = (armed_phase & ~(1u << qi)) | (qph << qi);
+          if (++qi == QS) { qi = 0; qph ^= 1; }
+        }
+      }
+      for (int s = 0; s < QS; ++s)
+        if (armed & (1u << s)) mbar_wait_drain(&qfull[s], (armed_phase >> s) & 1u, err);
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
@@ -415,7 +521,11 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&full[stage], phase, s_abort, err, kErrWaitFull)) { ok = false; break; }
+          if (!((QB && PAIR) ? mbar_wait_cluster(&full[stage], phase, s_abort, err, kErrWaitFull)
+                             : mbar_wait(&full[stage], phase, s_abort, err, kErrWaitFull))) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint64_t da = sdesc_k_sw128(smem_u32(sA + stage * A_BYTES));
           const uint64_t db = sdesc_k_sw128(smem_u32(sB + stage * B_BYTES));
@@ -438,6 +548,67 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       if (issued) {
         if (PAIR) tc_commit_pair(mma_done, 1); else tc_commit(mma_done);
         mbar_wait_drain(mma_done, 0, err);
+      }
+    }
+  } else if (QB && warp >= 2 + EW) {
+    // Dequantising warps. Unit u = (row u >> 1, block u & 1) of the stage: one 32-value block of a
+    // weight row (16 nibble bytes or 32 int8, one scale) -> four 16-byte chunks of the SW128 row.
+    // A warp's 32 units are 16 consecutive rows: its block loads cover 512 contiguous bytes and its
+    // chunk stores 4 distinct 16-byte positions per bank group, both conflict-free.
+    constexpr int UNITS = 2 * BN_CTA;
+    constexpr int DT = (DW > 0 ? DW : 1) * 32;
+    static_assert(UNITS % DT == 0, "units per dequantising thread");
+    const int dt = (int)threadIdx.x - 32 * (2 + EW);
+    const uint32_t full_leader = PAIR ? cluster_addr(smem_u32(&full[0]), 0) : 0u;
+    int stage = 0, qi = 0;
+    uint32_t phase = 0, qph = 0;
+    bool ok = true;
+    for (int t = unit; t < n_tiles && ok; t += n_units) {
+      for (int kb = 0; kb < nk; ++kb) {
+        // the stage's B buffer is free (its last MMAs completed) and the k-step's blocks landed
+        if (!mbar_wait(&empty[stage], phase ^ 1, s_abort, err, kErrWaitEmpty) ||
+            !mbar_wait(&qfull[qi], qph, s_abort, err, kErrWaitMisc)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* qv = sQ + qi * Q_BYTES;
+        const uint16_t* qs = reinterpret_cast<const uint16_t*>(qv + QV_BYTES);
+        uint8_t* sb = sB + stage * B_BYTES;
+#pragma unroll
+        for (int u = dt; u < UNITS; u += DT) {
+          const int r = u >> 1, b = u & 1;
+          const uint32_t d = qs[b * BN_CTA + r];
+          const uint32_t d2 = d | (d << 16);
+          uint4 o[4];
+          if (QB == 1) {
+            const uint4 w = *reinterpret_cast<const uint4*>(qv + r * 32 + b * 16);
+            o[0] = dequant8_q4(w.x, d2);
+            o[1] = dequant8_q4(w.y, d2);
+            o[2] = dequant8_q4(w.z, d2);
+            o[3] = dequant8_q4(w.w, d2);
+          } else {
+            const uint4 w0 = *reinterpret_cast<const uint4*>(qv + r * 64 + b * 32);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(qv + r * 64 + b * 32 + 16);
+            o[0] = dequant8_q8(make_uint2(w0.x, w0.y), d2);
+            o[1] = dequant8_q8(make_uint2(w0.z, w0.w), d2);
+            o[2] = dequant8_q8(make_uint2(w1.x, w1.y), d2);
+            o[3] = dequant8_q8(make_uint2(w1.z, w1.w), d2);
+          }
+          uint8_t* row = sb + r * 128;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(row + (((4 * b + j) ^ (r & 7)) << 4)) = o[j];
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&qempty[qi]);
+          if (PAIR)
+            mbar_arrive_cluster(full_leader + (uint32_t)(stage * 8));
+          else
+            mbar_arrive(&full[stage]);
+        }
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (++qi == QS) { qi = 0; qph ^= 1; }
       }
     }
   } else {
@@ -715,17 +886,48 @@ int make_map_deconv_out(CUtensorMap* map, const void* base, int F, int H, int W,
   return r == CUDA_SUCCESS ? 0 : -12;
 }
 
+// Unswizzled 2-D tensor map over a row-major [rows][cols] matrix of `dtype` (row stride ld elements),
+// box = box_cols x box_rows: the quantised weight planes of QB GEMMs.
+int make_map_plain_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, long long rows,
+                      long long cols, long long ld, int box_cols, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return -10;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * elem_bytes) % 16 != 0 ||
+      (box_cols * elem_bytes) % 16 != 0)
+    return -11;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * elem_bytes)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -12;
+}
+
 // BLK 1 / 2: A is the channel-last input map (geometry in ep.conv_*) of gemm_conv3x3 /
 // gemm_deconv2x2 and M the number of pixel-block tiles x the tile rows.
-template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW = 8, int BLK = 0>
-int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
-                const EpiParams& ep, int resid_in_place, int* err, cudaStream_t st) {
+// QB 1 / 2: B is the q4_0 nibble plane [N][K/2] / q8_0 value plane [N][K] (ldb unused) and
+// scales the f16 block-scale plane [K/32][N].
+template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW = 8, int BLK = 0, int QB = 0, int QS = 0>
+int launch_gemm(const __half* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                const EpiParams& ep, int resid_in_place, int* err, cudaStream_t st,
+                const __half* scales = nullptr) {
   constexpr int BN_CTA = PAIR ? BN / 2 : BN;
-  CUtensorMap ma, mb, mc, mr;
+  constexpr int DW = QB ? dequant_warps(EW) : 0;
+  constexpr int QROW = QB == 1 ? 32 : 64;
+  CUtensorMap ma, mb, mc, mr, ms;
   int rc = BLK ? make_map_conv(&ma, A, ep.conv_F, ep.conv_H, ep.conv_W, ep.conv_C, 2)
                : make_map_2d(&ma, A, M, K, lda, kBM, 2);
   if (rc) return rc;
-  rc = make_map_2d(&mb, B, N, K, ldb, BN_CTA, 2);
+  if (QB) {
+    const long long row_bytes = QB == 1 ? K / 2 : K;
+    rc = make_map_plain_2d(&mb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, row_bytes, row_bytes, QROW, BN_CTA);
+    if (rc) return rc;
+    rc = make_map_plain_2d(&ms, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K / 32, N, N, BN_CTA, 2);
+  } else {
+    rc = make_map_2d(&mb, B, N, K, ldb, BN_CTA, 2);
+    ms = mb;  // unused
+  }
   if (rc) return rc;
   if (TMA_EPI) {
     const int eb = ep.out_f32 ? 4 : 2;
@@ -743,11 +945,12 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
   } else {
     mr = mc;
   }
-  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN_CTA) * kBK * 2 + (TMA_EPI ? 4 * kStageBufBytes : 0) +
-                          (2 * STAGES + 9) * 8 + 16;
+  constexpr size_t q_bytes = QB ? (size_t)BN_CTA * QROW + 4 * BN_CTA : 0;
+  constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN_CTA) * kBK * 2 + (size_t)QS * q_bytes +
+                          (TMA_EPI ? 4 * kStageBufBytes : 0) + (2 * STAGES + 2 * QS + 9) * 8 + 16;
   static_assert(smem <= 232448, "shared memory per CTA");
-  auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR, EW, BLK>;
-  constexpr int kThreads = gemm_threads(EW);
+  auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR, EW, BLK, QB, QS>;
+  constexpr int kThreads = gemm_threads(EW, DW);
   static bool attr_set = false;
   static int max_units = 0;  // co-resident CTAs (or pairs)
   if (!attr_set) {
@@ -776,7 +979,7 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
   const int tiles = ((M + tm - 1) / tm) * ((N + BN - 1) / BN);
   const int units = tiles < max_units ? tiles : max_units;
   if (!PAIR) {
-    kernel<<<units, kThreads, smem, st>>>(ma, mb, mc, mr, M, N, K, ep, resid_in_place, err);
+    kernel<<<units, kThreads, smem, st>>>(ma, mb, mc, mr, ms, M, N, K, ep, resid_in_place, err);
     return launch_status("gemm");
   }
   cudaLaunchConfig_t cfg = {};
@@ -791,7 +994,7 @@ int launch_gemm(const __half* A, long long lda, const __half* B, long long ldb, 
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, mr, M, N, K, ep, resid_in_place, err);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, mr, ms, M, N, K, ep, resid_in_place, err);
   if (e != cudaSuccess) {
     fprintf(stderr, "s3b: CUDA error at gemm (pair) launch: %s (%d)\n", cudaGetErrorString(e), (int)e);
     cudaGetLastError();
@@ -822,10 +1025,9 @@ int num_sms() {
   return n;
 }
 
-int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
-             const EpiParams& ep, int* err, cudaStream_t st) {
-  if (M <= 0 || N <= 0 || K <= 0) return -1;
-  if (lda < K || ldb < K) return -2;
+// Checks the epilogue parameters of a plain GEMM and decides whether its output leaves through the
+// TMA epilogue (and whether that epilogue adds the residual in place). Returns 0 or a negative code.
+static int route_epilogue(const EpiParams& ep, int N, bool* tma_epi_out, int* rip_out) {
   if (ep.mode == EPI_DECONV2 && (ep.cout <= 0 || N != 4 * ep.cout)) return -3;
   if (ep.mode != EPI_STORE && ep.mode != EPI_DECONV2) return -3;
   if (ep.rope && (ep.rope_D <= 0 || (ep.rope_D & 1) || ep.rope_mod <= 0)) return -3;
@@ -843,7 +1045,19 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
                   : (ep.resid_mod == 0 && ep.ldr == ep.ldo)));
   const bool tma_epi = ep.mode == EPI_STORE && ep.map.kind == 0 && resid_ok &&
                        (reinterpret_cast<uintptr_t>(ep.out) & 15) == 0 && (ep.ldo * eb) % 16 == 0 && ep.ldo >= N;
-  const int resid_in_place = (tma_epi && ep.resid) ? 1 : 0;
+  *tma_epi_out = tma_epi;
+  *rip_out = (tma_epi && ep.resid) ? 1 : 0;
+  return 0;
+}
+
+int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int M, int N, int K,
+             const EpiParams& ep, int* err, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || K <= 0) return -1;
+  if (lda < K || ldb < K) return -2;
+  bool tma_epi = false;
+  int resid_in_place = 0;
+  const int rc = route_epilogue(ep, N, &tma_epi, &resid_in_place);
+  if (rc) return rc;
   if (tma_epi) {
     if (N <= 128) return launch_gemm<128, 4, true, false>(A, lda, B, ldb, M, N, K, ep, resid_in_place, err, st);
     // short-K GEMMs (QKV + RoPE, MLP fc1 + GELU, attention proj + residual): their epilogue outlasts
@@ -864,6 +1078,38 @@ int gemm_f16(const __half* A, long long lda, const __half* B, long long ldb, int
   }
   if (N <= 128) return launch_gemm<128, 6, false, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
   return launch_gemm<256, 4, false, false>(A, lda, B, ldb, M, N, K, ep, 0, err, st);
+}
+
+template <int QB>
+static int gemm_q_launch(const __half* A, long long lda, const QWeight& w, int M, int N, int K, const EpiParams& ep,
+                         bool tma_epi, int rip, int* err, cudaStream_t st) {
+  // 4 stages of A / f16 B and as many landing buffers as fit beside them (6 for q4_0, 3 for q8_0);
+  // the direct-store variant (no staging buffers, 256 B rows per CTA) 3 stages and 6 / 4 buffers
+  constexpr int QSP = QB == 1 ? 6 : 3;
+  constexpr int QSD = QB == 1 ? 6 : 4;
+  if (tma_epi) {
+    // 256-row tiles on SM pairs (each CTA dequantises half of the weight tile); 16 epilogue warps for
+    // the short-K GEMMs, as for f16 weights
+    if (K < 2048 && g_gemm_wide_epi)
+      return launch_gemm<256, 4, true, true, 16, 0, QB, QSP>(A, lda, w.values, 0, M, N, K, ep, rip, err, st,
+                                                            w.scales);
+    return launch_gemm<256, 4, true, true, 8, 0, QB, QSP>(A, lda, w.values, 0, M, N, K, ep, rip, err, st, w.scales);
+  }
+  return launch_gemm<256, 3, false, false, 8, 0, QB, QSD>(A, lda, w.values, 0, M, N, K, ep, 0, err, st, w.scales);
+}
+
+int gemm_q(const __half* A, long long lda, const QWeight& w, int M, int N, int K, const EpiParams& ep, int* err,
+           cudaStream_t st) {
+  if (M <= 0 || N <= 0 || K <= 0) return -1;
+  if (lda < K || K % 32 || N % 8 || !w.values || !w.scales) return -2;
+  if ((reinterpret_cast<uintptr_t>(w.values) & 15) || (reinterpret_cast<uintptr_t>(w.scales) & 15)) return -2;
+  bool tma_epi = false;
+  int rip = 0;
+  const int rc = route_epilogue(ep, N, &tma_epi, &rip);
+  if (rc) return rc;
+  if (w.type == QT_Q4_0) return gemm_q_launch<1>(A, lda, w, M, N, K, ep, tma_epi, rip, err, st);
+  if (w.type == QT_Q8_0) return gemm_q_launch<2>(A, lda, w, M, N, K, ep, tma_epi, rip, err, st);
+  return -2;
 }
 
 int gemm_conv3x3(const __half* x, int F, int H, int W, int C, const __half* Bw, long long ldb, int N,

@@ -180,6 +180,23 @@ long long qtype_row_bytes(int qtype, long long ne0);
 int dequant_rows(const void* src, int qtype, long long ne0, long long nrows, void* dst, int dst_f32,
                  long long ld_dst, cudaStream_t st);
 
+// A q4_0 / q8_0 weight [N][K] kept in block form for the GEMM (K a multiple of 32, N of 8):
+// values = q4_0 nibble plane [N][K/2] (per 8 values one 32-bit word, value 2p in nibble p and value
+// 2p + 1 in nibble p + 4) or q8_0 int8 plane [N][K]; scales = f16 block scales [K/32][N].
+struct QWeight {
+  int type = QT_F16;
+  const void* values = nullptr;
+  const __half* scales = nullptr;
+};
+// ggml rows of q4_0 / q8_0 blocks [N][row_bytes(K)] -> the QWeight planes (bytes: N*K/2 or N*K
+// values, 2*N*K/32 scales).
+int repack_q_rows(const void* src, int qtype, int N, int K, void* values, __half* scales, cudaStream_t st);
+// C[M,N] = A[M,K] B[N,K]^T with B in block form, dequantised inside the GEMM (its shared-memory
+// stages receive the block values and scales and dequantising warps write the f16 tile the
+// tensor cores read); same epilogues and results as gemm_f16 on the dequantised weight.
+int gemm_q(const __half* A, long long lda, const QWeight& w, int M, int N, int K, const EpiParams& ep, int* err,
+           cudaStream_t st);
+
 // Returns the number of SMs of the current device (cached).
 int num_sms();
 

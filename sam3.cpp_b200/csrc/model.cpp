@@ -280,14 +280,38 @@ int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Lin
   for (int i = 0; i < k_dims && i < 4; ++i) K64 *= t.ne[i];
   const int K = (int)K64;
   const int N = (int)(t.nelements() / K64);
-  std::vector<float> w;
-  tensor_to_f32(t, w);
-  int rc = upload_b_operand(ctx, w, N, K, kpad_to, L);
-  if (rc) return rc;
+  int rc = 0;
   L.file_dtype = t.dtype;
-  if (t.dtype == QT_Q4_0 || t.dtype == QT_Q4_1 || t.dtype == QT_Q8_0) {
-    L.raw = upload_bytes(ctx, t.data.data(), t.data.size(), &rc);
+  if (ctx->weights_quantised && k_dims == 1 && (t.dtype == QT_Q4_0 || t.dtype == QT_Q8_0) && K % 32 == 0 &&
+      N % 8 == 0) {
+    // block form on the device: the file's rows go up once and are split into the value and
+    // scale planes the GEMM's TMA loads read; no f16 copy of the weight exists
+    L.N = N;
+    L.K = K;
+    L.Kpad = K;
+    L.qtype = t.dtype;
+    std::shared_ptr<DevBuf> raw = upload_bytes(ctx, t.data.data(), t.data.size(), &rc);
     if (rc) return rc;
+    L.qv = std::make_shared<DevBuf>();
+    L.qs = std::make_shared<DevBuf>();
+    const size_t vbytes = (size_t)N * (t.dtype == QT_Q4_0 ? K / 2 : K);
+    if (L.qv->reserve(vbytes) || L.qs->reserve((size_t)N * (K / 32) * 2))
+      return set_error(ctx, kErrOOM, "out of device memory for %s", t.name.c_str());
+    if (repack_q_rows(raw->p, t.dtype, N, K, L.qv->p, L.qs->as<__half>(), ctx->stream))
+      return set_error(ctx, kErrCuda, "repack of %s failed", t.name.c_str());
+    if (cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+      return set_error(ctx, kErrCuda, "repack of %s failed", t.name.c_str());
+    ctx->model.device_bytes += vbytes + (size_t)N * (K / 32) * 2;
+    ctx->model.device_bytes -= t.data.size();  // the uploaded rows are released here
+  } else {
+    std::vector<float> w;
+    tensor_to_f32(t, w);
+    rc = upload_b_operand(ctx, w, N, K, kpad_to, L);
+    if (rc) return rc;
+    if (t.dtype == QT_Q4_0 || t.dtype == QT_Q4_1 || t.dtype == QT_Q8_0) {
+      L.raw = upload_bytes(ctx, t.data.data(), t.data.size(), &rc);
+      if (rc) return rc;
+    }
   }
   if (bias) {
     std::vector<float> b;
@@ -479,16 +503,30 @@ static int load_mem_attn(s3b_ctx* ctx, const Index& idx) {
       NEED(qb, p + ".sa.q_proj.bias");
       NEED(kb, p + ".sa.k_proj.bias");
       NEED(vb, p + ".sa.v_proj.bias");
-      std::vector<float> a, b, c, w;
-      tensor_to_f32(*qw, a);
-      tensor_to_f32(*kw, b);
-      tensor_to_f32(*vw, c);
       const int D = (int)qw->ne[0];
-      w.reserve(a.size() * 3);
-      w.insert(w.end(), a.begin(), a.end());
-      w.insert(w.end(), b.begin(), b.end());
-      w.insert(w.end(), c.begin(), c.end());
-      if ((rc = upload_b_operand(ctx, w, 3 * D, D, 8, L.sa_qkv))) return rc;
+      if (qw->dtype == kw->dtype && qw->dtype == vw->dtype && qw->ne[0] == kw->ne[0] && qw->ne[0] == vw->ne[0] &&
+          qw->ne[1] == D && kw->ne[1] == D && vw->ne[1] == D) {
+        // the three weights' rows, concatenated in their stored form (f32 / f16 / block rows)
+        FileTensor cat;
+        cat.name = p + ".sa.qkv_proj.weight";
+        cat.dtype = qw->dtype;
+        cat.n_dims = 2;
+        cat.ne[0] = D;
+        cat.ne[1] = 3 * D;
+        cat.data.reserve(qw->data.size() * 3);
+        for (const FileTensor* t : {qw, kw, vw}) cat.data.insert(cat.data.end(), t->data.begin(), t->data.end());
+        if ((rc = upload_linear(ctx, cat, nullptr, L.sa_qkv))) return rc;
+      } else {
+        std::vector<float> a, b, c, w;
+        tensor_to_f32(*qw, a);
+        tensor_to_f32(*kw, b);
+        tensor_to_f32(*vw, c);
+        w.reserve(a.size() * 3);
+        w.insert(w.end(), a.begin(), a.end());
+        w.insert(w.end(), b.begin(), b.end());
+        w.insert(w.end(), c.begin(), c.end());
+        if ((rc = upload_b_operand(ctx, w, 3 * D, D, 8, L.sa_qkv))) return rc;
+      }
       std::vector<float> ba, bb, bc;
       tensor_to_f32(*qb, ba);
       tensor_to_f32(*kb, bb);

@@ -42,13 +42,25 @@ int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long
     b = ctx->next_event();
     cudaEventRecord(a, ctx->stream);
   }
-  const int rc = gemm_f16(A, lda, L.w->as<__half>(), L.Kpad, (int)M, L.N, L.Kpad, ep, ctx->d_err, ctx->stream);
+  int rc;
+  if (L.qtype) {
+    QWeight qw;
+    qw.type = L.qtype;
+    qw.values = L.qv->p;
+    qw.scales = L.qs->as<__half>();
+    rc = gemm_q(A, lda, qw, (int)M, L.N, L.K, ep, ctx->d_err, ctx->stream);
+  } else {
+    rc = gemm_f16(A, lda, L.w->as<__half>(), L.Kpad, (int)M, L.N, L.Kpad, ep, ctx->d_err, ctx->stream);
+  }
   count_launch(ctx);
   if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "gemm M=%lld N=%d K=%d failed (%d)", M, L.N, L.Kpad, rc);
   if (ctx->prof) {
     cudaEventRecord(b, ctx->stream);
-    // algorithmic work: 2*M*N*K flops; bytes: A + B (f16) + output
-    const double bytes = 2.0 * M * L.K + 2.0 * L.N * L.K + (ep.out_f32 ? 4.0 : 2.0) * M * L.N;
+    // algorithmic work: 2*M*N*K flops; bytes: A + B (f16, or the block values + f16 scales) + output
+    const double wbytes = L.qtype == QT_Q4_0   ? L.N * (L.K / 2.0 + L.K / 16.0)
+                          : L.qtype == QT_Q8_0 ? L.N * (L.K + L.K / 16.0)
+                                               : 2.0 * L.N * L.K;
+    const double bytes = 2.0 * M * L.K + wbytes + (ep.out_f32 ? 4.0 : 2.0) * M * L.N;
     ctx->prof_entries.push_back({0, 2.0 * M * L.N * L.K, bytes, a, b});
   }
   return kOk;
