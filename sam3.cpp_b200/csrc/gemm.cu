@@ -374,7 +374,8 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
   uint64_t* rfull = mma_done + 1;  // [half*2 + buf]: residual chunk landed in its staging buffer
   uint64_t* qfull = rfull + 4;     // [QS] (QB): a k-step's block values and scales landed
   uint64_t* qempty = qfull + QS;   // [QS] (QB): the dequantising warps have read the landing buffer
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(qempty + QS);
+  uint64_t* dq = qempty + QS;      // [STAGES] (QB pairs, peer CTA): its half of the B tile is written
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(dq + (QS ? STAGES : 0));
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -389,9 +390,11 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      // QB: the producer's arrive (A bytes) + one arrive per dequantising warp (of both CTAs with pairs)
-      mbar_init(&full[s], QB ? 1 + (PAIR ? 2 : 1) * DW : 1);
+      // QB: the producer's arrive (A bytes) + one arrive per dequantising warp of this CTA (+ with
+      // pairs, one relayed arrive for all of the peer's)
+      mbar_init(&full[s], QB ? 1 + DW + (PAIR ? 1 : 0) : 1);
       mbar_init(&empty[s], 1);
+      if (QB) mbar_init(&dq[s], DW);
     }
     for (int s = 0; s < QS; ++s) {
       mbar_init(&qfull[s], 1);
@@ -508,6 +511,21 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
         if (armed & (1u << s)) mbar_wait_drain(&qfull[s], (armed_phase >> s) & 1u, err);
     }
   } else if (warp == 1) {
+    if (QB && PAIR && lane == 0 && rank == 1) {
+      // the peer's MMA warp is otherwise idle: it relays "this CTA's half of the B tile is written"
+      // to the leader's `full` barrier, one cluster-scope arrive per k-step instead of one per warp
+      const uint32_t full_leader = cluster_addr(smem_u32(&full[0]), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = unit; t < n_tiles && ok; t += n_units) {
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&dq[stage], phase, s_abort, err, kErrWaitMisc)) { ok = false; break; }
+          mbar_arrive_cluster(full_leader + (uint32_t)(stage * 8));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = idesc_f16(TM, BN, 0);
       int stage = 0;
@@ -559,7 +577,6 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
     constexpr int DT = (DW > 0 ? DW : 1) * 32;
     static_assert(UNITS % DT == 0, "units per dequantising thread");
     const int dt = (int)threadIdx.x - 32 * (2 + EW);
-    const uint32_t full_leader = PAIR ? cluster_addr(smem_u32(&full[0]), 0) : 0u;
     int stage = 0, qi = 0;
     uint32_t phase = 0, qph = 0;
     bool ok = true;
@@ -602,10 +619,7 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&qempty[qi]);
-          if (PAIR)
-            mbar_arrive_cluster(full_leader + (uint32_t)(stage * 8));
-          else
-            mbar_arrive(&full[stage]);
+          mbar_arrive(PAIR && rank == 1 ? &dq[stage] : &full[stage]);
         }
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
         if (++qi == QS) { qi = 0; qph ^= 1; }
@@ -947,7 +961,7 @@ int launch_gemm(const __half* A, long long lda, const void* B, long long ldb, in
   }
   constexpr size_t q_bytes = QB ? (size_t)BN_CTA * QROW + 4 * BN_CTA : 0;
   constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN_CTA) * kBK * 2 + (size_t)QS * q_bytes +
-                          (TMA_EPI ? 4 * kStageBufBytes : 0) + (2 * STAGES + 2 * QS + 9) * 8 + 16;
+                          (TMA_EPI ? 4 * kStageBufBytes : 0) + (2 * STAGES + 2 * QS + (QS ? STAGES : 0) + 9) * 8 + 16;
   static_assert(smem <= 232448, "shared memory per CTA");
   auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR, EW, BLK, QB, QS>;
   constexpr int kThreads = gemm_threads(EW, DW);
