@@ -384,6 +384,8 @@ def main():
                     help="1: quantised weights stay in block form in HBM, dequantised inside the GEMMs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-hiera", action="store_true", help="skip the Hiera-T (configs[1]) measurement")
+    ap.add_argument("--only-hiera", action="store_true",
+                    help="run only the Hiera-T (configs[1]) measurement and print its numbers (a profiling case)")
     ap.add_argument("--no-video", action="store_true",
                     help="skip the Hiera-L + memory attention (configs[4]) measurement")
     args = ap.parse_args()
@@ -434,6 +436,15 @@ def main():
     torch.cuda.set_device(local)
     s3b = load_pkg()
     from sam3_b200 import synth
+
+    if args.only_hiera:
+        h = bench_hiera(s3b, local, rank, world, args.steps, args.warmup, torch.cuda.Stream(), "cuda")
+        if rank == 0:
+            print(json.dumps({"impl": "b200", "n_gpus": n_gpus, "steps": args.steps, "warmup": args.warmup,
+                              "hiera_t_q4_0": h}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     path = os.path.join(tempfile.gettempdir(), f"s3b_bench_{args.workload}.ggml")
     t0 = time.time()

@@ -332,12 +332,10 @@ __device__ __forceinline__ float gelu_erf(float x) {
   const float h = rcp_approx(q);  // 0 once q^16 overflows (|x| > ~60): Phi = 1 or 0
   return x * (x >= 0.0f ? 1.0f - h : h);
 }
-// GELU with the tanh form (ggml_gelu, sam3.cpp:4449); tanh(u) = 1 - 2 / (exp(2u) + 1).
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  const float u = fminf(fmaxf(k0 * fmaf(k1 * x * x, x, x), -10.0f), 10.0f);  // tanh(+-10) == +-1 in f32
-  const float th = 1.0f - __fdividef(2.0f, __expf(2.0f * u) + 1.0f);
-  return 0.5f * x * (1.0f + th);
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // Packed two-wide f32 arithmetic (sm_100: one instruction for two lanes of a 64-bit register pair).
@@ -363,6 +361,21 @@ __device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsig
   unsigned long long d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
+}
+
+// GELU with the tanh form (ggml_gelu, sam3.cpp:4449) on a pair of values, as x * sigmoid(2u) = x / (1 + 2^t) with u = k0 (x + k1 x^3) and
+// t = -2 u / ln 2 = x (c1 + c3 x^2): 5 two-wide FMA-pipe operations and 2 MUFU operations per value
+// (ex2, rcp). Large positive t gives 2^t = inf and x * 0; large negative t gives x * 1.
+__device__ __forceinline__ void gelu_tanh2(float& a, float& b) {
+  const float c1 = -2.3022082f, c3 = -0.10294324f;  // -2 k0 / ln 2, times k1 = 0.044715 (k0 = sqrt(2/pi))
+  const unsigned long long x = f2_pack(a, b);
+  const unsigned long long t = f2_mul(f2_fma(f2_mul(x, x), f2_pack(c3, c3), f2_pack(c1, c1)), x);
+  float ta, tb;
+  f2_unpack(t, ta, tb);
+  const unsigned long long d = f2_add(f2_pack(ex2_approx(ta), ex2_approx(tb)), f2_pack(1.0f, 1.0f));
+  float da, db;
+  f2_unpack(d, da, db);
+  f2_unpack(f2_mul(x, f2_pack(rcp_approx(da), rcp_approx(db))), a, b);
 }
 
 // gelu_erf on a pair of values: the degree-6 polynomial and the four squarings run two-wide.

@@ -158,7 +158,7 @@ __device__ __forceinline__ void epi_math16(const EpiParams& ep, int rope_pos, in
     for (int i = 0; i < 16; i += 2) gelu_erf2(v[i], v[i + 1]);
   } else if (ep.act == ACT_GELU_TANH) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = gelu_tanh(v[i]);
+    for (int i = 0; i < 16; i += 2) gelu_tanh2(v[i], v[i + 1]);
   } else if (ep.act == ACT_RELU) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = fmaxf(v[i], 0.0f);
@@ -402,7 +402,9 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], PAIR ? 2 * EW : EW);
+      // pairs: the leader's epilogue warps + one arrive relayed for all of the peer's (quantised
+      // weights: every warp of both CTAs arrives on the leader's barrier)
+      mbar_init(&tempty[a], PAIR ? (QB ? 2 * EW : (rank == 0 ? EW + 1 : EW)) : EW);
     }
     mbar_init(mma_done, 1);
     for (int i = 0; i < 4; ++i) mbar_init(&rfull[i], 1);
@@ -511,6 +513,19 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
         if (armed & (1u << s)) mbar_wait_drain(&qfull[s], (armed_phase >> s) & 1u, err);
     }
   } else if (warp == 1) {
+    if (!QB && PAIR && lane == 0 && rank == 1) {
+      // the peer's MMA warp is otherwise idle: it relays "this CTA's epilogue warps have read the
+      // accumulator" to the leader's `tempty`, one cluster-scope arrive per tile instead of one per
+      // warp (per-warp cluster releases stalled the short-K GEMMs' epilogues on membar)
+      const uint32_t tempty_leader = cluster_addr(smem_u32(&tempty[0]), 0);
+      int acc = 0;
+      uint32_t aphase = 0;
+      for (int t = unit; t < n_tiles; t += n_units) {
+        if (!mbar_wait(&tempty[acc], aphase, s_abort, err, kErrWaitMisc)) break;
+        mbar_arrive_cluster(tempty_leader + (uint32_t)(acc * 8));
+        if (++acc == 2) { acc = 0; aphase ^= 1; }
+      }
+    }
     if (QB && PAIR && lane == 0 && rank == 1) {
       // the peer's MMA warp is otherwise idle: it relays "this CTA's half of the B tile is written"
       // to the leader's `full` barrier, one cluster-scope arrive per k-step instead of one per warp
@@ -670,10 +685,10 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
     };
     // this CTA's epilogue warps release an accumulator on the MMA-issuing CTA's barrier
     auto release_acc = [&](int a) {
-      if (PAIR)
+      if (PAIR && QB)
         mbar_arrive_cluster(cluster_addr(smem_u32(&tempty[a]), 0));
       else
-        mbar_arrive(&tempty[a]);
+        mbar_arrive(&tempty[a]);  // pairs: the peer's warps arrive on its own barrier, relayed below
     };
     for (int t = unit; t < n_tiles; t += n_units) {
       const int m0 = (t / tiles_n) * TM + (int)rank * kBM;
