@@ -211,6 +211,7 @@ void s3b_destroy(s3b_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->ma_exec) cudaGraphExecDestroy(ctx->ma_exec);
   for (void* p : ctx->ipc_mapped) cudaIpcCloseMemHandle(p);
   ctx->ipc_mapped.clear();
   ctx->user_allocs.clear();
@@ -257,6 +258,12 @@ int s3b_sync(s3b_ctx* ctx) {
 int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
   if (!ctx || !key) return kErrArg;
   const std::string k(key);
+  ++ctx->graph_epoch;  // kernel choices may change: recapture graphs
+  if (k == "graphs") {
+    if (value < 0 || value > 1) return set_error(ctx, kErrArg, "graphs must be 0 or 1");
+    ctx->graphs = (int)value;
+    return kOk;
+  }
   if (k == "frames_per_pass") {
     if (value < 1 || value > 256) return set_error(ctx, kErrArg, "frames_per_pass out of range");
     ctx->max_frames_per_pass = (int)value;
@@ -337,6 +344,7 @@ int s3b_load_model(s3b_ctx* ctx, const char* path) {
   if (rc) return rc;
   if (!path) return set_error(ctx, kErrArg, "null path");
   ctx->out = Outputs();
+  ++ctx->graph_epoch;  // graphs hold the old weights' addresses
   return load_model(ctx, path);
 }
 

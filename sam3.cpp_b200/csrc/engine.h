@@ -228,6 +228,13 @@ struct s3b_ctx {
   int weights_quantised = 0;   // q4_0 / q8_0 linear weights stay in block form, dequantised inside the GEMM
   int conv_implicit = 1;       // pixel-block GEMMs: implicit 3x3 convs, TMA-stored deconvs (0: im2col / scatter)
   int attention_exp_poly = 0;  // of every 8 softmax exponentials in the tcgen05 kernel, how many use the FMA pipe
+  // memory attention: its per-layer body replayed from a CUDA graph (mem_attn.cpp)
+  int graphs = 1;               // option "graphs"
+  long long graph_epoch = 0;    // bumped by every option change and model load: cached graphs are stale
+  cudaGraphExec_t ma_exec = nullptr;
+  std::vector<uintptr_t> ma_key;  // shapes, buffers, epoch and kernel choices the graph was captured with
+  long long ma_launches = 0;      // kernel launches inside the graph
+  int ma_seen = 0;                // eager calls with ma_key so far (the graph is captured on the second)
   // launch accounting + optional per-kernel CUDA-event timing (s3b_profile_*)
   long long n_launches = 0;
   bool prof = false;

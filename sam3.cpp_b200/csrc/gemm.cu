@@ -1184,5 +1184,6 @@ int gemm_deconv2x2(const __half* x, int F, int H, int W, int Cin, const __half* 
 
 void set_gemm_pairs(int mode) { g_gemm_pairs = mode; }
 void set_gemm_wide_epilogue(int mode) { g_gemm_wide_epi = mode; }
+int gemm_config_id() { return g_gemm_pairs * 2 + g_gemm_wide_epi; }
 
 }  // namespace s3b

@@ -95,6 +95,8 @@ void set_gemm_pairs(int mode);
 // Process-wide: which short-K (K < 2048) GEMMs use 16 epilogue warps: 0 none,
 // 1 (default) those with f16 outputs, 2 all.
 void set_gemm_wide_epilogue(int mode);
+// The current process-wide GEMM variant choices (pairs, epilogue warps) as one number.
+int gemm_config_id();
 
 // Flash attention (online softmax, f16 in / f32 acc / f16 out).
 struct AttnParams {

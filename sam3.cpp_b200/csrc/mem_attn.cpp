@@ -63,6 +63,98 @@ static const float* rope_table(s3b_ctx* ctx, int feat, int D, int* rc) {
   return b->as<float>();
 }
 
+// The layers of memory attention (sam3.cpp:9245-9327) on the context's work buffers: every launch
+// reads and writes only buffers of the context and the model, so the sequence can be captured once
+// and replayed.
+struct MemAttnBufs {
+  float* X;
+  __half *XN, *qkv, *ao, *hb, *kvin, *pin, *kb, *vb;
+  const float* rope;
+  long long N, Mt, m_sp;
+  int D, FFN;
+};
+
+static int mem_attn_layers(s3b_ctx* ctx, const MemAttnBufs& b) {
+  const Model& M = ctx->model;
+  const int D = b.D, FFN = b.FFN, MD = M.hp.mem_out_dim;
+  const long long N = b.N, Mt = b.Mt, m_sp = b.m_sp;
+  float* X = b.X;
+  __half* XN = b.XN;
+  const float* rope = b.rope;
+  const float scale = 1.0f / sqrtf((float)D);
+  RowMap id;
+  for (size_t l = 0; l < M.mem.size(); ++l) {
+    const MemAttnLayer& L = M.mem[l];
+    // self-attention with RoPE on q and k (sam3.cpp:9247-9271)
+    CKL(run_ln(ctx, X, D, XN, 0, D, N, D, L.n1w.ptr(), L.n1b.ptr(), 1e-5f, id));
+    EpiParams e = epi_store(L.sa_qkv, (void*)b.qkv, 0, 3LL * D);
+    e.rope = rope;
+    e.rope_D = D;
+    e.rope_cols = 2 * D;
+    e.rope_rows = N;
+    e.rope_mod = N;
+    CKR(run_gemm(ctx, XN, D, L.sa_qkv, N, e));
+    AttnParams a;
+    a.q = b.qkv;
+    a.k = a.q + D;
+    a.v = a.q + 2 * D;
+    a.q_n = a.k_n = a.v_n = 3LL * D;
+    a.heads = 1;
+    a.nq = a.nk = (int)N;
+    a.o = b.ao;
+    a.o_n = D;
+    a.scale = scale;
+    CKR(run_attn(ctx, a, D, 1));
+    EpiParams r = epi_store(L.sa_out, X, 1, D);
+    r.resid = X;
+    r.ldr = D;
+    CKR(run_gemm(ctx, b.ao, D, L.sa_out, N, r));
+    // cross-attention to the memory (sam3.cpp:9274-9316)
+    CKL(run_ln(ctx, X, D, XN, 0, D, N, D, L.n2w.ptr(), L.n2b.ptr(), 1e-5f, id));
+    EpiParams eq = epi_store(L.ca_q, (void*)b.qkv, 0, D);
+    eq.rope = rope;
+    eq.rope_D = D;
+    eq.rope_cols = D;
+    eq.rope_rows = N;
+    eq.rope_mod = N;
+    CKR(run_gemm(ctx, XN, D, L.ca_q, N, eq));
+    EpiParams ek = epi_store(L.ca_k, (void*)b.kb, 0, D);
+    if (m_sp > 0) {
+      ek.rope = rope;
+      ek.rope_D = D;
+      ek.rope_cols = D;
+      ek.rope_rows = m_sp;  // pointer tokens at the end get no RoPE
+      ek.rope_mod = N;      // the table repeats for every memory slot
+    }
+    CKR(run_gemm(ctx, b.kvin, MD, L.ca_k, Mt, ek));
+    CKR(run_gemm(ctx, b.pin, MD, L.ca_v, Mt, epi_store(L.ca_v, (void*)b.vb, 0, D)));
+    AttnParams c;
+    c.q = b.qkv;
+    c.k = b.kb;
+    c.v = b.vb;
+    c.q_n = c.k_n = c.v_n = D;
+    c.heads = 1;
+    c.nq = (int)N;
+    c.nk = (int)Mt;
+    c.o = b.ao;
+    c.o_n = D;
+    c.scale = scale;
+    CKR(run_attn(ctx, c, D, 1));
+    EpiParams r2 = epi_store(L.ca_out, X, 1, D);
+    r2.resid = X;
+    r2.ldr = D;
+    CKR(run_gemm(ctx, b.ao, D, L.ca_out, N, r2));
+    // FFN (sam3.cpp:9318-9326)
+    CKL(run_ln(ctx, X, D, XN, 0, D, N, D, L.n3w.ptr(), L.n3b.ptr(), 1e-5f, id));
+    CKR(run_gemm(ctx, XN, D, L.fc1, N, epi_store(L.fc1, (void*)b.hb, 0, FFN, ACT_RELU)));
+    EpiParams r3 = epi_store(L.fc2, X, 1, D);
+    r3.resid = X;
+    r3.ldr = D;
+    CKR(run_gemm(ctx, b.hb, FFN, L.fc2, N, r3));
+  }
+  return kOk;
+}
+
 int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const float* prompt,
                  const float* prompt_pos, int m_total, int n_ptr, float* out) {
   const Model& M = ctx->model;
@@ -93,76 +185,69 @@ int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat
   // memory keys see prompt + prompt_pos, values see prompt (sam3.cpp:9278-9283)
   CKL(add_scaled_to_f16(prompt, prompt_pos, 1.0f, Mt * MD, kvin->as<__half>(), ctx->stream));
   CKL(add_scaled_to_f16(prompt, nullptr, 0.0f, Mt * MD, pin->as<__half>(), ctx->stream));
-  const float scale = 1.0f / sqrtf((float)D);
-
-  for (size_t l = 0; l < M.mem.size(); ++l) {
-    const MemAttnLayer& L = M.mem[l];
-    // self-attention with RoPE on q and k (sam3.cpp:9247-9271)
-    CKL(run_ln(ctx, X, D, XN, 0, D, N, D, L.n1w.ptr(), L.n1b.ptr(), 1e-5f, id));
-    EpiParams e = epi_store(L.sa_qkv, qkv->p, 0, 3LL * D);
-    e.rope = rope;
-    e.rope_D = D;
-    e.rope_cols = 2 * D;
-    e.rope_rows = N;
-    e.rope_mod = N;
-    CKR(run_gemm(ctx, XN, D, L.sa_qkv, N, e));
-    AttnParams a;
-    a.q = qkv->as<__half>();
-    a.k = a.q + D;
-    a.v = a.q + 2 * D;
-    a.q_n = a.k_n = a.v_n = 3LL * D;
-    a.heads = 1;
-    a.nq = a.nk = (int)N;
-    a.o = ao->as<__half>();
-    a.o_n = D;
-    a.scale = scale;
-    CKR(run_attn(ctx, a, D, 1));
-    EpiParams r = epi_store(L.sa_out, X, 1, D);
-    r.resid = X;
-    r.ldr = D;
-    CKR(run_gemm(ctx, ao->as<__half>(), D, L.sa_out, N, r));
-    // cross-attention to the memory (sam3.cpp:9274-9316)
-    CKL(run_ln(ctx, X, D, XN, 0, D, N, D, L.n2w.ptr(), L.n2b.ptr(), 1e-5f, id));
-    EpiParams eq = epi_store(L.ca_q, qkv->p, 0, D);
-    eq.rope = rope;
-    eq.rope_D = D;
-    eq.rope_cols = D;
-    eq.rope_rows = N;
-    eq.rope_mod = N;
-    CKR(run_gemm(ctx, XN, D, L.ca_q, N, eq));
-    EpiParams ek = epi_store(L.ca_k, kb->p, 0, D);
-    if (m_sp > 0) {
-      ek.rope = rope;
-      ek.rope_D = D;
-      ek.rope_cols = D;
-      ek.rope_rows = m_sp;  // pointer tokens at the end get no RoPE
-      ek.rope_mod = N;      // the table repeats for every memory slot
+  MemAttnBufs mb;
+  mb.X = X;
+  mb.XN = XN;
+  mb.qkv = qkv->as<__half>();
+  mb.ao = ao->as<__half>();
+  mb.hb = hb->as<__half>();
+  mb.kvin = kvin->as<__half>();
+  mb.pin = pin->as<__half>();
+  mb.kb = kb->as<__half>();
+  mb.vb = vb->as<__half>();
+  mb.rope = rope;
+  mb.N = N;
+  mb.Mt = Mt;
+  mb.m_sp = m_sp;
+  mb.D = D;
+  mb.FFN = FFN;
+  // The layers are about 50 launches of short kernels. With profiling off and a capturable stream,
+  // the second call with the same shapes, buffers and options captures them into a CUDA graph (the
+  // first call has allocated every workspace and set every kernel attribute) and later calls replay
+  // it, which removes the host launch work and most of the gaps between the kernels.
+  const bool can_graph = ctx->graphs && !ctx->prof && ctx->stream != nullptr;
+  // every buffer the layers touch is in the key, the attention's key-split workspace included (an
+  // encoder call on the same context may grow and so move it)
+  const auto ws_it = ctx->ws.find("attn_wide_split");
+  const uintptr_t split_ws = (ws_it != ctx->ws.end() && ws_it->second) ? (uintptr_t)ws_it->second->p : 0;
+  const std::vector<uintptr_t> key = {(uintptr_t)ctx->graph_epoch, (uintptr_t)gemm_config_id(), (uintptr_t)N,
+                                      (uintptr_t)Mt, (uintptr_t)m_sp, (uintptr_t)X, (uintptr_t)XN,
+                                      (uintptr_t)mb.qkv, (uintptr_t)mb.ao, (uintptr_t)mb.hb, (uintptr_t)mb.kvin,
+                                      (uintptr_t)mb.pin, (uintptr_t)mb.kb, (uintptr_t)mb.vb, (uintptr_t)rope,
+                                      split_ws};
+  if (key != ctx->ma_key) {
+    if (ctx->ma_exec) cudaGraphExecDestroy(ctx->ma_exec);
+    ctx->ma_exec = nullptr;
+    ctx->ma_key = key;
+    ctx->ma_seen = 0;
+  }
+  if (can_graph && !ctx->ma_exec && ctx->ma_seen >= 1) {
+    const long long n0 = ctx->n_launches;
+    cudaGraph_t g = nullptr;
+    bool ok = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+    const int lrc = ok ? mem_attn_layers(ctx, mb) : kOk;
+    if (ok) ok = cudaStreamEndCapture(ctx->stream, &g) == cudaSuccess && lrc == kOk;
+    cudaGraphExec_t exec = nullptr;
+    if (ok) ok = cudaGraphInstantiate(&exec, g, 0) == cudaSuccess;
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();  // a failed capture leaves its error here; the eager path below reports real faults
+    const long long captured = ctx->n_launches - n0;
+    ctx->n_launches = n0;  // nothing ran during the capture
+    if (ok) {
+      ctx->ma_exec = exec;
+      ctx->ma_launches = captured;
+    } else {
+      if (exec) cudaGraphExecDestroy(exec);
+      ctx->ma_seen = -(1 << 30);  // not capturable on this stream: stay eager for this key
     }
-    CKR(run_gemm(ctx, kvin->as<__half>(), MD, L.ca_k, Mt, ek));
-    CKR(run_gemm(ctx, pin->as<__half>(), MD, L.ca_v, Mt, epi_store(L.ca_v, vb->p, 0, D)));
-    AttnParams c;
-    c.q = qkv->as<__half>();
-    c.k = kb->as<__half>();
-    c.v = vb->as<__half>();
-    c.q_n = c.k_n = c.v_n = D;
-    c.heads = 1;
-    c.nq = (int)N;
-    c.nk = (int)Mt;
-    c.o = ao->as<__half>();
-    c.o_n = D;
-    c.scale = scale;
-    CKR(run_attn(ctx, c, D, 1));
-    EpiParams r2 = epi_store(L.ca_out, X, 1, D);
-    r2.resid = X;
-    r2.ldr = D;
-    CKR(run_gemm(ctx, ao->as<__half>(), D, L.ca_out, N, r2));
-    // FFN (sam3.cpp:9318-9326)
-    CKL(run_ln(ctx, X, D, XN, 0, D, N, D, L.n3w.ptr(), L.n3b.ptr(), 1e-5f, id));
-    CKR(run_gemm(ctx, XN, D, L.fc1, N, epi_store(L.fc1, hb->p, 0, FFN, ACT_RELU)));
-    EpiParams r3 = epi_store(L.fc2, X, 1, D);
-    r3.resid = X;
-    r3.ldr = D;
-    CKR(run_gemm(ctx, hb->as<__half>(), FFN, L.fc2, N, r3));
+  }
+  if (can_graph && ctx->ma_exec) {
+    if (cudaGraphLaunch(ctx->ma_exec, ctx->stream) != cudaSuccess)
+      return set_error(ctx, kErrCuda, "memory-attention graph launch failed");
+    count_launch(ctx, (int)ctx->ma_launches);
+  } else {
+    ++ctx->ma_seen;
+    CKR(mem_attn_layers(ctx, mb));
   }
   // final norm (sam3.cpp:9330-9334)
   CKL(run_ln(ctx, X, D, out, 1, D, N, D, M.mem_norm_w.ptr(), M.mem_norm_b.ptr(), 1e-5f, id));

@@ -98,3 +98,47 @@ def test_mem_attn_vs_oracle(engine, s3b, tmp_path, qtype, feat, slots, ptrs):
     diff = np.abs(got - ref)
     cos = float((got * ref).sum() / (np.linalg.norm(got) * np.linalg.norm(ref)))
     assert cos >= 0.9995 and diff.mean() <= 0.01 * np.abs(ref).mean(), (cos, diff.mean(), diff.max())
+
+
+def test_mem_attn_graph_replay_equals_eager(engine, s3b, tmp_path):
+    """Option "graphs": from the second call with the same shapes and buffers, the memory-attention layers
+    replay from a CUDA graph (on a stream that can be captured). Replays give the same bits as eager runs,
+    and a model reload or an option change recaptures."""
+    from sam3_b200 import synth
+    cfg = synth.Sam3Config(img_size=336, patch=14, embed=128, depth=1, heads=2, window=8, global_idx=(),
+                           neck_dim=256, neck_mid=128, with_mem_attn=True)
+    path = str(tmp_path / "mem_g.ggml")
+    synth.write_sam3(path, cfg, seed=9, ftype=1, qtype=8, quantize=s3b.quantize_rows, ln_random=True)
+    rng = np.random.default_rng(7)
+    feat, slots, ptrs = 16, 2, 4
+    N, M = feat * feat, slots * feat * feat + 4 * ptrs
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    curr = d(rng.standard_normal((N, 256), dtype=np.float32))
+    pos = d(om.src_pos(feat))
+    prompt = d(rng.standard_normal((M, 64), dtype=np.float32))
+    ppos = d(rng.standard_normal((M, 64), dtype=np.float32))
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    engine.set_stream(stream.cuda_stream)
+    try:
+        engine.load_model(path)
+        outs = []
+        for i in range(5):
+            if i == 4:
+                engine.set_option("graphs", 0)
+            out = torch.empty_like(curr)
+            engine.mem_attn(curr, pos, feat, prompt, ppos, 4 * ptrs, out=out)
+            engine.sync()
+            outs.append(out.cpu())
+        engine.set_option("graphs", 1)
+        engine.load_model(path)  # new weight buffers: the next calls run eagerly, then recapture
+        for _ in range(3):
+            out = torch.empty_like(curr)
+            engine.mem_attn(curr, pos, feat, prompt, ppos, 4 * ptrs, out=out)
+            engine.sync()
+            outs.append(out.cpu())
+    finally:
+        engine.set_option("graphs", 1)
+        engine.set_stream(torch.cuda.current_stream().cuda_stream)
+    for i, o in enumerate(outs[1:], 1):
+        assert torch.equal(o, outs[0]), i
