@@ -16,6 +16,12 @@ namespace {
 
 constexpr int kMaxVec = 16;  // float4 per lane -> C <= 2048
 
+// The LayerNorms run between GEMMs that sweep their row tiles upwards: the rows a GEMM wrote last are the
+// ones still in L2. Blocks, which start roughly in index order, therefore take rows from the end: the
+// first reads hit the previous GEMM's most recent output, and the rows written last, the low ones, are
+// the first the next GEMM reads. Rows are independent, so the order changes no value.
+__device__ __forceinline__ unsigned layernorm_block_rev() { return gridDim.x - 1 - blockIdx.x; }
+
 // One warp per R rows, NV = ceil(C / 128) float4 per lane and row held in
 // registers (so the register footprint, and with it the number of rows in
 // flight per SM, follows the row width; narrow rows are batched R to a warp so
@@ -26,7 +32,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
                                                         void* __restrict__ y, int y_f32, long long ldy, long long rows,
                                                         int C, const float* __restrict__ gamma,
                                                         const float* __restrict__ beta, float eps, RowMap map) {
-  const long long row0 = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * R;
+  // blocks take rows from the end (see layernorm_block_rev)
+  const long long row0 = ((long long)layernorm_block_rev() * (blockDim.x >> 5) + (threadIdx.x >> 5)) * R;
   const int lane = threadIdx.x & 31;
   const int nvec = C >> 2;
   float4 v[R][NV];
@@ -401,7 +408,7 @@ __global__ void __launch_bounds__(256) layernorm_sub_kernel(const float* __restr
   constexpr int G = 32 / L;
   const int lane = threadIdx.x & 31;
   const int sub = lane / L, sl = lane % L;
-  const long long row0 = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * (G * RI);
+  const long long row0 = ((long long)layernorm_block_rev() * (blockDim.x >> 5) + (threadIdx.x >> 5)) * (G * RI);
   float4 v[RI][NV];
   long long src[RI];
 #pragma unroll
