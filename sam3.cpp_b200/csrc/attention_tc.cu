@@ -313,10 +313,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // 1-D grid, query tile fastest: the tiles of one (window, head) run together and share K/V in L2
+  // 1-D grid, query tile fastest: the tiles of one (window, head) run together and share K/V in L2.
+  // Blocks take the units from the end: the qkv rows the projection GEMM wrote last are still in L2,
+  // and the output rows written last (the first windows) are the first the next GEMM reads.
+  const unsigned unit = gridDim.x - 1 - blockIdx.x;
   const int n_qt = (a.ntok + kBQ - 1) / kBQ;
-  const int bh = (int)(blockIdx.x / n_qt);
-  const int qb = (int)(blockIdx.x - (unsigned)bh * n_qt);
+  const int bh = (int)(unit / n_qt);
+  const int qb = (int)(unit - (unsigned)bh * n_qt);
   const int w = bh / a.heads, h = bh - w * a.heads;
   const int nkb = (a.ntok + kBK - 1) / kBK;
 

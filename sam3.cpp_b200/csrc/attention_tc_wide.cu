@@ -231,10 +231,13 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // 1-D grid, query tile fastest: the tiles of one (batch, head) run together and share K/V in L2
+  // 1-D grid, query tile fastest: the tiles of one (batch, head) run together and share K/V in L2.
+  // Blocks take the units from the end, for the same L2 reuse with the GEMMs before and after as in the
+  // d = 64 kernel.
+  const unsigned unit = gridDim.x - 1 - blockIdx.x;
   const int n_qt = (a.nq + kBQ - 1) / kBQ;
-  const int qb = (int)(blockIdx.x % (unsigned)n_qt);
-  const int rest = (int)(blockIdx.x / (unsigned)n_qt);
+  const int qb = (int)(unit % (unsigned)n_qt);
+  const int rest = (int)(unit / (unsigned)n_qt);
   const int split = rest % a.n_split;
   const int bh = rest / a.n_split;
   const int b = bh / a.heads, h = bh - b * a.heads;
