@@ -81,6 +81,23 @@ static void dequant_row_host(int dtype, const uint8_t* p, int64_t n, float* y) {
   }
 }
 
+// Runs fn(begin, end) over disjoint parts of [0, n) on up to 32 host threads; one call when n is below
+// two chunks of min_chunk. Load-time conversions are independent per element or row, so the result does
+// not depend on the split.
+template <typename F>
+static void parallel_for(int64_t n, int64_t min_chunk, F fn) {
+  unsigned nt = std::thread::hardware_concurrency();
+  nt = std::max(1u, std::min(nt, 32u));
+  const int64_t parts = std::min<int64_t>((int64_t)nt, n / std::max<int64_t>(min_chunk, 1));
+  if (parts <= 1) {
+    fn((int64_t)0, n);
+    return;
+  }
+  std::vector<std::thread> th;
+  for (int64_t c = 0; c < parts; ++c) th.emplace_back([&, c]() { fn(n * c / parts, n * (c + 1) / parts); });
+  for (auto& x : th) x.join();
+}
+
 void tensor_to_f32(const FileTensor& t, std::vector<float>& out) {
   const int64_t n = t.nelements();
   out.resize(n);
@@ -88,11 +105,16 @@ void tensor_to_f32(const FileTensor& t, std::vector<float>& out) {
     memcpy(out.data(), t.data.data(), n * 4);
   } else if (t.dtype == QT_F16) {
     const uint16_t* h = reinterpret_cast<const uint16_t*>(t.data.data());
-    for (int64_t i = 0; i < n; ++i) out[i] = h2f(h[i]);
+    parallel_for(n, 1 << 18, [&](int64_t b, int64_t e) {
+      for (int64_t i = b; i < e; ++i) out[i] = h2f(h[i]);
+    });
   } else {
     const int64_t rows = n / t.ne[0];
     const long long rb = qtype_row_bytes(t.dtype, t.ne[0]);
-    for (int64_t r = 0; r < rows; ++r) dequant_row_host(t.dtype, t.data.data() + r * rb, t.ne[0], out.data() + r * t.ne[0]);
+    parallel_for(rows, (1 << 18) / std::max<int64_t>(t.ne[0], 1) + 1, [&](int64_t b, int64_t e) {
+      for (int64_t r = b; r < e; ++r)
+        dequant_row_host(t.dtype, t.data.data() + r * rb, t.ne[0], out.data() + r * t.ne[0]);
+    });
   }
 }
 
@@ -266,8 +288,10 @@ static int upload_b_operand(s3b_ctx* ctx, const std::vector<float>& w, int N, in
   L.K = K;
   L.Kpad = ((K + kpad_to - 1) / kpad_to) * kpad_to;
   std::vector<__half> h((size_t)N * L.Kpad, __float2half_rn(0.f));
-  for (int n = 0; n < N; ++n)
-    for (int k = 0; k < K; ++k) h[(size_t)n * L.Kpad + k] = __float2half_rn(w[(size_t)n * K + k]);
+  parallel_for(N, (1 << 18) / std::max(K, 1) + 1, [&](int64_t b, int64_t e) {
+    for (int64_t n = b; n < e; ++n)
+      for (int k = 0; k < K; ++k) h[(size_t)n * L.Kpad + k] = __float2half_rn(w[(size_t)n * K + k]);
+  });
   int rc = 0;
   L.w = upload_bytes(ctx, h.data(), h.size() * 2, &rc);
   return rc;
