@@ -1,25 +1,28 @@
 #!/usr/bin/env python3
 """Encoder throughput benchmark (frames/s) of the B200 engine for sam3.cpp.
 
-Workload: SAM 3 ViT image encoder + tracker
-SimpleFPN neck, q4_0 weights (seeded synthetic, random-init), 64 seeded
-1008x1008 frames per GPU (rank r encodes frames [64 r, 64 r + 64): weak
-scaling, one process per GPU, no data-path collective). One step = encode
-all frames of the rank; `value` = all ranks' frames / the slowest rank's time.
-The same line carries `hiera_t_q4_0` (configs[1]: SAM 2.1 Hiera-T + FPN
-neck, q4_0, 16 seeded 1024x1024 frames per GPU) and `video_hiera_l_q8_0`
-(configs[4]: Hiera-L q8_0 on 64 frames per GPU, then memory attention per
-frame on GPU 0), timed the same way.
+Headline: SAM 3 ViT-L image encoder + tracker SimpleFPN neck, q4_0 weights
+(seeded synthetic, random-init), a 64-frame batch of seeded 1008x1008 frames split 64/N over N GPUs (strong
+scaling; one process per GPU, no data-path collective). One step = encode the rank's frames; `value` = 64 /
+the slowest rank's step time. The q4_0 weights stay in block form in HBM (engine option weights_quantised = 1:
+each layer's weight is dequantised into an L2-resident f16 staging buffer right before its GEMM).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload vit_q4_0|vit_f16]
-  python bench.py --impl reference ...   # CPU restatement (oracle) of the same path
+The same line carries the other configurations:
+  vit_f16_b1       configs[2]: SAM 3 ViT-L f16, batch 1 (latency)
+  hiera_t_f16_b1   configs[0]: SAM 2.1 Hiera-T f16, batch 1 (latency)
+  hiera_t_q4_0     configs[1]: SAM 2.1 Hiera-T q4_0, 16 frames per GPU
+  video_hiera_l_q8_0  configs[4]: Hiera-L q8_0 on 64 frames over the GPUs, each frame's neck_trk_2 moved to
+                   the tracking GPU (rank 0) over NVLink (CUDA IPC + peer copy), memory attention per frame
+                   there from a device-resident memory bank; the end-to-end pipeline rate and its limiter.
 
-`value` is measured with inputs resident in HBM (device uint8 frames);
-`e2e` goes through the public C ABI with pinned host frames every step
-(s3b_encode_u8: host->device copy inside the timed region) and reads the
-tracker's level-2 feature map (neck_trk_2, the memory-attention input) back
-to the host. Inputs (64 x 3 MB frames + 2.5 GB of activations per pass) are
-far larger than L2 (126 MB), so no separate flush is needed.
+  python bench.py [--gpus N] [--steps K] [--warmup W]
+  python bench.py --impl reference ...   # the CPU restatement (oracle) of the same path, timed
+
+`value` is measured with the frames resident in HBM; `e2e` goes through the public C ABI with pinned host
+frames every step (s3b_encode_u8: host->device copy inside the timed region) and reads back neck_trk_0..2
+(f32, the maps sam3_propagate_single hands downstream) of every frame into pinned host memory through
+s3b_output_host_bind (copies overlap the next encoder pass). Inputs plus activations per step are far
+larger than L2 (126 MB), so no separate flush is added.
 """
 from __future__ import annotations
 
@@ -36,9 +39,13 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 FRAMES_TOTAL = 64
-# 1: q4_0 / q8_0 linear weights stay in block form in HBM and the GEMMs dequantise them in shared
-# memory (engine option weights_quantised); 0: dequantised to f16 at load (--weights-quantised)
-WEIGHTS_QUANTISED = 0
+# 1: q4_0 / q8_0 linear weights stay in block form in HBM and each layer's weight is dequantised into an
+# f16 staging buffer (L2-resident) before its GEMM; 2: the GEMM dequantises in shared memory; 0: f16 at load
+WEIGHTS_QUANTISED = 1
+WEIGHTS_DESC = {0: "f16, dequantised once at load",
+                1: "block form (q4_0 / q8_0 planes); each layer dequantised into an L2-resident f16 staging "
+                   "buffer right before its GEMM",
+                2: "block form; dequantised inside the GEMM's shared-memory stages"}
 # measured with ncu (one --set full capture of ViT block 0): mean DRAM read+write per launch of the
 # qkv / proj / fc1 / fc2 GEMMs of a ViT block at 8 frames per pass, and their algorithmic bytes
 GEMM_TRAFFIC_BYTES = 4.696e8
@@ -58,17 +65,16 @@ def load_pkg():
     return mod
 
 
-def rank_frames(per_gpu: int, rank: int) -> tuple[int, int]:
-    """Frames [first, first + per_gpu) encoded by `rank` (weak scaling: every rank encodes per_gpu frames
-    of its own; frame f keeps its seed on any world size)."""
-    return rank * per_gpu, per_gpu
-
-
 def shard_frames(total: int, rank: int, world: int) -> tuple[int, int]:
-    """Frames [first, first + count) encoded by `rank`: contiguous blocks whose
-    sizes differ by at most one; frame f keeps its seed on any world size."""
+    """Frames [first, first + count) encoded by `rank`: contiguous blocks whose sizes differ by at most one;
+    frame f keeps its seed on any world size."""
     first = total * rank // world
     return first, total * (rank + 1) // world - first
+
+
+def rank_frames(per_gpu: int, rank: int) -> tuple[int, int]:
+    """Frames [first, first + per_gpu) of `rank` when every rank encodes per_gpu frames of its own."""
+    return rank * per_gpu, per_gpu
 
 
 def max_over_ranks(x: float, world: int, device) -> float:
@@ -82,183 +88,49 @@ def max_over_ranks(x: float, world: int, device) -> float:
     return float(t.item())
 
 
-HIERA_FRAMES_PER_GPU = 16
-
-
-def bench_hiera(s3b, local: int, rank: int, world: int, steps: int, warmup: int, stream, device) -> dict:
-    """SAM 2.1 Hiera-T image encoder + FPN neck, q4_0 weights, a batch of 16 seeded
-    1024^2 frames per GPU (device-resident), CUDA events on the engine stream, max over ranks."""
-    import torch
-    import torch.distributed as dist
-    from sam3_b200 import synth
-    path = os.path.join(tempfile.gettempdir(), "s3b_bench_hiera_t_q4_0.ggml")
-    if local == 0 and not os.path.exists(path):
-        synth.write_sam2(path + ".tmp", synth.HIERA_T, seed=0, ftype=1, qtype=2, quantize=s3b.quantize_rows)
-        os.replace(path + ".tmp", path)
-    if world > 1:
-        dist.barrier()
-    eng = s3b.Engine(local)
-    eng.set_option("weights_quantised", WEIGHTS_QUANTISED)
-    eng.set_option("frames_per_pass", HIERA_FRAMES_PER_GPU)
-    eng.load_model(path)
-    n = HIERA_FRAMES_PER_GPU
-    frames = torch.from_numpy(synth.frames_u8(n, 1024, base_seed=1000 + rank * n)).to(device)
-    for _ in range(warmup):
-        eng.encode_u8(frames)
-    eng.sync()
-    eng.set_stream(stream.cuda_stream)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    eng.profile_begin(True)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        eng.encode_u8(frames)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    prof = eng.profile_end()
-    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
-    g, a = prof["gemm"], prof["attention"]
-    eng.set_stream(None)
-    eng.close()
-    return {"workload": f"configs[1]: SAM 2.1 Hiera-T image encoder + FPN neck, q4_0 weights, {n} seeded 1024^2 "
-                        f"frames per GPU (device-resident) x {world} GPU(s)",
-            "value": n * world / (ms / 1000.0), "unit": "frames/s", "ms_per_step": ms,
-            "gemm_tflops": g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0,
-            "gemm_ms_per_step": g["ms"] / steps,
-            "attention_tflops": a["flops"] / (a["ms"] / 1000.0) / 1e12 if a["ms"] > 0 else 0.0,
-            "attention_ms_per_step": a["ms"] / steps,
-            "algorithmic_tflop_per_step": (g["flops"] + a["flops"]) / steps / 1e12,
-            "gpu_launches_per_step": prof["launches"] / steps}
-
-
-def bench_video(s3b, local: int, rank: int, world: int, steps: int, warmup: int, stream, device) -> dict:
-    """SAM 2.1 Hiera-L image encoder + FPN neck, q8_0 weights, 64 seeded 1024^2 frames
-    sharded over the GPUs (frames/s of the job, max over ranks); then, on rank 0 (the tracking GPU), memory
-    attention per frame: 4 layers, d = 256, 64x64 current tokens from the encoder's level-2 map, cross-attention
-    to 7 memory frames of 64x64 tokens + 16 object pointers x 4 tokens (M = 28736, random memory bank)."""
-    import dataclasses
-
-    import torch
-    import torch.distributed as dist
-    from sam3_b200 import synth
-    cfg = dataclasses.replace(synth.HIERA_L, with_mem_attn=True)
-    path = os.path.join(tempfile.gettempdir(), "s3b_bench_hiera_l_q8_0.ggml")
-    if local == 0 and not os.path.exists(path):
-        synth.write_sam2(path + ".tmp", cfg, seed=0, ftype=1, qtype=8, quantize=s3b.quantize_rows)
-        os.replace(path + ".tmp", path)
-    if world > 1:
-        dist.barrier()
-    eng = s3b.Engine(local)
-    eng.set_option("weights_quantised", WEIGHTS_QUANTISED)
-    eng.load_model(path)
-    first, nf = rank_frames(FRAMES_TOTAL, rank)
-    frames = torch.from_numpy(synth.frames_u8(nf, 1024, base_seed=1000 + first)).to(device)
-    for _ in range(warmup):
-        eng.encode_u8(frames)
-    eng.sync()
-    eng.set_stream(stream.cuda_stream)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    eng.profile_begin(True)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        eng.encode_u8(frames)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    prof = eng.profile_end()
-    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
-    g, a = prof["gemm"], prof["attention"]
-    out = {"workload": f"configs[4]: SAM 2.1 Hiera-L image encoder + FPN neck, q8_0 weights, {FRAMES_TOTAL} seeded "
-                       f"1024^2 frames per GPU x {world} GPU(s); memory attention per frame on GPU 0",
-           "encoder_frames_per_s": FRAMES_TOTAL * world / (ms / 1000.0), "encoder_ms_per_step": ms,
-           "encoder_gemm_tflops": g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0,
-           "encoder_attention_tflops": a["flops"] / (a["ms"] / 1000.0) / 1e12 if a["ms"] > 0 else 0.0}
-    # hand-off of per-frame features to the tracking GPU (rank 0): every other rank copies its frame 0's
-    # neck_trk_2 (the memory-attention input) into its slot of a rank-0 buffer opened through CUDA IPC
-    # (s3b_peer_copy_output over NVLink); rank 0 then runs memory attention on the frame rank 1 encoded
-    ne = eng.output_shape("neck_trk_2")
-    fbytes = ne[0] * ne[1] * ne[2] * 4
-    recv = None
+def barrier(world):
     if world > 1:
         import torch.distributed as dist
-        if rank == 0:
-            recv = eng.device_alloc(fbytes * (world - 1))
-            handle = [eng.ipc_export(recv)]
-        else:
-            handle = [None]
-        dist.broadcast_object_list(handle, src=0)
-        ms_copy = 0.0
-        if rank > 0:
-            ptr = eng.ipc_open(handle[0])
-            dst = ptr + (rank - 1) * fbytes
-            for _ in range(warmup):
-                eng.peer_copy_output("neck_trk_2", 0, dst, 0, fbytes)
-            eng.sync()
-            e0.record(stream)
-            for _ in range(steps):
-                eng.peer_copy_output("neck_trk_2", 0, dst, 0, fbytes)
-            e1.record(stream)
-            torch.cuda.synchronize()
-            ms_copy = e0.elapsed_time(e1) / steps
-            eng.ipc_close(ptr)
         dist.barrier()
-        t = max_over_ranks(ms_copy, world, device)
-        out["p2p_neck_trk_2"] = {"bytes_per_frame": fbytes, "senders": world - 1, "ms_per_copy_max": t,
-                                 "gbs_per_sender": fbytes / (t / 1000.0) / 1e9 if t > 0 else None,
-                                 "path": "s3b_peer_copy_output into a rank-0 buffer opened with s3b_ipc_open"}
-    if rank == 0:
-        # current frame = frame 0 of rank 1 (received above) or of this rank's own batch; its PE; random
-        # memory bank and pointer tokens
-        if recv is not None:
-            curr = torch.as_tensor(_CudaArray(recv, fbytes // 4), device=device).view(-1, 256)
-        else:
-            curr = torch.from_numpy(eng.output("neck_trk_2", 0).reshape(-1, 256)).to(device)
-        pos = torch.from_numpy(eng.output("neck_trk_pe_2", 0).reshape(-1, 256)).to(device)
-        g2 = torch.Generator(device=device).manual_seed(5)
-        m_total, n_ptr = cfg.num_maskmem * 4096 + cfg.max_obj_ptrs * 4, cfg.max_obj_ptrs * 4
-        prompt = torch.randn(m_total, 64, device=device, generator=g2)
-        prompt_pos = torch.randn(m_total, 64, device=device, generator=g2) * 0.1
-        res = torch.empty_like(curr)
-        # timed without per-launch profiling (the layers replay from a CUDA graph from the second call on);
-        # one more profiled pass gives the algorithmic FLOPs and the attention kernels' share
-        for _ in range(max(warmup, 2)):
-            eng.mem_attn(curr, pos, 64, prompt, prompt_pos, n_ptr, out=res)
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(steps):
-            eng.mem_attn(curr, pos, 64, prompt, prompt_pos, n_ptr, out=res)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        mms = e0.elapsed_time(e1) / steps
-        eng.profile_begin(True)
-        eng.mem_attn(curr, pos, 64, prompt, prompt_pos, n_ptr, out=res)
-        torch.cuda.synchronize()
-        p2 = eng.profile_end()
-        fl = p2["gemm"]["flops"] + p2["attention"]["flops"]
-        out.update({"mem_attn_ms_per_frame": mms, "mem_attn_tflop_per_frame": fl / 1e12,
-                    "mem_attn_tflops": fl / (mms / 1000.0) / 1e12,
-                    "mem_attn_attention_tflops": p2["attention"]["flops"] / (p2["attention"]["ms"] / 1000.0) / 1e12
-                    if p2["attention"]["ms"] > 0 else 0.0,
-                    "mem_attn_timing": "CUDA events around the timed calls, no per-launch profiling; the layers "
-                                       "replay from a CUDA graph",
-                    "mem_attn_memory_tokens": m_total,
-                    "mem_attn_input": "frame 0 of rank 1 (peer-copied)" if recv is not None else "own frame 0"})
-        if recv is not None:
-            eng.device_free(recv)
-    eng.set_stream(None)
-    eng.close()
-    return out
 
 
 class _CudaArray:
     """Zero-copy view of engine-owned device memory for torch.as_tensor (the CUDA array interface)."""
 
-    def __init__(self, ptr: int, n: int):
-        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+    def __init__(self, ptr: int, n: int, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3}
+
+
+def model_file(s3b, kind: str) -> str:
+    """Seeded synthetic .ggml files of the configurations (written once per box under the temp dir)."""
+    import dataclasses
+    from sam3_b200 import synth
+    path = os.path.join(tempfile.gettempdir(), f"s3b_bench_{kind}.ggml")
+    if os.path.exists(path):
+        return path
+    tmp = path + f".tmp{os.getpid()}"
+    if kind in ("vit_q4_0", "vit_q8_0", "vit_f16"):
+        qtype = {"vit_q4_0": 2, "vit_q8_0": 8, "vit_f16": None}[kind]
+        synth.write_sam3(tmp, synth.SAM3_VIT_L, seed=0, ftype=1, qtype=qtype, quantize=s3b.quantize_rows)
+    elif kind in ("hiera_t_q4_0", "hiera_t_f16"):
+        synth.write_sam2(tmp, synth.HIERA_T, seed=0, ftype=1, qtype=2 if kind == "hiera_t_q4_0" else None,
+                         quantize=s3b.quantize_rows)
+    elif kind == "hiera_l_q8_0":
+        synth.write_sam2(tmp, dataclasses.replace(synth.HIERA_L, with_mem_attn=True), seed=0, ftype=1, qtype=8,
+                         quantize=s3b.quantize_rows)
+    else:
+        raise ValueError(kind)
+    os.replace(tmp, path)
+    return path
+
+
+def prepare_models(s3b, kinds, local, world):
+    """Local rank 0 writes the model files; the other ranks wait for them."""
+    if local == 0:
+        for k in kinds:
+            model_file(s3b, k)
+    barrier(world)
+    return {k: model_file(s3b, k) for k in kinds}
 
 
 def vit_flops_per_frame(cfg, with_neck=True):
@@ -332,70 +204,428 @@ def measured_peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def make_model(s3b, workload: str, path: str):
-    from sam3_b200 import synth
-    cfg = synth.SAM3_VIT_L
-    qtype = {"vit_q4_0": 2, "vit_q8_0": 8, "vit_f16": None}[workload]
-    synth.write_sam3(path, cfg, seed=0, ftype=1, qtype=qtype, quantize=s3b.quantize_rows)
-    return cfg
+def tflops(part):
+    return part["flops"] / (part["ms"] / 1000.0) / 1e12 if part["ms"] > 0 else 0.0
 
 
-def cpu_sample(workload: str, steps: int = 1):
-    """Times the oracle (numpy, all host threads) on a bounded sample of one
-    frame: prefix + one windowed block + one global block + the tracker neck,
-    and extrapolates to frames/s (28 windowed + 4 global blocks)."""
-    s3b = load_pkg()
+# ---------------------------------------------------------------- CPU reference (oracle port)
+def cpu_reference(workload: str, steps: int, warmup: int) -> dict:
+    """Times the CPU restatement of the path (oracle, numpy; BLAS on every host core) on configs[3]'s
+    per-frame forward, for real: one step = one eighth of a frame's forward, four of the 32 ViT blocks
+    in order (the prefix rides with the first eighth, the tracker neck with the last), so eight steps
+    compute one complete frame. The reference's own CPU backend (ggml) is not in the checkout."""
+    from threadpoolctl import threadpool_limits
+    cores = os.cpu_count() or 1
     sys.path.insert(0, ROOT)
+    load_pkg()
     from oracle import quant as oq
     from oracle import vit as ov
     from sam3_b200 import synth
     cfg = synth.SAM3_VIT_L
     qtype = {"vit_q4_0": 2, "vit_q8_0": 8, "vit_f16": None}[workload]
-    rng_cfg = synth.Sam3Config(depth=8, global_idx=(7,))  # blocks 0 (windowed) and 7 (global)
-    T = synth.sam3_tensors(rng_cfg, seed=0)
-    T = {k: v for k, v in T.items() if not k.startswith("vit.blocks.") or k.split(".")[2] in ("0", "7")}
-    W = synth.stored_values(T, 1, qtype, oq.quantize, oq.dequantize)
-    chw = ov.preprocess_u8(synth.frames_u8(1, cfg.img_size))
-    vals = []
-    parts = None
-    for _ in range(steps):
+    t_setup = time.perf_counter()
+    W = synth.stored_values(synth.sam3_tensors(cfg, seed=0), 1, qtype, oq.quantize, oq.dequantize)
+    setup_s = time.perf_counter() - t_setup
+    per = cfg.depth // 8
+
+    state = {"x": None, "frame": 0}
+
+    def eighth(e):
+        if e == 0:
+            chw = ov.preprocess_u8(synth.frames_u8(1, cfg.img_size, base_seed=1000 + state["frame"]))
+            state["x"] = ov.prefix(W, chw, cfg)
+        for b in range(e * per, (e + 1) * per):
+            state["x"] = ov.block(W, state["x"], b, cfg)
+        if e == 7:
+            ov.neck(W, state["x"])
+            state["frame"] += 1
+
+    with threadpool_limits(limits=cores):
+        for k in range(warmup):
+            eighth(k % 8)
+        # the timed steps start a fresh frame
+        step_s = []
         t0 = time.perf_counter()
-        x = ov.prefix(W, chw, cfg)
-        t1 = time.perf_counter()
-        x = ov.block(W, x, 0, rng_cfg)
-        t2 = time.perf_counter()
-        x = ov.block(W, x, 7, rng_cfg)
-        t3 = time.perf_counter()
-        ov.neck(W, x)
-        t4 = time.perf_counter()
-        t_frame = (t1 - t0) + 28 * (t2 - t1) + 4 * (t3 - t2) + (t4 - t3)
-        vals.append(1.0 / t_frame)
-        parts = {"prefix_s": t1 - t0, "win_block_s": t2 - t1, "global_block_s": t3 - t2, "neck_s": t4 - t3}
-    return float(np.median(vals)), parts
+        for k in range(steps):
+            t = time.perf_counter()
+            eighth(k % 8)
+            step_s.append(time.perf_counter() - t)
+        total = time.perf_counter() - t0
+    frames = steps / 8.0
+    return {"value": frames / total, "ms_per_step": 1000.0 * total / steps, "total_s": total, "frames": frames,
+            "cores": cores, "setup_s": setup_s,
+            "sample": f"{steps} timed eighths of the SAM 3 ViT-L + tracker-neck forward ({frames:g} frame(s)), "
+                      f"each eighth 4 of the 32 blocks in order (prefix with the first, neck with the last); "
+                      f"per-step seconds min {min(step_s):.2f} max {max(step_s):.2f}; oracle (numpy f32, "
+                      f"BLAS threads = {cores}); weights {workload.split('_', 1)[1]} (dequantised)"}
 
 
+# ---------------------------------------------------------------- GPU measurements
+def bench_vit(s3b, path, args, rank, world, local, stream) -> dict:
+    """64 frames split 64/N; device-resident timing, then e2e through the public API."""
+    import torch
+    from sam3_b200 import synth
+    cfg = synth.SAM3_VIT_L
+    first, nf = shard_frames(args.frames, rank, world)
+    eng = s3b.Engine(local)
+    eng.set_option("weights_quantised", args.weights_quantised)
+    eng.set_option("frames_per_pass", min(args.frames_per_pass, max(nf, 1)))
+    eng.set_option("gemm_pairs", args.gemm_pairs)
+    t0 = time.time()
+    eng.load_model(path)
+    load_s = time.time() - t0
+    host = synth.frames_u8(nf, cfg.img_size, base_seed=1000 + first)
+    host_t = torch.from_numpy(host).pin_memory()
+    dev = host_t.cuda()
+    for _ in range(args.warmup):
+        eng.encode_u8(dev)
+    eng.sync()
+
+    # --- timed region (device-resident inputs), profiled with CUDA events on the engine stream
+    eng.set_stream(stream.cuda_stream)
+    clocks = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    eng.profile_begin(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        eng.encode_u8(dev)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    prof = eng.profile_end()
+    clk = clocks.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world, "cuda")
+    value = args.frames / (ms / 1000.0)
+
+    # --- end to end through the public API: pinned host frames in, neck_trk_0..2 (f32) of every frame out
+    G = cfg.grid
+    sizes = [4 * G, 2 * G, G]
+    outs = {f"neck_trk_{i}": torch.empty(nf, S, S, cfg.neck_dim, dtype=torch.float32).pin_memory()
+            for i, S in enumerate(sizes)}
+    for n, t in outs.items():
+        eng.output_host_bind(n, t)
+    eng.encode_u8(host_t.numpy())  # one untimed call with the bindings in place
+    eng.sync()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host_np = host_t.numpy()
+    ev2.record(stream)
+    for _ in range(args.steps):
+        eng.encode_u8(host_np)  # H2D inside the public call; outputs land in `outs` per pass
+    eng.sync()  # the last pass's read-back included
+    ev3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(ev2.elapsed_time(ev3) / args.steps, world, "cuda")
+    # the read-back is the real output: spot-check one frame against s3b_output_copy
+    readback_ok = bool(np.array_equal(outs["neck_trk_2"][nf - 1].numpy(), eng.output("neck_trk_2", nf - 1)))
+    for n in outs:
+        eng.output_host_bind(n, None)
+    d2h = sum(int(t.numel()) * 4 for t in outs.values())
+
+    peak_burst, peak_sust, hbm, src = measured_peaks()
+    g, a, ln, wst = prof["gemm"], prof["attention"], prof["layernorm"], prof["weight_staging"]
+    gemm_tf = tflops(g)
+    fl_gemm, fl_attn, fl_neck = vit_flops_per_frame(cfg)
+    line = {
+        "value": value, "ms_per_step": ms,
+        "e2e": {"value": args.frames / (e2e_ms / 1000.0), "unit": "frames/s", "h2d_bytes_per_step": int(host.nbytes),
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "outputs_read_back": "neck_trk_0, neck_trk_1, neck_trk_2 (f32, every frame), via s3b_output_host_bind",
+                "readback_matches_output_copy": readback_ok},
+        "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak_sust, "unit": "TFLOP/s",
+                     "frac": gemm_tf / peak_sust,
+                     # DRAM bytes per GEMM launch (read + write), mean of the four block-0 GEMMs at 8 frames
+                     # from one ncu capture of ViT block 0; algorithmic 5.0e8
+                     "traffic": GEMM_TRAFFIC_BYTES, "traffic_algorithmic": GEMM_ALG_BYTES,
+                     "kernel": "gemm_f16_tc_kernel (tcgen05/TMEM, TMA)",
+                     "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
+                     "gemm_ms_per_step": g["ms"] / args.steps, "gemm_launches_per_step": g["launches"] / args.steps},
+        "attention": {"achieved_tflops": tflops(a), "ms_per_step": a["ms"] / args.steps,
+                      "frac_of_peak": tflops(a) / peak_sust},
+        "layernorm": {"achieved_gbs": ln["bytes"] / (ln["ms"] / 1000.0) / 1e9 if ln["ms"] > 0 else 0.0,
+                      "peak_gbs": hbm, "frac_of_peak": (ln["bytes"] / (ln["ms"] / 1000.0) / 1e9 / hbm)
+                      if ln["ms"] > 0 else 0.0, "ms_per_step": ln["ms"] / args.steps,
+                      "launches_per_step": ln["launches"] / args.steps,
+                      "bound": "hbm (algorithmic bytes: f32 rows in + f16 rows out)"},
+        "weight_staging": {"ms_per_step": wst["ms"] / args.steps, "launches_per_step": wst["launches"] / args.steps,
+                           "achieved_gbs": wst["bytes"] / (wst["ms"] / 1000.0) / 1e9 if wst["ms"] > 0 else 0.0,
+                           "what": "block-form weight planes read from HBM, f16 staging written (L2)"},
+        "whole_step_tflops": (fl_gemm + fl_attn + fl_neck) * value / 1e12, "flops_per_frame": fl_gemm + fl_attn + fl_neck,
+        "gpu_launches": int(prof["launches"]), "clocks": clk,
+        "setup": {"load_s": load_s, "weights_mib": eng.model_info()["weights_mib"], "frames_this_rank": nf}}
+    eng.set_stream(None)
+    eng.close()
+    return line
+
+
+def bench_latency(s3b, path, label, img, args, rank, world, local, stream) -> dict:
+    """Batch-1 latency: one frame per call, K calls back to back (device-resident frame)."""
+    import torch
+    from sam3_b200 import synth
+    eng = s3b.Engine(local)
+    eng.set_option("frames_per_pass", 1)
+    eng.load_model(path)
+    frame = torch.from_numpy(synth.frames_u8(1, img, base_seed=1000 + rank)).cuda()
+    for _ in range(args.warmup):
+        eng.encode_u8(frame)
+    eng.sync()
+    eng.set_stream(stream.cuda_stream)
+    barrier(world)
+    torch.cuda.synchronize()
+    eng.profile_begin(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        eng.encode_u8(frame)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prof = eng.profile_end()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, "cuda")
+    eng.set_stream(None)
+    eng.close()
+    g, a = prof["gemm"], prof["attention"]
+    return {"workload": label, "latency_ms": ms, "frames_per_s_per_gpu": 1000.0 / ms,
+            "gemm_tflops": tflops(g), "attention_tflops": tflops(a),
+            "algorithmic_tflop_per_frame": (g["flops"] + a["flops"]) / args.steps / 1e12,
+            "gpu_launches_per_frame": prof["launches"] / args.steps}
+
+
+HIERA_FRAMES_PER_GPU = 16
+
+
+def bench_hiera(s3b, path, args, rank, world, local, stream) -> dict:
+    """SAM 2.1 Hiera-T + FPN neck, q4_0, a batch of 16 seeded 1024^2 frames per GPU."""
+    import torch
+    from sam3_b200 import synth
+    eng = s3b.Engine(local)
+    eng.set_option("weights_quantised", args.weights_quantised)
+    eng.set_option("frames_per_pass", HIERA_FRAMES_PER_GPU)
+    eng.load_model(path)
+    n = HIERA_FRAMES_PER_GPU
+    frames = torch.from_numpy(synth.frames_u8(n, 1024, base_seed=1000 + rank * n)).cuda()
+    for _ in range(args.warmup):
+        eng.encode_u8(frames)
+    eng.sync()
+    eng.set_stream(stream.cuda_stream)
+    barrier(world)
+    torch.cuda.synchronize()
+    eng.profile_begin(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        eng.encode_u8(frames)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prof = eng.profile_end()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, "cuda")
+    g, a = prof["gemm"], prof["attention"]
+    eng.set_stream(None)
+    eng.close()
+    return {"workload": f"configs[1]: SAM 2.1 Hiera-T image encoder + FPN neck, q4_0 weights "
+                        f"({WEIGHTS_DESC[args.weights_quantised]}), {n} seeded 1024^2 frames per GPU "
+                        f"(device-resident) x {world} GPU(s)",
+            "value": n * world / (ms / 1000.0), "unit": "frames/s", "ms_per_step": ms,
+            "gemm_tflops": tflops(g), "gemm_ms_per_step": g["ms"] / args.steps,
+            "attention_tflops": tflops(a), "attention_ms_per_step": a["ms"] / args.steps,
+            "algorithmic_tflop_per_step": (g["flops"] + a["flops"]) / args.steps / 1e12,
+            "gpu_launches_per_step": prof["launches"] / args.steps}
+
+
+def bench_video(s3b, path, args, rank, world, local, stream) -> dict:
+    """Hiera-L q8_0 on 64 frames over N GPUs, then per-frame memory attention on the tracking GPU
+    (rank 0) from a device-resident memory bank (7 slots of 64x64x64 + 16 object pointers: M = 28,736).
+
+    Encoder throughput: every rank encodes its share of the 64 frames (64/N).
+    Pipeline (N > 1): ranks 1..N-1 encode the 64 frames of step k and copy each frame's neck_trk_2 (4 MB)
+    into rank 0's receive buffer k % 2 over NVLink (CUDA IPC + s3b_peer_copy_output); meanwhile rank 0 runs
+    memory attention on the 64 frames of step k - 1 from buffer (k - 1) % 2. A host barrier between steps
+    orders the two. With N = 1 one GPU does both, one after the other. Rate = 64 frames x K steps / the
+    slowest rank's time; the copies' contents are checked against the encoders' outputs."""
+    import torch
+    import torch.distributed as dist
+    from sam3_b200 import synth
+    cfg = synth.HIERA_L
+    eng = s3b.Engine(local)
+    eng.set_option("weights_quantised", args.weights_quantised)
+    eng.load_model(path)
+    out = {"workload": f"configs[4]: SAM 2.1 Hiera-L image encoder + FPN neck, q8_0 weights "
+                       f"({WEIGHTS_DESC[args.weights_quantised]}), {FRAMES_TOTAL} seeded 1024^2 frames over "
+                       f"{world} GPU(s); memory attention per frame on GPU 0 from a device memory bank"}
+
+    # --- encoder throughput (every rank its 64/N share)
+    first, nf = shard_frames(FRAMES_TOTAL, rank, world)
+    frames = torch.from_numpy(synth.frames_u8(nf, 1024, base_seed=1000 + first)).cuda()
+    for _ in range(args.warmup):
+        eng.encode_u8(frames)
+    eng.sync()
+    eng.set_stream(stream.cuda_stream)
+    barrier(world)
+    torch.cuda.synchronize()
+    eng.profile_begin(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        eng.encode_u8(frames)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prof = eng.profile_end()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, "cuda")
+    out.update({"encoder_frames_per_s": FRAMES_TOTAL / (ms / 1000.0), "encoder_ms_per_step": ms,
+                "encoder_gemm_tflops": tflops(prof["gemm"]), "encoder_attention_tflops": tflops(prof["attention"])})
+
+    # --- memory bank on the tracking GPU (random, seeded): 7 slots [4096][64], 16 pointers [256]
+    feat, n_slots, n_ptrs = 64, cfg.num_maskmem, cfg.max_obj_ptrs
+    fbytes = feat * feat * 256 * 4
+    slot_tpos = [n_slots - s for s in range(n_slots)]  # n_sel - s, no conditioning frame
+    ptr_tpos = list(range(1, n_ptrs + 1))
+    if rank == 0:
+        g2 = torch.Generator(device="cuda").manual_seed(5)
+        bank = [torch.randn(feat * feat, 64, device="cuda", generator=g2) for _ in range(n_slots)]
+        ptrs = torch.randn(n_ptrs, 256, device="cuda", generator=g2)
+        curr0 = torch.from_numpy(eng.output("neck_trk_2", 0).reshape(-1, 256)).cuda()
+        res = torch.empty_like(curr0)
+        for _ in range(max(args.warmup, 2)):
+            eng.mem_attn_bank(curr0, feat, bank, slot_tpos, ptrs, ptr_tpos, out=res)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            eng.mem_attn_bank(curr0, feat, bank, slot_tpos, ptrs, ptr_tpos, out=res)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        mms = e0.elapsed_time(e1) / args.steps
+        eng.profile_begin(True)
+        eng.mem_attn_bank(curr0, feat, bank, slot_tpos, ptrs, ptr_tpos, out=res)
+        torch.cuda.synchronize()
+        p2 = eng.profile_end()
+        fl = p2["gemm"]["flops"] + p2["attention"]["flops"]
+        out.update({"mem_attn_ms_per_frame": mms, "mem_attn_tflop_per_frame": fl / 1e12,
+                    "mem_attn_tflops": fl / (mms / 1000.0) / 1e12, "mem_attn_attention_tflops": tflops(p2["attention"]),
+                    "mem_attn_memory_tokens": n_slots * feat * feat + 4 * n_ptrs,
+                    "mem_attn_timing": "CUDA events around the timed calls (s3b_mem_attn_bank: prompt built on the "
+                                       "device from the bank, layers replayed from a CUDA graph)"})
+
+    # --- the pipeline
+    encoders = list(range(1, world)) if world > 1 else [0]
+    e_idx = encoders.index(rank) if rank in encoders else -1
+    efirst, enf = shard_frames(FRAMES_TOTAL, e_idx, len(encoders)) if e_idx >= 0 else (0, 0)
+    if enf:
+        eframes = torch.from_numpy(synth.frames_u8(enf, 1024, base_seed=1000 + efirst)).cuda()
+    recv = None
+    if rank == 0:
+        recv = eng.device_alloc(2 * FRAMES_TOTAL * fbytes)
+        handle = [eng.ipc_export(recv)] if world > 1 else [None]
+    else:
+        handle = [None]
+    if world > 1:
+        dist.broadcast_object_list(handle, src=0)
+    dst_base = recv if rank == 0 else eng.ipc_open(handle[0])
+
+    def encode_step(k):
+        if not enf:
+            return
+        eng.encode_u8(eframes)
+        buf = dst_base + (k % 2) * FRAMES_TOTAL * fbytes
+        for f in range(enf):
+            eng.peer_copy_output("neck_trk_2", f, buf + (efirst + f) * fbytes, 0, fbytes)
+
+    def track_step(k):
+        buf = recv + (k % 2) * FRAMES_TOTAL * fbytes
+        for f in range(FRAMES_TOTAL):
+            curr = torch.as_tensor(_CudaArray(buf + f * fbytes, feat * feat * 256), device="cuda").view(-1, 256)
+            eng.mem_attn_bank(curr, feat, bank, slot_tpos, ptrs, ptr_tpos, out=res)
+
+    def pipeline_step(k, last_k):
+        if world == 1:
+            encode_step(k)
+            track_step(k)
+        else:
+            if k <= last_k:
+                encode_step(k)
+            if rank == 0 and k > 0:
+                track_step(k - 1)
+        eng.sync()
+        barrier(world)
+
+    n_warm = max(args.warmup, 2)
+    for k in range(n_warm):
+        pipeline_step(k, 10 ** 9)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    steps = args.steps
+    for k in range(n_warm, n_warm + steps):
+        pipeline_step(k, 10 ** 9)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    pms = max_over_ranks(e0.elapsed_time(e1) / steps, world, "cuda")
+    # content check: the frames rank 0 tracked in the last step came from the encoders' last outputs
+    last = n_warm + steps - 1  # buffer last % 2 holds the frames encoded in step `last`
+    sums = []
+    if enf:
+        for f in range(enf):
+            p = eng.output_device_ptr("neck_trk_2", f)
+            v = torch.as_tensor(_CudaArray(p, feat * feat * 256, "<i4"), device="cuda")
+            sums.append((efirst + f, int(v.to(torch.int64).sum().item())))
+    all_sums = [None] * world
+    if world > 1:
+        dist.all_gather_object(all_sums, sums)
+    else:
+        all_sums = [sums]
+    ok = None
+    if rank == 0:
+        buf = recv + (last % 2) * FRAMES_TOTAL * fbytes
+        ok = True
+        n_checked = 0
+        for part in all_sums:
+            for f, sref in part:
+                v = torch.as_tensor(_CudaArray(buf + f * fbytes, feat * feat * 256, "<i4"), device="cuda")
+                ok = ok and int(v.to(torch.int64).sum().item()) == sref
+                n_checked += 1
+        ok = ok and n_checked == FRAMES_TOTAL
+    barrier(world)
+    if rank != 0:
+        eng.ipc_close(dst_base)
+    barrier(world)
+    if rank == 0:
+        enc_ms = ms if world == 1 else None
+        out.update({"pipeline_frames_per_s": FRAMES_TOTAL / (pms / 1000.0), "pipeline_ms_per_step": pms,
+                    "pipeline": ("one GPU: encode 64 frames, then 64 memory-attention calls" if world == 1 else
+                                 f"{len(encoders)} encoder GPU(s) -> NVLink peer copies (CUDA IPC) -> tracking GPU 0, "
+                                 f"double-buffered, one host barrier per step"),
+                    "pipeline_limiter": ("encoder + memory attention in series on one GPU" if world == 1 else
+                                         ("memory attention on the tracking GPU"
+                                          if 64 * out["mem_attn_ms_per_frame"] >= pms * 0.8 else "encoders")),
+                    "p2p_content_check": "pass" if ok else "FAIL",
+                    "p2p_bytes_per_frame": fbytes})
+        if enc_ms is not None:
+            out["pipeline_encoder_ms"] = enc_ms
+        eng.device_free(recv)
+    eng.set_stream(None)
+    eng.close()
+    return out
+
+
+# ---------------------------------------------------------------- main
 def main():
-    global WEIGHTS_QUANTISED
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="vit_q4_0", choices=["vit_q4_0", "vit_q8_0", "vit_f16"])
-    ap.add_argument("--frames", type=int, default=FRAMES_TOTAL, help="frames per GPU")
+    ap.add_argument("--frames", type=int, default=FRAMES_TOTAL, help="frames of the batch (split over the GPUs)")
     ap.add_argument("--frames-per-pass", type=int, default=8)
     ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1, 2],
                     help="256-row GEMM tiles on SM pairs: 1 (default) for K >= 2048, 2 for all, 0 never")
-    ap.add_argument("--weights-quantised", type=int, default=WEIGHTS_QUANTISED, choices=[0, 1],
-                    help="1: quantised weights stay in block form in HBM, dequantised inside the GEMMs")
+    ap.add_argument("--weights-quantised", type=int, default=WEIGHTS_QUANTISED, choices=[0, 1, 2],
+                    help="1 (default): block form in HBM, staged per layer; 2: dequantised inside the GEMM; "
+                         "0: f16 at load")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-hiera", action="store_true", help="skip the Hiera-T (configs[1]) measurement")
-    ap.add_argument("--only-hiera", action="store_true",
-                    help="run only the Hiera-T (configs[1]) measurement and print its numbers (a profiling case)")
-    ap.add_argument("--no-video", action="store_true",
-                    help="skip the Hiera-L + memory attention (configs[4]) measurement")
+    ap.add_argument("--only", default="", help="comma list of extra lines to run (vit_f16_b1, hiera_t_f16_b1, "
+                                               "hiera_t_q4_0, video); 'none' for the headline only")
     args = ap.parse_args()
-    WEIGHTS_QUANTISED = args.weights_quantised
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -403,33 +633,26 @@ def main():
     n_gpus = max(world, 1)
     metric = "encoder frames/sec (SAM 3 ViT 1008^2 + SimpleFPN neck)"
     cfg_json = {"workload": f"configs[3]: SAM 3 ViT-L encoder + tracker neck, {args.workload.split('_', 1)[1]} "
-                            f"weights, {args.frames} seeded 1008^2 frames per GPU x {n_gpus} GPU(s)",
-                "frames_total": args.frames * n_gpus, "frames_per_gpu": args.frames,
-                "img_size": 1008,
+                            f"weights, a {args.frames}-frame batch of seeded 1008^2 frames split {args.frames}/N "
+                            f"over {n_gpus} GPU(s)",
+                "frames_total": args.frames, "frames_per_gpu": args.frames / n_gpus, "img_size": 1008,
                 "parallelism": f"frame-sharded x{n_gpus} (no collective)",
-                "weights_in_hbm": ("block form, dequantised inside the GEMMs" if args.weights_quantised
-                                   else "f16, dequantised once at load"),
+                "weights_in_hbm": WEIGHTS_DESC[args.weights_quantised],
                 "l2_flush": "inputs + activations per step >> 126 MB L2"}
 
     if args.impl == "reference":
-        # CPU restatement of the reference path (the reference's ggml CPU backend cannot be built here)
+        # the CPU restatement of the reference path (the reference's ggml CPU backend is not in the checkout)
         if rank != 0:
             return
-        steps = max(1, min(args.steps, 3))
-        for _ in range(min(args.warmup, 1)):
-            cpu_sample(args.workload, 1)
-        t0 = time.perf_counter()
-        v, parts = cpu_sample(args.workload, steps)
-        elapsed = time.perf_counter() - t0
-        ms = 1000.0 * args.frames / v
-        line = {"impl": "reference", "metric": metric, "value": v, "unit": "frames/s", "n_gpus": n_gpus,
-                "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": ms, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init)",
-                "config": cfg_json,
-                "cpu_baseline": {"value": v, "unit": "frames/s", "cores": os.cpu_count(), "kind": "port",
-                                 "sample": f"1 frame: prefix + 1 windowed + 1 global ViT block + tracker neck, "
-                                           f"extrapolated to 28+4 blocks; {steps} step(s), {elapsed:.1f} s; {parts}"},
-                "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        r = cpu_reference(args.workload, args.steps, args.warmup)
+        line = {"impl": "reference", "metric": metric, "value": r["value"], "unit": "frames/s", "n_gpus": n_gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded random-init weights, seeded uniform uint8 frames)", "config": cfg_json,
+                "cpu_baseline": {"value": r["value"], "unit": "frames/s", "cores": r["cores"], "kind": "port",
+                                 "sample": r["sample"]},
+                "e2e": {"value": r["value"], "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "setup_s": r["setup_s"]}
         print(json.dumps(line), flush=True)
         return
 
@@ -441,130 +664,42 @@ def main():
                                 timeout=__import__("datetime").timedelta(seconds=600))
     torch.cuda.set_device(local)
     s3b = load_pkg()
-    from sam3_b200 import synth
-
-    if args.only_hiera:
-        h = bench_hiera(s3b, local, rank, world, args.steps, args.warmup, torch.cuda.Stream(), "cuda")
-        if rank == 0:
-            print(json.dumps({"impl": "b200", "n_gpus": n_gpus, "steps": args.steps, "warmup": args.warmup,
-                              "hiera_t_q4_0": h}), flush=True)
-        if world > 1:
-            dist.destroy_process_group()
-        return
-
-    path = os.path.join(tempfile.gettempdir(), f"s3b_bench_{args.workload}.ggml")
+    extra = {"vit_f16_b1", "hiera_t_f16_b1", "hiera_t_q4_0", "video"}
+    if args.only == "none":
+        extra = set()
+    elif args.only:
+        extra = set(args.only.split(","))
+    kinds = [args.workload] + (["vit_f16"] if "vit_f16_b1" in extra and args.workload != "vit_f16" else []) + \
+        (["hiera_t_f16"] if "hiera_t_f16_b1" in extra else []) + (["hiera_t_q4_0"] if "hiera_t_q4_0" in extra else []) + \
+        (["hiera_l_q8_0"] if "video" in extra else [])
     t0 = time.time()
-    if local == 0 and not os.path.exists(path):
-        make_model(s3b, args.workload, path + ".tmp")
-        os.replace(path + ".tmp", path)
-    if world > 1:
-        dist.barrier()
-    cfg = synth.SAM3_VIT_L
+    paths = prepare_models(s3b, kinds, local, world)
     gen_s = time.time() - t0
-    eng = s3b.Engine(local)
-    eng.set_option("weights_quantised", WEIGHTS_QUANTISED)
-    eng.set_option("frames_per_pass", args.frames_per_pass)
-    eng.set_option("gemm_pairs", args.gemm_pairs)
-    t0 = time.time()
-    eng.load_model(path)
-    load_s = time.time() - t0
-
-    first, nf = rank_frames(args.frames, rank)
-    host = synth.frames_u8(nf, cfg.img_size, base_seed=1000 + first)
-    host_t = torch.from_numpy(host).pin_memory()
-    dev = host_t.cuda()
-    out_host = torch.empty((nf, 72, 72, 256), dtype=torch.float32).pin_memory()
-
-    def step_device():
-        eng.encode_u8(dev)
-
-    for _ in range(args.warmup):
-        step_device()
-    eng.sync()
-
-    # --- timed region (device-resident inputs), profiled with CUDA events on the engine stream
     stream = torch.cuda.Stream()
-    eng.set_stream(stream.cuda_stream)
-    clocks = ClockSampler(local)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    eng.profile_begin(True)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        step_device()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    prof = eng.profile_end()
-    clk = clocks.stop()
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world, "cuda")
-    value = args.frames * n_gpus / (ms / 1000.0)
 
-    # --- end-to-end through the public API with host buffers
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev2 = torch.cuda.Event(enable_timing=True)
-    ev3 = torch.cuda.Event(enable_timing=True)
-    out_np = out_host.numpy()
-    host_np = host_t.numpy()  # pinned host frames
-    ev2.record(stream)
-    for _ in range(args.steps):
-        eng.encode_u8(host_np)                      # H2D inside the public call
-        for f in range(nf):                         # D2H of the tracker-level map, per frame
-            eng.output("neck_trk_2", f, out=out_np[f])
-    ev3.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(ev2.elapsed_time(ev3) / args.steps, world, "cuda")
-    e2e = args.frames * n_gpus / (e2e_ms / 1000.0)
-
-    # --- roofline of the dominant kernel (tensor-core GEMM)
-    peak_burst, peak_sust, hbm, src = measured_peaks()
-    g = prof["gemm"]
-    gemm_tflops = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0
-    a = prof["attention"]
-    ln = prof["layernorm"]
-    attn_tflops = a["flops"] / (a["ms"] / 1000.0) / 1e12 if a["ms"] > 0 else 0.0
-    fl_gemm, fl_attn, fl_neck = vit_flops_per_frame(cfg)
-    total_tflops = (fl_gemm + fl_attn + fl_neck) * value / 1e12
-
-    line = {"metric": metric, "value": value, "unit": "frames/s", "n_gpus": n_gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16 (f32 accumulate)", "data": "synthetic (seeded random-init weights, seeded uniform uint8 frames)",
-            "config": cfg_json,
-            "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": int(host.nbytes),
-                    "d2h_bytes_per_step": int(out_host.numel() * 4)},
-            "roofline": {"bound": "tensor", "achieved": gemm_tflops, "peak": peak_sust, "unit": "TFLOP/s",
-                         "frac": gemm_tflops / peak_sust,
-                         # DRAM bytes per GEMM launch (read + write), mean of the four block-0 GEMMs at 8 frames
-                         # from one ncu capture of ViT block 0; algorithmic 5.0e8
-                         "traffic": GEMM_TRAFFIC_BYTES, "traffic_algorithmic": GEMM_ALG_BYTES,
-                         "kernel": "gemm_f16_tc_kernel (tcgen05/TMEM, TMA)",
-                         "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
-                         "gemm_ms_per_step": g["ms"] / args.steps, "gemm_launches_per_step": g["launches"] / args.steps},
-            "attention": {"achieved_tflops": attn_tflops, "ms_per_step": a["ms"] / args.steps,
-                          "frac_of_peak": attn_tflops / peak_sust},
-            "layernorm": {"achieved_gbs": ln["bytes"] / (ln["ms"] / 1000.0) / 1e9 if ln["ms"] > 0 else 0.0,
-                          "peak_gbs": hbm, "frac_of_peak": (ln["bytes"] / (ln["ms"] / 1000.0) / 1e9 / hbm)
-                          if ln["ms"] > 0 else 0.0, "ms_per_step": ln["ms"] / args.steps,
-                          "launches_per_step": ln["launches"] / args.steps,
-                          "bound": "hbm (algorithmic bytes: f32 rows in + f16 rows out)"},
-            "whole_step_tflops": total_tflops, "flops_per_frame": fl_gemm + fl_attn + fl_neck,
-            "gpu_launches": int(prof["launches"]), "clocks": clk,
-            "setup": {"model_gen_s": gen_s, "load_s": load_s, "weights_mib": eng.model_info()["weights_mib"]}}
-    eng.set_stream(None)
-    eng.close()
-    if not args.no_hiera:
-        line["hiera_t_q4_0"] = bench_hiera(s3b, local, rank, world, args.steps, args.warmup, stream, "cuda")
-    if not args.no_video:
-        line["video_hiera_l_q8_0"] = bench_video(s3b, local, rank, world, args.steps, args.warmup, stream, "cuda")
+    v = bench_vit(s3b, paths[args.workload], args, rank, world, local, stream)
+    line = {"metric": metric, "value": v.pop("value"), "unit": "frames/s", "n_gpus": n_gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": v.pop("ms_per_step"), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 (f32 accumulate)",
+            "data": "synthetic (seeded random-init weights, seeded uniform uint8 frames)", "config": cfg_json}
+    line.update(v)
+    line["setup"]["model_gen_s"] = gen_s
+    if "vit_f16_b1" in extra:
+        line["vit_f16_b1"] = bench_latency(s3b, paths["vit_f16"], "configs[2]: SAM 3 ViT-L encoder + tracker neck, "
+                                           "f16 weights, batch 1 (one seeded 1008^2 frame per call)", 1008,
+                                           args, rank, world, local, stream)
+    if "hiera_t_f16_b1" in extra:
+        line["hiera_t_f16_b1"] = bench_latency(s3b, paths["hiera_t_f16"], "configs[0]: SAM 2.1 Hiera-T encoder + "
+                                               "FPN neck, f16 weights, batch 1 (one seeded 1024^2 frame per call)",
+                                               1024, args, rank, world, local, stream)
+    if "hiera_t_q4_0" in extra:
+        line["hiera_t_q4_0"] = bench_hiera(s3b, paths["hiera_t_q4_0"], args, rank, world, local, stream)
+    if "video" in extra:
+        line["video_hiera_l_q8_0"] = bench_video(s3b, paths["hiera_l_q8_0"], args, rank, world, local, stream)
     if rank == 0 and not args.no_cpu_baseline and world == 1:
-        v, parts = cpu_sample(args.workload, 1)
-        line["cpu_baseline"] = {"value": v, "unit": "frames/s", "cores": os.cpu_count(), "kind": "port",
-                                "sample": f"oracle (numpy) on 1 frame: prefix + 1 windowed + 1 global block + "
-                                          f"tracker neck, extrapolated to 28+4 blocks; {parts}"}
+        r = cpu_reference(args.workload, 8, 1)
+        line["cpu_baseline"] = {"value": r["value"], "unit": "frames/s", "cores": r["cores"], "kind": "port",
+                                "sample": r["sample"]}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -72,10 +72,13 @@ int s3b_sync(s3b_ctx* ctx);
  * applies to every context of the process);
  * "gemm_wide_epilogue" (1, default: GEMMs with K < 2048 run 16 epilogue
  * warps instead of 8; 0: all run 8; process-wide);
- * "weights_quantised" (read by s3b_load_model; 1: q4_0 / q8_0 linear
- * weights stay in block form in device memory and the GEMMs dequantise each
- * weight tile in shared memory; 0, default: they are dequantised to f16 once
- * at load; results are identical);
+ * "weights_quantised" (read by s3b_load_model; q4_0 / q8_0 linear weights
+ * stay in block form in device memory, read from HBM only in that form:
+ * 1: right before each GEMM one kernel dequantises the layer's weight into
+ * an f16 staging buffer sized for the largest layer, which stays in L2 while
+ * the unchanged f16 GEMM reads it; 2: the GEMM's own warps dequantise each
+ * weight tile in shared memory; 0, default: dequantised to f16 once at load;
+ * results are identical in all three);
  * "conv_implicit" (1, default: 3x3 convolutions with C a multiple of 64 run
  * as implicit GEMMs whose TMA loads fetch the shifted pixel blocks, no
  * column matrix, and the neck's 2x2 deconvolutions store their outputs
@@ -95,11 +98,12 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value);
 /* Profiling (CUDA events on the context stream around every GEMM, attention
  * and LayerNorm launch; the reference times compute with std::chrono around
  * ggml_backend_graph_compute, sam3.cpp:6118-6131). s3b_profile_end waits for
- * the stream and writes the first n (up to 13) of: out[0..3] GEMM {launches,
+ * the stream and writes the first n (up to 17) of: out[0..3] GEMM {launches,
  * ms, flops, bytes}, out[4..7] attention {launches, ms, flops, bytes},
  * out[8] the total number of kernel launches since s3b_profile_begin,
- * out[9..12] LayerNorm {launches, ms, 0, bytes}. Bytes and flops are
- * algorithmic (operands and results once). */
+ * out[9..12] LayerNorm {launches, ms, 0, bytes}, out[13..16] block-form
+ * weight staging {launches, ms, 0, bytes}. Bytes and flops are algorithmic
+ * (operands and results once). */
 int s3b_profile_begin(s3b_ctx* ctx, int with_events);
 int s3b_profile_end(s3b_ctx* ctx, double* out, int n);
 
@@ -157,8 +161,22 @@ int s3b_encode_chw_device(s3b_ctx* ctx, const float* d_frames_chw, int n_frames,
 int s3b_output_shape(s3b_ctx* ctx, const char* name, int64_t ne[4]);
 /* Copies frame `frame` of an output to host memory (n floats). */
 int s3b_output_copy(s3b_ctx* ctx, const char* name, int frame, float* dst, int64_t n);
-/* Device pointer of frame `frame` of an output (valid until the next encode). */
+/* Device pointer of frame `frame` of an output (valid until the next encode;
+ * the "neck_*_pe_i" outputs are one device table per size, the same for
+ * every frame, valid until the context is destroyed). */
 int s3b_output_device_ptr(s3b_ctx* ctx, const char* name, int frame, const float** dptr);
+
+/* Binds host memory (`n_floats` floats, pinned by the caller for the copies
+ * to overlap) to output `name` ("vit_output", "neck_trk_i", "neck_det_i"):
+ * every later encode call copies each pass's frames of that output (f32,
+ * frame f at host + f * frame_elems) to it on a copy stream of the context,
+ * while the next pass computes; the next call's pass waits only for the copy
+ * of the frames it overwrites. s3b_sync waits for the copies. host = NULL
+ * unbinds. An encode call fails with S3B_ERR_ARG if a bound buffer is
+ * smaller than n_frames * frame_elems. This is the host hand-off of
+ * state.neck_trk that sam3_propagate_single does with ggml_backend_tensor_get
+ * (sam3.cpp:11378-11391), moved off the critical path. */
+int s3b_output_host_bind(s3b_ctx* ctx, const char* name, float* host, int64_t n_floats);
 
 /* ---------------------------------------------------------------- features to the tracking GPU */
 
@@ -202,6 +220,49 @@ int s3b_ipc_close(s3b_ctx* ctx, void* dptr);
  * pointers, 0 if they are host pointers. */
 int s3b_mem_attn(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const float* prompt,
                  const float* prompt_pos, int m_total, int n_ptr_tokens, float* out, int device_ptrs);
+
+/* Memory attention with the memory prompt built on the device from a
+ * memory bank in device memory: replaces sam3_build_prompt_and_pos
+ * (sam3.cpp:9123-9209) + sam3_build_mem_attn_graph (9224-9337) as
+ * sam3_propagate_single calls them (11182-11307), with no host loop, host
+ * GEMV or host-to-device copy of the prompt. All pointers are device
+ * pointers except the int arrays and the two pointer arrays themselves:
+ *   curr [N][256], N = feat^2; src_pos [N][256] or NULL (the engine's sine
+ *     PE of the feat x feat grid, tracker.cached_sinpe_256);
+ *   slot_feats[s]: [N][64] f32 spatial memory features of selected slot s
+ *     (s < n_slots <= 16, in prompt order); slot_pes[s]: [N][64] or NULL
+ *     (the 64-channel sine PE, tracker.cached_sinpe_64); slot_pes may be NULL;
+ *   slot_tpos[s]: temporal position (0 = conditioning frame); when
+ *     0 <= tpos < num_maskmem the PE row maskmem_tpos_enc[num_maskmem -
+ *     tpos - 1] is added to the slot's PE;
+ *   obj_ptrs [n_ptrs][256] f32 (n_ptrs <= 16); ptr_tpos[p]: frame distance
+ *     of pointer p (< 0: skipped); each kept pointer becomes 4 tokens of 64
+ *     with the 256 -> 64 projection of the 1-D sine PE of distance / 15;
+ *   out [N][256].
+ * Results equal s3b_mem_attn on the prompt the reference builds. */
+int s3b_mem_attn_bank(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat,
+                      const float* const* slot_feats, const float* const* slot_pes, const int* slot_tpos, int n_slots,
+                      const float* obj_ptrs, const int* ptr_tpos, int n_ptrs, float* out);
+
+/* The device prompt build of s3b_mem_attn_bank alone: writes prompt and
+ * prompt_pos (device f32 [m_total][64], capacity_rows rows each) as
+ * sam3_build_prompt_and_pos (sam3.cpp:9123-9209) returns them, and
+ * m_total / n_ptr_tokens (either may be NULL). */
+int s3b_op_build_prompt(s3b_ctx* ctx, int feat, const float* const* slot_feats, const float* const* slot_pes,
+                        const int* slot_tpos, int n_slots, const float* obj_ptrs, const int* ptr_tpos, int n_ptrs,
+                        float* prompt, float* prompt_pos, int64_t capacity_rows, int* m_total, int* n_ptr_tokens);
+
+/* Host helper: memory-bank slots memory attention reads
+ * (sam3_select_memory_frames, sam3.cpp:9423-9447): every slot when
+ * bank_size <= max_slots, else the first, the last and max_slots - 2 evenly
+ * spaced ones, ascending and unique. Writes at most `capacity` indices and
+ * returns their count, or S3B_ERR_ARG. */
+int s3b_select_memory_frames(int bank_size, int max_slots, int* out_idx, int capacity);
+
+/* Host helper: sinusoidal 2D PE, channel-last [H][W][d_model], first half
+ * of the channels encoding y, second half x (sam3_sinusoidal_pe_2d,
+ * sam3.cpp:3597-3633); the values of the "neck_trk_pe_i" outputs. */
+int s3b_sine_pe_2d(int H, int W, int d_model, float* out);
 
 /* ---------------------------------------------------------------- operators (device pointers) */
 
@@ -289,6 +350,17 @@ int s3b_op_deconv2x2(s3b_ctx* ctx, const void* x, int B, int H, int W, int Cin, 
  * No counterpart in the reference (sam3.cpp always allocates through ggml). */
 int s3b_conv3x3_noalloc(const void* x, int B, int H, int W, int C, const void* w, const float* bias, float* out,
                         int Cout, void* cuda_stream);
+
+/* Device-side status of s3b_conv3x3_noalloc on the current device. The conv
+ * call only enqueues work, so a failure inside its kernels (a bounded wait
+ * that timed out, leaving `out` incomplete) cannot reach its return code;
+ * it is recorded in the error word of the static scratch instead. After the
+ * caller has waited for the stream of the last call (cudaStreamSynchronize),
+ * this reads the word: *code = 0 and S3B_OK when every wait finished, else
+ * *code = the kernel's code and S3B_ERR_DEVICE, and the word is cleared.
+ * S3B_ERR_CUDA if the word cannot be read. Allocates nothing (a 4-byte
+ * cudaMemcpyFromSymbol). No counterpart in the reference. */
+int s3b_conv3x3_noalloc_status(int* code);
 
 /* As s3b_op_gemm with B given as N rows of K values in q4_0 or q8_0 blocks
  * (device memory, ggml row layout; K a multiple of 32, N of 8): the rows are

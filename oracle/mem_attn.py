@@ -74,36 +74,64 @@ def mem_attn(W, curr, pos, feat, prompt, prompt_pos, n_ptr, taps=None, f16_input
 
 
 def one_d_sine_pe(pos, dim, temperature=10000.0):
-    """sam3_get_1d_sine_pe (sam3.cpp:3636-3647): first dim/2 sin, then cos."""
+    """sam3_get_1d_sine_pe (sam3.cpp:3636-3647): first dim/2 sinf, then cosf of pos / powf(T, paired / (dim/2)),
+    float32 operations and libm functions as the reference."""
     pe_dim = dim // 2
     i = np.arange(pe_dim)
-    dim_t = np.power(np.float32(temperature), (i & ~1).astype(np.float32) / np.float32(pe_dim)).astype(np.float32)
-    val = np.float32(pos) / dim_t
-    return np.concatenate([np.sin(val), np.cos(val)]).astype(np.float32)
+    dim_t = nn.libm_f32("powf", np.float32(temperature), (i & ~1).astype(np.float32) / np.float32(pe_dim))
+    val = (np.float32(pos) / dim_t).astype(np.float32)
+    return np.concatenate([nn.libm_f32("sinf", val), nn.libm_f32("cosf", val)]).astype(np.float32)
+
+
+def project_tpos(sine, tpos_w, tpos_b):
+    """obj_ptr_tpos_proj on the host (sam3.cpp:9186-9195): y[j] = b[j] + sum_i W[j][i] x[i], accumulated in
+    float32 from the bias, i in order, each product and sum rounded."""
+    acc = np.asarray(tpos_b, np.float32).copy()
+    w = np.asarray(tpos_w, np.float32)
+    for i in range(sine.shape[0]):
+        acc = (acc + (w[:, i] * np.float32(sine[i])).astype(np.float32)).astype(np.float32)
+    return acc
 
 
 def build_prompt(slot_feats, slot_pes, spatial_tpos, tpos_enc, obj_ptrs, ptr_tpos, tpos_w, tpos_b, num_maskmem,
                  max_obj_ptrs=16, MD=64):
     """sam3_build_prompt_and_pos (sam3.cpp:9123-9209): memory tokens + (PE + temporal PE), then each 256-d
-    object pointer split into 4 tokens of 64 with a projected 1-D sine PE of (rel / (max_obj_ptrs - 1))."""
+    object pointer split into 4 tokens of 64 with the projected 1-D sine PE of rel / 15 (9183). Returns
+    (prompt [M, 64], prompt_pos [M, 64], pointer tokens)."""
     prompt, pos = [], []
     for f, pe, tp in zip(slot_feats, slot_pes, spatial_tpos):
-        prompt.append(f)
-        pp = pe.copy()
+        prompt.append(np.asarray(f, np.float32))
+        pp = np.asarray(pe, np.float32).copy()
         if 0 <= tp < num_maskmem:
-            pp = pp + tpos_enc[num_maskmem - tp - 1][None, :]
+            pp = (pp + np.asarray(tpos_enc, np.float32)[num_maskmem - tp - 1][None, :]).astype(np.float32)
         pos.append(pp)
     n_ptr = 0
     for ptr, rel in zip(obj_ptrs, ptr_tpos):
         if rel < 0:
             continue
-        sine = one_d_sine_pe(rel / float(max_obj_ptrs - 1), ptr.shape[0])
-        proj = (tpos_w.astype(np.float64) @ sine.astype(np.float64) + tpos_b).astype(np.float32)  # [MD]
+        sine = one_d_sine_pe(np.float32(rel) / np.float32(15.0), ptr.shape[0])
+        proj = project_tpos(sine, tpos_w, tpos_b)  # [MD]
         split = ptr.shape[0] // MD
-        prompt.append(ptr.reshape(split, MD))
+        prompt.append(np.asarray(ptr, np.float32).reshape(split, MD))
         pos.append(np.repeat(proj[None, :], split, axis=0))
         n_ptr += split
+    if not prompt:
+        return np.zeros((0, MD), np.float32), np.zeros((0, MD), np.float32), 0
     return np.concatenate(prompt).astype(np.float32), np.concatenate(pos).astype(np.float32), n_ptr
+
+
+def select_memory_frames(bank_size, max_slots):
+    """sam3_select_memory_frames (sam3.cpp:9423-9447) for a bank of `bank_size` slots."""
+    if bank_size <= max_slots:
+        return list(range(bank_size))
+    sel = [0, bank_size - 1]
+    remaining = max_slots - 2
+    if remaining > 0:
+        step = np.float32(bank_size - 2) / np.float32(remaining + 1)
+        for i in range(remaining):
+            idx = 1 + int(np.float32(i + 1) * step)
+            sel.append(min(idx, bank_size - 2))
+    return sorted(set(sel))
 
 
 def golden_inputs(meta, D=256, MD=64):

@@ -4,6 +4,9 @@ Each function restates the ggml op sequence the reference builds; the
 `f16_inputs` switch rounds GEMM operands to f16 the way ggml's CPU mul_mat
 does for f16 weights (sam3.cpp:6635-6636 host reference rounds its input).
 """
+import ctypes
+import ctypes.util
+
 import numpy as np
 
 
@@ -147,18 +150,41 @@ def deconv2x2_cl(x, w, b, f16_inputs=False):
     return out
 
 
+# The C library's single-precision sinf / cosf / powf, the functions sam3.cpp calls for its
+# sinusoidal encodings (numpy's own float32 sin / cos may differ from them in the last bit).
+_libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+for _fn, _n in (("sinf", 1), ("cosf", 1), ("powf", 2)):
+    getattr(_libm, _fn).restype = ctypes.c_float
+    getattr(_libm, _fn).argtypes = [ctypes.c_float] * _n
+
+
+def libm_f32(fn, *args):
+    """Elementwise libm `fn` ("sinf", "cosf", "powf") over float32 arrays (broadcast), float32 result."""
+    f = getattr(_libm, fn)
+    arrs = np.broadcast_arrays(*[np.asarray(a, dtype=np.float32) for a in args])
+    out = np.empty(arrs[0].shape, np.float32)
+    flat = [a.ravel() for a in arrs]
+    o = out.ravel()
+    for k in range(o.size):
+        o[k] = f(*[float(a[k]) for a in flat])
+    return out
+
+
 def sine_pe_2d(H, W, d_model):
-    """sam3_sinusoidal_pe_2d (sam3.cpp:3597-3633) as channel-last [H, W, d_model]."""
+    """sam3_sinusoidal_pe_2d (sam3.cpp:3597-3633) as channel-last [H, W, d_model]: the same float32
+    operations (pos = (p + 1) / n * 2pi, dim_t = powf(1e4, paired / half), sinf / cosf of pos / dim_t)
+    and the same libm functions, so the values are bit-exact."""
     half = d_model // 2
-    scale = np.float32(2.0 * np.pi)
-    y = ((np.arange(H, dtype=np.float32) + 1) / np.float32(H)) * scale
-    x = ((np.arange(W, dtype=np.float32) + 1) / np.float32(W)) * scale
+    scale = np.float32(2.0) * np.float32(np.pi)
+    y = ((np.arange(H, dtype=np.float32) + np.float32(1)) / np.float32(H)) * scale
+    x = ((np.arange(W, dtype=np.float32) + np.float32(1)) / np.float32(W)) * scale
     i = np.arange(half)
-    dim_t = np.power(np.float32(10000.0), (i & ~1).astype(np.float32) / np.float32(half)).astype(np.float32)
-    py = y[:, None] / dim_t[None, :]
-    px = x[:, None] / dim_t[None, :]
-    vy = np.where(i % 2 == 0, np.sin(py), np.cos(py)).astype(np.float32)
-    vx = np.where(i % 2 == 0, np.sin(px), np.cos(px)).astype(np.float32)
+    dim_t = libm_f32("powf", np.float32(10000.0), (i & ~1).astype(np.float32) / np.float32(half))
+    py = (y[:, None] / dim_t[None, :]).astype(np.float32)
+    px = (x[:, None] / dim_t[None, :]).astype(np.float32)
+    even = (i % 2 == 0)[None, :]
+    vy = np.where(even, libm_f32("sinf", py), libm_f32("cosf", py)).astype(np.float32)
+    vx = np.where(even, libm_f32("sinf", px), libm_f32("cosf", px)).astype(np.float32)
     pe = np.empty((H, W, d_model), np.float32)
     pe[:, :, :half] = vy[:, None, :]
     pe[:, :, half:] = vx[None, :, :]

@@ -59,6 +59,7 @@ SYMBOLS = [
     ("s3b_output_shape", _I, [_P, _S, ctypes.POINTER(_I64)]),
     ("s3b_output_copy", _I, [_P, _S, _I, _P, _I64]),
     ("s3b_output_device_ptr", _I, [_P, _S, _I, ctypes.POINTER(_P)]),
+    ("s3b_output_host_bind", _I, [_P, _S, _P, _I64]),
     ("s3b_peer_copy_output", _I, [_P, _S, _I, _P, _I, _I64]),
     ("s3b_device_alloc", _I, [_P, _I64, ctypes.POINTER(_P)]),
     ("s3b_device_free", _I, [_P, _P]),
@@ -66,6 +67,11 @@ SYMBOLS = [
     ("s3b_ipc_open", _I, [_P, _P, ctypes.POINTER(_P)]),
     ("s3b_ipc_close", _I, [_P, _P]),
     ("s3b_mem_attn", _I, [_P, _P, _P, _I, _P, _P, _I, _I, _P, _I]),
+    ("s3b_mem_attn_bank", _I, [_P, _P, _P, _I, _P, _P, _P, _I, _P, _P, _I, _P]),
+    ("s3b_op_build_prompt", _I, [_P, _I, _P, _P, _P, _I, _P, _P, _I, _P, _P, _I64, ctypes.POINTER(_I),
+                                 ctypes.POINTER(_I)]),
+    ("s3b_select_memory_frames", _I, [_I, _I, ctypes.POINTER(_I), _I]),
+    ("s3b_sine_pe_2d", _I, [_I, _I, _I, _P]),
     ("s3b_op_gemm", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _I, _P, _I, _I64, _P, _I64]),
     ("s3b_op_gemm_rope", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _I, _I, _I64, _P, _I, _I64]),
     ("s3b_op_gemm_q", _I, [_P, _P, _I64, _P, _I, _I, _I, _I, _P, _I, _P, _I, _I64, _P, _I64]),
@@ -76,6 +82,7 @@ SYMBOLS = [
     ("s3b_op_conv3x3", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I]),
     ("s3b_op_deconv2x2", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _I, _P, _I, _I]),
     ("s3b_conv3x3_noalloc", _I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _P]),
+    ("s3b_conv3x3_noalloc_status", _I, [ctypes.POINTER(_I)]),
     ("s3b_op_dequantize", _I, [_P, _P, _I, _I64, _I64, _P]),
     ("s3b_row_size", _I64, [_I, _I64]),
     ("s3b_quantize_rows", _I, [_I, _P, _I64, _I64, _P]),
@@ -156,6 +163,24 @@ def dequantize_rows(qtype: int, raw: np.ndarray, ne0: int) -> np.ndarray:
     return out
 
 
+def select_memory_frames(bank_size: int, max_slots: int) -> list[int]:
+    """Memory-bank slots memory attention reads (s3b_select_memory_frames)."""
+    buf = (ctypes.c_int * max(bank_size, 1))()
+    n = lib().s3b_select_memory_frames(bank_size, max_slots, buf, max(bank_size, 1))
+    if n < 0:
+        raise S3BError(f"s3b_select_memory_frames: {ERRORS.get(n, n)}")
+    return list(buf[:n])
+
+
+def sine_pe_2d(H: int, W: int, d_model: int) -> np.ndarray:
+    """Sinusoidal 2D PE [H, W, d_model] as the engine computes it (s3b_sine_pe_2d)."""
+    out = np.empty((H, W, d_model), dtype=np.float32)
+    rc = lib().s3b_sine_pe_2d(H, W, d_model, out.ctypes.data)
+    if rc != 0:
+        raise S3BError(f"s3b_sine_pe_2d: {ERRORS.get(rc, rc)}")
+    return out
+
+
 def inspect_model(path: str) -> dict:
     """Host-only parse of a .ggml file (s3b_inspect_model); raises S3BError on corrupt files."""
     info = (ctypes.c_int32 * 7)()
@@ -218,12 +243,13 @@ class Engine:
         self._check(self._L.s3b_profile_begin(self.h, 1 if with_events else 0), "s3b_profile_begin")
 
     def profile_end(self) -> dict:
-        buf = (ctypes.c_double * 13)()
-        self._check(self._L.s3b_profile_end(self.h, buf, 13), "s3b_profile_end")
+        buf = (ctypes.c_double * 17)()
+        self._check(self._L.s3b_profile_end(self.h, buf, 17), "s3b_profile_end")
         v = list(buf)
         return {"gemm": {"launches": v[0], "ms": v[1], "flops": v[2], "bytes": v[3]},
                 "attention": {"launches": v[4], "ms": v[5], "flops": v[6], "bytes": v[7]},
                 "layernorm": {"launches": v[9], "ms": v[10], "bytes": v[12]},
+                "weight_staging": {"launches": v[13], "ms": v[14], "bytes": v[16]},
                 "launches": int(v[8])}
 
     def load_model(self, path: str):
@@ -282,6 +308,16 @@ class Engine:
                     "s3b_output_copy")
         return out
 
+    def output_host_bind(self, name: str, host=None):
+        """Binds host memory (a pinned torch CPU tensor or numpy array of f32, frames x frame elements) to
+        output `name`: every later encode copies each pass's frames into it, overlapped with the next pass
+        (s3b_output_host_bind). None unbinds."""
+        if host is None:
+            self._check(self._L.s3b_output_host_bind(self.h, name.encode(), None, 0), "s3b_output_host_bind")
+            return
+        n = host.numel() if hasattr(host, "numel") else host.size
+        self._check(self._L.s3b_output_host_bind(self.h, name.encode(), _ptr(host), n), "s3b_output_host_bind")
+
     def output_device_ptr(self, name: str, frame: int = 0) -> int:
         p = ctypes.c_void_p()
         self._check(self._L.s3b_output_device_ptr(self.h, name.encode(), frame, ctypes.byref(p)),
@@ -336,6 +372,46 @@ class Engine:
                                   m_total, n_ptr_tokens, _ptr(out), 1 if dev else 0)
         self._check(rc, "s3b_mem_attn")
         return out
+
+    @staticmethod
+    def _bank_args(slot_feats, slot_pes, slot_tpos, obj_ptrs, ptr_tpos):
+        n_slots = len(slot_feats)
+        feats = (ctypes.c_void_p * max(n_slots, 1))(*[_ptr(f) for f in slot_feats])
+        pes = None
+        if slot_pes is not None:
+            pes = (ctypes.c_void_p * max(n_slots, 1))(*[_ptr(p) for p in slot_pes])
+        tpos = (ctypes.c_int * max(n_slots, 1))(*[int(t) for t in slot_tpos])
+        n_ptrs = 0 if obj_ptrs is None else int(obj_ptrs.shape[0])
+        ptpos = (ctypes.c_int * max(n_ptrs, 1))(*[int(t) for t in (ptr_tpos if n_ptrs else [])])
+        return n_slots, feats, pes, tpos, n_ptrs, ptpos
+
+    def mem_attn_bank(self, curr, feat: int, slot_feats, slot_tpos, obj_ptrs=None, ptr_tpos=(), slot_pes=None,
+                      src_pos=None, out=None):
+        """Memory attention with the prompt built on the device from a memory bank (s3b_mem_attn_bank).
+        All tensors are torch CUDA tensors: curr [N, 256], slot_feats list of [N, 64], obj_ptrs [P, 256]."""
+        if out is None:
+            import torch
+            out = torch.empty_like(curr)
+        n_slots, feats, pes, tpos, n_ptrs, ptpos = self._bank_args(slot_feats, slot_pes, slot_tpos, obj_ptrs, ptr_tpos)
+        rc = self._L.s3b_mem_attn_bank(self.h, _ptr(curr), _ptr(src_pos), feat, feats, pes, tpos, n_slots,
+                                       _ptr(obj_ptrs), ptpos, n_ptrs, _ptr(out))
+        self._check(rc, "s3b_mem_attn_bank")
+        return out
+
+    def build_prompt(self, feat: int, slot_feats, slot_tpos, obj_ptrs=None, ptr_tpos=(), slot_pes=None):
+        """The device prompt build alone: (prompt [M, 64], prompt_pos [M, 64], n_ptr_tokens) as torch CUDA tensors."""
+        import torch
+        n_slots, feats, pes, tpos, n_ptrs, ptpos = self._bank_args(slot_feats, slot_pes, slot_tpos, obj_ptrs, ptr_tpos)
+        cap = n_slots * feat * feat + 4 * n_ptrs
+        dev = slot_feats[0].device if n_slots else obj_ptrs.device
+        prompt = torch.empty(max(cap, 1), 64, device=dev, dtype=torch.float32)
+        pos = torch.empty_like(prompt)
+        m_total, n_ptr = ctypes.c_int(0), ctypes.c_int(0)
+        rc = self._L.s3b_op_build_prompt(self.h, feat, feats, pes, tpos, n_slots, _ptr(obj_ptrs), ptpos, n_ptrs,
+                                         prompt.data_ptr(), pos.data_ptr(), cap, ctypes.byref(m_total),
+                                         ctypes.byref(n_ptr))
+        self._check(rc, "s3b_op_build_prompt")
+        return prompt[:m_total.value], pos[:m_total.value], n_ptr.value
 
     # -- operators on device pointers (torch CUDA tensors)
     def gemm(self, A, B, out, bias=None, act=ACT_NONE, resid=None, K=None):

@@ -358,13 +358,7 @@ __global__ void __launch_bounds__(128) attn_small_kernel(AttnParams p, int batch
 template <int D, int DR, int NKP>
 int launch_small(const AttnParams& p, int batch_heads, cudaStream_t st) {
   constexpr size_t smem = (size_t)4 * (16 + 2 * NKP) * (D + 8) * 2;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_small_kernel<D, DR, NKP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return -13;
-    attr = true;
-  }
+  if (kernel_setup(attn_small_kernel<D, DR, NKP>, smem) <= 0) return -13;
   const long long n_cta = ((long long)batch_heads + 3) / 4;
   if (n_cta > 0x7fffffffLL) return -2;
   attn_small_kernel<D, DR, NKP><<<(unsigned)n_cta, 128, smem, st>>>(p, batch_heads);
@@ -385,13 +379,7 @@ int launch_attn(const AttnParams& p, int batch_heads, cudaStream_t st) {
     if (p.nq <= 16 && p.nk <= 64) return launch_small_nk<D, DR>(p, batch_heads, st);
   }
   constexpr size_t smem = (size_t)(kBQ + 4 * kBKV) * (D + 8) * 2;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_fwd_kernel<D, DR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return -13;
-    attr = true;
-  }
+  if (kernel_setup(attn_fwd_kernel<D, DR>, smem) <= 0) return -13;
   const long long n_cta = (long long)((p.nq + kBQ - 1) / kBQ) * batch_heads;
   if (n_cta > 0x7fffffffLL) return -2;
   attn_fwd_kernel<D, DR><<<(unsigned)n_cta, 128, smem, st>>>(p);

@@ -585,12 +585,8 @@ int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v
   a.sl2 = scale * 1.4426950408889634f;
   const size_t smem = p_mode == 1 ? 1024 + kTileBytes * (1 + 5) + kXchgBytes + 24 * 8 + 16
                                   : 1024 + kTileBytes * (1 + kSlots) + kPBytes + kXchgBytes + 24 * 8 + 16;
-  static bool attr[2][5] = {};
   const KernelFn kfn = kernels[p_mode][exp_poly];
-  if (!attr[p_mode][exp_poly]) {
-    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -13;
-    attr[p_mode][exp_poly] = true;
-  }
+  if (kernel_setup(kfn, smem) <= 0) return -13;
   const long long n_cta = (long long)((ntok + kBQ - 1) / kBQ) * nwin * heads;
   if (n_cta > 0x7fffffffLL) return -2;
   kfn<<<(unsigned)n_cta, kThreads, smem, st>>>(tm, a, err);

@@ -613,13 +613,7 @@ int launch_wide(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes
   a.ws_o = ws;
   a.ws_ml = ws ? ws + (size_t)n_split * batch_heads * p.nq * D : nullptr;
   static_assert(C::Smem <= 232448, "shared memory per CTA");
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_wide_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::Smem) !=
-        cudaSuccess)
-      return -13;
-    attr = true;
-  }
+  if (kernel_setup(attn_wide_kernel<D>, (size_t)C::Smem) <= 0) return -13;
   const long long n_cta = units * n_split;
   if (n_cta > 0x7fffffffLL) return -2;
   attn_wide_kernel<D><<<(unsigned)n_cta, kThreads, C::Smem, st>>>(tq, tk, tv, a, err);

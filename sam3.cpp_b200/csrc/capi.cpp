@@ -2,15 +2,15 @@
 #include <math.h>
 #include <string.h>
 
+#include <algorithm>
 #include <string>
+#include <vector>
 
 #include "../../include/sam3_b200.h"
 #include "engine.h"
 
 namespace s3b {
 void quantize_row_host(int type, const float* x, int64_t n, uint8_t* dst);
-int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const float* prompt,
-                 const float* prompt_pos, int m_total, int n_ptr, float* out);
 }  // namespace s3b
 
 using namespace s3b;
@@ -68,6 +68,94 @@ void sine_pe_2d(int H, int W, int d_model, float* pe) {
         pe[((size_t)y * W + x) * d_model + i + half] = vx;
       }
     }
+}
+
+// 1-D sine PE (sam3_get_1d_sine_pe, sam3.cpp:3636-3647): [dim], first dim/2 sin, then cos.
+void sine_pe_1d(float* out, float pos_ind, int dim) {
+  const int pe_dim = dim / 2;
+  for (int i = 0; i < pe_dim; ++i) {
+    const int paired = i & ~1;
+    const float dim_t = powf(10000.0f, (float)paired / (float)pe_dim);
+    const float val = pos_ind / dim_t;
+    out[i] = sinf(val);
+    out[pe_dim + i] = cosf(val);
+  }
+}
+
+// Device copy of the sinusoidal PE [S][S][d] (computed on the host once per size, like the tracker's
+// cached_sinpe_256 / cached_sinpe_64, sam3.cpp:11137-11138).
+const float* device_sine_pe(s3b_ctx* ctx, int S, int d, int* rc) {
+  const std::string key = "sine_pe_" + std::to_string(S) + "_" + std::to_string(d);
+  auto it = ctx->ws.find(key);
+  if (it != ctx->ws.end() && it->second && it->second->p) return it->second->as<float>();
+  std::vector<float> pe((size_t)S * S * d);
+  sine_pe_2d(S, S, d, pe.data());
+  DevBuf* b = ctx->buf(key, pe.size() * 4, rc);
+  if (*rc) return nullptr;
+  if (cudaMemcpy(b->p, pe.data(), pe.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    *rc = set_error(ctx, kErrCuda, "sine PE upload failed");
+    return nullptr;
+  }
+  return b->as<float>();
+}
+
+// Parameters of the device prompt build from a memory bank (sam3_build_prompt_and_pos,
+// sam3.cpp:9123-9209, with the inputs sam3_propagate_single gathers at 11186-11228).
+int prompt_args(s3b_ctx* ctx, int feat, const float* const* slot_feats, const float* const* slot_pes,
+                const int* slot_tpos, int n_slots, const float* obj_ptrs, const int* ptr_tpos, int n_ptrs,
+                PromptArgs& pa) {
+  const Model& M = ctx->model;
+  const HParams& hp = M.hp;
+  const int D = hp.neck_dim, MD = hp.mem_out_dim;
+  if (MD != kPromptMD || D % MD) return set_error(ctx, kErrUnsupported, "memory dim %d / %d", MD, D);
+  if (n_slots < 0 || n_slots > kPromptMaxSlots || n_ptrs < 0 || n_ptrs > kPromptMaxPtrs || feat <= 0 ||
+      (n_slots > 0 && (!slot_feats || !slot_tpos)) || (n_ptrs > 0 && (!obj_ptrs || !ptr_tpos)))
+    return set_error(ctx, kErrArg, "bad memory-bank arguments (at most %d slots and %d pointers)", kPromptMaxSlots,
+                     kPromptMaxPtrs);
+  pa.n_slots = n_slots;
+  pa.slot_tokens = feat * feat;
+  pa.split = D / MD;
+  int rc = 0;
+  for (int s = 0; s < n_slots; ++s) {
+    pa.feat[s] = slot_feats[s];
+    pa.pe[s] = slot_pes && slot_pes[s] ? slot_pes[s] : device_sine_pe(ctx, feat, MD, &rc);  // cached_sinpe_64
+    if (rc) return rc;
+    if (!pa.feat[s]) return set_error(ctx, kErrArg, "null memory slot %d", s);
+    const int tp = slot_tpos[s];
+    pa.has_tpos[s] = 0;
+    if (tp >= 0 && tp < hp.num_maskmem) {
+      const int enc_idx = hp.num_maskmem - tp - 1;  // maskmem_tpos_enc[num_maskmem - tpos - 1]
+      if ((int)M.maskmem_tpos.size() < (enc_idx + 1) * MD)
+        return set_error(ctx, kErrState, "model has no temporal encodings (mem_enc.tpos_enc)");
+      memcpy(pa.tpos[s], M.maskmem_tpos.data() + (size_t)enc_idx * MD, MD * sizeof(float));
+      pa.has_tpos[s] = 1;
+    }
+  }
+  pa.ptrs = obj_ptrs;
+  pa.n_ptr = 0;
+  for (int p = 0; p < n_ptrs; ++p) {
+    const int rel = ptr_tpos[p];
+    if (rel < 0) continue;  // skipped pointers (sam3.cpp:9181)
+    auto it = ctx->ptr_pe_cache.find(rel);
+    if (it == ctx->ptr_pe_cache.end()) {
+      if ((int)M.obj_ptr_tpos_w.size() != D * MD || (int)M.obj_ptr_tpos_b.size() != MD)
+        return set_error(ctx, kErrState, "model has no obj_ptr_tpos_proj weights");
+      // 1-D sine PE of rel / 15 projected 256 -> 64 in f32, bias first then i in order (9182-9195)
+      std::vector<float> sine(D), proj(MD);
+      sine_pe_1d(sine.data(), (float)rel / 15.0f, D);
+      for (int j = 0; j < MD; ++j) {
+        float sum = M.obj_ptr_tpos_b[j];
+        for (int i = 0; i < D; ++i) sum += M.obj_ptr_tpos_w[(size_t)i + (size_t)j * D] * sine[i];
+        proj[j] = sum;
+      }
+      it = ctx->ptr_pe_cache.emplace(rel, proj).first;
+    }
+    memcpy(pa.ptr_pe[pa.n_ptr], it->second.data(), MD * sizeof(float));
+    pa.ptr_src[pa.n_ptr] = p;
+    ++pa.n_ptr;
+  }
+  if (pa.n_slots * pa.slot_tokens + pa.n_ptr * pa.split <= 0) return set_error(ctx, kErrArg, "empty memory");
+  return kOk;
 }
 
 struct OutRef {
@@ -184,6 +272,67 @@ int encode_device_image_u8(s3b_ctx* ctx, const uint8_t* d_u8, int n_frames, int 
 
 }  // namespace
 
+namespace s3b {
+
+int outputs_pass_begin(s3b_ctx* ctx, int pass, int fb) {
+  if (ctx->copy_done.empty()) return kOk;
+  if (fb != ctx->copy_fb) {
+    // another pass size: any pending copy may read frames this call writes
+    for (size_t p = 0; p < ctx->copy_done.size(); ++p)
+      if (ctx->copy_pending[p]) {
+        if (cudaStreamWaitEvent(ctx->stream, ctx->copy_done[p], 0) != cudaSuccess)
+          return set_error(ctx, kErrCuda, "waiting for output copies failed");
+        ctx->copy_pending[p] = 0;
+      }
+    return kOk;
+  }
+  if (pass < (int)ctx->copy_done.size() && ctx->copy_pending[pass]) {
+    if (cudaStreamWaitEvent(ctx->stream, ctx->copy_done[pass], 0) != cudaSuccess)
+      return set_error(ctx, kErrCuda, "waiting for output copies failed");
+    ctx->copy_pending[pass] = 0;
+  }
+  return kOk;
+}
+
+int outputs_pass_end(s3b_ctx* ctx, int pass, int f0, int F) {
+  if (ctx->host_bind.empty()) return kOk;
+  if (!ctx->copy_stream &&
+      cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "copy stream creation failed");
+  while ((int)ctx->copy_done.size() <= pass) {
+    cudaEvent_t a, b;
+    if (cudaEventCreateWithFlags(&a, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&b, cudaEventDisableTiming) != cudaSuccess)
+      return set_error(ctx, kErrCuda, "event creation failed");
+    ctx->pass_done.push_back(a);
+    ctx->copy_done.push_back(b);
+    ctx->copy_pending.push_back(0);
+  }
+  if (cudaEventRecord(ctx->pass_done[pass], ctx->stream) != cudaSuccess ||
+      cudaStreamWaitEvent(ctx->copy_stream, ctx->pass_done[pass], 0) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "output copy ordering failed");
+  for (const auto& kv : ctx->host_bind) {
+    OutRef r;
+    int rc = resolve_output(ctx, kv.first.c_str(), r);
+    if (rc) return rc;
+    if (r.is_pe) return set_error(ctx, kErrArg, "'%s' is host-computed and cannot be bound", kv.first.c_str());
+    if (kv.second.n < (int64_t)ctx->out.n_frames * r.frame_elems)
+      return set_error(ctx, kErrArg, "host buffer of '%s' holds %lld floats, the call needs %lld", kv.first.c_str(),
+                       (long long)kv.second.n, (long long)ctx->out.n_frames * r.frame_elems);
+    const size_t off = (size_t)f0 * r.frame_elems;
+    if (cudaMemcpyAsync(kv.second.host + off, r.dev + off, (size_t)F * r.frame_elems * 4, cudaMemcpyDeviceToHost,
+                        ctx->copy_stream) != cudaSuccess)
+      return set_error(ctx, kErrCuda, "output copy of '%s' failed", kv.first.c_str());
+  }
+  if (cudaEventRecord(ctx->copy_done[pass], ctx->copy_stream) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "output copy ordering failed");
+  ctx->copy_pending[pass] = 1;
+  ctx->copy_fb = ctx->max_frames_per_pass;
+  return kOk;
+}
+
+}  // namespace s3b
+
 extern "C" {
 
 int s3b_create(int device, s3b_ctx** out) {
@@ -211,6 +360,10 @@ void s3b_destroy(s3b_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);
+  for (cudaEvent_t e : ctx->pass_done) cudaEventDestroy(e);
+  for (cudaEvent_t e : ctx->copy_done) cudaEventDestroy(e);
+  if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
   if (ctx->ma_exec) cudaGraphExecDestroy(ctx->ma_exec);
   for (void* p : ctx->ipc_mapped) cudaIpcCloseMemHandle(p);
   ctx->ipc_mapped.clear();
@@ -252,7 +405,34 @@ int s3b_sync(s3b_ctx* ctx) {
   if (rc) return rc;
   cudaError_t e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return set_error(ctx, kErrCuda, "stream synchronize: %s", cudaGetErrorString(e));
+  if (ctx->copy_stream) {
+    e = cudaStreamSynchronize(ctx->copy_stream);
+    if (e != cudaSuccess) return set_error(ctx, kErrCuda, "output copies: %s", cudaGetErrorString(e));
+    for (auto& p : ctx->copy_pending) p = 0;
+  }
   return read_dev_err(ctx);
+}
+
+int s3b_output_host_bind(s3b_ctx* ctx, const char* name, float* host, int64_t n_floats) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!name) return set_error(ctx, kErrArg, "null output name");
+  const std::string n(name);
+  bool known = n == "vit_output" || n == "backbone";
+  for (int i = 0; i < 4; ++i)
+    known = known || n == "neck_trk_" + std::to_string(i) || n == "neck_det_" + std::to_string(i);
+  if (!known) return set_error(ctx, kErrArg, "output '%s' cannot be bound to host memory", name);
+  // copies still reading the previous binding finish first
+  if (ctx->copy_stream && cudaStreamSynchronize(ctx->copy_stream) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "output copies failed");
+  for (auto& p : ctx->copy_pending) p = 0;
+  if (!host) {
+    ctx->host_bind.erase(n);
+    return kOk;
+  }
+  if (n_floats <= 0) return set_error(ctx, kErrArg, "bad host buffer size");
+  ctx->host_bind[n] = s3b_ctx::HostBind{host, n_floats};
+  return kOk;
 }
 
 int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
@@ -285,7 +465,7 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     return kOk;
   }
   if (k == "weights_quantised") {
-    if (value < 0 || value > 1) return set_error(ctx, kErrArg, "weights_quantised must be 0 or 1");
+    if (value < 0 || value > 2) return set_error(ctx, kErrArg, "weights_quantised must be 0, 1 or 2");
     ctx->weights_quantised = (int)value;
     return kOk;
   }
@@ -321,18 +501,18 @@ int s3b_profile_end(s3b_ctx* ctx, double* out, int n) {
   int rc = ctx_enter(ctx);
   if (rc) return rc;
   if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return set_error(ctx, kErrCuda, "synchronize failed");
-  double v[13] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+  double v[17] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
   for (const auto& e : ctx->prof_entries) {
     float ms = 0.f;
     cudaEventElapsedTime(&ms, e.a, e.b);
-    const int base = e.kind == 0 ? 0 : e.kind == 1 ? 4 : 9;
+    const int base = e.kind == 0 ? 0 : e.kind == 1 ? 4 : e.kind == 2 ? 9 : 13;
     v[base + 0] += 1;
     v[base + 1] += ms;
     v[base + 2] += e.flops;
     v[base + 3] += e.bytes;
   }
   v[8] = (double)ctx->n_launches;
-  for (int i = 0; i < n && i < 13; ++i) out[i] = v[i];
+  for (int i = 0; i < n && i < 17; ++i) out[i] = v[i];
   ctx->prof = false;
   ctx->prof_entries.clear();
   ctx->event_next = 0;
@@ -344,6 +524,7 @@ int s3b_load_model(s3b_ctx* ctx, const char* path) {
   if (rc) return rc;
   if (!path) return set_error(ctx, kErrArg, "null path");
   ctx->out = Outputs();
+  ctx->ptr_pe_cache.clear();
   ++ctx->graph_epoch;  // graphs hold the old weights' addresses
   return load_model(ctx, path);
 }
@@ -463,8 +644,15 @@ int s3b_output_device_ptr(s3b_ctx* ctx, const char* name, int frame, const float
   OutRef r;
   int rc = resolve_output(ctx, name, r);
   if (rc) return rc;
-  if (r.is_pe) return set_error(ctx, kErrArg, "PE outputs are host-computed; use s3b_output_copy");
   if (frame < 0 || frame >= ctx->out.n_frames) return set_error(ctx, kErrArg, "frame out of range");
+  if (r.is_pe) {
+    // the same PE for every frame, kept on the device once per size
+    if ((rc = ctx_enter(ctx))) return rc;
+    const float* pe = device_sine_pe(ctx, r.pe_size, (int)r.ne[0], &rc);
+    if (rc) return rc;
+    *dptr = pe;
+    return kOk;
+  }
   *dptr = r.dev + (size_t)frame * r.frame_elems;
   return kOk;
 }
@@ -587,6 +775,75 @@ int s3b_mem_attn(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat
   return s3b_sync(ctx);
 }
 
+int s3b_mem_attn_bank(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat,
+                      const float* const* slot_feats, const float* const* slot_pes, const int* slot_tpos, int n_slots,
+                      const float* obj_ptrs, const int* ptr_tpos, int n_ptrs, float* out) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!ctx->model.has_mem_attn) return set_error(ctx, kErrState, "model has no memory-attention weights");
+  if (!curr || !out || feat <= 0) return set_error(ctx, kErrArg, "bad memory-attention arguments");
+  PromptArgs pa;
+  if ((rc = prompt_args(ctx, feat, slot_feats, slot_pes, slot_tpos, n_slots, obj_ptrs, ptr_tpos, n_ptrs, pa)))
+    return rc;
+  if (!src_pos) {
+    src_pos = device_sine_pe(ctx, feat, ctx->model.hp.neck_dim, &rc);  // cached_sinpe_256
+    if (rc) return rc;
+  }
+  return mem_attn_run_bank(ctx, curr, src_pos, feat, pa, out);
+}
+
+int s3b_op_build_prompt(s3b_ctx* ctx, int feat, const float* const* slot_feats, const float* const* slot_pes,
+                        const int* slot_tpos, int n_slots, const float* obj_ptrs, const int* ptr_tpos, int n_ptrs,
+                        float* prompt, float* prompt_pos, int64_t capacity_rows, int* m_total, int* n_ptr_tokens) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!prompt || !prompt_pos) return set_error(ctx, kErrArg, "null prompt outputs");
+  PromptArgs pa;
+  if ((rc = prompt_args(ctx, feat, slot_feats, slot_pes, slot_tpos, n_slots, obj_ptrs, ptr_tpos, n_ptrs, pa)))
+    return rc;
+  const int64_t rows = (int64_t)pa.n_slots * pa.slot_tokens + (int64_t)pa.n_ptr * pa.split;
+  if (m_total) *m_total = (int)rows;
+  if (n_ptr_tokens) *n_ptr_tokens = pa.n_ptr * pa.split;
+  if (rows > capacity_rows) return set_error(ctx, kErrArg, "prompt needs %lld rows, buffers hold %lld",
+                                             (long long)rows, (long long)capacity_rows);
+  rc = build_prompt(pa, prompt, prompt_pos, 0, ctx->stream);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "prompt build launch failed (%d)", rc);
+  return kOk;
+}
+
+int s3b_select_memory_frames(int bank_size, int max_slots, int* out_idx, int capacity) {
+  if (bank_size < 0 || max_slots < 0 || (!out_idx && capacity > 0)) return kErrArg;
+  // sam3_select_memory_frames (sam3.cpp:9423-9447): all slots when they fit, else the first, the
+  // last and max_slots - 2 evenly spaced between them, sorted and unique
+  std::vector<int> sel;
+  if (bank_size <= max_slots) {
+    for (int i = 0; i < bank_size; ++i) sel.push_back(i);
+  } else {
+    sel.push_back(0);
+    sel.push_back(bank_size - 1);
+    const int remaining = max_slots - 2;
+    if (remaining > 0) {
+      const float step = (float)(bank_size - 2) / (float)(remaining + 1);
+      for (int i = 0; i < remaining; ++i) {
+        int idx = 1 + (int)((float)(i + 1) * step);
+        if (idx > bank_size - 2) idx = bank_size - 2;
+        sel.push_back(idx);
+      }
+    }
+    std::sort(sel.begin(), sel.end());
+    sel.erase(std::unique(sel.begin(), sel.end()), sel.end());
+  }
+  if ((int)sel.size() > capacity) return kErrArg;
+  for (size_t i = 0; i < sel.size(); ++i) out_idx[i] = sel[i];
+  return (int)sel.size();
+}
+
+int s3b_sine_pe_2d(int H, int W, int d_model, float* out) {
+  if (H <= 0 || W <= 0 || d_model <= 0 || (d_model & 1) || !out) return kErrArg;
+  sine_pe_2d(H, W, d_model, out);
+  return kOk;
+}
+
 int s3b_op_gemm(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
                 const float* bias, int act, void* out, int out_f32, int64_t ldo, const float* resid, int64_t ldr) {
   int rc = ctx_enter(ctx);
@@ -603,7 +860,7 @@ int s3b_op_gemm(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, int64_t
   ep.ldr = ldr;
   rc = gemm_f16(reinterpret_cast<const __half*>(A), lda, reinterpret_cast<const __half*>(B), ldb, M, N, K, ep,
                 ctx->d_err, ctx->stream);
-  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "gemm launch failed (%d)", rc);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "gemm launch failed (%d)", rc);
   return kOk;
 }
 
@@ -637,7 +894,7 @@ int s3b_op_gemm_rope(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, in
   ep.rope_mod = rope_mod;
   rc = gemm_f16(reinterpret_cast<const __half*>(A), lda, reinterpret_cast<const __half*>(B), ldb, M, N, K, ep,
                 ctx->d_err, ctx->stream);
-  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "gemm_rope launch failed (%d)", rc);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "gemm_rope launch failed (%d)", rc);
   return kOk;
 }
 
@@ -662,7 +919,7 @@ int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, 
   p.o_n = (long long)heads * d;
   p.scale = scale;
   rc = attention(p, d, batch * heads, ctx->stream);
-  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "attention launch failed (%d)", rc);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "attention launch failed (%d)", rc);
   return kOk;
 }
 
@@ -727,7 +984,7 @@ int s3b_op_conv3x3(s3b_ctx* ctx, const void* x, int B, int H, int W, int C, cons
     rc = gemm_conv3x3(reinterpret_cast<const __half*>(x), B, H, W, C, reinterpret_cast<const __half*>(w), 9LL * C,
                       Cout, ep, ctx->d_err, ctx->stream);
     if (rc != -2) {
-      if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "implicit conv3x3 launch failed (%d)", rc);
+      if (rc) return set_error(ctx, launcher_status_code(rc), "implicit conv3x3 launch failed (%d)", rc);
       return kOk;
     }
   }
@@ -737,7 +994,7 @@ int s3b_op_conv3x3(s3b_ctx* ctx, const void* x, int B, int H, int W, int C, cons
   if (rc) return set_error(ctx, kErrCuda, "im2col launch failed (%d)", rc);
   rc = gemm_f16(col->as<__half>(), 9LL * C, reinterpret_cast<const __half*>(w), 9LL * C, (int)M, Cout, 9 * C, ep,
                 ctx->d_err, ctx->stream);
-  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "conv gemm launch failed (%d)", rc);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "conv gemm launch failed (%d)", rc);
   return kOk;
 }
 
@@ -760,7 +1017,7 @@ int s3b_op_deconv2x2(s3b_ctx* ctx, const void* x, int B, int H, int W, int Cin, 
   if (ctx->conv_implicit) {
     rc = gemm_deconv2x2(xh, B, H, W, Cin, wh, Cin, Cout, ep, ctx->d_err, ctx->stream);
     if (rc != -2) {
-      if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "deconv2x2 launch failed (%d)", rc);
+      if (rc) return set_error(ctx, launcher_status_code(rc), "deconv2x2 launch failed (%d)", rc);
       return kOk;
     }
   }
@@ -770,7 +1027,7 @@ int s3b_op_deconv2x2(s3b_ctx* ctx, const void* x, int B, int H, int W, int Cin, 
   ep.map.W = W;
   ep.map.H = H;
   rc = gemm_f16(xh, Cin, wh, Cin, B * H * W, 4 * Cout, Cin, ep, ctx->d_err, ctx->stream);
-  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "deconv2x2 gemm launch failed (%d)", rc);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "deconv2x2 gemm launch failed (%d)", rc);
   return kOk;
 }
 
@@ -803,7 +1060,7 @@ int s3b_op_gemm_q(s3b_ctx* ctx, const void* A, int64_t lda, const void* blocks, 
   w.values = qv->p;
   w.scales = qs->as<__half>();
   rc = gemm_q(reinterpret_cast<const __half*>(A), lda, w, M, N, K, ep, ctx->d_err, ctx->stream);
-  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "gemm_q launch failed (%d)", rc);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "gemm_q launch failed (%d)", rc);
   return kOk;
 }
 

@@ -606,6 +606,63 @@ int add_scaled_to_f16(const float* a, const float* b, float s, long long n, __ha
   return launch_ok();
 }
 
+// One thread per 4 values of a prompt row (16 per row); float4 loads and stores.
+__global__ void build_prompt_kernel(const PromptArgs args, long long rows, void* __restrict__ a,
+                                    void* __restrict__ b, int out_f16) {
+  const long long m_sp = (long long)args.n_slots * args.slot_tokens;
+  const long long n = rows * (kPromptMD / 4);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i >> 4;
+    const int c = (int)(i & 15) * 4;
+    float4 pr, ps;
+    if (r < m_sp) {
+      const int s = (int)(r / args.slot_tokens);
+      const long long t = r - (long long)s * args.slot_tokens;
+      pr = *reinterpret_cast<const float4*>(args.feat[s] + t * kPromptMD + c);
+      ps = *reinterpret_cast<const float4*>(args.pe[s] + t * kPromptMD + c);
+      if (args.has_tpos[s]) {  // pos[d + n*MD] += tpos_all[d + enc_idx*MD]
+        ps.x += args.tpos[s][c];
+        ps.y += args.tpos[s][c + 1];
+        ps.z += args.tpos[s][c + 2];
+        ps.w += args.tpos[s][c + 3];
+      }
+    } else {
+      const long long q = r - m_sp;
+      const int k = (int)(q / args.split), t = (int)(q - (long long)k * args.split);
+      pr = *reinterpret_cast<const float4*>(args.ptrs + ((long long)args.ptr_src[k] * args.split + t) * kPromptMD + c);
+      ps = make_float4(args.ptr_pe[k][c], args.ptr_pe[k][c + 1], args.ptr_pe[k][c + 2], args.ptr_pe[k][c + 3]);
+    }
+    if (out_f16) {
+      __half2* ka = reinterpret_cast<__half2*>(reinterpret_cast<__half*>(a) + r * kPromptMD + c);
+      __half2* vb = reinterpret_cast<__half2*>(reinterpret_cast<__half*>(b) + r * kPromptMD + c);
+      ka[0] = __halves2half2(__float2half_rn(pr.x + ps.x), __float2half_rn(pr.y + ps.y));
+      ka[1] = __halves2half2(__float2half_rn(pr.z + ps.z), __float2half_rn(pr.w + ps.w));
+      vb[0] = __halves2half2(__float2half_rn(pr.x), __float2half_rn(pr.y));
+      vb[1] = __halves2half2(__float2half_rn(pr.z), __float2half_rn(pr.w));
+    } else {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(a) + r * kPromptMD + c) = pr;
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(b) + r * kPromptMD + c) = ps;
+    }
+  }
+}
+
+int build_prompt(const PromptArgs& args, void* a, void* b, int out_f16, cudaStream_t st) {
+  if (args.n_slots < 0 || args.n_slots > kPromptMaxSlots || args.n_ptr < 0 || args.n_ptr > kPromptMaxPtrs ||
+      args.split <= 0 || (args.n_slots > 0 && args.slot_tokens <= 0) || (args.n_ptr > 0 && !args.ptrs) || !a || !b)
+    return -2;
+  for (int s = 0; s < args.n_slots; ++s)
+    if (!args.feat[s] || !args.pe[s] || (reinterpret_cast<uintptr_t>(args.feat[s]) & 15) ||
+        (reinterpret_cast<uintptr_t>(args.pe[s]) & 15))
+      return -11;
+  if ((args.ptrs && (reinterpret_cast<uintptr_t>(args.ptrs) & 15)) || (reinterpret_cast<uintptr_t>(a) & 15) ||
+      (reinterpret_cast<uintptr_t>(b) & 15))
+    return -11;
+  const long long rows = (long long)args.n_slots * args.slot_tokens + (long long)args.n_ptr * args.split;
+  if (rows <= 0) return -2;
+  build_prompt_kernel<<<grid_for(rows * 16, 256), 256, 0, st>>>(args, rows, a, b, out_f16);
+  return launch_ok();
+}
+
 long long qtype_row_bytes(int qtype, long long ne0) {
   switch (qtype) {
     case QT_F32: return ne0 * 4;

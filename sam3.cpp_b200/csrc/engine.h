@@ -119,7 +119,7 @@ struct DevBuf {
 // (K-major), plus the bias and, for quantised files, the raw blocks.
 // With the context option weights_quantised, a q4_0 / q8_0 weight keeps its block form on the
 // device instead (qtype != 0, w null): value plane qv and f16 scale plane qs in the QWeight
-// layout, dequantised inside the GEMM.
+// layout, dequantised before (1) or inside (2) the GEMM.
 struct Linear {
   int N = 0, K = 0, Kpad = 0;
   int file_dtype = 0;
@@ -189,6 +189,8 @@ struct Model {
   std::vector<float> maskmem_tpos;   // [num_maskmem][64]
   std::vector<float> obj_ptr_tpos_w, obj_ptr_tpos_b;  // [64][256], [64]
   size_t device_bytes = 0;
+  // largest N*K of a weight kept in block form: the f16 staging buffer of weights_quantised = 1
+  size_t qstage_elems = 0;
 };
 
 // Per-frame outputs of one encode call (device, channel-last f32 maps).
@@ -218,6 +220,20 @@ struct s3b_ctx {
   s3b::Outputs out;
   // workspace (grown on demand, reused across calls)
   std::map<std::string, std::shared_ptr<s3b::DevBuf>> ws;
+  // host destinations bound with s3b_output_host_bind: after each encoder pass, that pass's frames
+  // of these outputs are copied to host memory on copy_stream while the next pass computes
+  struct HostBind {
+    float* host = nullptr;
+    int64_t n = 0;  // floats the host buffer holds
+  };
+  std::map<std::string, HostBind> host_bind;
+  cudaStream_t copy_stream = nullptr;
+  std::vector<cudaEvent_t> pass_done, copy_done;  // per pass index of the encode call
+  std::vector<char> copy_pending;                  // copy_done[p] recorded and not yet waited for
+  int copy_fb = 0;                                 // frames per pass of the pending copies
+  // projected 1-D sine PE of an object pointer at frame distance `rel` (s3b_mem_attn_bank), per rel;
+  // cleared when a model is loaded
+  std::map<int, std::vector<float>> ptr_pe_cache;
   // s3b_device_alloc allocations and s3b_ipc_open mappings, released with the context
   std::map<void*, std::shared_ptr<s3b::DevBuf>> user_allocs;
   std::set<void*> ipc_mapped;
@@ -225,7 +241,9 @@ struct s3b_ctx {
   int stop_after_blocks = -1;  // test hook: run only the first n backbone blocks (-1: all)
   int attention_impl = 0;      // 0: tcgen05 where eligible, 1: always mma.sync, 2: d = 64 on the wide tcgen05 kernel,
                                // 3: as 0, d = 64 with P in shared memory
-  int weights_quantised = 0;   // q4_0 / q8_0 linear weights stay in block form, dequantised inside the GEMM
+  int weights_quantised = 0;   // q4_0 / q8_0 linear weights stay in block form in device memory: 1 each is
+                               // dequantised into an f16 staging buffer (L2-resident) right before its GEMM,
+                               // 2 the GEMM dequantises each weight tile in shared memory; 0 f16 at load
   int conv_implicit = 1;       // pixel-block GEMMs: implicit 3x3 convs, TMA-stored deconvs (0: im2col / scatter)
   int attention_exp_poly = 0;  // of every 8 softmax exponentials in the tcgen05 kernel, how many use the FMA pipe
   // memory attention: its per-layer body replayed from a CUDA graph (mem_attn.cpp)
@@ -239,7 +257,7 @@ struct s3b_ctx {
   long long n_launches = 0;
   bool prof = false;
   struct Prof {
-    int kind;  // 0 GEMM, 1 attention, 2 LayerNorm
+    int kind;  // 0 GEMM, 1 attention, 2 LayerNorm, 3 block-form weight staging
     double flops, bytes;
     cudaEvent_t a, b;
   };
@@ -252,6 +270,10 @@ struct s3b_ctx {
 };
 
 namespace s3b {
+// C-ABI status of a kernel launcher's negative code: -1..-9 argument checks and -11 (a pointer or
+// row stride that is not 16-byte aligned) are the caller's arguments; -10 (no tensor-map encoder
+// from the driver) and below -11 are CUDA failures.
+inline int launcher_status_code(int rc) { return (rc == -10 || rc < -11) ? kErrCuda : kErrArg; }
 int set_error(s3b_ctx* ctx, int code, const char* fmt, ...);
 int check_device(s3b_ctx* ctx, const char* where);
 
@@ -274,6 +296,20 @@ void count_launch(s3b_ctx* ctx, int n = 1);
 EpiParams epi_store(const Linear& L, void* out, int out_f32, long long ldo, int act = ACT_NONE);
 // RoPE table [npos][half_d][2] (cos, sin) -> the position-major [half_d][npos][2] the GEMM epilogue reads
 void rope_position_major(const std::vector<float>& in, int npos, int half_d, std::vector<float>& out);
+
+// Host-bound outputs (s3b_output_host_bind, capi.cpp). pass_begin: before pass `pass` (frames_per_pass
+// fb) writes its outputs, the context stream waits for the previous call's copy of the same frames.
+// pass_end: enqueues the copies of frames [f0, f0 + F) of every bound output on the copy stream after
+// the pass's work. Both are no-ops without bindings.
+int outputs_pass_begin(s3b_ctx* ctx, int pass, int fb);
+int outputs_pass_end(s3b_ctx* ctx, int pass, int f0, int F);
+
+// memory attention (mem_attn.cpp): from the caller's prompt arrays, or with the prompt built on the
+// device from the memory bank
+int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const float* prompt,
+                 const float* prompt_pos, int m_total, int n_ptr, float* out);
+int mem_attn_run_bank(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const PromptArgs& pa,
+                      float* out);
 
 // encoders
 int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);

@@ -29,7 +29,9 @@
 
 #include <stdio.h>
 
+#include <map>
 #include <mutex>
+#include <utility>
 
 namespace s3b {
 
@@ -46,6 +48,29 @@ constexpr uint32_t kStageBufBytes = 16384;  // 128 rows x 128 B
 
 int g_gemm_pairs = 1;         // 256-row tiles on SM pairs: 0 never, 1 long-K GEMMs, 2 every wide GEMM
 int g_gemm_wide_epi = 1;      // 16 epilogue warps for short-K GEMMs: 0 never, 1 always
+
+// kernel_setup callbacks: co-resident work units of a persistent GEMM on the current device, one CTA
+// per SM, or one cluster of 2 CTAs per SM pair (the cluster occupancy query)
+int sm_units(const void*, size_t, int) { return num_sms(); }
+int pair_units(const void* kernel, size_t smem, int threads) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (num_sms() / 2));
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return -13;
+  }
+  return n;
+}
 
 
 // Two f32 -> one packed f16x2 register (lo in the low half), round to nearest even.
@@ -98,6 +123,39 @@ __device__ __forceinline__ uint4 dequant8_q8(uint2 w, uint32_t d2) {
   o.z = h2_mul(h2_sub(byte_perm(u1, 0x64u, 0x4140u), off), d2);
   o.w = h2_mul(h2_sub(byte_perm(u1, 0x64u, 0x4342u), off), d2);
   return o;
+}
+
+// Block-form planes -> f16 rows [N][ldo] (the staged path of weights_quantised = 1): one thread
+// per 32-value block; consecutive threads take consecutive blocks of a row, so the value loads (16
+// or 32 bytes each) and the 64-byte f16 stores are contiguous across a warp. The values are the
+// same round_f16(q * d) the in-GEMM dequantisation and the load-time conversion produce.
+template <int QB>
+__global__ void __launch_bounds__(256) dequant_planes_kernel(const uint8_t* __restrict__ values,
+                                                             const uint16_t* __restrict__ scales, int N, int K,
+                                                             __half* __restrict__ out, long long ldo) {
+  const int nb = K / 32;
+  const long long total = (long long)N * nb;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(i / nb), kb = (int)(i - (long long)n * nb);
+    const uint32_t d = scales[(long long)kb * N + n];
+    const uint32_t d2 = d | (d << 16);
+    uint4* o = reinterpret_cast<uint4*>(out + (long long)n * ldo + (long long)kb * 32);
+    if (QB == 1) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(values + (long long)n * (K / 2) + (long long)kb * 16));
+      o[0] = dequant8_q4(w.x, d2);
+      o[1] = dequant8_q4(w.y, d2);
+      o[2] = dequant8_q4(w.z, d2);
+      o[3] = dequant8_q4(w.w, d2);
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(values + (long long)n * K + (long long)kb * 32);
+      const uint4 a = __ldg(src), b = __ldg(src + 1);
+      o[0] = dequant8_q8(make_uint2(a.x, a.y), d2);
+      o[1] = dequant8_q8(make_uint2(a.z, a.w), d2);
+      o[2] = dequant8_q8(make_uint2(b.x, b.y), d2);
+      o[3] = dequant8_q8(make_uint2(b.z, b.w), d2);
+    }
+  }
 }
 
 // All loops over the 16 values below are fully unrolled with compile-time
@@ -980,30 +1038,10 @@ int launch_gemm(const __half* A, long long lda, const void* B, long long ldb, in
   static_assert(smem <= 232448, "shared memory per CTA");
   auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR, EW, BLK, QB, QS>;
   constexpr int kThreads = gemm_threads(EW, DW);
-  static bool attr_set = false;
-  static int max_units = 0;  // co-resident CTAs (or pairs)
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return -13;
-    max_units = num_sms();
-    if (PAIR) {
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 2;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(2 * (num_sms() / 2));
-      cfg.blockDim = dim3(kThreads);
-      cfg.dynamicSmemBytes = smem;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) return -13;
-      max_units = n;
-    }
-    attr_set = true;
-  }
+  // co-resident CTAs (or SM pairs), set up once per device
+  const int max_units = kernel_setup(reinterpret_cast<const void*>(kernel), smem,
+                                     PAIR ? pair_units : sm_units, kThreads);
+  if (max_units <= 0) return -13;
   const int tm = PAIR ? 2 * kBM : kBM;
   const int tiles = ((M + tm - 1) / tm) * ((N + BN - 1) / BN);
   const int units = tiles < max_units ? tiles : max_units;
@@ -1043,15 +1081,42 @@ int launch_status(const char* what) {
   return -14;
 }
 
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_sms_mu;    // guards g_sms
+std::mutex g_setup_mu;  // guards g_setup (num_sms may be called while it is held)
+int g_sms[kMaxDevices] = {0};
+// (device, kernel) -> the value kernel_setup computed there
+std::map<std::pair<int, const void*>, int> g_setup;
+}  // namespace
+
 int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  std::lock_guard<std::mutex> lock(g_sms_mu);
+  if (g_sms[dev] == 0) {
+    int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+    g_sms[dev] = n > 0 ? n : 148;
   }
-  return n;
+  return g_sms[dev];
+}
+
+int kernel_setup(const void* kernel, size_t smem, int (*units)(const void*, size_t, int), int threads) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -13;
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  const auto key = std::make_pair(dev, kernel);
+  const auto it = g_setup.find(key);
+  if (it != g_setup.end()) return it->second;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+    cudaGetLastError();
+    return -13;
+  }
+  const int v = units ? units(kernel, smem, threads) : 1;
+  if (v <= 0) return -13;
+  g_setup[key] = v;
+  return v;
 }
 
 // Checks the epilogue parameters of a plain GEMM and decides whether its output leaves through the
@@ -1125,6 +1190,21 @@ static int gemm_q_launch(const __half* A, long long lda, const QWeight& w, int M
     return launch_gemm<256, 4, true, true, 8, 0, QB, QSP>(A, lda, w.values, 0, M, N, K, ep, rip, err, st, w.scales);
   }
   return launch_gemm<256, 3, false, false, 8, 0, QB, QSD>(A, lda, w.values, 0, M, N, K, ep, 0, err, st, w.scales);
+}
+
+int dequant_planes_f16(const QWeight& w, int N, int K, __half* out, long long ldo, cudaStream_t st) {
+  if (N <= 0 || K <= 0 || K % 32 || ldo < K || ldo % 8 || !w.values || !w.scales || !out) return -2;
+  if ((reinterpret_cast<uintptr_t>(w.values) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return -11;
+  const long long total = (long long)N * (K / 32);
+  const long long cap = (long long)num_sms() * 8;
+  const long long want = (total + 255) / 256;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  const uint16_t* sc = reinterpret_cast<const uint16_t*>(w.scales);
+  const uint8_t* v = reinterpret_cast<const uint8_t*>(w.values);
+  if (w.type == QT_Q4_0) dequant_planes_kernel<1><<<grid, 256, 0, st>>>(v, sc, N, K, out, ldo);
+  else if (w.type == QT_Q8_0) dequant_planes_kernel<2><<<grid, 256, 0, st>>>(v, sc, N, K, out, ldo);
+  else return -2;
+  return launch_status("dequant_planes");
 }
 
 int gemm_q(const __half* A, long long lda, const QWeight& w, int M, int N, int K, const EpiParams& ep, int* err,

@@ -22,7 +22,7 @@ namespace s3b {
   do {                                                                                                     \
     int _rc = (call);                                                                                      \
     count_launch(ctx);                                                                                     \
-    if (_rc) return set_error(ctx, _rc < -9 ? kErrCuda : kErrArg, "%s failed (%d)", #call, _rc);          \
+    if (_rc) return set_error(ctx, launcher_status_code(_rc), "%s failed (%d)", #call, _rc);          \
   } while (0)
 #define CKR(call)        \
   do {                   \
@@ -202,6 +202,7 @@ int hiera_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
   for (int f0 = 0; f0 < n_frames; f0 += FB) {
     const int F = (n_frames - f0) < FB ? (n_frames - f0) : FB;
     const long long T0 = (long long)F * S0 * S0;
+    if ((rc = outputs_pass_begin(ctx, f0 / FB, FB))) return rc;
     // patch embed: conv 7x7 / s4 / p3 + bias, + PE (sam3.cpp:4469-4490)
     CKH(im2col_image(d_chw + (size_t)f0 * 3 * img * img, F, 3, img, img, 7, 4, 3, S0, S0, col->as<__half>(), Kp,
                      ctx->stream));
@@ -240,6 +241,7 @@ int hiera_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
       if (cudaMemcpyAsync(O.backbone->as<float>() + (size_t)f0 * per_frame, x, (size_t)F * per_frame * 4,
                           cudaMemcpyDeviceToDevice, ctx->stream) != cudaSuccess)
         return set_error(ctx, kErrCuda, "backbone copy failed");
+      CKR(outputs_pass_end(ctx, f0 / FB, f0, F));
       continue;
     }
     // FPN neck (sam3.cpp:4532-4603): lateral 1x1 convs, nearest 2x top-down adds, scalp
@@ -265,6 +267,7 @@ int hiera_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
         prev_S = Si;
       }
     }
+    CKR(outputs_pass_end(ctx, f0 / FB, f0, F));
   }
   if (!want_neck) O.n_fpn = 0;
   return check_device(ctx, "hiera_encode");

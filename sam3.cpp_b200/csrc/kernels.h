@@ -174,6 +174,28 @@ int add_scaled_f32(const float* a, const float* b, float s, long long n, float* 
 // y = f16(a + s*b) (b may be null: y = f16(a)).
 int add_scaled_to_f16(const float* a, const float* b, float s, long long n, __half* y, cudaStream_t st);
 
+// Memory-attention prompt (sam3_build_prompt_and_pos, sam3.cpp:9123-9209) built on the device from
+// the memory bank: rows [0, n_slots*slot_tokens) are the spatial memory tokens of the slots in
+// order (prompt = slot features, prompt_pos = slot PE + the slot's temporal PE row when it has
+// one), then n_ptr kept object pointers, each split into `split` tokens of 64 values (prompt = the
+// pointer's values t*64..t*64+63, prompt_pos = its projected 1-D sine PE). The temporal and
+// pointer PE rows are host-computed and travel in the parameter block.
+constexpr int kPromptMaxSlots = 16, kPromptMaxPtrs = 16, kPromptMD = 64;
+struct PromptArgs {
+  const float* feat[kPromptMaxSlots];  // [slot_tokens][64] f32 each
+  const float* pe[kPromptMaxSlots];    // [slot_tokens][64] f32 each
+  float tpos[kPromptMaxSlots][kPromptMD];
+  int has_tpos[kPromptMaxSlots];
+  int n_slots = 0, slot_tokens = 0;
+  const float* ptrs = nullptr;  // [n_src][split*64] f32
+  int ptr_src[kPromptMaxPtrs];  // source row of the k-th kept pointer
+  float ptr_pe[kPromptMaxPtrs][kPromptMD];
+  int n_ptr = 0, split = 4;
+};
+// out_f16 = 0: a = prompt, b = prompt_pos (f32 [M][64]); out_f16 = 1: a = f16(prompt + prompt_pos),
+// b = f16(prompt) (the cross-attention key and value inputs, sam3.cpp:9278-9283).
+int build_prompt(const PromptArgs& args, void* a, void* b, int out_f16, cudaStream_t st);
+
 // ggml block formats (32 values per block along the row).
 enum QType : int { QT_F32 = 0, QT_F16 = 1, QT_Q4_0 = 2, QT_Q4_1 = 3, QT_Q8_0 = 8 };
 long long qtype_row_bytes(int qtype, long long ne0);
@@ -198,9 +220,23 @@ int repack_q_rows(const void* src, int qtype, int N, int K, void* values, __half
 // tensor cores read); same epilogues and results as gemm_f16 on the dequantised weight.
 int gemm_q(const __half* A, long long lda, const QWeight& w, int M, int N, int K, const EpiParams& ep, int* err,
            cudaStream_t st);
+// Block-form planes of a q4_0 / q8_0 weight -> f16 rows out [N][ldo] (K a multiple of 32, ldo a
+// multiple of 8, out 16-byte aligned), values round_f16(q * d) as the load-time dequantisation.
+int dequant_planes_f16(const QWeight& w, int N, int K, __half* out, long long ldo, cudaStream_t st);
 
-// Returns the number of SMs of the current device (cached).
+// Returns the number of SMs of the current device (cached per device).
 int num_sms();
+
+// Once per (current device, kernel): sets the kernel's dynamic shared-memory limit to `smem` (a
+// per-device-context attribute) and, when `units` is given, computes and caches an integer (e.g.
+// co-resident CTAs) on that device. Later calls on the same device return the cached value.
+// Thread-safe. Returns the value (1 without `units`) or -13 when CUDA refuses the set-up.
+int kernel_setup(const void* kernel, size_t smem, int (*units)(const void* kernel, size_t smem, int threads),
+                 int threads);
+template <typename K>
+inline int kernel_setup(K* kernel, size_t smem) {
+  return kernel_setup(reinterpret_cast<const void*>(kernel), smem, nullptr, 0);
+}
 
 // Status of the last launch: 0, or -14 after printing the CUDA error (a
 // failed launch, or an earlier asynchronous fault reported at this point).

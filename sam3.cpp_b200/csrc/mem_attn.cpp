@@ -21,7 +21,7 @@ namespace s3b {
   do {                                                                                                     \
     int _rc = (call);                                                                                      \
     count_launch(ctx);                                                                                     \
-    if (_rc) return set_error(ctx, _rc < -9 ? kErrCuda : kErrArg, "%s failed (%d)", #call, _rc);          \
+    if (_rc) return set_error(ctx, launcher_status_code(_rc), "%s failed (%d)", #call, _rc);          \
   } while (0)
 #define CKR(call)           \
   do {                      \
@@ -155,8 +155,11 @@ static int mem_attn_layers(s3b_ctx* ctx, const MemAttnBufs& b) {
   return kOk;
 }
 
-int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const float* prompt,
-                 const float* prompt_pos, int m_total, int n_ptr, float* out) {
+// Memory attention with its cross-attention inputs built by `prep` (prompt + prompt_pos -> kvin,
+// prompt -> pin, both f16 [Mt][64]) from the caller's prompt arrays or on the device from the memory bank.
+template <typename Prep>
+static int mem_attn_body(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, int m_total, int n_ptr,
+                         float* out, Prep prep) {
   const Model& M = ctx->model;
   const int D = M.hp.neck_dim, MD = M.hp.mem_out_dim;
   const long long N = (long long)feat * feat;
@@ -183,8 +186,7 @@ int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat
   // pos_enc_at_input: x = curr + 0.1 * src_pos (sam3.cpp:9243)
   CKL(add_scaled_f32(curr, src_pos, 0.1f, N * D, X, ctx->stream));
   // memory keys see prompt + prompt_pos, values see prompt (sam3.cpp:9278-9283)
-  CKL(add_scaled_to_f16(prompt, prompt_pos, 1.0f, Mt * MD, kvin->as<__half>(), ctx->stream));
-  CKL(add_scaled_to_f16(prompt, nullptr, 0.0f, Mt * MD, pin->as<__half>(), ctx->stream));
+  CKR(prep(kvin->as<__half>(), pin->as<__half>()));
   MemAttnBufs mb;
   mb.X = X;
   mb.XN = XN;
@@ -252,6 +254,25 @@ int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat
   // final norm (sam3.cpp:9330-9334)
   CKL(run_ln(ctx, X, D, out, 1, D, N, D, M.mem_norm_w.ptr(), M.mem_norm_b.ptr(), 1e-5f, id));
   return check_device(ctx, "mem_attn");
+}
+
+int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const float* prompt,
+                 const float* prompt_pos, int m_total, int n_ptr, float* out) {
+  const long long n = (long long)m_total * ctx->model.hp.mem_out_dim;
+  return mem_attn_body(ctx, curr, src_pos, feat, m_total, n_ptr, out, [&](__half* kvin, __half* pin) {
+    CKL(add_scaled_to_f16(prompt, prompt_pos, 1.0f, n, kvin, ctx->stream));
+    CKL(add_scaled_to_f16(prompt, nullptr, 0.0f, n, pin, ctx->stream));
+    return (int)kOk;
+  });
+}
+
+int mem_attn_run_bank(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const PromptArgs& pa,
+                      float* out) {
+  const int m_total = pa.n_slots * pa.slot_tokens + pa.n_ptr * pa.split;
+  return mem_attn_body(ctx, curr, src_pos, feat, m_total, pa.n_ptr * pa.split, out, [&](__half* kvin, __half* pin) {
+    CKL(build_prompt(pa, kvin, pin, 1, ctx->stream));
+    return (int)kOk;
+  });
 }
 
 }  // namespace s3b

@@ -93,8 +93,18 @@ static void parallel_for(int64_t n, int64_t min_chunk, F fn) {
     fn((int64_t)0, n);
     return;
   }
+  // chunks whose thread could not be started (a thread or resource limit) run on this thread, so no
+  // exception leaves the C ABI
   std::vector<std::thread> th;
-  for (int64_t c = 0; c < parts; ++c) th.emplace_back([&, c]() { fn(n * c / parts, n * (c + 1) / parts); });
+  int64_t started = 0;
+  try {
+    for (; started < parts; ++started) {
+      const int64_t c = started;
+      th.emplace_back([&, c]() { fn(n * c / parts, n * (c + 1) / parts); });
+    }
+  } catch (...) {
+  }
+  for (int64_t c = started; c < parts; ++c) fn(n * c / parts, n * (c + 1) / parts);
   for (auto& x : th) x.join();
 }
 
@@ -326,6 +336,7 @@ int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Lin
     if (cudaStreamSynchronize(ctx->stream) != cudaSuccess)
       return set_error(ctx, kErrCuda, "repack of %s failed", t.name.c_str());
     ctx->model.device_bytes += vbytes + (size_t)N * (K / 32) * 2;
+    ctx->model.qstage_elems = std::max(ctx->model.qstage_elems, (size_t)N * K);
     ctx->model.device_bytes -= t.data.size();  // the uploaded rows are released here
   } else {
     std::vector<float> w;
@@ -836,6 +847,11 @@ int load_model(s3b_ctx* ctx, const std::string& path) {
   cudaSetDevice(ctx->device);
   rc = hp.is_sam2 ? load_sam2(ctx, idx) : load_sam3(ctx, idx);
   if (rc) return rc;
+  if (ctx->model.qstage_elems > 0) {
+    // the staging buffer is sized once here, so it never moves under a captured graph
+    ctx->buf("wq_stage", ctx->model.qstage_elems * 2, &rc);
+    if (rc) return rc;
+  }
   ctx->model.loaded = true;
   return kOk;
 }

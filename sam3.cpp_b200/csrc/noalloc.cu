@@ -19,7 +19,10 @@
 //
 // All calls share the array and it keeps the previous call's contents: the
 // error word is cleared at the start of every call; the im2col region is
-// fully rewritten before it is read. Calls whose work overlaps on the GPU
+// fully rewritten before it is read. The call only enqueues work, so a
+// device-side failure (a bounded wait in the GEMM that timed out) cannot be
+// in its return code: s3b_conv3x3_noalloc_status reads (and clears) the
+// error word once the caller has waited for the stream. Calls whose work overlaps on the GPU
 // (different streams, or different host threads without ordering) race on
 // the array and must be serialised by the caller.
 #include <stdio.h>
@@ -91,5 +94,27 @@ extern "C" int s3b_conv3x3_noalloc(const void* x, int B, int H, int W, int C, co
   ep.out_f32 = 1;
   ep.ldo = Cout;
   rc = s3b::gemm_f16(col, 9LL * C, reinterpret_cast<const __half*>(w), 9LL * C, (int)M, Cout, 9 * C, ep, err, st);
-  return rc == 0 ? S3B_OK : (rc < -9 ? S3B_ERR_CUDA : S3B_ERR_ARG);
+  // launcher codes: -1..-11 argument / alignment checks (-11: a pointer or row stride not 16-byte
+  // aligned, -10 no tensor-map encoder), below -11 CUDA errors
+  if (rc == 0) return S3B_OK;
+  if (rc == -10) return S3B_ERR_CUDA;
+  return rc < -11 ? S3B_ERR_CUDA : S3B_ERR_ARG;
+}
+
+extern "C" int s3b_conv3x3_noalloc_status(int* code) {
+  if (!code) return S3B_ERR_ARG;
+  *code = 0;
+  int h = 0;
+  // the word is the first int of the scratch array on the current device (no allocation, no lookup)
+  cudaError_t e = cudaMemcpyFromSymbol(&h, g_noalloc_scratch, sizeof(int), 0, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    fprintf(stderr, "s3b_conv3x3_noalloc_status: reading the error word failed: %s\n", cudaGetErrorString(e));
+    return S3B_ERR_CUDA;
+  }
+  if (h == 0) return S3B_OK;
+  *code = h;
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(g_noalloc_scratch, &zero, sizeof(int), 0, cudaMemcpyHostToDevice);
+  fprintf(stderr, "s3b_conv3x3_noalloc: a bounded device wait timed out (code %d); the output is incomplete\n", h);
+  return e == cudaSuccess ? S3B_ERR_DEVICE : S3B_ERR_CUDA;
 }

@@ -48,12 +48,37 @@ int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long
     qw.type = L.qtype;
     qw.values = L.qv->p;
     qw.scales = L.qs->as<__half>();
-    rc = gemm_q(A, lda, qw, (int)M, L.N, L.K, ep, ctx->d_err, ctx->stream);
+    if (ctx->weights_quantised == 2) {
+      rc = gemm_q(A, lda, qw, (int)M, L.N, L.K, ep, ctx->d_err, ctx->stream);
+    } else {
+      // the weight is read from HBM in block form once and written as f16 into the staging buffer,
+      // which the GEMM then reads from L2 across its tile sweep
+      const auto it = ctx->ws.find("wq_stage");
+      if (it == ctx->ws.end() || !it->second || it->second->bytes < (size_t)L.N * L.K * 2)
+        return set_error(ctx, kErrState, "no staging buffer for block-form weights (model not loaded with it)");
+      __half* stage = it->second->as<__half>();
+      cudaEvent_t da = nullptr, db = nullptr;
+      if (ctx->prof) {
+        da = ctx->next_event();
+        db = ctx->next_event();
+        cudaEventRecord(da, ctx->stream);
+      }
+      rc = dequant_planes_f16(qw, L.N, L.K, stage, L.K, ctx->stream);
+      count_launch(ctx);
+      if (rc) return set_error(ctx, launcher_status_code(rc), "weight staging N=%d K=%d failed (%d)", L.N, L.K, rc);
+      if (ctx->prof) {
+        cudaEventRecord(db, ctx->stream);
+        const double qbytes = L.qtype == QT_Q4_0 ? L.N * (L.K / 2.0 + L.K / 16.0) : L.N * (L.K + L.K / 16.0);
+        ctx->prof_entries.push_back({3, 0.0, qbytes + 2.0 * L.N * L.K, da, db});
+      }
+      if (ctx->prof) cudaEventRecord(a, ctx->stream);  // the GEMM's own time starts after the staging
+      rc = gemm_f16(A, lda, stage, L.K, (int)M, L.N, L.K, ep, ctx->d_err, ctx->stream);
+    }
   } else {
     rc = gemm_f16(A, lda, L.w->as<__half>(), L.Kpad, (int)M, L.N, L.Kpad, ep, ctx->d_err, ctx->stream);
   }
   count_launch(ctx);
-  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "gemm M=%lld N=%d K=%d failed (%d)", M, L.N, L.Kpad, rc);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "gemm M=%lld N=%d K=%d failed (%d)", M, L.N, L.Kpad, rc);
   if (ctx->prof) {
     cudaEventRecord(b, ctx->stream);
     // algorithmic work: 2*M*N*K flops; bytes: A + B (f16, or the block values + f16 scales) + output
@@ -82,7 +107,7 @@ int run_conv3x3(s3b_ctx* ctx, const Linear& L, const __half* x, int F, int H, in
     const int rc = gemm_conv3x3(x, F, H, W, C, L.w->as<__half>(), L.Kpad, L.N, ep, ctx->d_err, ctx->stream);
     if (rc != -2) {
       count_launch(ctx);
-      if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "implicit conv3x3 failed (%d)", rc);
+      if (rc) return set_error(ctx, launcher_status_code(rc), "implicit conv3x3 failed (%d)", rc);
       if (ctx->prof) {
         cudaEventRecord(b, ctx->stream);
         const double bytes = 2.0 * M * C + 2.0 * L.N * L.K + (ep.out_f32 ? 4.0 : 2.0) * M * L.N;
@@ -114,7 +139,7 @@ int run_deconv2x2(s3b_ctx* ctx, const Linear& L, const __half* x, int F, int H, 
     const int rc = gemm_deconv2x2(x, F, H, W, L.K, L.w->as<__half>(), L.Kpad, cout, ep, ctx->d_err, ctx->stream);
     if (rc != -2) {
       count_launch(ctx);
-      if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "deconv2x2 failed (%d)", rc);
+      if (rc) return set_error(ctx, launcher_status_code(rc), "deconv2x2 failed (%d)", rc);
       if (ctx->prof) {
         cudaEventRecord(b, ctx->stream);
         const double bytes = 2.0 * M * L.K + 2.0 * L.N * L.K + (ep.out_f32 ? 4.0 : 2.0) * M * L.N;
@@ -189,7 +214,7 @@ int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
     if (rc == -2) rc = attention(p, D, batch_heads, ctx->stream);
   }
   count_launch(ctx);
-  if (rc) return set_error(ctx, rc < -9 ? kErrCuda : kErrArg, "attention D=%d failed (%d)", D, rc);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "attention D=%d failed (%d)", D, rc);
   if (ctx->prof) {
     cudaEventRecord(b, ctx->stream);
     const double flops = 4.0 * p.nq * (double)p.nk * D * batch_heads;

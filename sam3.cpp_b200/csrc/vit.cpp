@@ -19,7 +19,7 @@ namespace s3b {
   do {                                                                                                    \
     int _rc = (call);                                                                                     \
     count_launch(ctx);                                                                                    \
-    if (_rc) return set_error(ctx, _rc < -9 ? kErrCuda : kErrArg, "%s failed (%d) at %s:%d", #call, _rc, \
+    if (_rc) return set_error(ctx, launcher_status_code(_rc), "%s failed (%d) at %s:%d", #call, _rc, \
                               __FILE__, __LINE__);                                                        \
   } while (0)
 #define CKG(call)                                                                                         \
@@ -198,6 +198,7 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
   for (int f0 = 0; f0 < n_frames; f0 += FB) {
     const int F = (n_frames - f0) < FB ? (n_frames - f0) : FB;
     const long long T = (long long)F * tok_per_frame;
+    if ((rc = outputs_pass_begin(ctx, f0 / FB, FB))) return rc;
     float* x = O.backbone->as<float>() + (size_t)f0 * tok_per_frame * E;
     // patch embed (conv 14x14/s14, no bias) + tiled abs pos (sam3.cpp:3815-3822)
     CK(im2col_image(d_chw + (size_t)f0 * 3 * S * S, F, 3, S, S, P, P, 0, G, G, col->as<__half>(), Kp, ctx->stream));
@@ -231,6 +232,7 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
         if ((rc = vit_neck(ctx, M.neck_det, xh, F, outs))) return rc;
       }
     }
+    if ((rc = outputs_pass_end(ctx, f0 / FB, f0, F))) return rc;
   }
   return check_device(ctx, "vit_encode");
 }

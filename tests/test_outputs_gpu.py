@@ -1,0 +1,84 @@
+"""The engine's output contract on the GPU:
+
+- the "neck_trk_pe_i" outputs (sam3_sinusoidal_pe_2d, sam3.cpp:3597-3633) served by s3b_output_copy and by
+  s3b_output_device_ptr are bit-exact against the oracle at the SAM 3 and SAM 2 level sizes;
+- outputs bound to host memory with s3b_output_host_bind (the host copy of state.neck_trk that
+  sam3_propagate_single makes, sam3.cpp:11378-11391, overlapped with the next encoder pass) hold exactly
+  what s3b_output_copy returns, over several passes per call and over consecutive calls.
+"""
+import numpy as np
+import pytest
+
+from oracle import nn
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _tiny_vit(s3b, tmp_path):
+    from sam3_b200 import synth
+    cfg = synth.Sam3Config(img_size=336, patch=14, embed=256, depth=2, heads=4, window=8, global_idx=(1,),
+                           neck_dim=64, neck_mid=128)
+    path = str(tmp_path / "pe_vit.ggml")
+    synth.write_sam3(path, cfg, seed=12, ftype=1, qtype=2, quantize=s3b.quantize_rows)
+    return cfg, path
+
+
+def test_neck_pe_outputs_bit_exact(engine, s3b, tmp_path):
+    from sam3_b200 import synth
+    cfg, path = _tiny_vit(s3b, tmp_path)
+    engine.load_model(path)
+    engine.encode_u8(synth.frames_u8(1, cfg.img_size, base_seed=3))
+    engine.sync()
+    G = cfg.grid
+    for i, S in enumerate([4 * G, 2 * G, G, G // 2]):
+        ref = nn.sine_pe_2d(S, S, cfg.neck_dim)
+        got = engine.output(f"neck_trk_pe_{i}", 0)
+        assert np.array_equal(got, ref), i
+        ptr = engine.output_device_ptr(f"neck_trk_pe_{i}", 0)
+        dev = torch.empty(S * S * cfg.neck_dim, device="cuda")
+        torch.cuda.synchronize()
+        src = torch.as_tensor(_CudaArray(ptr, S * S * cfg.neck_dim), device="cuda")
+        dev.copy_(src)
+        assert np.array_equal(dev.cpu().numpy().reshape(S, S, cfg.neck_dim), ref), i
+    # the SAM 2 / memory-attention sizes, through the host helper the outputs use
+    for S in (256, 128, 64):
+        assert np.array_equal(s3b.sine_pe_2d(S, S, 256), nn.sine_pe_2d(S, S, 256))
+
+
+class _CudaArray:
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, True), "version": 3}
+
+
+@pytest.mark.parametrize("n_frames,per_pass", [(5, 2), (3, 8)])
+def test_host_bound_outputs_equal_output_copy(s3b, tmp_path, n_frames, per_pass):
+    from sam3_b200 import synth
+    cfg, path = _tiny_vit(s3b, tmp_path)
+    eng = s3b.Engine(0)
+    try:
+        eng.set_option("frames_per_pass", per_pass)
+        eng.load_model(path)
+        G = cfg.grid
+        names = [f"neck_trk_{i}" for i in range(3)]
+        sizes = [4 * G, 2 * G, G]
+        host = {n: torch.zeros(n_frames, S, S, cfg.neck_dim).pin_memory() for n, S in zip(names, sizes)}
+        for n in names:
+            eng.output_host_bind(n, host[n])
+        for call in range(2):  # the second call overwrites the first one's slots after their copies finished
+            frames = synth.frames_u8(n_frames, cfg.img_size, base_seed=50 + 10 * call)
+            eng.encode_u8(frames)
+            eng.sync()
+            for n in names:
+                for f in range(n_frames):
+                    assert np.array_equal(host[n][f].numpy(), eng.output(n, f)), (call, n, f)
+        with pytest.raises(s3b.S3BError):
+            eng.output_host_bind("neck_trk_pe_0", host[names[0]])  # host-computed PE: not bindable
+        small = torch.zeros(1, 4 * G, 4 * G, cfg.neck_dim).pin_memory()
+        eng.output_host_bind(names[0], small)
+        with pytest.raises(s3b.S3BError):
+            eng.encode_u8(synth.frames_u8(n_frames, cfg.img_size, base_seed=7))  # too small for n_frames
+        for n in names:
+            eng.output_host_bind(n, None)
+    finally:
+        eng.close()
