@@ -115,6 +115,29 @@ int s3b_profile_end(s3b_ctx* ctx, double* out, int n);
  * tensors outside the engine's scope are skipped. */
 int s3b_load_model(s3b_ctx* ctx, const char* path);
 
+/* A weight tensor in the caller's host memory, as sam3.cpp holds it after
+ * sam3_load_tensors (sam3.cpp:3091-3194): the .ggml tensor name, its ggml
+ * type, shape in ggml order (ne[0] contiguous; unused dims 1) and data in
+ * ggml row layout (s3b_row_size(dtype, ne[0]) bytes per row). */
+typedef struct s3b_tensor_desc {
+    const char* name;
+    int32_t dtype;
+    int32_t n_dims;
+    int64_t ne[4];
+    const void* data;
+} s3b_tensor_desc;
+
+/* Loads the weights from tensors the caller already holds (copied to the
+ * device, the host memory stays the caller's), so a sam3.cpp that has
+ * loaded its model does not parse the file a second time. hparams are the
+ * n_hparams i32 values of the file header after magic / version / ftype /
+ * n_tensors, in file order (SAM 3: sam3.cpp:1477-1520, is_sam2 = 0;
+ * SAM 2: 1564-1626, is_sam2 = 1); ftype is the file type. The result is the
+ * same device model as s3b_load_model on the file the tensors came from;
+ * tensors outside the engine's scope are skipped. */
+int s3b_load_weights(s3b_ctx* ctx, int is_sam2, const int32_t* hparams, int n_hparams, int ftype,
+                     const s3b_tensor_desc* descs, int n);
+
 /* Parses a .ggml file on the host only (no device needed) and checks every
  * record: info[0] = 1 for SAM 2 else 0, info[1] = img_size, info[2] = number
  * of tensor records, info[3] = file ftype, info[4] = backbone depth,
@@ -251,6 +274,17 @@ int s3b_mem_attn_bank(s3b_ctx* ctx, const float* curr, const float* src_pos, int
 int s3b_op_build_prompt(s3b_ctx* ctx, int feat, const float* const* slot_feats, const float* const* slot_pes,
                         const int* slot_tpos, int n_slots, const float* obj_ptrs, const int* ptr_tpos, int n_ptrs,
                         float* prompt, float* prompt_pos, int64_t capacity_rows, int* m_total, int* n_ptr_tokens);
+
+/* Test hook for the engine's failure detection: enqueues on the context
+ * stream one kernel that waits on a device barrier with the same bounded
+ * wait every GEMM / attention kernel uses, limited to limit_ns (0 < limit_ns
+ * <= 2e9). With withhold = 1 nothing completes the barrier, so the wait
+ * runs out, records its code in the context's device error word and the
+ * kernel returns; the next s3b_sync then reports S3B_ERR_DEVICE and clears
+ * the word, and the context stays usable. With withhold = 0 the barrier
+ * completes and s3b_sync returns S3B_OK. The reference has no device waits
+ * (its error path is "return false + stderr", sam3.cpp:1021-1022). */
+int s3b_test_wait_timeout(s3b_ctx* ctx, int64_t limit_ns, int withhold);
 
 /* Host helper: memory-bank slots memory attention reads
  * (sam3_select_memory_frames, sam3.cpp:9423-9447): every slot when

@@ -31,6 +31,12 @@ ERRORS = {
     -5: "S3B_ERR_STATE", -6: "S3B_ERR_UNSUPPORTED", -7: "S3B_ERR_DEVICE", -8: "S3B_ERR_OOM",
 }
 
+class TensorDesc(ctypes.Structure):
+    """s3b_tensor_desc: one caller-owned host tensor for s3b_load_weights."""
+    _fields_ = [("name", ctypes.c_char_p), ("dtype", ctypes.c_int32), ("n_dims", ctypes.c_int32),
+                ("ne", ctypes.c_int64 * 4), ("data", ctypes.c_void_p)]
+
+
 # Every symbol declared in include/sam3_b200.h: (name, restype, argtypes)
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -48,6 +54,7 @@ SYMBOLS = [
     ("s3b_profile_begin", _I, [_P, _I]),
     ("s3b_profile_end", _I, [_P, ctypes.POINTER(ctypes.c_double), _I]),
     ("s3b_load_model", _I, [_P, _S]),
+    ("s3b_load_weights", _I, [_P, _I, ctypes.POINTER(ctypes.c_int32), _I, _I, ctypes.POINTER(TensorDesc), _I]),
     ("s3b_inspect_model", _I, [_S, ctypes.POINTER(ctypes.c_int32), _I, _S, _I]),
     ("s3b_model_info", _I, [_P, ctypes.POINTER(ctypes.c_int32), _I]),
     ("s3b_encode_u8", _I, [_P, _P, _I, _I, _I]),
@@ -70,6 +77,7 @@ SYMBOLS = [
     ("s3b_mem_attn_bank", _I, [_P, _P, _P, _I, _P, _P, _P, _I, _P, _P, _I, _P]),
     ("s3b_op_build_prompt", _I, [_P, _I, _P, _P, _P, _I, _P, _P, _I, _P, _P, _I64, ctypes.POINTER(_I),
                                  ctypes.POINTER(_I)]),
+    ("s3b_test_wait_timeout", _I, [_P, _I64, _I]),
     ("s3b_select_memory_frames", _I, [_I, _I, ctypes.POINTER(_I), _I]),
     ("s3b_sine_pe_2d", _I, [_I, _I, _I, _P]),
     ("s3b_op_gemm", _I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _P, _I, _P, _I, _I64, _P, _I64]),
@@ -254,6 +262,19 @@ class Engine:
 
     def load_model(self, path: str):
         self._check(self._L.s3b_load_model(self.h, path.encode()), "s3b_load_model")
+
+    def load_weights(self, is_sam2: int, hparams, ftype: int, tensors):
+        """s3b_load_weights from host tensors: tensors = [(name, dtype, shape (PyTorch order), bytes-like)]."""
+        descs = (TensorDesc * len(tensors))()
+        keep = []
+        for i, (name, dtype, shape, data) in enumerate(tensors):
+            buf = np.frombuffer(data, dtype=np.uint8)
+            keep.append(buf)
+            ne = list(reversed(shape)) + [1] * (4 - len(shape))
+            descs[i] = TensorDesc(name.encode(), dtype, len(shape), (ctypes.c_int64 * 4)(*ne), buf.ctypes.data)
+        hp = (ctypes.c_int32 * len(hparams))(*[int(v) for v in hparams])
+        self._check(self._L.s3b_load_weights(self.h, is_sam2, hp, len(hparams), ftype, descs, len(tensors)),
+                    "s3b_load_weights")
 
     def model_info(self) -> dict:
         buf = (ctypes.c_int32 * 7)()

@@ -529,6 +529,48 @@ int s3b_load_model(s3b_ctx* ctx, const char* path) {
   return load_model(ctx, path);
 }
 
+int s3b_load_weights(s3b_ctx* ctx, int is_sam2, const int32_t* hparams, int n_hparams, int ftype,
+                     const s3b_tensor_desc* descs, int n) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!hparams || n_hparams <= 0 || !descs || n <= 0) return set_error(ctx, kErrArg, "bad load_weights arguments");
+  HParams hp;
+  std::string err;
+  if ((rc = parse_hparams_array(is_sam2, hparams, n_hparams, hp, err))) return set_error(ctx, rc, "%s", err.c_str());
+  hp.ftype = ftype;
+  // the caller's tensors as the file reader would return them (sam3_load_tensors, sam3.cpp:3091-3194):
+  // same names, ggml shapes and dtypes, data in ggml row layout
+  std::vector<FileTensor> tensors(n);
+  for (int i = 0; i < n; ++i) {
+    const s3b_tensor_desc& d = descs[i];
+    FileTensor& t = tensors[i];
+    if (!d.name || !d.data || d.n_dims < 1 || d.n_dims > 4)
+      return set_error(ctx, kErrArg, "tensor %d: bad descriptor", i);
+    t.name = d.name;
+    t.dtype = d.dtype;
+    t.n_dims = d.n_dims;
+    for (int k = 0; k < 4; ++k) {
+      t.ne[k] = k < d.n_dims ? d.ne[k] : 1;
+      if (t.ne[k] <= 0) return set_error(ctx, kErrArg, "tensor %s: bad shape", d.name);
+    }
+    int64_t bytes;
+    if (d.dtype == QT_F32 || d.dtype == QT_F16) {
+      bytes = t.nelements() * (d.dtype == QT_F16 ? 2 : 4);
+    } else if (d.dtype == QT_Q4_0 || d.dtype == QT_Q4_1 || d.dtype == QT_Q8_0) {
+      if (t.ne[0] % 32) return set_error(ctx, kErrFormat, "quantised tensor with ne0 %% 32 != 0: %s", d.name);
+      bytes = qtype_row_bytes(d.dtype, t.ne[0]) * (t.nelements() / t.ne[0]);
+    } else {
+      return set_error(ctx, kErrFormat, "unsupported dtype %d in %s", d.dtype, d.name);
+    }
+    const uint8_t* src = static_cast<const uint8_t*>(d.data);
+    t.data.assign(src, src + bytes);
+  }
+  ctx->out = Outputs();
+  ctx->ptr_pe_cache.clear();
+  ++ctx->graph_epoch;
+  return load_model_tensors(ctx, hp, tensors);
+}
+
 int s3b_inspect_model(const char* path, int32_t* info, int n, char* err, int err_len) {
   if (!path) return kErrArg;
   HParams hp;
@@ -808,6 +850,15 @@ int s3b_op_build_prompt(s3b_ctx* ctx, int feat, const float* const* slot_feats, 
                                              (long long)rows, (long long)capacity_rows);
   rc = build_prompt(pa, prompt, prompt_pos, 0, ctx->stream);
   if (rc) return set_error(ctx, launcher_status_code(rc), "prompt build launch failed (%d)", rc);
+  return kOk;
+}
+
+int s3b_test_wait_timeout(s3b_ctx* ctx, int64_t limit_ns, int withhold) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  rc = wait_probe(ctx->d_err, limit_ns, withhold, ctx->stream);
+  count_launch(ctx);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "wait probe: limit_ns must be in (0, 2e9] (%d)", rc);
   return kOk;
 }
 

@@ -84,19 +84,23 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // recording `code`) on timeout or when another role of the CTA aborted.
 // Between checks of the abort flag and of the time limit the waiting thread
 // sleeps in the barrier (up to 1 ms per try).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                              int code, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       if (err) atomicCAS(err, 0, code);
       *abort_flag = 1;
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err, int code) {
+  return mbar_wait_for(bar, parity, abort_flag, err, code, kWaitNs);
 }
 
 // As mbar_wait, with cluster-scope acquire: for phases completed by release

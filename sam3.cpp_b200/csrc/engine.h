@@ -83,6 +83,8 @@ struct HParams {
 };
 
 int read_ggml_file(const std::string& path, HParams& hp, std::vector<FileTensor>& tensors, std::string& err);
+// The hparam block of a .ggml header given as n i32 values in file order.
+int parse_hparams_array(int is_sam2, const int32_t* v, int n, HParams& hp, std::string& err);
 
 // f32 values of a file tensor (f32 / f16 / q4_0 / q4_1 / q8_0).
 void tensor_to_f32(const FileTensor& t, std::vector<float>& out);
@@ -129,6 +131,8 @@ struct Linear {
   int qtype = 0;                 // QT_Q4_0 / QT_Q8_0 when the weight is kept in block form
   std::shared_ptr<DevBuf> qv;    // q4_0 nibble plane [N][K/2] or q8_0 int8 plane [N][K]
   std::shared_ptr<DevBuf> qs;    // f16 block scales [K/32][N]
+  // set on a per-call copy by stage_linears: the f16 [N][K] staging copy the GEMM reads instead
+  const __half* staged = nullptr;
 };
 
 struct Vec {
@@ -189,7 +193,8 @@ struct Model {
   std::vector<float> maskmem_tpos;   // [num_maskmem][64]
   std::vector<float> obj_ptr_tpos_w, obj_ptr_tpos_b;  // [64][256], [64]
   size_t device_bytes = 0;
-  // largest N*K of a weight kept in block form: the f16 staging buffer of weights_quantised = 1
+  // largest N*K of a weight kept in block form; the f16 staging arena of weights_quantised = 1 holds
+  // the block-form weights of one ViT / Hiera block or memory-attention layer (stage_arena_elems)
   size_t qstage_elems = 0;
 };
 
@@ -279,6 +284,8 @@ int check_device(s3b_ctx* ctx, const char* where);
 
 // weight preparation (model.cpp)
 int load_model(s3b_ctx* ctx, const std::string& path);
+// Prepares the device weights from parsed tensors (the file reader's or the caller's).
+int load_model_tensors(s3b_ctx* ctx, const HParams& hp, const std::vector<FileTensor>& tensors);
 int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Linear& L, int kpad_to = 8,
                   int k_dims = 1);
 
@@ -293,6 +300,13 @@ int run_deconv2x2(s3b_ctx* ctx, const Linear& L, const __half* x, int F, int H, 
 int run_ln(s3b_ctx* ctx, const float* x, long long ldx, void* y, int y_f32, long long ldy, long long rows, int C,
            const float* g, const float* b, float eps, const RowMap& map);
 void count_launch(s3b_ctx* ctx, int n = 1);
+// weights_quantised = 1: dequantises the block-form weights among in[0..n) in one launch into
+// consecutive regions of the staging arena and sets out[i]->staged (out[i] starts as a copy of
+// *in[i]); f16 weights, and every weight under weights_quantised = 2, pass through unchanged.
+// The staged copies stay valid until the next stage_linears call on the context.
+int stage_linears(s3b_ctx* ctx, const Linear* const* in, Linear* const* out, int n);
+// f16 elements of the staging arena the loaded model needs (0 without block-form weights).
+size_t stage_arena_elems(const Model& M);
 EpiParams epi_store(const Linear& L, void* out, int out_f32, long long ldo, int act = ACT_NONE);
 // RoPE table [npos][half_d][2] (cos, sin) -> the position-major [half_d][npos][2] the GEMM epilogue reads
 void rope_position_major(const std::vector<float>& in, int npos, int half_d, std::vector<float>& out);

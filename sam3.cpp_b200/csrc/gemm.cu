@@ -158,6 +158,46 @@ __global__ void __launch_bounds__(256) dequant_planes_kernel(const uint8_t* __re
   }
 }
 
+struct StageJobs {
+  const uint8_t* values[kMaxStageJobs];
+  const uint16_t* scales[kMaxStageJobs];
+  __half* out[kMaxStageJobs];
+  int N[kMaxStageJobs], K[kMaxStageJobs], q4[kMaxStageJobs];
+  long long start[kMaxStageJobs + 1];  // first block index of each job (prefix sums of N * K / 32)
+  int n;
+};
+
+// The weights of one block / layer in one launch: a grid-stride loop over the concatenated 32-value
+// blocks of all jobs, each block done as in dequant_planes_kernel.
+__global__ void __launch_bounds__(256) dequant_planes_multi_kernel(const StageJobs J) {
+  const long long total = J.start[J.n];
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    int j = 0;
+    while (j + 1 < J.n && i >= J.start[j + 1]) ++j;
+    const long long b = i - J.start[j];
+    const int K = J.K[j], N = J.N[j], nb = K / 32;
+    const int n = (int)(b / nb), kb = (int)(b - (long long)n * nb);
+    const uint32_t d = J.scales[j][(long long)kb * N + n];
+    const uint32_t d2 = d | (d << 16);
+    uint4* o = reinterpret_cast<uint4*>(J.out[j] + (long long)n * K + (long long)kb * 32);
+    if (J.q4[j]) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(J.values[j] + (long long)n * (K / 2) + (long long)kb * 16));
+      o[0] = dequant8_q4(w.x, d2);
+      o[1] = dequant8_q4(w.y, d2);
+      o[2] = dequant8_q4(w.z, d2);
+      o[3] = dequant8_q4(w.w, d2);
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(J.values[j] + (long long)n * K + (long long)kb * 32);
+      const uint4 a = __ldg(src), c = __ldg(src + 1);
+      o[0] = dequant8_q8(make_uint2(a.x, a.y), d2);
+      o[1] = dequant8_q8(make_uint2(a.z, a.w), d2);
+      o[2] = dequant8_q8(make_uint2(c.x, c.y), d2);
+      o[3] = dequant8_q8(make_uint2(c.z, c.w), d2);
+    }
+  }
+}
+
 // All loops over the 16 values below are fully unrolled with compile-time
 // indices (tails are predicated), so v[] stays in registers.
 __device__ __forceinline__ void store16(void* base, long long idx, int is_f32, const float (&v)[16], int n_valid,
@@ -1205,6 +1245,30 @@ int dequant_planes_f16(const QWeight& w, int N, int K, __half* out, long long ld
   else if (w.type == QT_Q8_0) dequant_planes_kernel<2><<<grid, 256, 0, st>>>(v, sc, N, K, out, ldo);
   else return -2;
   return launch_status("dequant_planes");
+}
+
+int dequant_planes_multi(const StageJob* jobs, int n, cudaStream_t st) {
+  if (n <= 0 || n > kMaxStageJobs) return -2;
+  StageJobs J;
+  J.n = n;
+  J.start[0] = 0;
+  for (int j = 0; j < n; ++j) {
+    const StageJob& a = jobs[j];
+    if (a.N <= 0 || a.K <= 0 || a.K % 32 || !a.w.values || !a.w.scales || !a.out) return -2;
+    if (a.w.type != QT_Q4_0 && a.w.type != QT_Q8_0) return -2;
+    if ((reinterpret_cast<uintptr_t>(a.w.values) & 15) || (reinterpret_cast<uintptr_t>(a.out) & 15)) return -11;
+    J.values[j] = reinterpret_cast<const uint8_t*>(a.w.values);
+    J.scales[j] = reinterpret_cast<const uint16_t*>(a.w.scales);
+    J.out[j] = a.out;
+    J.N[j] = a.N;
+    J.K[j] = a.K;
+    J.q4[j] = a.w.type == QT_Q4_0;
+    J.start[j + 1] = J.start[j] + (long long)a.N * (a.K / 32);
+  }
+  const long long cap = (long long)num_sms() * 8;
+  const long long want = (J.start[n] + 255) / 256;
+  dequant_planes_multi_kernel<<<(unsigned)(want < cap ? want : cap), 256, 0, st>>>(J);
+  return launch_status("dequant_planes_multi");
 }
 
 int gemm_q(const __half* A, long long lda, const QWeight& w, int M, int N, int K, const EpiParams& ep, int* err,

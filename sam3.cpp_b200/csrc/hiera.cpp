@@ -72,8 +72,16 @@ BlockGeom geom(const HieraBlock& B, int S) {
 
 }  // namespace
 
-static int hiera_block(s3b_ctx* ctx, const HieraBlock& B, int F, int S, float* x, float* xalt, float** x_out,
+static int hiera_block(s3b_ctx* ctx, const HieraBlock& B0, int F, int S, float* x, float* xalt, float** x_out,
                        __half* xn, __half* xw, __half* qkv, __half* qp, __half* ao, __half* hbuf, float* tmp) {
+  // block-form weights of the block staged in f16 in one launch (weights_quantised = 1)
+  HieraBlock B = B0;
+  {
+    const Linear* in[5] = {&B0.qkv, &B0.proj, &B0.fc1, &B0.fc2, &B0.dim_proj};
+    Linear* outl[5] = {&B.qkv, &B.proj, &B.fc1, &B.fc2, &B.dim_proj};
+    const int rc = stage_linears(ctx, in, outl, 5);
+    if (rc) return rc;
+  }
   const BlockGeom g = geom(B, S);
   const int din = B.dim_in, dout = B.dim_out, hd = dout / B.heads;
   const long long T = (long long)F * S * S, T2 = (long long)F * g.S2 * g.S2;

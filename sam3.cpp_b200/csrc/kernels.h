@@ -223,6 +223,19 @@ int gemm_q(const __half* A, long long lda, const QWeight& w, int M, int N, int K
 // Block-form planes of a q4_0 / q8_0 weight -> f16 rows out [N][ldo] (K a multiple of 32, ldo a
 // multiple of 8, out 16-byte aligned), values round_f16(q * d) as the load-time dequantisation.
 int dequant_planes_f16(const QWeight& w, int N, int K, __half* out, long long ldo, cudaStream_t st);
+// Up to kMaxStageJobs such weights (out [N][K] each) in one launch.
+constexpr int kMaxStageJobs = 8;
+struct StageJob {
+  QWeight w;
+  int N = 0, K = 0;
+  __half* out = nullptr;
+};
+int dequant_planes_multi(const StageJob* jobs, int n, cudaStream_t st);
+
+// Self-test of the bounded device waits: one CTA waits on an mbarrier (limit_ns <= 2 s) whose only arrive
+// is withheld (withhold = 1) or made (0); a wait that runs out records its code in *err and the kernel
+// returns.
+int wait_probe(int* err, long long limit_ns, int withhold, cudaStream_t st);
 
 // Returns the number of SMs of the current device (cached per device).
 int num_sms();

@@ -84,7 +84,12 @@ static int mem_attn_layers(s3b_ctx* ctx, const MemAttnBufs& b) {
   const float scale = 1.0f / sqrtf((float)D);
   RowMap id;
   for (size_t l = 0; l < M.mem.size(); ++l) {
-    const MemAttnLayer& L = M.mem[l];
+    // block-form weights of the layer staged in f16 in one launch (weights_quantised = 1)
+    const MemAttnLayer& L0 = M.mem[l];
+    MemAttnLayer L = L0;
+    const Linear* in[8] = {&L0.sa_qkv, &L0.sa_out, &L0.ca_q, &L0.ca_k, &L0.ca_v, &L0.ca_out, &L0.fc1, &L0.fc2};
+    Linear* outl[8] = {&L.sa_qkv, &L.sa_out, &L.ca_q, &L.ca_k, &L.ca_v, &L.ca_out, &L.fc1, &L.fc2};
+    CKR(stage_linears(ctx, in, outl, 8));
     // self-attention with RoPE on q and k (sam3.cpp:9247-9271)
     CKL(run_ln(ctx, X, D, XN, 0, D, N, D, L.n1w.ptr(), L.n1b.ptr(), 1e-5f, id));
     EpiParams e = epi_store(L.sa_qkv, (void*)b.qkv, 0, 3LL * D);

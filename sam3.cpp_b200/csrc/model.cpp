@@ -133,29 +133,21 @@ static bool rd32(std::ifstream& f, int32_t& v) {
   return !f.fail();
 }
 
-int read_ggml_file(const std::string& path, HParams& hp, std::vector<FileTensor>& tensors, std::string& err) {
-  std::ifstream f(path, std::ios::binary);
-  if (!f) {
-    err = "cannot open " + path;
-    return kErrIO;
-  }
-  uint32_t magic = 0;
-  f.read(reinterpret_cast<char*>(&magic), 4);
-  int32_t version = 0, ftype = 0, n_tensors = 0;
-  rd32(f, version);
-  rd32(f, ftype);
-  rd32(f, n_tensors);
-  if (f.fail() || (magic != kMagicSam3 && magic != kMagicSam2)) {
-    err = "bad magic in " + path;
-    return kErrFormat;
-  }
-  hp.ftype = ftype;
-  int32_t v;
+// Reads the hparam block that follows magic / version / ftype / n_tensors, in file order, through
+// next(v) (false when the source is exhausted): sam3_load_hparams (sam3.cpp:1477-1520) for SAM 3,
+// sam2_load_hparams (1564-1626) for SAM 2.
+template <typename Next>
+static int parse_hparams(bool sam2, Next next, HParams& hp, std::string& err) {
+  bool ok = true;
+  int32_t v = 0;
   auto rd = [&](int& dst) {
-    rd32(f, v);
+    if (!next(v)) {
+      ok = false;
+      v = 0;
+    }
     dst = v;
   };
-  if (magic == kMagicSam3) {
+  if (!sam2) {
     // sam3_load_hparams (sam3.cpp:1477-1520)
     hp.is_sam2 = 0;
     int dummy;
@@ -169,7 +161,15 @@ int read_ggml_file(const std::string& path, HParams& hp, std::vector<FileTensor>
     hp.vit_mlp_dim = (int)(hp.vit_embed_dim * (mlp_ratio_x1000 / 1000.0f));
     rd(hp.vit_window_size);
     rd(hp.n_global_attn);
-    for (int i = 0; i < hp.n_global_attn && i < 4; ++i) rd(hp.global_attn_idx[i]);
+    if (hp.n_global_attn < 0 || hp.n_global_attn > 64) {
+      err = "corrupt global-attention count";
+      return kErrFormat;
+    }
+    for (int i = 0; i < hp.n_global_attn; ++i) {
+      int g;
+      rd(g);
+      if (i < 4) hp.global_attn_idx[i] = g;
+    }
     for (int i = 0; i < 6; ++i) rd(dummy);  // text_width..text_out_dim
     rd(hp.neck_dim);
     for (int i = 0; i < 10; ++i) rd(dummy);  // fenc (3), ddec (4), geom, presence, geom queries
@@ -206,10 +206,38 @@ int read_ggml_file(const std::string& path, HParams& hp, std::vector<FileTensor>
     rd(hp.num_maskmem);
     rd(hp.max_obj_ptrs);
     for (int i = 0; i < 2 + 15; ++i) rd(dummy);  // sigmoid scale/bias + tracking flags
-    if (hp.backbone_type != 1) {
+    if (ok && hp.backbone_type != 1) {
       err = "only the Hiera backbone (backbone_type 1) is supported by the encoder engine";
       return kErrUnsupported;
     }
+  }
+  if (!ok) {
+    err = "truncated header";
+    return kErrFormat;
+  }
+  return kOk;
+}
+
+int read_ggml_file(const std::string& path, HParams& hp, std::vector<FileTensor>& tensors, std::string& err) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) {
+    err = "cannot open " + path;
+    return kErrIO;
+  }
+  uint32_t magic = 0;
+  f.read(reinterpret_cast<char*>(&magic), 4);
+  int32_t version = 0, ftype = 0, n_tensors = 0;
+  rd32(f, version);
+  rd32(f, ftype);
+  rd32(f, n_tensors);
+  if (f.fail() || (magic != kMagicSam3 && magic != kMagicSam2)) {
+    err = "bad magic in " + path;
+    return kErrFormat;
+  }
+  hp.ftype = ftype;
+  {
+    const int rc = parse_hparams(magic == kMagicSam2, [&](int32_t& v) { return rd32(f, v); }, hp, err);
+    if (rc) return rc;
   }
   if (f.fail()) {
     err = "truncated header";
@@ -834,12 +862,32 @@ static int load_sam2(s3b_ctx* ctx, const Index& idx) {
   return load_mem_attn(ctx, idx);
 }
 
+int parse_hparams_array(int is_sam2, const int32_t* v, int n, HParams& hp, std::string& err) {
+  int i = 0;
+  const int rc = parse_hparams(is_sam2 != 0, [&](int32_t& x) {
+    if (i >= n) return false;
+    x = v[i++];
+    return true;
+  }, hp, err);
+  if (rc) return rc;
+  if (i != n) {
+    err = "hparams: " + std::to_string(n) + " values given, the header has " + std::to_string(i);
+    return kErrFormat;
+  }
+  return kOk;
+}
+
 int load_model(s3b_ctx* ctx, const std::string& path) {
   HParams hp;
   std::vector<FileTensor> tensors;
   std::string err;
   int rc = read_ggml_file(path, hp, tensors, err);
   if (rc) return set_error(ctx, rc, "%s", err.c_str());
+  return load_model_tensors(ctx, hp, tensors);
+}
+
+int load_model_tensors(s3b_ctx* ctx, const HParams& hp, const std::vector<FileTensor>& tensors) {
+  int rc = 0;
   ctx->model = Model();
   ctx->model.hp = hp;
   Index idx;
@@ -847,9 +895,12 @@ int load_model(s3b_ctx* ctx, const std::string& path) {
   cudaSetDevice(ctx->device);
   rc = hp.is_sam2 ? load_sam2(ctx, idx) : load_sam3(ctx, idx);
   if (rc) return rc;
-  if (ctx->model.qstage_elems > 0) {
-    // the staging buffer is sized once here, so it never moves under a captured graph
-    ctx->buf("wq_stage", ctx->model.qstage_elems * 2, &rc);
+  if (const size_t elems = stage_arena_elems(ctx->model)) {
+    // the staging buffers are sized once here, so they never move under a captured graph: the arena
+    // of the staged groups and a buffer for a single weight outside them
+    ctx->buf("wq_stage", elems * 2, &rc);
+    if (rc) return rc;
+    ctx->buf("wq_stage1", ctx->model.qstage_elems * 2, &rc);
     if (rc) return rc;
   }
   ctx->model.loaded = true;

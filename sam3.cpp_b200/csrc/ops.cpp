@@ -1,5 +1,7 @@
 // Launch helpers shared by the encoders: launch accounting and optional
 // CUDA-event timing of each GEMM / attention launch on the context stream.
+#include <algorithm>
+
 #include "engine.h"
 
 cudaEvent_t s3b_ctx::next_event() {
@@ -43,7 +45,10 @@ int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long
     cudaEventRecord(a, ctx->stream);
   }
   int rc;
-  if (L.qtype) {
+  if (L.staged) {
+    // block-form weight staged in f16 for this block / layer (stage_linears)
+    rc = gemm_f16(A, lda, L.staged, L.K, (int)M, L.N, L.K, ep, ctx->d_err, ctx->stream);
+  } else if (L.qtype) {
     QWeight qw;
     qw.type = L.qtype;
     qw.values = L.qv->p;
@@ -51,9 +56,9 @@ int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long
     if (ctx->weights_quantised == 2) {
       rc = gemm_q(A, lda, qw, (int)M, L.N, L.K, ep, ctx->d_err, ctx->stream);
     } else {
-      // the weight is read from HBM in block form once and written as f16 into the staging buffer,
-      // which the GEMM then reads from L2 across its tile sweep
-      const auto it = ctx->ws.find("wq_stage");
+      // a block-form weight outside a staged group: read from HBM in block form once and written as
+      // f16 into its own staging buffer, which the GEMM then reads from L2 across its tile sweep
+      const auto it = ctx->ws.find("wq_stage1");
       if (it == ctx->ws.end() || !it->second || it->second->bytes < (size_t)L.N * L.K * 2)
         return set_error(ctx, kErrState, "no staging buffer for block-form weights (model not loaded with it)");
       __half* stage = it->second->as<__half>();
@@ -87,6 +92,70 @@ int run_gemm(s3b_ctx* ctx, const __half* A, long long lda, const Linear& L, long
                                                : 2.0 * L.N * L.K;
     const double bytes = 2.0 * M * L.K + wbytes + (ep.out_f32 ? 4.0 : 2.0) * M * L.N;
     ctx->prof_entries.push_back({0, 2.0 * M * L.N * L.K, bytes, a, b});
+  }
+  return kOk;
+}
+
+size_t stage_arena_elems(const Model& M) {
+  auto q = [](const Linear& L) -> size_t { return L.qtype ? (size_t)L.N * L.K : 0; };
+  size_t best = M.qstage_elems;
+  for (const VitBlock& B : M.vit) best = std::max(best, q(B.qkv) + q(B.proj) + q(B.fc1) + q(B.fc2));
+  for (const HieraBlock& B : M.hiera)
+    best = std::max(best, q(B.qkv) + q(B.proj) + q(B.fc1) + q(B.fc2) + q(B.dim_proj));
+  for (const MemAttnLayer& L : M.mem)
+    best = std::max(best, q(L.sa_qkv) + q(L.sa_out) + q(L.ca_q) + q(L.ca_k) + q(L.ca_v) + q(L.ca_out) + q(L.fc1) +
+                              q(L.fc2));
+  // every region starts on a 256-byte boundary
+  return best ? best + 128 * kMaxStageJobs : 0;
+}
+
+int stage_linears(s3b_ctx* ctx, const Linear* const* in, Linear* const* out, int n) {
+  StageJob jobs[kMaxStageJobs];
+  int nj = 0;
+  size_t off = 0;
+  DevBuf* arena = nullptr;
+  for (int i = 0; i < n; ++i) {
+    *out[i] = *in[i];
+    out[i]->staged = nullptr;
+    const Linear& L = *in[i];
+    if (!L.qtype || ctx->weights_quantised == 2) continue;
+    if (!arena) {
+      const auto it = ctx->ws.find("wq_stage");
+      if (it == ctx->ws.end() || !it->second) return set_error(ctx, kErrState, "no staging arena for block-form weights");
+      arena = it->second.get();
+    }
+    if (nj == kMaxStageJobs) return set_error(ctx, kErrArg, "more than %d weights staged at once", kMaxStageJobs);
+    const size_t elems = (size_t)L.N * L.K;
+    if ((off + elems) * 2 > arena->bytes) return set_error(ctx, kErrState, "staging arena too small");
+    __half* dst = arena->as<__half>() + off;
+    off += (elems + 127) / 128 * 128;
+    jobs[nj].w.type = L.qtype;
+    jobs[nj].w.values = L.qv->p;
+    jobs[nj].w.scales = L.qs->as<__half>();
+    jobs[nj].N = L.N;
+    jobs[nj].K = L.K;
+    jobs[nj].out = dst;
+    ++nj;
+    out[i]->staged = dst;
+  }
+  if (!nj) return kOk;
+  cudaEvent_t a = nullptr, b = nullptr;
+  if (ctx->prof) {
+    a = ctx->next_event();
+    b = ctx->next_event();
+    cudaEventRecord(a, ctx->stream);
+  }
+  const int rc = dequant_planes_multi(jobs, nj, ctx->stream);
+  count_launch(ctx);
+  if (rc) return set_error(ctx, launcher_status_code(rc), "weight staging failed (%d)", rc);
+  if (ctx->prof) {
+    cudaEventRecord(b, ctx->stream);
+    double bytes = 0;
+    for (int j = 0; j < nj; ++j) {
+      const double nk = (double)jobs[j].N * jobs[j].K;
+      bytes += (jobs[j].w.type == QT_Q4_0 ? nk * (0.5 + 1.0 / 16) : nk * (1.0 + 1.0 / 16)) + 2.0 * nk;
+    }
+    ctx->prof_entries.push_back({3, 0.0, bytes, a, b});
   }
   return kOk;
 }

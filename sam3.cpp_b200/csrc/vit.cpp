@@ -195,11 +195,16 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
   DevBuf* ao = ctx->buf("vit_ao", (size_t)Tmax * E * 2, &rc);
   DevBuf* hb = ctx->buf("vit_h", (size_t)Tmax * hp.vit_mlp_dim * 2, &rc);
   if (rc) return rc;
-  for (int f0 = 0; f0 < n_frames; f0 += FB) {
-    const int F = (n_frames - f0) < FB ? (n_frames - f0) : FB;
+  // Passes of at most FB frames. The blocks run layer-major: block b on every pass, then block b + 1,
+  // so each block's block-form weights are staged once per call and stay hot in L2 across the passes.
+  const int n_pass = (n_frames + FB - 1) / FB;
+  const bool bound_backbone = ctx->host_bind.count("vit_output") || ctx->host_bind.count("backbone");
+  auto pass_frames = [&](int p) { return (n_frames - p * FB) < FB ? (n_frames - p * FB) : FB; };
+  auto pass_x = [&](int p) { return O.backbone->as<float>() + (size_t)p * FB * tok_per_frame * E; };
+  for (int p = 0; p < n_pass; ++p) {
+    const int f0 = p * FB, F = pass_frames(p);
     const long long T = (long long)F * tok_per_frame;
-    if ((rc = outputs_pass_begin(ctx, f0 / FB, FB))) return rc;
-    float* x = O.backbone->as<float>() + (size_t)f0 * tok_per_frame * E;
+    if (bound_backbone && (rc = outputs_pass_begin(ctx, p, FB))) return rc;
     // patch embed (conv 14x14/s14, no bias) + tiled abs pos (sam3.cpp:3815-3822)
     CK(im2col_image(d_chw + (size_t)f0 * 3 * S * S, F, 3, S, S, P, P, 0, G, G, col->as<__half>(), Kp, ctx->stream));
     EpiParams pe = epi_store(M.patch, xp->p, 1, E);
@@ -210,20 +215,31 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
     CKG(gemm(ctx, col->as<__half>(), Kp, M.patch, T, pe));
     // ln_pre (sam3.cpp:3825-3827)
     RowMap id;
-    CK(run_ln(ctx, xp->as<float>(), E, x, 1, E, T, E, M.ln_pre_w.ptr(), M.ln_pre_b.ptr(), 1e-5f, id));
-    // stage runner (test hook, like sam3_test_run_vit_block_stage): stop after `stop_after_blocks`
-    const int n_blocks = ctx->stop_after_blocks >= 0 && ctx->stop_after_blocks < hp.vit_depth
-                             ? ctx->stop_after_blocks
-                             : hp.vit_depth;
-    for (int b = 0; b < n_blocks; ++b) {
-      if ((rc = vit_block(ctx, M.vit[b], F, x, xn->as<__half>(), qkv->as<__half>(), ao->as<__half>(),
+    CK(run_ln(ctx, xp->as<float>(), E, pass_x(p), 1, E, T, E, M.ln_pre_w.ptr(), M.ln_pre_b.ptr(), 1e-5f, id));
+  }
+  // stage runner (test hook, like sam3_test_run_vit_block_stage): stop after `stop_after_blocks`
+  const int n_blocks = ctx->stop_after_blocks >= 0 && ctx->stop_after_blocks < hp.vit_depth
+                           ? ctx->stop_after_blocks
+                           : hp.vit_depth;
+  for (int b = 0; b < n_blocks; ++b) {
+    VitBlock Bs = M.vit[b];
+    const Linear* in[4] = {&M.vit[b].qkv, &M.vit[b].proj, &M.vit[b].fc1, &M.vit[b].fc2};
+    Linear* outl[4] = {&Bs.qkv, &Bs.proj, &Bs.fc1, &Bs.fc2};
+    if ((rc = stage_linears(ctx, in, outl, 4))) return rc;
+    for (int p = 0; p < n_pass; ++p) {
+      if ((rc = vit_block(ctx, Bs, pass_frames(p), pass_x(p), xn->as<__half>(), qkv->as<__half>(), ao->as<__half>(),
                           hb->as<__half>())))
         return rc;
     }
+  }
+  for (int p = 0; p < n_pass; ++p) {
+    const int f0 = p * FB, F = pass_frames(p);
+    const long long T = (long long)F * tok_per_frame;
+    if (!bound_backbone && (rc = outputs_pass_begin(ctx, p, FB))) return rc;
     if (want_neck) {
       // neck input in f16 (ggml converts the conv input to the f16 kernel type)
       __half* xh = xn->as<__half>();
-      CK(cast_f32_f16(x, T * E, xh, ctx->stream));
+      CK(cast_f32_f16(pass_x(p), T * E, xh, ctx->stream));
       float* outs[4];
       for (int i = 0; i < 4; ++i) outs[i] = O.fpn[i]->as<float>() + (size_t)f0 * sizes[i] * sizes[i] * hp.neck_dim;
       if ((rc = vit_neck(ctx, M.neck_trk, xh, F, outs))) return rc;
@@ -232,7 +248,7 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
         if ((rc = vit_neck(ctx, M.neck_det, xh, F, outs))) return rc;
       }
     }
-    if ((rc = outputs_pass_end(ctx, f0 / FB, f0, F))) return rc;
+    if ((rc = outputs_pass_end(ctx, p, f0, F))) return rc;
   }
   return check_device(ctx, "vit_encode");
 }

@@ -15,6 +15,9 @@ Run in a container that has the reference checkout (read-only) and torch:
 2. mem_attn_golden.npz — run_memory_attention() imported from the
    reference's tests/dump_phase7_reference.py on seeded synthetic tracker
    weights, current features, memory prompt and prompt PE.
+3. window_golden.npz — window_partition / window_unpartition imported from
+   the reference's tests/dump_vit_reference.py on seeded padded inputs (the
+   Hiera window path: 64 -> 70 at ws 14, q-pooled unpartition at ws // 2).
 
 Each dumped tensor is stored as deterministic samples (indices + values)
 plus summary statistics, so the fixtures stay small; tests regenerate the
@@ -176,15 +179,56 @@ def make_mem_attn(reference: str, out_path: str):
     print("wrote", out_path)
 
 
+WINDOW_SEED = 31
+# (input shape [B, H, W, C], window size): padded grids of the Hiera stages (64 -> 70 at ws 14, the
+# q-pooled 32 -> 35 at ws 7), an exact fit and a non-square padded one
+WINDOW_CASES = [((1, 64, 64, 3), 14), ((2, 32, 32, 2), 7), ((1, 32, 32, 2), 8), ((1, 20, 30, 3), 8)]
+
+
+def make_window(reference: str, out_path: str):
+    """window_partition / window_unpartition of the reference's tests/dump_vit_reference.py (imported, not
+    modified) on seeded padded inputs, plus the Hiera q-stride path: partition at ws, 2x2 max pool of every
+    window (torch max_pool2d, as sam2's do_pool), unpartition at ws // 2 onto the halved, padded grid."""
+    import torch
+    spec = importlib.util.spec_from_file_location("dump_vit_reference",
+                                                  os.path.join(reference, "tests", "dump_vit_reference.py"))
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    rng = np.random.default_rng(WINDOW_SEED)
+    out = {}
+    for c, (shape, ws) in enumerate(WINDOW_CASES):
+        x = rng.standard_normal(shape).astype(np.float32)
+        win, pad_hw = ref.window_partition(torch.from_numpy(x), ws)
+        back = ref.window_unpartition(win, ws, pad_hw, shape[1:3])
+        B, H, W, C = shape
+        # the inputs are regenerated by the tests from the seed (standard normals in case order)
+        assert np.array_equal(back.numpy(), x)  # the reference's own round trip
+        out[f"case{c}_windows"] = win.numpy()
+        out[f"case{c}_pad_hw"] = np.array(pad_hw, np.int64)
+        if ws % 2 == 0:  # q-stride blocks have even windows (Hiera pools 8 -> 4 and 14 -> 7)
+            pooled = torch.nn.functional.max_pool2d(win.permute(0, 3, 1, 2), 2, 2).permute(0, 2, 3, 1)
+            ws2 = ws // 2
+            th, tw = H // 2, W // 2
+            pad2 = (th + (ws2 - th % ws2) % ws2, tw + (ws2 - tw % ws2) % ws2)
+            out[f"case{c}_qpool_unpartition"] = ref.window_unpartition(pooled, ws2, pad2, (th, tw)).numpy()
+    meta = {"seed": WINDOW_SEED, "cases": WINDOW_CASES,
+            "generator": "window_partition / window_unpartition of the reference's tests/dump_vit_reference.py "
+                         "(lines 64-86), torch max_pool2d for the q pooling"}
+    np.savez_compressed(out_path, meta=json.dumps(meta), **out)
+    print("wrote", out_path)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the sam3.cpp checkout (read-only)")
-    ap.add_argument("--only", choices=["vit", "mem_attn"], default=None)
+    ap.add_argument("--only", choices=["vit", "mem_attn", "window"], default=None)
     a = ap.parse_args()
     if a.only in (None, "vit"):
         make_vit(a.reference, os.path.join(HERE, "vit_golden.npz"))
     if a.only in (None, "mem_attn"):
         make_mem_attn(a.reference, os.path.join(HERE, "mem_attn_golden.npz"))
+    if a.only in (None, "window"):
+        make_window(a.reference, os.path.join(HERE, "window_golden.npz"))
 
 
 if __name__ == "__main__":

@@ -24,6 +24,32 @@ def test_oracle_bicubic_matches_torch():
         np.testing.assert_allclose(oh.bicubic(src, H, W), ref, rtol=1e-5, atol=1e-5)
 
 
+def test_oracle_window_path_matches_reference():
+    """The oracle's padded window partition / unpartition and the Hiera q-stride path (partition at ws, 2x2 max
+    pool per window, unpartition at ws // 2 onto the halved padded grid, crop) against the reference's own
+    window_partition / window_unpartition (tests/dump_vit_reference.py:64-86; fixture by
+    tests/golden/make_golden.py). Pure data movement and max: bit-exact."""
+    import json
+    import os
+    from oracle import nn
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "window_golden.npz"))
+    meta = json.loads(str(g["meta"]))
+    rng = np.random.default_rng(meta["seed"])
+    for c, (shape, ws) in enumerate(meta["cases"]):
+        x = rng.standard_normal(tuple(shape)).astype(np.float32)
+        win, pad_hw = nn.window_partition(x, ws)
+        assert tuple(pad_hw) == tuple(g[f"case{c}_pad_hw"]), c
+        assert np.array_equal(win, g[f"case{c}_windows"]), c
+        assert np.array_equal(nn.window_unpartition(win, ws, pad_hw, tuple(shape[1:3])), x), c
+        key = f"case{c}_qpool_unpartition"
+        if key in g:
+            B, H, W, C = shape
+            ws2, th, tw = ws // 2, H // 2, W // 2
+            pad2 = (th + (ws2 - th % ws2) % ws2, tw + (ws2 - tw % ws2) % ws2)
+            got = nn.window_unpartition(nn.maxpool2(win), ws2, pad2, (th, tw))
+            assert np.array_equal(got, g[key]), c
+
+
 def test_hiera_block_metadata(s3b):
     """Per-block dims / heads / windows / q-stride of Hiera-T (sam3.cpp:1676-1742)."""
     from sam3_b200 import synth

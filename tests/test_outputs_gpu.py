@@ -48,7 +48,7 @@ def test_neck_pe_outputs_bit_exact(engine, s3b, tmp_path):
 
 class _CudaArray:
     def __init__(self, ptr, n):
-        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, True), "version": 3}
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
 
 
 @pytest.mark.parametrize("n_frames,per_pass", [(5, 2), (3, 8)])
