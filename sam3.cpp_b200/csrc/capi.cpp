@@ -39,7 +39,9 @@ int read_dev_err(s3b_ctx* ctx) {
   if (cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
     return set_error(ctx, kErrCuda, "reading the device error word: %s", cudaGetErrorString(cudaGetLastError()));
   if (h != 0) {
-    cudaMemset(ctx->d_err, 0, sizeof(int));
+    // cleared in the context stream's order, so no later kernel's code can be wiped by it
+    cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream);
+    cudaStreamSynchronize(ctx->stream);
     return set_error(ctx, kErrDevice, "device-side wait timed out (code %d)", h);
   }
   return kOk;
@@ -92,10 +94,7 @@ const float* device_sine_pe(s3b_ctx* ctx, int S, int d, int* rc) {
   sine_pe_2d(S, S, d, pe.data());
   DevBuf* b = ctx->buf(key, pe.size() * 4, rc);
   if (*rc) return nullptr;
-  if (cudaMemcpy(b->p, pe.data(), pe.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
-    *rc = set_error(ctx, kErrCuda, "sine PE upload failed");
-    return nullptr;
-  }
+  if ((*rc = upload_sync(ctx, b->p, pe.data(), pe.size() * 4))) return nullptr;
   return b->as<float>();
 }
 

@@ -280,6 +280,10 @@ namespace s3b {
 // from the driver) and below -11 are CUDA failures.
 inline int launcher_status_code(int rc) { return (rc == -10 || rc < -11) ? kErrCuda : kErrArg; }
 int set_error(s3b_ctx* ctx, int code, const char* fmt, ...);
+// Host -> device copy ordered on the context stream and complete on return. A plain cudaMemcpy from
+// pageable memory may return before its DMA has landed, and kernels on the context's non-blocking
+// stream do not wait for it, so every upload a kernel reads goes through this.
+int upload_sync(s3b_ctx* ctx, void* dst, const void* src, size_t bytes);
 int check_device(s3b_ctx* ctx, const char* where);
 
 // weight preparation (model.cpp)

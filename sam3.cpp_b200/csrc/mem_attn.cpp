@@ -56,10 +56,7 @@ static const float* rope_table(s3b_ctx* ctx, int feat, int D, int* rc) {
   rope_position_major(t0, feat * feat, D / 2, t);
   DevBuf* b = ctx->buf(key, t.size() * 4, rc);
   if (*rc) return nullptr;
-  if (cudaMemcpy(b->p, t.data(), t.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
-    *rc = set_error(ctx, kErrCuda, "RoPE table upload failed");
-    return nullptr;
-  }
+  if ((*rc = upload_sync(ctx, b->p, t.data(), t.size() * 4))) return nullptr;
   return b->as<float>();
 }
 

@@ -303,10 +303,7 @@ static std::shared_ptr<DevBuf> upload_bytes(s3b_ctx* ctx, const void* src, size_
     *rc = set_error(ctx, kErrOOM, "cudaMalloc(%zu) failed", bytes);
     return nullptr;
   }
-  if (cudaMemcpy(b->p, src, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
-    *rc = set_error(ctx, kErrCuda, "upload of %zu bytes failed", bytes);
-    return nullptr;
-  }
+  if ((*rc = upload_sync(ctx, b->p, src, bytes))) return nullptr;
   ctx->model.device_bytes += bytes;
   return b;
 }

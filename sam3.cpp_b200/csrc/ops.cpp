@@ -26,6 +26,13 @@ void rope_position_major(const std::vector<float>& in, int npos, int half_d, std
 
 void count_launch(s3b_ctx* ctx, int n) { ctx->n_launches += n; }
 
+int upload_sync(s3b_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  if (cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess ||
+      cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "upload of %zu bytes failed: %s", bytes, cudaGetErrorString(cudaGetLastError()));
+  return kOk;
+}
+
 EpiParams epi_store(const Linear& L, void* out, int out_f32, long long ldo, int act) {
   EpiParams ep;
   ep.mode = EPI_STORE;
