@@ -27,6 +27,8 @@
 //              sum and stored (32 columns per thread).
 // Every wait is bounded; a timeout records an error code and the CTA unwinds
 // without skipping any named barrier.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -109,6 +111,11 @@ __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sy
                "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),                     \
                "r"(R[0]), "r"(R[1]), "r"(R[2]), "r"(R[3]), "r"(R[4]), "r"(R[5]), "r"(R[6]), "r"(R[7]),       \
                "r"(R[8]), "r"(R[9]), "r"(R[10]), "r"(R[11]), "r"(R[12]), "r"(R[13]), "r"(R[14]), "r"(R[15])  \
+               : "memory")
+
+#define TMEM_ST8(taddr, R)                                                                                   \
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(R[0]), \
+               "r"(R[1]), "r"(R[2]), "r"(R[3]), "r"(R[4]), "r"(R[5]), "r"(R[6]), "r"(R[7])                    \
                : "memory")
 
 #define TMEM_ST32(taddr, R)                                                                                  \
@@ -541,6 +548,371 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+// ---------------------------------------------------------------- two query tiles per CTA (FA kernel)
+// One persistent CTA per SM walks work units = (window, head, pair of 128-query tiles), with 96-key
+// tiles (576 = 6 x 96 and 5184 = 54 x 96: the ViT windows and the global grid have no ragged tile).
+// 10 warps:
+//   warp 0     TMA: a unit's Q tiles into one of two Q buffers (the next unit's Q loads while the
+//              current one computes), then K_j, V_j (96 rows) through an 8-slot ring, across units.
+//   warp 1+t   MMA issue for tile t (t = 0, 1), one thread each, in order: S_t(n) = Q_t K_j^T
+//              (128 x 96 x 64) into TMEM region n & 1 of the tile, then O_t += P_t(n - 1) V_{j-1} with P
+//              read from the region S_t(n - 1) was written to. The two issuers wait (bounded, suspended)
+//              only on their own tile's barriers, so a tile whose softmax lags never holds up the other.
+//              Every K / V ring entry and Q buffer is released by both issuers (barrier count 2).
+//   warps 4-7  softmax of tile 0, warps 8-11 of tile 1 (warp 3 idle): one query row per thread (TMEM lane), the 96
+//              scores of the row in registers; row max, lazy reference max (moved only when the row max
+//              grows by more than 2^8, then the sum and the O row are rescaled), p = 2^(s * scale *
+//              log2 e - m) written as f16 pairs over the scores it came from (the region's first 48
+//              columns), and at the end of the unit O / sum stored through the output row map.
+// TMEM (512 columns): tile t region r at 192 t + 96 r, O_t at 384 + 64 t. A region is rewritten by the
+// next-but-one S of its tile only after the P V product that read it: the MMAs of the issuing thread
+// execute in order, and S_t(n + 2) is issued after P V(n).
+// No named barriers: the roles meet only on mbarriers, every wait is bounded, and a timeout unwinds
+// every role to the final __syncthreads.
+constexpr int kFaWarps = 12;
+constexpr int kFaThreads = 32 * kFaWarps;
+constexpr int kFaBK = 96;
+constexpr int kFaSlots = 8;
+constexpr uint32_t kFaKVBytes = kFaBK * kD * 2;  // 12 KB
+constexpr uint32_t kFaTmemCols = 512;
+
+struct FaArgs {
+  int heads, ntok, nwin;
+  int q_col, k_col, v_col;
+  __half* o;
+  long long o_n;
+  RowMap omap;
+  float sl2;
+  int n_qp;     // query-tile pairs per (window, head)
+  int n_units;  // nwin * heads * n_qp
+};
+
+template <int NPOLY>
+__global__ void __launch_bounds__(kFaThreads, 1)
+    attn_fa_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv, FaArgs a,
+                   int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sQ = smem;                        // [2 buffers][2 tiles] x 16 KB
+  uint8_t* sKV = sQ + 4 * kTileBytes;        // kFaSlots x 12 KB (1024-byte multiples)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kFaSlots * kFaKVBytes);
+  uint64_t* q_full = bars;                   // [2]
+  uint64_t* q_empty = q_full + 2;            // [2]
+  uint64_t* kv_full = q_empty + 2;           // [kFaSlots]
+  uint64_t* kv_empty = kv_full + kFaSlots;   // [kFaSlots]
+  uint64_t* s_full = kv_empty + kFaSlots;    // [2 tiles][2 regions]: one barrier per region, so the two
+                                             // S products in flight for a tile never share a phase count
+  uint64_t* p_full = s_full + 4;             // [2 tiles]
+  uint64_t* pv_done = p_full + 2;            // [2 tiles]
+  uint64_t* mma_done = pv_done + 2;          // [2 tiles]
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mma_done + 2);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = (a.ntok + kFaBK - 1) / kFaBK;
+  const int stride = gridDim.x;
+  const int n_it = a.n_units > (int)blockIdx.x ? (a.n_units - 1 - (int)blockIdx.x) / stride + 1 : 0;
+  // tile 1 of a unit exists when the unit's second query tile holds a real query
+  auto has_tile1 = [&](int it) -> bool {
+    const int u = (int)blockIdx.x + it * stride;
+    return (2 * (u % a.n_qp) + 1) * kBQ < a.ntok;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&q_full[b], 1);
+      mbar_init(&q_empty[b], 2);  // released by both issuers
+      mbar_init(&s_full[2 * b], 1);
+      mbar_init(&s_full[2 * b + 1], 1);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&pv_done[b], 1);
+      mbar_init(&mma_done[b], 1);
+    }
+    for (int s = 0; s < kFaSlots; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 2);  // released by both issuers
+    }
+    *s_abort = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tkv);
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, kFaTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t armed = 0, armed_phase = 0, q_armed = 0, q_phase = 0;
+      long long g = 0;  // ring loads so far
+      bool ok = true;
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int u = (int)blockIdx.x + it * stride;
+        const int bh = u / a.n_qp, qp = u - bh * a.n_qp;
+        const int w = bh / a.heads, h = bh - w * a.heads;
+        const bool two = has_tile1(it);
+        const int qb = it & 1;
+        if (!mbar_wait(&q_empty[qb], ((uint32_t)(it >> 1) & 1) ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
+        mbar_arrive_expect_tx(&q_full[qb], (two ? 2 : 1) * kTileBytes);
+        tma_load_3d(&tq, &q_full[qb], sQ + (2 * qb) * kTileBytes, a.q_col + h * kD, 2 * qp * kBQ, w);
+        if (two) tma_load_3d(&tq, &q_full[qb], sQ + (2 * qb + 1) * kTileBytes, a.q_col + h * kD, (2 * qp + 1) * kBQ, w);
+        q_armed |= 1u << qb;
+        q_phase = (q_phase & ~(1u << qb)) | ((uint32_t)((it >> 1) & 1) << qb);
+        for (int t = 0; t < 2 * nkb; ++t, ++g) {  // K_0, V_0, K_1, V_1, ...
+          const int s = (int)(g % kFaSlots);
+          const uint32_t use = (uint32_t)(g / kFaSlots);
+          if (!mbar_wait(&kv_empty[s], (use & 1) ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[s], kFaKVBytes);
+          const int col = ((t & 1) ? a.v_col : a.k_col) + h * kD;
+          tma_load_3d(&tkv, &kv_full[s], sKV + s * kFaKVBytes, col, (t >> 1) * kFaBK, w);
+          armed |= 1u << s;
+          armed_phase = (armed_phase & ~(1u << s)) | ((use & 1) << s);
+        }
+      }
+      // no copy may still be landing when the CTA exits
+      for (int b = 0; b < 2; ++b)
+        if (q_armed & (1u << b)) mbar_wait_drain(&q_full[b], (q_phase >> b) & 1u, err);
+      for (int s = 0; s < kFaSlots; ++s)
+        if (armed & (1u << s)) mbar_wait_drain(&kv_full[s], (armed_phase >> s) & 1u, err);
+    }
+  } else if (warp == 1 || warp == 2) {
+    if (lane == 0) {
+      const int t = warp - 1;
+      constexpr uint32_t idesc_s = idesc_f16(kBQ, kFaBK, 0);            // Q, K both K-major
+      constexpr uint32_t idesc_o = idesc_f16(kBQ, kD, 0) | (1u << 16);  // B (V) MN-major
+      const uint32_t q_base = smem_u32(sQ), kv_base = smem_u32(sKV);
+      uint32_t ns = 0, npv = 0;
+      bool ok = true, issued = false;
+      // ring entry of K_j (v = 0) or V_j (v = 1) of unit iteration it
+      auto slot = [&](int it, int j, int v, uint32_t* par) -> int {
+        const long long g = 2LL * nkb * it + 2 * j + v;
+        *par = (uint32_t)(g / kFaSlots) & 1;
+        return (int)(g % kFaSlots);
+      };
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int qb = it & 1;
+        uint32_t par;
+        if (t == 1 && !has_tile1(it)) {
+          // no second query tile in this unit: release its Q buffer and ring entries as they fill, so
+          // the counts of both issuers stay in step
+          if (!mbar_wait(&q_full[qb], (uint32_t)(it >> 1) & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
+          mbar_arrive(&q_empty[qb]);
+          for (int e = 0; e < 2 * nkb && ok; ++e) {
+            const int sl = slot(it, e >> 1, e & 1, &par);
+            if (!mbar_wait(&kv_full[sl], par, s_abort, err, kErrWaitFull)) { ok = false; break; }
+            mbar_arrive(&kv_empty[sl]);
+          }
+          continue;
+        }
+        if (!mbar_wait(&q_full[qb], (uint32_t)(it >> 1) & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t dq = sdesc_k_sw128(q_base + (uint32_t)((2 * qb + t) * kTileBytes));
+        // S(n) = Q K_j^T into region n & 1 (its last reader, P V(n - 2), was issued before by this thread)
+        auto issue_s = [&](int j) -> bool {
+          uint32_t pk;
+          const int sk = slot(it, j, 0, &pk);
+          if (!mbar_wait(&kv_full[sk], pk, s_abort, err, kErrWaitFull)) return false;
+          tc_fence_after();
+          const uint64_t dk = sdesc_k_sw128(kv_base + (uint32_t)(sk * kFaKVBytes));
+          const uint32_t sa = tmem + (uint32_t)(192 * t + 96 * (ns & 1));
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk)
+            tc_mma_f16(sa, dq + (uint64_t)(kk * 2), dk + (uint64_t)(kk * 2), idesc_s, kk != 0);
+          tc_commit(&s_full[2 * t + (ns & 1)]);
+          tc_commit(&kv_empty[sk]);
+          if (j == nkb - 1) tc_commit(&q_empty[qb]);
+          ++ns;
+          issued = true;
+          return true;
+        };
+        // O += P(npv) V_j, P read from the region of S(npv)
+        auto issue_pv = [&](int j) -> bool {
+          uint32_t pv_par;
+          const int sv = slot(it, j, 1, &pv_par);
+          if (!mbar_wait(&p_full[t], npv & 1, s_abort, err, kErrWaitMisc)) return false;
+          if (!mbar_wait(&kv_full[sv], pv_par, s_abort, err, kErrWaitFull)) return false;
+          tc_fence_after();
+          const uint32_t va = kv_base + (uint32_t)(sv * kFaKVBytes);
+          const uint32_t pa = tmem + (uint32_t)(192 * t + 96 * (npv & 1));
+          const int nk16 = min(kFaBK / 16, (a.ntok - j * kFaBK + 15) / 16);  // K steps holding a real key
+#pragma unroll
+          for (int kk = 0; kk < kFaBK / 16; ++kk) {
+            if (kk >= nk16) break;
+            tc_mma_f16_ts(tmem + 384 + 64 * t, pa + (uint32_t)(kk * 8), sdesc_mn_sw128(va + (uint32_t)(kk * 2048)),
+                          idesc_o, (j > 0 || kk != 0) ? 1u : 0u);
+          }
+          tc_commit(&pv_done[t]);
+          tc_commit(&kv_empty[sv]);
+          ++npv;
+          issued = true;
+          return true;
+        };
+        if (!issue_s(0)) { ok = false; break; }
+        for (int j = 0; j < nkb && ok; ++j) {
+          if (j + 1 < nkb && !issue_s(j + 1)) { ok = false; break; }
+          if (!issue_pv(j)) { ok = false; break; }
+        }
+      }
+      if (issued) {
+        tc_commit(&mma_done[t]);
+        mbar_wait_drain(&mma_done[t], 0, err);
+      }
+    }
+  } else if (warp >= 4) {
+    // softmax: warps 4-7 tile 0, warps 8-11 tile 1; TMEM lanes 32*(warp % 4) .. +31
+    const int t = (warp - 4) >> 2;
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t o_addr = tmem + lane_off + 384 + 64 * t;
+    uint32_t n = 0;  // S / P count of this tile (its TMEM region is n & 1)
+    bool ok = true;
+    for (int it = 0; it < n_it && ok; ++it) {
+      if (t == 1 && !has_tile1(it)) continue;
+      const int u = (int)blockIdx.x + it * stride;
+      const int bh = u / a.n_qp, qp = u - bh * a.n_qp;
+      const int w = bh / a.heads, h = bh - w * a.heads;
+      const int qt = 2 * qp + t;
+      float m_ref = -INFINITY, l = 0.f;
+      for (int j = 0; j < nkb; ++j, ++n) {
+        // S(n) of this tile: region n & 1, its barrier's use (n >> 1)
+        if (!mbar_wait(&s_full[2 * t + (n & 1)], (n >> 1) & 1, s_abort, err, kErrWaitTmemFull)) ok = false;
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t r_addr = tmem + lane_off + (uint32_t)(192 * t + 96 * (n & 1));
+        const int kvalid = a.ntok - j * kFaBK;  // keys at or past this count are padding
+        const bool full = kvalid >= kFaBK;
+        uint32_t r[kFaBK];
+        TMEM_LD32(r_addr, r);
+        TMEM_LD32(r_addr + 32, (r + 32));
+        TMEM_LD32(r_addr + 64, (r + 64));
+        tc_wait_ld();
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kFaBK; i += 4) {
+          float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
+          float v2 = __uint_as_float(r[i + 2]), v3 = __uint_as_float(r[i + 3]);
+          if (!full) {
+            v0 = i < kvalid ? v0 : -INFINITY;
+            v1 = i + 1 < kvalid ? v1 : -INFINITY;
+            v2 = i + 2 < kvalid ? v2 : -INFINITY;
+            v3 = i + 3 < kvalid ? v3 : -INFINITY;
+          }
+          mx0 = fmaxf(mx0, v0);
+          mx1 = fmaxf(mx1, v1);
+          mx2 = fmaxf(mx2, v2);
+          mx3 = fmaxf(mx3, v3);
+        }
+        const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.sl2;
+        float alpha = 1.f;
+        bool resc = false;
+        if (m_tile > m_ref + kLazyMax) {  // always at the first key tile
+          alpha = ex2(m_ref - m_tile);
+          resc = j > 0;
+          m_ref = m_tile;
+          l *= alpha;
+        }
+        // p = 2^(s * sl2 - m_ref) (padding keys p = 0) as f16 pairs over the region's first 48 columns (this
+        // thread's scores are in registers; the region's previous reader, P V(n - 2), completed before
+        // S(n) was written), row sum
+        const unsigned long long sl2x2 = f2_pack(a.sl2, a.sl2), negm2 = f2_pack(-m_ref, -m_ref);
+        unsigned long long acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+        for (int c = 0; c < kFaBK / 16; ++c) {  // 16 keys (8 packed columns) per store
+          uint32_t pk[8];
+#pragma unroll
+          for (int u8 = 0; u8 < 2; ++u8) {
+            float pv[8];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              const int i = 16 * c + 8 * u8 + e;
+              float x0, x1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2x2, negm2), x0, x1);
+              pv[e] = e < NPOLY ? exp2_poly3(x0) : ex2(x0);
+              pv[e + 1] = e + 1 < NPOLY ? exp2_poly3(x1) : ex2(x1);
+              if (!full) {
+                pv[e] = i < kvalid ? pv[e] : 0.f;
+                pv[e + 1] = i + 1 < kvalid ? pv[e + 1] : 0.f;
+              }
+            }
+            acc0 = f2_add(acc0, f2_add(f2_pack(pv[0], pv[1]), f2_pack(pv[4], pv[5])));
+            acc1 = f2_add(acc1, f2_add(f2_pack(pv[2], pv[3]), f2_pack(pv[6], pv[7])));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) pk[4 * u8 + e] = pack_h2(pv[2 * e], pv[2 * e + 1]);
+          }
+          TMEM_ST8(r_addr + 8 * c, pk);
+        }
+        float a0, a1, b0, b1;
+        f2_unpack(acc0, a0, a1);
+        f2_unpack(acc1, b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+        // O_t current: the previous P V product of this tile has completed (also keeps this thread's walk
+        // over the pv_done phases in order)
+        if (j > 0 && !mbar_wait(&pv_done[t], (n - 1) & 1, s_abort, err, kErrWaitMisc)) ok = false;
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        // the reference max moved (rare after the first key tile): rescale this row of O_t
+        if (__any_sync(0xffffffffu, resc)) {
+          uint32_t o[32];
+          const float f = resc ? alpha : 1.f;
+#pragma unroll
+          for (int cc = 0; cc < kD; cc += 32) {
+            TMEM_LD32(o_addr + cc, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            TMEM_ST32(o_addr + cc, o);
+          }
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      }
+      if (!ok) break;
+      // the unit's last P V product has completed: O_t / l to the output rows
+      if (!mbar_wait(&pv_done[t], (n - 1) & 1, s_abort, err, kErrWaitMisc)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t o[kD];
+      TMEM_LD32(o_addr, o);
+      TMEM_LD32(o_addr + 32, (o + 32));
+      tc_wait_ld();
+      const int qi = qt * kBQ + row;
+      if (qi < a.ntok) {
+        const long long orow = map_row(a.omap, (long long)w * a.ntok + qi);
+        if (orow >= 0) {
+          const float inv = 1.0f / l;
+          uint4* op = reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * kD);
+#pragma unroll
+          for (int u8 = 0; u8 < 8; ++u8)
+            op[u8] = make_uint4(pack_h2(__uint_as_float(o[8 * u8]) * inv, __uint_as_float(o[8 * u8 + 1]) * inv),
+                                pack_h2(__uint_as_float(o[8 * u8 + 2]) * inv, __uint_as_float(o[8 * u8 + 3]) * inv),
+                                pack_h2(__uint_as_float(o[8 * u8 + 4]) * inv, __uint_as_float(o[8 * u8 + 5]) * inv),
+                                pack_h2(__uint_as_float(o[8 * u8 + 6]) * inv, __uint_as_float(o[8 * u8 + 7]) * inv));
+        }
+      }
+      // these TMEM loads completed (wait::ld) before this thread's next p_full arrive, and the next unit's
+      // first P V product (accumulate = 0) is issued only after that arrive
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kFaTmemCols);
+  }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -591,6 +963,59 @@ int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v
   if (n_cta > 0x7fffffffLL) return -2;
   kfn<<<(unsigned)n_cta, kThreads, smem, st>>>(tm, a, err);
   return launch_status("attention_tc64");
+}
+
+int attention_fa64(const __half* base, long long ld, int q_col, int k_col, int v_col, int heads, int ntok, int nwin,
+                   __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int* err,
+                   cudaStream_t st) {
+  typedef void (*KernelFn)(const CUtensorMap, const CUtensorMap, FaArgs, int*);
+  static const KernelFn kernels[5] = {attn_fa_kernel<0>, attn_fa_kernel<1>, attn_fa_kernel<2>, attn_fa_kernel<3>,
+                                      attn_fa_kernel<4>};
+  if (exp_poly < 0 || exp_poly > 4 || ntok <= 0 || nwin <= 0 || heads <= 0) return -2;
+  EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!enc) return -10;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16 || (q_col % 8) || (k_col % 8) || (v_col % 8) ||
+      (o_n % 8) || (reinterpret_cast<uintptr_t>(o) & 15))
+    return -2;
+  // 3-D maps (channels, token, window) over the fused qkv buffer: 128-row Q boxes, 96-row K / V boxes;
+  // rows past the window's last token read zeros
+  CUtensorMap tq, tkv;
+  cuuint64_t dims[3] = {(cuuint64_t)ld, (cuuint64_t)ntok, (cuuint64_t)nwin};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(ld * 2 * ntok)};
+  cuuint32_t box_q[3] = {(cuuint32_t)kD, (cuuint32_t)kBQ, 1};
+  cuuint32_t box_kv[3] = {(cuuint32_t)kD, (cuuint32_t)kFaBK, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  if (enc(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box_q, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+      enc(&tkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box_kv, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return -12;
+  FaArgs a;
+  a.heads = heads;
+  a.ntok = ntok;
+  a.nwin = nwin;
+  a.q_col = q_col;
+  a.k_col = k_col;
+  a.v_col = v_col;
+  a.o = o;
+  a.o_n = o_n;
+  a.omap = omap;
+  a.sl2 = scale * 1.4426950408889634f;
+  const int n_qt = (ntok + kBQ - 1) / kBQ;
+  a.n_qp = (n_qt + 1) / 2;
+  const long long units = (long long)a.n_qp * nwin * heads;
+  if (units > 0x7fffffffLL) return -2;
+  a.n_units = (int)units;
+  constexpr size_t smem = 1024 + 4 * kTileBytes + kFaSlots * kFaKVBytes + (14 + 2 * kFaSlots) * 8 + 16;
+  static_assert(smem <= 232448, "shared memory per CTA");
+  static_assert(kFaKVBytes % 1024 == 0, "K / V slots keep the 1024-byte alignment of the 128B swizzle");
+  const KernelFn kfn = kernels[exp_poly];
+  if (kernel_setup(kfn, smem) <= 0) return -13;
+  const int grid = (int)std::min<long long>(units, (long long)num_sms());
+  kfn<<<grid, kFaThreads, smem, st>>>(tq, tkv, a, err);
+  return launch_status("attention_fa64");
 }
 
 }  // namespace s3b

@@ -449,7 +449,7 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     return kOk;
   }
   if (k == "attention_impl") {
-    if (value < 0 || value > 3) return set_error(ctx, kErrArg, "attention_impl must be 0, 1, 2 or 3");
+    if (value < 0 || value > 4) return set_error(ctx, kErrArg, "attention_impl must be in [0, 4]");
     ctx->attention_impl = (int)value;
     return kOk;
   }
@@ -471,6 +471,11 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
   if (k == "conv_implicit") {
     if (value < 0 || value > 1) return set_error(ctx, kErrArg, "conv_implicit must be 0 or 1");
     ctx->conv_implicit = (int)value;
+    return kOk;
+  }
+  if (k == "attention_fa_exp_poly") {
+    if (value < 0 || value > 4) return set_error(ctx, kErrArg, "attention_fa_exp_poly must be in [0, 4]");
+    ctx->attention_fa_exp_poly = (int)value;
     return kOk;
   }
   if (k == "attention_exp_poly") {

@@ -251,6 +251,7 @@ struct s3b_ctx {
                                // 2 the GEMM dequantises each weight tile in shared memory; 0 f16 at load
   int conv_implicit = 1;       // pixel-block GEMMs: implicit 3x3 convs, TMA-stored deconvs (0: im2col / scatter)
   int attention_exp_poly = 0;  // of every 8 softmax exponentials in the tcgen05 kernel, how many use the FMA pipe
+  int attention_fa_exp_poly = 1;  // the same for the persistent two-tile d = 64 kernel
   // memory attention: its per-layer body replayed from a CUDA graph (mem_attn.cpp)
   int graphs = 1;               // option "graphs"
   long long graph_epoch = 0;    // bumped by every option change and model load: cached graphs are stale

@@ -123,6 +123,12 @@ int attention(const AttnParams& p, int D, int batch_heads, cudaStream_t st);
 int attention_tc64(const __half* base, long long ld, int q_col, int k_col, int v_col, int heads, int ntok, int nwin,
                    __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int p_mode,
                    int* err, cudaStream_t st);
+// The same attention (d = 64, fused qkv buffer) on one persistent CTA per SM, two 128-query tiles
+// per work unit whose softmax warpgroups (one thread per query row) interleave with the tensor-core
+// products of the other tile.
+int attention_fa64(const __half* base, long long ld, int q_col, int k_col, int v_col, int heads, int ntok, int nwin,
+                   __half* o, long long o_n, const RowMap& omap, float scale, int exp_poly, int* err,
+                   cudaStream_t st);
 // Tensor-core (tcgen05) flash attention for head dims d = 72, 96, 256
 // (Hiera-L, Hiera-T, memory attention): q / k / v with their own row strides
 // and row counts (nq, nk), heads as column offsets (q_h etc. < row length) or

@@ -258,12 +258,19 @@ int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
   }
   // the tcgen05 kernel serves d = 64 attention over one fused qkv buffer (the ViT blocks)
   const long long kq = p.k - p.q, vq = p.v - p.q;
-  const bool tc_ok = (ctx->attention_impl == 0 || ctx->attention_impl == 3) && D == 64 && p.nq == p.nk && p.q_n == p.k_n && p.q_n == p.v_n &&
+  const bool tc_ok = (ctx->attention_impl == 0 || ctx->attention_impl == 3 || ctx->attention_impl == 4) && D == 64 &&
+                     p.nq == p.nk && p.q_n == p.k_n && p.q_n == p.v_n &&
                      p.q_b == p.k_b && p.q_b == p.v_b && p.q_b == (long long)p.nq * p.q_n && p.q_h == 64 &&
                      p.k_h == 64 && p.v_h == 64 && kq > 0 && vq > 0 && kq + 64LL * p.heads <= p.q_n &&
                      vq + 64LL * p.heads <= p.q_n && batch_heads % p.heads == 0;
   int rc;
-  if (tc_ok) {
+  // d = 64: the persistent two-tile kernel for windows (few key tiles per query tile, where its persistence
+  // hides the per-tile prologue and epilogue), the one-tile-per-CTA kernel for the long global rows
+  const bool fa = tc_ok && (ctx->attention_impl == 4 || (ctx->attention_impl == 0 && p.nk <= 1152));
+  if (fa) {
+    rc = attention_fa64(p.q, p.q_n, 0, (int)kq, (int)vq, p.heads, p.nq, batch_heads / p.heads, p.o, p.o_n, p.omap,
+                        p.scale, ctx->attention_fa_exp_poly, ctx->d_err, ctx->stream);
+  } else if (tc_ok) {
     rc = attention_tc64(p.q, p.q_n, 0, (int)kq, (int)vq, p.heads, p.nq, batch_heads / p.heads, p.o, p.o_n, p.omap,
                         p.scale, ctx->attention_exp_poly, ctx->attention_impl == 3 ? 0 : 1, ctx->d_err,
                         ctx->stream);

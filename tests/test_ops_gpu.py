@@ -237,9 +237,10 @@ def _ref_attention_qkv(qkv, nwin, heads, ntok, d, scale):
 @pytest.mark.parametrize("nwin,heads,ntok,d,pad", [(9, 16, 576, 64, 0), (1, 16, 5184, 64, 0), (3, 2, 64, 64, 0),
                                                    (2, 3, 200, 64, 64), (5, 1, 129, 64, 8), (1, 4, 1, 64, 0),
                                                    (4, 2, 300, 72, 0), (2, 2, 256, 96, 32)])
-@pytest.mark.parametrize("impl", [0, 3])
+@pytest.mark.parametrize("impl", [0, 3, 4])
 def test_attention_qkv(engine, nwin, heads, ntok, d, pad, impl):
-    """impl 0: the d = 64 softmax splits each row over two warps; 3: over two threads of one warp."""
+    """impl 0: the d = 64 softmax splits each row over two warps; 3: P in shared memory; 4: one persistent
+    CTA per SM with two query tiles and one thread per query row."""
     g = torch.Generator(device="cuda").manual_seed(nwin * 1000 + heads * 10 + ntok)
     E = heads * d
     qkv = (torch.randn(nwin * ntok, 3 * E + pad, device="cuda", generator=g) * 1.5).half()
@@ -264,20 +265,22 @@ def test_attention_qkv_impls_agree(engine):
     g = torch.Generator(device="cuda").manual_seed(5)
     qkv = (torch.randn(nwin * ntok, 3 * heads * d, device="cuda", generator=g) * 2).half()
     outs = []
-    for impl, poly in ((1, 0), (0, 0), (0, 2), (0, 4), (3, 0), (3, 3)):
+    for impl, poly in ((1, 0), (0, 0), (0, 2), (0, 4), (3, 0), (3, 3), (4, 0), (4, 2), (4, 4)):
         engine.set_option("attention_impl", impl)
         engine.set_option("attention_exp_poly", poly)
+        engine.set_option("attention_fa_exp_poly", poly)
         out = torch.empty(nwin * ntok, heads * d, device="cuda", dtype=torch.float16)
         engine.attention_qkv(qkv, out, nwin, heads, ntok, d, 0.125)
         engine.sync()
         outs.append(out.float())
     engine.set_option("attention_impl", 0)
     engine.set_option("attention_exp_poly", 0)
+    engine.set_option("attention_fa_exp_poly", 1)
     for o in outs[1:]:
         assert (o - outs[0]).abs().max().item() < 1e-2
 
 
-@pytest.mark.parametrize("impl", [0, 3])
+@pytest.mark.parametrize("impl", [0, 3, 4])
 def test_attention_qkv_growing_max(engine, impl):
     """Keys whose logits grow tile by tile, so the running reference max of the d = 64 kernel moves
     after the first key tile and the running O rows are rescaled in TMEM (both softmax layouts)."""
