@@ -281,6 +281,51 @@ int s3b_op_build_prompt(s3b_ctx* ctx, int feat, const float* const* slot_feats, 
                         const int* slot_tpos, int n_slots, const float* obj_ptrs, const int* ptr_tpos, int n_ptrs,
                         float* prompt, float* prompt_pos, int64_t capacity_rows, int* m_total, int* n_ptr_tokens);
 
+/* ---------------------------------------------------------------- SAM mask decoder */
+
+/* SAM mask decoder (sam3_build_sam_dec_graph, sam3.cpp:10544-10757, with the
+ * prompt encoder's dense inputs of sam3_populate_pe_cache, 10288-10345) on
+ * one frame, as the image predictor (sam3_segment_pvs, 10760-10990) and the
+ * tracker (sam3_propagate_single, 11171-11453) call it:
+ *   image_feats [feat*feat][256] f32: neck_trk_2 (image predictor, with
+ *     S3B_DEC_ADD_NO_MEM: no_mem_embed is added as sam3.cpp:10922-10931 does)
+ *     or the memory-attention output (tracker);
+ *   feat_s0 [(4 feat)^2][256], feat_s1 [(2 feat)^2][256]: neck_trk_0 / 1;
+ *   sparse [n_sparse][256]: prompt tokens (s3b_sam_prompt_tokens); n_sparse
+ *     = 0 uses the single not_a_point token of the tracker (11311-11314);
+ *     at most 26 tokens;
+ *   outputs (each may be NULL): masks [4][(4 feat)^2] mask logits, iou [4]
+ *     (sigmoid), obj_score [1] (logit; 10 without an object-score head),
+ *     mask_tokens [4][256] (token 0 is the SAM output token of the object
+ *     pointer).
+ * With S3B_DEC_DEVICE_PTRS every array is device memory and the call is
+ * asynchronous on the context stream; otherwise they are host arrays and the
+ * call returns when the outputs are written. */
+#define S3B_DEC_ADD_NO_MEM 1
+#define S3B_DEC_DEVICE_PTRS 2
+int s3b_sam_decode(s3b_ctx* ctx, int feat, const float* image_feats, const float* feat_s0, const float* feat_s1,
+                   const float* sparse, int n_sparse, int flags, float* masks, float* iou, float* obj_score,
+                   float* mask_tokens);
+
+/* Sparse prompt tokens of the image predictor (sam3_collect_pvs_prompt_tokens,
+ * sam3.cpp:10361-10391, encoded as sam3_segment_pvs does at 10877-10900):
+ * box corners (labels 2, 3; box = {x0, y0, x1, y1} or NULL), positive points,
+ * negative points, then one padding token, in original-image pixels
+ * (orig_width x orig_height). Writes [n][256] host floats and returns n, or a
+ * negative status (S3B_ERR_ARG also when n > capacity). */
+int s3b_sam_prompt_tokens(s3b_ctx* ctx, const float* box, const float* pos_points, int n_pos, const float* neg_points,
+                          int n_neg, int orig_width, int orig_height, float* out, int capacity);
+
+/* The decoder's dense image PE of a feat x feat grid (the dense_pe_cache of
+ * sam3_populate_pe_cache, sam3.cpp:10330-10341) into host floats
+ * [feat*feat][256]. */
+int s3b_sam_dense_pe(s3b_ctx* ctx, int feat, float* out);
+
+/* Mask choice of sam3_propagate_single (sam3.cpp:11395-11420): 0 without
+ * multimask output, else the index in 1 .. n_masks-1 with the highest IoU
+ * (first on ties). S3B_ERR_ARG on bad arguments. */
+int s3b_sam_best_mask(const float* iou, int n_masks, int multimask);
+
 /* Test hook for the engine's failure detection: enqueues on the context
  * stream one kernel that waits on a device barrier with the same bounded
  * wait every GEMM / attention kernel uses, limited to limit_ns (0 < limit_ns

@@ -25,6 +25,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 S3B_F32, S3B_F16, S3B_Q4_0, S3B_Q4_1, S3B_Q8_0 = 0, 1, 2, 3, 8
 ACT_NONE, ACT_GELU_ERF, ACT_GELU_TANH, ACT_RELU = 0, 1, 2, 3
 ENCODE_NO_NECK, ENCODE_NO_DET = 1, 2
+DEC_ADD_NO_MEM, DEC_DEVICE_PTRS = 1, 2
 
 ERRORS = {
     0: "S3B_OK", -1: "S3B_ERR_ARG", -2: "S3B_ERR_IO", -3: "S3B_ERR_FORMAT", -4: "S3B_ERR_CUDA",
@@ -77,6 +78,10 @@ SYMBOLS = [
     ("s3b_mem_attn_bank", _I, [_P, _P, _P, _I, _P, _P, _P, _I, _P, _P, _I, _P]),
     ("s3b_op_build_prompt", _I, [_P, _I, _P, _P, _P, _I, _P, _P, _I, _P, _P, _I64, ctypes.POINTER(_I),
                                  ctypes.POINTER(_I)]),
+    ("s3b_sam_decode", _I, [_P, _I, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
+    ("s3b_sam_prompt_tokens", _I, [_P, _P, _P, _I, _P, _I, _I, _I, _P, _I]),
+    ("s3b_sam_dense_pe", _I, [_P, _I, _P]),
+    ("s3b_sam_best_mask", _I, [_P, _I, _I]),
     ("s3b_test_wait_timeout", _I, [_P, _I64, _I]),
     ("s3b_select_memory_frames", _I, [_I, _I, ctypes.POINTER(_I), _I]),
     ("s3b_sine_pe_2d", _I, [_I, _I, _I, _P]),
@@ -169,6 +174,15 @@ def dequantize_rows(qtype: int, raw: np.ndarray, ne0: int) -> np.ndarray:
     if rc != 0:
         raise S3BError(f"s3b_dequantize_rows: {ERRORS.get(rc, rc)}")
     return out
+
+
+def sam_best_mask(iou, multimask: bool) -> int:
+    """Index of the mask sam3_propagate_single keeps (s3b_sam_best_mask)."""
+    a = np.ascontiguousarray(np.asarray(iou, np.float32).reshape(-1))
+    r = lib().s3b_sam_best_mask(_ptr(a), a.size, 1 if multimask else 0)
+    if r < 0:
+        raise S3BError(f"s3b_sam_best_mask: {ERRORS.get(r, r)}")
+    return r
 
 
 def select_memory_frames(bank_size: int, max_slots: int) -> list[int]:
@@ -433,6 +447,49 @@ class Engine:
                                          ctypes.byref(n_ptr))
         self._check(rc, "s3b_op_build_prompt")
         return prompt[:m_total.value], pos[:m_total.value], n_ptr.value
+
+    # -- SAM mask decoder
+    def sam_prompt_tokens(self, box=None, pos_points=(), neg_points=(), orig_size=None) -> np.ndarray:
+        """Sparse prompt tokens [n, 256] (box corners, positive, negative points, padding token)."""
+        pos = np.ascontiguousarray(np.asarray(pos_points, np.float32).reshape(-1, 2))
+        neg = np.ascontiguousarray(np.asarray(neg_points, np.float32).reshape(-1, 2))
+        bx = None if box is None else np.ascontiguousarray(np.asarray(box, np.float32).reshape(4))
+        w, h = orig_size if orig_size is not None else (self.model_info()["img_size"],) * 2
+        cap = 32
+        out = np.empty((cap, 256), np.float32)
+        n = self._L.s3b_sam_prompt_tokens(self.h, _ptr(bx), _ptr(pos) if len(pos) else None, len(pos),
+                                          _ptr(neg) if len(neg) else None, len(neg), int(w), int(h), _ptr(out), cap)
+        self._check(min(n, 0), "s3b_sam_prompt_tokens")
+        return out[:n].copy()
+
+    def sam_dense_pe(self, feat: int) -> np.ndarray:
+        out = np.empty((feat * feat, 256), np.float32)
+        self._check(self._L.s3b_sam_dense_pe(self.h, feat, _ptr(out)), "s3b_sam_dense_pe")
+        return out
+
+    def sam_decode(self, feat: int, image_feats, feat_s0, feat_s1, sparse=None, add_no_mem=False, outs=None):
+        """SAM mask decoder: all numpy (host) or all torch CUDA tensors (device, asynchronous on the engine's
+        stream). Returns (masks [4, 4 feat, 4 feat], iou [4], obj_score [1], mask_tokens [4, 256])."""
+        dev = hasattr(image_feats, "is_cuda") and image_feats.is_cuda
+        S = 4 * feat
+        if outs is None:
+            if dev:
+                import torch
+                mk = lambda *s: torch.empty(*s, device=image_feats.device, dtype=torch.float32)
+            else:
+                mk = lambda *s: np.empty(s, np.float32)
+            outs = (mk(4, S, S), mk(4), mk(1), mk(4, 256))
+        if not dev:
+            image_feats, feat_s0, feat_s1 = (np.ascontiguousarray(x, dtype=np.float32)
+                                             for x in (image_feats, feat_s0, feat_s1))
+            if sparse is not None:
+                sparse = np.ascontiguousarray(sparse, dtype=np.float32)
+        n_sparse = 0 if sparse is None else int(sparse.shape[0])
+        flags = (DEC_ADD_NO_MEM if add_no_mem else 0) | (DEC_DEVICE_PTRS if dev else 0)
+        rc = self._L.s3b_sam_decode(self.h, feat, _ptr(image_feats), _ptr(feat_s0), _ptr(feat_s1), _ptr(sparse),
+                                    n_sparse, flags, *[_ptr(o) for o in outs])
+        self._check(rc, "s3b_sam_decode")
+        return outs
 
     # -- operators on device pointers (torch CUDA tensors)
     def gemm(self, A, B, out, bias=None, act=ACT_NONE, resid=None, K=None):

@@ -857,6 +857,78 @@ int s3b_op_build_prompt(s3b_ctx* ctx, int feat, const float* const* slot_feats, 
   return kOk;
 }
 
+int s3b_sam_decode(s3b_ctx* ctx, int feat, const float* image_feats, const float* feat_s0, const float* feat_s1,
+                   const float* sparse, int n_sparse, int flags, float* masks, float* iou, float* obj_score,
+                   float* mask_tokens) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  const SamDecoder& d = ctx->model.dec;
+  if (!d.loaded) return set_error(ctx, kErrState, "model has no SAM mask decoder weights");
+  if (feat <= 0 || feat > 1024 || !image_feats || !feat_s0 || !feat_s1 || n_sparse < 0 || (n_sparse && !sparse) ||
+      (flags & ~(S3B_DEC_ADD_NO_MEM | S3B_DEC_DEVICE_PTRS)))
+    return set_error(ctx, kErrArg, "bad mask-decoder arguments");
+  const int add_no_mem = (flags & S3B_DEC_ADD_NO_MEM) ? 1 : 0;
+  if (flags & S3B_DEC_DEVICE_PTRS)
+    return sam_dec_run(ctx, feat, image_feats, feat_s0, feat_s1, sparse, n_sparse, add_no_mem, masks, iou, obj_score,
+                       mask_tokens);
+  const size_t D = d.D, HH = (size_t)feat * feat, nm = d.n_mask;
+  float *di, *d0, *d1, *dsp = nullptr;
+  if ((rc = stage_host(ctx, image_feats, HH * D, "dec_h_img", &di))) return rc;
+  if ((rc = stage_host(ctx, feat_s0, 16 * HH * D, "dec_h_s0", &d0))) return rc;
+  if ((rc = stage_host(ctx, feat_s1, 4 * HH * D, "dec_h_s1", &d1))) return rc;
+  if (n_sparse && (rc = stage_host(ctx, sparse, (size_t)n_sparse * D, "dec_h_sparse", &dsp))) return rc;
+  DevBuf* o = ctx->buf("dec_h_out", (16 * HH * nm + nm + 1 + nm * D) * 4, &rc);
+  if (rc) return rc;
+  float* om = o->as<float>();
+  float* oi = om + 16 * HH * nm;
+  float* oo = oi + nm;
+  float* ot = oo + 1;
+  if ((rc = sam_dec_run(ctx, feat, di, d0, d1, dsp, n_sparse, add_no_mem, om, oi, oo, ot))) return rc;
+  struct Out {
+    float* dst;
+    const float* src;
+    size_t n;
+  } outs[4] = {{masks, om, 16 * HH * nm}, {iou, oi, nm}, {obj_score, oo, 1}, {mask_tokens, ot, nm * D}};
+  for (const Out& x : outs)
+    if (x.dst && cudaMemcpyAsync(x.dst, x.src, x.n * 4, cudaMemcpyDeviceToHost, ctx->stream) != cudaSuccess)
+      return set_error(ctx, kErrCuda, "device-to-host copy failed");
+  return s3b_sync(ctx);
+}
+
+int s3b_sam_prompt_tokens(s3b_ctx* ctx, const float* box, const float* pos_points, int n_pos, const float* neg_points,
+                          int n_neg, int orig_width, int orig_height, float* out, int capacity) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!ctx->model.dec.loaded) return set_error(ctx, kErrState, "model has no SAM prompt encoder weights");
+  const int n = sam_prompt_tokens(ctx->model.dec, box, pos_points, n_pos, neg_points, n_neg, (float)orig_width,
+                                  (float)orig_height, ctx->model.hp.img_size, out, capacity);
+  if (n < 0) return set_error(ctx, kErrArg, "bad prompt arguments (or more than %d tokens)", capacity);
+  return n;
+}
+
+int s3b_sam_dense_pe(s3b_ctx* ctx, int feat, float* out) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!ctx->model.dec.loaded) return set_error(ctx, kErrState, "model has no SAM prompt encoder weights");
+  if (feat <= 0 || feat > 1024 || !out) return set_error(ctx, kErrArg, "bad dense-PE arguments");
+  const float* pe = sam_dec_dense_pe(ctx, feat, &rc);
+  if (rc) return rc;
+  if (cudaMemcpyAsync(out, pe, (size_t)feat * feat * ctx->model.dec.D * 4, cudaMemcpyDeviceToHost, ctx->stream) !=
+      cudaSuccess)
+    return set_error(ctx, kErrCuda, "device-to-host copy failed");
+  return s3b_sync(ctx);
+}
+
+int s3b_sam_best_mask(const float* iou, int n_masks, int multimask) {
+  if (!iou || n_masks <= 0) return S3B_ERR_ARG;
+  if (!multimask || n_masks < 2) return 0;
+  // multimask output: the best of the tokens 1 .. n-1 by predicted IoU, first one on ties
+  int best = 1;
+  for (int m = 2; m < n_masks; ++m)
+    if (iou[m] > iou[best]) best = m;
+  return best;
+}
+
 int s3b_test_wait_timeout(s3b_ctx* ctx, int64_t limit_ns, int withhold) {
   int rc = ctx_enter(ctx);
   if (rc) return rc;

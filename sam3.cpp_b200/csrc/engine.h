@@ -168,6 +168,40 @@ struct MemAttnLayer {
   Linear sa_qkv, sa_out, ca_q, ca_k, ca_v, ca_out, fc1, fc2;
 };
 
+// SAM mask decoder (sam3.cpp:563-599, registered at 1848-1966). Token-side weights are read by
+// tok_linear, image-side weights by the tcgen05 GEMM; all f16 [N][Kpad] (dequantised at load).
+struct SamTwoWay {
+  Linear sa_q, sa_k, sa_v, sa_out;  // token self-attention (256 -> 256, 8 heads)
+  Linear t2i_q, t2i_out;            // token side of tokens -> image (256 -> 128, 128 -> 256)
+  Linear kq;                        // image side, input keys + key_pe: [t2i k ; i2t q] (256 rows)
+  Linear t2i_v;                     // image side, input keys: t2i v (128 rows)
+  Linear i2t_k, i2t_v;              // token side of image -> tokens (256 -> 128)
+  Linear i2t_out;                   // image side, 128 -> 256 (residual into the keys)
+  Linear mlp1, mlp2;                // token MLP 256 -> 2048 -> 256 (ReLU)
+  Vec n1w, n1b, n2w, n2b, n3w, n3b, n4w, n4b;
+};
+
+struct SamDecoder {
+  bool loaded = false;
+  int D = 256, n_mask = 4, has_obj = 1, heads = 8;
+  std::vector<SamTwoWay> blocks;
+  Linear fin_q, fin_k, fin_v, fin_out;
+  Vec fin_nw, fin_nb;
+  Linear up1;      // deconv 2x2 D -> D/4, rows [(ky*2 + kx)*64 + co][D]
+  Vec up1_nw, up1_nb;
+  Linear up2;      // deconv 2x2 D/4 -> D/8, rows [(ky*2 + kx)*32 + co][64]
+  Linear conv_s0;  // 1x1 D -> D/8 on neck_trk_0
+  Linear conv_s1;  // 1x1 D -> D/4 on neck_trk_1
+  std::vector<Linear> hyper;  // n_mask x 3 layers
+  Linear iou[3], obj[3];
+  // prompt encoder values kept on the host (sam3_populate_pe_cache, sam3.cpp:10288-10345)
+  std::vector<float> pe_gauss, point_emb[4], not_a_point, no_mask, no_mem;
+  // device: the special output tokens [obj?, iou, masks] [n_special][D], no_mask, no_mem, not_a_point
+  std::shared_ptr<DevBuf> tokens;
+  Vec d_no_mask, d_no_mem, d_not_a_point;
+  int n_special() const { return (has_obj ? 1 : 0) + 1 + n_mask; }
+};
+
 struct Model {
   HParams hp;
   bool loaded = false;
@@ -192,6 +226,7 @@ struct Model {
   bool has_mem_attn = false;
   std::vector<float> maskmem_tpos;   // [num_maskmem][64]
   std::vector<float> obj_ptr_tpos_w, obj_ptr_tpos_b;  // [64][256], [64]
+  SamDecoder dec;
   size_t device_bytes = 0;
   // largest N*K of a weight kept in block form; the f16 staging arena of weights_quantised = 1 holds
   // the block-form weights of one ViT / Hiera block or memory-attention layer (stage_arena_elems)
@@ -329,6 +364,19 @@ int mem_attn_run(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat
                  const float* prompt_pos, int m_total, int n_ptr, float* out);
 int mem_attn_run_bank(s3b_ctx* ctx, const float* curr, const float* src_pos, int feat, const PromptArgs& pa,
                       float* out);
+
+// SAM mask decoder (mask_decoder.cpp). Inputs are device pointers: image_feats [H*H][256] (memory-attention
+// output or neck_trk_2), feat_s0 [(4H)^2][256], feat_s1 [(2H)^2][256] (neck_trk_0 / 1), sparse [n_sparse][256]
+// prompt tokens (n_sparse = 0: the single not_a_point token of the tracker's propagation). Outputs (device):
+// masks [n_mask][(4H)^2], iou [n_mask], obj [1], mask_tokens [n_mask][256] (each may be null).
+int sam_dec_run(s3b_ctx* ctx, int H, const float* image_feats, const float* feat_s0, const float* feat_s1,
+                const float* sparse, int n_sparse, int add_no_mem, float* masks, float* iou, float* obj,
+                float* mask_tokens);
+// dense image PE of the H x H grid (sam3_populate_pe_cache's dense_pe_cache), device f32 [H*H][256], cached
+const float* sam_dec_dense_pe(s3b_ctx* ctx, int H, int* rc);
+// sparse prompt tokens of the image predictor (sam3_segment_pvs, sam3.cpp:10877-10900) on the host
+int sam_prompt_tokens(const SamDecoder& dec, const float* box, const float* pos, int n_pos, const float* neg,
+                      int n_neg, float orig_w, float orig_h, int input_size, float* out, int capacity);
 
 // encoders
 int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);

@@ -202,6 +202,64 @@ struct PromptArgs {
 // b = f16(prompt) (the cross-attention key and value inputs, sam3.cpp:9278-9283).
 int build_prompt(const PromptArgs& args, void* a, void* b, int out_f16, cudaStream_t st);
 
+// ---------------------------------------------------------------- SAM mask decoder (sam_dec.cu)
+// Token-side linear layers of the decoder: a few rows (the output + prompt tokens) times an f16
+// weight [N][ldw] (K-major, K and ldw multiples of 8, rows 16-byte aligned):
+//   y[r][n] = act((x[r] (+ x2[r])) . W[n] + b[n]) (+ resid[r][n]),  r < R <= kTokMaxRows.
+// Up to kTokMaxJobs independent layers run in one launch. act: 0 none, 1 ReLU, 2 sigmoid.
+constexpr int kTokMaxRows = 32, kTokMaxJobs = 8;
+struct TokJob {
+  const float* x = nullptr;
+  const float* x2 = nullptr;  // optional second input added to x (the token PE), row stride ldx too
+  long long ldx = 0;
+  int R = 0;
+  const __half* W = nullptr;
+  long long ldw = 0;
+  const float* b = nullptr;
+  int N = 0, K = 0;
+  float* y = nullptr;
+  long long ldy = 0;
+  const float* resid = nullptr;  // may equal y (in-place residual)
+  long long ldr = 0;
+  int act = 0;
+};
+int tok_linear(const TokJob* jobs, int n_jobs, cudaStream_t st);
+// y[r] = LayerNorm(a[r] (+ b[r])) * g + beta over C (<= 1024, a multiple of 32) channels; y may equal a.
+int tok_layernorm(const float* a, const float* b, long long ld, int rows, int C, const float* g, const float* beta,
+                  float eps, float* y, cudaStream_t st);
+// Multi-head attention among the tokens: q / k / v f32 rows [nt][ld*] with head h in columns h*hd ..,
+// out [nt][ldo]; nt <= kTokMaxRows, heads * nt <= 256, hd <= 32.
+int tok_attention(const float* q, long long ldq, const float* k, long long ldk, const float* v, long long ldv,
+                  int nt, int heads, int hd, float scale, float* out, long long ldo, cudaStream_t st);
+// Tokens -> image cross-attention with head dim 16: q f32 [nt][ldq], k / v f16 image rows [nkv][ldk / ldv]
+// (head h in columns h*16 ..), out f32 [nt][ldo]. Keys are split over CTAs in chunks of kT2iChunk whose
+// partial (max, sum, 16 outputs) per (token, head) go to ws (t2i_ws_floats floats) and are merged by a
+// second kernel.
+constexpr int kT2iChunk = 64;
+long long t2i_ws_floats(int nt, int heads, long long nkv);
+int t2i_attention(const float* q, long long ldq, const __half* k, long long ldk, const __half* v, long long ldv,
+                  int nt, int heads, long long nkv, float scale, float* ws, float* out, long long ldo,
+                  cudaStream_t st);
+// Image -> tokens cross-attention with head dim 16: one thread per (image row, head); q f16 [n][ldq],
+// k / v f32 token rows [nt][ldk / ldv], out f16 [n][ldo].
+int i2t_attention(const __half* q, long long ldq, const float* k, long long ldk, const float* v, long long ldv,
+                  int nt, int heads, long long n, float scale, __half* out, long long ldo, cudaStream_t st);
+// Image keys of the decoder, one row of C = 256 channels per token:
+//   mode 0: v = (x + add1) + add0 (add1 optional);  mode 1: v = LayerNorm(x) * g + beta (eps)
+// keys = v (f32, may equal x), k16 = f16(v), kpe16 = f16(v + pe[row]).
+int dec_keys(const float* x, long long rows, int mode, const float* add0, const float* add1, const float* g,
+             const float* beta, float eps, const float* pe, float* keys, __half* k16, __half* kpe16, cudaStream_t st);
+// First upscaling stage at the 2H x 2H grid (n = (2H)^2 pixels): v = up1[p] + (feat_s1[p] . Ws1 + bs1),
+// out[p] = f16(GELU-erf(LayerNorm2d(v) * g + beta)), 64 channels; feat_s1 f32 [n][256], Ws1 f16 [64][256].
+int dec_upscale1(const float* up1, const float* feat_s1, const __half* ws1, const float* bs1, const float* g,
+                 const float* beta, float eps, long long n, __half* out, cudaStream_t st);
+// Second upscaling stage and the mask products at the S x S grid (S = 4H): per pixel (y, x),
+// u = GELU-erf((u1[y/2][x/2] . W2[(y%2)*2 + x%2] + b2) + (feat_s0[p] . Ws0 + bs0)) (32 channels), then
+// masks[m][p] = hyper[m] . u for m < 4. u1 f16 [S/2][S/2][64], W2 f16 rows [(ky*2 + kx)*32 + co][64],
+// feat_s0 f32 [S*S][256], Ws0 f16 [32][256], hyper f32 [4][32], masks f32 [4][S*S].
+int dec_masks(const __half* u1, const __half* w2, const float* b2, const float* feat_s0, const __half* ws0,
+              const float* bs0, const float* hyper, int S, float* masks, cudaStream_t st);
+
 // ggml block formats (32 values per block along the row).
 enum QType : int { QT_F32 = 0, QT_F16 = 1, QT_Q4_0 = 2, QT_Q4_1 = 3, QT_Q8_0 = 8 };
 long long qtype_row_bytes(int qtype, long long ne0);

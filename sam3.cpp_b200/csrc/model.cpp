@@ -642,6 +642,152 @@ static int load_mem_attn(s3b_ctx* ctx, const Index& idx) {
   return rc;
 }
 
+// SAM prompt encoder + mask decoder weights (sam3.cpp:1848-1966; optional: files without them load the
+// encoder path alone). Every linear and 1x1 weight is dequantised to f16 at load whatever the file's type:
+// the decoder is a few MB and its token-side layers read their weights with plain loads.
+static int load_sam_dec(s3b_ctx* ctx, const Index& idx) {
+  // dense PE grids cached for the previous model's Gaussian matrix
+  for (auto it = ctx->ws.begin(); it != ctx->ws.end();)
+    it = it->first.compare(0, 7, "dec_pe_") == 0 ? ctx->ws.erase(it) : std::next(it);
+  if (!idx.get("sam_dec.iou_token.weight")) return kOk;
+  SamDecoder& d = ctx->model.dec;
+  d = SamDecoder();
+  const int saved_q = ctx->weights_quantised;
+  ctx->weights_quantised = 0;
+  struct Restore {
+    s3b_ctx* c;
+    int v;
+    ~Restore() { c->weights_quantised = v; }
+  } restore{ctx, saved_q};
+  int rc = 0;
+  auto lin = [&](const std::string& p, Linear& L, int k_dims = 1) -> int {
+    NEED(w, p + ".weight");
+    NEED(b, p + ".bias");
+    return upload_linear(ctx, *w, b, L, 8, k_dims);
+  };
+  auto vec = [&](const std::string& n, Vec& v) -> int {
+    NEED(t, n);
+    v = upload_vec(ctx, *t, &rc);
+    return rc;
+  };
+  auto host = [&](const std::string& n, std::vector<float>& v, size_t want) -> int {
+    NEED(t, n);
+    tensor_to_f32(*t, v);
+    if (want && v.size() != want) return set_error(ctx, kErrFormat, "%s: %zu values, expected %zu", n.c_str(), v.size(), want);
+    return kOk;
+  };
+  NEED(mt, "sam_dec.mask_tokens.weight");
+  d.D = (int)mt->ne[0];
+  d.n_mask = (int)mt->ne[1];
+  const int D = d.D;
+  if (D != 256 || d.n_mask != 4) return set_error(ctx, kErrFormat, "mask decoder: D %d / %d mask tokens unsupported", D, d.n_mask);
+  d.has_obj = idx.get("sam_dec.obj_score_token.weight") != nullptr;
+  if ((rc = host("sam_pe.pe_gaussian", d.pe_gauss, (size_t)D))) return rc;
+  for (int i = 0; i < 4; ++i)
+    if ((rc = host("sam_pe.point_embeddings." + std::to_string(i) + ".weight", d.point_emb[i], D))) return rc;
+  if ((rc = host("sam_pe.not_a_point_embed.weight", d.not_a_point, D))) return rc;
+  if ((rc = host("sam_pe.no_mask_embed.weight", d.no_mask, D))) return rc;
+  if (idx.get("no_mem_embed")) {
+    if ((rc = host("no_mem_embed", d.no_mem, D))) return rc;
+  } else {
+    d.no_mem.assign(D, 0.f);
+  }
+  {
+    // output tokens in the decoder's order: [obj_score?], iou, mask tokens (sam3.cpp:10575-10590)
+    std::vector<float> tok, t;
+    if (d.has_obj) {
+      if ((rc = host("sam_dec.obj_score_token.weight", t, D))) return rc;
+      tok.insert(tok.end(), t.begin(), t.end());
+    }
+    if ((rc = host("sam_dec.iou_token.weight", t, D))) return rc;
+    tok.insert(tok.end(), t.begin(), t.end());
+    if ((rc = host("sam_dec.mask_tokens.weight", t, (size_t)D * d.n_mask))) return rc;
+    tok.insert(tok.end(), t.begin(), t.end());
+    d.tokens = upload_bytes(ctx, tok.data(), tok.size() * 4, &rc);
+    if (rc) return rc;
+    d.d_no_mask.n = d.d_no_mem.n = d.d_not_a_point.n = D;
+    d.d_no_mask.d = upload_bytes(ctx, d.no_mask.data(), D * 4, &rc);
+    if (!rc) d.d_no_mem.d = upload_bytes(ctx, d.no_mem.data(), D * 4, &rc);
+    if (!rc) d.d_not_a_point.d = upload_bytes(ctx, d.not_a_point.data(), D * 4, &rc);
+    if (rc) return rc;
+  }
+  int depth = 0;
+  while (idx.get("sam_dec.twoway." + std::to_string(depth) + ".norm1.weight")) ++depth;
+  if (depth == 0) return set_error(ctx, kErrFormat, "mask decoder without TwoWay blocks");
+  d.blocks.resize(depth);
+  for (int i = 0; i < depth; ++i) {
+    SamTwoWay& B = d.blocks[i];
+    const std::string p = "sam_dec.twoway." + std::to_string(i);
+    if ((rc = lin(p + ".sa.q_proj", B.sa_q)) || (rc = lin(p + ".sa.k_proj", B.sa_k)) ||
+        (rc = lin(p + ".sa.v_proj", B.sa_v)) || (rc = lin(p + ".sa.out_proj", B.sa_out)) ||
+        (rc = lin(p + ".cross_attn_token_to_image.q_proj", B.t2i_q)) ||
+        (rc = lin(p + ".cross_attn_token_to_image.v_proj", B.t2i_v)) ||
+        (rc = lin(p + ".cross_attn_token_to_image.out_proj", B.t2i_out)) ||
+        (rc = lin(p + ".cross_attn_image_to_token.k_proj", B.i2t_k)) ||
+        (rc = lin(p + ".cross_attn_image_to_token.v_proj", B.i2t_v)) ||
+        (rc = lin(p + ".cross_attn_image_to_token.out_proj", B.i2t_out)) || (rc = lin(p + ".mlp.lin1", B.mlp1)) ||
+        (rc = lin(p + ".mlp.lin2", B.mlp2)))
+      return rc;
+    {
+      // the two image-side projections of keys + key_pe share one GEMM: rows [t2i k ; i2t q]
+      NEED(kw, p + ".cross_attn_token_to_image.k_proj.weight");
+      NEED(kb, p + ".cross_attn_token_to_image.k_proj.bias");
+      NEED(qw, p + ".cross_attn_image_to_token.q_proj.weight");
+      NEED(qb, p + ".cross_attn_image_to_token.q_proj.bias");
+      std::vector<float> a, b, ba, bb;
+      tensor_to_f32(*kw, a);
+      tensor_to_f32(*qw, b);
+      tensor_to_f32(*kb, ba);
+      tensor_to_f32(*qb, bb);
+      const int K = (int)kw->ne[0];
+      if (qw->ne[0] != K || (int)ba.size() * K != (int)a.size() || (int)bb.size() * K != (int)b.size())
+        return set_error(ctx, kErrFormat, "%s: cross-attention projection shapes", p.c_str());
+      const int N = (int)(ba.size() + bb.size());
+      a.insert(a.end(), b.begin(), b.end());
+      ba.insert(ba.end(), bb.begin(), bb.end());
+      if ((rc = upload_b_operand(ctx, a, N, K, 8, B.kq))) return rc;
+      B.kq.b = upload_bytes(ctx, ba.data(), ba.size() * 4, &rc);
+      if (rc) return rc;
+    }
+    if ((rc = vec(p + ".norm1.weight", B.n1w)) || (rc = vec(p + ".norm1.bias", B.n1b)) ||
+        (rc = vec(p + ".norm2.weight", B.n2w)) || (rc = vec(p + ".norm2.bias", B.n2b)) ||
+        (rc = vec(p + ".norm3.weight", B.n3w)) || (rc = vec(p + ".norm3.bias", B.n3b)) ||
+        (rc = vec(p + ".norm4.weight", B.n4w)) || (rc = vec(p + ".norm4.bias", B.n4b)))
+      return rc;
+    if (B.sa_q.N != D || B.t2i_q.N != 128 || B.kq.N != 256 || B.t2i_v.N != 128 || B.i2t_k.N != 128 ||
+        B.i2t_out.K != 128 || B.mlp2.N != D)
+      return set_error(ctx, kErrFormat, "%s: unsupported attention dims", p.c_str());
+  }
+  if ((rc = lin("sam_dec.final_attn.q_proj", d.fin_q)) || (rc = lin("sam_dec.final_attn.k_proj", d.fin_k)) ||
+      (rc = lin("sam_dec.final_attn.v_proj", d.fin_v)) || (rc = lin("sam_dec.final_attn.out_proj", d.fin_out)) ||
+      (rc = vec("sam_dec.final_norm.weight", d.fin_nw)) || (rc = vec("sam_dec.final_norm.bias", d.fin_nb)))
+    return rc;
+  {
+    NEED(w0, "sam_dec.upscale.0.weight");
+    NEED(b0, "sam_dec.upscale.0.bias");
+    NEED(w3, "sam_dec.upscale.3.weight");
+    NEED(b3, "sam_dec.upscale.3.bias");
+    if ((rc = upload_deconv(ctx, *w0, *b0, d.up1)) || (rc = upload_deconv(ctx, *w3, *b3, d.up2))) return rc;
+    if ((rc = vec("sam_dec.upscale.1.weight", d.up1_nw)) || (rc = vec("sam_dec.upscale.1.bias", d.up1_nb))) return rc;
+    if ((rc = lin("sam_dec.conv_s0", d.conv_s0, 3)) || (rc = lin("sam_dec.conv_s1", d.conv_s1, 3))) return rc;
+    if (d.up1.N != 4 * 64 || d.up1.K != D || d.up2.N != 4 * 32 || d.up2.K != 64 || d.conv_s0.N != 32 ||
+        d.conv_s0.K != D || d.conv_s1.N != 64 || d.conv_s1.K != D || d.up1_nw.n != 64)
+      return set_error(ctx, kErrFormat, "mask decoder: unsupported upscaling shapes");
+  }
+  d.hyper.resize((size_t)d.n_mask * 3);
+  for (int m = 0; m < d.n_mask; ++m)
+    for (int j = 0; j < 3; ++j)
+      if ((rc = lin("sam_dec.hyper." + std::to_string(m) + ".layers." + std::to_string(j), d.hyper[m * 3 + j])))
+        return rc;
+  for (int j = 0; j < 3; ++j) {
+    if ((rc = lin("sam_dec.iou_prediction_head.layers." + std::to_string(j), d.iou[j]))) return rc;
+    if (d.has_obj && (rc = lin("sam_dec.pred_obj_score_head.layers." + std::to_string(j), d.obj[j]))) return rc;
+  }
+  if (d.hyper[2].N != 32 || d.iou[2].N != d.n_mask) return set_error(ctx, kErrFormat, "mask decoder: head shapes");
+  d.loaded = true;
+  return kOk;
+}
+
 static int load_sam3(s3b_ctx* ctx, const Index& idx) {
   Model& M = ctx->model;
   const HParams& hp = M.hp;
@@ -716,7 +862,8 @@ static int load_sam3(s3b_ctx* ctx, const Index& idx) {
     if ((rc = load_neck(ctx, idx, "neck.det.", M.neck_det))) return rc;
     M.has_neck_det = true;
   }
-  return load_mem_attn(ctx, idx);
+  if ((rc = load_mem_attn(ctx, idx))) return rc;
+  return load_sam_dec(ctx, idx);
 }
 
 // Per-block Hiera metadata (sam2_precompute_hiera_metadata, sam3.cpp:1676-1742):
@@ -856,7 +1003,8 @@ static int load_sam2(s3b_ctx* ctx, const Index& idx) {
     NEED(b, p + ".bias");
     if ((rc = upload_linear(ctx, *w, b, M.fpn[i], 8, 3))) return rc;
   }
-  return load_mem_attn(ctx, idx);
+  if ((rc = load_mem_attn(ctx, idx))) return rc;
+  return load_sam_dec(ctx, idx);
 }
 
 int parse_hparams_array(int is_sam2, const int32_t* v, int n, HParams& hp, std::string& err) {

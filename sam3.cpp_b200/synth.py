@@ -41,6 +41,7 @@ class Sam3Config:
     num_maskmem: int = 7
     max_obj_ptrs: int = 16
     mem_ffn: int = 2048
+    with_sam_dec: bool = False
 
     @property
     def grid(self) -> int:
@@ -90,6 +91,7 @@ class Sam2Config:
     num_maskmem: int = 7
     max_obj_ptrs: int = 16
     mem_ffn: int = 2048
+    with_sam_dec: bool = False
 
     def hparams(self) -> list[int]:
         # sam2_load_hparams order (sam3.cpp:1564-1626), 57 fields for the Hiera backbone
@@ -161,6 +163,8 @@ def sam2_tensors(cfg: Sam2Config, seed: int = 0, ln_random: bool = False) -> dic
         T[f"fpn.convs.{i}.bias"] = g.w(cfg.neck_dim)
     if cfg.with_mem_attn:
         _mem_attn(g, T, cfg.neck_dim, cfg.mem_out_dim, cfg.mem_attn_layers, cfg.mem_ffn, cfg.num_maskmem)
+    if cfg.with_sam_dec:
+        _sam_dec(g, T, cfg.neck_dim)
     return T
 
 
@@ -241,6 +245,69 @@ def _mem_attn(g: _Gen, T: dict, D: int, MD: int, layers: int, ffn: int, num_mask
     T["obj_ptr_tpos_proj.bias"] = g.w(MD)
 
 
+def _sam_dec(g: _Gen, T: dict, D: int, ffn: int = 2048, n_mask: int = 4, depth: int = 2):
+    """SAM prompt-encoder embeddings + SAM mask decoder + the tracker's no_mem_embed, in .ggml naming
+    (convert_sam3_to_ggml.py:167-185; shapes as registered at sam3.cpp:1848-1966). Embeddings and the
+    Gaussian PE matrix are N(0, 1) like their PyTorch initialisation, linear weights N(0, 0.02)."""
+    Di = D // 2  # the cross-attention internal dim (downsample rate 2)
+    T["sam_pe.pe_gaussian"] = g.w(2, D // 2, std=1.0)
+    for i in range(4):
+        T[f"sam_pe.point_embeddings.{i}.weight"] = g.w(1, D, std=1.0)
+    T["sam_pe.not_a_point_embed.weight"] = g.w(1, D, std=1.0)
+    T["sam_pe.no_mask_embed.weight"] = g.w(1, D, std=1.0)
+    T["sam_dec.iou_token.weight"] = g.w(1, D, std=1.0)
+    T["sam_dec.mask_tokens.weight"] = g.w(n_mask, D, std=1.0)
+    T["sam_dec.obj_score_token.weight"] = g.w(1, D, std=1.0)
+
+    def attn(pfx, di):
+        for a in ("q_proj", "k_proj", "v_proj"):
+            T[f"{pfx}.{a}.weight"] = g.w(di, D)
+            T[f"{pfx}.{a}.bias"] = g.w(di)
+        T[f"{pfx}.out_proj.weight"] = g.w(D, di)
+        T[f"{pfx}.out_proj.bias"] = g.w(D)
+
+    for i in range(depth):
+        p = f"sam_dec.twoway.{i}"
+        attn(p + ".sa", D)
+        attn(p + ".cross_attn_token_to_image", Di)
+        attn(p + ".cross_attn_image_to_token", Di)
+        for n in ("norm1", "norm2", "norm3", "norm4"):
+            T[f"{p}.{n}.weight"], T[f"{p}.{n}.bias"] = g.ln(D)
+        T[f"{p}.mlp.lin1.weight"] = g.w(ffn, D)
+        T[f"{p}.mlp.lin1.bias"] = g.w(ffn)
+        T[f"{p}.mlp.lin2.weight"] = g.w(D, ffn)
+        T[f"{p}.mlp.lin2.bias"] = g.w(D)
+    attn("sam_dec.final_attn", Di)
+    T["sam_dec.final_norm.weight"], T["sam_dec.final_norm.bias"] = g.ln(D)
+    T["sam_dec.upscale.0.weight"] = g.w(D, D // 4, 2, 2)          # ConvTranspose2d [Cin, Cout, kH, kW]
+    T["sam_dec.upscale.0.bias"] = g.w(D // 4)
+    T["sam_dec.upscale.1.weight"], T["sam_dec.upscale.1.bias"] = g.ln(D // 4)   # LayerNorm2d
+    T["sam_dec.upscale.3.weight"] = g.w(D // 4, D // 8, 2, 2)
+    T["sam_dec.upscale.3.bias"] = g.w(D // 8)
+    T["sam_dec.conv_s0.weight"] = g.w(D // 8, D, 1, 1)
+    T["sam_dec.conv_s0.bias"] = g.w(D // 8)
+    T["sam_dec.conv_s1.weight"] = g.w(D // 4, D, 1, 1)
+    T["sam_dec.conv_s1.bias"] = g.w(D // 4)
+    for m in range(n_mask):
+        for j in range(3):
+            T[f"sam_dec.hyper.{m}.layers.{j}.weight"] = g.w(D // 8 if j == 2 else D, D)
+            T[f"sam_dec.hyper.{m}.layers.{j}.bias"] = g.w(D // 8 if j == 2 else D)
+    for j in range(3):
+        T[f"sam_dec.iou_prediction_head.layers.{j}.weight"] = g.w(n_mask if j == 2 else D, D)
+        T[f"sam_dec.iou_prediction_head.layers.{j}.bias"] = g.w(n_mask if j == 2 else D)
+        T[f"sam_dec.pred_obj_score_head.layers.{j}.weight"] = g.w(1 if j == 2 else D, D)
+        T[f"sam_dec.pred_obj_score_head.layers.{j}.bias"] = g.w(1 if j == 2 else D)
+    T["no_mem_embed"] = g.w(1, 1, D)
+
+
+def sam_dec_tensors(seed: int, D: int = 256, ln_random: bool = True) -> dict:
+    """The SAM prompt encoder + mask decoder tensors alone (the names and shapes _sam_dec writes)."""
+    g = _Gen(seed, ln_random)
+    T: dict[str, np.ndarray] = {}
+    _sam_dec(g, T, D)
+    return T
+
+
 def sam3_tensors(cfg: Sam3Config, seed: int = 0, ln_random: bool = False, neck_det: bool = False) -> dict:
     """name -> f32 array (PyTorch shape) of a SAM 3 image encoder (+ optional memory attention)."""
     g = _Gen(seed, ln_random)
@@ -271,6 +338,8 @@ def sam3_tensors(cfg: Sam3Config, seed: int = 0, ln_random: bool = False, neck_d
     _neck(g, T, "neck.trk.", E, cfg.neck_dim, cfg.neck_mid)
     if cfg.with_mem_attn:
         _mem_attn(g, T, cfg.neck_dim, cfg.mem_out_dim, cfg.mem_attn_layers, cfg.mem_ffn, cfg.num_maskmem)
+    if cfg.with_sam_dec:
+        _sam_dec(g, T, cfg.neck_dim)
     return T
 
 

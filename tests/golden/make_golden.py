@@ -18,6 +18,10 @@ Run in a container that has the reference checkout (read-only) and torch:
 3. window_golden.npz — window_partition / window_unpartition imported from
    the reference's tests/dump_vit_reference.py on seeded padded inputs (the
    Hiera window path: 64 -> 70 at ws 14, q-pooled unpartition at ws // 2).
+4. sam_dec_golden.npz — dump_case() imported from the reference's
+   tests/dump_phase6_reference.py (SAM prompt encoder + SAM mask decoder) on
+   seeded synthetic decoder weights, seeded neck_trk_0..2 feature maps at the
+   SAM 3 size (72^2 image tokens) and three prompt cases of our own.
 
 Each dumped tensor is stored as deterministic samples (indices + values)
 plus summary statistics, so the fixtures stay small; tests regenerate the
@@ -218,10 +222,93 @@ def make_window(reference: str, out_path: str):
     print("wrote", out_path)
 
 
+SAMDEC_SEED = 91
+SAMDEC_FEAT_SEED = 92
+# (case name, positive points, negative points, box) in 1008^2 input coordinates
+SAMDEC_CASES = [
+    ("point", [(412.0, 530.0)], [], None),
+    ("box", [], [], (150.0, 210.0, 790.0, 880.0)),
+    ("box_points", [(600.0, 610.0)], [(300.0, 280.0)], (150.0, 210.0, 790.0, 880.0)),
+]
+
+
+def sam_dec_weights():
+    """Stored (f16-rounded) values of the seeded synthetic prompt-encoder / mask-decoder tensors."""
+    load_pkg()
+    from sam3_b200 import synth
+    return synth.stored_values(synth.sam_dec_tensors(SAMDEC_SEED), 1, None)
+
+
+def sam_dec_features(H=72, seed=SAMDEC_FEAT_SEED):
+    """neck_trk_0..2 stand-ins, channel-last f32 [4H, 4H, 256], [2H, 2H, 256], [H, H, 256]."""
+    rng = np.random.default_rng(seed)
+    return [rng.standard_normal((s, s, 256), dtype=np.float32) for s in (4 * H, 2 * H, H)]
+
+
+def sam_dec_torch_names(W: dict):
+    """.ggml decoder names -> (prompt encoder dict, mask decoder dict, no_mem_embed) as dump_phase6 reads them
+    (the converter's renames, convert_sam3_to_ggml.py:167-187, undone)."""
+    import torch
+    pe, dec = {}, {}
+    for k, v in W.items():
+        t = torch.from_numpy(np.ascontiguousarray(v))
+        if k == "sam_pe.pe_gaussian":
+            pe["pe_layer.positional_encoding_gaussian_matrix"] = t
+        elif k.startswith("sam_pe."):
+            pe[k[len("sam_pe."):]] = t
+        elif k.startswith("sam_dec."):
+            n = k[len("sam_dec."):]
+            n = n.replace("final_attn.", "transformer.final_attn_token_to_image.")
+            n = n.replace("final_norm.", "transformer.norm_final_attn.")
+            n = n.replace("upscale.", "output_upscaling.").replace("hyper.", "output_hypernetworks_mlps.")
+            if n.startswith("twoway."):
+                n = "transformer.layers." + n[len("twoway."):].replace(".sa.", ".self_attn.")
+            dec[n] = t
+    return pe, dec, torch.from_numpy(W["no_mem_embed"].reshape(-1))
+
+
+def make_sam_dec(reference: str, out_path: str):
+    import torch
+    spec = importlib.util.spec_from_file_location("dump_phase6_reference",
+                                                  os.path.join(reference, "tests", "dump_phase6_reference.py"))
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    W = sam_dec_weights()
+    pe, dec, no_mem = sam_dec_torch_names(W)
+    f0, f1, f2 = sam_dec_features()
+    nchw = [torch.from_numpy(np.ascontiguousarray(f.transpose(2, 0, 1)))[None] for f in (f0, f1, f2)]
+    out = {}
+
+    def load(d, name):
+        shape = tuple(int(x) for x in open(os.path.join(d, name + ".shape")).read().split(","))
+        return np.fromfile(os.path.join(d, name + ".bin"), dtype=np.float32).reshape(tuple(reversed(shape)))
+
+    for c, (name, pos, neg, box) in enumerate(SAMDEC_CASES):
+        case = ref.PromptCase(case_id=name, multimask=False, pos_points=[list(p) for p in pos],
+                              neg_points=[list(p) for p in neg], box=list(box) if box else [])
+        with tempfile.TemporaryDirectory() as d, torch.no_grad():
+            ref.dump_case(case, pe, dec, no_mem, nchw[0], nchw[1], nchw[2], d)
+            masks = load(d, "sam_dec_masks")[0]                # [4, 288*288]
+            out[f"{name}_sparse"] = load(d, "sam_pe_sparse")[0]  # [n, 256]
+            out[f"{name}_iou"] = load(d, "sam_dec_iou")[0]
+            out[f"{name}_obj_score"] = load(d, "sam_dec_obj_score")[0]
+            out[f"{name}_sam_token"] = load(d, "sam_dec_sam_token")[0]
+            out[f"{name}_mask_tokens"] = load(d, "sam_dec_mask_tokens")[0]
+            out[f"{name}_final_queries"] = load(d, "sam_dec_final_queries")[0]
+            out.update(sample(load(d, "sam_dec_block1_keys")[0], f"{name}_block1_keys", 300 + 10 * c))
+            out.update(sample(load(d, "sam_dec_upscaled")[0], f"{name}_upscaled", 301 + 10 * c))
+            out.update(sample(masks, f"{name}_masks", 302 + 10 * c))
+    meta = {"weights_seed": SAMDEC_SEED, "features_seed": SAMDEC_FEAT_SEED, "feat": 72, "input_size": 1008,
+            "cases": SAMDEC_CASES,
+            "generator": "dump_case() of the reference's tests/dump_phase6_reference.py, imported unmodified"}
+    np.savez_compressed(out_path, meta=json.dumps(meta), **out)
+    print("wrote", out_path)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the sam3.cpp checkout (read-only)")
-    ap.add_argument("--only", choices=["vit", "mem_attn", "window"], default=None)
+    ap.add_argument("--only", choices=["vit", "mem_attn", "window", "sam_dec"], default=None)
     a = ap.parse_args()
     if a.only in (None, "vit"):
         make_vit(a.reference, os.path.join(HERE, "vit_golden.npz"))
@@ -229,6 +316,8 @@ def main():
         make_mem_attn(a.reference, os.path.join(HERE, "mem_attn_golden.npz"))
     if a.only in (None, "window"):
         make_window(a.reference, os.path.join(HERE, "window_golden.npz"))
+    if a.only in (None, "sam_dec"):
+        make_sam_dec(a.reference, os.path.join(HERE, "sam_dec_golden.npz"))
 
 
 if __name__ == "__main__":
