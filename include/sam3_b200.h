@@ -326,6 +326,31 @@ int s3b_sam_dense_pe(s3b_ctx* ctx, int feat, float* out);
  * (first on ties). S3B_ERR_ARG on bad arguments. */
 int s3b_sam_best_mask(const float* iou, int n_masks, int multimask);
 
+/* ---------------------------------------------------------------- memory encoder */
+
+/* Memory encoder of the tracker (sam3_encode_memory, sam3.cpp:11506-11603):
+ * the frame's mask logits [mask_h][mask_w] (the decoder's chosen mask) are
+ * resized to the model input size, mapped through sigmoid * scale + bias
+ * (20 / -10, or the SAM 2 file's values), resized to 16 feat, downsampled
+ * (4 conv stages + 1x1), added to the 1x1 projection of pix_feat
+ * [feat*feat][256] (neck_trk_2), fused by two CXBlocks and projected to the
+ * memory features out [feat*feat][64]. obj_score (one float, may be NULL =
+ * object present): when <= 0, no_obj_embed_spatial is added (11575-11589).
+ * With S3B_MEMENC_DEVICE_PTRS all pointers are device memory (asynchronous on
+ * the context stream, the score is read on the device); otherwise host
+ * memory and the call returns when out is written. The slot's spatial PE is
+ * the 64-channel sine PE (s3b_sine_pe_2d, or NULL slot_pes in
+ * s3b_mem_attn_bank). */
+#define S3B_MEMENC_DEVICE_PTRS 2
+int s3b_mem_encode(s3b_ctx* ctx, int feat, const float* pix_feat, const float* mask_logits, int mask_h, int mask_w,
+                   const float* obj_score, float* out, int flags);
+
+/* Object pointer (sam3_extract_obj_ptr_cpu, sam3.cpp:9344-9418): the 3-layer
+ * ReLU MLP of the SAM output token sam_token [256] (s3b_sam_decode's
+ * mask_tokens[0]), replaced by no_obj_ptr when *obj_score <= 0 (NULL: object
+ * present); out [256]. Pointers as in s3b_mem_encode. */
+int s3b_obj_ptr(s3b_ctx* ctx, const float* sam_token, const float* obj_score, float* out, int flags);
+
 /* Test hook for the engine's failure detection: enqueues on the context
  * stream one kernel that waits on a device barrier with the same bounded
  * wait every GEMM / attention kernel uses, limited to limit_ns (0 < limit_ns

@@ -82,6 +82,8 @@ SYMBOLS = [
     ("s3b_sam_prompt_tokens", _I, [_P, _P, _P, _I, _P, _I, _I, _I, _P, _I]),
     ("s3b_sam_dense_pe", _I, [_P, _I, _P]),
     ("s3b_sam_best_mask", _I, [_P, _I, _I]),
+    ("s3b_mem_encode", _I, [_P, _I, _P, _P, _I, _I, _P, _P, _I]),
+    ("s3b_obj_ptr", _I, [_P, _P, _P, _P, _I]),
     ("s3b_test_wait_timeout", _I, [_P, _I64, _I]),
     ("s3b_select_memory_frames", _I, [_I, _I, ctypes.POINTER(_I), _I]),
     ("s3b_sine_pe_2d", _I, [_I, _I, _I, _P]),
@@ -490,6 +492,44 @@ class Engine:
                                     n_sparse, flags, *[_ptr(o) for o in outs])
         self._check(rc, "s3b_sam_decode")
         return outs
+
+    # -- memory encoder / object pointer
+    def mem_encode(self, feat: int, pix_feat, mask_logits, obj_score=None, out=None):
+        """Memory features [feat*feat, 64]: all numpy (host) or all torch CUDA tensors (device; obj_score a
+        1-element device tensor or None)."""
+        dev = hasattr(pix_feat, "is_cuda") and pix_feat.is_cuda
+        mh, mw = int(mask_logits.shape[-2]), int(mask_logits.shape[-1])
+        if out is None:
+            if dev:
+                import torch
+                out = torch.empty(feat * feat, 64, device=pix_feat.device, dtype=torch.float32)
+            else:
+                out = np.empty((feat * feat, 64), np.float32)
+        if not dev:
+            pix_feat = np.ascontiguousarray(pix_feat, dtype=np.float32)
+            mask_logits = np.ascontiguousarray(mask_logits, dtype=np.float32)
+            if obj_score is not None:
+                obj_score = np.ascontiguousarray(np.asarray(obj_score, np.float32).reshape(1))
+        rc = self._L.s3b_mem_encode(self.h, feat, _ptr(pix_feat), _ptr(mask_logits), mh, mw, _ptr(obj_score),
+                                    _ptr(out), 0 if not dev else 2)
+        self._check(rc, "s3b_mem_encode")
+        return out
+
+    def obj_ptr(self, sam_token, obj_score=None, out=None):
+        dev = hasattr(sam_token, "is_cuda") and sam_token.is_cuda
+        if out is None:
+            if dev:
+                import torch
+                out = torch.empty(256, device=sam_token.device, dtype=torch.float32)
+            else:
+                out = np.empty(256, np.float32)
+        if not dev:
+            sam_token = np.ascontiguousarray(sam_token, dtype=np.float32)
+            if obj_score is not None:
+                obj_score = np.ascontiguousarray(np.asarray(obj_score, np.float32).reshape(1))
+        self._check(self._L.s3b_obj_ptr(self.h, _ptr(sam_token), _ptr(obj_score), _ptr(out), 0 if not dev else 2),
+                    "s3b_obj_ptr")
+        return out
 
     # -- operators on device pointers (torch CUDA tensors)
     def gemm(self, A, B, out, bias=None, act=ACT_NONE, resid=None, K=None):

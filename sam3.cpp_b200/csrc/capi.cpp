@@ -919,6 +919,47 @@ int s3b_sam_dense_pe(s3b_ctx* ctx, int feat, float* out) {
   return s3b_sync(ctx);
 }
 
+int s3b_mem_encode(s3b_ctx* ctx, int feat, const float* pix_feat, const float* mask_logits, int mask_h, int mask_w,
+                   const float* obj_score, float* out, int flags) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  const MemEncoder& E = ctx->model.menc;
+  if (!E.loaded) return set_error(ctx, kErrState, "model has no memory-encoder weights");
+  if (feat <= 0 || feat > 512 || !pix_feat || !mask_logits || mask_h < 2 || mask_w < 2 || !out ||
+      (flags & ~S3B_MEMENC_DEVICE_PTRS))
+    return set_error(ctx, kErrArg, "bad memory-encoder arguments");
+  if (flags & S3B_MEMENC_DEVICE_PTRS) return mem_encode_run(ctx, feat, pix_feat, mask_logits, mask_h, mask_w, obj_score, out);
+  const size_t HH = (size_t)feat * feat;
+  float *dp, *dm, *ds = nullptr;
+  if ((rc = stage_host(ctx, pix_feat, HH * E.D, "me_h_pix", &dp))) return rc;
+  if ((rc = stage_host(ctx, mask_logits, (size_t)mask_h * mask_w, "me_h_mask", &dm))) return rc;
+  if (obj_score && (rc = stage_host(ctx, obj_score, 1, "me_h_score", &ds))) return rc;
+  DevBuf* o = ctx->buf("me_h_out", HH * E.MD * 4, &rc);
+  if (rc) return rc;
+  if ((rc = mem_encode_run(ctx, feat, dp, dm, mask_h, mask_w, ds, o->as<float>()))) return rc;
+  if (cudaMemcpyAsync(out, o->p, HH * E.MD * 4, cudaMemcpyDeviceToHost, ctx->stream) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "device-to-host copy failed");
+  return s3b_sync(ctx);
+}
+
+int s3b_obj_ptr(s3b_ctx* ctx, const float* sam_token, const float* obj_score, float* out, int flags) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  const MemEncoder& E = ctx->model.menc;
+  if (!E.loaded) return set_error(ctx, kErrState, "model has no object-pointer weights");
+  if (!sam_token || !out || (flags & ~S3B_MEMENC_DEVICE_PTRS)) return set_error(ctx, kErrArg, "bad obj_ptr arguments");
+  if (flags & S3B_MEMENC_DEVICE_PTRS) return obj_ptr_run(ctx, sam_token, obj_score, out);
+  float *dt, *ds = nullptr;
+  if ((rc = stage_host(ctx, sam_token, (size_t)E.D, "op_h_tok", &dt))) return rc;
+  if (obj_score && (rc = stage_host(ctx, obj_score, 1, "op_h_score", &ds))) return rc;
+  DevBuf* o = ctx->buf("op_h_out", (size_t)E.D * 4, &rc);
+  if (rc) return rc;
+  if ((rc = obj_ptr_run(ctx, dt, ds, o->as<float>()))) return rc;
+  if (cudaMemcpyAsync(out, o->p, (size_t)E.D * 4, cudaMemcpyDeviceToHost, ctx->stream) != cudaSuccess)
+    return set_error(ctx, kErrCuda, "device-to-host copy failed");
+  return s3b_sync(ctx);
+}
+
 int s3b_sam_best_mask(const float* iou, int n_masks, int multimask) {
   if (!iou || n_masks <= 0) return S3B_ERR_ARG;
   if (!multimask || n_masks < 2) return 0;

@@ -68,6 +68,10 @@ struct HParams {
   int scalp = 1;
   int fpn_top_down_n = 2;
   int fpn_top_down_levels[4] = {2, 3, 0, 0};
+  // SAM 2 tracking fields (sam3.cpp:137-153): sigmoid scale / bias of the memory mask (x100) and the
+  // 15 flags after them in file order
+  int sigmoid_scale_x100 = 2000, sigmoid_bias_x100 = -1000;
+  int trk_flags[15] = {1, 1, 1, 1, 1, 1, 0, 1, 0, 1, 1, 1, 1, 1, 1};
 
   bool is_global(int layer) const {
     for (int i = 0; i < n_global_attn && i < 4; ++i)
@@ -202,6 +206,27 @@ struct SamDecoder {
   int n_special() const { return (has_obj ? 1 : 0) + 1 + n_mask; }
 };
 
+// Memory encoder + object-pointer MLP (sam3.cpp:1968-2056 / 3060-3085).
+struct MemEncoder {
+  bool loaded = false;
+  int D = 256, MD = 64;
+  // mask downsampler: stages 0-2 direct convs (f32 [9][cin][cout] weights), stage 3 a GEMM over the
+  // stride-2 column matrix [256][9*64] in (ky, kx, ci) order; LayerNorm2d of every stage; 1x1 conv ds12
+  Vec ds_w[3], ds_b[3];
+  Linear ds3;
+  Vec ds_nw[4], ds_nb[4];
+  Linear ds12, pix;
+  struct Fuser {
+    Vec dw, dw_b, nw, nb;  // dw f32 [49][256]
+    Linear fc1, fc2;       // fc2 rows and bias scaled by the layer scale gamma at load
+  } fuser[2];
+  Linear out;
+  Vec no_obj_spatial;  // [MD] (may be empty)
+  Linear ptr[3];
+  Vec no_obj_ptr;      // [D]
+  float sig_scale = 20.0f, sig_bias = -10.0f;
+};
+
 struct Model {
   HParams hp;
   bool loaded = false;
@@ -227,6 +252,7 @@ struct Model {
   std::vector<float> maskmem_tpos;   // [num_maskmem][64]
   std::vector<float> obj_ptr_tpos_w, obj_ptr_tpos_b;  // [64][256], [64]
   SamDecoder dec;
+  MemEncoder menc;
   size_t device_bytes = 0;
   // largest N*K of a weight kept in block form; the f16 staging arena of weights_quantised = 1 holds
   // the block-form weights of one ViT / Hiera block or memory-attention layer (stage_arena_elems)
@@ -377,6 +403,13 @@ const float* sam_dec_dense_pe(s3b_ctx* ctx, int H, int* rc);
 // sparse prompt tokens of the image predictor (sam3_segment_pvs, sam3.cpp:10877-10900) on the host
 int sam_prompt_tokens(const SamDecoder& dec, const float* box, const float* pos, int n_pos, const float* neg,
                       int n_neg, float orig_w, float orig_h, int input_size, float* out, int capacity);
+
+// memory encoder (memory_encoder.cpp), device pointers: pix_feat [H*H][256] (neck_trk_2), mask_logits
+// [mask_h][mask_w], obj_score (device float or null: object present) -> out [H*H][64]; obj_ptr: sam_token
+// [256] -> out [256].
+int mem_encode_run(s3b_ctx* ctx, int H, const float* pix_feat, const float* mask_logits, int mask_h, int mask_w,
+                   const float* obj_score, float* out);
+int obj_ptr_run(s3b_ctx* ctx, const float* sam_token, const float* obj_score, float* out);
 
 // encoders
 int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);

@@ -260,6 +260,29 @@ int dec_upscale1(const float* up1, const float* feat_s1, const __half* ws1, cons
 int dec_masks(const __half* u1, const __half* w2, const float* b2, const float* feat_s0, const __half* ws0,
               const float* bs0, const float* hyper, int S, float* masks, cudaStream_t st);
 
+// ---------------------------------------------------------------- memory encoder (mem_enc.cu)
+// sam3_bilinear_interpolate (sam3.cpp:9614-9639) of an f32 [sh][sw] map to [dh][dw] (sw, sh >= 2), bit for
+// bit; sigmoid_mode 1 then maps v -> sigmoid(v) * scale + bias (sam3.cpp:11518-11519).
+int bilinear_resize(const float* src, int sw, int sh, float* dst, int dw, int dh, int sigmoid_mode, float scale,
+                    float bias, cudaStream_t st);
+// One mask-downsampler stage with cin -> cout in {1 -> 4, 4 -> 16, 16 -> 64}: 3x3 / stride 2 / pad 1 conv
+// of channel-last f32 x [Hi][Wi][cin] (inputs rounded to f16) with weights w [9][cin][cout] (f32) + bias,
+// LayerNorm2d (eps) and GELU-tanh -> y [(Hi+1)/2][(Wi+1)/2][cout] f32.
+int mask_ds_conv(const float* x, int Hi, int Wi, int cin, int cout, const float* w, const float* bias, const float* g,
+                 const float* beta, float eps, float* y, cudaStream_t st);
+// Column matrix [(Hi+1)/2 * (Wi+1)/2][9*C] f16 of a 3x3 / stride 2 / pad 1 conv over f32 [Hi][Wi][C].
+int im2col_s2(const float* x, int Hi, int Wi, int C, __half* col, cudaStream_t st);
+// y = f16(GELU-tanh(LayerNorm(x) * g + beta)) over rows of C in {64, 256} channels.
+int ln_gelu_rows(const float* x, long long rows, int C, const float* g, const float* beta, float eps, __half* y,
+                 cudaStream_t st);
+// CXBlock depthwise 7x7 / pad 3 conv of f32 [H][W][256] (w f32 [49][256]) + b, LayerNorm2d -> f16 [H*W][256].
+int dwconv7_ln(const float* x, int H, int W, const float* w, const float* b, const float* g, const float* beta,
+               float eps, __half* y, cudaStream_t st);
+// out[r][c] += emb[c] for all rows when *score <= 0 (device value).
+int add_if_absent(float* out, long long rows, int C, const float* emb, const float* score, cudaStream_t st);
+// out = mlp if score is null or *score > 0, else no_obj (n floats).
+int select_obj_ptr(const float* mlp, const float* no_obj, const float* score, int n, float* out, cudaStream_t st);
+
 // ggml block formats (32 values per block along the row).
 enum QType : int { QT_F32 = 0, QT_F16 = 1, QT_Q4_0 = 2, QT_Q4_1 = 3, QT_Q8_0 = 8 };
 long long qtype_row_bytes(int qtype, long long ne0);

@@ -205,7 +205,9 @@ static int parse_hparams(bool sam2, Next next, HParams& hp, std::string& err) {
     rd(hp.mem_attn_layers);
     rd(hp.num_maskmem);
     rd(hp.max_obj_ptrs);
-    for (int i = 0; i < 2 + 15; ++i) rd(dummy);  // sigmoid scale/bias + tracking flags
+    rd(hp.sigmoid_scale_x100);
+    rd(hp.sigmoid_bias_x100);
+    for (int i = 0; i < 15; ++i) rd(hp.trk_flags[i]);
     if (ok && hp.backbone_type != 1) {
       err = "only the Hiera backbone (backbone_type 1) is supported by the encoder engine";
       return kErrUnsupported;
@@ -788,6 +790,123 @@ static int load_sam_dec(s3b_ctx* ctx, const Index& idx) {
   return kOk;
 }
 
+// Memory encoder + object-pointer MLP weights (optional). The downsampler's narrow stages keep f32
+// copies of their (f16-stored) weights for the direct convolution kernels; the CXBlocks' layer scale
+// gamma is multiplied into pwconv2's rows and bias (gamma (W t + b) = (gamma W) t + gamma b), rounded
+// to f16 once.
+static int load_mem_enc(s3b_ctx* ctx, const Index& idx) {
+  if (!idx.get("mem_enc.ds.0.weight") || !idx.get("obj_ptr_proj.layers.0.weight")) return kOk;
+  MemEncoder& E = ctx->model.menc;
+  E = MemEncoder();
+  const int saved_q = ctx->weights_quantised;
+  ctx->weights_quantised = 0;
+  struct Restore {
+    s3b_ctx* c;
+    int v;
+    ~Restore() { c->weights_quantised = v; }
+  } restore{ctx, saved_q};
+  int rc = 0;
+  auto vec = [&](const std::string& n, Vec& v) -> int {
+    NEED(t, n);
+    v = upload_vec(ctx, *t, &rc);
+    return rc;
+  };
+  const int ch[5] = {1, 4, 16, 64, 256};
+  const int conv_id[4] = {0, 3, 6, 9}, norm_id[4] = {1, 4, 7, 10};
+  for (int s = 0; s < 4; ++s) {
+    const std::string c = "mem_enc.ds." + std::to_string(conv_id[s]), nm = "mem_enc.ds." + std::to_string(norm_id[s]);
+    NEED(w, c + ".weight");
+    NEED(b, c + ".bias");
+    if (w->ne[0] != 3 || w->ne[1] != 3 || w->ne[2] != ch[s] || w->ne[3] != ch[s + 1])
+      return set_error(ctx, kErrFormat, "%s: unexpected shape", c.c_str());
+    if ((rc = vec(nm + ".weight", E.ds_nw[s])) || (rc = vec(nm + ".bias", E.ds_nb[s]))) return rc;
+    if (s < 3) {
+      // ggml [3, 3, cin, cout] -> [ky*3 + kx][ci][co]
+      std::vector<float> f, r((size_t)9 * ch[s] * ch[s + 1]);
+      tensor_to_f32(*w, f);
+      for (int co = 0; co < ch[s + 1]; ++co)
+        for (int ci = 0; ci < ch[s]; ++ci)
+          for (int t = 0; t < 9; ++t)
+            r[((size_t)t * ch[s] + ci) * ch[s + 1] + co] = f[(size_t)t + 9 * (ci + (size_t)ch[s] * co)];
+      E.ds_w[s].n = (int)r.size();
+      E.ds_w[s].d = upload_bytes(ctx, r.data(), r.size() * 4, &rc);
+      if (rc || (rc = vec(c + ".bias", E.ds_b[s]))) return rc;
+    } else if ((rc = upload_conv_cl(ctx, *w, *b, E.ds3))) {
+      return rc;
+    }
+  }
+  {
+    NEED(w, "mem_enc.ds.12.weight");
+    NEED(b, "mem_enc.ds.12.bias");
+    NEED(pw, "mem_enc.pix_feat_proj.weight");
+    NEED(pb, "mem_enc.pix_feat_proj.bias");
+    NEED(ow, "mem_enc.out_proj.weight");
+    NEED(ob, "mem_enc.out_proj.bias");
+    if ((rc = upload_linear(ctx, *w, b, E.ds12, 8, 3)) || (rc = upload_linear(ctx, *pw, pb, E.pix, 8, 3)) ||
+        (rc = upload_linear(ctx, *ow, ob, E.out, 8, 3)))
+      return rc;
+  }
+  for (int i = 0; i < 2; ++i) {
+    const std::string p = "mem_enc.fuser." + std::to_string(i);
+    MemEncoder::Fuser& F = E.fuser[i];
+    NEED(dw, p + ".dwconv.weight");
+    if (dw->ne[0] != 7 || dw->ne[1] != 7 || dw->ne[2] != 1) return set_error(ctx, kErrFormat, "%s.dwconv: shape", p.c_str());
+    {
+      // ggml [7, 7, 1, C] -> [ky*7 + kx][c]
+      const int C = (int)dw->ne[3];
+      std::vector<float> f, r((size_t)49 * C);
+      tensor_to_f32(*dw, f);
+      for (int c = 0; c < C; ++c)
+        for (int t = 0; t < 49; ++t) r[(size_t)t * C + c] = f[(size_t)c * 49 + t];
+      F.dw.n = (int)r.size();
+      F.dw.d = upload_bytes(ctx, r.data(), r.size() * 4, &rc);
+      if (rc) return rc;
+    }
+    if ((rc = vec(p + ".dwconv.bias", F.dw_b)) || (rc = vec(p + ".norm.weight", F.nw)) ||
+        (rc = vec(p + ".norm.bias", F.nb)))
+      return rc;
+    NEED(w1, p + ".pwconv1.weight");
+    NEED(b1, p + ".pwconv1.bias");
+    if ((rc = upload_linear(ctx, *w1, b1, F.fc1))) return rc;
+    NEED(w2, p + ".pwconv2.weight");
+    NEED(b2, p + ".pwconv2.bias");
+    NEED(gm, p + ".gamma");
+    std::vector<float> w, b, g;
+    tensor_to_f32(*w2, w);
+    tensor_to_f32(*b2, b);
+    tensor_to_f32(*gm, g);
+    const int K = (int)w2->ne[0], N = (int)(w.size() / K);
+    if ((int)g.size() != N || (int)b.size() != N) return set_error(ctx, kErrFormat, "%s: gamma / bias size", p.c_str());
+    for (int n = 0; n < N; ++n) {
+      for (int k = 0; k < K; ++k) w[(size_t)n * K + k] *= g[n];
+      b[n] *= g[n];
+    }
+    if ((rc = upload_b_operand(ctx, w, N, K, 8, F.fc2))) return rc;
+    F.fc2.b = upload_bytes(ctx, b.data(), b.size() * 4, &rc);
+    if (rc) return rc;
+  }
+  for (int j = 0; j < 3; ++j) {
+    const std::string p = "obj_ptr_proj.layers." + std::to_string(j);
+    NEED(w, p + ".weight");
+    NEED(b, p + ".bias");
+    if ((rc = upload_linear(ctx, *w, b, E.ptr[j]))) return rc;
+  }
+  if ((rc = vec("no_obj_ptr", E.no_obj_ptr))) return rc;
+  if (idx.get("no_obj_embed_spatial") && (rc = vec("no_obj_embed_spatial", E.no_obj_spatial))) return rc;
+  E.D = E.pix.N;
+  E.MD = E.out.N;
+  const HParams& hp = ctx->model.hp;
+  if (hp.is_sam2) {
+    E.sig_scale = hp.sigmoid_scale_x100 / 100.0f;
+    E.sig_bias = hp.sigmoid_bias_x100 / 100.0f;
+  }
+  if (E.D != 256 || E.ds3.N != 256 || E.ds3.K != 9 * 64 || E.ds12.K != 256 || E.fuser[0].fc1.K != 256 ||
+      E.no_obj_ptr.n != E.D || (E.no_obj_spatial.n && E.no_obj_spatial.n != E.MD))
+    return set_error(ctx, kErrFormat, "memory encoder: unsupported shapes");
+  E.loaded = true;
+  return kOk;
+}
+
 static int load_sam3(s3b_ctx* ctx, const Index& idx) {
   Model& M = ctx->model;
   const HParams& hp = M.hp;
@@ -862,7 +981,7 @@ static int load_sam3(s3b_ctx* ctx, const Index& idx) {
     if ((rc = load_neck(ctx, idx, "neck.det.", M.neck_det))) return rc;
     M.has_neck_det = true;
   }
-  if ((rc = load_mem_attn(ctx, idx))) return rc;
+  if ((rc = load_mem_attn(ctx, idx)) || (rc = load_mem_enc(ctx, idx))) return rc;
   return load_sam_dec(ctx, idx);
 }
 
@@ -1003,7 +1122,7 @@ static int load_sam2(s3b_ctx* ctx, const Index& idx) {
     NEED(b, p + ".bias");
     if ((rc = upload_linear(ctx, *w, b, M.fpn[i], 8, 3))) return rc;
   }
-  if ((rc = load_mem_attn(ctx, idx))) return rc;
+  if ((rc = load_mem_attn(ctx, idx)) || (rc = load_mem_enc(ctx, idx))) return rc;
   return load_sam_dec(ctx, idx);
 }
 

@@ -300,6 +300,47 @@ def _sam_dec(g: _Gen, T: dict, D: int, ffn: int = 2048, n_mask: int = 4, depth: 
     T["no_mem_embed"] = g.w(1, 1, D)
 
 
+def _mem_enc(g: _Gen, T: dict, D: int = 256, MD: int = 64, ffn: int = 1024):
+    """Memory encoder (mask downsampler, pixel projection, 2 CXBlock fusers, out projection), object-
+    pointer MLP and the no-object embeddings, in .ggml naming (convert_sam3_to_ggml.py:158-187; shapes as
+    registered at sam3.cpp:1968-2056). gamma is the CXBlocks' layer scale (PyTorch init 1e-6; drawn
+    around 0.5 here so the fusers matter)."""
+    ch = [1, 4, 16, 64, D]
+    for s, (ci, ni) in enumerate(((0, 1), (3, 4), (6, 7), (9, 10))):
+        T[f"mem_enc.ds.{ci}.weight"] = g.w(ch[s + 1], ch[s], 3, 3, std=0.3)
+        T[f"mem_enc.ds.{ci}.bias"] = g.w(ch[s + 1])
+        T[f"mem_enc.ds.{ni}.weight"], T[f"mem_enc.ds.{ni}.bias"] = g.ln(ch[s + 1])
+    T["mem_enc.ds.12.weight"] = g.w(D, D, 1, 1, std=0.05)
+    T["mem_enc.ds.12.bias"] = g.w(D)
+    T["mem_enc.pix_feat_proj.weight"] = g.w(D, D, 1, 1, std=0.05)
+    T["mem_enc.pix_feat_proj.bias"] = g.w(D)
+    for i in range(2):
+        p = f"mem_enc.fuser.{i}"
+        T[p + ".dwconv.weight"] = g.w(D, 1, 7, 7, std=0.1)
+        T[p + ".dwconv.bias"] = g.w(D)
+        T[p + ".norm.weight"], T[p + ".norm.bias"] = g.ln(D)
+        T[p + ".pwconv1.weight"] = g.w(ffn, D, std=0.05)
+        T[p + ".pwconv1.bias"] = g.w(ffn)
+        T[p + ".pwconv2.weight"] = g.w(D, ffn, std=0.05)
+        T[p + ".pwconv2.bias"] = g.w(D)
+        T[p + ".gamma"] = (0.5 + g.w(D, std=0.1)).astype(np.float32)
+    T["mem_enc.out_proj.weight"] = g.w(MD, D, 1, 1, std=0.05)
+    T["mem_enc.out_proj.bias"] = g.w(MD)
+    for j in range(3):
+        T[f"obj_ptr_proj.layers.{j}.weight"] = g.w(D, D, std=0.05)
+        T[f"obj_ptr_proj.layers.{j}.bias"] = g.w(D)
+    T["no_obj_ptr"] = g.w(1, D, std=1.0)
+    T["no_obj_embed_spatial"] = g.w(1, MD, std=1.0)
+
+
+def mem_enc_tensors(seed: int, D: int = 256, MD: int = 64, ln_random: bool = True) -> dict:
+    """The memory-encoder + object-pointer tensors alone (the names and shapes _mem_enc writes)."""
+    g = _Gen(seed, ln_random)
+    T: dict[str, np.ndarray] = {}
+    _mem_enc(g, T, D, MD)
+    return T
+
+
 def sam_dec_tensors(seed: int, D: int = 256, ln_random: bool = True) -> dict:
     """The SAM prompt encoder + mask decoder tensors alone (the names and shapes _sam_dec writes)."""
     g = _Gen(seed, ln_random)

@@ -22,6 +22,10 @@ Run in a container that has the reference checkout (read-only) and torch:
    tests/dump_phase6_reference.py (SAM prompt encoder + SAM mask decoder) on
    seeded synthetic decoder weights, seeded neck_trk_0..2 feature maps at the
    SAM 3 size (72^2 image tokens) and three prompt cases of our own.
+5. mem_enc_golden.npz — run_memory_encoder() and run_obj_ptr() imported
+   from the reference's tests/dump_phase7_reference.py on seeded synthetic
+   memory-encoder weights, a seeded neck_trk_2 map and seeded 288^2 mask
+   logits (object present and absent).
 
 Each dumped tensor is stored as deterministic samples (indices + values)
 plus summary statistics, so the fixtures stay small; tests regenerate the
@@ -305,10 +309,70 @@ def make_sam_dec(reference: str, out_path: str):
     print("wrote", out_path)
 
 
+MEMENC_SEED = 61
+MEMENC_FEAT_SEED = 62
+
+
+def mem_enc_weights():
+    load_pkg()
+    from sam3_b200 import synth
+    return synth.stored_values(synth.mem_enc_tensors(MEMENC_SEED), 1, None)
+
+
+def mem_enc_inputs(H=72, seed=MEMENC_FEAT_SEED):
+    """neck_trk_2 stand-in [H, H, 256], mask logits [4H, 4H] (a smooth blob plus noise), SAM token [256]."""
+    rng = np.random.default_rng(seed)
+    pix = rng.standard_normal((H, H, 256), dtype=np.float32)
+    S = 4 * H
+    yy, xx = np.mgrid[0:S, 0:S].astype(np.float32) / np.float32(S)
+    logits = (8.0 * np.exp(-((xx - 0.45) ** 2 + (yy - 0.55) ** 2) / 0.03) - 4.0).astype(np.float32)
+    logits += rng.standard_normal((S, S), dtype=np.float32) * np.float32(0.5)
+    token = rng.standard_normal(256, dtype=np.float32)
+    return pix, logits, token
+
+
+def mem_enc_torch_names(W: dict):
+    import torch
+    sd = {}
+    for k, v in W.items():
+        n = k.replace("mem_enc.ds.", "maskmem_backbone.mask_downsampler.encoder.")
+        n = n.replace("mem_enc.fuser.", "maskmem_backbone.fuser.layers.").replace("mem_enc.", "maskmem_backbone.")
+        sd[n] = torch.from_numpy(np.ascontiguousarray(v))
+    sd["no_obj_ptr"] = sd["no_obj_ptr"].reshape(-1)
+    return sd
+
+
+def make_mem_enc(reference: str, out_path: str):
+    import torch
+    spec = importlib.util.spec_from_file_location("dump_phase7_reference",
+                                                  os.path.join(reference, "tests", "dump_phase7_reference.py"))
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    W = mem_enc_weights()
+    sd = mem_enc_torch_names(W)
+    pix, logits, token = mem_enc_inputs()
+    out = {}
+    with torch.no_grad():
+        pix_t = torch.from_numpy(np.ascontiguousarray(pix.transpose(2, 0, 1)))[None]
+        m_t = torch.from_numpy(logits)[None, None]
+        for c, score in enumerate((2.5, -1.5)):
+            r = ref.run_memory_encoder(sd, pix_t, m_t, torch.tensor([[score]]))
+            name = "present" if score > 0 else "absent"
+            for i, key in enumerate(("mask_downsampled", "fuser0", "fuser1", "output")):
+                a = r[key][0].permute(1, 2, 0).numpy()  # channel-last
+                out.update(sample(a, f"{name}_{key}", 400 + 10 * c + i))
+            out[f"{name}_obj_ptr"] = ref.run_obj_ptr(sd, torch.from_numpy(token)[None], torch.tensor([[score]]))[0].numpy()
+    meta = {"weights_seed": MEMENC_SEED, "inputs_seed": MEMENC_FEAT_SEED, "feat": 72, "img_size": 1008,
+            "scores": [2.5, -1.5], "gelu": "erf (the Python reference's F.gelu)",
+            "generator": "run_memory_encoder() / run_obj_ptr() of the reference's tests/dump_phase7_reference.py"}
+    np.savez_compressed(out_path, meta=json.dumps(meta), **out)
+    print("wrote", out_path)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the sam3.cpp checkout (read-only)")
-    ap.add_argument("--only", choices=["vit", "mem_attn", "window", "sam_dec"], default=None)
+    ap.add_argument("--only", choices=["vit", "mem_attn", "window", "sam_dec", "mem_enc"], default=None)
     a = ap.parse_args()
     if a.only in (None, "vit"):
         make_vit(a.reference, os.path.join(HERE, "vit_golden.npz"))
@@ -318,6 +382,8 @@ def main():
         make_window(a.reference, os.path.join(HERE, "window_golden.npz"))
     if a.only in (None, "sam_dec"):
         make_sam_dec(a.reference, os.path.join(HERE, "sam_dec_golden.npz"))
+    if a.only in (None, "mem_enc"):
+        make_mem_enc(a.reference, os.path.join(HERE, "mem_enc_golden.npz"))
 
 
 if __name__ == "__main__":
