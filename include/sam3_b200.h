@@ -351,6 +351,28 @@ int s3b_mem_encode(s3b_ctx* ctx, int feat, const float* pix_feat, const float* m
  * present); out [256]. Pointers as in s3b_mem_encode. */
 int s3b_obj_ptr(s3b_ctx* ctx, const float* sam_token, const float* obj_score, float* out, int flags);
 
+/* ---------------------------------------------------------------- tracking step */
+
+/* One tracking step of one object on a frame the encoder has processed, as
+ * sam3_propagate_frame runs it per object (sam3.cpp:12128-12203):
+ * sam3_propagate_single (11171-11453: memory attention on neck_trk_2 with the
+ * prompt built from the object's memory bank, the SAM mask decoder on its
+ * output with neck_trk_0 / 1 and the single not_a_point token, the mask kept
+ * by IoU: token 0 for SAM 3, the best of tokens 1-3 for SAM 2 with multimask
+ * output), then sam3_encode_memory of the kept mask (11506-11603) and
+ * sam3_extract_obj_ptr_cpu of its SAM token (9344-9418). The bank arguments
+ * are those of s3b_mem_attn_bank. Every array is device memory and the step
+ * is asynchronous on the context stream; outputs (each may be NULL):
+ *   mask_logits [(4 feat)^2] the kept mask; scores [3] = {its IoU, the object
+ *   score logit, its token index}; mem_feats [feat*feat][64] the frame's
+ *   memory features (its spatial PE is the 64-channel sine PE); obj_ptr [256].
+ * The caller keeps the tracker's bookkeeping: it appends mem_feats / obj_ptr
+ * to the bank and thresholds the mask at the original resolution. */
+int s3b_track_step(s3b_ctx* ctx, int feat, const float* neck_trk_0, const float* neck_trk_1, const float* neck_trk_2,
+                   const float* const* slot_feats, const float* const* slot_pes, const int* slot_tpos, int n_slots,
+                   const float* obj_ptrs, const int* ptr_tpos, int n_ptrs, float* mask_logits, float* scores,
+                   float* mem_feats, float* obj_ptr);
+
 /* Test hook for the engine's failure detection: enqueues on the context
  * stream one kernel that waits on a device barrier with the same bounded
  * wait every GEMM / attention kernel uses, limited to limit_ns (0 < limit_ns

@@ -84,6 +84,7 @@ SYMBOLS = [
     ("s3b_sam_best_mask", _I, [_P, _I, _I]),
     ("s3b_mem_encode", _I, [_P, _I, _P, _P, _I, _I, _P, _P, _I]),
     ("s3b_obj_ptr", _I, [_P, _P, _P, _P, _I]),
+    ("s3b_track_step", _I, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _P, _P, _P, _P]),
     ("s3b_test_wait_timeout", _I, [_P, _I64, _I]),
     ("s3b_select_memory_frames", _I, [_I, _I, ctypes.POINTER(_I), _I]),
     ("s3b_sine_pe_2d", _I, [_I, _I, _I, _P]),
@@ -530,6 +531,22 @@ class Engine:
         self._check(self._L.s3b_obj_ptr(self.h, _ptr(sam_token), _ptr(obj_score), _ptr(out), 0 if not dev else 2),
                     "s3b_obj_ptr")
         return out
+
+    def track_step(self, feat: int, trk0, trk1, trk2, slot_feats, slot_tpos, obj_ptrs=None, ptr_tpos=(),
+                   slot_pes=None, want=("mask", "scores", "mem", "ptr")):
+        """One tracking step (s3b_track_step) on torch CUDA tensors; returns a dict of the outputs asked for."""
+        import torch
+        dev = trk2.device
+        outs = {"mask": torch.empty(16 * feat * feat, device=dev) if "mask" in want else None,
+                "scores": torch.empty(3, device=dev) if "scores" in want else None,
+                "mem": torch.empty(feat * feat, 64, device=dev) if "mem" in want else None,
+                "ptr": torch.empty(256, device=dev) if "ptr" in want else None}
+        n_slots, feats, pes, tpos, n_ptrs, ptpos = self._bank_args(slot_feats, slot_pes, slot_tpos, obj_ptrs, ptr_tpos)
+        rc = self._L.s3b_track_step(self.h, feat, _ptr(trk0), _ptr(trk1), _ptr(trk2), feats, pes, tpos, n_slots,
+                                    _ptr(obj_ptrs), ptpos, n_ptrs, _ptr(outs["mask"]), _ptr(outs["scores"]),
+                                    _ptr(outs["mem"]), _ptr(outs["ptr"]))
+        self._check(rc, "s3b_track_step")
+        return {k: v for k, v in outs.items() if v is not None}
 
     # -- operators on device pointers (torch CUDA tensors)
     def gemm(self, A, B, out, bias=None, act=ACT_NONE, resid=None, K=None):

@@ -273,6 +273,8 @@ int encode_device_image_u8(s3b_ctx* ctx, const uint8_t* d_u8, int n_frames, int 
 
 namespace s3b {
 
+const float* sine_pe_device(s3b_ctx* ctx, int S, int d, int* rc) { return device_sine_pe(ctx, S, d, rc); }
+
 int outputs_pass_begin(s3b_ctx* ctx, int pass, int fb) {
   if (ctx->copy_done.empty()) return kOk;
   if (fb != ctx->copy_fb) {
@@ -958,6 +960,20 @@ int s3b_obj_ptr(s3b_ctx* ctx, const float* sam_token, const float* obj_score, fl
   if (cudaMemcpyAsync(out, o->p, (size_t)E.D * 4, cudaMemcpyDeviceToHost, ctx->stream) != cudaSuccess)
     return set_error(ctx, kErrCuda, "device-to-host copy failed");
   return s3b_sync(ctx);
+}
+
+int s3b_track_step(s3b_ctx* ctx, int feat, const float* neck_trk_0, const float* neck_trk_1, const float* neck_trk_2,
+                   const float* const* slot_feats, const float* const* slot_pes, const int* slot_tpos, int n_slots,
+                   const float* obj_ptrs, const int* ptr_tpos, int n_ptrs, float* mask_logits, float* scores,
+                   float* mem_feats, float* obj_ptr) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (feat <= 0 || feat > 512 || !neck_trk_0 || !neck_trk_1 || !neck_trk_2)
+    return set_error(ctx, kErrArg, "bad tracking-step arguments");
+  PromptArgs pa;
+  if ((rc = prompt_args(ctx, feat, slot_feats, slot_pes, slot_tpos, n_slots, obj_ptrs, ptr_tpos, n_ptrs, pa)))
+    return rc;
+  return track_step_run(ctx, feat, neck_trk_0, neck_trk_1, neck_trk_2, pa, mask_logits, scores, mem_feats, obj_ptr);
 }
 
 int s3b_sam_best_mask(const float* iou, int n_masks, int multimask) {

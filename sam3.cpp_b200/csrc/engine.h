@@ -411,6 +411,13 @@ int mem_encode_run(s3b_ctx* ctx, int H, const float* pix_feat, const float* mask
                    const float* obj_score, float* out);
 int obj_ptr_run(s3b_ctx* ctx, const float* sam_token, const float* obj_score, float* out);
 
+// sinusoidal PE [S][S][d] on the device, computed once per size (sam3_sinusoidal_pe_2d)
+const float* sine_pe_device(s3b_ctx* ctx, int S, int d, int* rc);
+// One tracking step of one object (tracker.cpp): memory attention from the bank, the mask decoder on its
+// output, the kept mask, the memory encoder and the object pointer, all on the context stream.
+int track_step_run(s3b_ctx* ctx, int H, const float* trk0, const float* trk1, const float* trk2, const PromptArgs& pa,
+                   float* mask_out, float* scores_out, float* mem_out, float* ptr_out);
+
 // encoders
 int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);
 int hiera_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);

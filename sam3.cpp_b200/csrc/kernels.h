@@ -260,6 +260,13 @@ int dec_upscale1(const float* up1, const float* feat_s1, const __half* ws1, cons
 int dec_masks(const __half* u1, const __half* w2, const float* b2, const float* feat_s0, const __half* ws0,
               const float* bs0, const float* hyper, int S, float* masks, cudaStream_t st);
 
+// The mask a tracking step keeps: masks [n_masks][plane], iou [n_masks], tokens [n_masks][256] (device).
+// Index 0, or with multimask the best IoU among 1 .. n-1; out_mask = that plane, out_token = that token
+// (use_mm_token) or token 0, out_scores = {iou, *obj, index}. Outputs may be null.
+int pick_mask(const float* masks, long long plane, const float* iou, const float* tokens, int n_masks, int multimask,
+              int use_mm_token, float* out_mask, float* out_token, float* out_scores, const float* obj,
+              cudaStream_t st);
+
 // ---------------------------------------------------------------- memory encoder (mem_enc.cu)
 // sam3_bilinear_interpolate (sam3.cpp:9614-9639) of an f32 [sh][sw] map to [dh][dw] (sw, sh >= 2), bit for
 // bit; sigmoid_mode 1 then maps v -> sigmoid(v) * scale + bias (sam3.cpp:11518-11519).

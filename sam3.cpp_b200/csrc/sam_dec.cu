@@ -606,9 +606,50 @@ __global__ void __launch_bounds__(256) dec_masks_kernel(const __half* u1, const 
   }
 }
 
+// The mask a tracking step keeps (sam3_propagate_single, sam3.cpp:11395-11430): token 0 without multimask
+// output, else the best IoU among tokens 1 .. n-1 (first on ties); the object pointer's token is the
+// chosen one when use_mm_token, else token 0. One CTA: thread 0 decides, all threads copy the mask.
+__global__ void __launch_bounds__(256) pick_mask_kernel(const float* masks, long long plane, const float* iou,
+                                                        const float* tokens, int n_masks, int multimask,
+                                                        int use_mm_token, float* out_mask, float* out_token,
+                                                        float* out_scores, const float* obj) {
+  __shared__ int best_s;
+  if (threadIdx.x == 0) {
+    int best = 0;
+    if (multimask && n_masks > 1) {
+      best = 1;
+      for (int m = 2; m < n_masks; ++m)
+        if (iou[m] > iou[best]) best = m;
+    }
+    best_s = best;
+    if (out_scores) {
+      out_scores[0] = iou[best];
+      out_scores[1] = obj ? *obj : 0.f;
+      out_scores[2] = (float)best;
+    }
+  }
+  __syncthreads();
+  const int best = best_s;
+  if (out_mask)
+    for (long long i = threadIdx.x; i < plane; i += blockDim.x) out_mask[i] = masks[best * plane + i];
+  if (out_token) {
+    const int t = use_mm_token ? best : 0;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) out_token[i] = tokens[t * 256 + i];
+  }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- launchers
+int pick_mask(const float* masks, long long plane, const float* iou, const float* tokens, int n_masks, int multimask,
+              int use_mm_token, float* out_mask, float* out_token, float* out_scores, const float* obj,
+              cudaStream_t st) {
+  if (!masks || !iou || !tokens || n_masks <= 0 || plane <= 0) return -2;
+  pick_mask_kernel<<<1, 256, 0, st>>>(masks, plane, iou, tokens, n_masks, multimask, use_mm_token, out_mask, out_token,
+                                      out_scores, obj);
+  return dec_launch_ok();
+}
+
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int tok_linear(const TokJob* jobs, int n_jobs, cudaStream_t st) {
