@@ -11,9 +11,11 @@ The same line carries the other configurations:
   vit_f16_b1       configs[2]: SAM 3 ViT-L f16, batch 1 (latency)
   hiera_t_f16_b1   configs[0]: SAM 2.1 Hiera-T f16, batch 1 (latency)
   hiera_t_q4_0     configs[1]: SAM 2.1 Hiera-T q4_0, 16 frames per GPU
-  video_hiera_l_q8_0  configs[4]: Hiera-L q8_0 on 64 frames over the GPUs, each frame's neck_trk_2 moved to
-                   the tracking GPU (rank 0) over NVLink (CUDA IPC + peer copy), memory attention per frame
-                   there from a device-resident memory bank; the end-to-end pipeline rate and its limiter.
+  video_hiera_l_q8_0  configs[4]: Hiera-L q8_0 on 64 frames over the GPUs, each frame's neck_trk_0/1/2 moved
+                   to the tracking GPU (rank 0) over NVLink (CUDA IPC + peer copy), one tracking step per
+                   frame there (memory attention from a device-resident memory bank, SAM mask decoder,
+                   memory encoder, object pointer: s3b_track_step); the end-to-end pipeline rate and its
+                   limiter.
 
   python bench.py [--gpus N] [--steps K] [--warmup W]
   python bench.py --impl reference ...   # the CPU restatement (oracle) of the same path, timed
@@ -105,7 +107,7 @@ def model_file(s3b, kind: str) -> str:
     """Seeded synthetic .ggml files of the configurations (written once per box under the temp dir)."""
     import dataclasses
     from sam3_b200 import synth
-    path = os.path.join(tempfile.gettempdir(), f"s3b_bench_{kind}.ggml")
+    path = os.path.join(tempfile.gettempdir(), f"s3b_bench_{kind}_v2.ggml")
     if os.path.exists(path):
         return path
     tmp = path + f".tmp{os.getpid()}"
@@ -116,8 +118,12 @@ def model_file(s3b, kind: str) -> str:
         synth.write_sam2(tmp, synth.HIERA_T, seed=0, ftype=1, qtype=2 if kind == "hiera_t_q4_0" else None,
                          quantize=s3b.quantize_rows)
     elif kind == "hiera_l_q8_0":
-        synth.write_sam2(tmp, dataclasses.replace(synth.HIERA_L, with_mem_attn=True), seed=0, ftype=1, qtype=8,
-                         quantize=s3b.quantize_rows)
+        # the video configuration carries the tracker: memory attention, SAM mask decoder, memory encoder
+        from sam3_b200 import ggml_io
+        cfg = dataclasses.replace(synth.HIERA_L, with_mem_attn=True, with_sam_dec=True)
+        T = synth.sam2_tensors(cfg, seed=0)
+        T.update(synth.mem_enc_tensors(1))
+        synth.write_model(tmp, T, cfg.hparams(), ggml_io.MAGIC_SAM2, 1, 1, 8, s3b.quantize_rows)
     else:
         raise ValueError(kind)
     os.replace(tmp, path)
@@ -475,133 +481,169 @@ def bench_video(s3b, path, args, rank, world, local, stream) -> dict:
     out.update({"encoder_frames_per_s": FRAMES_TOTAL / (ms / 1000.0), "encoder_ms_per_step": ms,
                 "encoder_gemm_tflops": tflops(prof["gemm"]), "encoder_attention_tflops": tflops(prof["attention"])})
 
-    # --- memory bank on the tracking GPU (random, seeded): 7 slots [4096][64], 16 pointers [256]
+    # --- the tracker's per-frame work on the tracking GPU (rank 0), from a device memory bank (seeded):
+    # 7 slots [4096][64] (slot 0 the conditioning frame), 16 object pointers [256]
     feat, n_slots, n_ptrs = 64, cfg.num_maskmem, cfg.max_obj_ptrs
-    fbytes = feat * feat * 256 * 4
-    slot_tpos = [n_slots - s for s in range(n_slots)]  # n_sel - s, no conditioning frame
+    levels = [("neck_trk_0", 4 * feat), ("neck_trk_1", 2 * feat), ("neck_trk_2", feat)]
+    lbytes = [s * s * 256 * 4 for _, s in levels]
+    fbytes = sum(lbytes)  # the three feature maps a tracking step reads
+    slot_tpos = [0] + [n_slots - s for s in range(1, n_slots)]
     ptr_tpos = list(range(1, n_ptrs + 1))
+
+    def timed(fn, n):
+        for _ in range(max(args.warmup, 2)):
+            fn()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
     if rank == 0:
         g2 = torch.Generator(device="cuda").manual_seed(5)
         bank = [torch.randn(feat * feat, 64, device="cuda", generator=g2) for _ in range(n_slots)]
         ptrs = torch.randn(n_ptrs, 256, device="cuda", generator=g2)
-        curr0 = torch.from_numpy(eng.output("neck_trk_2", 0).reshape(-1, 256)).cuda()
-        res = torch.empty_like(curr0)
-        for _ in range(max(args.warmup, 2)):
-            eng.mem_attn_bank(curr0, feat, bank, slot_tpos, ptrs, ptr_tpos, out=res)
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(args.steps):
-            eng.mem_attn_bank(curr0, feat, bank, slot_tpos, ptrs, ptr_tpos, out=res)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        mms = e0.elapsed_time(e1) / args.steps
+        lv = [torch.from_numpy(eng.output(name, 0).reshape(-1, 256)).cuda() for name, _ in levels]
+        res = torch.empty_like(lv[2])
+        touts = {"mask": torch.empty(16 * feat * feat, device="cuda"), "scores": torch.empty(3, device="cuda"),
+                 "mem": torch.empty(feat * feat, 64, device="cuda"), "ptr": torch.empty(256, device="cuda")}
+        dec_outs = (torch.empty(4, 4 * feat, 4 * feat, device="cuda"), torch.empty(4, device="cuda"),
+                    torch.empty(1, device="cuda"), torch.empty(4, 256, device="cuda"))
+        mms = timed(lambda: eng.mem_attn_bank(lv[2], feat, bank, slot_tpos, ptrs, ptr_tpos, out=res), args.steps)
+        dms = timed(lambda: eng.sam_decode(feat, res, lv[0], lv[1], None, outs=dec_outs), args.steps)
+        ems = timed(lambda: eng.mem_encode(feat, lv[2], dec_outs[0][0], dec_outs[2], out=touts["mem"]), args.steps)
+        tms = timed(lambda: eng.track_step(feat, lv[0], lv[1], lv[2], bank, slot_tpos, ptrs, ptr_tpos, outs=touts),
+                    args.steps)
         eng.profile_begin(True)
-        eng.mem_attn_bank(curr0, feat, bank, slot_tpos, ptrs, ptr_tpos, out=res)
+        eng.mem_attn_bank(lv[2], feat, bank, slot_tpos, ptrs, ptr_tpos, out=res)
         torch.cuda.synchronize()
         p2 = eng.profile_end()
         fl = p2["gemm"]["flops"] + p2["attention"]["flops"]
+        eng.profile_begin(False)
+        eng.track_step(feat, lv[0], lv[1], lv[2], bank, slot_tpos, ptrs, ptr_tpos, outs=touts)
+        torch.cuda.synchronize()
+        p3 = eng.profile_end()
         out.update({"mem_attn_ms_per_frame": mms, "mem_attn_tflop_per_frame": fl / 1e12,
                     "mem_attn_tflops": fl / (mms / 1000.0) / 1e12, "mem_attn_attention_tflops": tflops(p2["attention"]),
                     "mem_attn_memory_tokens": n_slots * feat * feat + 4 * n_ptrs,
-                    "mem_attn_timing": "CUDA events around the timed calls (s3b_mem_attn_bank: prompt built on the "
-                                       "device from the bank, layers replayed from a CUDA graph)"})
+                    "mask_decoder_ms_per_frame": dms, "memory_encoder_ms_per_frame": ems,
+                    "track_step_ms_per_frame": tms, "track_step_launches": p3["launches"],
+                    "track_timing": "CUDA events around the timed calls; s3b_mem_attn_bank (prompt built on the "
+                                    "device from the bank, layers replayed from a CUDA graph), s3b_sam_decode, "
+                                    "s3b_mem_encode, and s3b_track_step = all of them + the mask choice + the "
+                                    "object pointer"})
 
-    # --- the pipeline
+    # --- the pipeline: encode, hand the three feature maps to the tracking GPU, one tracking step per frame
     encoders = list(range(1, world)) if world > 1 else [0]
     e_idx = encoders.index(rank) if rank in encoders else -1
     efirst, enf = shard_frames(FRAMES_TOTAL, e_idx, len(encoders)) if e_idx >= 0 else (0, 0)
     if enf:
         eframes = torch.from_numpy(synth.frames_u8(enf, 1024, base_seed=1000 + efirst)).cuda()
     recv = None
-    if rank == 0:
+    if rank == 0 and world > 1:
         recv = eng.device_alloc(2 * FRAMES_TOTAL * fbytes)
-        handle = [eng.ipc_export(recv)] if world > 1 else [None]
+        handle = [eng.ipc_export(recv)]
     else:
         handle = [None]
     if world > 1:
         dist.broadcast_object_list(handle, src=0)
-    dst_base = recv if rank == 0 else eng.ipc_open(handle[0])
+    dst_base = None if world == 1 else (recv if rank == 0 else eng.ipc_open(handle[0]))
+
+    def frame_slot(base, f):
+        return [base + f * fbytes + sum(lbytes[:i]) for i in range(3)]
 
     def encode_step(k):
         if not enf:
             return
         eng.encode_u8(eframes)
+        if world == 1:
+            return
         buf = dst_base + (k % 2) * FRAMES_TOTAL * fbytes
         for f in range(enf):
-            eng.peer_copy_output("neck_trk_2", f, buf + (efirst + f) * fbytes, 0, fbytes)
+            for (name, _), dst, nb in zip(levels, frame_slot(buf, efirst + f), lbytes):
+                eng.peer_copy_output(name, f, dst, 0, nb)
 
-    def track_step(k):
-        buf = recv + (k % 2) * FRAMES_TOTAL * fbytes
+    def track_frames(k):
         for f in range(FRAMES_TOTAL):
-            curr = torch.as_tensor(_CudaArray(buf + f * fbytes, feat * feat * 256), device="cuda").view(-1, 256)
-            eng.mem_attn_bank(curr, feat, bank, slot_tpos, ptrs, ptr_tpos, out=res)
+            if world == 1:
+                t = [eng.output_device_ptr(name, f) for name, _ in levels]
+            else:
+                t = frame_slot(recv + (k % 2) * FRAMES_TOTAL * fbytes, f)
+            # the step's memory and pointer go back into the bank rings (slot 0 stays the conditioning frame)
+            touts["mem"] = bank[1 + f % (n_slots - 1)]
+            touts["ptr"] = ptrs[f % n_ptrs]
+            eng.track_step(feat, t[0], t[1], t[2], bank, slot_tpos, ptrs, ptr_tpos, outs=touts)
 
-    def pipeline_step(k, last_k):
+    def pipeline_step(k):
         if world == 1:
             encode_step(k)
-            track_step(k)
+            track_frames(k)
         else:
-            if k <= last_k:
-                encode_step(k)
+            encode_step(k)
             if rank == 0 and k > 0:
-                track_step(k - 1)
+                track_frames(k - 1)
         eng.sync()
         barrier(world)
 
     n_warm = max(args.warmup, 2)
     for k in range(n_warm):
-        pipeline_step(k, 10 ** 9)
+        pipeline_step(k)
     barrier(world)
     torch.cuda.synchronize()
     e0.record(stream)
     steps = args.steps
     for k in range(n_warm, n_warm + steps):
-        pipeline_step(k, 10 ** 9)
+        pipeline_step(k)
     e1.record(stream)
     torch.cuda.synchronize()
     pms = max_over_ranks(e0.elapsed_time(e1) / steps, world, "cuda")
-    # content check: the frames rank 0 tracked in the last step came from the encoders' last outputs
-    last = n_warm + steps - 1  # buffer last % 2 holds the frames encoded in step `last`
-    sums = []
-    if enf:
-        for f in range(enf):
-            p = eng.output_device_ptr("neck_trk_2", f)
-            v = torch.as_tensor(_CudaArray(p, feat * feat * 256, "<i4"), device="cuda")
-            sums.append((efirst + f, int(v.to(torch.int64).sum().item())))
-    all_sums = [None] * world
-    if world > 1:
-        dist.all_gather_object(all_sums, sums)
-    else:
-        all_sums = [sums]
+    # content check (N > 1): the frames rank 0 tracked in the last step came from the encoders' last outputs
     ok = None
+    if world > 1:
+        last = n_warm + steps - 1  # buffer last % 2 holds the frames encoded in step `last`
+        sums = []
+        for f in range(enf):
+            for (name, s), nb in zip(levels, lbytes):
+                p = eng.output_device_ptr(name, f)
+                v = torch.as_tensor(_CudaArray(p, nb // 4, "<i4"), device="cuda")
+                sums.append((efirst + f, name, int(v.to(torch.int64).sum().item())))
+        all_sums = [None] * world
+        dist.all_gather_object(all_sums, sums)
+        if rank == 0:
+            buf = recv + (last % 2) * FRAMES_TOTAL * fbytes
+            ok = True
+            n_checked = 0
+            for part in all_sums:
+                for f, name, sref in part:
+                    i = [n for n, _ in levels].index(name)
+                    v = torch.as_tensor(_CudaArray(frame_slot(buf, f)[i], lbytes[i] // 4, "<i4"), device="cuda")
+                    ok = ok and int(v.to(torch.int64).sum().item()) == sref
+                    n_checked += 1
+            ok = ok and n_checked == 3 * FRAMES_TOTAL
+        barrier(world)
+        if rank != 0:
+            eng.ipc_close(dst_base)
+        barrier(world)
     if rank == 0:
-        buf = recv + (last % 2) * FRAMES_TOTAL * fbytes
-        ok = True
-        n_checked = 0
-        for part in all_sums:
-            for f, sref in part:
-                v = torch.as_tensor(_CudaArray(buf + f * fbytes, feat * feat * 256, "<i4"), device="cuda")
-                ok = ok and int(v.to(torch.int64).sum().item()) == sref
-                n_checked += 1
-        ok = ok and n_checked == FRAMES_TOTAL
-    barrier(world)
-    if rank != 0:
-        eng.ipc_close(dst_base)
-    barrier(world)
-    if rank == 0:
-        enc_ms = ms if world == 1 else None
+        track_total = FRAMES_TOTAL * out["track_step_ms_per_frame"]
         out.update({"pipeline_frames_per_s": FRAMES_TOTAL / (pms / 1000.0), "pipeline_ms_per_step": pms,
-                    "pipeline": ("one GPU: encode 64 frames, then 64 memory-attention calls" if world == 1 else
-                                 f"{len(encoders)} encoder GPU(s) -> NVLink peer copies (CUDA IPC) -> tracking GPU 0, "
-                                 f"double-buffered, one host barrier per step"),
-                    "pipeline_limiter": ("encoder + memory attention in series on one GPU" if world == 1 else
-                                         ("memory attention on the tracking GPU"
-                                          if 64 * out["mem_attn_ms_per_frame"] >= pms * 0.8 else "encoders")),
-                    "p2p_content_check": "pass" if ok else "FAIL",
+                    "pipeline": ("one GPU: encode 64 frames, then one tracking step per frame (memory attention, "
+                                 "mask decoder, memory encoder, object pointer)" if world == 1 else
+                                 f"{len(encoders)} encoder GPU(s) -> NVLink peer copies of neck_trk_0/1/2 (CUDA IPC) "
+                                 f"-> tracking GPU 0 (one tracking step per frame), double-buffered, one host "
+                                 f"barrier per step"),
+                    "pipeline_limiter": ("encoder + tracking in series on one GPU" if world == 1 else
+                                         ("tracking steps on the tracking GPU"
+                                          if track_total >= pms * 0.8 else "encoders")),
                     "p2p_bytes_per_frame": fbytes})
-        if enc_ms is not None:
-            out["pipeline_encoder_ms"] = enc_ms
-        eng.device_free(recv)
+        if ok is not None:
+            out["p2p_content_check"] = "pass" if ok else "FAIL"
+        if world == 1:
+            out["pipeline_encoder_ms"] = ms
+        if recv is not None:
+            eng.device_free(recv)
     eng.set_stream(None)
     eng.close()
     return out

@@ -533,14 +533,17 @@ class Engine:
         return out
 
     def track_step(self, feat: int, trk0, trk1, trk2, slot_feats, slot_tpos, obj_ptrs=None, ptr_tpos=(),
-                   slot_pes=None, want=("mask", "scores", "mem", "ptr")):
-        """One tracking step (s3b_track_step) on torch CUDA tensors; returns a dict of the outputs asked for."""
+                   slot_pes=None, want=("mask", "scores", "mem", "ptr"), outs=None):
+        """One tracking step (s3b_track_step) on torch CUDA tensors (or raw device addresses for the inputs);
+        returns a dict of the outputs asked for (or fills `outs`, a dict of preallocated tensors)."""
         import torch
-        dev = trk2.device
-        outs = {"mask": torch.empty(16 * feat * feat, device=dev) if "mask" in want else None,
-                "scores": torch.empty(3, device=dev) if "scores" in want else None,
-                "mem": torch.empty(feat * feat, 64, device=dev) if "mem" in want else None,
-                "ptr": torch.empty(256, device=dev) if "ptr" in want else None}
+        if outs is None:
+            dev = trk2.device
+            outs = {"mask": torch.empty(16 * feat * feat, device=dev) if "mask" in want else None,
+                    "scores": torch.empty(3, device=dev) if "scores" in want else None,
+                    "mem": torch.empty(feat * feat, 64, device=dev) if "mem" in want else None,
+                    "ptr": torch.empty(256, device=dev) if "ptr" in want else None}
+        outs = {k: outs.get(k) for k in ("mask", "scores", "mem", "ptr")}
         n_slots, feats, pes, tpos, n_ptrs, ptpos = self._bank_args(slot_feats, slot_pes, slot_tpos, obj_ptrs, ptr_tpos)
         rc = self._L.s3b_track_step(self.h, feat, _ptr(trk0), _ptr(trk1), _ptr(trk2), feats, pes, tpos, n_slots,
                                     _ptr(obj_ptrs), ptpos, n_ptrs, _ptr(outs["mask"]), _ptr(outs["scores"]),

@@ -198,66 +198,98 @@ __global__ void __launch_bounds__(256) ln_gelu_rows_kernel(const float* __restri
   }
 }
 
-// CXBlock depthwise 7x7 / pad 3 convolution (f32 weights [49][256] in shared memory, f32 math as
-// ggml_conv_2d_dw_direct) + bias + LayerNorm2d over the 256 channels: one warp per pixel, 8 consecutive
-// channels per lane; out f16 [H*W][256] (the pointwise MLP's GEMM operand).
+// CXBlock depthwise 7x7 / pad 3 convolution (f32 math as ggml_conv_2d_dw_direct) + bias + LayerNorm2d
+// over the 256 channels. Persistent CTAs over 4 x 8 pixel tiles: the tile's 10 x 14 input halo (zeros
+// outside the map) and the 49 x 256 weights are staged in shared memory; warp w takes 4 consecutive
+// pixels of tile row w / 2, lane 8 consecutive channels, so each tap's weights are loaded once for 4
+// pixels. Out f16 [H*W][256] (the pointwise MLP's GEMM operand).
+constexpr int kDwTY = 4, kDwTX = 8, kDwHY = kDwTY + 6, kDwHX = kDwTX + 6;
+constexpr size_t kDwSmem = (size_t)(kDwHY * kDwHX + 49) * 256 * 4;
+
 __global__ void __launch_bounds__(256) dwconv7_ln_kernel(const float* __restrict__ x, int H, int W, const float* w,
                                                          const float* b, const float* g, const float* beta, float eps,
                                                          __half* __restrict__ y) {
-  extern __shared__ __align__(16) float dws[];  // [49][256]
-  for (int i = threadIdx.x; i < 49 * 256; i += blockDim.x) dws[i] = w[i];
-  __syncthreads();
-  const int lane = threadIdx.x & 31, c = lane * 8;
-  float bb[8];
+  extern __shared__ __align__(16) float dsm[];
+  float* xs = dsm;                          // [kDwHY * kDwHX][256]
+  float* ws = dsm + kDwHY * kDwHX * 256;    // [49][256]
+  for (int i = threadIdx.x; i < 49 * 64; i += blockDim.x)
+    reinterpret_cast<float4*>(ws)[i] = reinterpret_cast<const float4*>(w)[i];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, c = lane * 8;
+  const int ly = warp >> 1, lx0 = (warp & 1) * 4;
+  float bb[8], gg[8], be[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) bb[i] = b[c + i];
-  const long long n = (long long)H * W;
-  for (long long p = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); p < n; p += (long long)gridDim.x * 8) {
-    const int py = (int)(p / W), px = (int)(p - (long long)py * W);
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int i = 0; i < 8; ++i) {
+    bb[i] = b[c + i];
+    gg[i] = g[c + i];
+    be[i] = beta[c + i];
+  }
+  const int tiles_x = (W + kDwTX - 1) / kDwTX, tiles = tiles_x * ((H + kDwTY - 1) / kDwTY);
+  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int ty0 = (tile / tiles_x) * kDwTY, tx0 = (tile % tiles_x) * kDwTX;
+    __syncthreads();
+    for (int i = threadIdx.x; i < kDwHY * kDwHX * 64; i += blockDim.x) {
+      const int pix = i >> 6, q = i & 63;
+      const int iy = ty0 - 3 + pix / kDwHX, ix = tx0 - 3 + pix % kDwHX;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+        v = reinterpret_cast<const float4*>(x + ((long long)iy * W + ix) * 256)[q];
+      reinterpret_cast<float4*>(xs + pix * 256)[q] = v;
+    }
+    __syncthreads();
+    float acc[4][8];
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[p][i] = 0.f;
     for (int ky = 0; ky < 7; ++ky) {
-      const int iy = py - 3 + ky;
-      if (iy < 0 || iy >= H) continue;
+#pragma unroll
       for (int kx = 0; kx < 7; ++kx) {
-        const int ix = px - 3 + kx;
-        if (ix < 0 || ix >= W) continue;
-        const float* s = x + ((long long)iy * W + ix) * 256 + c;
-        const float4 a0 = *reinterpret_cast<const float4*>(s);
-        const float4 a1 = *reinterpret_cast<const float4*>(s + 4);
-        const float* wk = dws + (ky * 7 + kx) * 256 + c;
+        const float* wk = ws + (ky * 7 + kx) * 256 + c;
         const float4 w0 = *reinterpret_cast<const float4*>(wk);
         const float4 w1 = *reinterpret_cast<const float4*>(wk + 4);
-        acc[0] = fmaf(a0.x, w0.x, acc[0]);
-        acc[1] = fmaf(a0.y, w0.y, acc[1]);
-        acc[2] = fmaf(a0.z, w0.z, acc[2]);
-        acc[3] = fmaf(a0.w, w0.w, acc[3]);
-        acc[4] = fmaf(a1.x, w1.x, acc[4]);
-        acc[5] = fmaf(a1.y, w1.y, acc[5]);
-        acc[6] = fmaf(a1.z, w1.z, acc[6]);
-        acc[7] = fmaf(a1.w, w1.w, acc[7]);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float* xp = xs + ((ly + ky) * kDwHX + lx0 + p + kx) * 256 + c;
+          const float4 a0 = *reinterpret_cast<const float4*>(xp);
+          const float4 a1 = *reinterpret_cast<const float4*>(xp + 4);
+          acc[p][0] = fmaf(a0.x, w0.x, acc[p][0]);
+          acc[p][1] = fmaf(a0.y, w0.y, acc[p][1]);
+          acc[p][2] = fmaf(a0.z, w0.z, acc[p][2]);
+          acc[p][3] = fmaf(a0.w, w0.w, acc[p][3]);
+          acc[p][4] = fmaf(a1.x, w1.x, acc[p][4]);
+          acc[p][5] = fmaf(a1.y, w1.y, acc[p][5]);
+          acc[p][6] = fmaf(a1.z, w1.z, acc[p][6]);
+          acc[p][7] = fmaf(a1.w, w1.w, acc[p][7]);
+        }
       }
     }
-    float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      acc[i] += bb[i];
-      s += acc[i];
+    for (int p = 0; p < 4; ++p) {
+      const int py = ty0 + ly, px = tx0 + lx0 + p;
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        acc[p][i] += bb[i];
+        s += acc[p][i];
+      }
+      const float mean = warp_sum(s) * (1.0f / 256);
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        acc[p][i] -= mean;
+        q = fmaf(acc[p][i], acc[p][i], q);
+      }
+      const float rstd = rsqrtf(warp_sum(q) * (1.0f / 256) + eps);
+      if (py < H && px < W) {
+        uint4 o;
+        __half2* h = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          h[k] = __floats2half2_rn(acc[p][2 * k] * rstd * gg[2 * k] + be[2 * k],
+                                   acc[p][2 * k + 1] * rstd * gg[2 * k + 1] + be[2 * k + 1]);
+        *reinterpret_cast<uint4*>(y + ((long long)py * W + px) * 256 + c) = o;
+      }
     }
-    const float mean = warp_sum(s) * (1.0f / 256);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      acc[i] -= mean;
-      q = fmaf(acc[i], acc[i], q);
-    }
-    const float rstd = rsqrtf(warp_sum(q) * (1.0f / 256) + eps);
-    uint4 o;
-    __half2* h = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      h[k] = __floats2half2_rn(acc[2 * k] * rstd * g[c + 2 * k] + beta[c + 2 * k],
-                               acc[2 * k + 1] * rstd * g[c + 2 * k + 1] + beta[c + 2 * k + 1]);
-    *reinterpret_cast<uint4*>(y + p * 256 + c) = o;
   }
 }
 
@@ -328,12 +360,10 @@ int dwconv7_ln(const float* x, int H, int W, const float* w, const float* b, con
                float eps, __half* y, cudaStream_t st) {
   if (!x || !w || !b || !g || !beta || !y || H <= 0 || W <= 0) return -2;
   if (!al16(x) || !al16(w) || !al16(y)) return -11;
-  const size_t smem = 49 * 256 * 4;
-  if (kernel_setup(dwconv7_ln_kernel, smem) < 0) return -13;
-  const long long n = (long long)H * W;
-  const long long want = (n + 7) / 8, cap = (long long)num_sms() * 4;
-  const int grid = (int)(want < cap ? want : cap);
-  dwconv7_ln_kernel<<<grid, 256, smem, st>>>(x, H, W, w, b, g, beta, eps, y);
+  if (kernel_setup(dwconv7_ln_kernel, kDwSmem) < 0) return -13;
+  const long long tiles = (long long)((W + kDwTX - 1) / kDwTX) * ((H + kDwTY - 1) / kDwTY);
+  const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+  dwconv7_ln_kernel<<<grid, 256, kDwSmem, st>>>(x, H, W, w, b, g, beta, eps, y);
   return me_launch_ok();
 }
 

@@ -62,20 +62,24 @@ struct TokJobs {
   TokJob j[kTokMaxJobs];
 };
 
-constexpr int kTokThreads = 256, kTokCols = kTokThreads / 32;  // one output column per warp
-constexpr int kTokSmemFloats = 8192;                             // 32 KB of staged input rows
+constexpr int kTokThreads = 256, kTokWarps = 8, kTokCols = 32;  // 32 output columns per CTA
+constexpr int kTokSmemFloats = 8192;                                  // 32 KB of staged input rows
 
-// CTA (blockIdx.x, blockIdx.y): columns [8 x, 8 x + 8) of job y. The job's input rows are staged in
-// shared memory in K chunks of kTokSmemFloats / RB columns; every lane then reads 8 weights at a
-// time (one 16-byte load) and accumulates them against all R rows.
+// CTA (blockIdx.x, blockIdx.y): columns [32 x, 32 x + 32) of job y, one per lane; the 8 warps split the
+// reduction dimension into contiguous slices. The job's input rows are staged in shared memory in K
+// chunks of kTokSmemFloats / RB columns; each lane streams its column's weight slice (16-byte loads)
+// and accumulates it against all R rows; the 8 partial sums per (row, column) meet in shared memory.
 template <int RB>
 __global__ void __launch_bounds__(kTokThreads) tok_linear_kernel(const TokJobs jobs) {
   const TokJob& jb = jobs.j[blockIdx.y];
-  if ((int)blockIdx.x * kTokCols >= jb.N) return;  // uniform over the CTA
-  __shared__ __align__(16) float xs[kTokSmemFloats];
+  const int n0 = blockIdx.x * kTokCols;
+  if (n0 >= jb.N) return;  // uniform over the CTA
+  extern __shared__ __align__(16) float tok_smem[];
+  float* xs = tok_smem;                          // [RB][KC]
+  float* red = tok_smem + kTokSmemFloats;        // [kTokWarps][RB][kTokCols]
   constexpr int KC = kTokSmemFloats / RB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * kTokCols + warp;
+  const int n = n0 + lane;
   const int R = jb.R;
   float acc[RB];
 #pragma unroll
@@ -90,9 +94,13 @@ __global__ void __launch_bounds__(kTokThreads) tok_linear_kernel(const TokJobs j
       xs[r * KC + c] = v;
     }
     __syncthreads();
+    // this warp's slice of the chunk, in whole 8-value vectors
+    const int nvec = kc / 8, per = (nvec + kTokWarps - 1) / kTokWarps;
+    const int v0 = warp * per, v1 = min(nvec, v0 + per);
     if (n < jb.N) {
       const __half* w = jb.W + (long long)n * jb.ldw + k0;
-      for (int c = lane * 8; c < kc; c += 256) {
+      for (int vv = v0; vv < v1; ++vv) {
+        const int c = vv * 8;
         float wf[8];
         unpack8(*reinterpret_cast<const uint4*>(w + c), wf);
 #pragma unroll
@@ -115,20 +123,28 @@ __global__ void __launch_bounds__(kTokThreads) tok_linear_kernel(const TokJobs j
       }
     }
   }
-  if (n >= jb.N) return;
 #pragma unroll
-  for (int r = 0; r < RB; ++r) {
-    if (r < R) {
-      const float s = warp_sum(acc[r]);
-      if (lane == (r & 31)) {
-        float v = s + (jb.b ? jb.b[n] : 0.f);
-        if (jb.act == 1) v = fmaxf(v, 0.f);
-        else if (jb.act == 2) v = 1.f / (1.f + expf(-v));
-        if (jb.resid) v += jb.resid[r * jb.ldr + n];
-        jb.y[r * jb.ldy + n] = v;
-      }
-    }
+  for (int r = 0; r < RB; ++r)
+    if (r < R) red[(warp * RB + r) * kTokCols + lane] = acc[r];
+  __syncthreads();
+  for (int i = threadIdx.x; i < R * kTokCols; i += kTokThreads) {
+    const int r = i / kTokCols, c = i - r * kTokCols;
+    const int col = n0 + c;
+    if (col >= jb.N) continue;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kTokWarps; ++w) v += red[(w * RB + r) * kTokCols + c];
+    v += jb.b ? jb.b[col] : 0.f;
+    if (jb.act == 1) v = fmaxf(v, 0.f);
+    else if (jb.act == 2) v = 1.f / (1.f + expf(-v));
+    if (jb.resid) v += jb.resid[r * jb.ldr + col];
+    jb.y[r * jb.ldy + col] = v;
   }
+}
+
+template <int RB>
+constexpr size_t tok_smem_bytes() {
+  return (size_t)(kTokSmemFloats + kTokWarps * RB * kTokCols) * 4;
 }
 
 // ---------------------------------------------------------------- token LayerNorm
@@ -166,20 +182,33 @@ __global__ void __launch_bounds__(256) tok_ln_kernel(const float* a, const float
 }
 
 // ---------------------------------------------------------------- token self-attention
-// One CTA; thread (token i, head h) computes its softmax row over the nt keys and its hd outputs.
+// One CTA; the nt rows of q, k and v (heads * hd <= 256 columns each) are staged in shared memory, then
+// thread (token i, head h) computes its softmax row over the nt keys and its hd outputs.
 __global__ void __launch_bounds__(256) tok_attn_kernel(const float* q, long long ldq, const float* k, long long ldk,
                                                        const float* v, long long ldv, int nt, int heads, int hd,
                                                        float scale, float* out, long long ldo) {
+  extern __shared__ float tsm[];  // q, k, v rows [nt][cols + 1] each
+  const int cols = heads * hd, ld = cols + 1;
+  float* qs = tsm;
+  float* ks = qs + nt * ld;
+  float* vs = ks + nt * ld;
+  for (int i = threadIdx.x; i < nt * cols; i += blockDim.x) {
+    const int r = i / cols, c = i - r * cols;
+    qs[r * ld + c] = q[r * ldq + c];
+    ks[r * ld + c] = k[r * ldk + c];
+    vs[r * ld + c] = v[r * ldv + c];
+  }
+  __syncthreads();
   const int t = threadIdx.x;
   if (t >= nt * heads) return;
   const int i = t / heads, h = t - i * heads;
-  const float* qi = q + i * ldq + h * hd;
+  const float* qi = qs + i * ld + h * hd;
   float s[kTokMaxRows];
   float m = -INFINITY;
 #pragma unroll
   for (int j = 0; j < kTokMaxRows; ++j) {
     if (j < nt) {
-      const float* kj = k + j * ldk + h * hd;
+      const float* kj = ks + j * ld + h * hd;
       float d = 0.f;
       for (int c = 0; c < hd; ++c) d = fmaf(qi[c], kj[c], d);
       s[j] = d * scale;
@@ -198,7 +227,7 @@ __global__ void __launch_bounds__(256) tok_attn_kernel(const float* q, long long
     float o = 0.f;
 #pragma unroll
     for (int j = 0; j < kTokMaxRows; ++j)
-      if (j < nt) o = fmaf(s[j], v[j * ldv + h * hd + c], o);
+      if (j < nt) o = fmaf(s[j], vs[j * ld + h * hd + c], o);
     out[i * ldo + h * hd + c] = o * inv;
   }
 }
@@ -608,49 +637,51 @@ __global__ void __launch_bounds__(256) dec_masks_kernel(const __half* u1, const 
 
 // The mask a tracking step keeps (sam3_propagate_single, sam3.cpp:11395-11430): token 0 without multimask
 // output, else the best IoU among tokens 1 .. n-1 (first on ties); the object pointer's token is the
-// chosen one when use_mm_token, else token 0. One CTA: thread 0 decides, all threads copy the mask.
+// chosen one when use_mm_token, else token 0. Every CTA takes the same decision from the n IoU values and
+// copies its share of the plane; CTA 0 also writes the token and the scores.
 __global__ void __launch_bounds__(256) pick_mask_kernel(const float* masks, long long plane, const float* iou,
                                                         const float* tokens, int n_masks, int multimask,
                                                         int use_mm_token, float* out_mask, float* out_token,
                                                         float* out_scores, const float* obj) {
-  __shared__ int best_s;
-  if (threadIdx.x == 0) {
-    int best = 0;
-    if (multimask && n_masks > 1) {
-      best = 1;
-      for (int m = 2; m < n_masks; ++m)
-        if (iou[m] > iou[best]) best = m;
+  int best = 0;
+  if (multimask && n_masks > 1) {
+    best = 1;
+    for (int m = 2; m < n_masks; ++m)
+      if (iou[m] > iou[best]) best = m;
+  }
+  if (out_mask) {
+    const float4* src = reinterpret_cast<const float4*>(masks + best * plane);
+    float4* dst = reinterpret_cast<float4*>(out_mask);
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < plane / 4; i += (long long)gridDim.x * blockDim.x)
+      dst[i] = src[i];
+  }
+  if (blockIdx.x == 0) {
+    if (out_token) {
+      const int t = use_mm_token ? best : 0;
+      for (int i = threadIdx.x; i < 256; i += blockDim.x) out_token[i] = tokens[t * 256 + i];
     }
-    best_s = best;
-    if (out_scores) {
+    if (out_scores && threadIdx.x == 0) {
       out_scores[0] = iou[best];
       out_scores[1] = obj ? *obj : 0.f;
       out_scores[2] = (float)best;
     }
-  }
-  __syncthreads();
-  const int best = best_s;
-  if (out_mask)
-    for (long long i = threadIdx.x; i < plane; i += blockDim.x) out_mask[i] = masks[best * plane + i];
-  if (out_token) {
-    const int t = use_mm_token ? best : 0;
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) out_token[i] = tokens[t * 256 + i];
   }
 }
 
 }  // namespace
 
 // ---------------------------------------------------------------- launchers
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 int pick_mask(const float* masks, long long plane, const float* iou, const float* tokens, int n_masks, int multimask,
               int use_mm_token, float* out_mask, float* out_token, float* out_scores, const float* obj,
               cudaStream_t st) {
-  if (!masks || !iou || !tokens || n_masks <= 0 || plane <= 0) return -2;
-  pick_mask_kernel<<<1, 256, 0, st>>>(masks, plane, iou, tokens, n_masks, multimask, use_mm_token, out_mask, out_token,
-                                      out_scores, obj);
+  if (!masks || !iou || !tokens || n_masks <= 0 || plane <= 0 || plane % 4) return -2;
+  if (!al16(masks) || (out_mask && !al16(out_mask))) return -11;
+  pick_mask_kernel<<<dec_grid(plane / 4, 256, 2), 256, 0, st>>>(masks, plane, iou, tokens, n_masks, multimask,
+                                                                 use_mm_token, out_mask, out_token, out_scores, obj);
   return dec_launch_ok();
 }
-
-static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int tok_linear(const TokJob* jobs, int n_jobs, cudaStream_t st) {
   if (n_jobs <= 0 || n_jobs > kTokMaxJobs) return -1;
@@ -667,9 +698,16 @@ int tok_linear(const TokJob* jobs, int n_jobs, cudaStream_t st) {
     maxR = max(maxR, j.R);
   }
   const dim3 grid((maxN + kTokCols - 1) / kTokCols, n_jobs);
-  if (maxR <= 8) tok_linear_kernel<8><<<grid, kTokThreads, 0, st>>>(J);
-  else if (maxR <= 16) tok_linear_kernel<16><<<grid, kTokThreads, 0, st>>>(J);
-  else tok_linear_kernel<32><<<grid, kTokThreads, 0, st>>>(J);
+  if (maxR <= 8) {
+    if (kernel_setup(tok_linear_kernel<8>, tok_smem_bytes<8>()) < 0) return -13;
+    tok_linear_kernel<8><<<grid, kTokThreads, tok_smem_bytes<8>(), st>>>(J);
+  } else if (maxR <= 16) {
+    if (kernel_setup(tok_linear_kernel<16>, tok_smem_bytes<16>()) < 0) return -13;
+    tok_linear_kernel<16><<<grid, kTokThreads, tok_smem_bytes<16>(), st>>>(J);
+  } else {
+    if (kernel_setup(tok_linear_kernel<32>, tok_smem_bytes<32>()) < 0) return -13;
+    tok_linear_kernel<32><<<grid, kTokThreads, tok_smem_bytes<32>(), st>>>(J);
+  }
   return dec_launch_ok();
 }
 
@@ -682,9 +720,12 @@ int tok_layernorm(const float* a, const float* b, long long ld, int rows, int C,
 
 int tok_attention(const float* q, long long ldq, const float* k, long long ldk, const float* v, long long ldv,
                   int nt, int heads, int hd, float scale, float* out, long long ldo, cudaStream_t st) {
-  if (!q || !k || !v || !out || nt <= 0 || nt > kTokMaxRows || heads <= 0 || nt * heads > 256 || hd <= 0 || hd > 32)
+  if (!q || !k || !v || !out || nt <= 0 || nt > kTokMaxRows || heads <= 0 || nt * heads > 256 || hd <= 0 || hd > 32 ||
+      heads * hd > 256)
     return -2;
-  tok_attn_kernel<<<1, 256, 0, st>>>(q, ldq, k, ldk, v, ldv, nt, heads, hd, scale, out, ldo);
+  const size_t smem = (size_t)3 * nt * (heads * hd + 1) * 4;
+  if (kernel_setup(tok_attn_kernel, (size_t)3 * kTokMaxRows * 257 * 4) < 0) return -13;
+  tok_attn_kernel<<<1, 256, smem, st>>>(q, ldq, k, ldk, v, ldv, nt, heads, hd, scale, out, ldo);
   return dec_launch_ok();
 }
 
