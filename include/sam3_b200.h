@@ -121,6 +121,18 @@ int s3b_profile_end(s3b_ctx* ctx, double* out, int n);
  * tensors outside the engine's scope are skipped. */
 int s3b_load_model(s3b_ctx* ctx, const char* path);
 
+/* s3b_load_model through a persistent cache of the model's device form
+ * (the row layouts, block-form planes, folded and fused weights and tables
+ * that loading computes from the file; sam3_load_tensors, sam3.cpp:3091-3194,
+ * redoes its conversions at every start). When cache_path holds a cache made
+ * from the same file (size, modification time and a hash of its first and
+ * last MiB), the same engine format and the same "weights_quantised" option,
+ * the model is copied from it to the device with no conversion and 1 is
+ * returned. Otherwise the file is loaded as s3b_load_model does, the cache is
+ * (re)written and 0 is returned; a cache that cannot be written is reported
+ * on stderr and does not fail the load. Negative: the load failed. */
+int s3b_load_model_cached(s3b_ctx* ctx, const char* model_path, const char* cache_path);
+
 /* A weight tensor in the caller's host memory, as sam3.cpp holds it after
  * sam3_load_tensors (sam3.cpp:3091-3194): the .ggml tensor name, its ggml
  * type, shape in ggml order (ne[0] contiguous; unused dims 1) and data in

@@ -55,6 +55,7 @@ SYMBOLS = [
     ("s3b_profile_begin", _I, [_P, _I]),
     ("s3b_profile_end", _I, [_P, ctypes.POINTER(ctypes.c_double), _I]),
     ("s3b_load_model", _I, [_P, _S]),
+    ("s3b_load_model_cached", _I, [_P, _S, _S]),
     ("s3b_load_weights", _I, [_P, _I, ctypes.POINTER(ctypes.c_int32), _I, _I, ctypes.POINTER(TensorDesc), _I]),
     ("s3b_inspect_model", _I, [_S, ctypes.POINTER(ctypes.c_int32), _I, _S, _I]),
     ("s3b_model_info", _I, [_P, ctypes.POINTER(ctypes.c_int32), _I]),
@@ -279,6 +280,12 @@ class Engine:
 
     def load_model(self, path: str):
         self._check(self._L.s3b_load_model(self.h, path.encode()), "s3b_load_model")
+
+    def load_model_cached(self, path: str, cache_path: str) -> bool:
+        """s3b_load_model through the device-weight cache; True when the model came from the cache."""
+        rc = self._L.s3b_load_model_cached(self.h, path.encode(), cache_path.encode())
+        self._check(min(rc, 0), "s3b_load_model_cached")
+        return rc == 1
 
     def load_weights(self, is_sam2: int, hparams, ftype: int, tensors):
         """s3b_load_weights from host tensors: tensors = [(name, dtype, shape (PyTorch order), bytes-like)]."""

@@ -535,6 +535,18 @@ int s3b_load_model(s3b_ctx* ctx, const char* path) {
   return load_model(ctx, path);
 }
 
+int s3b_load_model_cached(s3b_ctx* ctx, const char* model_path, const char* cache_path) {
+  int rc = ctx_enter(ctx);
+  if (rc) return rc;
+  if (!model_path || !cache_path) return set_error(ctx, kErrArg, "null path");
+  ctx->out = Outputs();
+  ctx->ptr_pe_cache.clear();
+  for (auto it = ctx->ws.begin(); it != ctx->ws.end();)  // dense PE grids of the previous decoder
+    it = it->first.compare(0, 7, "dec_pe_") == 0 ? ctx->ws.erase(it) : std::next(it);
+  ++ctx->graph_epoch;  // graphs hold the old weights' addresses
+  return load_model_cached(ctx, model_path, cache_path);
+}
+
 int s3b_load_weights(s3b_ctx* ctx, int is_sam2, const int32_t* hparams, int n_hparams, int ftype,
                      const s3b_tensor_desc* descs, int n) {
   int rc = ctx_enter(ctx);

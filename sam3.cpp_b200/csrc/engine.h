@@ -350,6 +350,9 @@ int check_device(s3b_ctx* ctx, const char* where);
 
 // weight preparation (model.cpp)
 int load_model(s3b_ctx* ctx, const std::string& path);
+// load_model through the device-weight cache (weight_cache.cpp): 1 = loaded from a valid cache file,
+// 0 = loaded from the model file (and the cache written), < 0 = error.
+int load_model_cached(s3b_ctx* ctx, const std::string& model_path, const std::string& cache_path);
 // Prepares the device weights from parsed tensors (the file reader's or the caller's).
 int load_model_tensors(s3b_ctx* ctx, const HParams& hp, const std::vector<FileTensor>& tensors);
 int upload_linear(s3b_ctx* ctx, const FileTensor& t, const FileTensor* bias, Linear& L, int kpad_to = 8,
