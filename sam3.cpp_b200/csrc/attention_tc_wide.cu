@@ -57,7 +57,10 @@ struct WideCfg {
   static constexpr uint32_t KVBytes = NA * KVAtom;
   static constexpr uint32_t TmemCols = kOCol + DK <= 256 ? 256 : 512;
   static constexpr int MinBlocks = TmemCols <= 256 ? 2 : 1;  // CTAs per SM (TMEM, shared memory)
-  static constexpr size_t Smem = 1024 + QBytes + kSlots * KVBytes + kPBytes + 16 * 8 + 16;
+  // P buffers: two for the one-CTA-per-SM d = 256 kernel, so the softmax of key tile j writes P_j while
+  // the P V product of tile j - 1 still reads its buffer; one where two CTAs share the SM's shared memory
+  static constexpr int NP = MinBlocks == 1 ? 2 : 1;
+  static constexpr size_t Smem = 1024 + QBytes + kSlots * KVBytes + NP * kPBytes + 24 * 8 + 16;
 };
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -215,16 +218,18 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem;                           // NA atoms of 16 KB
   uint8_t* sKV = sQ + C::QBytes;                // kSlots x NA x 8 KB
-  uint8_t* sP = sKV + kSlots * C::KVBytes;      // 16 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  constexpr int NP = C::NP;
+  uint8_t* sP = sKV + kSlots * C::KVBytes;      // NP x 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + NP * kPBytes);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;                 // [kSlots]
   uint64_t* kv_empty = kv_full + kSlots;        // [kSlots]
   uint64_t* s_full = kv_empty + kSlots;         // [2]
   uint64_t* s_empty = s_full + 2;               // [2]
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* p_empty = p_full + 1;
-  uint64_t* o_done = p_empty + 1;
+  uint64_t* p_full = s_empty + 2;               // [NP]: P_j written (barrier j % NP)
+  uint64_t* p_empty = p_full + 2;               // [NP]: the P V product that read buffer j % NP completed
+  uint64_t* pv_done = p_empty + 2;              // [2] (NP = 2): P V_j completed (barrier j & 1), O current
+  uint64_t* o_done = pv_done + 2;
   uint64_t* mma_done = o_done + 1;
   uint64_t* q_ready = mma_done + 1;             // Q padding zeroed (d = 72)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(q_ready + 1);
@@ -257,8 +262,11 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 4);
     }
-    mbar_init(p_full, 4);
-    mbar_init(p_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&p_full[b], 4);
+      mbar_init(&p_empty[b], 1);
+      mbar_init(&pv_done[b], 1);
+    }
     mbar_init(o_done, 1);
     mbar_init(mma_done, 1);
     mbar_init(q_ready, 4);
@@ -336,11 +344,11 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
       if (ok && nkb > 1) ok = issue_s(1);
       for (int j = 0; j < nkb && ok; ++j) {
         // O += P_j V_j (after the softmax wrote P_j and, where needed, rescaled O)
-        const int t = 2 * j + 1, s = t % kSlots;
-        if (!mbar_wait(p_full, (uint32_t)j & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
+        const int t = 2 * j + 1, s = t % kSlots, pb = j % NP;
+        if (!mbar_wait(&p_full[pb], (uint32_t)(j / NP) & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
         if (!mbar_wait(&kv_full[s], (uint32_t)(t / kSlots) & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t pa = smem_u32(sP), va = smem_u32(sKV + s * C::KVBytes);
+        const uint32_t pa = smem_u32(sP + pb * kPBytes), va = smem_u32(sKV + s * C::KVBytes);
         const int nk16 = min(kBK / 16, (a.nk - (j0 + j) * kBK + 15) / 16);  // K steps holding a real key
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
@@ -350,7 +358,8 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
           tc_mma_f16(tmem + kOCol, dp, dv, idesc_o, (j > 0 || kk != 0) ? 1u : 0u);
         }
         tc_commit(&kv_empty[s]);
-        tc_commit(p_empty);
+        tc_commit(&p_empty[pb]);
+        if (NP == 2) tc_commit(&pv_done[j & 1]);
         if (j + 2 < nkb && !issue_s(j + 2)) { ok = false; break; }
       }
       if (ok) tc_commit(o_done);
@@ -365,7 +374,6 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
     const int row = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const bool rows_live = qb * kBQ + q4 * 32 < a.nq;  // else only the barrier protocol
-    uint8_t* prow = sP + row * 128;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     if constexpr (kPadQ) {
@@ -402,14 +410,27 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
           l *= alpha;
         }
       }
-      // P buffer free and O final for tile j-1
-      if (j > 0 && !mbar_wait(p_empty, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc)) ok = false;
+      // P buffer j % NP free (its last reader, P V_{j-NP}, completed; with one buffer that also makes O
+      // final for tile j - 1)
+      const int pb = j % NP;
+      if (j >= NP && !mbar_wait(&p_empty[pb], (uint32_t)(j / NP - 1) & 1, s_abort, err, kErrWaitMisc)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       if (rows_live) {
         tc_fence_after();
+        uint8_t* prow = sP + pb * kPBytes + row * 128;
         l += full_tile ? row_p64<false>(s_addr, kvalid, a.sl2, m_ref, prow, row)
                        : row_p64<true>(s_addr, kvalid, a.sl2, m_ref, prow, row);
+      }
+      // with two P buffers, O is current only once P V_{j-1} completed: waited for only when a row of
+      // this warp rescales (its barrier cannot run two phases ahead: P V_{j+1} needs this tile's P_{j+1})
+      if (NP == 2 && __any_sync(0xffffffffu, resc) &&
+          !mbar_wait(&pv_done[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1, s_abort, err, kErrWaitMisc))
+        ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      if (rows_live) {
+        tc_fence_after();
         if (__any_sync(0xffffffffu, resc)) {
           const float f = resc ? alpha : 1.f;
 #pragma unroll 1
@@ -430,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&s_empty[sb]);
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[pb]);
       }
     }
     if (ok) ok = mbar_wait(o_done, 0, s_abort, err, kErrWaitMisc);

@@ -413,22 +413,17 @@ static void fold_1x1_into_deconv(const std::vector<float>& d, const std::vector<
     bf[o] = (float)acc;
   }
   const int n_rows = 4 * Co;
-  unsigned nt = std::thread::hardware_concurrency();
-  nt = std::max(1u, std::min(nt, 32u));
-  std::vector<std::thread> th;
-  for (unsigned t = 0; t < nt; ++t)
-    th.emplace_back([&, t]() {
-      for (int row = (int)t; row < n_rows; row += (int)nt) {
-        const int p = row / Co, o = row % Co;
-        float* out = f.data() + (size_t)row * Cin;
-        for (int k = 0; k < Cd; ++k) {
-          const float s = c[(size_t)o * Cd + k];
-          const float* in = d.data() + (size_t)(p * Cd + k) * Cin;
-          for (int i = 0; i < Cin; ++i) out[i] += s * in[i];
-        }
+  parallel_for(n_rows, 1, [&](int64_t b, int64_t e) {
+    for (int64_t row = b; row < e; ++row) {
+      const int p = (int)(row / Co), o = (int)(row % Co);
+      float* out = f.data() + (size_t)row * Cin;
+      for (int k = 0; k < Cd; ++k) {
+        const float s = c[(size_t)o * Cd + k];
+        const float* in = d.data() + (size_t)(p * Cd + k) * Cin;
+        for (int i = 0; i < Cin; ++i) out[i] += s * in[i];
       }
-    });
-  for (auto& x : th) x.join();
+    }
+  });
 }
 
 static int upload_deconv(s3b_ctx* ctx, const FileTensor& t, const FileTensor& bias, Linear& L) {

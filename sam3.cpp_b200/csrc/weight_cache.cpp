@@ -15,6 +15,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -102,12 +103,19 @@ struct Writer {
   }
 };
 
-// Deserialising side: fields read from the mapped file, device buffers allocated and uploaded.
+// Deserialising side: fields read from the mapped file; device buffers are allocated while parsing and
+// their bytes queued, then streamed to the device through two pinned staging halves (stream_uploads).
 struct Reader {
   s3b_ctx* ctx;
   const uint8_t* p;
   size_t left;
   bool ok = true;
+  struct Pending {
+    void* dst;
+    const uint8_t* src;
+    size_t n;
+  };
+  std::vector<Pending> uploads;
   void raw(void* dst, size_t n) {
     if (!ok || n > left) {
       ok = false;
@@ -131,10 +139,11 @@ struct Reader {
     if (!present) return;
     b = std::make_shared<DevBuf>();
     if (!n) return;
-    if (n > left || b->reserve(n) != 0 || upload_sync(ctx, b->p, p, n) != kOk) {
+    if (n > left || b->reserve(n) != 0) {
       ok = false;
       return;
     }
+    uploads.push_back({b->p, p, (size_t)n});
     ctx->model.device_bytes += n;
     p += n;
     left -= n;
@@ -161,6 +170,53 @@ struct Reader {
     for (T& x : v) each(x);
   }
 };
+
+// The queued buffers in file order through two pinned staging halves of 32 MiB: the host fills one half
+// while the copy engine drains the other; an event per half orders the reuse.
+bool stream_uploads(s3b_ctx* ctx, const std::vector<Reader::Pending>& ups) {
+  constexpr size_t kHalf = 32u << 20;
+  uint8_t* pin = nullptr;
+  if (cudaMallocHost(&pin, 2 * kHalf) != cudaSuccess) return false;
+  cudaEvent_t ev[2];
+  cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming);
+  cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming);
+  bool ok = true, used[2] = {false, false};
+  int half = 0;
+  size_t fill = 0;
+  struct Seg {
+    void* dst;
+    size_t off, n;
+  };
+  std::vector<Seg> segs;
+  auto flush = [&]() {
+    for (const Seg& g : segs)
+      if (cudaMemcpyAsync(g.dst, pin + half * kHalf + g.off, g.n, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
+        ok = false;
+    cudaEventRecord(ev[half], ctx->stream);
+    used[half] = true;
+    segs.clear();
+    half ^= 1;
+    fill = 0;
+    if (used[half]) cudaEventSynchronize(ev[half]);
+  };
+  for (const Reader::Pending& u : ups) {
+    size_t done = 0;
+    while (done < u.n && ok) {
+      if (fill == kHalf) flush();
+      const size_t take = std::min(u.n - done, kHalf - fill);
+      memcpy(pin + half * kHalf + fill, u.src + done, take);
+      segs.push_back({static_cast<uint8_t*>(u.dst) + done, fill, take});
+      fill += take;
+      done += take;
+    }
+  }
+  if (fill) flush();
+  if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) ok = false;
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  cudaFreeHost(pin);
+  return ok;
+}
 
 // Every field of the model, in one order for both directions.
 template <typename IO>
@@ -324,7 +380,7 @@ int read_cache(s3b_ctx* ctx, const std::string& cache_path, const CacheHeader& w
     ctx->model = Model();
     Reader r{ctx, static_cast<const uint8_t*>(map) + sizeof(CacheHeader), (size_t)h.payload_bytes};
     io_model(r, ctx->model);
-    rc = (r.ok && r.left == 0) ? 0 : 1;
+    rc = (r.ok && r.left == 0 && stream_uploads(ctx, r.uploads)) ? 0 : 1;
     if (rc) ctx->model = Model();  // damaged: the caller rebuilds from the model file
   }
   munmap(map, (size_t)st.st_size);
