@@ -84,6 +84,13 @@ __device__ __forceinline__ float exp2_poly3(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
 }
 
+// max(a, b, c) in one instruction (three-input max.f32, sm_100)
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -151,20 +158,17 @@ __device__ __forceinline__ float half_row_max(uint32_t taddr, int cbase, int kva
     TMEM_LD32(taddr + (uint32_t)c, r);
     tc_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
-      float v2 = __uint_as_float(r[i + 2]), v3 = __uint_as_float(r[i + 3]);
-      if (MASKED) {
-        const int k = cbase + c + i;
-        v0 = k < kvalid ? v0 : -INFINITY;
-        v1 = k + 1 < kvalid ? v1 : -INFINITY;
-        v2 = k + 2 < kvalid ? v2 : -INFINITY;
-        v3 = k + 3 < kvalid ? v3 : -INFINITY;
+    for (int i = 0; i < 32; i += 8) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[e] = __uint_as_float(r[i + e]);
+        if (MASKED) v[e] = cbase + c + i + e < kvalid ? v[e] : -INFINITY;
       }
-      mx0 = fmaxf(mx0, v0);
-      mx1 = fmaxf(mx1, v1);
-      mx2 = fmaxf(mx2, v2);
-      mx3 = fmaxf(mx3, v3);
+      mx0 = fmax3f(mx0, v[0], v[1]);
+      mx1 = fmax3f(mx1, v[2], v[3]);
+      mx2 = fmax3f(mx2, v[4], v[5]);
+      mx3 = fmax3f(mx3, v[6], v[7]);
     }
   }
   return fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
@@ -576,6 +580,79 @@ constexpr int kFaSlots = 8;
 constexpr uint32_t kFaKVBytes = kFaBK * kD * 2;  // 12 KB
 constexpr uint32_t kFaTmemCols = 512;
 
+// One key tile of one query row (this thread's TMEM lane) in the FA kernel: the row's 96 scores from the TMEM
+// region at r_addr, their maximum (three-input max), the lazy reference max, p = 2^(s * sl2 - m_ref) written back
+// as f16 pairs over the region's first 48 columns, and the row sum added to l. MASKED: keys at or past kvalid are
+// tiling padding (p = 0); full tiles compile without any per-key select. Returns true when the reference max moved
+// after the first key tile, i.e. when the row of O must be rescaled by alpha.
+template <bool MASKED, int NPOLY>
+__device__ __forceinline__ bool fa_row_tile(uint32_t r_addr, int kvalid, float sl2, bool first, float& m_ref,
+                                            float& l, float& alpha) {
+  uint32_t r[kFaBK];
+  TMEM_LD32(r_addr, r);
+  TMEM_LD32(r_addr + 32, (r + 32));
+  TMEM_LD32(r_addr + 64, (r + 64));
+  tc_wait_ld();
+  if (MASKED) {
+#pragma unroll
+    for (int i = 0; i < kFaBK; ++i)
+      if (i >= kvalid) r[i] = __float_as_uint(-INFINITY);
+  }
+  float mx0 = fmax3f(__uint_as_float(r[0]), __uint_as_float(r[1]), __uint_as_float(r[2]));
+  float mx1 = fmax3f(__uint_as_float(r[3]), __uint_as_float(r[4]), __uint_as_float(r[5]));
+  float mx2 = fmax3f(__uint_as_float(r[6]), __uint_as_float(r[7]), __uint_as_float(r[8]));
+  float mx3 = fmax3f(__uint_as_float(r[9]), __uint_as_float(r[10]), __uint_as_float(r[11]));
+#pragma unroll
+  for (int i = 12; i < kFaBK; i += 8) {
+    mx0 = fmax3f(mx0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+    mx1 = fmax3f(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+    mx2 = fmax3f(mx2, __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+    mx3 = fmax3f(mx3, __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+  }
+  const float m_tile = fmax3f(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
+  bool resc = false;
+  alpha = 1.f;
+  if (m_tile > m_ref + kLazyMax) {  // always at the first key tile
+    alpha = ex2(m_ref - m_tile);
+    resc = !first;
+    m_ref = m_tile;
+    l *= alpha;
+  }
+  // the region's previous reader, P V(n - 2), completed before S(n) was written
+  const unsigned long long sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m_ref, -m_ref);
+  unsigned long long acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+  for (int c = 0; c < kFaBK / 16; ++c) {  // 16 keys (8 packed columns) per store
+    uint32_t pk[8];
+#pragma unroll
+    for (int u8 = 0; u8 < 2; ++u8) {
+      float pv[8];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const int i = 16 * c + 8 * u8 + e;
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2x2, negm2), x0, x1);
+        pv[e] = e < NPOLY ? exp2_poly3(x0) : ex2(x0);
+        pv[e + 1] = e + 1 < NPOLY ? exp2_poly3(x1) : ex2(x1);
+        if (MASKED) {
+          pv[e] = i < kvalid ? pv[e] : 0.f;
+          pv[e + 1] = i + 1 < kvalid ? pv[e + 1] : 0.f;
+        }
+      }
+      acc0 = f2_add(acc0, f2_add(f2_pack(pv[0], pv[1]), f2_pack(pv[4], pv[5])));
+      acc1 = f2_add(acc1, f2_add(f2_pack(pv[2], pv[3]), f2_pack(pv[6], pv[7])));
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pk[4 * u8 + e] = pack_h2(pv[2 * e], pv[2 * e + 1]);
+    }
+    TMEM_ST8(r_addr + 8 * c, pk);
+  }
+  float a0, a1, b0, b1;
+  f2_unpack(acc0, a0, a1);
+  f2_unpack(acc1, b0, b1);
+  l += (a0 + a1) + (b0 + b1);
+  return resc;
+}
+
 struct FaArgs {
   int heads, ntok, nwin;
   int q_col, k_col, v_col;
@@ -788,71 +865,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         tc_fence_after();
         const uint32_t r_addr = tmem + lane_off + (uint32_t)(192 * t + 96 * (n & 1));
         const int kvalid = a.ntok - j * kFaBK;  // keys at or past this count are padding
-        const bool full = kvalid >= kFaBK;
-        uint32_t r[kFaBK];
-        TMEM_LD32(r_addr, r);
-        TMEM_LD32(r_addr + 32, (r + 32));
-        TMEM_LD32(r_addr + 64, (r + 64));
-        tc_wait_ld();
-        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < kFaBK; i += 4) {
-          float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
-          float v2 = __uint_as_float(r[i + 2]), v3 = __uint_as_float(r[i + 3]);
-          if (!full) {
-            v0 = i < kvalid ? v0 : -INFINITY;
-            v1 = i + 1 < kvalid ? v1 : -INFINITY;
-            v2 = i + 2 < kvalid ? v2 : -INFINITY;
-            v3 = i + 3 < kvalid ? v3 : -INFINITY;
-          }
-          mx0 = fmaxf(mx0, v0);
-          mx1 = fmaxf(mx1, v1);
-          mx2 = fmaxf(mx2, v2);
-          mx3 = fmaxf(mx3, v3);
-        }
-        const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.sl2;
-        float alpha = 1.f;
-        bool resc = false;
-        if (m_tile > m_ref + kLazyMax) {  // always at the first key tile
-          alpha = ex2(m_ref - m_tile);
-          resc = j > 0;
-          m_ref = m_tile;
-          l *= alpha;
-        }
-        // p = 2^(s * sl2 - m_ref) (padding keys p = 0) as f16 pairs over the region's first 48 columns (this
-        // thread's scores are in registers; the region's previous reader, P V(n - 2), completed before
-        // S(n) was written), row sum
-        const unsigned long long sl2x2 = f2_pack(a.sl2, a.sl2), negm2 = f2_pack(-m_ref, -m_ref);
-        unsigned long long acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
-#pragma unroll
-        for (int c = 0; c < kFaBK / 16; ++c) {  // 16 keys (8 packed columns) per store
-          uint32_t pk[8];
-#pragma unroll
-          for (int u8 = 0; u8 < 2; ++u8) {
-            float pv[8];
-#pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              const int i = 16 * c + 8 * u8 + e;
-              float x0, x1;
-              f2_unpack(f2_fma(f2_pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2x2, negm2), x0, x1);
-              pv[e] = e < NPOLY ? exp2_poly3(x0) : ex2(x0);
-              pv[e + 1] = e + 1 < NPOLY ? exp2_poly3(x1) : ex2(x1);
-              if (!full) {
-                pv[e] = i < kvalid ? pv[e] : 0.f;
-                pv[e + 1] = i + 1 < kvalid ? pv[e + 1] : 0.f;
-              }
-            }
-            acc0 = f2_add(acc0, f2_add(f2_pack(pv[0], pv[1]), f2_pack(pv[4], pv[5])));
-            acc1 = f2_add(acc1, f2_add(f2_pack(pv[2], pv[3]), f2_pack(pv[6], pv[7])));
-#pragma unroll
-            for (int e = 0; e < 4; ++e) pk[4 * u8 + e] = pack_h2(pv[2 * e], pv[2 * e + 1]);
-          }
-          TMEM_ST8(r_addr + 8 * c, pk);
-        }
-        float a0, a1, b0, b1;
-        f2_unpack(acc0, a0, a1);
-        f2_unpack(acc1, b0, b1);
-        l += (a0 + a1) + (b0 + b1);
+        float alpha;
+        const bool resc = kvalid >= kFaBK ? fa_row_tile<false, NPOLY>(r_addr, kvalid, a.sl2, j == 0, m_ref, l, alpha)
+                                          : fa_row_tile<true, NPOLY>(r_addr, kvalid, a.sl2, j == 0, m_ref, l, alpha);
         // O_t current: the previous P V product of this tile has completed (also keeps this thread's walk
         // over the pv_done phases in order)
         if (j > 0 && !mbar_wait(&pv_done[t], (n - 1) & 1, s_abort, err, kErrWaitMisc)) ok = false;
