@@ -669,8 +669,9 @@ def main():
     ap.add_argument("--workload", default="vit_q4_0", choices=["vit_q4_0", "vit_q8_0", "vit_f16"])
     ap.add_argument("--frames", type=int, default=FRAMES_TOTAL, help="frames of the batch (split over the GPUs)")
     ap.add_argument("--frames-per-pass", type=int, default=8)
-    ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1, 2],
-                    help="256-row GEMM tiles on SM pairs: 1 (default) for K >= 2048, 2 for all, 0 never")
+    ap.add_argument("--gemm-pairs", type=int, default=2, choices=[0, 1, 2],
+                    help="256-row GEMM tiles on SM pairs: 2 (default) every wide GEMM, 1 K >= 2048 and the "
+                         "f16-output ones, 0 never")
     ap.add_argument("--weights-quantised", type=int, default=WEIGHTS_QUANTISED, choices=[0, 1, 2],
                     help="1 (default): block form in HBM, staged per layer; 2: dequantised inside the GEMM; "
                          "0: f16 at load")

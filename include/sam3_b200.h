@@ -65,16 +65,15 @@ int s3b_sync(s3b_ctx* ctx);
 /* Options: "frames_per_pass" (encoder micro-batch, default 8);
  * "attention_impl" (0: tcgen05 flash attention where eligible: for d = 64
  * the persistent kernel with two 128-query tiles per CTA (one thread per
- * query row, 96-key tiles) when the rows have at most 1152 keys (windows),
- * the one-tile-per-CTA kernel for longer rows (global blocks); 1: always the
+ * query row, 96-key tiles), windows and global rows alike; 1: always the
  * mma.sync kernel, 2: as 0 but d = 64 on the 64-key-tile tcgen05 kernel,
- * 3: as 0 but d = 64 on the one-tile kernel with P in shared memory instead
- * of TMEM, 4: d = 64 always on the persistent two-tile kernel);
+ * 3: as 0 but d = 64 on the one-tile-per-CTA kernel (two threads per query
+ * row, 128-key tiles), 4: the same as 0);
  * "attention_fa_exp_poly" (0-4, default 1: of every 8 exponentials of the
  * persistent two-tile kernel, how many are evaluated on the FMA pipe);
  * "gemm_pairs" (which wide GEMMs run 256-row tiles on pairs of SMs, tcgen05
- * cta_group::2: 1, default, those with K >= 2048 and the f16-output ones
- * with 16 epilogue warps; 2 all; 0 none, 128-row tiles on single SMs;
+ * cta_group::2: 2, default, all; 1 those with K >= 2048 and the f16-output
+ * ones with 16 epilogue warps; 0 none, 128-row tiles on single SMs;
  * applies to every context of the process);
  * "gemm_wide_epilogue" (1, default: GEMMs with K < 2048 run 16 epilogue
  * warps instead of 8; 0: all run 8; process-wide);

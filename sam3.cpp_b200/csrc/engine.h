@@ -305,8 +305,9 @@ struct s3b_ctx {
   std::set<void*> ipc_mapped;
   int max_frames_per_pass = 8;
   int stop_after_blocks = -1;  // test hook: run only the first n backbone blocks (-1: all)
-  int attention_impl = 0;      // 0: tcgen05 where eligible, 1: always mma.sync, 2: d = 64 on the wide tcgen05 kernel,
-                               // 3: as 0, d = 64 with P in shared memory
+  int attention_impl = 0;      // 0 (or 4): tcgen05 where eligible, d = 64 on the persistent two-tile kernel;
+                               // 1: always mma.sync; 2: d = 64 on the wide tcgen05 kernel; 3: d = 64 on the
+                               // one-tile-per-CTA kernel
   int weights_quantised = 0;   // q4_0 / q8_0 linear weights stay in block form in device memory: 1 each is
                                // dequantised into an f16 staging buffer (L2-resident) right before its GEMM,
                                // 2 the GEMM dequantises each weight tile in shared memory; 0 f16 at load

@@ -264,15 +264,16 @@ int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
                      p.k_h == 64 && p.v_h == 64 && kq > 0 && vq > 0 && kq + 64LL * p.heads <= p.q_n &&
                      vq + 64LL * p.heads <= p.q_n && batch_heads % p.heads == 0;
   int rc;
-  // d = 64: the persistent two-tile kernel for windows (few key tiles per query tile, where its persistence
-  // hides the per-tile prologue and epilogue), the one-tile-per-CTA kernel for the long global rows
-  const bool fa = tc_ok && (ctx->attention_impl == 4 || (ctx->attention_impl == 0 && p.nk <= 1152));
+  // d = 64: the persistent two-tile kernel (measured faster than the one-tile-per-CTA kernel for the
+  // ViT windows, 499 against 408 TF/s, and for the global rows, 680 against 667 TF/s); attention_impl 3
+  // selects the one-tile kernel
+  const bool fa = tc_ok && (ctx->attention_impl == 4 || ctx->attention_impl == 0);
   if (fa) {
     rc = attention_fa64(p.q, p.q_n, 0, (int)kq, (int)vq, p.heads, p.nq, batch_heads / p.heads, p.o, p.o_n, p.omap,
                         p.scale, ctx->attention_fa_exp_poly, ctx->d_err, ctx->stream);
   } else if (tc_ok) {
     rc = attention_tc64(p.q, p.q_n, 0, (int)kq, (int)vq, p.heads, p.nq, batch_heads / p.heads, p.o, p.o_n, p.omap,
-                        p.scale, ctx->attention_exp_poly, ctx->attention_impl == 3 ? 0 : 1, ctx->d_err,
+                        p.scale, ctx->attention_exp_poly, 1, ctx->d_err,
                         ctx->stream);
   } else {
     // d = 256 (memory attention) and d = 72 / 96 (Hiera) with at least one full query tile on the

@@ -68,7 +68,7 @@ def test_gemm_pairs_and_single(engine, wide, pairs, M, N, K, resid):
         err = (out.float() - ref).abs().max().item()
         assert err < 2e-3 * max(1.0, ref.abs().max().item()) + 1e-4 * K ** 0.5 + (0 if resid else 1e-2), err
     finally:
-        engine.set_option("gemm_pairs", 1)
+        engine.set_option("gemm_pairs", 2)  # the default
         engine.set_option("gemm_wide_epilogue", 1)
 
 
@@ -93,7 +93,7 @@ def test_gemm_f16_epilogue_warps(engine, pairs, wide, M, N, K, act):
         assert (out.float() - ref).abs().max().item() < 1e-2 * max(1.0, ref.abs().max().item())
     finally:
         engine.set_option("gemm_wide_epilogue", 1)
-        engine.set_option("gemm_pairs", 1)
+        engine.set_option("gemm_pairs", 2)  # the default
 
 
 @pytest.mark.parametrize("wide", [0, 1])
@@ -239,8 +239,8 @@ def _ref_attention_qkv(qkv, nwin, heads, ntok, d, scale):
                                                    (4, 2, 300, 72, 0), (2, 2, 256, 96, 32)])
 @pytest.mark.parametrize("impl", [0, 3, 4])
 def test_attention_qkv(engine, nwin, heads, ntok, d, pad, impl):
-    """impl 0: the d = 64 softmax splits each row over two warps; 3: P in shared memory; 4: one persistent
-    CTA per SM with two query tiles and one thread per query row."""
+    """impl 0 (and 4): one persistent CTA per SM with two query tiles and one thread per query row; 3: one
+    query tile per CTA, each row's softmax split over two warps."""
     g = torch.Generator(device="cuda").manual_seed(nwin * 1000 + heads * 10 + ntok)
     E = heads * d
     qkv = (torch.randn(nwin * ntok, 3 * E + pad, device="cuda", generator=g) * 1.5).half()
@@ -282,8 +282,8 @@ def test_attention_qkv_impls_agree(engine):
 
 @pytest.mark.parametrize("impl", [0, 3, 4])
 def test_attention_qkv_growing_max(engine, impl):
-    """Keys whose logits grow tile by tile, so the running reference max of the d = 64 kernel moves
-    after the first key tile and the running O rows are rescaled in TMEM (both softmax layouts)."""
+    """Keys whose logits grow tile by tile, so the running reference max of the d = 64 kernels moves
+    after the first key tile and the running O rows are rescaled in TMEM (both kernels)."""
     nwin, heads, ntok, d = 2, 4, 600, 64
     E = heads * d
     g = torch.Generator(device="cuda").manual_seed(21)
@@ -338,7 +338,7 @@ def test_conv3x3(engine, implicit, pairs, B, H, W, C, Cout):
         engine.sync()
     finally:
         engine.set_option("conv_implicit", 1)
-        engine.set_option("gemm_pairs", 1)
+        engine.set_option("gemm_pairs", 2)  # the default
     ref = torch.nn.functional.conv2d(x.float().permute(0, 3, 1, 2), w.float().permute(0, 3, 1, 2), bias, padding=1)
     ref = ref.permute(0, 2, 3, 1)
     err = (out - ref).abs().max().item()
@@ -364,7 +364,7 @@ def test_deconv2x2(engine, blocks, pairs, B, H, W, Cin, Cout, act, f32):
         engine.sync()
     finally:
         engine.set_option("conv_implicit", 1)
-        engine.set_option("gemm_pairs", 1)
+        engine.set_option("gemm_pairs", 2)  # the default
     # torch weight layout for conv_transpose2d: [Cin][Cout][kh][kw]
     wt = w.float().permute(3, 2, 0, 1).contiguous()
     ref = torch.nn.functional.conv_transpose2d(x.float().permute(0, 3, 1, 2), wt, bias, stride=2)

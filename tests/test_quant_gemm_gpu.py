@@ -53,7 +53,7 @@ def test_gemm_q_equals_f16_path(engine, qtype, M, N, K, resid, act):
         engine.gemm_q(A, raw, qtype, N, got, bias=bias, act=act, resid=got if resid else None)
         engine.sync()
     finally:
-        engine.set_option("gemm_pairs", 1)
+        engine.set_option("gemm_pairs", 2)  # the default
     assert torch.equal(got, want), (got.float() - want.float()).abs().max().item()
     ref = A.float() @ Bh.float().T + bias
     if act == 1:
