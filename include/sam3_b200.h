@@ -91,10 +91,12 @@ int s3b_sync(s3b_ctx* ctx);
  * "attention_exp_poly" (0-4: of every 8 softmax exponentials in the tcgen05
  * kernel, how many are evaluated by a polynomial on the FMA pipe instead of
  * the MUFU unit; a tuning knob, results agree to f16 rounding);
- * "graphs" (1, default: s3b_mem_attn replays its per-layer body from a CUDA
- * graph captured on the second call with the same shapes, buffers and
- * options, when the context's stream is not the legacy default stream and
- * profiling is off; 0: every launch issued from the host);
+ * "graphs" (1, default: s3b_mem_attn replays its per-layer body, and the
+ * s3b_encode_* calls their whole launch sequence, from a CUDA graph captured
+ * on the second call with the same shapes, input pointer, buffers and
+ * options, when the context's stream is not the legacy default stream,
+ * profiling is off and (encoder) no output is host-bound; 0: every launch
+ * issued from the host);
  * "stop_after_blocks" (test hook: run only the first n backbone blocks and
  * no neck, -1 = all; the stage runners of sam3.h:441-496 play this role in
  * the reference). */

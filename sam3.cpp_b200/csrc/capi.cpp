@@ -3,6 +3,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <functional>
 #include <string>
 #include <vector>
 
@@ -269,6 +270,70 @@ int encode_device_image_u8(s3b_ctx* ctx, const uint8_t* d_u8, int n_frames, int 
   return encode_device_chw(ctx, chw->as<float>(), n_frames, S, flags);
 }
 
+constexpr size_t kMaxEncGraphs = 8;
+
+// Runs one encoder call (`body`: all of its work on the context stream) eagerly, or replays it from a
+// CUDA graph. An encoder call is a few hundred launches of a fixed sequence; from the second call with
+// the same key (`key` + the option epoch, the GEMM configuration and the DevBuf generation, so every
+// pointer the launches hold is unchanged) the sequence is captured once and replayed, which removes the
+// host launch work and most of the gaps between kernels (the batch-1 latency). Calls with profiling on,
+// with host-bound outputs (their per-pass copies run on a second stream), behind pending output copies or
+// on the legacy default stream stay eager, and so does a key whose capture failed.
+int run_encode(s3b_ctx* ctx, std::vector<uintptr_t> key, const std::function<int()>& body) {
+  if (!ctx->graphs || ctx->prof || !ctx->stream || !ctx->host_bind.empty()) return body();
+  // output copies of an earlier host-bound call still pending: the eager call orders itself after them
+  for (char pending : ctx->copy_pending)
+    if (pending) return body();
+  key.push_back((uintptr_t)ctx->graph_epoch);
+  key.push_back((uintptr_t)gemm_config_id());
+  key.push_back((uintptr_t)devbuf_generation().load());
+  auto& G = ctx->enc_graphs;
+  auto it = std::find_if(G.begin(), G.end(), [&](const s3b_ctx::EncGraph& g) { return g.key == key; });
+  if (it == G.end()) {
+    if (G.size() >= kMaxEncGraphs) {
+      if (G.front().exec) cudaGraphExecDestroy(G.front().exec);
+      G.erase(G.begin());
+    }
+    G.push_back(s3b_ctx::EncGraph());
+    G.back().key = key;
+    it = G.end() - 1;
+  } else if (it != G.end() - 1) {
+    std::rotate(it, it + 1, G.end());  // most recently used last
+    it = G.end() - 1;
+  }
+  s3b_ctx::EncGraph& g = *it;
+  if (!g.exec && g.seen >= 1) {
+    const long long n0 = ctx->n_launches;
+    cudaGraph_t graph = nullptr;
+    bool ok = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+    const int brc = ok ? body() : kOk;
+    if (ok) ok = cudaStreamEndCapture(ctx->stream, &graph) == cudaSuccess && brc == kOk;
+    cudaGraphExec_t exec = nullptr;
+    if (ok) ok = cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();  // a failed capture leaves its error here; the eager run below reports real faults
+    const long long captured = ctx->n_launches - n0;
+    ctx->n_launches = n0;  // nothing ran during the capture
+    // the capture is valid only if the body allocated nothing (a DevBuf growing inside it fails the
+    // capture anyway; this also covers one that was released)
+    if (ok && (uintptr_t)devbuf_generation().load() == key.back()) {
+      g.exec = exec;
+      g.launches = captured;
+    } else {
+      if (exec) cudaGraphExecDestroy(exec);
+      g.seen = -(1 << 30);  // not capturable: stay eager for this key
+    }
+  }
+  if (g.exec) {
+    if (cudaGraphLaunch(g.exec, ctx->stream) != cudaSuccess)
+      return set_error(ctx, kErrCuda, "encoder graph launch failed");
+    count_launch(ctx, (int)g.launches);
+    return check_device(ctx, "encoder graph");
+  }
+  ++g.seen;
+  return body();
+}
+
 }  // namespace
 
 namespace s3b {
@@ -366,6 +431,9 @@ void s3b_destroy(s3b_ctx* ctx) {
   for (cudaEvent_t e : ctx->copy_done) cudaEventDestroy(e);
   if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
   if (ctx->ma_exec) cudaGraphExecDestroy(ctx->ma_exec);
+  for (auto& g : ctx->enc_graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+  ctx->enc_graphs.clear();
   for (void* p : ctx->ipc_mapped) cudaIpcCloseMemHandle(p);
   ctx->ipc_mapped.clear();
   ctx->user_allocs.clear();
@@ -628,7 +696,8 @@ int s3b_encode_u8(s3b_ctx* ctx, const uint8_t* frames, int n_frames, int img_siz
   if (!frames || n_frames <= 0 || img_size <= 0) return set_error(ctx, kErrArg, "bad arguments");
   uint8_t* d = nullptr;
   if ((rc = stage_host(ctx, frames, (size_t)n_frames * img_size * img_size * 3, "frames_u8", &d))) return rc;
-  return encode_device_u8(ctx, d, n_frames, img_size, flags);
+  return run_encode(ctx, {1, (uintptr_t)d, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
+                    [&] { return encode_device_u8(ctx, d, n_frames, img_size, flags); });
 }
 
 int s3b_encode_image_u8(s3b_ctx* ctx, const uint8_t* frames, int n_frames, int width, int height, int flags) {
@@ -637,7 +706,8 @@ int s3b_encode_image_u8(s3b_ctx* ctx, const uint8_t* frames, int n_frames, int w
   if (!frames || n_frames <= 0 || width <= 0 || height <= 0) return set_error(ctx, kErrArg, "bad arguments");
   uint8_t* d = nullptr;
   if ((rc = stage_host(ctx, frames, (size_t)n_frames * width * height * 3, "frames_u8", &d))) return rc;
-  return encode_device_image_u8(ctx, d, n_frames, width, height, flags);
+  return run_encode(ctx, {2, (uintptr_t)d, (uintptr_t)n_frames, (uintptr_t)width, (uintptr_t)height, (uintptr_t)flags},
+                    [&] { return encode_device_image_u8(ctx, d, n_frames, width, height, flags); });
 }
 
 int s3b_encode_image_u8_device(s3b_ctx* ctx, const uint8_t* d_frames, int n_frames, int width, int height,
@@ -645,7 +715,9 @@ int s3b_encode_image_u8_device(s3b_ctx* ctx, const uint8_t* d_frames, int n_fram
   int rc = ctx_enter(ctx);
   if (rc) return rc;
   if (!d_frames) return set_error(ctx, kErrArg, "null frames");
-  return encode_device_image_u8(ctx, d_frames, n_frames, width, height, flags);
+  return run_encode(ctx,
+                    {2, (uintptr_t)d_frames, (uintptr_t)n_frames, (uintptr_t)width, (uintptr_t)height, (uintptr_t)flags},
+                    [&] { return encode_device_image_u8(ctx, d_frames, n_frames, width, height, flags); });
 }
 
 int s3b_encode_chw(s3b_ctx* ctx, const float* chw, int n_frames, int img_size, int flags) {
@@ -654,21 +726,24 @@ int s3b_encode_chw(s3b_ctx* ctx, const float* chw, int n_frames, int img_size, i
   if (!chw || n_frames <= 0 || img_size <= 0) return set_error(ctx, kErrArg, "bad arguments");
   float* d = nullptr;
   if ((rc = stage_host(ctx, chw, (size_t)n_frames * 3 * img_size * img_size, "frames_chw_in", &d))) return rc;
-  return encode_device_chw(ctx, d, n_frames, img_size, flags);
+  return run_encode(ctx, {3, (uintptr_t)d, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
+                    [&] { return encode_device_chw(ctx, d, n_frames, img_size, flags); });
 }
 
 int s3b_encode_u8_device(s3b_ctx* ctx, const uint8_t* d_frames, int n_frames, int img_size, int flags) {
   int rc = ctx_enter(ctx);
   if (rc) return rc;
   if (!d_frames) return set_error(ctx, kErrArg, "null frames");
-  return encode_device_u8(ctx, d_frames, n_frames, img_size, flags);
+  return run_encode(ctx, {1, (uintptr_t)d_frames, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
+                    [&] { return encode_device_u8(ctx, d_frames, n_frames, img_size, flags); });
 }
 
 int s3b_encode_chw_device(s3b_ctx* ctx, const float* d_chw, int n_frames, int img_size, int flags) {
   int rc = ctx_enter(ctx);
   if (rc) return rc;
   if (!d_chw) return set_error(ctx, kErrArg, "null frames");
-  return encode_device_chw(ctx, d_chw, n_frames, img_size, flags);
+  return run_encode(ctx, {3, (uintptr_t)d_chw, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
+                    [&] { return encode_device_chw(ctx, d_chw, n_frames, img_size, flags); });
 }
 
 int s3b_output_shape(s3b_ctx* ctx, const char* name, int64_t ne[4]) {

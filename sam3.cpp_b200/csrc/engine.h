@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <map>
 #include <memory>
 #include <set>
@@ -94,6 +95,13 @@ int parse_hparams_array(int is_sam2, const int32_t* v, int n, HParams& hp, std::
 void tensor_to_f32(const FileTensor& t, std::vector<float>& out);
 
 // ---------------------------------------------------------------- device memory
+// Counts every allocation and release of a DevBuf in the process: a CUDA graph captured while the
+// count had one value holds only pointers that are still valid while it has that value.
+inline std::atomic<long long>& devbuf_generation() {
+  static std::atomic<long long> g{0};
+  return g;
+}
+
 struct DevBuf {
   void* p = nullptr;
   size_t bytes = 0;
@@ -102,7 +110,10 @@ struct DevBuf {
   DevBuf& operator=(const DevBuf&) = delete;
   ~DevBuf() { release(); }
   void release() {
-    if (p) cudaFree(p);
+    if (p) {
+      cudaFree(p);
+      ++devbuf_generation();
+    }
     p = nullptr;
     bytes = 0;
   }
@@ -114,6 +125,7 @@ struct DevBuf {
       p = nullptr;
       return kErrOOM;
     }
+    ++devbuf_generation();
     bytes = n;
     return 0;
   }
@@ -321,6 +333,16 @@ struct s3b_ctx {
   std::vector<uintptr_t> ma_key;  // shapes, buffers, epoch and kernel choices the graph was captured with
   long long ma_launches = 0;      // kernel launches inside the graph
   int ma_seen = 0;                // eager calls with ma_key so far (the graph is captured on the second)
+  // encoder calls replayed from CUDA graphs (capi.cpp run_encode): one per key (entry point, input
+  // pointer, frame count and size, flags, option epoch, GEMM configuration, DevBuf generation), most
+  // recently used last
+  struct EncGraph {
+    std::vector<uintptr_t> key;
+    cudaGraphExec_t exec = nullptr;
+    long long launches = 0;  // kernel launches inside the graph
+    int seen = 0;            // eager calls with this key so far (the graph is captured on the second)
+  };
+  std::vector<EncGraph> enc_graphs;
   // launch accounting + optional per-kernel CUDA-event timing (s3b_profile_*)
   long long n_launches = 0;
   bool prof = false;
