@@ -507,6 +507,358 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
   }
 }
 
+// ---------------------------------------------------------------- d = 256 with 128-key tiles (memory attention)
+// The d = 256 products on the kernel above issue 20 MMAs per 64 keys, 16 of them N = 64 (S = Q K^T over
+// d = 256 in K = 16 steps); this kernel takes 128-key tiles, so S runs N = 128 and each 128 keys cost 24
+// MMAs (16 for S, 8 for P V with N = 256) instead of 40. P goes back to TMEM over the scores it came from
+// (the A operand of P V), which frees the shared memory for one 128-key K tile and one V tile (64 KB each)
+// beside the 64 KB Q tile. TMEM (512 columns): S / P regions r = 0, 1 at 128 r (S_j in region j & 1), O at
+// 256. 7 warps:
+//   warp 0     TMA: the Q tile, then K_j (four 64-column boxes of 128 rows) once S_{j-1} has read K_{j-1}
+//   warp 6     TMA: V_j once P V_{j-1} has read V_{j-1}
+//   warp 1     MMA: S_0, S_1, then per key tile j: O += P_j V_j (A = P_j from TMEM), S_{j+2}. S_{j+2}
+//              rewrites the region P_j was read from; the MMAs of one thread execute in order.
+//   warps 2-5  softmax, one query row per thread (TMEM lane): the row's 128 scores in registers, row max,
+//              lazy reference max (moved only when the row max grows by more than 2^8, then the sum and
+//              the O row are rescaled once P V_{j-1} has completed), p = 2^(s * scale * log2 e - m) as f16
+//              pairs over the region's first 64 columns; at the end O / sum, or with key splits the
+//              unnormalised O, m and sum for the combine kernel.
+constexpr int kB2 = 128;                    // keys per tile
+constexpr uint32_t kAtom2 = 128 * 128;      // 16 KB: 128 rows x 128 B
+constexpr uint32_t kTile2 = 4 * kAtom2;     // 64 KB: Q, K or V tile (four 64-column atoms)
+constexpr int kThreads2 = 224;
+constexpr size_t kSmem2 = 1024 + 3 * (size_t)kTile2 + 16 * 8 + 16;
+
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// MN-major SW128 V operand of 128 key rows: SBO = 1024 B between 8-key groups, LBO = 16 KB between the
+// 64-wide d atoms.
+__device__ __forceinline__ uint64_t sdesc_mn_v128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(kAtom2 >> 4) << 16;  // LBO
+  d |= (uint64_t)(1024u >> 4) << 32;   // SBO
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+#define TMEM_ST32W(taddr, R)                                                                                 \
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "                                               \
+               "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"                                    \
+               "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),             \
+               "r"(R[0]), "r"(R[1]), "r"(R[2]), "r"(R[3]), "r"(R[4]), "r"(R[5]), "r"(R[6]), "r"(R[7]),       \
+               "r"(R[8]), "r"(R[9]), "r"(R[10]), "r"(R[11]), "r"(R[12]), "r"(R[13]), "r"(R[14]), "r"(R[15]), \
+               "r"(R[16]), "r"(R[17]), "r"(R[18]), "r"(R[19]), "r"(R[20]), "r"(R[21]), "r"(R[22]),           \
+               "r"(R[23]), "r"(R[24]), "r"(R[25]), "r"(R[26]), "r"(R[27]), "r"(R[28]), "r"(R[29]),           \
+               "r"(R[30]), "r"(R[31])                                                                        \
+               : "memory")
+
+// One 128-key tile of one query row: scores from the region at r_addr, row max, lazy reference max,
+// P as f16 pairs over the region's first 64 columns, row sum added to l. MASKED: keys at or past kvalid
+// are padding (p = 0). Returns true when the reference max moved after the first tile.
+template <bool MASKED>
+__device__ __forceinline__ bool row_tile128(uint32_t r_addr, int kvalid, float sl2, bool first, float& m_ref,
+                                            float& l, float& alpha) {
+  uint32_t r[kB2];
+  TMEM_LD32(r_addr, r);
+  TMEM_LD32(r_addr + 32, (r + 32));
+  TMEM_LD32(r_addr + 64, (r + 64));
+  TMEM_LD32(r_addr + 96, (r + 96));
+  tc_wait_ld();
+  if (MASKED) {
+#pragma unroll
+    for (int i = 0; i < kB2; ++i)
+      if (i >= kvalid) r[i] = __float_as_uint(-INFINITY);
+  }
+  float mx0 = __uint_as_float(r[0]), mx1 = __uint_as_float(r[1]), mx2 = __uint_as_float(r[2]),
+        mx3 = __uint_as_float(r[3]);
+#pragma unroll
+  for (int i = 4; i < kB2 - 4; i += 8) {
+    mx0 = fmax3f(mx0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+    mx1 = fmax3f(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+    mx2 = fmax3f(mx2, __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+    mx3 = fmax3f(mx3, __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+  }
+  mx0 = fmax3f(mx0, __uint_as_float(r[kB2 - 4]), __uint_as_float(r[kB2 - 3]));
+  mx1 = fmax3f(mx1, __uint_as_float(r[kB2 - 2]), __uint_as_float(r[kB2 - 1]));
+  const float m_tile = fmax3f(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
+  bool resc = false;
+  alpha = 1.f;
+  if (m_tile > m_ref + kLazyMax) {  // always at the first key tile
+    alpha = ex2(m_ref - m_tile);
+    resc = !first;
+    m_ref = m_tile;
+    l *= alpha;
+  }
+  const unsigned long long sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m_ref, -m_ref);
+  unsigned long long acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+  for (int c = 0; c < kB2 / 64; ++c) {  // 64 keys (32 packed columns) per store
+    uint32_t pk[32];
+#pragma unroll
+    for (int u8 = 0; u8 < 8; ++u8) {
+      float pv[8];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const int i = 64 * c + 8 * u8 + e;
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2x2, negm2), x0, x1);
+        pv[e] = ex2(x0);
+        pv[e + 1] = ex2(x1);
+        if (MASKED) {
+          pv[e] = i < kvalid ? pv[e] : 0.f;
+          pv[e + 1] = i + 1 < kvalid ? pv[e + 1] : 0.f;
+        }
+      }
+      acc0 = f2_add(acc0, f2_add(f2_pack(pv[0], pv[1]), f2_pack(pv[4], pv[5])));
+      acc1 = f2_add(acc1, f2_add(f2_pack(pv[2], pv[3]), f2_pack(pv[6], pv[7])));
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pk[4 * u8 + e] = pack_h2(pv[2 * e], pv[2 * e + 1]);
+    }
+    TMEM_ST32W(r_addr + 32 * c, pk);
+  }
+  float a0, a1, b0, b1;
+  f2_unpack(acc0, a0, a1);
+  f2_unpack(acc1, b0, b1);
+  l += (a0 + a1) + (b0 + b1);
+  return resc;
+}
+
+__global__ void __launch_bounds__(kThreads2, 1)
+    attn256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tv, WideArgs a, int* err) {
+  constexpr int D = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTile2;
+  uint8_t* sV = sK + kTile2;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kTile2);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 2;
+  uint64_t* v_full = bars + 3;
+  uint64_t* v_empty = bars + 4;
+  uint64_t* s_full = bars + 5;    // [2]: S_j in region j & 1
+  uint64_t* p_full = bars + 7;    // P_j written (4 softmax warps)
+  uint64_t* pv_done = bars + 8;   // P V_j completed
+  uint64_t* o_done = bars + 9;
+  uint64_t* mma_done = bars + 10;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 11);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned unit = gridDim.x - 1 - blockIdx.x;
+  const int n_qt = (a.nq + kBQ - 1) / kBQ;
+  const int qb = (int)(unit % (unsigned)n_qt);
+  const int rest = (int)(unit / (unsigned)n_qt);
+  const int split = rest % a.n_split;
+  const int bh = rest / a.n_split;
+  const int b = bh / a.heads, h = bh - b * a.heads;
+  const int rb = a.head_rows ? bh : b;
+  const int hc = a.head_rows ? 0 : h;
+  const int j0 = split * a.tiles_per;
+  const int nkb = min((a.nk + kB2 - 1) / kB2 - j0, a.tiles_per);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(k_full, 1);
+    mbar_init(k_empty, 1);
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(o_done, 1);
+    mbar_init(mma_done, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0 || warp == 6) {
+    if (lane == 0) {
+      // warp 0: Q, then K_j; warp 6: V_j. A slot is refilled once the product that read it completed.
+      const bool is_k = warp == 0;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      uint8_t* dst = is_k ? sK : sV;
+      const CUtensorMap* map = is_k ? &tk : &tv;
+      const int col0 = hc * (is_k ? a.k_h : a.v_h);
+      if (is_k) {
+        mbar_arrive_expect_tx(q_full, kTile2);
+#pragma unroll
+        for (int at = 0; at < 4; ++at) tma_load_3d(&tq, q_full, sQ + at * kAtom2, hc * a.q_h + at * 64, qb * kBQ, rb);
+      }
+      int armed = -1;
+      for (int j = 0; j < nkb; ++j) {
+        if (!mbar_wait(empty, ((uint32_t)j & 1) ^ 1, s_abort, err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(full, kTile2);
+#pragma unroll
+        for (int at = 0; at < 4; ++at) tma_load_3d(map, full, dst + at * kAtom2, col0 + at * 64, (j0 + j) * kB2, rb);
+        armed = j;
+      }
+      // no copy may still be landing when the CTA exits
+      if (is_k) mbar_wait_drain(q_full, 0, err);
+      if (armed >= 0) mbar_wait_drain(full, (uint32_t)armed & 1, err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16(kBQ, kB2, 0);             // Q, K both K-major
+      constexpr uint32_t idesc_o = idesc_f16(kBQ, D, 0) | (1u << 16);  // B (V) MN-major
+      bool ok = mbar_wait(q_full, 0, s_abort, err, kErrWaitFull);
+      tc_fence_after();
+      const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK), va = smem_u32(sV);
+      bool issued = false;
+      auto issue_s = [&](int j) -> bool {
+        if (!mbar_wait(k_full, (uint32_t)j & 1, s_abort, err, kErrWaitFull)) return false;
+        tc_fence_after();
+        const uint32_t sa = tmem + (uint32_t)((j & 1) * kB2);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * kAtom2 + (kk & 3) * 32);
+          tc_mma_f16(sa, sdesc_k_sw128(qa + off), sdesc_k_sw128(ka + off), idesc_s, kk != 0);
+        }
+        tc_commit(&s_full[j & 1]);
+        tc_commit(k_empty);
+        issued = true;
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && nkb > 1) ok = issue_s(1);
+      for (int j = 0; j < nkb && ok; ++j) {
+        if (!mbar_wait(p_full, (uint32_t)j & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
+        if (!mbar_wait(v_full, (uint32_t)j & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t pa = tmem + (uint32_t)((j & 1) * kB2);
+        const int nk16 = min(kB2 / 16, (a.nk - (j0 + j) * kB2 + 15) / 16);  // K steps holding a real key
+#pragma unroll
+        for (int kk = 0; kk < kB2 / 16; ++kk) {
+          if (kk >= nk16) break;
+          tc_mma_f16_ts(tmem + 256, pa + (uint32_t)(kk * 8), sdesc_mn_v128(va + (uint32_t)(kk * 2048)), idesc_o,
+                        (j > 0 || kk != 0) ? 1u : 0u);
+        }
+        tc_commit(pv_done);
+        tc_commit(v_empty);
+        if (j + 2 < nkb && !issue_s(j + 2)) { ok = false; break; }
+      }
+      if (ok) tc_commit(o_done);
+      if (issued) {
+        tc_commit(mma_done);
+        mbar_wait_drain(mma_done, 0, err);
+      }
+    }
+  } else {
+    // softmax: warp w owns TMEM lanes 32*(w%4) .. +31 (query rows)
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const bool rows_live = qb * kBQ + q4 * 32 < a.nq;  // else only the barrier protocol
+    const uint32_t o_addr = tmem + lane_off + 256;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      if (!mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1, s_abort, err, kErrWaitTmemFull)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int kvalid = a.nk - (j0 + j) * kB2;
+      const uint32_t r_addr = tmem + lane_off + (uint32_t)((j & 1) * kB2);
+      float alpha = 1.f;
+      bool resc = false;
+      if (rows_live)
+        resc = kvalid >= kB2 ? row_tile128<false>(r_addr, kvalid, a.sl2, j == 0, m_ref, l, alpha)
+                             : row_tile128<true>(r_addr, kvalid, a.sl2, j == 0, m_ref, l, alpha);
+      // O current: P V_{j-1} has completed (also keeps this thread's walk over the pv_done phases in order;
+      // P V_j needs this tile's P_j, so the barrier is never two phases ahead)
+      if (j > 0 && !mbar_wait(pv_done, (uint32_t)(j - 1) & 1, s_abort, err, kErrWaitMisc)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      if (rows_live && __any_sync(0xffffffffu, resc)) {
+        const float f = resc ? alpha : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          uint32_t o[32];
+          TMEM_LD32(o_addr + (uint32_t)c, o);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          TMEM_ST32W(o_addr + (uint32_t)c, o);
+        }
+      }
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok) ok = mbar_wait(o_done, 0, s_abort, err, kErrWaitMisc);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok && rows_live) {
+      tc_fence_after();
+      const int qi = qb * kBQ + row;
+      if (a.n_split > 1) {
+        const size_t pidx = ((size_t)bh * a.n_split + split) * a.nq + qi;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 16) {
+          uint32_t o[16];
+          TMEM_LD16(o_addr + (uint32_t)c, o);
+          tc_wait_ld();
+          if (qi < a.nq) {
+            float4* op = reinterpret_cast<float4*>(a.ws_o + pidx * D + c);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              op[u] = make_float4(__uint_as_float(o[4 * u]), __uint_as_float(o[4 * u + 1]),
+                                  __uint_as_float(o[4 * u + 2]), __uint_as_float(o[4 * u + 3]));
+          }
+        }
+        if (qi < a.nq) *reinterpret_cast<float2*>(a.ws_ml + pidx * 2) = make_float2(m_ref, l);
+      } else {
+        const long long orow = qi < a.nq ? map_row(a.omap, (long long)b * a.nq + qi) : -1;
+        const float inv = 1.0f / l;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 16) {
+          uint32_t o[16];
+          TMEM_LD16(o_addr + (uint32_t)c, o);
+          tc_wait_ld();
+          if (orow >= 0) {
+            uint4* op = reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * D + c);
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+              op[u] = make_uint4(pack_h2(__uint_as_float(o[8 * u]) * inv, __uint_as_float(o[8 * u + 1]) * inv),
+                                 pack_h2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv),
+                                 pack_h2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv),
+                                 pack_h2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv));
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // Merges the key splits of each query row: M = max of the splits' reference
 // maxima, O = sum_s 2^(m_s - M) O_s, l = sum_s 2^(m_s - M) l_s, out = O / l
 // (f16). One warp per row.
@@ -598,10 +950,12 @@ int launch_wide(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes
     kc = (long long)(p.heads - 1) * p.k_h + D;
     vc = (long long)(p.heads - 1) * p.v_h + D;
   }
+  // d = 256 runs the 128-key-tile kernel (attn256_kernel)
+  constexpr int BK = D == 256 ? kB2 : kBK;
   CUtensorMap tq, tk, tv;
   int rc = map3(enc, &tq, p.q, qc, p.q_n, qb, p.nq, blocks, kBQ);
-  if (!rc) rc = map3(enc, &tk, p.k, kc, p.k_n, kb, p.nk, blocks, kBK);
-  if (!rc) rc = map3(enc, &tv, p.v, vc, p.v_n, vb, p.nk, blocks, kBK);
+  if (!rc) rc = map3(enc, &tk, p.k, kc, p.k_n, kb, p.nk, blocks, BK);
+  if (!rc) rc = map3(enc, &tv, p.v, vc, p.v_n, vb, p.nk, blocks, BK);
   if (rc) return rc;
   WideArgs a;
   a.heads = p.heads;
@@ -620,7 +974,7 @@ int launch_wide(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes
   const int n_qt = (p.nq + kBQ - 1) / kBQ;
   const long long units = (long long)n_qt * batch_heads;
   const long long slots = (long long)num_sms() * C::MinBlocks;
-  const int nkb = (p.nk + kBK - 1) / kBK;
+  const int nkb = (p.nk + BK - 1) / BK;
   int n_split = 1;
   if (ws && units < slots) n_split = (int)std::max(1LL, std::min(slots / units, (long long)nkb / 4));
   int tiles_per = (nkb + n_split - 1) / n_split;
@@ -633,11 +987,16 @@ int launch_wide(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes
   a.tiles_per = tiles_per;
   a.ws_o = ws;
   a.ws_ml = ws ? ws + (size_t)n_split * batch_heads * p.nq * D : nullptr;
-  static_assert(C::Smem <= 232448, "shared memory per CTA");
-  if (kernel_setup(attn_wide_kernel<D>, (size_t)C::Smem) <= 0) return -13;
+  static_assert(C::Smem <= 232448 && kSmem2 <= 232448, "shared memory per CTA");
   const long long n_cta = units * n_split;
   if (n_cta > 0x7fffffffLL) return -2;
-  attn_wide_kernel<D><<<(unsigned)n_cta, kThreads, C::Smem, st>>>(tq, tk, tv, a, err);
+  if (D == 256) {
+    if (kernel_setup(attn256_kernel, kSmem2) <= 0) return -13;
+    attn256_kernel<<<(unsigned)n_cta, kThreads2, kSmem2, st>>>(tq, tk, tv, a, err);
+  } else {
+    if (kernel_setup(attn_wide_kernel<D>, (size_t)C::Smem) <= 0) return -13;
+    attn_wide_kernel<D><<<(unsigned)n_cta, kThreads, C::Smem, st>>>(tq, tk, tv, a, err);
+  }
   int rc2 = launch_status("attention_wide");
   if (rc2 || n_split == 1) return rc2;
   const long long rows = (long long)batch_heads * p.nq;

@@ -304,6 +304,25 @@ def test_attention_qkv_growing_max(engine, impl):
     assert (out.float() - ref).abs().max().item() < 3e-2
 
 
+@pytest.mark.parametrize("nq,nk", [(4096, 1100), (300, 777)])
+def test_attention_d256_growing_max(engine, nq, nk):
+    """d = 256 (memory attention): keys whose logits grow tile by tile, so the reference max moves after
+    the first 128-key tile and the O rows are rescaled in TMEM; with 4096 queries the keys are also split
+    over CTAs and merged by the combine kernel."""
+    g = torch.Generator(device="cuda").manual_seed(nq + nk)
+    q = torch.randn(1, 1, nq, 256, device="cuda", generator=g) * 0.5
+    k = torch.randn(1, 1, nk, 256, device="cuda", generator=g) * 0.5
+    k *= (1.0 + torch.arange(nk, device="cuda").float() / 96.0).view(1, 1, nk, 1)
+    v = torch.randn(1, 1, nk, 256, device="cuda", generator=g)
+    q, k, v = q.half(), k.half(), v.half()
+    out = torch.empty(1, nq, 256, device="cuda", dtype=torch.float16)
+    engine.attention(q, k, v, out, 1.0 / 16)
+    engine.sync()
+    ref = torch.softmax((q.float() @ k.float().transpose(-1, -2)) / 16, dim=-1) @ v.float()
+    assert torch.isfinite(out).all()
+    assert (out.float() - ref.reshape(1, nq, 256)).abs().max().item() < 3e-2
+
+
 @pytest.mark.parametrize("rows,C,f32", [(5184, 1024, 0), (1000, 96, 1), (37, 256, 0), (64, 1152, 1), (5000, 144, 0),
                                         (777, 192, 1), (301, 288, 0), (129, 576, 1), (65, 64, 0), (33, 80, 1),
                                         (70001, 96, 0)])
