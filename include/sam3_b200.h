@@ -69,6 +69,10 @@ int s3b_sync(s3b_ctx* ctx);
  * mma.sync kernel, 2: as 0 but d = 64 on the 64-key-tile tcgen05 kernel,
  * 3: as 0 but d = 64 on the one-tile-per-CTA kernel (two threads per query
  * row, 128-key tiles), 4: the same as 0);
+ * "attention_wide_k128" (-1, default: d = 72 / 96 attention over rows of at
+ * least 1024 keys, the Hiera global blocks, on the 128-key-tile tcgen05
+ * kernel, shorter rows on the 64-key-tile kernel with two CTAs per SM; 1
+ * always the 128-key kernel; 0 never; d = 256 always uses it);
  * "attention_fa_exp_poly" (0-4, default 1: of every 8 exponentials of the
  * persistent two-tile kernel, how many are evaluated on the FMA pipe);
  * "gemm_pairs" (which wide GEMMs run 256-row tiles on pairs of SMs, tcgen05
@@ -429,7 +433,9 @@ int s3b_op_gemm_rope(s3b_ctx* ctx, const void* A, int64_t lda, const void* B, in
 
 /* softmax(q k^T * scale) v for q [B*H][nq][d], k/v [B*H][nk][d] (f16),
  * out [B][nq][H*d] f16. Replaces ggml_flash_attn_ext (sam3.cpp:3774, 4395,
- * 9267, 9312) with no mask. d in {64, 80, 96, 128, 256}. */
+ * 9267, 9312) with no mask. d in {64, 72, 80, 96, 128, 256}; the engine's
+ * dispatch picks the kernel (tcgen05 for d = 256, and for d = 72 / 96 with at
+ * least 128 queries; mma.sync otherwise). */
 int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, void* out, int batch, int heads,
                      int nq, int nk, int d, float scale);
 

@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
   }
 }
 
-// ---------------------------------------------------------------- d = 256 with 128-key tiles (memory attention)
+// ---------------------------------------------------------------- 128-key tiles (d = 256; d = 72 / 96 as an option)
 // The d = 256 products on the kernel above issue 20 MMAs per 64 keys, 16 of them N = 64 (S = Q K^T over
 // d = 256 in K = 16 steps); this kernel takes 128-key tiles, so S runs N = 128 and each 128 keys cost 24
 // MMAs (16 for S, 8 for P V with N = 256) instead of 40. P goes back to TMEM over the scores it came from
@@ -525,9 +525,14 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
 //              unnormalised O, m and sum for the combine kernel.
 constexpr int kB2 = 128;                    // keys per tile
 constexpr uint32_t kAtom2 = 128 * 128;      // 16 KB: 128 rows x 128 B
-constexpr uint32_t kTile2 = 4 * kAtom2;     // 64 KB: Q, K or V tile (four 64-column atoms)
 constexpr int kThreads2 = 224;
-constexpr size_t kSmem2 = 1024 + 3 * (size_t)kTile2 + 16 * 8 + 16;
+template <int D>
+struct Cfg2 {
+  static constexpr int DK = WideCfg<D>::DK;         // K of Q K^T and N of P V (d rounded up to 16)
+  static constexpr int NA = WideCfg<D>::NA;         // 64-column atoms per row
+  static constexpr uint32_t Tile = NA * kAtom2;     // Q, K or V tile of 128 rows
+  static constexpr size_t Smem = 1024 + 3 * (size_t)Tile + 16 * 8 + 16;
+};
 
 __device__ __forceinline__ float fmax3f(float a, float b, float c) {
   float r;
@@ -629,10 +634,14 @@ __device__ __forceinline__ bool row_tile128(uint32_t r_addr, int kvalid, float s
   return resc;
 }
 
+template <int D>
 __global__ void __launch_bounds__(kThreads2, 1)
-    attn256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                   const __grid_constant__ CUtensorMap tv, WideArgs a, int* err) {
-  constexpr int D = 256;
+    attn128k_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, WideArgs a, int* err) {
+  using C = Cfg2<D>;
+  constexpr int DK = C::DK, NA = C::NA;
+  constexpr uint32_t kTile2 = C::Tile;
+  constexpr bool kPadQ = DK > D;  // Q columns [D, DK) must read as zero (d = 72)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem;
@@ -649,7 +658,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
   uint64_t* pv_done = bars + 8;   // P V_j completed
   uint64_t* o_done = bars + 9;
   uint64_t* mma_done = bars + 10;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* q_ready = bars + 11;  // Q padding columns zeroed (d = 72)
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -677,6 +687,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     mbar_init(pv_done, 1);
     mbar_init(o_done, 1);
     mbar_init(mma_done, 1);
+    mbar_init(q_ready, 4);
     *s_abort = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -705,14 +716,14 @@ __global__ void __launch_bounds__(kThreads2, 1)
       if (is_k) {
         mbar_arrive_expect_tx(q_full, kTile2);
 #pragma unroll
-        for (int at = 0; at < 4; ++at) tma_load_3d(&tq, q_full, sQ + at * kAtom2, hc * a.q_h + at * 64, qb * kBQ, rb);
+        for (int at = 0; at < NA; ++at) tma_load_3d(&tq, q_full, sQ + at * kAtom2, hc * a.q_h + at * 64, qb * kBQ, rb);
       }
       int armed = -1;
       for (int j = 0; j < nkb; ++j) {
         if (!mbar_wait(empty, ((uint32_t)j & 1) ^ 1, s_abort, err, kErrWaitEmpty)) break;
         mbar_arrive_expect_tx(full, kTile2);
 #pragma unroll
-        for (int at = 0; at < 4; ++at) tma_load_3d(map, full, dst + at * kAtom2, col0 + at * 64, (j0 + j) * kB2, rb);
+        for (int at = 0; at < NA; ++at) tma_load_3d(map, full, dst + at * kAtom2, col0 + at * 64, (j0 + j) * kB2, rb);
         armed = j;
       }
       // no copy may still be landing when the CTA exits
@@ -721,9 +732,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_f16(kBQ, kB2, 0);             // Q, K both K-major
-      constexpr uint32_t idesc_o = idesc_f16(kBQ, D, 0) | (1u << 16);  // B (V) MN-major
-      bool ok = mbar_wait(q_full, 0, s_abort, err, kErrWaitFull);
+      constexpr uint32_t idesc_s = idesc_f16(kBQ, kB2, 0);              // Q, K both K-major
+      constexpr uint32_t idesc_o = idesc_f16(kBQ, DK, 0) | (1u << 16);  // B (V) MN-major
+      bool ok = mbar_wait(kPadQ ? q_ready : q_full, 0, s_abort, err, kErrWaitFull);
       tc_fence_after();
       const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK), va = smem_u32(sV);
       bool issued = false;
@@ -732,7 +743,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         tc_fence_after();
         const uint32_t sa = tmem + (uint32_t)((j & 1) * kB2);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
+        for (int kk = 0; kk < DK / 16; ++kk) {
           const uint32_t off = (uint32_t)((kk >> 2) * kAtom2 + (kk & 3) * 32);
           tc_mma_f16(sa, sdesc_k_sw128(qa + off), sdesc_k_sw128(ka + off), idesc_s, kk != 0);
         }
@@ -774,6 +785,20 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const uint32_t o_addr = tmem + lane_off + 256;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
+    if constexpr (kPadQ) {
+      // zero this row's Q columns [D, DK) (one 16-byte unit of the last atom)
+      ok = mbar_wait(q_full, 0, s_abort, err, kErrWaitFull);
+      if (ok) {
+        constexpr int col = D % 64;  // first padding column inside its atom
+        static_assert(DK - D == 8 && col % 8 == 0, "d = 72-like padding: one 16-byte unit");
+        uint8_t* qrow = sQ + (D / 64) * kAtom2 + row * 128;
+        *reinterpret_cast<uint4*>(qrow + (((col >> 3) ^ (row & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+      ok = __all_sync(0xffffffffu, ok);
+    }
     for (int j = 0; j < nkb && ok; ++j) {
       if (!mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1, s_abort, err, kErrWaitTmemFull)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
@@ -795,13 +820,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
       if (rows_live && __any_sync(0xffffffffu, resc)) {
         const float f = resc ? alpha : 1.f;
 #pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
-          uint32_t o[32];
-          TMEM_LD32(o_addr + (uint32_t)c, o);
+        for (int c = 0; c < DK; c += 16) {
+          uint32_t o[16];
+          TMEM_LD16(o_addr + (uint32_t)c, o);
           tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-          TMEM_ST32W(o_addr + (uint32_t)c, o);
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          TMEM_ST16(o_addr + (uint32_t)c, o);
         }
       }
       tc_wait_st();
@@ -817,7 +842,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       if (a.n_split > 1) {
         const size_t pidx = ((size_t)bh * a.n_split + split) * a.nq + qi;
 #pragma unroll 1
-        for (int c = 0; c < D; c += 16) {
+        for (int c = 0; c < DK; c += 16) {
           uint32_t o[16];
           TMEM_LD16(o_addr + (uint32_t)c, o);
           tc_wait_ld();
@@ -825,8 +850,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
             float4* op = reinterpret_cast<float4*>(a.ws_o + pidx * D + c);
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-              op[u] = make_float4(__uint_as_float(o[4 * u]), __uint_as_float(o[4 * u + 1]),
-                                  __uint_as_float(o[4 * u + 2]), __uint_as_float(o[4 * u + 3]));
+              if (c + 4 * u < D)
+                op[u] = make_float4(__uint_as_float(o[4 * u]), __uint_as_float(o[4 * u + 1]),
+                                    __uint_as_float(o[4 * u + 2]), __uint_as_float(o[4 * u + 3]));
           }
         }
         if (qi < a.nq) *reinterpret_cast<float2*>(a.ws_ml + pidx * 2) = make_float2(m_ref, l);
@@ -834,7 +860,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const long long orow = qi < a.nq ? map_row(a.omap, (long long)b * a.nq + qi) : -1;
         const float inv = 1.0f / l;
 #pragma unroll 1
-        for (int c = 0; c < D; c += 16) {
+        for (int c = 0; c < DK; c += 16) {
           uint32_t o[16];
           TMEM_LD16(o_addr + (uint32_t)c, o);
           tc_wait_ld();
@@ -842,6 +868,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
             uint4* op = reinterpret_cast<uint4*>(a.o + orow * a.o_n + h * D + c);
 #pragma unroll
             for (int u = 0; u < 2; ++u)
+              if (c + 8 * u < D)
               op[u] = make_uint4(pack_h2(__uint_as_float(o[8 * u]) * inv, __uint_as_float(o[8 * u + 1]) * inv),
                                  pack_h2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv),
                                  pack_h2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv),
@@ -918,7 +945,8 @@ int map3(EncodeTiledFn enc, CUtensorMap* m, const __half* x, long long cols, lon
 }
 
 template <int D>
-int launch_wide(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes, int* err, cudaStream_t st) {
+int launch_wide(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes, int bk128, int* err,
+                cudaStream_t st) {
   using C = WideCfg<D>;
   EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!enc) return -10;
@@ -950,8 +978,9 @@ int launch_wide(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes
     kc = (long long)(p.heads - 1) * p.k_h + D;
     vc = (long long)(p.heads - 1) * p.v_h + D;
   }
-  // d = 256 runs the 128-key-tile kernel (attn256_kernel)
-  constexpr int BK = D == 256 ? kB2 : kBK;
+  // d = 256 runs the 128-key-tile kernel, d = 72 / 96 when `bk128` is set
+  const bool k128 = D == 256 || (bk128 && (D == 72 || D == 96));
+  const int BK = k128 ? kB2 : kBK;
   CUtensorMap tq, tk, tv;
   int rc = map3(enc, &tq, p.q, qc, p.q_n, qb, p.nq, blocks, kBQ);
   if (!rc) rc = map3(enc, &tk, p.k, kc, p.k_n, kb, p.nk, blocks, BK);
@@ -973,7 +1002,7 @@ int launch_wide(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes
   // 32 tiles on 148 SMs), keeping at least 4 key tiles per split and no split empty
   const int n_qt = (p.nq + kBQ - 1) / kBQ;
   const long long units = (long long)n_qt * batch_heads;
-  const long long slots = (long long)num_sms() * C::MinBlocks;
+  const long long slots = (long long)num_sms() * (k128 ? 1 : C::MinBlocks);
   const int nkb = (p.nk + BK - 1) / BK;
   int n_split = 1;
   if (ws && units < slots) n_split = (int)std::max(1LL, std::min(slots / units, (long long)nkb / 4));
@@ -987,12 +1016,12 @@ int launch_wide(const AttnParams& p, int batch_heads, float* ws, size_t ws_bytes
   a.tiles_per = tiles_per;
   a.ws_o = ws;
   a.ws_ml = ws ? ws + (size_t)n_split * batch_heads * p.nq * D : nullptr;
-  static_assert(C::Smem <= 232448 && kSmem2 <= 232448, "shared memory per CTA");
+  static_assert(C::Smem <= 232448 && Cfg2<D>::Smem <= 232448, "shared memory per CTA");
   const long long n_cta = units * n_split;
   if (n_cta > 0x7fffffffLL) return -2;
-  if (D == 256) {
-    if (kernel_setup(attn256_kernel, kSmem2) <= 0) return -13;
-    attn256_kernel<<<(unsigned)n_cta, kThreads2, kSmem2, st>>>(tq, tk, tv, a, err);
+  if (k128) {
+    if (kernel_setup(attn128k_kernel<D>, Cfg2<D>::Smem) <= 0) return -13;
+    attn128k_kernel<D><<<(unsigned)n_cta, kThreads2, Cfg2<D>::Smem, st>>>(tq, tk, tv, a, err);
   } else {
     if (kernel_setup(attn_wide_kernel<D>, (size_t)C::Smem) <= 0) return -13;
     attn_wide_kernel<D><<<(unsigned)n_cta, kThreads, C::Smem, st>>>(tq, tk, tv, a, err);
@@ -1015,13 +1044,13 @@ int attention_wide_max_split(int d, long long units) {
   return units < slots ? (int)(slots / units) : 1;
 }
 
-int attention_wide(const AttnParams& p, int d, int batch_heads, float* ws, size_t ws_bytes, int* err,
+int attention_wide(const AttnParams& p, int d, int batch_heads, float* ws, size_t ws_bytes, int bk128, int* err,
                    cudaStream_t st) {
   switch (d) {
-    case 64: return launch_wide<64>(p, batch_heads, ws, ws_bytes, err, st);
-    case 72: return launch_wide<72>(p, batch_heads, ws, ws_bytes, err, st);
-    case 96: return launch_wide<96>(p, batch_heads, ws, ws_bytes, err, st);
-    case 256: return launch_wide<256>(p, batch_heads, ws, ws_bytes, err, st);
+    case 64: return launch_wide<64>(p, batch_heads, ws, ws_bytes, bk128, err, st);
+    case 72: return launch_wide<72>(p, batch_heads, ws, ws_bytes, bk128, err, st);
+    case 96: return launch_wide<96>(p, batch_heads, ws, ws_bytes, bk128, err, st);
+    case 256: return launch_wide<256>(p, batch_heads, ws, ws_bytes, bk128, err, st);
     default: return -2;
   }
 }

@@ -543,6 +543,11 @@ int s3b_set_option(s3b_ctx* ctx, const char* key, int64_t value) {
     ctx->conv_implicit = (int)value;
     return kOk;
   }
+  if (k == "attention_wide_k128") {
+    if (value < -1 || value > 1) return set_error(ctx, kErrArg, "attention_wide_k128 must be -1, 0 or 1");
+    ctx->attention_wide_k128 = (int)value;
+    return kOk;
+  }
   if (k == "attention_fa_exp_poly") {
     if (value < 0 || value > 4) return set_error(ctx, kErrArg, "attention_fa_exp_poly must be in [0, 4]");
     ctx->attention_fa_exp_poly = (int)value;
@@ -1189,9 +1194,8 @@ int s3b_op_attention(s3b_ctx* ctx, const void* q, const void* k, const void* v, 
   p.nk = nk;
   p.o_n = (long long)heads * d;
   p.scale = scale;
-  rc = attention(p, d, batch * heads, ctx->stream);
-  if (rc) return set_error(ctx, launcher_status_code(rc), "attention launch failed (%d)", rc);
-  return kOk;
+  // the engine's own dispatch (tcgen05 kernels where their layout rules hold, else mma.sync)
+  return run_attn(ctx, p, d, batch * heads);
 }
 
 int s3b_op_attention_qkv(s3b_ctx* ctx, const void* qkv, int64_t ld, void* out, int64_t ld_out, int nwin, int heads,

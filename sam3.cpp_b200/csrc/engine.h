@@ -326,6 +326,7 @@ struct s3b_ctx {
   int conv_implicit = 1;       // pixel-block GEMMs: implicit 3x3 convs, TMA-stored deconvs (0: im2col / scatter)
   int attention_exp_poly = 0;  // of every 8 softmax exponentials in the tcgen05 kernel, how many use the FMA pipe
   int attention_fa_exp_poly = 1;  // the same for the persistent two-tile d = 64 kernel
+  int attention_wide_k128 = -1;   // d = 72 / 96 on the 128-key-tile kernel: 1 always, 0 never, -1 rows of >= 1024 keys
   // memory attention: its per-layer body replayed from a CUDA graph (mem_attn.cpp)
   int graphs = 1;               // option "graphs"
   long long graph_epoch = 0;    // bumped by every option change and model load: cached graphs are stale

@@ -137,7 +137,9 @@ int attention_fa64(const __half* base, long long ld, int q_col, int k_col, int v
 // several CTAs whose partial results (in `ws`: attention_wide_ws_bytes(d,
 // n_split, ...) bytes for n_split up to attention_wide_max_split(d, query
 // tiles x batch_heads)) a second kernel merges; ws = NULL disables splitting.
-int attention_wide(const AttnParams& p, int d, int batch_heads, float* ws, size_t ws_bytes, int* err,
+// d = 256 runs 128-key tiles with P in TMEM; d = 72 / 96 too when bk128 is set (else 64-key tiles, two
+// CTAs per SM).
+int attention_wide(const AttnParams& p, int d, int batch_heads, float* ws, size_t ws_bytes, int bk128, int* err,
                    cudaStream_t st);
 size_t attention_wide_ws_bytes(int d, int n_split, int batch_heads, int nq);
 int attention_wide_max_split(int d, long long units);

@@ -293,7 +293,11 @@ int run_attn(s3b_ctx* ctx, const AttnParams& p, int D, int batch_heads) {
         if (brc) return brc;
         ws = buf->as<float>();
       }
-      rc = attention_wide(p, D, batch_heads, ws, ws_bytes, ctx->d_err, ctx->stream);
+      // d = 72 / 96: 128-key tiles for long rows (the Hiera global blocks: 4096 keys, measured 560 -> 674
+      // TF/s at d = 96, 410 -> 449 at d = 72), 64-key tiles and two CTAs per SM for the windows (196 / 256
+      // keys: 208 against 140 TF/s at d = 96)
+      const int k128 = ctx->attention_wide_k128 >= 0 ? ctx->attention_wide_k128 : (p.nk >= 1024 ? 1 : 0);
+      rc = attention_wide(p, D, batch_heads, ws, ws_bytes, k128, ctx->d_err, ctx->stream);
     }
     if (rc == -2) rc = attention(p, D, batch_heads, ctx->stream);
   }

@@ -304,6 +304,34 @@ def test_attention_qkv_growing_max(engine, impl):
     assert (out.float() - ref).abs().max().item() < 3e-2
 
 
+@pytest.mark.parametrize("D", [72, 96])
+@pytest.mark.parametrize("k128", [0, 1])
+def test_attention_wide_key_tiles(engine, D, k128):
+    """d = 72 / 96 on both tcgen05 kernels (option attention_wide_k128): 64-key tiles with two CTAs per SM and
+    128-key tiles with P in TMEM, heads as column offsets of a fused qkv buffer (Hiera) and as row blocks,
+    ragged query and key counts (the last 128-key tile masked), key splits."""
+    engine.set_option("attention_wide_k128", k128)
+    try:
+        nwin, heads, ntok = 2, 3, 1300
+        g = torch.Generator(device="cuda").manual_seed(D + 7 * k128)
+        E = heads * D
+        qkv = (torch.randn(nwin * ntok, 3 * E, device="cuda", generator=g) * 1.5).half()
+        out = torch.empty(nwin * ntok, E, device="cuda", dtype=torch.float16)
+        engine.attention_qkv(qkv, out, nwin, heads, ntok, D, D ** -0.5)
+        engine.sync()
+        assert (out.float() - _ref_attention_qkv(qkv, nwin, heads, ntok, D, D ** -0.5)).abs().max().item() < 2e-2
+        q = torch.randn(1, 2, 4096, D, device="cuda", generator=g).half()
+        k = torch.randn(1, 2, 1500, D, device="cuda", generator=g).half()
+        v = torch.randn(1, 2, 1500, D, device="cuda", generator=g).half()
+        o = torch.empty(1, 4096, 2 * D, device="cuda", dtype=torch.float16)
+        engine.attention(q, k, v, o, D ** -0.5)
+        engine.sync()
+        ref = torch.softmax((q.float() @ k.float().transpose(-1, -2)) * D ** -0.5, dim=-1) @ v.float()
+        assert (o.float() - ref.permute(0, 2, 1, 3).reshape(1, 4096, 2 * D)).abs().max().item() < 2e-2
+    finally:
+        engine.set_option("attention_wide_k128", -1)
+
+
 @pytest.mark.parametrize("nq,nk", [(4096, 1100), (300, 777)])
 def test_attention_d256_growing_max(engine, nq, nk):
     """d = 256 (memory attention): keys whose logits grow tile by tile, so the reference max moves after
