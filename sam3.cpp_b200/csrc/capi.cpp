@@ -226,30 +226,23 @@ int stage_host(s3b_ctx* ctx, const T* host, size_t n, const char* name, T** dev)
   return kOk;
 }
 
-// SAM 3 normalisation (p/255 - 0.5)/0.5 (sam3.cpp:3505-3511); SAM 2 ImageNet mean/std (3519-3520).
-const float kMeanSam3[3] = {0.5f, 0.5f, 0.5f}, kStdSam3[3] = {0.5f, 0.5f, 0.5f};
-const float kMeanSam2[3] = {0.485f, 0.456f, 0.406f}, kStdSam2[3] = {0.229f, 0.224f, 0.225f};
-
-int encode_device_chw(s3b_ctx* ctx, const float* d_chw, int n_frames, int img_size, int flags) {
+// d_u8 (uint8 HWC frames at the model size) instead of d_chw: the preprocessing (sam3_preprocess_image /
+// sam2_preprocess_image, sam3.cpp:3486-3544, normalisation only) runs inside the patch-column kernel.
+int encode_device_chw(s3b_ctx* ctx, const float* d_chw, int n_frames, int img_size, int flags,
+                      const uint8_t* d_u8 = nullptr) {
   if (!ctx->model.loaded) return set_error(ctx, kErrState, "no model loaded");
   if (n_frames <= 0) return set_error(ctx, kErrArg, "n_frames must be > 0");
   if (img_size != ctx->model.hp.img_size)
     return set_error(ctx, kErrUnsupported, "img_size %d != model img_size %d (resize is done by the caller)", img_size,
                      ctx->model.hp.img_size);
-  return ctx->model.hp.is_sam2 ? hiera_encode(ctx, d_chw, n_frames, flags) : vit_encode(ctx, d_chw, n_frames, flags);
+  return ctx->model.hp.is_sam2 ? hiera_encode(ctx, d_chw, n_frames, flags, d_u8)
+                               : vit_encode(ctx, d_chw, n_frames, flags, d_u8);
 }
 
 int encode_device_u8(s3b_ctx* ctx, const uint8_t* d_u8, int n_frames, int img_size, int flags) {
   if (!ctx->model.loaded) return set_error(ctx, kErrState, "no model loaded");
   if (n_frames <= 0 || img_size <= 0) return set_error(ctx, kErrArg, "bad frame count / size");
-  int rc = 0;
-  DevBuf* chw = ctx->buf("frames_chw", (size_t)n_frames * 3 * img_size * img_size * 4, &rc);
-  if (rc) return rc;
-  const bool sam2 = ctx->model.hp.is_sam2 != 0;
-  rc = preprocess_u8(d_u8, n_frames, img_size, img_size, sam2 ? kMeanSam2 : kMeanSam3, sam2 ? kStdSam2 : kStdSam3,
-                     chw->as<float>(), ctx->stream);
-  if (rc) return set_error(ctx, kErrCuda, "preprocess launch failed");
-  return encode_device_chw(ctx, chw->as<float>(), n_frames, img_size, flags);
+  return encode_device_chw(ctx, nullptr, n_frames, img_size, flags, d_u8);
 }
 
 // Frames of any size: resized on the device to the model size and normalised in the same pass

@@ -120,43 +120,62 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
   }
 }
 
-// One thread per 8 consecutive columns of an output row (one 16-byte store):
-// 32-bit index math once per thread, then (ci, ky, kx) advance column by
-// column without divisions; consecutive threads take consecutive column
-// groups, so their reads run along the input rows.
-__global__ void im2col_image_kernel(const float* __restrict__ img, int B, int Cin, int H, int W, int k, int stride,
-                                    int pad, int OH, int OW, __half* __restrict__ out, int Kpad) {
-  const int vpr = Kpad >> 3;  // 8-column groups per output row
-  const int total = B * OH * OW * vpr;
-  const int K = Cin * k * k, kk = k * k, ohw = OH * OW;
-  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
-    const int row = t / vpr, v = t - row * vpr;
-    const int b = row / ohw, pix = row - b * ohw;
-    const int oy = pix / OW, ox = pix - oy * OW;
-    const int iy0 = oy * stride - pad, ix0 = ox * stride - pad;
-    const int col0 = v * 8;
-    int ci = col0 / kk;
-    const int rem = col0 - ci * kk;
-    int ky = rem / k, kx = rem - ky * k;
-    float val[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      val[e] = 0.f;
-      const int iy = iy0 + ky, ix = ix0 + kx;
-      if (col0 + e < K && iy >= 0 && iy < H && ix >= 0 && ix < W)
-        val[e] = __ldg(img + (((long long)b * Cin + ci) * H + iy) * (long long)W + ix);
-      if (++kx == k) {
-        kx = 0;
-        if (++ky == k) {
-          ky = 0;
-          ++ci;
+// Patch columns of the image convolutions (ViT 14x14 / s14, Hiera 7x7 / s4 / p3) staged through shared
+// memory: one block per (frame, output row). The block first writes the k input rows its patches read (all
+// channels, f16, zeros for the padding; from the f32 CHW planes, or with U8 straight from the uint8 HWC frame
+// with the preprocessing's normalisation in f32, (p / 255 - mean) / std), then its OW x Kpad
+// slab of the column matrix, which is contiguous, in consecutive 16-byte stores. Column = (ci*k + ky)*k + kx.
+template <bool U8>
+__global__ void __launch_bounds__(256) patch_cols_kernel(const void* __restrict__ src, int Cin, int H, int W, int k,
+                                                         int stride, int pad, int OH, int OW, __half* __restrict__ out,
+                                                         int Kpad, float m0, float m1, float m2, float s0, float s1,
+                                                         float s2) {
+  extern __shared__ uint8_t pc_smem[];
+  const int Wp = (OW - 1) * stride + k;  // input columns the row's patches span, from ix = -pad
+  __half* rows = reinterpret_cast<__half*>(pc_smem);            // [Cin][k][Wp]
+  int* coff = reinterpret_cast<int*>(pc_smem + (((size_t)Cin * k * Wp * 2 + 15) & ~(size_t)15));  // [Kpad]
+  const int b = blockIdx.x / OH, oy = blockIdx.x - b * OH;
+  const int K = Cin * k * k;
+  for (int c = threadIdx.x; c < Kpad; c += blockDim.x) {
+    if (c < K) {
+      const int ci = c / (k * k), r = c - ci * k * k, ky = r / k, kx = r - ky * k;
+      coff[c] = (ci * k + ky) * Wp + kx;
+    } else {
+      coff[c] = -1;
+    }
+  }
+  for (int r = 0; r < Cin * k; ++r) {
+    const int ci = r / k, ky = r - ci * k;
+    const int iy = oy * stride - pad + ky;
+    __half* dst = rows + (size_t)r * Wp;
+    for (int xx = threadIdx.x; xx < Wp; xx += blockDim.x) {
+      const int ix = xx - pad;
+      float v = 0.f;
+      if (iy >= 0 && iy < H && ix >= 0 && ix < W) {
+        if (U8) {
+          const float p = (float)reinterpret_cast<const uint8_t*>(src)[(((size_t)b * H + iy) * W + ix) * 3 + ci];
+          v = ci == 0 ? (p / 255.0f - m0) / s0 : ci == 1 ? (p / 255.0f - m1) / s1 : (p / 255.0f - m2) / s2;
+        } else {
+          v = reinterpret_cast<const float*>(src)[(((size_t)b * Cin + ci) * H + iy) * W + ix];
         }
       }
+      dst[xx] = __float2half_rn(v);
     }
-    __half2 h[4];
+  }
+  __syncthreads();
+  const int vpr = Kpad >> 3;
+  uint4* o = reinterpret_cast<uint4*>(out + ((size_t)b * OH + oy) * OW * Kpad);
+  const __half zero = __float2half_rn(0.f);
+  for (int t = threadIdx.x; t < OW * vpr; t += blockDim.x) {
+    const int ox = t / vpr, v = t - ox * vpr;
+    const int base = ox * stride;
+    __half h[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(val[2 * e], val[2 * e + 1]);
-    *reinterpret_cast<uint4*>(out + (long long)row * Kpad + col0) = *reinterpret_cast<const uint4*>(h);
+    for (int e = 0; e < 8; ++e) {
+      const int off = coff[8 * v + e];
+      h[e] = off >= 0 ? rows[off + base] : zero;
+    }
+    o[t] = *reinterpret_cast<const uint4*>(h);
   }
 }
 
@@ -240,20 +259,6 @@ __global__ void qpool_kernel(const __half* __restrict__ q, long long ld, long lo
 #pragma unroll
     for (int e = 0; e < 4; ++e) ho[e] = __hmax2(__hmax2(ha[e], hb[e]), __hmax2(hc[e], hd[e]));
     *reinterpret_cast<uint4*>(out + t * C + c8 * 8) = o;
-  }
-}
-
-__global__ void preprocess_kernel(const uint8_t* __restrict__ img, int B, int H, int W, float m0, float m1, float m2,
-                                  float s0, float s1, float s2, float* __restrict__ out) {
-  const long long total = (long long)B * H * W;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const long long b = i / ((long long)H * W);
-    const long long pix = i - b * H * W;
-    const uint8_t* p = img + i * 3;
-    const long long plane = (long long)H * W;
-    out[(b * 3 + 0) * plane + pix] = ((float)p[0] / 255.0f - m0) / s0;
-    out[(b * 3 + 1) * plane + pix] = ((float)p[1] / 255.0f - m1) / s1;
-    out[(b * 3 + 2) * plane + pix] = ((float)p[2] / 255.0f - m2) / s2;
   }
 }
 
@@ -530,13 +535,36 @@ int layernorm(const float* x, long long ldx, void* y, int y_f32, long long ldy, 
   return launch_ok();
 }
 
-int im2col_image(const float* img, int B, int Cin, int H, int W, int k, int stride, int pad, int OH, int OW,
-                 __half* out, int Kpad, cudaStream_t st) {
-  if (Kpad < Cin * k * k || Kpad % 8 || (reinterpret_cast<uintptr_t>(out) & 15)) return -1;
-  const long long n = (long long)B * OH * OW * (Kpad / 8);  // threads: one per 8 output columns
-  if (n > 0x7fffffffLL) return -1;
-  im2col_image_kernel<<<grid_for(n, 256), 256, 0, st>>>(img, B, Cin, H, W, k, stride, pad, OH, OW, out, Kpad);
+static size_t patch_cols_smem(int Cin, int k, int stride, int OW, int Kpad) {
+  const size_t Wp = (size_t)(OW - 1) * stride + k;
+  return (((size_t)Cin * k * Wp * 2 + 15) & ~(size_t)15) + (size_t)Kpad * 4;
+}
+
+template <bool U8>
+static int launch_patch_cols(const void* src, int B, int Cin, int H, int W, int k, int stride, int pad, int OH, int OW,
+                             __half* out, int Kpad, const float* mean, const float* stdv, cudaStream_t st) {
+  if (Kpad < Cin * k * k || Kpad % 8 || (reinterpret_cast<uintptr_t>(out) & 15) || B <= 0 || OH <= 0 || OW <= 0 ||
+      (U8 && Cin != 3))
+    return -1;
+  if ((long long)B * OH > 0x7fffffffLL) return -1;
+  const size_t smem = patch_cols_smem(Cin, k, stride, OW, Kpad);
+  if (smem > 232448) return -1;
+  // the opt-in limit once per device (models with other patch sizes need other amounts)
+  if (kernel_setup(patch_cols_kernel<U8>, 232448) <= 0) return -13;
+  patch_cols_kernel<U8><<<(unsigned)(B * OH), 256, smem, st>>>(
+      src, Cin, H, W, k, stride, pad, OH, OW, out, Kpad, U8 ? mean[0] : 0.f, U8 ? mean[1] : 0.f, U8 ? mean[2] : 0.f,
+      U8 ? stdv[0] : 1.f, U8 ? stdv[1] : 1.f, U8 ? stdv[2] : 1.f);
   return launch_ok();
+}
+
+int patch_cols_f32(const float* img, int B, int Cin, int H, int W, int k, int stride, int pad, int OH, int OW,
+                   __half* out, int Kpad, cudaStream_t st) {
+  return launch_patch_cols<false>(img, B, Cin, H, W, k, stride, pad, OH, OW, out, Kpad, nullptr, nullptr, st);
+}
+
+int patch_cols_u8(const uint8_t* hwc, int B, int H, int W, const float mean[3], const float stdv[3], int k, int stride,
+                  int pad, int OH, int OW, __half* out, int Kpad, cudaStream_t st) {
+  return launch_patch_cols<true>(hwc, B, 3, H, W, k, stride, pad, OH, OW, out, Kpad, mean, stdv, st);
 }
 
 int im2col_3x3_cl(const __half* x, int B, int H, int W, int C, __half* out, cudaStream_t st) {
@@ -565,14 +593,6 @@ int qpool_windows(const __half* q, long long ld, long long nwin, int ws, int C, 
   if (C % 8 || ld % 8) return -1;
   const long long n = nwin * (ws / 2) * (ws / 2) * (C / 8);
   qpool_kernel<<<grid_for(n, 256), 256, 0, st>>>(q, ld, nwin, ws, C, out);
-  return launch_ok();
-}
-
-int preprocess_u8(const uint8_t* img, int B, int H, int W, const float mean[3], const float stdv[3], float* out,
-                  cudaStream_t st) {
-  const long long n = (long long)B * H * W;
-  preprocess_kernel<<<grid_for(n, 256), 256, 0, st>>>(img, B, H, W, mean[0], mean[1], mean[2], stdv[0], stdv[1],
-                                                      stdv[2], out);
   return launch_ok();
 }
 

@@ -446,7 +446,12 @@ int track_step_run(s3b_ctx* ctx, int H, const float* trk0, const float* trk1, co
                    float* mask_out, float* scores_out, float* mem_out, float* ptr_out);
 
 // encoders
-int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);
-int hiera_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags);
+// The backbone input is the f32 CHW batch d_chw, or, when d_u8 is given, the uint8 HWC frames themselves,
+// normalised inside the patch-column kernel (the preprocessing fused into the first launch).
+int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags, const uint8_t* d_u8 = nullptr);
+int hiera_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags, const uint8_t* d_u8 = nullptr);
+// SAM 3 normalisation (p/255 - 0.5)/0.5 (sam3.cpp:3505-3511); SAM 2 ImageNet mean/std (3519-3520).
+constexpr float kMeanSam3[3] = {0.5f, 0.5f, 0.5f}, kStdSam3[3] = {0.5f, 0.5f, 0.5f};
+constexpr float kMeanSam2[3] = {0.485f, 0.456f, 0.406f}, kStdSam2[3] = {0.229f, 0.224f, 0.225f};
 
 }  // namespace s3b

@@ -148,7 +148,7 @@ static int hiera_block(s3b_ctx* ctx, const HieraBlock& B0, int F, int S, float* 
   return kOk;
 }
 
-int hiera_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
+int hiera_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags, const uint8_t* d_u8) {
   Model& M = ctx->model;
   const HParams& hp = M.hp;
   const int E0 = hp.hiera_embed_dim, S0 = hp.img_size / 4, img = hp.img_size;
@@ -212,8 +212,12 @@ int hiera_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
     const long long T0 = (long long)F * S0 * S0;
     if ((rc = outputs_pass_begin(ctx, f0 / FB, FB))) return rc;
     // patch embed: conv 7x7 / s4 / p3 + bias, + PE (sam3.cpp:4469-4490)
-    CKH(im2col_image(d_chw + (size_t)f0 * 3 * img * img, F, 3, img, img, 7, 4, 3, S0, S0, col->as<__half>(), Kp,
-                     ctx->stream));
+    if (d_u8)
+      CKH(patch_cols_u8(d_u8 + (size_t)f0 * img * img * 3, F, img, img, kMeanSam2, kStdSam2, 7, 4, 3, S0, S0,
+                        col->as<__half>(), Kp, ctx->stream));
+    else
+      CKH(patch_cols_f32(d_chw + (size_t)f0 * 3 * img * img, F, 3, img, img, 7, 4, 3, S0, S0, col->as<__half>(), Kp,
+                         ctx->stream));
     EpiParams pe = epi_store(M.hpatch, xa->p, 1, E0);
     pe.resid = M.hiera_pe->as<float>();
     pe.ldr = E0;

@@ -150,10 +150,15 @@ void* tensor_map_encoder();
 int layernorm(const float* x, long long ldx, void* y, int y_f32, long long ldy, long long rows, int C,
               const float* gamma, const float* beta, float eps, const RowMap& map, cudaStream_t st);
 
-// im2col for a stride-s convolution over an f32 CHW image batch [B][3][H][W]:
-// out f16 [B*OH*OW][Kpad], column = (ci*k + ky)*k + kx, zeros beyond K.
-int im2col_image(const float* img, int B, int Cin, int H, int W, int k, int stride, int pad, int OH, int OW,
-                 __half* out, int Kpad, cudaStream_t st);
+// Patch columns of a stride-s image convolution over an f32 CHW batch [B][Cin][H][W]: out f16
+// [B*OH*OW][Kpad], column = (ci*k + ky)*k + kx, zeros beyond K; staged through shared memory, one block
+// per (frame, output row). patch_cols_u8 reads uint8 HWC frames and applies the preprocessing's
+// normalisation (p / 255 - mean) / std in f32 first (sam3_preprocess_image / sam2_preprocess_image,
+// sam3.cpp:3486-3544), so it gives the bits of normalising into f32 CHW and then taking the columns.
+int patch_cols_f32(const float* img, int B, int Cin, int H, int W, int k, int stride, int pad, int OH, int OW,
+                   __half* out, int Kpad, cudaStream_t st);
+int patch_cols_u8(const uint8_t* hwc, int B, int H, int W, const float mean[3], const float stdv[3], int k, int stride,
+                  int pad, int OH, int OW, __half* out, int Kpad, cudaStream_t st);
 
 // im2col for a 3x3 / pad 1 / stride 1 convolution over channel-last f16
 // maps [B][H][W][C]: out [B*H*W][9*C], column = (ky*3 + kx)*C + ci.
@@ -167,13 +172,9 @@ int maxpool2_cl_f32(const float* x, int B, int H, int W, int C, float* y, cudaSt
 // q (row stride ld elements, C channels) -> out [nwin][(ws/2)^2][C] contiguous.
 int qpool_windows(const __half* q, long long ld, long long nwin, int ws, int C, __half* out, cudaStream_t st);
 
-// uint8 HWC frames -> f32 CHW normalised ((p/255 - mean)/std).
-int preprocess_u8(const uint8_t* img, int B, int H, int W, const float mean[3], const float stdv[3], float* out,
-                  cudaStream_t st);
-
 // Bilinear resize of uint8 HWC frames [B][SH][SW][3] to DH x DW (sam3.cpp:3441-3481: half-pixel
 // centres, f64 weights, rounded to uint8). mean / stdv null: uint8 HWC out; else the rounded
-// frame normalised to f32 CHW [B][3][DH][DW] as preprocess_u8 does.
+// frame normalised to f32 CHW [B][3][DH][DW] ((p / 255 - mean) / std in f32).
 int resize_bilinear_u8(const uint8_t* src, int B, int SH, int SW, int DH, int DW, const float* mean,
                        const float* stdv, void* out, cudaStream_t st);
 

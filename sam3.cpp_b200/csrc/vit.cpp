@@ -149,7 +149,7 @@ static int vit_neck(s3b_ctx* ctx, const NeckScale* sc, const __half* xh, int F, 
   return kOk;
 }
 
-int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
+int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags, const uint8_t* d_u8) {
   Model& M = ctx->model;
   const HParams& hp = M.hp;
   const int E = hp.vit_embed_dim, G = hp.n_img_embd(), P = hp.patch_size, S = hp.img_size;
@@ -206,7 +206,11 @@ int vit_encode(s3b_ctx* ctx, const float* d_chw, int n_frames, int flags) {
     const long long T = (long long)F * tok_per_frame;
     if (bound_backbone && (rc = outputs_pass_begin(ctx, p, FB))) return rc;
     // patch embed (conv 14x14/s14, no bias) + tiled abs pos (sam3.cpp:3815-3822)
-    CK(im2col_image(d_chw + (size_t)f0 * 3 * S * S, F, 3, S, S, P, P, 0, G, G, col->as<__half>(), Kp, ctx->stream));
+    if (d_u8)
+      CK(patch_cols_u8(d_u8 + (size_t)f0 * S * S * 3, F, S, S, kMeanSam3, kStdSam3, P, P, 0, G, G, col->as<__half>(), Kp,
+                       ctx->stream));
+    else
+      CK(patch_cols_f32(d_chw + (size_t)f0 * 3 * S * S, F, 3, S, S, P, P, 0, G, G, col->as<__half>(), Kp, ctx->stream));
     EpiParams pe = epi_store(M.patch, xp->p, 1, E);
     pe.resid = M.pos_tiled->as<float>();
     pe.ldr = E;

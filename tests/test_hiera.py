@@ -105,6 +105,33 @@ def test_hiera_small_vs_oracle(engine, s3b, tmp_path, name, qtype):
 
 
 @pytest.mark.gpu
+def test_hiera_u8_entry_matches_chw(engine, s3b, tmp_path):
+    """The uint8 path normalises the frames inside the patch-column kernel; it gives the bits of the f32
+    CHW path fed with the same normalisation (the oracle's, f32 (p / 255 - mean) / std), from host and
+    device memory, for frames of the model size and for frames the device resize brings to it."""
+    import torch
+    from sam3_b200 import synth
+    cfg = small_cfgs(synth)["t"]
+    path = str(tmp_path / "h_u8.ggml")
+    synth.write_sam2(path, cfg, seed=8, ftype=1)
+    engine.load_model(path)
+    frames = synth.frames_u8(3, cfg.img_size, base_seed=77)
+    engine.encode_chw(oh.preprocess_u8(frames))
+    ref = [[engine.output(f"neck_trk_{i}", f) for i in range(3)] for f in range(3)]
+    engine.encode_u8(frames)
+    host = [[engine.output(f"neck_trk_{i}", f) for i in range(3)] for f in range(3)]
+    engine.encode_u8(torch.from_numpy(frames).cuda())
+    dev = [[engine.output(f"neck_trk_{i}", f) for i in range(3)] for f in range(3)]
+    engine.encode_image_u8(frames)  # the model size: no resize, the fused path
+    img = [[engine.output(f"neck_trk_{i}", f) for i in range(3)] for f in range(3)]
+    for f in range(3):
+        for i in range(3):
+            assert np.array_equal(host[f][i], ref[f][i]), (f, i)
+            assert np.array_equal(dev[f][i], ref[f][i]), (f, i)
+            assert np.array_equal(img[f][i], ref[f][i]), (f, i)
+
+
+@pytest.mark.gpu
 def test_hiera_t_full_vs_oracle(engine, s3b, tmp_path):
     """SAM 2.1 Hiera-Tiny at 1024^2 (BASELINE configs[0] shape), f16 weights, one frame."""
     from sam3_b200 import synth
