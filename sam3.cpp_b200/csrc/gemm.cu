@@ -767,9 +767,11 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
     };
     // Residual chunk `ctr` (columns gcb.., rows m0..) -> its staging buffer, once
     // the TMA store that last used that buffer has finished reading it.
-    auto issue_resid = [&](uint32_t ctr, int gcb, int m0) {
+    // all_read: wait for every earlier TMA store to have read its buffer (the chunk two ahead reuses the
+    // buffer of the store just issued)
+    auto issue_resid = [&](uint32_t ctr, int gcb, int m0, bool all_read = false) {
       const int bsel = buf_of(ctr);
-      wait_buf_read();
+      if (all_read) bulk_wait_read0(); else wait_buf_read();
       if (gcb < N) {
         mbar_arrive_expect_tx(&rfull[bsel], kStageBufBytes);
         // the residual's row: the output row itself, or (resid_mod: a table repeated every
@@ -796,8 +798,14 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
       // a column group wholly past N (the last column tile of an N that is not a multiple of BN) has
       // nothing to store: it only takes part in the accumulator hand-over
       const bool grp_live = n0 + grp * CG < N;
-      // the first residual chunk does not depend on the accumulator: fetch it during the main loop
-      if (TMA_EPI && rip && leader && grp_live) issue_resid(chunk_ctr, n0 + grp * CG, m0);
+      // the first residual chunks do not depend on the accumulator: fetch them during the main loop, one per
+      // staging buffer of the group (two with 8 epilogue warps), so a short-K GEMM waits for one residual
+      // load per tile instead of one per chunk
+      const int pre = (NBUF == 2 && CG >= 2 * cw) ? 2 : 1;
+      if (TMA_EPI && rip && leader && grp_live) {
+        issue_resid(chunk_ctr, n0 + grp * CG, m0);
+        if (pre == 2) issue_resid(chunk_ctr + 1, n0 + grp * CG + cw, m0, true);
+      }
       if (!mbar_wait(&tfull[acc], aphase, s_abort, err, kErrWaitTmemFull)) break;
       tc_fence_after();
       if (!grp_live) {
@@ -893,7 +901,7 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
             }
             bulk_commit();
           }
-          if (rip && leader && c0 + cw < CG) issue_resid(chunk_ctr + 1, gcb + cw, m0);
+          if (rip && leader && c0 + pre * cw < CG) issue_resid(chunk_ctr + pre, gcb + pre * cw, m0, pre == 2);
           ++chunk_ctr;
         }
         if (!ok) break;
