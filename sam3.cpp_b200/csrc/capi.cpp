@@ -263,16 +263,17 @@ int encode_device_image_u8(s3b_ctx* ctx, const uint8_t* d_u8, int n_frames, int 
   return encode_device_chw(ctx, chw->as<float>(), n_frames, S, flags);
 }
 
-constexpr size_t kMaxEncGraphs = 8;
+constexpr size_t kMaxEncGraphs = 16;
 
-// Runs one encoder call (`body`: all of its work on the context stream) eagerly, or replays it from a
-// CUDA graph. An encoder call is a few hundred launches of a fixed sequence; from the second call with
-// the same key (`key` + the option epoch, the GEMM configuration and the DevBuf generation, so every
-// pointer the launches hold is unchanged) the sequence is captured once and replayed, which removes the
-// host launch work and most of the gaps between kernels (the batch-1 latency). Calls with profiling on,
-// with host-bound outputs (their per-pass copies run on a second stream), behind pending output copies or
-// on the legacy default stream stay eager, and so does a key whose capture failed.
-int run_encode(s3b_ctx* ctx, std::vector<uintptr_t> key, const std::function<int()>& body) {
+// Runs one call (`body`: all of its work on the context stream; an encoder call or a tracking step)
+// eagerly, or replays it from a CUDA graph. Such a call is a fixed sequence of tens to hundreds of
+// launches; from the second call with the same key (`key` + the option epoch, the GEMM configuration and
+// the DevBuf generation, so every pointer the launches hold is unchanged) the sequence is captured once
+// and replayed, which removes the host launch work and most of the gaps between kernels (the batch-1
+// latency). Calls with profiling on, with host-bound outputs (their per-pass copies run on a second
+// stream), behind pending output copies or on the legacy default stream stay eager, and so does a key
+// whose capture failed.
+int run_graphed(s3b_ctx* ctx, std::vector<uintptr_t> key, const std::function<int()>& body) {
   if (!ctx->graphs || ctx->prof || !ctx->stream || !ctx->host_bind.empty()) return body();
   // output copies of an earlier host-bound call still pending: the eager call orders itself after them
   for (char pending : ctx->copy_pending)
@@ -694,7 +695,7 @@ int s3b_encode_u8(s3b_ctx* ctx, const uint8_t* frames, int n_frames, int img_siz
   if (!frames || n_frames <= 0 || img_size <= 0) return set_error(ctx, kErrArg, "bad arguments");
   uint8_t* d = nullptr;
   if ((rc = stage_host(ctx, frames, (size_t)n_frames * img_size * img_size * 3, "frames_u8", &d))) return rc;
-  return run_encode(ctx, {1, (uintptr_t)d, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
+  return run_graphed(ctx, {1, (uintptr_t)d, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
                     [&] { return encode_device_u8(ctx, d, n_frames, img_size, flags); });
 }
 
@@ -704,7 +705,7 @@ int s3b_encode_image_u8(s3b_ctx* ctx, const uint8_t* frames, int n_frames, int w
   if (!frames || n_frames <= 0 || width <= 0 || height <= 0) return set_error(ctx, kErrArg, "bad arguments");
   uint8_t* d = nullptr;
   if ((rc = stage_host(ctx, frames, (size_t)n_frames * width * height * 3, "frames_u8", &d))) return rc;
-  return run_encode(ctx, {2, (uintptr_t)d, (uintptr_t)n_frames, (uintptr_t)width, (uintptr_t)height, (uintptr_t)flags},
+  return run_graphed(ctx, {2, (uintptr_t)d, (uintptr_t)n_frames, (uintptr_t)width, (uintptr_t)height, (uintptr_t)flags},
                     [&] { return encode_device_image_u8(ctx, d, n_frames, width, height, flags); });
 }
 
@@ -713,9 +714,9 @@ int s3b_encode_image_u8_device(s3b_ctx* ctx, const uint8_t* d_frames, int n_fram
   int rc = ctx_enter(ctx);
   if (rc) return rc;
   if (!d_frames) return set_error(ctx, kErrArg, "null frames");
-  return run_encode(ctx,
-                    {2, (uintptr_t)d_frames, (uintptr_t)n_frames, (uintptr_t)width, (uintptr_t)height, (uintptr_t)flags},
-                    [&] { return encode_device_image_u8(ctx, d_frames, n_frames, width, height, flags); });
+  return run_graphed(ctx,
+                     {2, (uintptr_t)d_frames, (uintptr_t)n_frames, (uintptr_t)width, (uintptr_t)height, (uintptr_t)flags},
+                     [&] { return encode_device_image_u8(ctx, d_frames, n_frames, width, height, flags); });
 }
 
 int s3b_encode_chw(s3b_ctx* ctx, const float* chw, int n_frames, int img_size, int flags) {
@@ -724,7 +725,7 @@ int s3b_encode_chw(s3b_ctx* ctx, const float* chw, int n_frames, int img_size, i
   if (!chw || n_frames <= 0 || img_size <= 0) return set_error(ctx, kErrArg, "bad arguments");
   float* d = nullptr;
   if ((rc = stage_host(ctx, chw, (size_t)n_frames * 3 * img_size * img_size, "frames_chw_in", &d))) return rc;
-  return run_encode(ctx, {3, (uintptr_t)d, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
+  return run_graphed(ctx, {3, (uintptr_t)d, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
                     [&] { return encode_device_chw(ctx, d, n_frames, img_size, flags); });
 }
 
@@ -732,7 +733,7 @@ int s3b_encode_u8_device(s3b_ctx* ctx, const uint8_t* d_frames, int n_frames, in
   int rc = ctx_enter(ctx);
   if (rc) return rc;
   if (!d_frames) return set_error(ctx, kErrArg, "null frames");
-  return run_encode(ctx, {1, (uintptr_t)d_frames, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
+  return run_graphed(ctx, {1, (uintptr_t)d_frames, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
                     [&] { return encode_device_u8(ctx, d_frames, n_frames, img_size, flags); });
 }
 
@@ -740,7 +741,7 @@ int s3b_encode_chw_device(s3b_ctx* ctx, const float* d_chw, int n_frames, int im
   int rc = ctx_enter(ctx);
   if (rc) return rc;
   if (!d_chw) return set_error(ctx, kErrArg, "null frames");
-  return run_encode(ctx, {3, (uintptr_t)d_chw, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
+  return run_graphed(ctx, {3, (uintptr_t)d_chw, (uintptr_t)n_frames, (uintptr_t)img_size, (uintptr_t)flags},
                     [&] { return encode_device_chw(ctx, d_chw, n_frames, img_size, flags); });
 }
 
@@ -1058,7 +1059,29 @@ int s3b_track_step(s3b_ctx* ctx, int feat, const float* neck_trk_0, const float*
   PromptArgs pa;
   if ((rc = prompt_args(ctx, feat, slot_feats, slot_pes, slot_tpos, n_slots, obj_ptrs, ptr_tpos, n_ptrs, pa)))
     return rc;
-  return track_step_run(ctx, feat, neck_trk_0, neck_trk_1, neck_trk_2, pa, mask_logits, scores, mem_feats, obj_ptr);
+  // a tracker that keeps its memory bank and feature maps in the same buffers from frame to frame replays
+  // the step (about 130 launches) from a CUDA graph; the key holds every pointer and position it depends on
+  std::vector<uintptr_t> key = {10,
+                                (uintptr_t)feat,
+                                (uintptr_t)neck_trk_0,
+                                (uintptr_t)neck_trk_1,
+                                (uintptr_t)neck_trk_2,
+                                (uintptr_t)n_slots,
+                                (uintptr_t)obj_ptrs,
+                                (uintptr_t)n_ptrs,
+                                (uintptr_t)mask_logits,
+                                (uintptr_t)scores,
+                                (uintptr_t)mem_feats,
+                                (uintptr_t)obj_ptr};
+  for (int s = 0; s < n_slots; ++s) {
+    key.push_back((uintptr_t)slot_feats[s]);
+    key.push_back((uintptr_t)(slot_pes ? slot_pes[s] : nullptr));
+    key.push_back((uintptr_t)(intptr_t)slot_tpos[s]);
+  }
+  for (int p = 0; p < n_ptrs; ++p) key.push_back((uintptr_t)(intptr_t)ptr_tpos[p]);
+  return run_graphed(ctx, key, [&] {
+    return track_step_run(ctx, feat, neck_trk_0, neck_trk_1, neck_trk_2, pa, mask_logits, scores, mem_feats, obj_ptr);
+  });
 }
 
 int s3b_sam_best_mask(const float* iou, int n_masks, int multimask) {

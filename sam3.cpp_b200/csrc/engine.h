@@ -334,7 +334,7 @@ struct s3b_ctx {
   std::vector<uintptr_t> ma_key;  // shapes, buffers, epoch and kernel choices the graph was captured with
   long long ma_launches = 0;      // kernel launches inside the graph
   int ma_seen = 0;                // eager calls with ma_key so far (the graph is captured on the second)
-  // encoder calls replayed from CUDA graphs (capi.cpp run_encode): one per key (entry point, input
+  // encoder calls and tracking steps replayed from CUDA graphs (capi.cpp run_graphed): one per key (entry point, input
   // pointer, frame count and size, flags, option epoch, GEMM configuration, DevBuf generation), most
   // recently used last
   struct EncGraph {

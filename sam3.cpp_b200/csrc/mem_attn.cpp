@@ -209,7 +209,10 @@ static int mem_attn_body(s3b_ctx* ctx, const float* curr, const float* src_pos, 
   // the second call with the same shapes, buffers and options captures them into a CUDA graph (the
   // first call has allocated every workspace and set every kernel attribute) and later calls replay
   // it, which removes the host launch work and most of the gaps between the kernels.
-  const bool can_graph = ctx->graphs && !ctx->prof && ctx->stream != nullptr;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(ctx->stream, &cap);
+  // inside a capture of the whole call (a tracking step) the layers are recorded eagerly into that graph
+  const bool can_graph = ctx->graphs && !ctx->prof && ctx->stream != nullptr && cap == cudaStreamCaptureStatusNone;
   // every buffer the layers touch is in the key, the attention's key-split workspace included (an
   // encoder call on the same context may grow and so move it)
   const auto ws_it = ctx->ws.find("attn_wide_split");

@@ -118,3 +118,58 @@ def test_track_loop_vs_oracle(tmp_path, engine):
         ptrs.insert(0, out["ptr"])
         ref_bank.append(rmem)
         ref_ptrs.insert(0, rptr)
+
+
+@pytest.mark.parametrize("sam2", [True, False], ids=["sam2", "sam3"])
+def test_track_step_graph_replay_equals_eager(tmp_path, engine, sam2):
+    """On a capturable stream, the second tracking step with the same buffers, bank layout and positions is
+    captured into a CUDA graph and later steps replay it: they give the eager bits, read the current
+    contents of the same buffers, and a changed position or buffer runs (and later captures) its own key."""
+    cfg, path, W = _model(tmp_path, sam2, 37)
+    H = 16
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    engine.set_stream(stream.cuda_stream)
+    try:
+        engine.load_model(path)
+        with torch.cuda.stream(stream):
+            t0, t1, t2 = _frame(H, 3)
+            g = torch.Generator(device="cuda").manual_seed(4)
+            feats = [torch.randn(H * H, 64, device="cuda", generator=g) for _ in range(3)]
+            ptrs = torch.randn(2, 256, device="cuda", generator=g)
+            new_feats = [torch.randn(H * H, 64, device="cuda", generator=g) for _ in range(3)]
+            outs = {"mask": torch.empty(16 * H * H, device="cuda"), "scores": torch.empty(3, device="cuda"),
+                    "mem": torch.empty(H * H, 64, device="cuda"), "ptr": torch.empty(256, device="cuda")}
+
+        def step(slot_tpos=(0, 2, 1), ptr_tpos=(1, 2)):
+            engine.track_step(H, t0, t1, t2, feats, list(slot_tpos), ptrs, list(ptr_tpos), outs=outs)
+            engine.sync()
+            return {k: v.cpu().clone() for k, v in outs.items()}
+
+        engine.set_option("graphs", 0)
+        ref = step()
+        ref_tpos = step(slot_tpos=(0, 1, 2))
+        for f, nf in zip(feats, new_feats):
+            f.copy_(nf)
+        ref_new = step()
+        engine.set_option("graphs", 1)
+        with torch.cuda.stream(stream):
+            g = torch.Generator(device="cuda").manual_seed(4)
+            old = [torch.randn(H * H, 64, device="cuda", generator=g) for _ in range(3)]
+        for f, o in zip(feats, old):
+            f.copy_(o)
+        for i in range(4):  # eager, eager, capture + replay, replay
+            got = step()
+            for k in ref:
+                assert torch.equal(got[k], ref[k]), (i, k)
+        got = step(slot_tpos=(0, 1, 2))  # another key
+        for k in ref:
+            assert torch.equal(got[k], ref_tpos[k]), ("tpos", k)
+        for f, nf in zip(feats, new_feats):  # new contents, same buffers: the replay reads them
+            f.copy_(nf)
+        got = step()
+        for k in ref:
+            assert torch.equal(got[k], ref_new[k]), ("refill", k)
+    finally:
+        engine.set_option("graphs", 1)
+        engine.set_stream(torch.cuda.current_stream().cuda_stream)
