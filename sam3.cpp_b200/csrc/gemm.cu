@@ -229,9 +229,22 @@ __device__ __forceinline__ void store16(void* base, long long idx, int is_f32, c
 
 // bias + activation + RoPE + scale on 16 consecutive columns [gc, gc+16) of
 // row gr; rope_pos = RoPE position of the row (gr % rope_mod), or -1 for none.
-__device__ __forceinline__ void epi_math16(const EpiParams& ep, int rope_pos, int gc, int N, float (&v)[16]) {
+// SB: the bias of these 16 columns is staged in shared memory at sbias (16-byte aligned) instead of read
+// from global memory.
+template <bool SB = false>
+__device__ __forceinline__ void epi_math16(const EpiParams& ep, int rope_pos, int gc, int N, float (&v)[16],
+                                           const float* sbias = nullptr) {
   const int n_valid = min(16, N - gc);
-  if (ep.bias) {
+  if (SB) {
+    if (ep.bias) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        const float4 b = *reinterpret_cast<const float4*>(sbias + i);  // one address for the warp: broadcast
+        f2_unpack(f2_add(f2_pack(v[i], v[i + 1]), f2_pack(b.x, b.y)), v[i], v[i + 1]);
+        f2_unpack(f2_add(f2_pack(v[i + 2], v[i + 3]), f2_pack(b.z, b.w)), v[i + 2], v[i + 3]);
+      }
+    }
+  } else if (ep.bias) {
     if (ep.mode == EPI_DECONV2) {
       const int c0 = gc % ep.cout;
 #pragma unroll
@@ -448,6 +461,7 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = 2 * BN;
   constexpr uint32_t STAGING = TMA_EPI ? 4 * kStageBufBytes : 0;
+  constexpr uint32_t BIAS_BYTES = TMA_EPI ? BN * 4 : 0;
   constexpr int DW = QB ? dequant_warps(EW) : 0;
   constexpr uint32_t QROW = QB == 1 ? 32 : 64;              // value bytes per weight row per stage
   constexpr uint32_t QV_BYTES = QB ? BN_CTA * QROW : 0;     // block values of the stage
@@ -463,7 +477,8 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sC = sB + STAGES * B_BYTES;  // staging (TMA epilogue only), 1024-aligned
-  uint8_t* sQ = sC + STAGING;           // QB landing buffers, 512-byte multiples
+  float* sBias = reinterpret_cast<float*>(sC + STAGING);  // TMA epilogue: the tile's bias, BN floats
+  uint8_t* sQ = sC + STAGING + BIAS_BYTES;  // QB landing buffers, 512-byte multiples
   uint64_t* full = reinterpret_cast<uint64_t*>(sQ + QS * Q_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -798,6 +813,7 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
       // a column group wholly past N (the last column tile of an N that is not a multiple of BN) has
       // nothing to store: it only takes part in the accumulator hand-over
       const bool grp_live = n0 + grp * CG < N;
+      const bool sb_on = TMA_EPI && ep.bias != nullptr && grp_live;
       // the first residual chunks do not depend on the accumulator: fetch them during the main loop, one per
       // staging buffer of the group (two with 8 epilogue warps), so a short-K GEMM waits for one residual
       // load per tile instead of one per chunk
@@ -805,6 +821,18 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
       if (TMA_EPI && rip && leader && grp_live) {
         issue_resid(chunk_ctr, n0 + grp * CG, m0);
         if (pre == 2) issue_resid(chunk_ctr + 1, n0 + grp * CG + cw, m0, true);
+      }
+      // the bias of the group's columns goes to shared memory once per tile, before the accumulator wait,
+      // instead of sitting in every chunk's critical path as an L2 load. The previous tile's reads of the
+      // slice finished before its last group barrier; without a residual the first chunk's group barrier
+      // orders these stores before the reads.
+      if (sb_on) {
+        const int gt = ((warp - 2) & 3) * 32 + lane;  // thread within the group
+        if (gt < CG) {
+          const int col = n0 + grp * CG + gt;
+          sBias[grp * CG + gt] = col < N ? __ldg(ep.bias + (ep.mode == EPI_DECONV2 ? col % ep.cout : col)) : 0.0f;
+        }
+        if (rip) named_bar(1 + grp, 128);
       }
       if (!mbar_wait(&tfull[acc], aphase, s_abort, err, kErrWaitTmemFull)) break;
       tc_fence_after();
@@ -862,7 +890,7 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
 #pragma unroll
                 for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[j * 16 + i]);
                 const int gc = gcb + s0 + j * 16;
-                if (gc < N) epi_math16(ep, rope_pos, gc, N, v);
+                if (gc < N) epi_math16<true>(ep, rope_pos, gc, N, v, sBias + (gc - n0));
                 if (out_f32) {
 #pragma unroll
                   for (int u = 0; u < 4; ++u) {
@@ -1082,7 +1110,8 @@ int launch_gemm(const __half* A, long long lda, const void* B, long long ldb, in
   }
   constexpr size_t q_bytes = QB ? (size_t)BN_CTA * QROW + 4 * BN_CTA : 0;
   constexpr size_t smem = 1024 + (size_t)STAGES * (kBM + BN_CTA) * kBK * 2 + (size_t)QS * q_bytes +
-                          (TMA_EPI ? 4 * kStageBufBytes : 0) + (2 * STAGES + 2 * QS + (QS ? STAGES : 0) + 9) * 8 + 16;
+                          (TMA_EPI ? 4 * kStageBufBytes + BN * 4 : 0) +
+                          (2 * STAGES + 2 * QS + (QS ? STAGES : 0) + 9) * 8 + 16;
   static_assert(smem <= 232448, "shared memory per CTA");
   auto kernel = gemm_f16_tc_kernel<BN, STAGES, TMA_EPI, PAIR, EW, BLK, QB, QS>;
   constexpr int kThreads = gemm_threads(EW, DW);
