@@ -448,6 +448,12 @@ __device__ __forceinline__ void conv_tile_origin(int mt, const EpiParams& ep, ui
 // the TMA would have produced, fence it for the async proxy, release the landing
 // buffer and arrive on `full` (with pairs: on the leader's `full`, whose count then
 // includes both CTAs' dequantising warps).
+// Column tile of linear tile t (row tile t / tiles_n): the column order is rotated by the row tile, so that
+// a persistent CTA whose tile stride is a multiple of tiles_n still meets every column tile. Without the
+// rotation such a CTA would meet one column tile only, and when N is not a multiple of BN the CTAs holding
+// the narrow last column tile idle while the others work (Hiera-T stage-0 qkv, N = 288 on 74 SM pairs).
+__device__ __forceinline__ int tile_col(int t, int tiles_n) { return (t % tiles_n + t / tiles_n) % tiles_n; }
+
 template <int BN, int STAGES, bool TMA_EPI, bool PAIR, int EW, int BLK = 0, int QB = 0, int QS = 0>
 __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 1)
     gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -555,7 +561,7 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
       const int cbn = BLK == 1 ? ep.conv_C / kBK : 1;  // 64-channel blocks per tap
       for (int t = unit; t < n_tiles && ok; t += n_units) {
         const int m0 = (t / tiles_n) * TM + (int)rank * kBM;
-        const int n0 = (t % tiles_n) * BN + (int)rank * BN_CTA;
+        const int n0 = tile_col(t, tiles_n) * BN + (int)rank * BN_CTA;
         int cx = 0, cy = 0, cf = 0;
         if (BLK) conv_tile_origin<PAIR ? 2 : 1>(t / tiles_n, ep, rank, &cx, &cy, &cf);
         for (int kb = 0; kb < nk; ++kb) {
@@ -611,7 +617,7 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
       uint32_t armed = 0, armed_phase = 0;
       bool ok = true;
       for (int t = unit; t < n_tiles && ok; t += n_units) {
-        const int n0 = (t % tiles_n) * BN + (int)rank * BN_CTA;
+        const int n0 = tile_col(t, tiles_n) * BN + (int)rank * BN_CTA;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&qempty[qi], qph ^ 1, s_abort, err, kErrWaitEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&qfull[qi], Q_BYTES);
@@ -807,7 +813,7 @@ __global__ void __launch_bounds__(gemm_threads(EW, QB ? dequant_warps(EW) : 0), 
     };
     for (int t = unit; t < n_tiles; t += n_units) {
       const int m0 = (t / tiles_n) * TM + (int)rank * kBM;
-      const int n0 = (t % tiles_n) * BN;
+      const int n0 = tile_col(t, tiles_n) * BN;
       int cx = 0, cy = 0, cf = 0;
       if (BLK) conv_tile_origin<PAIR ? 2 : 1>(t / tiles_n, ep, rank, &cx, &cy, &cf);
       // a column group wholly past N (the last column tile of an N that is not a multiple of BN) has
