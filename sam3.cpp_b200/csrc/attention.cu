@@ -69,14 +69,16 @@ __device__ __forceinline__ void load_tile(__half* s, const __half* g, long long 
 // D: compute head dim (multiple of 16); DR: real head dim (multiple of 8). For
 // DR < D (Hiera-L's 72 -> 80) the pad columns stay zero in shared memory, which
 // leaves q.k unchanged and gives zero output columns that are not stored.
-template <int D, int DR>
+// ONE: nk <= 64, a single key tile: K and V take one buffer each (40 KB instead of 66 KB of shared memory
+// at d = 96), so five CTAs fit on an SM instead of three (Hiera-T's stage-0 windows, 64 x 64).
+template <int D, int DR, bool ONE = false>
 __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
   constexpr int LD = D + 8;
   constexpr int NT = D / 8;  // n-tiles of the output
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __half* sQ = reinterpret_cast<__half*>(smem_raw);
   __half* sK = sQ + kBQ * LD;
-  __half* sV = sK + 2 * kBKV * LD;
+  __half* sV = sK + (ONE ? 1 : 2) * kBKV * LD;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // 1-D grid, query tile fastest: the tiles of one (batch, head) run together and share K/V in L2
@@ -90,7 +92,7 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
 
   if constexpr (DR < D) {
     constexpr int PADC = (DR < D) ? D - DR : 1;
-    for (int i = tid; i < (kBQ + 4 * kBKV) * PADC; i += 128) {
+    for (int i = tid; i < (kBQ + (ONE ? 2 : 4) * kBKV) * PADC; i += 128) {
       const int r = i / PADC, c = DR + i % PADC;
       sQ[r * LD + c] = __float2half_rn(0.f);
     }
@@ -111,8 +113,8 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
   const int g = lane >> 2, t4 = lane & 3;
 
   for (int j = 0; j < nkt; ++j) {
-    const int buf = j & 1;
-    if (j + 1 < nkt) {
+    const int buf = ONE ? 0 : (j & 1);
+    if (!ONE && j + 1 < nkt) {
       const int nb = buf ^ 1;
       load_tile<D, DR>(sK + nb * kBKV * LD, Kg + (long long)(j + 1) * kBKV * p.k_n, p.k_n, p.nk - (j + 1) * kBKV, tid);
       load_tile<D, DR>(sV + nb * kBKV * LD, Vg + (long long)(j + 1) * kBKV * p.v_n, p.v_n, p.nk - (j + 1) * kBKV, tid);
@@ -233,14 +235,22 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnParams p) {
 // windows, e.g. 16 queries x 16 keys): one warp per (batch, head), four per
 // CTA, each with its own Q (16 rows), K and V (NKP rows) in shared memory; S,
 // the softmax and P V of the single key tile stay in registers.
+// Warps per CTA of attn_small_kernel: 4, or for 64-key windows (30 KB of shared memory per warp, so one
+// 4-warp CTA per SM) as many as one CTA's shared memory holds, up to 8: each warp waits for its loads before
+// computing, so the warps in flight per SM set the throughput.
+template <int D, int NKP>
+constexpr int small_warps() {
+  return NKP < 64 ? 4 : (232448 / ((16 + 2 * NKP) * (D + 8) * 2) < 8 ? 232448 / ((16 + 2 * NKP) * (D + 8) * 2) : 8);
+}
+
 template <int D, int DR, int NKP>
-__global__ void __launch_bounds__(128) attn_small_kernel(AttnParams p, int batch_heads) {
+__global__ void __launch_bounds__(32 * small_warps<D, NKP>()) attn_small_kernel(AttnParams p, int batch_heads) {
   constexpr int LD = D + 8;
   constexpr int NT = D / 8;
   constexpr int WROWS = 16 + 2 * NKP;  // Q, K, V rows of one warp
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.x * 4 + warp;
+  const int bh = blockIdx.x * small_warps<D, NKP>() + warp;
   if (bh >= batch_heads) return;  // whole warp; no CTA-wide barrier below
   __half* sQ = reinterpret_cast<__half*>(smem_raw) + warp * WROWS * LD;
   __half* sK = sQ + 16 * LD;
@@ -357,11 +367,13 @@ __global__ void __launch_bounds__(128) attn_small_kernel(AttnParams p, int batch
 
 template <int D, int DR, int NKP>
 int launch_small(const AttnParams& p, int batch_heads, cudaStream_t st) {
-  constexpr size_t smem = (size_t)4 * (16 + 2 * NKP) * (D + 8) * 2;
+  constexpr int W = small_warps<D, NKP>();
+  constexpr size_t smem = (size_t)W * (16 + 2 * NKP) * (D + 8) * 2;
+  static_assert(W >= 4 && smem <= 232448, "shared memory per CTA");
   if (kernel_setup(attn_small_kernel<D, DR, NKP>, smem) <= 0) return -13;
-  const long long n_cta = ((long long)batch_heads + 3) / 4;
+  const long long n_cta = ((long long)batch_heads + W - 1) / W;
   if (n_cta > 0x7fffffffLL) return -2;
-  attn_small_kernel<D, DR, NKP><<<(unsigned)n_cta, 128, smem, st>>>(p, batch_heads);
+  attn_small_kernel<D, DR, NKP><<<(unsigned)n_cta, 32 * W, smem, st>>>(p, batch_heads);
   return launch_status("attention (small windows)");
 }
 
@@ -378,10 +390,16 @@ int launch_attn(const AttnParams& p, int batch_heads, cudaStream_t st) {
   if constexpr (D <= 128) {
     if (p.nq <= 16 && p.nk <= 64) return launch_small_nk<D, DR>(p, batch_heads, st);
   }
-  constexpr size_t smem = (size_t)(kBQ + 4 * kBKV) * (D + 8) * 2;
-  if (kernel_setup(attn_fwd_kernel<D, DR>, smem) <= 0) return -13;
   const long long n_cta = (long long)((p.nq + kBQ - 1) / kBQ) * batch_heads;
   if (n_cta > 0x7fffffffLL) return -2;
+  if (p.nk <= kBKV) {
+    constexpr size_t smem1 = (size_t)(kBQ + 2 * kBKV) * (D + 8) * 2;
+    if (kernel_setup(attn_fwd_kernel<D, DR, true>, smem1) <= 0) return -13;
+    attn_fwd_kernel<D, DR, true><<<(unsigned)n_cta, 128, smem1, st>>>(p);
+    return launch_status("attention");
+  }
+  constexpr size_t smem = (size_t)(kBQ + 4 * kBKV) * (D + 8) * 2;
+  if (kernel_setup(attn_fwd_kernel<D, DR>, smem) <= 0) return -13;
   attn_fwd_kernel<D, DR><<<(unsigned)n_cta, 128, smem, st>>>(p);
   return launch_status("attention");
 }
