@@ -50,8 +50,8 @@ WEIGHTS_DESC = {0: "f16, dequantised once at load",
                 2: "block form; dequantised inside the GEMM's shared-memory stages"}
 # measured with ncu (one --set full capture of ViT block 0): mean DRAM read+write per launch of the
 # qkv / proj / fc1 / fc2 GEMMs of a ViT block at 8 frames per pass, and their algorithmic bytes
-GEMM_TRAFFIC_BYTES = 4.696e8
-GEMM_ALG_BYTES = 5.006e8
+GEMM_TRAFFIC_BYTES = 4.728e8  # (294.5 + 374.3 + 435.7 + 786.5) MB / 4
+GEMM_ALG_BYTES = 5.007e8  # (346.4 + 426.8 + 487.4 + 742.3) MB / 4
 
 
 def load_pkg():
