@@ -531,7 +531,10 @@ struct Cfg2 {
   static constexpr int DK = WideCfg<D>::DK;         // K of Q K^T and N of P V (d rounded up to 16)
   static constexpr int NA = WideCfg<D>::NA;         // 64-column atoms per row
   static constexpr uint32_t Tile = NA * kAtom2;     // Q, K or V tile of 128 rows
-  static constexpr size_t Smem = 1024 + 3 * (size_t)Tile + 16 * 8 + 16;
+  // K / V slots each: two where they fit beside Q (d <= 128), so the copy of a key tile starts one MMA round
+  // earlier; one for d = 256
+  static constexpr int KVB = NA <= 2 ? 2 : 1;
+  static constexpr size_t Smem = 1024 + (1 + 2 * KVB) * (size_t)Tile + 16 * 8 + 16;
 };
 
 __device__ __forceinline__ float fmax3f(float a, float b, float c) {
@@ -639,27 +642,28 @@ __global__ void __launch_bounds__(kThreads2, 1)
     attn128k_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, WideArgs a, int* err) {
   using C = Cfg2<D>;
-  constexpr int DK = C::DK, NA = C::NA;
+  constexpr int DK = C::DK, NA = C::NA, KVB = C::KVB;
   constexpr uint32_t kTile2 = C::Tile;
   constexpr bool kPadQ = DK > D;  // Q columns [D, DK) must read as zero (d = 72)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kTile2;
-  uint8_t* sV = sK + kTile2;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kTile2);
+  uint8_t* sK = sQ + kTile2;        // [KVB] slots: K_j in slot j % KVB
+  uint8_t* sV = sK + KVB * kTile2;  // [KVB] slots: V_j in slot j % KVB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KVB * kTile2);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 2;
-  uint64_t* v_full = bars + 3;
-  uint64_t* v_empty = bars + 4;
-  uint64_t* s_full = bars + 5;    // [2]: S_j in region j & 1
-  uint64_t* p_full = bars + 7;    // P_j written (4 softmax warps)
-  uint64_t* pv_done = bars + 8;   // P V_j completed
-  uint64_t* o_done = bars + 9;
-  uint64_t* mma_done = bars + 10;
-  uint64_t* q_ready = bars + 11;  // Q padding columns zeroed (d = 72)
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* s_full = bars + 1;    // [2]: S_j in region j & 1
+  uint64_t* p_full = bars + 3;    // P_j written (4 softmax warps)
+  uint64_t* pv_done = bars + 4;   // P V_j completed
+  uint64_t* o_done = bars + 5;
+  uint64_t* mma_done = bars + 6;
+  uint64_t* q_ready = bars + 7;   // Q padding columns zeroed (d = 72)
+  uint64_t* k_full = bars + 8;    // [KVB]
+  uint64_t* k_empty = k_full + KVB;
+  uint64_t* v_full = k_empty + KVB;
+  uint64_t* v_empty = v_full + KVB;
+  static_assert(8 + 4 * KVB <= 16, "barrier area");
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -677,10 +681,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(k_full, 1);
-    mbar_init(k_empty, 1);
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
+    for (int i = 0; i < KVB; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
     mbar_init(p_full, 4);
@@ -720,15 +726,19 @@ __global__ void __launch_bounds__(kThreads2, 1)
       }
       int armed = -1;
       for (int j = 0; j < nkb; ++j) {
-        if (!mbar_wait(empty, ((uint32_t)j & 1) ^ 1, s_abort, err, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(full, kTile2);
+        const int sl = j % KVB;
+        const uint32_t use = (uint32_t)(j / KVB);
+        if (!mbar_wait(&empty[sl], (use & 1) ^ 1, s_abort, err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&full[sl], kTile2);
 #pragma unroll
-        for (int at = 0; at < NA; ++at) tma_load_3d(map, full, dst + at * kAtom2, col0 + at * 64, (j0 + j) * kB2, rb);
+        for (int at = 0; at < NA; ++at)
+          tma_load_3d(map, &full[sl], dst + sl * kTile2 + at * kAtom2, col0 + at * 64, (j0 + j) * kB2, rb);
         armed = j;
       }
-      // no copy may still be landing when the CTA exits
+      // no copy may still be landing when the CTA exits: the last arming of each slot
       if (is_k) mbar_wait_drain(q_full, 0, err);
-      if (armed >= 0) mbar_wait_drain(full, (uint32_t)armed & 1, err);
+      for (int j = armed; j >= 0 && j > armed - KVB; --j)
+        mbar_wait_drain(&full[j % KVB], (uint32_t)(j / KVB) & 1, err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -739,16 +749,18 @@ __global__ void __launch_bounds__(kThreads2, 1)
       const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK), va = smem_u32(sV);
       bool issued = false;
       auto issue_s = [&](int j) -> bool {
-        if (!mbar_wait(k_full, (uint32_t)j & 1, s_abort, err, kErrWaitFull)) return false;
+        const int sl = j % KVB;
+        if (!mbar_wait(&k_full[sl], (uint32_t)(j / KVB) & 1, s_abort, err, kErrWaitFull)) return false;
         tc_fence_after();
         const uint32_t sa = tmem + (uint32_t)((j & 1) * kB2);
+        const uint32_t kb = ka + (uint32_t)(sl * kTile2);
 #pragma unroll
         for (int kk = 0; kk < DK / 16; ++kk) {
           const uint32_t off = (uint32_t)((kk >> 2) * kAtom2 + (kk & 3) * 32);
-          tc_mma_f16(sa, sdesc_k_sw128(qa + off), sdesc_k_sw128(ka + off), idesc_s, kk != 0);
+          tc_mma_f16(sa, sdesc_k_sw128(qa + off), sdesc_k_sw128(kb + off), idesc_s, kk != 0);
         }
         tc_commit(&s_full[j & 1]);
-        tc_commit(k_empty);
+        tc_commit(&k_empty[sl]);
         issued = true;
         return true;
       };
@@ -756,18 +768,20 @@ __global__ void __launch_bounds__(kThreads2, 1)
       if (ok && nkb > 1) ok = issue_s(1);
       for (int j = 0; j < nkb && ok; ++j) {
         if (!mbar_wait(p_full, (uint32_t)j & 1, s_abort, err, kErrWaitMisc)) { ok = false; break; }
-        if (!mbar_wait(v_full, (uint32_t)j & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
+        const int vsl = j % KVB;
+        if (!mbar_wait(&v_full[vsl], (uint32_t)(j / KVB) & 1, s_abort, err, kErrWaitFull)) { ok = false; break; }
         tc_fence_after();
         const uint32_t pa = tmem + (uint32_t)((j & 1) * kB2);
+        const uint32_t vb = va + (uint32_t)(vsl * kTile2);
         const int nk16 = min(kB2 / 16, (a.nk - (j0 + j) * kB2 + 15) / 16);  // K steps holding a real key
 #pragma unroll
         for (int kk = 0; kk < kB2 / 16; ++kk) {
           if (kk >= nk16) break;
-          tc_mma_f16_ts(tmem + 256, pa + (uint32_t)(kk * 8), sdesc_mn_v128(va + (uint32_t)(kk * 2048)), idesc_o,
+          tc_mma_f16_ts(tmem + 256, pa + (uint32_t)(kk * 8), sdesc_mn_v128(vb + (uint32_t)(kk * 2048)), idesc_o,
                         (j > 0 || kk != 0) ? 1u : 0u);
         }
         tc_commit(pv_done);
-        tc_commit(v_empty);
+        tc_commit(&v_empty[vsl]);
         if (j + 2 < nkb && !issue_s(j + 2)) { ok = false; break; }
       }
       if (ok) tc_commit(o_done);
