@@ -511,11 +511,11 @@ __global__ void __launch_bounds__(kThreads, WideCfg<D>::MinBlocks)
 // The d = 256 products on the kernel above issue 20 MMAs per 64 keys, 16 of them N = 64 (S = Q K^T over
 // d = 256 in K = 16 steps); this kernel takes 128-key tiles, so S runs N = 128 and each 128 keys cost 24
 // MMAs (16 for S, 8 for P V with N = 256) instead of 40. P goes back to TMEM over the scores it came from
-// (the A operand of P V), which frees the shared memory for one 128-key K tile and one V tile (64 KB each)
-// beside the 64 KB Q tile. TMEM (512 columns): S / P regions r = 0, 1 at 128 r (S_j in region j & 1), O at
-// 256. 7 warps:
-//   warp 0     TMA: the Q tile, then K_j (four 64-column boxes of 128 rows) once S_{j-1} has read K_{j-1}
-//   warp 6     TMA: V_j once P V_{j-1} has read V_{j-1}
+// (the A operand of P V), which frees the shared memory for 128-key K and V tiles beside the Q tile: one
+// slot each at d = 256 (64 KB tiles), two at d <= 128 (32 KB tiles), K_j / V_j in slot j % slots. TMEM (512
+// columns): S / P regions r = 0, 1 at 128 r (S_j in region j & 1), O at 256. 7 warps:
+//   warp 0     TMA: the Q tile, then K_j (64-column boxes of 128 rows) once S_{j-slots} has read its slot
+//   warp 6     TMA: V_j once P V_{j-slots} has read its slot
 //   warp 1     MMA: S_0, S_1, then per key tile j: O += P_j V_j (A = P_j from TMEM), S_{j+2}. S_{j+2}
 //              rewrites the region P_j was read from; the MMAs of one thread execute in order.
 //   warps 2-5  softmax, one query row per thread (TMEM lane): the row's 128 scores in registers, row max,
